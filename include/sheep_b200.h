@@ -1,0 +1,93 @@
+// libsheep_b200.so: the B200 decode engine's C ABI beyond the reference's
+// sml-gpu.h. Plain pointers and sizes only. "device" arguments are CUDA device
+// pointers on the current device; "host" arguments are host memory.
+#pragma once
+
+#include <stdint.h>
+
+#include "sml-gpu.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+// ------------------------------------------------------------------ engine
+// A handle form of the sml-gpu.h API (several models per process, explicit
+// n_ctx). Replaces the reference's gpu_setup / gpu_forward / graph_token
+// (sml/sml-gpu-fwd.c:1789, :1643, :636).
+typedef struct sb_engine sb_engine;
+
+sb_engine * sb_open(const char * path, int n_ctx, char * why, int nwhy);
+void        sb_close(sb_engine * e);
+// out[0..11]: n_layer, n_embd, n_head, n_head_kv, head_dim, n_ff, n_vocab,
+// n_ctx, n_expert, n_expert_used, weight bytes per token (low, high 32 bits)
+void        sb_info(const sb_engine * e, int * out);
+uint64_t    sb_bytes_per_token(const sb_engine * e);
+// sml/sml-gpu.h:17 semantics on a handle: logits in host memory, NULL on failure.
+const float * sb_step(sb_engine * e, int tok, int pos);
+// sml/sml-gpu.h:14 semantics on a handle.
+const float * sb_prefill(sb_engine * e, const int * ids, int pos0, int n);
+// Greedy decode with the choice made on the device (the reference's
+// graph-replay benchmark loop, sml/sml-gpu-fwd.c:2626-2662): host prompt in,
+// ngen host ids out. Returns 1, or 0 on failure.
+int sb_generate(sb_engine * e, const int * prompt, int np, int ngen, int * out_ids);
+// The same, with the generation loop (prompt excluded) timed by CUDA events.
+int sb_generate_timed(sb_engine * e, const int * prompt, int np, int ngen, int * out_ids, float * ms_out);
+const float * sb_device_logits(const sb_engine * e);
+int sb_launches_per_token(const sb_engine * e);
+const char * sb_last_error(void);
+// The engine behind sml_gpu_open, and its release.
+sb_engine * sml_gpu_engine(void);
+void sml_gpu_close(void);
+
+// ------------------------------------------------------------------ tensors
+// Every flat tensor of an SSF file on the device, by name. Kernel-level entry
+// points over it replace the reference's per-kernel GPU bench and check
+// drivers (sml/sml-gpu-bench.c:99-157, sml/sml-check.c:166-283).
+typedef struct sb_tset sb_tset;
+
+sb_tset * sb_tset_open(const char * path, char * why, int nwhy);
+void      sb_tset_close(sb_tset * t);
+int       sb_tset_shape(const sb_tset * t, const char * name, int * rows, int * cols, int * nbits);
+// Weight bytes of the tensor (codes + fields): the bytes one GEMV streams.
+unsigned long long sb_tset_bytes(const sb_tset * t, const char * name);
+// y[b] = W x[b], nb vectors, device pointers (x nb x cols, y nb x rows),
+// activation gathered through the tensor's perm and quantized per 32 inside.
+// Replaces sml_g_mv3s / sml_g_qdmv2 (sml/sml-gpu-fast.cu:267-315).
+int sb_tset_gemv_dev(sb_tset * t, const char * name, const float * x, int nb, float * y, void * stream);
+// Host-buffer form of one GEMV; q/s/sums (host, may be NULL) receive the int8
+// activation the kernel used. Mirrors what sml-check writes
+// (sml/sml-check.c:194-245).
+int sb_tset_matvec(sb_tset * t, const char * name, const float * x, float * y, int8_t * q, float * s,
+                   int32_t * sums);
+// Rows dequantized on the GPU, permuted column order (sml_dequant_row_flat*,
+// sml/sml-kernel.c:2134-2260; the embedding path sml_g_embed,
+// sml/sml-gpu-fast.cu:461). Host buffers.
+int sb_tset_dequant_rows(sb_tset * t, const char * name, const int * rows, int nrows, float * out);
+
+// sml_gather + sml_quantize_act (sml/sml-kernel.c:41, :253) on device
+// pointers: q natural order (n bytes), s and sums per 32. perm may be NULL.
+int sb_quantize_act(const float * x, const int32_t * perm, int n, int8_t * q, float * s, int32_t * sums,
+                    void * stream);
+
+// ------------------------------------------------------------------ models
+// Seeded synthetic SSF writer (the inputs every test and bench runs on; the
+// reference builds SSF files offline, tooling/sml_quantize.py:596-651).
+typedef struct {
+    uint32_t n_layer, n_embd, n_head, n_head_kv, head_dim, n_ff, n_vocab;
+    float    rope_theta, rms_eps;
+    uint32_t tied, qkv_bias, qk_norm;
+    uint32_t nbits, emb_nbits;
+    uint32_t scale6, minneg;
+    uint32_t n_expert, n_expert_used, moe_flags, expert_ff;
+    uint32_t perm_mode;
+    uint64_t seed;
+    float    sigma;
+    int      threads;
+} ssfgen_spec;
+
+int ssfgen_write(const char * path, const ssfgen_spec * s, char * why, int nwhy);
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,483 @@
+// TEST INFRASTRUCTURE ONLY -- a CPU restatement of the reference decode path,
+// the checker for the CUDA engine. Not linked into the product.
+//
+// Each step cites the reference line it restates. Written as plain loops from
+// the algorithm (codes unpacked to integers, one integer dot per group, one
+// float epilogue per group), not as a copy of the reference's vector code, so
+// agreement between the two means the format was read the same way twice.
+#include "sml_oracle.h"
+
+#include <fcntl.h>
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#define G 32
+
+// ------------------------------------------------------------- format bits
+
+#pragma pack(push, 1)
+typedef struct {   // the 248-byte SSF record (sml/sml-model.h:83-103)
+    char name[64];
+    uint32_t kind, rows, cols, group;
+    uint64_t off, nbytes, sd_off, sd_n, sq_off, sq_n, perm_off, perm_n, md_off, md_n, mq_off, mq_n;
+    uint64_t codes_off[4], codes_n[4];
+    uint32_t layout, nbits;
+} rec_t;
+#pragma pack(pop)
+
+// sml/sml-kernel.c:14-39: binary16 -> binary32, exact
+static float f16(uint16_t h) {
+    const uint32_t s = (uint32_t) (h & 0x8000u) << 16;
+    uint32_t e = (h >> 10) & 31u, m = h & 0x3ffu, b;
+    if (!e) {
+        if (!m) b = s;
+        else { e = 113; while (!(m & 0x400u)) { m <<= 1; e--; } b = s | (e << 23) | ((m & 0x3ffu) << 13); }
+    } else if (e == 31) b = s | 0x7f800000u | (m << 13);
+    else b = s | ((e + 112) << 23) | (m << 13);
+    float f; memcpy(&f, &b, 4); return f;
+}
+
+// sml/sml-run.c:76-96: binary32 -> binary16, round to nearest even (the KV cache)
+static uint16_t to_f16(float f) {
+    uint32_t x; memcpy(&x, &f, 4);
+    const uint32_t sign = (x >> 16) & 0x8000u;
+    const int32_t e = (int32_t) ((x >> 23) & 0xff);
+    uint32_t m = x & 0x7fffffu;
+    if (e == 0xff) return (uint16_t) (sign | 0x7c00u | (m ? 0x200u : 0u));
+    const int32_t he = e - 112;
+    if (he >= 31) return (uint16_t) (sign | 0x7c00u);
+    if (he <= 0) {
+        if (he < -10) return (uint16_t) sign;
+        m |= 0x800000u;
+        const uint32_t sh = (uint32_t) (14 - he), half = 1u << (sh - 1);
+        uint32_t v = m >> sh; const uint32_t rem = m & ((1u << sh) - 1u);
+        if (rem > half || (rem == half && (v & 1u))) v++;
+        return (uint16_t) (sign | v);
+    }
+    uint32_t v = ((uint32_t) he << 10) | (m >> 13);
+    const uint32_t rem = m & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (v & 1u))) v++;
+    return (uint16_t) (sign | v);
+}
+
+// sml/sml-kernel.h:65-96: a group's field, 8-bit or 6-bit (4 per 3 bytes)
+static int field(const uint8_t * row, int g, int six) {
+    if (!six) return row[g];
+    const uint8_t * p = row + (g >> 2) * 3;
+    const uint32_t b0 = p[0], b1 = p[1], b2 = p[2];
+    switch (g & 3) {
+    case 0: return (int) (b0 & 63u);
+    case 1: return (int) (((b0 >> 6) | (b1 << 2)) & 63u);
+    case 2: return (int) (((b1 >> 4) | (b2 << 4)) & 63u);
+    default: return (int) ((b2 >> 2) & 63u);
+    }
+}
+
+// ------------------------------------------------------------- activation
+
+// sml/sml-kernel.c:89-109
+void so_quantize_act(const float * x, int n, int8_t * q, float * scale, int32_t * sums) {
+    for (int g = 0; g < n / G; g++) {
+        float amax = 0.0f;
+        for (int i = 0; i < G; i++) { const float v = fabsf(x[g * G + i]); if (v > amax) amax = v; }
+        const float s = amax / 127.0f;
+        const float is = s > 0.0f ? 1.0f / s : 0.0f;
+        int32_t sum = 0;
+        for (int i = 0; i < G; i++) {
+            int v = (int) lrintf(x[g * G + i] * is);
+            v = v > 127 ? 127 : v < -127 ? -127 : v;
+            q[g * G + i] = (int8_t) v;
+            sum += v;
+        }
+        scale[g] = s;
+        sums[g] = sum;
+    }
+}
+
+// ------------------------------------------------------------- model
+
+struct so_model {
+    const uint8_t * base;
+    size_t size;
+    uint32_t n_layer, n_embd, n_head, n_kv, n_ff, n_vocab, flags, n_expert_used, moe_flags;
+    float theta, eps;
+    int six, minneg, hd, n_ctx, half;
+    const rec_t * recs;
+    uint64_t n_rec;
+    uint16_t * kc, * vc;
+    float * cos_t, * sin_t;
+};
+
+static const rec_t * find(const so_model * m, const char * name) {
+    for (uint64_t i = 0; i < m->n_rec; i++)
+        if (strncmp(m->recs[i].name, name, 64) == 0) return &m->recs[i];
+    return NULL;
+}
+static const rec_t * findf(const so_model * m, const char * fmt, int a, int b) {
+    char nm[80]; snprintf(nm, sizeof nm, fmt, a, b); return find(m, nm);
+}
+static const float * f32p(const so_model * m, const rec_t * r) {
+    return r ? (const float *) (m->base + r->off) : NULL;
+}
+
+so_model * so_open(const char * path, int n_ctx) {
+    const int fd = open(path, O_RDONLY);
+    if (fd < 0) return NULL;
+    struct stat st;
+    if (fstat(fd, &st)) { close(fd); return NULL; }
+    void * b = mmap(NULL, (size_t) st.st_size, PROT_READ, MAP_SHARED, fd, 0);
+    close(fd);
+    if (b == MAP_FAILED) return NULL;
+    so_model * m = (so_model *) calloc(1, sizeof *m);
+    m->base = (const uint8_t *) b;
+    m->size = (size_t) st.st_size;
+    const uint8_t * h = m->base;
+    // header fields at their HEADER_FMT offsets (tooling/sml_format.py:53-74)
+    uint32_t u[8]; memcpy(u, h + 8, 28);
+    m->n_layer = u[0]; m->n_embd = u[1]; m->n_head = u[2]; m->n_kv = u[3]; m->n_ff = u[4]; m->n_vocab = u[5];
+    memcpy(&m->theta, h + 36, 4); memcpy(&m->eps, h + 40, 4);
+    memcpy(&m->n_rec, h + 68, 8);
+    uint64_t toff; memcpy(&toff, h + 76, 8);
+    memcpy(&m->flags, h + 152, 4);
+    memcpy(&m->n_expert_used, h + 168, 4); memcpy(&m->moe_flags, h + 172, 4);
+    m->recs = (const rec_t *) (m->base + toff);
+    m->six = (m->flags & 2u) != 0;
+    m->minneg = m->six && (m->flags & 4u);
+    const rec_t * q0 = findf(m, "blk.%d.attn_q.weight", 0, 0);
+    m->hd = q0 ? (int) (q0->rows / m->n_head) : (int) (m->n_embd / m->n_head);
+    m->n_ctx = n_ctx;
+    m->half = m->hd / 2;
+    const size_t kvd = (size_t) m->n_kv * m->hd;
+    m->kc = (uint16_t *) calloc((size_t) m->n_layer * n_ctx * kvd, 2);
+    m->vc = (uint16_t *) calloc((size_t) m->n_layer * n_ctx * kvd, 2);
+    // RoPE tables, sml/sml-run.c:1383-1393
+    m->cos_t = (float *) malloc((size_t) n_ctx * m->half * 4);
+    m->sin_t = (float *) malloc((size_t) n_ctx * m->half * 4);
+    for (int p = 0; p < n_ctx; p++)
+        for (int i = 0; i < m->half; i++) {
+            const float fr = powf(m->theta, -(float) i / (float) m->half);
+            const float a = (float) p * fr;
+            m->cos_t[(size_t) p * m->half + i] = cosf(a);
+            m->sin_t[(size_t) p * m->half + i] = sinf(a);
+        }
+    return m;
+}
+
+void so_close(so_model * m) {
+    if (!m) return;
+    munmap((void *) m->base, m->size);
+    free(m->kc); free(m->vc); free(m->cos_t); free(m->sin_t);
+    free(m);
+}
+
+int so_info(const so_model * m, int * out) {
+    out[0] = (int) m->n_layer; out[1] = (int) m->n_embd; out[2] = (int) m->n_head; out[3] = (int) m->n_kv;
+    out[4] = m->hd; out[5] = (int) m->n_ff; out[6] = (int) m->n_vocab; out[7] = (int) m->flags;
+    return (int) m->n_vocab;
+}
+
+// ------------------------------------------------------------- codes
+
+// One row's codes as integers, permuted column order. Plane layouts:
+//   nibble plane  sml/sml-kernel.c:2035-2046 (quad of 4 groups = 64 bytes;
+//                 bytes 0-31 groups 4p|4p+1<<4, bytes 32-63 groups 4p+2|4p+3<<4)
+//   2-bit plane   sml/sml-kernel.h:8-16 (128 weights in 32 bytes, group g in bits 2g)
+//   1-bit plane   sml/sml-kernel.c:1986-1999 (4 bytes per group, bit j = weight j)
+// and the per-width plane order of tooling/sml_quantize.py:106.
+static void row_codes(const so_model * m, const rec_t * r, int row, uint8_t * c) {
+    const int n = (int) r->cols;
+    static const int kinds[9][3] = {{0},{0},{2},{2,1},{4},{4,1},{2,4},{4,2,1},{4,4}};
+    static const int shifts[9][3] = {{0},{0},{0},{0,2},{0},{0,4},{4,0},{0,4,6},{0,4}};
+    memset(c, 0, (size_t) n);
+    for (int p = 0; p < 3; p++) {
+        const int kd = kinds[r->nbits][p], sh = shifts[r->nbits][p];
+        if (!kd) break;
+        const uint8_t * pl = m->base + r->codes_off[p];
+        for (int i = 0; i < n; i++) {
+            const int g = i / G, j = i % G;
+            int v;
+            if (kd == 4) {
+                const uint8_t b = pl[(size_t) row * (n / 2) + (g / 4) * 64 + ((g % 4) >= 2 ? 32 : 0) + j];
+                v = (g & 1) ? (b >> 4) & 15 : b & 15;
+            } else if (kd == 2) {
+                const uint8_t b = pl[(size_t) row * (n / 4) + (g / 4) * 32 + j];
+                v = (b >> (2 * (g % 4))) & 3;
+            } else {
+                const uint8_t b = pl[(size_t) row * (n / 8) + g * 4 + j / 8];
+                v = (b >> (j % 8)) & 1;
+            }
+            c[i] = (uint8_t) (c[i] + (v << sh));
+        }
+    }
+}
+
+// Step and min of group g of a row: d*sq and md*(mq - bias), the bias 127 at
+// 8 bits, 31 at 6 bits, 63 with MINNEG (sml/sml-kernel.c:246-250, 2146-2150).
+static void group_grid(const so_model * m, const rec_t * r, int row, int g, float * step, float * mn) {
+    const int n = (int) r->cols, ng = n / G, nsb = (ng + 7) / 8;
+    const size_t frow = m->six ? (size_t) (ng / 4) * 3 : (size_t) ng;
+    const uint16_t * sd = (const uint16_t *) (m->base + r->sd_off);
+    const uint8_t * sq = m->base + r->sq_off;
+    *step = f16(sd[(size_t) row * nsb + g / 8]) * (float) field(sq + row * frow, g, m->six);
+    *mn = 0.0f;
+    if (r->mq_n) {
+        const uint16_t * md = (const uint16_t *) (m->base + r->md_off);
+        const uint8_t * mq = m->base + r->mq_off;
+        const float bias = m->six ? (m->minneg ? 63.0f : 31.0f) : 127.0f;
+        *mn = f16(md[(size_t) row * nsb + g / 8]) * ((float) field(mq + row * frow, g, m->six) - bias);
+    }
+}
+
+int so_codes_row(so_model * m, const char * name, int row, uint8_t * out) {
+    const rec_t * r = find(m, name);
+    if (!r || r->kind != 1 || r->layout != 1 || row < 0 || row >= (int) r->rows) return 0;
+    row_codes(m, r, row, out);
+    return 1;
+}
+
+// sml/sml-kernel.c:2134-2158: w = code * step + min
+int so_dequant_row(so_model * m, const char * name, int row, float * out) {
+    const rec_t * r = find(m, name);
+    if (!r || r->kind != 1 || r->layout != 1 || row < 0 || row >= (int) r->rows) return 0;
+    uint8_t * c = (uint8_t *) malloc(r->cols);
+    row_codes(m, r, row, c);
+    for (int g = 0; g < (int) r->cols / G; g++) {
+        float st, mn;
+        group_grid(m, r, row, g, &st, &mn);
+        for (int j = 0; j < G; j++) out[g * G + j] = (float) c[g * G + j] * st + mn;
+    }
+    free(c);
+    return 1;
+}
+
+// Per group: y += step*xs*dot(code, xq) + min*xs*sum(xq)   (sml/sml-kernel.c:2049-2063)
+static void matvec_rec(const so_model * m, const rec_t * r, const float * x, float * y, int row0, int row1) {
+    const int n = (int) r->cols, ng = n / G;
+    const int32_t * perm = (const int32_t *) (m->base + r->perm_off);
+    float * xg = (float *) malloc((size_t) n * 4);
+    int8_t * q = (int8_t *) malloc((size_t) n);
+    float * xs = (float *) malloc((size_t) ng * 4);
+    int32_t * sums = (int32_t *) malloc((size_t) ng * 4);
+    for (int i = 0; i < n; i++) xg[i] = x[perm[i]];          // sml/sml-kernel.c:253-255
+    so_quantize_act(xg, n, q, xs, sums);
+#pragma omp parallel for schedule(static)
+    for (int row = row0; row < row1; row++) {
+        uint8_t * c = (uint8_t *) malloc((size_t) n);
+        row_codes(m, r, row, c);
+        float acc = 0.0f;
+        for (int g = 0; g < ng; g++) {
+            int32_t d = 0;
+            for (int j = 0; j < G; j++) d += (int32_t) c[g * G + j] * (int32_t) q[g * G + j];
+            float st, mn;
+            group_grid(m, r, row, g, &st, &mn);
+            acc += st * xs[g] * (float) d;
+            if (r->mq_n) acc += mn * xs[g] * (float) sums[g];
+        }
+        y[row] = acc;
+        free(c);
+    }
+    free(xg); free(q); free(xs); free(sums);
+}
+
+static void matvec_f32(const float * w, int rows, int n, const float * x, float * y) {
+    for (int i = 0; i < rows; i++) {                         // sml/sml-run.c:3076-3081
+        double s = 0.0;
+        for (int j = 0; j < n; j++) s += (double) w[(size_t) i * n + j] * x[j];
+        y[i] = (float) s;
+    }
+}
+
+int so_matvec(so_model * m, const char * name, const float * x, float * y, int row0, int row1) {
+    const rec_t * r = find(m, name);
+    if (!r || r->kind != 1 || r->layout != 1) return 0;
+    matvec_rec(m, r, x, y, row0, row1);
+    return 1;
+}
+
+// ------------------------------------------------------------- forward pieces
+
+// sml/sml-run.c:147-152
+static void rms_norm(float * out, const float * x, const float * w, int n, float eps) {
+    double ss = 0.0;
+    for (int i = 0; i < n; i++) ss += (double) x[i] * x[i];
+    const float s = 1.0f / sqrtf((float) (ss / n) + eps);
+    for (int i = 0; i < n; i++) out[i] = x[i] * s * w[i];
+}
+
+// sml/sml-run.c:339-375, halved pairs (i, i + half)
+static void rope(const so_model * m, float * v, int nh, int pos) {
+    const float * cs = m->cos_t + (size_t) pos * m->half, * sn = m->sin_t + (size_t) pos * m->half;
+    for (int h = 0; h < nh; h++) {
+        float * x = v + (size_t) h * m->hd;
+        for (int i = 0; i < m->half; i++) {
+            const float a = x[i], b = x[i + m->half];
+            x[i] = a * cs[i] - b * sn[i];
+            x[i + m->half] = a * sn[i] + b * cs[i];
+        }
+    }
+}
+
+// sml/sml-run.c:295-325, one RMS norm per head sharing a head_dim weight
+static void qk_norm(float * v, const float * w, int nh, int hd, float eps) {
+    for (int h = 0; h < nh; h++) rms_norm(v + (size_t) h * hd, v + (size_t) h * hd, w, hd, eps);
+}
+
+// sml/sml-run.c:180-266 (scores, max-subtracted softmax with expf, weighted V)
+static void attn_head(const so_model * m, int L, int h, int pos, const float * q, float * out, float * sc) {
+    const int hd = m->hd, kvd = (int) m->n_kv * hd, rep = (int) (m->n_head / m->n_kv);
+    const size_t base = (size_t) L * m->n_ctx * kvd + (size_t) (h / rep) * hd;
+    const float inv = 1.0f / sqrtf((float) hd);
+    for (int t = 0; t <= pos; t++) {
+        const uint16_t * k = m->kc + base + (size_t) t * kvd;
+        float s = 0.0f;
+        for (int i = 0; i < hd; i++) s += q[i] * f16(k[i]);
+        sc[t] = s * inv;
+    }
+    float mx = sc[0];
+    for (int t = 1; t <= pos; t++) if (sc[t] > mx) mx = sc[t];
+    float sum = 0.0f;
+    for (int t = 0; t <= pos; t++) { sc[t] = expf(sc[t] - mx); sum += sc[t]; }
+    const float is = 1.0f / sum;
+    for (int t = 0; t <= pos; t++) sc[t] *= is;
+    for (int i = 0; i < hd; i++) out[i] = 0.0f;
+    for (int t = 0; t <= pos; t++) {
+        const uint16_t * v = m->vc + base + (size_t) t * kvd;
+        for (int i = 0; i < hd; i++) out[i] += sc[t] * f16(v[i]);
+    }
+}
+
+// sml/sml-run.c:437-455 (portable arm): silu(g) * u with libm expf
+static void silu_mul(float * g, const float * u, int n) {
+    for (int i = 0; i < n; i++) g[i] = (g[i] / (1.0f + expf(-g[i]))) * u[i];
+}
+
+// sml/sml-run.c:3009-3030: top-k on the logits (ties to the lower index), then
+// softmax over the chosen (bit 0) or over all experts
+int so_moe_route(const float * lg, int ne, int k, unsigned moe_flags, int * sel, float * w) {
+    if (k <= 0 || k > ne) k = ne;
+    if (k > 16) k = 16;
+    for (int j = 0; j < k; j++) {
+        int best = -1;
+        for (int e = 0; e < ne; e++) {
+            int taken = 0;
+            for (int q = 0; q < j; q++) taken |= sel[q] == e;
+            if (!taken && (best < 0 || lg[e] > lg[best])) best = e;
+        }
+        sel[j] = best;
+    }
+    if (moe_flags & 1u) {
+        double sum = 0.0;
+        for (int j = 0; j < k; j++) { w[j] = expf(lg[sel[j]] - lg[sel[0]]); sum += w[j]; }
+        for (int j = 0; j < k; j++) w[j] = (float) (w[j] / sum);
+    } else {
+        float mx = lg[0];
+        for (int e = 1; e < ne; e++) if (lg[e] > mx) mx = lg[e];
+        double sum = 0.0;
+        for (int e = 0; e < ne; e++) sum += expf(lg[e] - mx);
+        for (int j = 0; j < k; j++) w[j] = (float) (expf(lg[sel[j]] - mx) / sum);
+    }
+    return k;
+}
+
+// sml/sml-run.c:3071-3125 (gated experts, no shared expert)
+static void moe_ffn(so_model * m, int L, const float * xb, float * out) {
+    const int E = (int) m->n_embd;
+    const rec_t * rt = findf(m, "blk.%d.ffn_gate_inp.weight", L, 0);
+    const int ne = (int) ((uint64_t) rt->rows * rt->cols / E);
+    float * lg = (float *) malloc((size_t) ne * 4);
+    matvec_f32(f32p(m, rt), ne, E, xb, lg);
+    int sel[16]; float w[16];
+    const int k = so_moe_route(lg, ne, (int) m->n_expert_used, m->moe_flags, sel, w);
+    const rec_t * u0 = findf(m, "blk.%d.ffn_up.%d.weight", L, 0);
+    const int F = (int) u0->rows;
+    float * g = (float *) malloc((size_t) F * 4), * u = (float *) malloc((size_t) F * 4);
+    float * t = (float *) malloc((size_t) E * 4);
+    for (int i = 0; i < E; i++) out[i] = 0.0f;
+    for (int j = 0; j < k; j++) {
+        matvec_rec(m, findf(m, "blk.%d.ffn_gate.%d.weight", L, sel[j]), xb, g, 0, F);
+        matvec_rec(m, findf(m, "blk.%d.ffn_up.%d.weight", L, sel[j]), xb, u, 0, F);
+        silu_mul(g, u, F);
+        matvec_rec(m, findf(m, "blk.%d.ffn_down.%d.weight", L, sel[j]), g, t, 0, E);
+        for (int i = 0; i < E; i++) out[i] += w[j] * t[i];
+    }
+    free(lg); free(g); free(u); free(t);
+}
+
+static void add_bias(float * y, const float * b, int n) { if (b) for (int i = 0; i < n; i++) y[i] += b[i]; }
+
+// sml/sml-run.c:3243-3523, the dense / MoE decoder branch
+int so_forward(so_model * m, int tok, int pos, float * logits) {
+    if (pos >= m->n_ctx || tok < 0 || tok >= (int) m->n_vocab) return 0;
+    const int E = (int) m->n_embd, hd = m->hd, nh = (int) m->n_head, nkv = (int) m->n_kv;
+    const int qd = nh * hd, kvd = nkv * hd;
+    const int wide = (int) (m->n_ff > (uint32_t) E ? m->n_ff : (uint32_t) E) > qd
+                   ? (int) (m->n_ff > (uint32_t) E ? m->n_ff : (uint32_t) E) : qd;
+    float * x = (float *) calloc((size_t) E, 4), * xb = (float *) calloc((size_t) wide, 4);
+    float * q = (float *) malloc((size_t) qd * 4), * k = (float *) malloc((size_t) kvd * 4);
+    float * v = (float *) malloc((size_t) kvd * 4), * att = (float *) malloc((size_t) qd * 4);
+    float * hb = (float *) malloc((size_t) wide * 4), * hb2 = (float *) malloc((size_t) wide * 4);
+    float * sc = (float *) malloc((size_t) m->n_ctx * 4);
+    // embedding row, dequantized, scattered back through its perm (:3283-3338)
+    const rec_t * emb = find(m, "token_embd.weight");
+    so_dequant_row(m, "token_embd.weight", tok, xb);
+    const int32_t * pe = (const int32_t *) (m->base + emb->perm_off);
+    for (int i = 0; i < E; i++) x[pe[i]] = xb[i];
+    for (int L = 0; L < (int) m->n_layer; L++) {
+        rms_norm(xb, x, f32p(m, findf(m, "blk.%d.attn_norm.weight", L, 0)), E, m->eps);
+        matvec_rec(m, findf(m, "blk.%d.attn_q.weight", L, 0), xb, q, 0, qd);
+        matvec_rec(m, findf(m, "blk.%d.attn_k.weight", L, 0), xb, k, 0, kvd);
+        matvec_rec(m, findf(m, "blk.%d.attn_v.weight", L, 0), xb, v, 0, kvd);
+        add_bias(q, f32p(m, findf(m, "blk.%d.attn_q.bias", L, 0)), qd);
+        add_bias(k, f32p(m, findf(m, "blk.%d.attn_k.bias", L, 0)), kvd);
+        add_bias(v, f32p(m, findf(m, "blk.%d.attn_v.bias", L, 0)), kvd);
+        const float * qn = f32p(m, findf(m, "blk.%d.attn_q_norm.weight", L, 0));
+        const float * kn = f32p(m, findf(m, "blk.%d.attn_k_norm.weight", L, 0));
+        if (qn) qk_norm(q, qn, nh, hd, m->eps);
+        if (kn) qk_norm(k, kn, nkv, hd, m->eps);
+        rope(m, q, nh, pos);
+        rope(m, k, nkv, pos);
+        const size_t at = ((size_t) L * m->n_ctx + pos) * kvd;   // :3414-3415
+        for (int i = 0; i < kvd; i++) { m->kc[at + i] = to_f16(k[i]); m->vc[at + i] = to_f16(v[i]); }
+        for (int h = 0; h < nh; h++) attn_head(m, L, h, pos, q + (size_t) h * hd, att + (size_t) h * hd, sc);
+        matvec_rec(m, findf(m, "blk.%d.attn_output.weight", L, 0), att, hb2, 0, E);
+        for (int i = 0; i < E; i++) x[i] += hb2[i];
+        rms_norm(xb, x, f32p(m, findf(m, "blk.%d.ffn_norm.weight", L, 0)), E, m->eps);
+        if (findf(m, "blk.%d.ffn_gate_inp.weight", L, 0)) {
+            moe_ffn(m, L, xb, hb2);
+            for (int i = 0; i < E; i++) x[i] += hb2[i];
+            continue;
+        }
+        const int F = (int) m->n_ff;
+        matvec_rec(m, findf(m, "blk.%d.ffn_gate.weight", L, 0), xb, hb, 0, F);
+        matvec_rec(m, findf(m, "blk.%d.ffn_up.weight", L, 0), xb, hb2, 0, F);
+        silu_mul(hb, hb2, F);
+        matvec_rec(m, findf(m, "blk.%d.ffn_down.weight", L, 0), hb, xb, 0, E);
+        for (int i = 0; i < E; i++) x[i] += xb[i];
+    }
+    rms_norm(xb, x, f32p(m, find(m, "output_norm.weight")), E, m->eps);
+    const rec_t * head = find(m, "output.weight");
+    matvec_rec(m, head ? head : emb, xb, logits, 0, (int) m->n_vocab);
+    free(x); free(xb); free(q); free(k); free(v); free(att); free(hb); free(hb2); free(sc);
+    int best = 0;                                                  // sml/sml-run.c:3539-3544
+    for (int i = 1; i < (int) m->n_vocab; i++) if (logits[i] > logits[best]) best = i;
+    return best;
+}
+
+int so_decode(so_model * m, const int * prompt, int np, int ngen, int * ids, float * logits) {
+    const int nv = (int) m->n_vocab;
+    float * lg = (float *) malloc((size_t) nv * 4);
+    int t = 0;
+    for (int i = 0; i < np; i++) t = so_forward(m, prompt[i], i, lg);
+    for (int g = 0; g < ngen; g++) {
+        ids[g] = t;
+        if (logits) memcpy(logits + (size_t) g * nv, lg, (size_t) nv * 4);
+        if (g + 1 < ngen) t = so_forward(m, t, np + g, lg);
+    }
+    free(lg);
+    return 1;
+}

@@ -1,0 +1,38 @@
+// TEST INFRASTRUCTURE ONLY. A plain-C restatement of the reference's decode
+// path over SSF flat tensors, used by tests/ as the checker for the CUDA
+// engine and pinned itself against the reference build (oracle/_ref) and the
+// golden vectors in tests/golden/. Never linked into, or called by, the product.
+#pragma once
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+// sml/sml-kernel.c:89-109 (scalar arm of sml_quantize_act)
+void so_quantize_act(const float * x, int n, int8_t * q, float * scale, int32_t * sums);
+
+typedef struct so_model so_model;
+
+so_model * so_open(const char * path, int n_ctx);
+void       so_close(so_model * m);
+int        so_info(const so_model * m, int * out);   // same fields as refh_info
+
+// y[row0..row1) of one named tensor for an activation x in natural order.
+int so_matvec(so_model * m, const char * name, const float * x, float * y, int row0, int row1);
+// One dequantized row (permuted column order).
+int so_dequant_row(so_model * m, const char * name, int row, float * out);
+// Unpacked integer codes of one row (permuted column order): bit-exact view of the planes.
+int so_codes_row(so_model * m, const char * name, int row, uint8_t * out);
+
+// Decode step: logits for token at absolute position pos (KV cache kept inside).
+int so_forward(so_model * m, int tok, int pos, float * logits);
+int so_decode(so_model * m, const int * prompt, int np, int ngen, int * ids, float * logits);
+
+// sml/sml-run.c:2925-3040, the softmax-top-k branch (moe_flags bit 0 = renormalise)
+int so_moe_route(const float * lg, int ne, int k, unsigned moe_flags, int * sel, float * w);
+
+#ifdef __cplusplus
+}
+#endif

@@ -1,0 +1,253 @@
+"""sheep_b200: a B200-native decode engine for SML's SSF models.
+
+The product is libsheep_b200.so (C ABI, include/sml-gpu.h and
+include/sheep_b200.h): CUDA kernels for sm_100a behind the reference's
+sml_gpu_* entry points. This module is a thin ctypes mirror of that ABI for
+Python callers, tests and the bench. It never computes anything itself, and it
+fails loudly when the library is missing rather than falling back to the CPU.
+"""
+import ctypes
+import os
+
+import numpy as np
+
+from .configs import CONFIGS, spec_for  # noqa: F401
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+# SHEEP_B200_LIB selects another build of the same ABI (the checked build).
+LIB_PATH = os.environ.get("SHEEP_B200_LIB") or os.path.join(_HERE, "lib", "libsheep_b200.so")
+_lib = None
+
+
+class SsfSpec(ctypes.Structure):
+    """ssfgen_spec (include/sheep_b200.h)."""
+    _fields_ = [(n, ctypes.c_uint32) for n in
+                "n_layer n_embd n_head n_head_kv head_dim n_ff n_vocab".split()] + \
+               [("rope_theta", ctypes.c_float), ("rms_eps", ctypes.c_float)] + \
+               [(n, ctypes.c_uint32) for n in
+                "tied qkv_bias qk_norm nbits emb_nbits scale6 minneg "
+                "n_expert n_expert_used moe_flags expert_ff perm_mode".split()] + \
+               [("seed", ctypes.c_uint64), ("sigma", ctypes.c_float), ("threads", ctypes.c_int)]
+
+
+def lib():
+    """The loaded engine library; raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise RuntimeError(f"{LIB_PATH} is missing: build it with `python -m sheep_b200.build` "
+                           "(there is no CPU fallback)")
+    L = ctypes.CDLL(LIB_PATH)
+    vp, cp, ip, fp = ctypes.c_void_p, ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(ctypes.c_float)
+    sig = {
+        "sml_gpu_open": (ip, [cp, ip, ip, ip, cp, ip]),
+        "sml_gpu_prefill": (fp, [vp, ip, ip]),
+        "sml_gpu_step": (fp, [ip, ip]),
+        "sml_gpu_layers": (ip, [vp]),
+        "sml_gpu_prompt_mode": (None, [ip]),
+        "sml_gpu_decode_cpu": (ip, [ip]),
+        "sml_gpu_set_middle": (None, [ip, vp]),
+        "sml_gpu_engine": (vp, []),
+        "sml_gpu_close": (None, []),
+        "sb_open": (vp, [cp, ip, cp, ip]),
+        "sb_close": (None, [vp]),
+        "sb_info": (None, [vp, vp]),
+        "sb_bytes_per_token": (ctypes.c_uint64, [vp]),
+        "sb_step": (fp, [vp, ip, ip]),
+        "sb_prefill": (fp, [vp, vp, ip, ip]),
+        "sb_generate": (ip, [vp, vp, ip, ip, vp]),
+        "sb_generate_timed": (ip, [vp, vp, ip, ip, vp, fp]),
+        "sb_device_logits": (vp, [vp]),
+        "sb_launches_per_token": (ip, [vp]),
+        "sb_last_error": (cp, []),
+        "sb_tset_open": (vp, [cp, cp, ip]),
+        "sb_tset_close": (None, [vp]),
+        "sb_tset_shape": (ip, [vp, cp, vp, vp, vp]),
+        "sb_tset_bytes": (ctypes.c_ulonglong, [vp, cp]),
+        "sb_tset_gemv_dev": (ip, [vp, cp, vp, ip, vp, vp]),
+        "sb_tset_matvec": (ip, [vp, cp, vp, vp, vp, vp, vp]),
+        "sb_tset_dequant_rows": (ip, [vp, cp, vp, ip, vp]),
+        "sb_quantize_act": (ip, [vp, vp, ip, vp, vp, vp, vp]),
+        "ssfgen_write": (ip, [cp, vp, cp, ip]),
+    }
+    for name, (res, args) in sig.items():
+        f = getattr(L, name)
+        f.restype = res
+        f.argtypes = args
+    _lib = L
+    return L
+
+
+def _p(a):
+    return a.ctypes.data_as(ctypes.c_void_p) if a is not None else None
+
+
+def write_model(path, **spec):
+    """Write a seeded synthetic SSF model (ssfgen_write)."""
+    s = SsfSpec()
+    for k, v in spec.items():
+        setattr(s, k, v)
+    why = ctypes.create_string_buffer(512)
+    if not lib().ssfgen_write(path.encode(), ctypes.byref(s), why, 512):
+        raise RuntimeError(why.value.decode())
+    return path
+
+
+class Engine:
+    """A model on the GPU with its KV cache (the handle form of sml-gpu.h)."""
+
+    def __init__(self, path, n_ctx=256):
+        why = ctypes.create_string_buffer(512)
+        self.h = lib().sb_open(path.encode(), n_ctx, why, 512)
+        if not self.h:
+            raise RuntimeError(f"sb_open: {why.value.decode()}")
+        info = (ctypes.c_int * 12)()
+        lib().sb_info(self.h, info)
+        (self.n_layer, self.n_embd, self.n_head, self.n_head_kv, self.head_dim, self.n_ff,
+         self.n_vocab, self.n_ctx) = info[:8]
+        self.bytes_per_token = int(lib().sb_bytes_per_token(self.h))
+
+    def step(self, tok, pos):
+        p = lib().sb_step(self.h, int(tok), int(pos))
+        if not p:
+            raise RuntimeError(f"sb_step failed: {lib().sb_last_error().decode()}")
+        return np.ctypeslib.as_array(p, shape=(self.n_vocab,)).copy()
+
+    def prefill(self, ids, pos0=0):
+        ids = np.ascontiguousarray(ids, dtype=np.int32)
+        p = lib().sb_prefill(self.h, _p(ids), int(pos0), len(ids))
+        if not p:
+            raise RuntimeError(f"sb_prefill failed: {lib().sb_last_error().decode()}")
+        return np.ctypeslib.as_array(p, shape=(self.n_vocab,)).copy()
+
+    def generate(self, prompt, ngen, timed=False):
+        prompt = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(ngen, np.int32)
+        ms = ctypes.c_float(0)
+        if timed:
+            ok = lib().sb_generate_timed(self.h, _p(prompt), len(prompt), ngen, _p(out), ctypes.byref(ms))
+        else:
+            ok = lib().sb_generate(self.h, _p(prompt), len(prompt), ngen, _p(out))
+        if not ok:
+            raise RuntimeError(f"sb_generate failed: {lib().sb_last_error().decode()}")
+        return (out, ms.value) if timed else out
+
+    @property
+    def launches_per_token(self):
+        return lib().sb_launches_per_token(self.h)
+
+    def close(self):
+        if self.h:
+            lib().sb_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class TensorSet:
+    """Every flat tensor of an SSF file on the GPU, for kernel-level calls."""
+
+    def __init__(self, path):
+        why = ctypes.create_string_buffer(512)
+        self.h = lib().sb_tset_open(path.encode(), why, 512)
+        if not self.h:
+            raise RuntimeError(f"sb_tset_open: {why.value.decode()}")
+
+    def shape(self, name):
+        r, c, b = ctypes.c_int(), ctypes.c_int(), ctypes.c_int()
+        if not lib().sb_tset_shape(self.h, name.encode(), ctypes.byref(r), ctypes.byref(c), ctypes.byref(b)):
+            raise KeyError(name)
+        return r.value, c.value, b.value
+
+    def nbytes(self, name):
+        return int(lib().sb_tset_bytes(self.h, name.encode()))
+
+    def matvec(self, name, x):
+        rows, cols, _ = self.shape(name)
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        assert x.shape == (cols,)
+        y = np.zeros(rows, np.float32)
+        q = np.zeros(cols, np.int8)
+        s = np.zeros(cols // 32, np.float32)
+        sums = np.zeros(cols // 32, np.int32)
+        if not lib().sb_tset_matvec(self.h, name.encode(), _p(x), _p(y), _p(q), _p(s), _p(sums)):
+            raise RuntimeError(f"sb_tset_matvec failed: {lib().sb_last_error().decode()}")
+        return y, q, s, sums
+
+    def dequant_rows(self, name, rows):
+        _, cols, _ = self.shape(name)
+        rows = np.ascontiguousarray(rows, dtype=np.int32)
+        out = np.zeros((len(rows), cols), np.float32)
+        if not lib().sb_tset_dequant_rows(self.h, name.encode(), _p(rows), len(rows), _p(out)):
+            raise RuntimeError("sb_tset_dequant_rows failed")
+        return out
+
+    def gemv_dev(self, name, x_ptr, nb, y_ptr, stream=0):
+        if not lib().sb_tset_gemv_dev(self.h, name.encode(), x_ptr, nb, y_ptr, stream):
+            raise RuntimeError("sb_tset_gemv_dev failed")
+
+    def close(self):
+        if self.h:
+            lib().sb_tset_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+# ----------------------------------------------------------------- sml-gpu.h mirror
+# Same names, argument meaning and error behaviour as the reference's C API
+# (sml/sml-gpu.h:11-34), for Python callers.
+
+def sml_gpu_open(path, n_ctx=0, threads=0, gpu_layers=0):
+    """Returns (1, "") or (0, why)."""
+    why = ctypes.create_string_buffer(512)
+    ok = lib().sml_gpu_open(path.encode(), n_ctx, threads, gpu_layers, why, 512)
+    return ok, why.value.decode()
+
+
+def _n_vocab():
+    info = (ctypes.c_int * 12)()
+    lib().sb_info(lib().sml_gpu_engine(), info)
+    return info[6]
+
+
+def sml_gpu_prefill(ids, pos0, n=None):
+    ids = np.ascontiguousarray(ids, dtype=np.int32)
+    p = lib().sml_gpu_prefill(_p(ids), pos0, len(ids) if n is None else n)
+    return None if not p else np.ctypeslib.as_array(p, shape=(_n_vocab(),)).copy()
+
+
+def sml_gpu_step(tok, pos):
+    p = lib().sml_gpu_step(tok, pos)
+    return None if not p else np.ctypeslib.as_array(p, shape=(_n_vocab(),)).copy()
+
+
+def sml_gpu_layers():
+    of = ctypes.c_int()
+    n = lib().sml_gpu_layers(ctypes.byref(of))
+    return n, of.value
+
+
+def sml_gpu_prompt_mode(level):
+    lib().sml_gpu_prompt_mode(level)
+
+
+def sml_gpu_decode_cpu(on):
+    return lib().sml_gpu_decode_cpu(on)
+
+
+def sml_gpu_set_middle(layers, fn=None):
+    lib().sml_gpu_set_middle(layers, None)
+
+
+def sml_gpu_close():
+    lib().sml_gpu_close()

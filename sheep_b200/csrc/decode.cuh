@@ -1,0 +1,338 @@
+// Decode-step kernels: one token through the stack, device-resident.
+//
+// Per layer (the reference's f2_layer order, sml/sml-gpu-fwd.c:604-633, and the
+// CPU forward sml/sml-run.c:3340-3520):
+//   k_tgemv<QKV>   RMSNorm + gather + int8 quant (prologue), q|k|v rows, + bias
+//   k_attn         Q/K norm (if any), RoPE, fp16 KV write, split-position attention
+//   k_tgemv<O>     gather + quant of the attention output, o rows, x += y
+//   k_tgemv<FFN>   RMSNorm + quant, gate and up rows, silu(g)*u written in the
+//                  down projection's permuted order
+//   k_tgemv<DOWN>  quant, down rows, x += y
+// then k_tgemv<HEAD> (final norm, head rows, logits, greedy argmax). The GEMV
+// kernels live in tgemv.cuh; this file holds the rest.
+//
+// Every kernel signals its dependents at entry (programmatic dependent
+// launch) and every CTA calls pdl_wait() before it can exit: a grid may only
+// complete after its predecessor has.
+#pragma once
+
+#include "qgemv.cuh"
+
+namespace sb {
+
+enum GemvMode { GM_QKV = 0, GM_O = 1, GM_FFN = 2, GM_DOWN = 3, GM_HEAD = 4, GM_PLAIN = 5 };
+
+// Shared memory for the activation of a width-n input.
+__host__ __device__ inline size_t act_smem_bytes(int n) {
+    return (size_t) n + (size_t) (n / kGroup) * 8 + 64;
+}
+
+SB_DEV ActS act_carve(uint8_t * smem, int n) {
+    ActS a;
+    a.q = reinterpret_cast<int8_t *>(smem);
+    a.xs = reinterpret_cast<float *>(smem + n);
+    a.xsum = a.xs + n / kGroup;
+    a.n = n;
+    return a;
+}
+
+SB_DEV float silu_mul(float g, float u) {
+    // sml/sml-run.c:450-455: (g / (1 + expf(-g))) * u
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
+}
+
+// ---------------------------------------------------------------- embedding
+
+// One code of row `row`, column i (permuted order), from every plane.
+template <int NB>
+SB_DEV int code_at(const QT & t, int row, int i) {
+    const int n = t.cols, grp = i / kGroup, j = i % kGroup;
+    auto nib = [&](const uint8_t * pl) {
+        const uint8_t b = pl[(size_t) row * (n / 2) + (grp / 4) * 64 + ((grp & 3) >= 2 ? 32 : 0) + j];
+        return (grp & 1) ? (b >> 4) & 15 : b & 15;
+    };
+    auto two = [&](const uint8_t * pl) {
+        return (pl[(size_t) row * (n / 4) + (grp / 4) * 32 + j] >> (2 * (grp & 3))) & 3;
+    };
+    auto one = [&](const uint8_t * pl) {
+        return (pl[(size_t) row * (n / 8) + grp * 4 + j / 8] >> (j & 7)) & 1;
+    };
+    switch (NB) {
+    case 2: return two(t.pl[0]);
+    case 3: return two(t.pl[0]) + (one(t.pl[1]) << 2);
+    case 4: return nib(t.pl[0]);
+    case 5: return nib(t.pl[0]) + (one(t.pl[1]) << 4);
+    case 6: return (two(t.pl[0]) << 4) + nib(t.pl[1]);
+    case 7: return nib(t.pl[0]) + (two(t.pl[1]) << 4) + (one(t.pl[2]) << 6);
+    default: return nib(t.pl[0]) + (nib(t.pl[1]) << 4);
+    }
+}
+
+template <int SIX>
+SB_DEV int field_at(const uint8_t * f, int frow, int row, int grp) {
+    if (!SIX) return f[(size_t) row * frow + grp];
+    const uint8_t * p = f + (size_t) row * frow + (grp >> 2) * 3;
+    const uint32_t b0 = p[0], b1 = p[1], b2 = p[2];
+    switch (grp & 3) {
+    case 0: return (int) (b0 & 63u);
+    case 1: return (int) (((b0 >> 6) | (b1 << 2)) & 63u);
+    case 2: return (int) (((b1 >> 4) | (b2 << 4)) & 63u);
+    default: return (int) ((b2 >> 2) & 63u);
+    }
+}
+
+// w = code * (d * sq) + md * (mq - bias), multiply and add rounded separately
+// (sml/sml-kernel.c:2146-2157).
+template <int NB, int SIX>
+SB_DEV float dequant_at(const QT & t, int row, int i) {
+    const int grp = i / kGroup;
+    const float step = __fmul_rn(h2f(t.sd[(size_t) row * t.nsb + grp / kGps]), (float) field_at<SIX>(t.sq, t.frow, row, grp));
+    float mn = 0.0f;
+    if (t.has_min)
+        mn = __fmul_rn(h2f(t.md[(size_t) row * t.nsb + grp / kGps]),
+                       __fsub_rn((float) field_at<SIX>(t.mq, t.frow, row, grp), t.mbias));
+    return __fadd_rn(__fmul_rn((float) code_at<NB>(t, row, i), step), mn);
+}
+
+// x[perm[i]] = dequant(emb[tok], i): the embedding row scattered back to
+// natural order (sml/sml-run.c:3332-3336). tok is read from device memory so a
+// captured graph replays the greedy loop without the host.
+template <int NB, int SIX>
+__global__ void k_embed(const __grid_constant__ QT t, const int * dtok, float * x, int * err) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= t.cols) return;
+    const int tok = *dtok;
+    if (!SB_CHECK(err, tok >= 0 && tok < t.rows, 301)) return;
+    x[t.perm[i]] = dequant_at<NB, SIX>(t, tok, i);
+}
+
+// Standalone activation quantization (sml_quantize_act after sml_gather):
+// q in natural group order. One warp per group.
+static __global__ void k_quant_act(const float * x, const int32_t * perm, int n, int8_t * q, float * s, int32_t * sums) {
+    const int lane = threadIdx.x & 31;
+    const int grp = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (grp >= n / kGroup) return;
+    const int i = grp * kGroup + lane;
+    const float v = x[perm ? perm[i] : i];
+    const float amax = warp_max(fabsf(v));
+    const float sc = __fdiv_rn(amax, 127.0f);
+    const float is = sc > 0.0f ? __fdiv_rn(1.0f, sc) : 0.0f;
+    int c = __float2int_rn(__fmul_rn(v, is));
+    c = c > 127 ? 127 : c < -127 ? -127 : c;
+    const int sum = warp_sum_i(c);
+    q[i] = (int8_t) c;
+    if (lane == 0) { s[grp] = sc; sums[grp] = sum; }
+}
+
+template <int NB, int SIX>
+__global__ void k_dequant_rows(const __grid_constant__ QT t, const int * rows, int nrows, float * out) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    const int r = blockIdx.y;
+    if (i >= t.cols || r >= nrows) return;
+    out[(size_t) r * t.cols + i] = dequant_at<NB, SIX>(t, rows[r], i);
+}
+
+// ---------------------------------------------------------------- attention
+
+struct AttnArgs {
+    const float * qkv;       // [q | k | v] of this token, before RoPE
+    int n_head, n_kv, hd, qd, kvd;
+    const float * qn, * kn;  // Q/K norm gains (per head, hd long) or NULL
+    float eps;
+    const float * rcos, * rsin;   // [n_ctx][hd/2] RoPE tables
+    uint16_t * kc, * vc;     // this layer's cache, [n_ctx][kvd] fp16
+    int n_ctx;
+    const int * pos;
+    int chunk;               // positions per CTA
+    float scale;             // 1/sqrt(hd)
+    float * part;            // [n_head][max_chunks][hd + 2]
+    unsigned * cnt;          // [n_head]
+    int max_chunks;
+    float * out;             // [qd] attention output
+    int * err;
+    unsigned long long * trace;
+    int launch_id;
+};
+
+constexpr int kAttnThreads = 256;
+
+// Per-head RMS norm (sml/sml-run.c:295-325, one head at a time) then RoPE by
+// halved pairs (sml/sml-run.c:339-375) of a 128-thread block's head vector.
+SB_DEV void norm_rope(float * v, const float * w, float eps, int hd, const float * cs, const float * sn, double * red) {
+    if (w) {
+        const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+        double s = 0.0;
+        for (int i = threadIdx.x; i < hd; i += blockDim.x) s += (double) v[i] * (double) v[i];
+        s = warp_sum_d(s);
+        if (lane == 0) red[wp] = s;
+        __syncthreads();
+        double ss = 0.0;
+        for (int k = 0; k < (int) (blockDim.x >> 5); k++) ss += red[k];
+        const float f = __fdiv_rn(1.0f, sqrtf(__fadd_rn((float) (ss / hd), eps)));
+        __syncthreads();
+        for (int i = threadIdx.x; i < hd; i += blockDim.x) v[i] = __fmul_rn(__fmul_rn(v[i], f), w[i]);
+        __syncthreads();
+    }
+    const int half = hd / 2;
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+        const float a = v[i], b = v[i + half];
+        v[i] = a * cs[i] - b * sn[i];
+        v[i + half] = a * sn[i] + b * cs[i];
+    }
+    __syncthreads();
+}
+
+// Shared memory of k_attn for head width hd and `chunk` positions.
+__host__ __device__ inline size_t attn_smem_bytes(int hd, int chunk) {
+    return (size_t) (4 * hd + chunk) * 4 + (size_t) chunk * (hd + 4) * 2 + (size_t) chunk * hd * 2;
+}
+
+// One CTA per (query head, chunk of positions): RoPE of q and of the new key,
+// the fp16 KV write at pos (by one CTA per KV head), then attention over the
+// chunk. The chunk's keys and values and the position's RoPE row are loaded
+// into shared memory with every load issued at once. Scores take two threads
+// per position, alternating 4-byte words of a key row padded to hd+4 halves
+// (a warp's 32 reads fall in 32 banks); weighted values one thread per
+// dimension. Chunks are combined by the last CTA of the head, in chunk order
+// (flash-decoding partials).
+static __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_constant__ AttnArgs g) {
+    extern __shared__ __align__(16) float sm[];
+    __shared__ double red[kAttnThreads / 32];
+    __shared__ float wred[kAttnThreads / 32];
+    __shared__ unsigned last_flag;
+    pdl_launch_dependents();
+    SB_MARK(g.trace, g.launch_id, 0);
+    pdl_wait();
+    SB_MARK(g.trace, g.launch_id, 1);
+    const int h = blockIdx.x, c = blockIdx.y, hd = g.hd, tid = threadIdx.x;
+    const int pos = *g.pos;
+    const int nchunk = pos / g.chunk + 1;
+    if (c >= nchunk) return;
+    const int t0 = c * g.chunk, t1 = min(pos + 1, t0 + g.chunk), nt = t1 - t0;
+    if (!SB_CHECK(g.err, pos >= 0 && pos < g.n_ctx && nchunk <= g.max_chunks && nt <= g.chunk && (hd & 7) == 0, 201))
+        return;
+    const int rep = g.n_head / g.n_kv, kvh = h / rep;
+    float * q = sm, * kn = sm + hd, * vn = sm + 2 * hd, * cs = sm + 3 * hd, * sn = cs + hd / 2;
+    float * sc = sm + 4 * hd;
+    uint16_t * Ks = reinterpret_cast<uint16_t *>(sm + 4 * hd + g.chunk);   // [chunk][hd + 4]
+    uint16_t * Vs = Ks + (size_t) g.chunk * (hd + 4);                        // [chunk][hd]
+    const int kst = hd + 4;
+    // every load of this CTA issued before any is used
+    for (int i = tid; i < hd; i += blockDim.x) {
+        q[i] = g.qkv[h * hd + i];
+        kn[i] = g.qkv[g.qd + kvh * hd + i];
+        vn[i] = g.qkv[g.qd + g.kvd + kvh * hd + i];
+        if (i < hd / 2) {
+            cs[i] = g.rcos[(size_t) pos * (hd / 2) + i];
+            sn[i] = g.rsin[(size_t) pos * (hd / 2) + i];
+        }
+    }
+    const int per = hd / 8;   // 16-byte pieces per row
+    // in batches of kB pieces per thread: all of a batch's loads before its stores
+    constexpr int kB = 8;
+    for (int b0 = 0; b0 < nt * per; b0 += kB * (int) blockDim.x) {
+        uint4 kv[kB], vv[kB];
+#pragma unroll
+        for (int r = 0; r < kB; r++) {
+            const int idx = b0 + r * blockDim.x + tid;
+            const int t = t0 + idx / per, part = idx % per;
+            if (idx < nt * per && t != pos) {
+                const size_t at = (size_t) t * g.kvd + (size_t) kvh * hd + part * 8;
+                kv[r] = *reinterpret_cast<const uint4 *>(g.kc + at);
+                vv[r] = *reinterpret_cast<const uint4 *>(g.vc + at);
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < kB; r++) {
+            const int idx = b0 + r * blockDim.x + tid;
+            const int t = t0 + idx / per, part = idx % per;
+            if (idx < nt * per && t != pos) {
+                *reinterpret_cast<uint2 *>(Ks + (size_t) (t - t0) * kst + part * 8) = make_uint2(kv[r].x, kv[r].y);
+                *reinterpret_cast<uint2 *>(Ks + (size_t) (t - t0) * kst + part * 8 + 4) = make_uint2(kv[r].z, kv[r].w);
+                *reinterpret_cast<uint4 *>(Vs + (size_t) (t - t0) * hd + part * 8) = vv[r];
+            }
+        }
+    }
+    __syncthreads();
+    SB_MARK(g.trace, g.launch_id, 2);
+    norm_rope(q, g.qn, g.eps, hd, cs, sn, red);
+    norm_rope(kn, g.kn, g.eps, hd, cs, sn, red);
+    // the new key and value as the cache stores them (fp16, round to nearest even)
+    const size_t at = (size_t) pos * g.kvd + (size_t) kvh * hd;
+    const bool mine = pos >= t0 && pos < t1;
+    for (int i = tid; i < hd; i += blockDim.x) {
+        const uint16_t kh = f2h(kn[i]), vh = f2h(vn[i]);
+        if (mine) { Ks[(size_t) (pos - t0) * kst + i] = kh; Vs[(size_t) (pos - t0) * hd + i] = vh; }
+        if (h % rep == 0 && mine) { g.kc[at + i] = kh; g.vc[at + i] = vh; }
+    }
+    __syncthreads();
+    // scores, two threads per position (sml/sml-run.c:180-235: dot * 1/sqrt(hd))
+    const int lane = tid & 31, wp = tid >> 5, nw = blockDim.x >> 5;
+    for (int base = 0; base < nt; base += blockDim.x / 2) {
+        const int p = base + (tid >> 1), half = tid & 1;
+        float s = 0.0f;
+        if (p < nt) {
+            const uint32_t * kr = reinterpret_cast<const uint32_t *>(Ks + (size_t) p * kst);
+            for (int i = half; i < hd / 2; i += 2) {
+                const uint32_t w2 = kr[i];
+                s += q[2 * i] * h2f((uint16_t) (w2 & 0xffffu));
+                s += q[2 * i + 1] * h2f((uint16_t) (w2 >> 16));
+            }
+        }
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        if (p < nt && half == 0) sc[p] = s * g.scale;
+    }
+    __syncthreads();
+    SB_MARK(g.trace, g.launch_id, 3);
+    float m = -INFINITY;
+    for (int t = tid; t < nt; t += blockDim.x) m = fmaxf(m, sc[t]);
+    m = warp_max(m);
+    if (lane == 0) wred[wp] = m;
+    __syncthreads();
+    m = wred[0];
+    for (int k = 1; k < nw; k++) m = fmaxf(m, wred[k]);
+    __syncthreads();
+    float l = 0.0f;
+    for (int t = tid; t < nt; t += blockDim.x) { const float e = expf(sc[t] - m); sc[t] = e; l += e; }
+    l = warp_sum(l);
+    if (lane == 0) wred[wp] = l;
+    __syncthreads();
+    l = 0.0f;
+    for (int k = 0; k < nw; k++) l += wred[k];
+    SB_MARK(g.trace, g.launch_id, 4);
+    // weighted values: one dimension per thread
+    for (int i = tid; i < hd; i += blockDim.x) {
+        float o = 0.0f;
+        for (int t = 0; t < nt; t++) o += sc[t] * h2f(Vs[(size_t) t * hd + i]);
+        if (nchunk == 1) g.out[h * hd + i] = o / l;
+        else g.part[((size_t) h * g.max_chunks + c) * (hd + 2) + 2 + i] = o;
+    }
+    SB_MARK(g.trace, g.launch_id, 5);
+    if (nchunk == 1) return;
+    if (tid == 0) {
+        g.part[((size_t) h * g.max_chunks + c) * (hd + 2)] = m;
+        g.part[((size_t) h * g.max_chunks + c) * (hd + 2) + 1] = l;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last_flag = atomicAdd(&g.cnt[h], 1u) == (unsigned) nchunk - 1;
+    __syncthreads();
+    if (!last_flag) return;
+    __threadfence();
+    // the last chunk of this head combines every chunk, in chunk order
+    const volatile float * P = g.part + (size_t) h * g.max_chunks * (hd + 2);
+    float M = -INFINITY;
+    for (int k = 0; k < nchunk; k++) M = fmaxf(M, P[k * (hd + 2)]);
+    float Lsum = 0.0f;
+    for (int k = 0; k < nchunk; k++) Lsum += P[k * (hd + 2) + 1] * expf(P[k * (hd + 2)] - M);
+    for (int i = tid; i < hd; i += blockDim.x) {
+        float o = 0.0f;
+        for (int k = 0; k < nchunk; k++) o += P[k * (hd + 2) + 2 + i] * expf(P[k * (hd + 2)] - M);
+        g.out[h * hd + i] = o / Lsum;
+    }
+    if (tid == 0) g.cnt[h] = 0;
+}
+
+}  // namespace sb

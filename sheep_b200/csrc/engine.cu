@@ -1,0 +1,551 @@
+// Host engine for the decode path: upload, plan, graph capture, step API.
+//
+// Replaces the reference's GPU host driver (sml/sml-gpu-fwd.c: gpu_setup :1789,
+// gpu_forward :1643, graph_token :636, sml_gpu_open/step/prefill :2353-2412)
+// with the Linux CUDA runtime: one arena for the model, one stream, one
+// captured graph per token whose kernels chain by programmatic dependent
+// launch, and the greedy choice made on the device so a generation loop is
+// graph replays with no host round trip.
+#include "tgemv.cuh"
+#include "sheep_b200.h"
+#include "ssf.h"
+#include "upload.h"
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+#include <unordered_map>
+#include <vector>
+
+using namespace sb;
+
+static thread_local char g_err[512];
+
+const char * sb_last_error(void) { return g_err; }
+
+static bool ck(cudaError_t e, const char * what) {
+    if (e == cudaSuccess) return true;
+    snprintf(g_err, sizeof g_err, "%s: %s", what, cudaGetErrorString(e));
+    return false;
+}
+
+struct LayerD {
+    TT qkv, gateup, o, down;          // tiled: q|k|v rows; gate/up interleaved by 8 rows
+    const float * an = nullptr, * fn = nullptr;
+    const float * qkv_b = nullptr;    // q|k|v biases, or NULL
+    const float * qn = nullptr, * kn = nullptr;
+    const int32_t * down_iperm = nullptr;
+};
+
+struct sb_engine {
+    ssf_file f{};
+    int n_layer = 0, E = 0, nh = 0, nkv = 0, hd = 0, qd = 0, kvd = 0, F = 0, V = 0, n_ctx = 0;
+    float eps = 0.f, theta = 0.f, scale = 0.f;
+    int six = 0, minneg = 0;
+    Arena ar;
+    std::vector<LayerD> L;
+    QT emb{};                         // file layout: the embedding lookup reads rows
+    TT head{};
+    const float * out_norm = nullptr;
+    // decode state
+    float * x = nullptr, * qkv = nullptr, * att = nullptr, * hp = nullptr, * logits = nullptr;
+    uint16_t * kc = nullptr, * vc = nullptr;
+    float * rcos = nullptr, * rsin = nullptr;
+    int * tok = nullptr, * pos = nullptr, * tlog = nullptr;
+    float * am_val = nullptr;
+    int * am_idx = nullptr;
+    unsigned * am_cnt = nullptr;
+    float * apart = nullptr;
+    unsigned * acnt = nullptr;
+    int * err = nullptr;              // bounded waits that gave up
+    unsigned long long * trace = nullptr;   // trace build: [launch][cta][8] timestamps
+    int n_launch_trace = 0;
+    int attn_chunk = 64, max_chunks = 0;
+    int nsm = 148;
+    cudaStream_t st = nullptr;
+    cudaGraphExec_t g_tok = nullptr;
+    int launches = 0;
+    int sync_mode = 0;                // SB_SYNC=1: eager launches, each synchronized and checked
+    char cur[64] = {0};               // the kernel being enqueued (for sync-mode errors)
+    bool failed = false;
+    float * h_logits = nullptr;
+    int * h_io = nullptr;
+    uint64_t bytes_tok = 0;
+};
+
+// ------------------------------------------------------------------ arena
+
+static void * carve(sb_engine * e, size_t n) { return e->ar.carve(n); }
+static const float * up_f32(sb_engine * e, const ssf_rec * r) { return upload_f32(e->ar, e->f, r); }
+
+
+// ------------------------------------------------------------------ launch
+
+template <typename... KArgs, typename... Args>
+static cudaError_t launch(sb_engine * e, bool pdl, void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          Args &&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = e->st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 1 : 0;
+    e->launches++;
+    cudaError_t r = cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
+    if (e->sync_mode && !e->failed) {
+        if (r == cudaSuccess) r = cudaStreamSynchronize(e->st);
+        int err = 0;
+        if (r == cudaSuccess) r = cudaMemcpy(&err, e->err, 4, cudaMemcpyDeviceToHost);
+        if (r != cudaSuccess || err) {
+            snprintf(g_err, sizeof g_err, "kernel %s: %s (check code %d)", e->cur,
+                     r != cudaSuccess ? cudaGetErrorString(r) : "bounds check failed", err);
+            e->failed = true;
+        }
+    }
+    return r;
+}
+
+template <int NB, int SIX>
+static void launch_embed(sb_engine * e, const QT & t) {
+    launch(e, true, k_embed<NB, SIX>, dim3((t.cols + 255) / 256), dim3(256), 0, t, (const int *) e->tok, e->x, e->err);
+}
+
+template <int MODE, int NB, int SIX>
+static void launch_tg_t(sb_engine * e, const TGArgs & g, int grid, size_t smem) {
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(k_tgemv<MODE, NB, SIX>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        attr = true;
+    }
+    launch(e, true, k_tgemv<MODE, NB, SIX>, dim3(grid), dim3(kTgThreads), smem, g);
+}
+
+template <int NB, int SIX>
+static void launch_tg_nb(sb_engine * e, int mode, const TGArgs & g, int grid, size_t smem) {
+    switch (mode) {
+    case GM_QKV: launch_tg_t<GM_QKV, NB, SIX>(e, g, grid, smem); break;
+    case GM_O: launch_tg_t<GM_O, NB, SIX>(e, g, grid, smem); break;
+    case GM_FFN: launch_tg_t<GM_FFN, NB, SIX>(e, g, grid, smem); break;
+    case GM_DOWN: launch_tg_t<GM_DOWN, NB, SIX>(e, g, grid, smem); break;
+    case GM_HEAD: launch_tg_t<GM_HEAD, NB, SIX>(e, g, grid, smem); break;
+    default: launch_tg_t<GM_PLAIN, NB, SIX>(e, g, grid, smem); break;
+    }
+}
+
+// Ring stages: a multiple of the consumer warps (tgemv.cuh), as many as fit
+// in ~96 KB so a CTA of the next kernel can share the SM, at least one per warp.
+static int tg_stages(const TT & t) {
+    int ns = (int) ((96 * 1024) / t.tb) / kConsWarps * kConsWarps;
+    return ns < kConsWarps ? kConsWarps : ns > kMaxStages ? kMaxStages : ns;
+}
+
+static size_t tg_smem(const TGArgs & g) {
+    return tg_ring_off(g.t.cols, g.in_permuted, g.norm_w != nullptr) + (size_t) g.nstage * g.t.tb;
+}
+
+static TGArgs tg_args(sb_engine * e, const TT & t, const float * in, const float * nw, float * out) {
+    TGArgs g;
+    memset(&g, 0, sizeof g);
+    g.t = t;
+    g.in = in;
+    g.norm_w = nw;
+    g.eps = e->eps;
+    g.out = out;
+    g.nstage = tg_stages(t);
+    g.trace = e->trace;
+    g.launch_id = e->launches;
+    g.prefetch = 1;
+    g.err = e->err;
+    return g;
+}
+
+// The GEMV that follows `t` in the token (for the L2 prefetch one kernel ahead).
+static void set_next(TGArgs & g, const TT * nt, int nsm) {
+    if (!nt) return;
+    g.next_tiles = nt->tiles;
+    g.next_ntiles = nt->ntiles;
+    g.next_grid = nt->ntiles < nsm ? nt->ntiles : nsm;
+    g.next_tb = nt->tb;
+}
+
+static void launch_tg(sb_engine * e, int mode, const TGArgs & g) {
+    const int grid = g.t.ntiles < e->nsm ? g.t.ntiles : e->nsm;
+    SB_DISPATCH_QT(g.t.nbits, g.t.six, launch_tg_nb, e, mode, g, grid, tg_smem(g));
+}
+
+// One token: embed, every layer, head and argmax. Enqueued on e->st (captured).
+static void enqueue_token(sb_engine * e) {
+    snprintf(e->cur, sizeof e->cur, "embed");
+    SB_DISPATCH_QT(e->emb.nbits, e->emb.six, launch_embed, e, e->emb);
+    for (int l = 0; l < e->n_layer; l++) {
+        const LayerD & y = e->L[l];
+        snprintf(e->cur, sizeof e->cur, "L%d.qkv", l);
+        {
+            TGArgs g = tg_args(e, y.qkv, e->x, y.an, e->qkv);
+            g.bias = y.qkv_b;
+            set_next(g, &y.o, e->nsm);
+            launch_tg(e, GM_QKV, g);
+        }
+        AttnArgs a;
+        memset(&a, 0, sizeof a);
+        a.qkv = e->qkv; a.n_head = e->nh; a.n_kv = e->nkv; a.hd = e->hd; a.qd = e->qd; a.kvd = e->kvd;
+        a.qn = y.qn; a.kn = y.kn; a.eps = e->eps;
+        a.rcos = e->rcos; a.rsin = e->rsin;
+        a.kc = e->kc + (size_t) l * e->n_ctx * e->kvd;
+        a.vc = e->vc + (size_t) l * e->n_ctx * e->kvd;
+        a.n_ctx = e->n_ctx; a.pos = e->pos; a.chunk = e->attn_chunk; a.scale = e->scale;
+        a.part = e->apart; a.cnt = e->acnt; a.max_chunks = e->max_chunks; a.out = e->att; a.err = e->err;
+        a.trace = e->trace; a.launch_id = e->launches;
+        snprintf(e->cur, sizeof e->cur, "L%d.attn", l);
+        launch(e, true, k_attn, dim3(e->nh, e->max_chunks), dim3(kAttnThreads), attn_smem_bytes(e->hd, e->attn_chunk), a);
+        snprintf(e->cur, sizeof e->cur, "L%d.o", l);
+        {
+            TGArgs g = tg_args(e, y.o, e->att, nullptr, e->x);
+            set_next(g, &y.gateup, e->nsm);
+            launch_tg(e, GM_O, g);
+        }
+        snprintf(e->cur, sizeof e->cur, "L%d.ffn", l);
+        {
+            TGArgs g = tg_args(e, y.gateup, e->x, y.fn, e->hp);
+            g.ffn_f = e->F;
+            g.scatter = y.down_iperm;
+            set_next(g, &y.down, e->nsm);
+            launch_tg(e, GM_FFN, g);
+        }
+        snprintf(e->cur, sizeof e->cur, "L%d.down", l);
+        {
+            TGArgs g = tg_args(e, y.down, e->hp, nullptr, e->x);
+            g.in_permuted = 1;
+            set_next(g, l + 1 < e->n_layer ? &e->L[l + 1].qkv : nullptr, e->nsm);
+            launch_tg(e, GM_DOWN, g);
+        }
+    }
+    snprintf(e->cur, sizeof e->cur, "head");
+    TGArgs g = tg_args(e, e->head, e->x, e->out_norm, e->logits);
+    g.prefetch = 0;   // larger than L2: streamed, not staged
+    g.am_val = e->am_val; g.am_idx = e->am_idx; g.am_cnt = e->am_cnt;
+    g.tok = e->tok; g.pos = e->pos; g.tlog = e->tlog;
+    launch_tg(e, GM_HEAD, g);
+}
+
+// ------------------------------------------------------------------ open
+
+static const char * unsupported(const ssf_file & f) {
+    const ssf_hdr * h = f.hdr;
+    if (h->flags & SSF_FLAG_HADAMARD) return "Hadamard-rotated weights";
+    if (h->flags & SSF_FLAG_EXACT) return "an exact-weight (f32) file";
+    if (h->norm_type != 0) return "LayerNorm";
+    if (h->rope_type != 0) return "interleaved RoPE";
+    if (h->arch_bits) return "architecture flags beyond a plain decoder";
+    if (h->logit_softcap != 0.0f || h->attn_softcap != 0.0f) return "soft-capping";
+    if (h->n_swa) return "sliding-window attention";
+    if (h->emb_scale != 0.0f || h->res_scale != 0.0f || h->logit_scale != 0.0f) return "embedding/residual/logit scales";
+    if (h->clip_qkv != 0.0f) return "Q/K/V clamping";
+    const char * names[] = {"position_embd.weight", "token_embd_norm.weight", "output.bias", "rope_freqs",
+                            "attn_window", "attn_rope"};
+    for (const char * n : names) if (ssf_find(&f, n)) return n;
+    return nullptr;
+}
+
+static void close_all(sb_engine * e) {
+    if (e->g_tok) cudaGraphExecDestroy(e->g_tok);
+    if (e->st) cudaStreamDestroy(e->st);
+    e->ar.release();
+    if (e->h_logits) cudaFreeHost(e->h_logits);
+    if (e->h_io) cudaFreeHost(e->h_io);
+    ssf_close(&e->f);
+}
+
+// Bytes one GEMV over t streams per launch (the tiles are exactly those bytes).
+static uint64_t tt_bytes(const TT & t) { return (uint64_t) t.ntiles * t.tb; }
+
+static bool build(sb_engine * e, char * why, int nwhy) {
+    const ssf_file & f = e->f;
+    e->bytes_tok = 0;
+    const ssf_rec * er = ssf_find(&f, "token_embd.weight");
+    if (!upload_qt(e->ar, f, er, e->emb, why, nwhy)) return false;
+    const ssf_rec * hr = ssf_find(&f, "output.weight");
+    if (!hr) hr = er;   // tied head (Qwen2.5): the embedding is streamed as the head
+    const int min_tiles = 6 * e->nsm;
+    if (!upload_tt(e->ar, f, hr, (int) hr->rows, 0, min_tiles, 0,
+                   [&](int v) { return RowSrc{v < (int) hr->rows ? hr : nullptr, v}; }, e->head, why, nwhy))
+        return false;
+    e->bytes_tok += tt_bytes(e->head);
+    e->out_norm = up_f32(e, ssf_find(&f, "output_norm.weight"));
+    e->L.assign(e->n_layer, LayerD());
+    for (int l = 0; l < e->n_layer; l++) {
+        LayerD & y = e->L[l];
+        auto R = [&](const char * fmt) { return ssf_findf(&f, fmt, l, 0); };
+        if (R("blk.%d.ffn_gate_inp.weight")) { snprintf(why, nwhy, "mixture-of-experts layers"); return false; }
+        if (!R("blk.%d.attn_norm.weight") || !R("blk.%d.ffn_norm.weight")) { snprintf(why, nwhy, "layer %d: missing norms", l); return false; }
+        const ssf_rec * q = R("blk.%d.attn_q.weight"), * k = R("blk.%d.attn_k.weight"), * v = R("blk.%d.attn_v.weight");
+        const ssf_rec * o = R("blk.%d.attn_output.weight"), * gt = R("blk.%d.ffn_gate.weight"), * up = R("blk.%d.ffn_up.weight");
+        const ssf_rec * dn = R("blk.%d.ffn_down.weight");
+        if (!q || !k || !v || !o || !gt || !up || !dn) { snprintf(why, nwhy, "layer %d: missing projections", l); return false; }
+        if ((int) q->rows != e->qd || (int) k->rows != e->kvd || (int) v->rows != e->kvd || (int) q->cols != e->E ||
+            (int) o->rows != e->E || (int) o->cols != e->qd || (int) gt->cols != e->E || gt->rows != up->rows ||
+            (int) dn->rows != e->E || dn->cols != gt->rows || gt->rows % 8) {
+            snprintf(why, nwhy, "layer %d: tensor shapes do not match the header", l);
+            return false;
+        }
+        const int F = (int) gt->rows;
+        e->F = F > e->F ? F : e->F;
+        // q | k | v as one tensor (they share an input; sml/sml-run.c:1796 groups them)
+        if (!upload_tt(e->ar, f, q, e->qd + 2 * e->kvd, 0, min_tiles, 0, [&](int r) {
+                return r < e->qd ? RowSrc{q, r} : r < e->qd + e->kvd ? RowSrc{k, r - e->qd}
+                     : r < e->qd + 2 * e->kvd ? RowSrc{v, r - e->qd - e->kvd} : RowSrc{nullptr, 0}; },
+                       y.qkv, why, nwhy))
+            return false;
+        // gate / up: a tile of TR rows holds TR/2 gate rows then the same TR/2 up rows
+        const int gtr = pick_tr(2 * F, (int) tile_geom(e->E, 1, (int) gt->nbits, e->six, gt->mq_n != 0).bytes,
+                                min_tiles, 1);
+        if (!upload_tt(e->ar, f, gt, 2 * F, gtr, min_tiles, 1, [&](int r) {
+                const int h = gtr / 2, ti = r / gtr, j = r % gtr, i = ti * h + j % h;
+                return i >= F ? RowSrc{nullptr, 0} : RowSrc{j < h ? gt : up, i}; },
+                       y.gateup, why, nwhy))
+            return false;
+        if (!upload_tt(e->ar, f, o, e->E, 0, min_tiles, 0, [&](int r) { return RowSrc{r < e->E ? o : nullptr, r}; },
+                       y.o, why, nwhy) ||
+            !upload_tt(e->ar, f, dn, e->E, 0, min_tiles, 0, [&](int r) { return RowSrc{r < e->E ? dn : nullptr, r}; },
+                       y.down, why, nwhy))
+            return false;
+        y.down_iperm = y.down.iperm;
+        e->bytes_tok += tt_bytes(y.qkv) + tt_bytes(y.gateup) + tt_bytes(y.o) + tt_bytes(y.down);
+        y.an = up_f32(e, R("blk.%d.attn_norm.weight"));
+        y.fn = up_f32(e, R("blk.%d.ffn_norm.weight"));
+        const ssf_rec * qb = R("blk.%d.attn_q.bias"), * kb = R("blk.%d.attn_k.bias"), * vb = R("blk.%d.attn_v.bias");
+        if (qb || kb || vb) {
+            std::vector<float> b((size_t) e->qd + 2 * e->kvd, 0.0f);
+            if (qb) memcpy(b.data(), f.base + qb->off, (size_t) e->qd * 4);
+            if (kb) memcpy(b.data() + e->qd, f.base + kb->off, (size_t) e->kvd * 4);
+            if (vb) memcpy(b.data() + e->qd + e->kvd, f.base + vb->off, (size_t) e->kvd * 4);
+            y.qkv_b = (const float *) e->ar.upload(b.data(), b.size() * 4);
+        }
+        const ssf_rec * qn = R("blk.%d.attn_q_norm.weight"), * kn = R("blk.%d.attn_k_norm.weight");
+        if ((qn && qn->rows * qn->cols != (uint32_t) e->hd) || (kn && kn->rows * kn->cols != (uint32_t) e->hd)) {
+            snprintf(why, nwhy, "layer %d: Q/K norm over other than one head", l);
+            return false;
+        }
+        y.qn = up_f32(e, qn);
+        y.kn = up_f32(e, kn);
+    }
+    if (e->emb.cols != e->E || e->emb.rows != e->V || e->head.cols != e->E || e->head.rows != e->V) {
+        snprintf(why, nwhy, "embedding or head shape does not match the header");
+        return false;
+    }
+    // decode state
+    const size_t kv = (size_t) e->n_layer * e->n_ctx * e->kvd * 2;
+    e->x = (float *) carve(e, (size_t) e->E * 4);
+    e->qkv = (float *) carve(e, (size_t) (e->qd + 2 * e->kvd) * 4);
+    e->att = (float *) carve(e, (size_t) e->qd * 4);
+    e->hp = (float *) carve(e, (size_t) (e->F > 0 ? e->F : 1) * 4);
+    e->logits = (float *) carve(e, (size_t) e->V * 4);
+    e->kc = (uint16_t *) carve(e, kv);
+    e->vc = (uint16_t *) carve(e, kv);
+    e->rcos = (float *) carve(e, (size_t) e->n_ctx * (e->hd / 2) * 4);
+    e->rsin = (float *) carve(e, (size_t) e->n_ctx * (e->hd / 2) * 4);
+    e->tok = (int *) carve(e, 4);
+    e->pos = (int *) carve(e, 4);
+    e->tlog = (int *) carve(e, (size_t) (e->n_ctx + 1) * 4);
+    e->am_val = (float *) carve(e, (size_t) 4 * e->nsm * 4);
+    e->am_idx = (int *) carve(e, (size_t) 4 * e->nsm * 4);
+    e->am_cnt = (unsigned *) carve(e, 4);
+    e->attn_chunk = e->hd <= 128 ? 64 : 32;   // the chunk's keys and values fit in 48 KB
+    e->max_chunks = (e->n_ctx + e->attn_chunk - 1) / e->attn_chunk;
+    e->apart = (float *) carve(e, (size_t) e->nh * e->max_chunks * (e->hd + 2) * 4);
+    e->acnt = (unsigned *) carve(e, (size_t) e->nh * 4);
+    e->err = (int *) carve(e, 4);
+#ifdef SB_TRACE
+    e->n_launch_trace = 6 * e->n_layer + 8;
+    e->trace = (unsigned long long *) carve(e, (size_t) e->n_launch_trace * kTraceCtas * 8 * 8);
+#endif
+    return true;
+}
+
+// Trace build: copy the per-CTA timestamps of the last token (launch x CTA x 8).
+extern "C" int sb_trace(const sb_engine * e, unsigned long long * out, int cap) {
+    if (!e->trace) return 0;
+    const int n = e->n_launch_trace * kTraceCtas * 8;
+    if (cap < n) return 0;
+    cudaDeviceSynchronize();
+    cudaMemcpy(out, e->trace, (size_t) n * 8, cudaMemcpyDeviceToHost);
+    return e->n_launch_trace;
+}
+
+sb_engine * sb_open(const char * path, int n_ctx, char * why, int nwhy) {
+    g_err[0] = 0;
+    sb_engine * e = new sb_engine();
+    if (!ssf_open(&e->f, path, why, nwhy)) { delete e; return nullptr; }
+    const ssf_hdr * h = e->f.hdr;
+    if (const char * u = unsupported(e->f)) {
+        snprintf(why, nwhy, "%s: not on the GPU yet", u);
+        close_all(e);
+        delete e;
+        return nullptr;
+    }
+    e->n_layer = (int) h->n_layer; e->E = (int) h->n_embd; e->nh = (int) h->n_head; e->nkv = (int) h->n_head_kv;
+    e->V = (int) h->n_vocab; e->eps = h->rms_eps; e->theta = h->rope_theta;
+    e->six = e->f.scale6; e->minneg = e->f.minneg;
+    const ssf_rec * q0 = ssf_find(&e->f, "blk.0.attn_q.weight");
+    e->hd = q0 && q0->rows % e->nh == 0 ? (int) q0->rows / e->nh : e->E / e->nh;
+    e->qd = e->nh * e->hd;
+    e->kvd = e->nkv * e->hd;
+    e->scale = h->attn_scale != 0.0f ? h->attn_scale : 1.0f / sqrtf((float) e->hd);
+    e->n_ctx = n_ctx > 0 ? n_ctx : 256;
+    if (e->n_ctx < 64) e->n_ctx = 64;
+    if (h->n_rot && (int) h->n_rot != e->hd) {
+        snprintf(why, nwhy, "partial rotary: not on the GPU yet");
+        close_all(e); delete e; return nullptr;
+    }
+    if (e->nh % e->nkv || e->hd % 64 || e->hd > 256) {
+        snprintf(why, nwhy, "head layout %d/%d x %d not supported", e->nh, e->nkv, e->hd);
+        close_all(e); delete e; return nullptr;
+    }
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&e->nsm, cudaDevAttrMultiProcessorCount, dev);
+    // pass 1 sizes the arena, pass 2 fills it
+    if (!build(e, why, nwhy)) { close_all(e); delete e; return nullptr; }
+    if (!e->ar.allocate()) {
+        snprintf(why, nwhy, "cudaMalloc of %.2f GB for the model failed", e->ar.size / 1e9);
+        close_all(e); delete e; return nullptr;
+    }
+    if (!build(e, why, nwhy)) { close_all(e); delete e; return nullptr; }
+    // RoPE tables exactly as the CPU builds them (sml/sml-run.c:1383-1393)
+    {
+        const int half = e->hd / 2;
+        std::vector<float> c((size_t) e->n_ctx * half), s((size_t) e->n_ctx * half);
+        for (int p = 0; p < e->n_ctx; p++)
+            for (int i = 0; i < half; i++) {
+                const float fr = powf(e->theta, -(float) i / (float) half);
+                const float a = (float) p * fr;
+                c[(size_t) p * half + i] = cosf(a);
+                s[(size_t) p * half + i] = sinf(a);
+            }
+        cudaMemcpy(e->rcos, c.data(), c.size() * 4, cudaMemcpyHostToDevice);
+        cudaMemcpy(e->rsin, s.data(), s.size() * 4, cudaMemcpyHostToDevice);
+    }
+    if (!ck(cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking), "stream") ||
+        !ck(cudaMallocHost(&e->h_logits, (size_t) e->V * 4), "pinned logits") ||
+        !ck(cudaMallocHost(&e->h_io, 64 * 4), "pinned io")) {
+        snprintf(why, nwhy, "%s", g_err);
+        close_all(e); delete e; return nullptr;
+    }
+    // capture one token (SB_SYNC=1: no graph, every kernel synchronized and checked)
+    const char * sm = getenv("SB_SYNC");
+    e->sync_mode = sm && atoi(sm) != 0;
+    cudaGraph_t gr = nullptr;
+    e->launches = 0;
+    bool ok = true;
+    if (!e->sync_mode) {
+        ok = ck(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal), "begin capture");
+        if (ok) {
+            enqueue_token(e);
+            ok = ck(cudaStreamEndCapture(e->st, &gr), "end capture");
+        }
+        ok = ok && ck(cudaGraphInstantiateWithFlags(&e->g_tok, gr, 0), "instantiate");
+        if (gr) cudaGraphDestroy(gr);
+    }
+    ok = ok && ck(cudaDeviceSynchronize(), "open");
+    if (!ok) {
+        snprintf(why, nwhy, "%s", g_err);
+        close_all(e); delete e; return nullptr;
+    }
+    return e;
+}
+
+void sb_close(sb_engine * e) {
+    if (!e) return;
+    cudaStreamSynchronize(e->st);
+    close_all(e);
+    delete e;
+}
+
+void sb_info(const sb_engine * e, int * out) {
+    out[0] = e->n_layer; out[1] = e->E; out[2] = e->nh; out[3] = e->nkv; out[4] = e->hd; out[5] = e->F;
+    out[6] = e->V; out[7] = e->n_ctx; out[8] = 0; out[9] = 0;
+    out[10] = (int) (e->bytes_tok & 0xffffffffu); out[11] = (int) (e->bytes_tok >> 32);
+}
+
+uint64_t sb_bytes_per_token(const sb_engine * e) { return e->bytes_tok; }
+int sb_launches_per_token(const sb_engine * e) { return e->launches; }
+const float * sb_device_logits(const sb_engine * e) { return e->logits; }
+
+static bool set_tok_pos(sb_engine * e, int tok, int pos) {
+    e->h_io[0] = tok;
+    e->h_io[1] = pos;
+    return ck(cudaMemcpyAsync(e->tok, &e->h_io[0], 4, cudaMemcpyHostToDevice, e->st), "tok") &&
+           ck(cudaMemcpyAsync(e->pos, &e->h_io[1], 4, cudaMemcpyHostToDevice, e->st), "pos");
+}
+
+// One token through the captured graph, or eagerly with per-kernel checks.
+static bool run_token(sb_engine * e) {
+    if (!e->sync_mode) return ck(cudaGraphLaunch(e->g_tok, e->st), "graph launch");
+    enqueue_token(e);
+    return !e->failed;
+}
+
+const float * sb_step(sb_engine * e, int tok, int pos) {
+    if (!e || pos < 0 || pos >= e->n_ctx || tok < 0 || tok >= e->V) return nullptr;
+    if (!set_tok_pos(e, tok, pos)) return nullptr;
+    if (!run_token(e)) return nullptr;
+    if (!ck(cudaMemcpyAsync(e->h_logits, e->logits, (size_t) e->V * 4, cudaMemcpyDeviceToHost, e->st), "logits")) return nullptr;
+    if (!ck(cudaStreamSynchronize(e->st), "step")) return nullptr;
+    return e->h_logits;
+}
+
+const float * sb_prefill(sb_engine * e, const int * ids, int pos0, int n) {
+    if (!e || n <= 0 || pos0 < 0 || pos0 + n > e->n_ctx) return nullptr;
+    for (int i = 0; i < n; i++) {
+        if (ids[i] < 0 || ids[i] >= e->V) return nullptr;
+        // each token's id must reach the device before its graph runs; every
+        // staging slot is its own pinned word, reused only after a sync
+        const int slot = 2 + (i % 30) * 2;
+        e->h_io[slot] = ids[i];
+        e->h_io[slot + 1] = pos0 + i;
+        if (!ck(cudaMemcpyAsync(e->tok, &e->h_io[slot], 4, cudaMemcpyHostToDevice, e->st), "tok") ||
+            !ck(cudaMemcpyAsync(e->pos, &e->h_io[slot + 1], 4, cudaMemcpyHostToDevice, e->st), "pos") ||
+            !run_token(e))
+            return nullptr;
+        if (i % 30 == 29) { if (!ck(cudaStreamSynchronize(e->st), "prefill")) return nullptr; }
+    }
+    if (!ck(cudaMemcpyAsync(e->h_logits, e->logits, (size_t) e->V * 4, cudaMemcpyDeviceToHost, e->st), "logits")) return nullptr;
+    if (!ck(cudaStreamSynchronize(e->st), "prefill")) return nullptr;
+    return e->h_logits;
+}
+
+static int generate(sb_engine * e, const int * prompt, int np, int ngen, int * out_ids, float * ms) {
+    if (!e || np < 1 || ngen < 0 || np + ngen > e->n_ctx) return 0;
+    if (!sb_prefill(e, prompt, 0, np)) return 0;
+    // the head of the last prompt token has written tok = argmax, pos = np,
+    // tlog[np-1]; from here each replay reads them and writes the next
+    cudaEvent_t a = nullptr, b = nullptr;
+    if (ms) { cudaEventCreate(&a); cudaEventCreate(&b); cudaEventRecord(a, e->st); }
+    for (int g = 0; g + 1 < ngen; g++)
+        if (!run_token(e)) return 0;
+    if (ms) cudaEventRecord(b, e->st);
+    if (!ck(cudaMemcpyAsync(out_ids, e->tlog + np - 1, (size_t) ngen * 4, cudaMemcpyDeviceToHost, e->st), "ids"))
+        return 0;
+    if (!ck(cudaStreamSynchronize(e->st), "generate")) return 0;
+    if (ms) {
+        cudaEventElapsedTime(ms, a, b);
+        cudaEventDestroy(a);
+        cudaEventDestroy(b);
+    }
+    return 1;
+}
+
+int sb_generate(sb_engine * e, const int * prompt, int np, int ngen, int * out_ids) {
+    return generate(e, prompt, np, ngen, out_ids, nullptr);
+}
+
+int sb_generate_timed(sb_engine * e, const int * prompt, int np, int ngen, int * out_ids, float * ms_out) {
+    return generate(e, prompt, np, ngen, out_ids, ms_out);
+}

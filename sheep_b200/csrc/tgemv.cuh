@@ -1,0 +1,447 @@
+// Streaming quantized GEMV over tile-major weights (tiles.h).
+//
+// One CTA per SM takes a contiguous range of tiles (TR whole rows each). A
+// producer warp streams them into a ring of shared-memory stages with
+// cp.async.bulk and mbarrier transaction counts -- it starts before the kernel
+// waits on its predecessor, since weights never depend on it. Eight consumer
+// warps stage the int8 activation (the mode's prologue: RMSNorm, gather,
+// per-32 quantization), then take whole tiles round-robin: lane l owns row
+// l % TR and every (32/TR)-th unit of it, so a lane's units are independent
+// work and the warp reduces once per tile. The ring depth is a multiple of the
+// eight consumer warps, so tile k lands in stage k % ns and stage s is always
+// consumed by warp s % 8, in order -- the mbarrier parity protocol needs that.
+//
+// Arithmetic per group (sml/sml-kernel.c:2027-2066 and the plane kinds of
+// :1934-2018): y += d*sq*xs*dot(code, xq) + md*(mq-bias)*xs*sum(xq), the dot
+// exact in integers (dp4a), the float epilogue summed per unit then per row.
+// Every row is finished by exactly one warp, in a fixed order of additions, so
+// results do not depend on timing.
+#pragma once
+
+#include "decode.cuh"
+#include "tiles.h"
+
+namespace sb {
+
+constexpr int kConsWarps = 16;
+constexpr int kConsThreads = kConsWarps * 32;
+constexpr int kTgThreads = kConsThreads + 32;   // + one producer warp
+constexpr int kMaxStages = 32;   // a multiple of kConsWarps: stage s belongs to warp s % kConsWarps
+
+struct TGArgs {
+    TT t;
+    const float * in;        // input activation
+    const float * norm_w;    // RMSNorm gain, NULL: none
+    float eps;
+    int in_permuted;         // `in` already in t.perm order
+    const float * bias;      // per logical row (QKV: q|k|v concatenated); FFN: [gate bias | up bias]
+    int ffn_f;               // FFN: hidden size
+    float * out;
+    const int32_t * scatter; // FFN: write index of hidden value i
+    float * am_val; int * am_idx; unsigned * am_cnt;
+    int * tok; int * pos; int * tlog;
+    int nstage;
+    int prefetch;            // L2 prefetch of this CTA's tiles before the wait
+    int8_t * act_q; float * act_s; int32_t * act_sum;   // optional export (CTA 0)
+    int * err;               // set if a bounded wait gave up
+    unsigned long long * trace;   // trace build: per-CTA timestamps
+    int launch_id;
+    // the next GEMV's tiles: this CTA prefetches the range its own index will
+    // take there into L2, so the next kernel's bulk copies hit L2
+    const uint8_t * next_tiles;
+    int next_ntiles, next_grid;
+    uint32_t next_tb;
+};
+
+// Shared memory: [act | perm | norm gain | input x | ring]. perm and the gain
+// are static, so the producer bulk-loads them before the dependency wait; the
+// input is read once, coalesced, after it.
+struct StageLayout {
+    uint32_t perm_off, w_off, x_off, ring_off;
+};
+__host__ __device__ inline StageLayout stage_layout(int n, int has_perm, int has_norm) {
+    StageLayout L;
+    uint32_t off = (uint32_t) ((act_smem_bytes(n) + 127) / 128 * 128);
+    L.perm_off = off;
+    if (has_perm) off += (uint32_t) n * 4;
+    L.w_off = off;
+    if (has_norm) off += (uint32_t) n * 4;
+    L.x_off = off;
+    if (has_perm) off += (uint32_t) n * 4;
+    L.ring_off = (off + 127) / 128 * 128;
+    return L;
+}
+__host__ __device__ inline size_t tg_ring_off(int n, int in_permuted, int has_norm) {
+    return stage_layout(n, !in_permuted, has_norm).ring_off;
+}
+
+// Quantize groups of 32 with 8 lanes per group, 4 values per lane (4 groups
+// per warp at a time): amax and sum by 3 shuffles inside the 8-lane team,
+// s = amax/127, is = 1/s (0 if s = 0), q = clamp(rint(v*is), +-127) with IEEE
+// division and round-to-nearest-even (sml/sml-kernel.c:89-109). The team's 32
+// codes land as four 4-byte stores in the slot layout. Every lane of the warp
+// runs the shuffles; `store` is false for a team past the last group.
+SB_DEV void quant_team(float4 v, int grp, int sub, ActS & a, const TGArgs & g, bool ex, bool store) {
+    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+    for (int o = 4; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float sc = __fdiv_rn(amax, 127.0f);
+    const float is = sc > 0.0f ? __fdiv_rn(1.0f, sc) : 0.0f;
+    const float vv[4] = {v.x, v.y, v.z, v.w};
+    uint32_t word = 0;
+    int sum = 0;
+#pragma unroll
+    for (int b = 0; b < 4; b++) {
+        int q = __float2int_rn(__fmul_rn(vv[b], is));
+        q = q > 127 ? 127 : q < -127 ? -127 : q;
+        sum += q;
+        word |= ((uint32_t) (q & 0xff)) << (8 * b);
+    }
+#pragma unroll
+    for (int o = 4; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (!store) return;
+    *reinterpret_cast<uint32_t *>(a.q + act_slot_off(a.n, grp, 4 * sub)) = word;
+    if (sub == 0) {
+        a.xs[grp] = sc;
+        a.xsum[grp] = sc * (float) sum;
+    }
+    if (ex) {
+        *reinterpret_cast<uint32_t *>(g.act_q + grp * kGroup + 4 * sub) = word;
+        if (sub == 0) { g.act_s[grp] = sc; g.act_sum[grp] = sum; }
+    }
+}
+
+// Stage the activation with the consumer threads only (named barrier 1).
+// Gathered input: x is read into shared memory once, coalesced; the RMSNorm
+// factor comes from a block reduction over it (sum in double, as
+// sml/sml-run.c:147-152); teams of 8 lanes then quantize groups, reading
+// x[perm[i]] and the gain from shared memory (both bulk-loaded by the producer
+// before the wait; `statics` completes when they land). Pre-permuted input:
+// each team reads its group with 16-byte loads.
+SB_DEV void tg_stage(const TGArgs & g, ActS & a, double * red, uint8_t * smem, const StageLayout & L,
+                     uint64_t * statics, bool & failed) {
+    const int n = g.t.cols, ng = n / kGroup, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int team = tid >> 3, sub = tid & 7, nteam = kConsThreads / 8;
+    const bool ex = g.act_q && blockIdx.x == 0;
+    if (g.in_permuted) {
+        // every round's load issued before any group is quantized
+        constexpr int kR = 8;   // rounds held in registers: n <= 8 * nteam * 32
+        float4 v[kR];
+#pragma unroll
+        for (int r = 0; r < kR; r++) {
+            const int grp = r * nteam + team;
+            v[r] = grp < ng ? *reinterpret_cast<const float4 *>(g.in + grp * kGroup + 4 * sub) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int r = 0; r < kR; r++) {
+            const int grp = r * nteam + team;
+            if (r * nteam < ng) quant_team(v[r], grp, sub, a, g, ex, grp < ng);
+        }
+        for (int base = kR * nteam; base < ng; base += nteam) {
+            const int grp = base + team;
+            const float4 w4 = grp < ng ? *reinterpret_cast<const float4 *>(g.in + grp * kGroup + 4 * sub) : make_float4(0.f, 0.f, 0.f, 0.f);
+            quant_team(w4, grp, sub, a, g, ex, grp < ng);
+        }
+        bar_sync(1, kConsThreads);
+        return;
+    }
+    float * xs = reinterpret_cast<float *>(smem + L.x_off);
+    const int32_t * perm = reinterpret_cast<const int32_t *>(smem + L.perm_off);
+    const float * gw = reinterpret_cast<const float *>(smem + L.w_off);
+    double q = 0.0;
+    for (int i = 4 * tid; i < n; i += 4 * kConsThreads) {
+        const float4 f = *reinterpret_cast<const float4 *>(g.in + i);
+        *reinterpret_cast<float4 *>(xs + i) = f;
+        q += (double) f.x * f.x + (double) f.y * f.y + (double) f.z * f.z + (double) f.w * f.w;
+    }
+    float s = 1.0f;
+    if (g.norm_w) {
+        q = warp_sum_d(q);
+        if (lane == 0) red[w] = q;
+    }
+    bar_sync(1, kConsThreads);
+    if (g.norm_w) {
+        double ss = 0.0;
+        for (int k = 0; k < kConsWarps; k++) ss += red[k];
+        s = __fdiv_rn(1.0f, sqrtf(__fadd_rn((float) (ss / n), g.eps)));
+    }
+    if (!failed && !mbar_wait(statics, 0, g.err, 4)) failed = true;
+    if (!failed) {
+        for (int base = 0; base < ng; base += nteam) {
+            const int grp = base + team;
+            const int gg = grp < ng ? grp : 0;   // a team past the end reads group 0 and stores nothing
+            const int4 p4 = *reinterpret_cast<const int4 *>(perm + gg * kGroup + 4 * sub);
+            const int pi[4] = {p4.x, p4.y, p4.z, p4.w};
+            float vv[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++)
+                vv[k] = g.norm_w ? __fmul_rn(__fmul_rn(xs[pi[k]], s), gw[pi[k]]) : xs[pi[k]];
+            quant_team(make_float4(vv[0], vv[1], vv[2], vv[3]), grp, sub, a, g, ex, grp < ng);
+        }
+    }
+    bar_sync(1, kConsThreads);
+}
+
+// Integer dots of unit u of tile row j against the unit's activation slots.
+template <int NB>
+SB_DEV void tile_dots(const uint8_t * tile, const TileGeom & tg, int j, int u, const uint4 (&a)[4], int (&d)[4]) {
+    int kinds[3], shifts[3];
+    plane_kinds(NB, kinds, shifts);
+    d[0] = d[1] = d[2] = d[3] = 0;
+    const int at = u * tg.TR + j;
+#pragma unroll
+    for (int p = 0; p < 3; p++) {
+        if (!kinds[p]) break;
+        const uint8_t * sec = tile + tg.pl_off[p];
+        const int sh = shifts[p];
+        if (kinds[p] == 4) {
+            const uint4 w0 = *reinterpret_cast<const uint4 *>(sec + 16 * at);
+            const uint4 w1 = *reinterpret_cast<const uint4 *>(sec + tg.pl_sec[p] + 16 * at);
+            const uint32_t x0[4] = {w0.x, w0.y, w0.z, w0.w}, x1[4] = {w1.x, w1.y, w1.z, w1.w};
+            const uint32_t a0[4] = {a[0].x, a[0].y, a[0].z, a[0].w}, a1[4] = {a[1].x, a[1].y, a[1].z, a[1].w};
+            const uint32_t a2[4] = {a[2].x, a[2].y, a[2].z, a[2].w}, a3[4] = {a[3].x, a[3].y, a[3].z, a[3].w};
+            int s0 = 0, s1 = 0, s2 = 0, s3 = 0;
+#pragma unroll
+            for (int w = 0; w < 4; w++) {
+                s0 = __dp4a((int) (x0[w] & 0x0f0f0f0fu), (int) a0[w], s0);
+                s1 = __dp4a((int) ((x0[w] >> 4) & 0x0f0f0f0fu), (int) a1[w], s1);
+                s2 = __dp4a((int) (x1[w] & 0x0f0f0f0fu), (int) a2[w], s2);
+                s3 = __dp4a((int) ((x1[w] >> 4) & 0x0f0f0f0fu), (int) a3[w], s3);
+            }
+            d[0] += s0 << sh; d[1] += s1 << sh; d[2] += s2 << sh; d[3] += s3 << sh;
+        } else if (kinds[p] == 2) {
+            const uint4 w = *reinterpret_cast<const uint4 *>(sec + 16 * at);
+            const uint32_t x[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const uint32_t ak[4] = {a[k].x, a[k].y, a[k].z, a[k].w};
+                int s = 0;
+#pragma unroll
+                for (int ww = 0; ww < 4; ww++) s = __dp4a((int) ((x[ww] >> (2 * k)) & 0x03030303u), (int) ak[ww], s);
+                d[k] += s << sh;
+            }
+        } else {
+            // 8 bytes: the unit's 16 columns of each of its 4 groups, 2 bytes each
+            const uint2 w = *reinterpret_cast<const uint2 *>(sec + 8 * at);
+            const uint32_t h[4] = {w.x & 0xffffu, w.x >> 16, w.y & 0xffffu, w.y >> 16};
+#pragma unroll
+            for (int k = 0; k < 4; k++) {
+                const uint32_t ak[4] = {a[k].x, a[k].y, a[k].z, a[k].w};
+                int s = 0;
+#pragma unroll
+                for (int ww = 0; ww < 4; ww++) s = __dp4a((int) nib_to_bytes((h[k] >> (4 * ww)) & 15u), (int) ak[ww], s);
+                d[k] += s << sh;
+            }
+        }
+    }
+}
+
+template <int SIX>
+SB_DEV void tile_fields(const uint8_t * f, int (&v)[4]) {
+    if (SIX) {
+        const uint32_t b0 = f[0], b1 = f[1], b2 = f[2];
+        v[0] = (int) (b0 & 63u);
+        v[1] = (int) (((b0 >> 6) | (b1 << 2)) & 63u);
+        v[2] = (int) (((b1 >> 4) | (b2 << 4)) & 63u);
+        v[3] = (int) ((b2 >> 2) & 63u);
+    } else {
+        const uint32_t w = *reinterpret_cast<const uint32_t *>(f);
+        v[0] = (int) (w & 255u); v[1] = (int) ((w >> 8) & 255u);
+        v[2] = (int) ((w >> 16) & 255u); v[3] = (int) (w >> 24);
+    }
+}
+
+// Lane share of tile row j: units u = u0, u0 + step, ...
+template <int NB, int SIX>
+SB_DEV float tile_row(const uint8_t * tile, const TileGeom & tg, const ActS & a, int j, int u0, int step,
+                      bool has_min, float mbias, int * err) {
+    float acc = 0.0f;
+    if (!SB_CHECK(err, j < tg.TR && u0 >= 0 && step > 0, 101)) return 0.0f;
+    for (int u = u0; u < tg.U; u += step) {
+        if (!SB_CHECK(err, (u * tg.TR + j) * 16 + 16 <= (int) tg.pl_sec[0] || tg.pl_kind[0] != 4, 102)) return acc;
+        if (!SB_CHECK(err, 3 * (a.n >> 2) + 16 * u + 16 <= a.n, 103)) return acc;
+        if (!SB_CHECK(err, ((u >> 1) * tg.TR + j) * (int) tg.f_w + (int) tg.f_w + (int) tg.sq_off <= (int) tg.bytes, 104)) return acc;
+        if (!SB_CHECK(err, ((u >> 2) * tg.TR + j) * 2 + 2 + (int) tg.sd_off <= (int) tg.bytes, 105)) return acc;
+        uint4 av[4];
+#pragma unroll
+        for (int k = 0; k < 4; k++) av[k] = *reinterpret_cast<const uint4 *>(a.q + k * (a.n >> 2) + 16 * u);
+        int d[4];
+        tile_dots<NB>(tile, tg, j, u, av, d);
+        const int pq = u >> 1;
+        const float4 xs = *reinterpret_cast<const float4 *>(a.xs + 4 * pq);
+        int sq[4];
+        tile_fields<SIX>(tile + tg.sq_off + (pq * tg.TR + j) * tg.f_w, sq);
+        const float sd = h2f(*reinterpret_cast<const uint16_t *>(tile + tg.sd_off + ((u >> 2) * tg.TR + j) * 2));
+        float t1 = (float) sq[0] * xs.x * (float) d[0];
+        t1 += (float) sq[1] * xs.y * (float) d[1];
+        t1 += (float) sq[2] * xs.z * (float) d[2];
+        t1 += (float) sq[3] * xs.w * (float) d[3];
+        acc += sd * t1;
+        if (has_min && (u & 1) == 0) {
+            const float4 xm = *reinterpret_cast<const float4 *>(a.xsum + 4 * pq);
+            int mq[4];
+            tile_fields<SIX>(tile + tg.mq_off + (pq * tg.TR + j) * tg.f_w, mq);
+            const float md = h2f(*reinterpret_cast<const uint16_t *>(tile + tg.md_off + ((u >> 2) * tg.TR + j) * 2));
+            float t2 = ((float) mq[0] - mbias) * xm.x;
+            t2 += ((float) mq[1] - mbias) * xm.y;
+            t2 += ((float) mq[2] - mbias) * xm.z;
+            t2 += ((float) mq[3] - mbias) * xm.w;
+            acc += md * t2;
+        }
+    }
+    return acc;
+}
+
+template <int MODE, int NB, int SIX>
+__global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__ TGArgs g) {
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages], statics;
+    __shared__ double red[kConsWarps];
+    __shared__ float am_v[kConsWarps];
+    __shared__ int am_i[kConsWarps];
+    pdl_launch_dependents();
+    SB_MARK(g.trace, g.launch_id, 0);
+    const TT & t = g.t;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int T = t.ntiles;
+    const int t0 = (int) ((long) T * blockIdx.x / gridDim.x), t1 = (int) ((long) T * (blockIdx.x + 1) / gridDim.x);
+    const int ns = g.nstage;
+    const StageLayout SL = stage_layout(t.cols, !g.in_permuted, g.norm_w != nullptr);
+    uint8_t * ring = smem + SL.ring_off;
+#ifdef SB_CHECKED
+    uint32_t dsm;
+    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dsm));
+    const size_t ring_end = dsm;
+    if (!SB_CHECK(g.err, ns >= kConsWarps && ns % kConsWarps == 0 && ns <= kMaxStages &&
+                           SL.ring_off + (size_t) ns * t.tb <= dsm, 107)) return;
+#else
+    const size_t ring_end = ~(size_t) 0;
+#endif
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < ns; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        mbar_init(&statics, 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+
+    if (warp == kConsWarps) {
+        // ---------------- producer: weights never depend on the previous kernel
+        if (lane == 0) {
+            // the column order and the norm gain do not depend on the previous kernel
+            const uint32_t sb = (g.in_permuted ? 0u : (uint32_t) t.cols * 4) + (g.norm_w ? (uint32_t) t.cols * 4 : 0u);
+            mbar_expect_tx(&statics, sb);
+            if (!g.in_permuted) bulk_g2s(smem + SL.perm_off, t.perm, (uint32_t) t.cols * 4, &statics);
+            if (g.norm_w) bulk_g2s(smem + SL.w_off, g.norm_w, (uint32_t) t.cols * 4, &statics);
+            if (g.prefetch && t1 > t0) prefetch_l2(t.tiles + (size_t) t0 * t.tb, (size_t) (t1 - t0) * t.tb);
+            if (g.next_tiles && (int) blockIdx.x < g.next_grid) {
+                const int n0 = (int) ((long) g.next_ntiles * blockIdx.x / g.next_grid);
+                const int n1 = (int) ((long) g.next_ntiles * (blockIdx.x + 1) / g.next_grid);
+                if (n1 > n0) prefetch_l2(g.next_tiles + (size_t) n0 * g.next_tb, (size_t) (n1 - n0) * g.next_tb);
+            }
+            int issued = 0;
+            for (int i = t0; i < t1; i++) {
+                const int k = i - t0, s = k % ns;
+                if (k >= ns && !mbar_wait(&empty[s], ((k / ns) - 1) & 1, g.err, 1)) break;
+                mbar_expect_tx(&full[s], t.tb);
+                bulk_g2s(ring + (size_t) s * t.tb, t.tiles + (size_t) i * t.tb, t.tb, &full[s]);
+                issued++;
+            }
+            // no copy may still be landing in shared memory when the CTA exits:
+            // wait (bounded) for the last copy into every stage
+            for (int k = issued - ns < 0 ? 0 : issued - ns; k < issued; k++)
+                mbar_wait(&full[k % ns], (k / ns) & 1, g.err, 3);
+            mbar_wait(&statics, 0, g.err, 5);
+        }
+        pdl_wait();
+        return;
+    }
+
+    // ---------------- consumers
+    pdl_wait();
+    SB_MARK(g.trace, g.launch_id, 1);
+    ActS a = act_carve(smem, t.cols);
+    bool failed = false;   // after one wait gives up, the rest are skipped
+    tg_stage(g, a, red, smem, SL, &statics, failed);
+    SB_MARK(g.trace, g.launch_id, 2);
+    const TileGeom tg = tile_geom(t.cols, t.TR, NB, SIX, t.has_min);
+    const int TR = t.TR, j = lane % TR, v = lane / TR, VS = 32 / TR;
+    float best_v = -INFINITY;
+    int best_i = 0x7fffffff;
+    for (int i = t0 + warp; i < t1; i += kConsWarps) {
+        const int k = i - t0, s = k % ns;
+        const bool ok = !failed && mbar_wait(&full[s], (k / ns) & 1, g.err, 2);
+        failed = !ok;
+        if (k == 0) SB_MARK(g.trace, g.launch_id, 3);
+        float acc = 0.0f;
+        if (ok && SB_CHECK(g.err, tg.bytes == t.tb && (size_t) (s + 1) * t.tb + SL.ring_off <= ring_end, 106))
+            acc = tile_row<NB, SIX>(ring + (size_t) s * t.tb, tg, a, j, v, VS, t.has_min, t.mbias, g.err);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        for (int o = 16; o >= TR; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        if (MODE == GM_FFN) {
+            // rows 0..TR/2-1 of the tile are gate rows, TR/2..TR-1 the matching up rows
+            const float up = __shfl_down_sync(0xffffffffu, acc, TR / 2);
+            const int idx = i * (TR / 2) + lane;
+            if (lane < TR / 2 && idx < g.ffn_f) {
+                float gv = acc, uv = up;
+                if (g.bias) { gv += g.bias[idx]; uv += g.bias[g.ffn_f + idx]; }
+                if (SB_CHECK(g.err, g.scatter[idx] >= 0 && g.scatter[idx] < g.ffn_f, 108))
+                    g.out[g.scatter[idx]] = silu_mul(gv, uv);
+            }
+            continue;
+        }
+        const int r = i * TR + lane;
+        if (lane < TR && r < t.rows) {
+            float y = acc;
+            if (MODE == GM_QKV || MODE == GM_PLAIN) {
+                if (g.bias) y += g.bias[r];
+                g.out[r] = y;
+            } else if (MODE == GM_O || MODE == GM_DOWN) {
+                g.out[r] += y;
+            } else if (MODE == GM_HEAD) {
+                g.out[r] = y;
+                if (y > best_v || (y == best_v && r < best_i)) { best_v = y; best_i = r; }
+            }
+        }
+    }
+
+    bar_sync(1, kConsThreads);
+    SB_MARK(g.trace, g.launch_id, 4);
+    if (MODE == GM_HEAD) {
+        // greedy argmax, ties to the lower index (sml/sml-run.c:3539-3544)
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best_v, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, best_i, o);
+            if (ov > best_v || (ov == best_v && oi < best_i)) { best_v = ov; best_i = oi; }
+        }
+        if (lane == 0) { am_v[warp] = best_v; am_i[warp] = best_i; }
+        bar_sync(1, kConsThreads);
+        if (threadIdx.x == 0) {
+            float bv = am_v[0];
+            int bi = am_i[0];
+            for (int w = 1; w < kConsWarps; w++)
+                if (am_v[w] > bv || (am_v[w] == bv && am_i[w] < bi)) { bv = am_v[w]; bi = am_i[w]; }
+            g.am_val[blockIdx.x] = bv;
+            g.am_idx[blockIdx.x] = bi;
+            __threadfence();
+            if (atomicAdd(g.am_cnt, 1u) == gridDim.x - 1) {
+                __threadfence();
+                float fv = -INFINITY;
+                int fi = 0x7fffffff;
+                for (unsigned b = 0; b < gridDim.x; b++) {
+                    const float v2 = ((volatile float *) g.am_val)[b];
+                    const int ix = ((volatile int *) g.am_idx)[b];
+                    if (v2 > fv || (v2 == fv && ix < fi)) { fv = v2; fi = ix; }
+                }
+                *g.am_cnt = 0;
+                const int p = *g.pos;
+                if (g.tlog) g.tlog[p] = fi;
+                *g.tok = fi;
+                *g.pos = p + 1;
+            }
+        }
+    }
+}
+
+}  // namespace sb

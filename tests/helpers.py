@@ -1,0 +1,252 @@
+"""Test helpers: synthetic models, the CPU checkers, the reference build.
+
+The checkers are test infrastructure: oracle/_build/liboracle.so (this
+repository's C restatement) and oracle/_ref/libsmlref.so (the reference's own
+CPU code, when it was built). Neither is ever used by the engine.
+
+The reference keeps its group-field width as process-global state
+(sml/sml-model.c:225-250), so every call into it runs in a fresh spawned
+process.
+"""
+import concurrent.futures as cf
+import ctypes
+import hashlib
+import json
+import multiprocessing as mp
+import os
+import subprocess
+import tempfile
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+ORACLE_DIR = os.path.join(ROOT, "oracle")
+ORACLE_LIB = os.path.join(ORACLE_DIR, "_build", "liboracle.so")
+REF_LIB = os.path.join(ORACLE_DIR, "_ref", "libsmlref.so")
+MODEL_DIR = os.path.join(tempfile.gettempdir(), "sheep_b200_models")
+
+
+def build_oracle():
+    subprocess.run(["make", "-s", "-C", ORACLE_DIR, "oracle"], check=True)
+    subprocess.run(["make", "-s", "-C", ORACLE_DIR, "ref"], check=True)
+
+
+def have_ref():
+    return os.path.exists(REF_LIB)
+
+
+def model_path(spec):
+    """A synthetic SSF for `spec` (cached by its content)."""
+    import sheep_b200
+    os.makedirs(MODEL_DIR, exist_ok=True)
+    key = hashlib.sha1(json.dumps(spec, sort_keys=True).encode()).hexdigest()[:16]
+    path = os.path.join(MODEL_DIR, key + ".ssf")
+    if not os.path.exists(path):
+        tmp = path + f".tmp{os.getpid()}"
+        sheep_b200.write_model(tmp, **spec)
+        os.replace(tmp, path)
+    return path
+
+
+def file_sha(path):
+    h = hashlib.sha256()
+    with open(path, "rb") as f:
+        for b in iter(lambda: f.read(1 << 22), b""):
+            h.update(b)
+    return h.hexdigest()
+
+
+def _p(a):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+# ------------------------------------------------------------------ restatement
+
+class Oracle:
+    """ctypes view of oracle/_build/liboracle.so (one model)."""
+
+    _L = None
+
+    @classmethod
+    def lib(cls):
+        if cls._L is None:
+            L = ctypes.CDLL(ORACLE_LIB)
+            L.so_open.restype = ctypes.c_void_p
+            L.so_open.argtypes = [ctypes.c_char_p, ctypes.c_int]
+            for n in ("so_close",):
+                getattr(L, n).argtypes = [ctypes.c_void_p]
+            cls._L = L
+        return cls._L
+
+    def __init__(self, path, n_ctx=256):
+        self.m = ctypes.c_void_p(self.lib().so_open(path.encode(), n_ctx))
+        assert self.m.value, path
+        info = (ctypes.c_int * 8)()
+        self.lib().so_info(self.m, info)
+        self.info = list(info)
+        self.n_vocab = info[6]
+
+    def matvec(self, name, x, rows):
+        y = np.zeros(rows, np.float32)
+        assert self.lib().so_matvec(self.m, name.encode(), _p(np.ascontiguousarray(x, np.float32)), _p(y), 0, rows)
+        return y
+
+    def dequant_row(self, name, row, cols):
+        out = np.zeros(cols, np.float32)
+        assert self.lib().so_dequant_row(self.m, name.encode(), row, _p(out))
+        return out
+
+    def codes_row(self, name, row, cols):
+        out = np.zeros(cols, np.uint8)
+        assert self.lib().so_codes_row(self.m, name.encode(), row, _p(out))
+        return out
+
+    def forward(self, tok, pos):
+        lg = np.zeros(self.n_vocab, np.float32)
+        self.lib().so_forward(self.m, tok, pos, _p(lg))
+        return lg
+
+    def decode(self, prompt, ngen):
+        prompt = np.ascontiguousarray(prompt, np.int32)
+        ids = np.zeros(ngen, np.int32)
+        lg = np.zeros((ngen, self.n_vocab), np.float32)
+        self.lib().so_decode(self.m, _p(prompt), len(prompt), ngen, _p(ids), _p(lg))
+        return ids, lg
+
+    def close(self):
+        if self.m:
+            self.lib().so_close(self.m)
+            self.m = None
+
+
+def oracle_quant(x):
+    x = np.ascontiguousarray(x, np.float32)
+    n = len(x)
+    q = np.zeros(n, np.int8)
+    s = np.zeros(n // 32, np.float32)
+    sums = np.zeros(n // 32, np.int32)
+    Oracle.lib().so_quantize_act(_p(x), n, _p(q), _p(s), _p(sums))
+    return q, s, sums
+
+
+def oracle_route(lg, k, flags=1):
+    lg = np.ascontiguousarray(lg, np.float32)
+    sel = np.zeros(16, np.int32)
+    w = np.zeros(16, np.float32)
+    got = Oracle.lib().so_moe_route(_p(lg), len(lg), k, flags, _p(sel), _p(w))
+    return sel[:got], w[:got]
+
+
+# ------------------------------------------------------------------ reference
+
+def _ref_lib():
+    L = ctypes.CDLL(REF_LIB)
+    L.refh_open.restype = ctypes.c_void_p
+    L.refh_open.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    L.refh_bytes_per_token.restype = ctypes.c_ulonglong
+    return L
+
+
+def _ref_task(kind, path, args):
+    L = _ref_lib()
+    if kind == "quant":
+        x = np.ascontiguousarray(args["x"], np.float32)
+        n = len(x)
+        q, s, sums = np.zeros(n, np.int8), np.zeros(n // 32, np.float32), np.zeros(n // 32, np.int32)
+        L.refh_quantize_act(_p(x), n, _p(q), _p(s), _p(sums))
+        return q, s, sums
+    if kind == "route":
+        lg = np.ascontiguousarray(args["lg"], np.float32)
+        sel, w = np.zeros(16, np.int32), np.zeros(16, np.float32)
+        got = L.refh_moe_route(_p(lg), len(lg), args["k"], args.get("flags", 1), ctypes.c_float(0.0), _p(sel), _p(w))
+        return sel[:got], w[:got]
+    with_ctx = 1 if kind in ("decode", "forward") else 0
+    h = ctypes.c_void_p(L.refh_open(path.encode(), args.get("n_ctx", 256), args.get("threads", 4), with_ctx))
+    if not h.value:
+        raise RuntimeError(f"reference could not open {path}")
+    try:
+        if kind == "matvec":
+            x = np.ascontiguousarray(args["x"], np.float32)
+            rows, cols = args["rows"], len(x)
+            y = np.zeros(rows, np.float32)
+            q, s, sums = np.zeros(cols, np.int8), np.zeros(cols // 32, np.float32), np.zeros(cols // 32, np.int32)
+            assert L.refh_matvec(h, args["name"].encode(), _p(x), _p(y), 0, rows, _p(q), _p(s), _p(sums))
+            return y, q, s, sums
+        if kind == "dequant":
+            out = np.zeros((len(args["rows"]), args["cols"]), np.float32)
+            for i, r in enumerate(args["rows"]):
+                assert L.refh_dequant_row(h, args["name"].encode(), int(r), _p(out[i]))
+            return out
+        if kind == "decode":
+            info = (ctypes.c_int * 8)()
+            nv = L.refh_info(h, info)
+            prompt = np.ascontiguousarray(args["prompt"], np.int32)
+            ngen = args["ngen"]
+            ids = np.zeros(ngen, np.int32)
+            lg = np.zeros((ngen, nv), np.float32)
+            assert L.refh_decode(h, _p(prompt), len(prompt), ngen, _p(ids), _p(lg))
+            return ids, lg
+        if kind == "forward":   # teacher-forced: logits after every token of `tokens`
+            info = (ctypes.c_int * 8)()
+            nv = L.refh_info(h, info)
+            toks = args["tokens"]
+            lg = np.zeros((len(toks), nv), np.float32)
+            for i, t in enumerate(toks):
+                L.refh_forward(h, int(t), i, _p(lg[i]))
+            return lg
+        if kind == "bytes":
+            return int(L.refh_bytes_per_token(h))
+    finally:
+        L.refh_close(h)
+    raise ValueError(kind)
+
+
+def ref(kind, path=None, **args):
+    """Run one reference call in a fresh spawned process."""
+    with cf.ProcessPoolExecutor(max_workers=1, mp_context=mp.get_context("spawn")) as ex:
+        return ex.submit(_ref_task, kind, path, args).result()
+
+
+def rel_rms(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.sqrt(np.mean((a - b) ** 2)) / (np.sqrt(np.mean(a ** 2)) + 1e-30))
+
+
+def agree_with_ties(ref_logits, got_logits):
+    """Top-1 agreement under the reference's tie rule (sml/sml-gpu-fwd.c:2586-2598):
+    a different top-1 is a tie when the reference's own logits for the two
+    tokens are within 1% of its logits' standard deviation."""
+    ac, ag = int(np.argmax(ref_logits)), int(np.argmax(got_logits))
+    if ac == ag:
+        return True, False
+    sd = float(np.std(ref_logits.astype(np.float64)))
+    tie = float(ref_logits[ac]) - float(ref_logits[ag]) <= 0.01 * sd
+    return tie, tie
+
+
+# ------------------------------------------------------------------ file reading
+
+REC_FMT = "<64s4I2Q2Q2Q2Q2Q2Q4Q4Q2I"   # the 248-byte SSF record
+
+
+def read_records(path):
+    """name -> dict of the record's fields (tooling/sml_format.py:76-88 REC_FMT)."""
+    import struct
+    with open(path, "rb") as f:
+        head = f.read(4096)
+        n_tensors, table_off = struct.unpack_from("<QQ", head, 68)
+        f.seek(table_off)
+        raw = f.read(n_tensors * 248)
+    out = {}
+    names = ("kind rows cols group off nbytes sd_off sd_n sq_off sq_n perm_off perm_n "
+             "md_off md_n mq_off mq_n c0 c1 c2 c3 n0 n1 n2 n3 layout nbits").split()
+    for i in range(n_tensors):
+        v = struct.unpack_from(REC_FMT, raw, i * 248)
+        out[v[0].rstrip(b"\0").decode()] = dict(zip(names, v[1:]))
+    return out
+
+
+def read_perm(path, name):
+    r = read_records(path)[name]
+    return np.fromfile(path, dtype=np.int32, count=r["cols"], offset=r["perm_off"])

@@ -1,0 +1,153 @@
+"""Kernel-level parity on the GPU, through the C ABI, against the CPU oracle.
+
+Bit-exact: int8 activation codes, scales and sums from identical inputs;
+dequantized weights (multiply and add rounded separately, as the CPU does).
+Tolerance: GEMV outputs rel-RMS <= 1e-5 (same integer dots, float epilogue
+summed in another order; the reference's own kernel gate is 1e-4,
+sml/sml-gpu-bench.c:147-154).
+"""
+import numpy as np
+import pytest
+
+import sheep_b200
+from tests import helpers
+
+pytestmark = pytest.mark.gpu
+
+GEMV_TOL = 1e-5
+
+
+def _torch():
+    import torch
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    return torch
+
+
+def _quant_cases():
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal(4096).astype(np.float32)
+    x[:32] = 0.0                                   # an all-zero group: s = 0, is = 0
+    x[32:64] = np.linspace(-1, 1, 32, dtype=np.float32)
+    x[64:96] = (np.arange(32) - 15.5).astype(np.float32) * (127.0 / 15.5)   # ties at .5 after scaling
+    x[96:128] = 1e-30                               # subnormal-range scale
+    x[128:160] = 3e38 * np.sign(rng.standard_normal(32)).astype(np.float32)
+    return [x, rng.standard_normal(1536).astype(np.float32) * 40.0, rng.standard_normal(8960).astype(np.float32)]
+
+
+@pytest.mark.parametrize("case", range(3))
+def test_quantize_act_bitexact(case):
+    torch = _torch()
+    x = _quant_cases()[case]
+    n = len(x)
+    dx = torch.from_numpy(x).cuda()
+    dq = torch.zeros(n, dtype=torch.int8, device="cuda")
+    ds = torch.zeros(n // 32, dtype=torch.float32, device="cuda")
+    dsum = torch.zeros(n // 32, dtype=torch.int32, device="cuda")
+    L = sheep_b200.lib()
+    assert L.sb_quantize_act(dx.data_ptr(), None, n, dq.data_ptr(), ds.data_ptr(), dsum.data_ptr(), None)
+    torch.cuda.synchronize()
+    q, s, sums = helpers.oracle_quant(x)
+    assert np.array_equal(dq.cpu().numpy(), q)
+    assert np.array_equal(ds.cpu().numpy().view(np.uint32), s.view(np.uint32))
+    assert np.array_equal(dsum.cpu().numpy(), sums)
+    if helpers.have_ref():
+        rq, rs, rsum = helpers.ref("quant", x=x)
+        assert np.array_equal(rq, q) and np.array_equal(rs.view(np.uint32), s.view(np.uint32))
+        assert np.array_equal(rsum, sums)
+
+
+WIDTHS = [(nb, six) for six in (0, 1) for nb in (2, 3, 4, 5, 6, 7, 8)]
+
+
+def _width_model(nb, six):
+    spec = sheep_b200.spec_for("tiny-q4", n_embd=512, n_ff=1408, n_head=8, n_head_kv=2, head_dim=64,
+                               nbits=nb, emb_nbits=nb, scale6=six, minneg=six, n_layer=1, seed=100 + nb)
+    return helpers.model_path(spec)
+
+
+@pytest.mark.parametrize("nb,six", WIDTHS)
+def test_gemv_all_widths(nb, six):
+    path = _width_model(nb, six)
+    ts = sheep_b200.TensorSet(path)
+    orc = helpers.Oracle(path)
+    rng = np.random.default_rng(nb * 10 + six)
+    try:
+        for name in ("blk.0.attn_q.weight", "blk.0.ffn_down.weight", "blk.0.ffn_gate.weight", "output.weight"):
+            rows, cols, got_nb = ts.shape(name)
+            assert got_nb == nb
+            x = rng.standard_normal(cols).astype(np.float32)
+            y, q, s, sums = ts.matvec(name, x)
+            yo = orc.matvec(name, x, rows)
+            assert helpers.rel_rms(yo, y) <= GEMV_TOL, name
+            # the activation the kernel quantized: bit-exact against the CPU's
+            perm = helpers.read_perm(path, name)
+            oq, os_, osum = helpers.oracle_quant(x[perm])
+            assert np.array_equal(q, oq) and np.array_equal(s.view(np.uint32), os_.view(np.uint32))
+            assert np.array_equal(sums, osum)
+    finally:
+        ts.close()
+        orc.close()
+
+
+@pytest.mark.parametrize("nb,six", WIDTHS)
+def test_dequant_rows_bitexact(nb, six):
+    path = _width_model(nb, six)
+    ts = sheep_b200.TensorSet(path)
+    orc = helpers.Oracle(path)
+    try:
+        name = "token_embd.weight"
+        rows, cols, _ = ts.shape(name)
+        pick = [0, 1, 7, rows // 2, rows - 1]
+        got = ts.dequant_rows(name, pick)
+        for i, r in enumerate(pick):
+            want = orc.dequant_row(name, r, cols)
+            assert np.array_equal(got[i].view(np.uint32), want.view(np.uint32)), (name, r)
+    finally:
+        ts.close()
+        orc.close()
+
+
+@pytest.mark.skipif(not helpers.have_ref(), reason="reference CPU build (oracle/_ref) not present")
+@pytest.mark.parametrize("nb,six", [(4, 0), (8, 0), (6, 1), (4, 1), (3, 0)])
+def test_gemv_against_reference_build(nb, six):
+    """The same GEMV against the reference's own kernels (oracle/_ref)."""
+    path = _width_model(nb, six)
+    ts = sheep_b200.TensorSet(path)
+    try:
+        rng = np.random.default_rng(77)
+        for name in ("blk.0.attn_q.weight", "blk.0.ffn_down.weight"):
+            rows, cols, _ = ts.shape(name)
+            x = rng.standard_normal(cols).astype(np.float32)
+            y, q, s, sums = ts.matvec(name, x)
+            ry, rq, rs, rsum = helpers.ref("matvec", path, name=name, x=x, rows=rows)
+            assert np.array_equal(q, rq) and np.array_equal(sums, rsum)
+            assert helpers.rel_rms(ry, y) <= GEMV_TOL
+    finally:
+        ts.close()
+
+
+def _cfg0_layer_model():
+    # one layer at the config-0 widths with a 32768-row head: tensors tile at
+    # TR = 1..8 with many tiles per CTA, so every ring stage is reused
+    spec = sheep_b200.spec_for("qwen2.5-1.5b-q4", n_layer=1, n_vocab=32768, tied=0, seed=21)
+    return helpers.model_path(spec)
+
+
+def test_gemv_cfg0_shapes_stage_reuse():
+    path = _cfg0_layer_model()
+    ts = sheep_b200.TensorSet(path)
+    orc = helpers.Oracle(path)
+    rng = np.random.default_rng(99)
+    try:
+        for name in ("blk.0.attn_q.weight", "blk.0.attn_k.weight", "blk.0.ffn_gate.weight",
+                     "blk.0.ffn_down.weight", "output.weight"):
+            rows, cols, _ = ts.shape(name)
+            x = rng.standard_normal(cols).astype(np.float32)
+            y, q, s, sums = ts.matvec(name, x)
+            assert helpers.rel_rms(orc.matvec(name, x, rows), y) <= GEMV_TOL, name
+            # repeated calls are bit-identical (no dependence on timing)
+            y2, _, _, _ = ts.matvec(name, x)
+            assert np.array_equal(y.view(np.uint32), y2.view(np.uint32)), name
+    finally:
+        ts.close()
+        orc.close()
