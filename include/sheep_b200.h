@@ -31,10 +31,21 @@ const float * sb_prefill(sb_engine * e, const int * ids, int pos0, int n);
 // graph-replay benchmark loop, sml/sml-gpu-fwd.c:2626-2662): host prompt in,
 // ngen host ids out. Returns 1, or 0 on failure.
 int sb_generate(sb_engine * e, const int * prompt, int np, int ngen, int * out_ids);
-// The same, with the generation loop (prompt excluded) timed by CUDA events.
-int sb_generate_timed(sb_engine * e, const int * prompt, int np, int ngen, int * out_ids, float * ms_out);
+// The same after nwarm untimed tokens: out_ids gets nwarm + ngen ids, ms_out
+// the CUDA-event time of the generation loop after the warm-up. Each of the
+// ngen tokens replays the token graph once; the first is chosen by the last
+// warm-up (or prompt) replay, so ngen ids cost ngen - 1 timed replays.
+int sb_generate_timed(sb_engine * e, const int * prompt, int np, int nwarm, int ngen, int * out_ids,
+                      float * ms_out);
 const float * sb_device_logits(const sb_engine * e);
 int sb_launches_per_token(const sb_engine * e);
+// Average duration (ms) of one kernel class of the token, each launch alone,
+// timed by CUDA events, layers cycled so weights come from HBM; bytes_out =
+// the weight bytes one launch reads. which: 0 q|k|v, 2 o, 3 gate/up, 4 down,
+// 5 head. Leaves the decode state undefined (call after generating).
+int sb_time_kernel(sb_engine * e, int which, int reps, float * ms_avg, double * bytes_out);
+// Trace build only (-DSB_TRACE): per-CTA timestamps of the last token.
+int sb_trace(const sb_engine * e, unsigned long long * out, int cap);
 const char * sb_last_error(void);
 // The engine behind sml_gpu_open, and its release.
 sb_engine * sml_gpu_engine(void);
@@ -87,6 +98,10 @@ typedef struct {
 } ssfgen_spec;
 
 int ssfgen_write(const char * path, const ssfgen_spec * s, char * why, int nwhy);
+
+// The loader's validation alone, no GPU needed: 1, or 0 with the reason
+// (the acceptance rules of sml/sml-model.c:24-75 and :174-260, v8+ files).
+int sb_ssf_check(const char * path, char * why, int nwhy);
 
 #ifdef __cplusplus
 }

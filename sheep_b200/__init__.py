@@ -57,9 +57,11 @@ def lib():
         "sb_step": (fp, [vp, ip, ip]),
         "sb_prefill": (fp, [vp, vp, ip, ip]),
         "sb_generate": (ip, [vp, vp, ip, ip, vp]),
-        "sb_generate_timed": (ip, [vp, vp, ip, ip, vp, fp]),
+        "sb_generate_timed": (ip, [vp, vp, ip, ip, ip, vp, fp]),
         "sb_device_logits": (vp, [vp]),
         "sb_launches_per_token": (ip, [vp]),
+        "sb_time_kernel": (ip, [vp, ip, ip, fp, ctypes.POINTER(ctypes.c_double)]),
+        "sb_trace": (ip, [vp, vp, ip]),
         "sb_last_error": (cp, []),
         "sb_tset_open": (vp, [cp, cp, ip]),
         "sb_tset_close": (None, [vp]),
@@ -70,6 +72,7 @@ def lib():
         "sb_tset_dequant_rows": (ip, [vp, cp, vp, ip, vp]),
         "sb_quantize_act": (ip, [vp, vp, ip, vp, vp, vp, vp]),
         "ssfgen_write": (ip, [cp, vp, cp, ip]),
+        "sb_ssf_check": (ip, [cp, cp, ip]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -92,6 +95,13 @@ def write_model(path, **spec):
     if not lib().ssfgen_write(path.encode(), ctypes.byref(s), why, 512):
         raise RuntimeError(why.value.decode())
     return path
+
+
+def ssf_check(path):
+    """(1, "") if the loader accepts the file, else (0, why). No GPU needed."""
+    why = ctypes.create_string_buffer(512)
+    ok = lib().sb_ssf_check(path.encode(), why, 512)
+    return ok, why.value.decode()
 
 
 class Engine:
@@ -121,12 +131,14 @@ class Engine:
             raise RuntimeError(f"sb_prefill failed: {lib().sb_last_error().decode()}")
         return np.ctypeslib.as_array(p, shape=(self.n_vocab,)).copy()
 
-    def generate(self, prompt, ngen, timed=False):
+    def generate(self, prompt, ngen, timed=False, warmup=0):
+        """Greedy ids; with timed=True also the CUDA-event ms of the loop after
+        `warmup` untimed tokens (ngen ids = ngen - 1 timed replays)."""
         prompt = np.ascontiguousarray(prompt, dtype=np.int32)
-        out = np.zeros(ngen, np.int32)
+        out = np.zeros(ngen + (warmup if timed else 0), np.int32)
         ms = ctypes.c_float(0)
         if timed:
-            ok = lib().sb_generate_timed(self.h, _p(prompt), len(prompt), ngen, _p(out), ctypes.byref(ms))
+            ok = lib().sb_generate_timed(self.h, _p(prompt), len(prompt), warmup, ngen, _p(out), ctypes.byref(ms))
         else:
             ok = lib().sb_generate(self.h, _p(prompt), len(prompt), ngen, _p(out))
         if not ok:
@@ -136,6 +148,16 @@ class Engine:
     @property
     def launches_per_token(self):
         return lib().sb_launches_per_token(self.h)
+
+    KERNELS = {"qkv": 0, "o": 2, "ffn": 3, "down": 4, "head": 5}
+
+    def time_kernel(self, which, reps):
+        """(avg ms per launch, weight bytes per launch) of one kernel class, each
+        launch alone; leaves the decode state undefined."""
+        ms, by = ctypes.c_float(0), ctypes.c_double(0)
+        if not lib().sb_time_kernel(self.h, self.KERNELS[which], reps, ctypes.byref(ms), ctypes.byref(by)):
+            raise RuntimeError(f"sb_time_kernel failed: {lib().sb_last_error().decode()}")
+        return ms.value, by.value
 
     def close(self):
         if self.h:

@@ -5,6 +5,7 @@
 // position past n_ctx; nothing exits the process.
 #include "sheep_b200.h"
 #include "sml-gpu.h"
+#include "ssf.h"
 
 #include <cstdio>
 #include <cstdlib>
@@ -67,4 +68,13 @@ extern "C" sb_engine * sml_gpu_engine(void) { return g_eng; }
 extern "C" void sml_gpu_close(void) {
     if (g_eng) sb_close(g_eng);
     g_eng = nullptr;
+}
+
+// Open and validate an SSF file without a GPU (the loader's checks alone).
+// Returns 1, or 0 with the reason in why.
+extern "C" int sb_ssf_check(const char * path, char * why, int nwhy) {
+    ssf_file f;
+    if (!ssf_open(&f, path, why, nwhy)) return 0;
+    ssf_close(&f);
+    return 1;
 }

@@ -369,6 +369,72 @@ static bool build(sb_engine * e, char * why, int nwhy) {
     return true;
 }
 
+// Algorithmic bytes of one record: codes and fields as the file stores them.
+static uint64_t rec_bytes(const ssf_rec * r) {
+    uint64_t b = r->sd_n + r->sq_n + r->md_n + r->mq_n;
+    for (int p = 0; p < SSF_MAX_LEVELS; p++) b += r->codes_n[p];
+    return b;
+}
+
+// Average duration of one kernel class of the token, each launch alone on the
+// engine's stream (no programmatic overlap), timed by CUDA events, cycling
+// over the layers so the weights come from HBM rather than L2 (a layer's
+// gate/up is 16 MB, the 28 layers 445 MB). which: 0 q|k|v, 2 o, 3 gate/up,
+// 4 down, 5 head. bytes_out: the file's bytes of the weights one launch reads.
+// Leaves the decode state undefined: call it after generating, not between.
+extern "C" int sb_time_kernel(sb_engine * e, int which, int reps, float * ms_avg, double * bytes_out) {
+    if (!e || reps < 1 || e->sync_mode) return 0;
+    const ssf_file & f = e->f;
+    auto layer_bytes = [&](int l) -> double {
+        auto R = [&](const char * fmt) { return ssf_findf(&f, fmt, l, 0); };
+        switch (which) {
+        case 0: return (double) (rec_bytes(R("blk.%d.attn_q.weight")) + rec_bytes(R("blk.%d.attn_k.weight")) +
+                                 rec_bytes(R("blk.%d.attn_v.weight")));
+        case 2: return (double) rec_bytes(R("blk.%d.attn_output.weight"));
+        case 3: return (double) (rec_bytes(R("blk.%d.ffn_gate.weight")) + rec_bytes(R("blk.%d.ffn_up.weight")));
+        case 4: return (double) rec_bytes(R("blk.%d.ffn_down.weight"));
+        default: {
+            const ssf_rec * h = ssf_find(&f, "output.weight");
+            return (double) rec_bytes(h ? h : ssf_find(&f, "token_embd.weight"));
+        }
+        }
+    };
+    cudaEvent_t a, b;
+    cudaEventCreate(&a);
+    cudaEventCreate(&b);
+    double bytes = 0;
+    auto one = [&](int r) {
+        const int l = r % e->n_layer;
+        const LayerD & y = e->L[l];
+        TGArgs g;
+        switch (which) {
+        case 0: g = tg_args(e, y.qkv, e->x, y.an, e->qkv); g.bias = y.qkv_b; launch_tg(e, GM_QKV, g); break;
+        case 2: g = tg_args(e, y.o, e->att, nullptr, e->x); launch_tg(e, GM_O, g); break;
+        case 3: g = tg_args(e, y.gateup, e->x, y.fn, e->hp); g.ffn_f = e->F; g.scatter = y.down_iperm;
+                launch_tg(e, GM_FFN, g); break;
+        case 4: g = tg_args(e, y.down, e->hp, nullptr, e->x); g.in_permuted = 1; launch_tg(e, GM_DOWN, g); break;
+        default: g = tg_args(e, e->head, e->x, e->out_norm, e->logits); g.prefetch = 0;
+                 g.am_val = e->am_val; g.am_idx = e->am_idx; g.am_cnt = e->am_cnt;
+                 g.tok = e->tok; g.pos = e->pos; g.tlog = nullptr; launch_tg(e, GM_HEAD, g); break;
+        }
+        bytes += layer_bytes(l);
+    };
+    for (int r = 0; r < 3; r++) one(r);   // warm-up
+    bytes = 0;
+    cudaStreamSynchronize(e->st);
+    cudaEventRecord(a, e->st);
+    for (int r = 0; r < reps; r++) one(r + 3);
+    cudaEventRecord(b, e->st);
+    const bool ok = ck(cudaStreamSynchronize(e->st), "time kernel");
+    float ms = 0;
+    cudaEventElapsedTime(&ms, a, b);
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    if (ms_avg) *ms_avg = ms / reps;
+    if (bytes_out) *bytes_out = bytes / reps;
+    return ok ? 1 : 0;
+}
+
 // Trace build: copy the per-CTA timestamps of the last token (launch x CTA x 8).
 extern "C" int sb_trace(const sb_engine * e, unsigned long long * out, int cap) {
     if (!e->trace) return 0;
@@ -521,17 +587,28 @@ const float * sb_prefill(sb_engine * e, const int * ids, int pos0, int n) {
     return e->h_logits;
 }
 
-static int generate(sb_engine * e, const int * prompt, int np, int ngen, int * out_ids, float * ms) {
-    if (!e || np < 1 || ngen < 0 || np + ngen > e->n_ctx) return 0;
+// Greedy generation on the device: the prompt stepped from position 0, then
+// nwarm + ngen tokens, each chosen on the GPU and fed back by graph replay. ms
+// (if not NULL) times the last ngen replays by CUDA events on the stream.
+static int generate(sb_engine * e, const int * prompt, int np, int nwarm, int ngen, int * out_ids, float * ms) {
+    const int total = nwarm + ngen;
+    if (!e || np < 1 || nwarm < 0 || ngen < 1 || np + total > e->n_ctx + 1) return 0;
     if (!sb_prefill(e, prompt, 0, np)) return 0;
-    // the head of the last prompt token has written tok = argmax, pos = np,
-    // tlog[np-1]; from here each replay reads them and writes the next
+    // the head of the last prompt token has written tok = argmax, pos = np and
+    // tlog[np-1]; each replay reads them and writes the next
+    for (int g = 0; g < nwarm; g++)
+        if (!run_token(e)) return 0;
     cudaEvent_t a = nullptr, b = nullptr;
-    if (ms) { cudaEventCreate(&a); cudaEventCreate(&b); cudaEventRecord(a, e->st); }
+    if (ms) {
+        if (!ck(cudaStreamSynchronize(e->st), "generate")) return 0;
+        cudaEventCreate(&a);
+        cudaEventCreate(&b);
+        cudaEventRecord(a, e->st);
+    }
     for (int g = 0; g + 1 < ngen; g++)
         if (!run_token(e)) return 0;
     if (ms) cudaEventRecord(b, e->st);
-    if (!ck(cudaMemcpyAsync(out_ids, e->tlog + np - 1, (size_t) ngen * 4, cudaMemcpyDeviceToHost, e->st), "ids"))
+    if (!ck(cudaMemcpyAsync(out_ids, e->tlog + np - 1, (size_t) total * 4, cudaMemcpyDeviceToHost, e->st), "ids"))
         return 0;
     if (!ck(cudaStreamSynchronize(e->st), "generate")) return 0;
     if (ms) {
@@ -543,9 +620,10 @@ static int generate(sb_engine * e, const int * prompt, int np, int ngen, int * o
 }
 
 int sb_generate(sb_engine * e, const int * prompt, int np, int ngen, int * out_ids) {
-    return generate(e, prompt, np, ngen, out_ids, nullptr);
+    return generate(e, prompt, np, 0, ngen, out_ids, nullptr);
 }
 
-int sb_generate_timed(sb_engine * e, const int * prompt, int np, int ngen, int * out_ids, float * ms_out) {
-    return generate(e, prompt, np, ngen, out_ids, ms_out);
+int sb_generate_timed(sb_engine * e, const int * prompt, int np, int nwarm, int ngen, int * out_ids, float * ms_out) {
+    return generate(e, prompt, np, nwarm, ngen, out_ids, ms_out);
 }
+

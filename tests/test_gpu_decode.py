@@ -146,3 +146,24 @@ def test_decode_cfg0_widths():
     toks = np.random.default_rng(5).integers(0, 32768, 6)
     corr, rms, strict, agree = _check_teacher_forced(path, toks)
     assert corr >= LOGIT_CORR and rms <= LOGIT_RELRMS and agree == len(toks), (corr, rms, strict, agree)
+
+
+@pytest.mark.skipif(not helpers.have_ref(), reason="reference CPU build (oracle/_ref) not present")
+def test_cfg0_logits_within_reference_spread():
+    """Configuration 0 (28 layers): the GPU's logits are as close to the
+    reference build's as an independent exact CPU implementation (the scalar
+    oracle) is. Teacher-forced on 6 positions."""
+    path = helpers.model_path(dict(sheep_b200.CONFIGS["qwen2.5-1.5b-q4"]))
+    toks = [int(t) for t in np.random.default_rng(0).integers(0, 151936, 6)]
+    ref = helpers.ref("forward", path, tokens=toks, n_ctx=64, threads=8)
+    eng = sheep_b200.Engine(path, n_ctx=64)
+    orc = helpers.Oracle(path, n_ctx=64)
+    try:
+        for pos, t in enumerate(toks):
+            lg, lo = eng.step(t, pos), orc.forward(t, pos)
+            spread = helpers.rel_rms(ref[pos], lo)
+            assert helpers.rel_rms(ref[pos], lg) <= max(2e-2, 1.5 * spread), (pos, spread)
+            assert float(np.corrcoef(ref[pos], lg)[0, 1]) >= LOGIT_CORR
+    finally:
+        eng.close()
+        orc.close()

@@ -1,0 +1,101 @@
+"""The CPU oracle (oracle/sml_oracle.c) pinned against golden vectors that the
+reference's own CPU code wrote (tests/golden/make_golden.py), and the
+synthetic-model writer pinned by the files' sha256. No GPU.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+from tests import helpers
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+GOLD = os.path.join(HERE, "golden")
+INDEX = json.load(open(os.path.join(GOLD, "index.json")))
+WIDTH_FIXTURES = sorted(k for k in INDEX if k.startswith("width_"))
+
+
+def check_input(n):
+    i = np.arange(n, dtype=np.float32)
+    return (np.sin(np.float32(0.001) * i) * (np.float32(1.0) + np.float32(0.5) * (i % 7).astype(np.float32))).astype(np.float32)
+
+
+@pytest.mark.parametrize("fx", WIDTH_FIXTURES)
+def test_writer_is_pinned(fx):
+    path = helpers.model_path(INDEX[fx]["spec"])
+    assert helpers.file_sha(path) == INDEX[fx]["sha256"]
+
+
+@pytest.mark.parametrize("fx", WIDTH_FIXTURES)
+def test_oracle_against_reference_vectors(fx):
+    g = np.load(os.path.join(GOLD, fx))
+    path = helpers.model_path(INDEX[fx]["spec"])
+    recs = helpers.read_records(path)
+    orc = helpers.Oracle(path, n_ctx=64)
+    try:
+        for t in ("blk.0.ffn_down.weight", "output.weight"):
+            key = t.replace(".", "_")
+            rows, cols = recs[t]["rows"], recs[t]["cols"]
+            x = check_input(cols)
+            # activation: gather through the tensor's perm, quantize -- bit-exact
+            q, s, sums = helpers.oracle_quant(x[helpers.read_perm(path, t)])
+            assert np.array_equal(q, g[key + "_q"])
+            assert np.array_equal(s.view(np.uint32), g[key + "_s"].view(np.uint32))
+            assert np.array_equal(sums, g[key + "_sums"])
+            # the GEMV: same integer dots, float sums in another order
+            y = orc.matvec(t, x, rows)
+            assert helpers.rel_rms(g[key + "_y"], y) <= 1e-5
+        r = recs["token_embd.weight"]
+        for i, row in enumerate(g["embd_rows"]):
+            d = orc.dequant_row("token_embd.weight", int(row), r["cols"])
+            assert np.array_equal(d.view(np.uint32), g["embd_deq"][i].view(np.uint32))
+    finally:
+        orc.close()
+
+
+def test_oracle_decode_against_reference():
+    g = np.load(os.path.join(GOLD, "decode_tiny.npz"))
+    path = helpers.model_path(INDEX["decode_tiny.npz"]["spec"])
+    assert helpers.file_sha(path) == INDEX["decode_tiny.npz"]["sha256"]
+    orc = helpers.Oracle(path, n_ctx=64)
+    try:
+        ids, lg = orc.decode(g["prompt"], 8)
+    finally:
+        orc.close()
+    assert np.array_equal(ids, g["ids"])
+    for k in range(8):
+        assert float(np.corrcoef(g["logits"][k], lg[k])[0, 1]) >= 0.9999
+        assert helpers.rel_rms(g["logits"][k], lg[k]) <= 2e-2
+
+
+def test_quantize_edge_cases():
+    """sml_quantize_act's rules on hand-made groups: zero group, exact .5 ties
+    (round half to even), saturation at +-127, sums."""
+    x = np.zeros(128, np.float32)
+    x[32:64] = np.arange(32, dtype=np.float32) - 16.0          # amax 16: codes = rint(v * 127/16)
+    x[64:96] = 127.0
+    x[64] = -127.0
+    x[96:128] = np.float32(0.5) * np.arange(32, dtype=np.float32)
+    q, s, sums = helpers.oracle_quant(x)
+    assert (q[:32] == 0).all() and s[0] == 0.0 and sums[0] == 0
+    assert s[1] == np.float32(16.0) / np.float32(127.0)
+    assert q[64] == -127 and (q[65:96] == 127).all()
+    assert sums[2] == 31 * 127 - 127
+    assert int(q[32:64].astype(np.int32).sum()) == int(sums[1])
+
+
+def test_moe_route_matches_reference():
+    rng = np.random.default_rng(12)
+    for trial in range(20):
+        lg = rng.standard_normal(128).astype(np.float32)
+        if trial % 4 == 0:
+            lg[rng.integers(0, 128, 8)] = lg.max()      # ties: the lower index wins
+        sel, w = helpers.oracle_route(lg, 8, 1)
+        order = sorted(range(128), key=lambda e: (-lg[e], e))[:8]
+        assert list(sel) == order
+        e = np.exp((lg[sel] - lg[sel[0]]).astype(np.float64))
+        assert np.allclose(w, e / e.sum(), rtol=1e-6)
+        if helpers.have_ref():
+            rs, rw = helpers.ref("route", lg=lg, k=8, flags=1)
+            assert np.array_equal(rs, sel) and np.array_equal(rw.view(np.uint32), w.view(np.uint32))
