@@ -81,6 +81,21 @@ int sb_tset_dequant_rows(sb_tset * t, const char * name, const int * rows, int n
 int sb_quantize_act(const float * x, const int32_t * perm, int n, int8_t * q, float * s, int32_t * sums,
                     void * stream);
 
+// ------------------------------------------------------------------ attention
+// One decode step of attention (the decode graph's k_attn kernel), device
+// pointers: qkv = this token's [q (n_head*hd) | k (n_kv*hd) | v (n_kv*hd)]
+// before RoPE; kc, vc = fp16 caches [n_ctx][n_kv*hd] (positions < pos are read,
+// the token's roped key and its value are written at pos); rope_cos, rope_sin
+// = [n_ctx][hd/2] tables; q_norm, k_norm = per-head RMS gains (hd) or NULL;
+// out = [n_head*hd]. The chunk partials live in scratch the call allocates and
+// frees. Synchronizes the stream; returns 1, or 0 (sb_attn_last_error()).
+// Replaces the sml_g_attn2 launch (sml/sml-gpu-fwd.c:346-356; the kernel
+// sml/sml-gpu-fast.cu:363-453).
+int sb_attn_decode(const float * qkv, uint16_t * kc, uint16_t * vc, const float * rope_cos, const float * rope_sin,
+                   const float * q_norm, const float * k_norm, float eps, int n_head, int n_head_kv, int head_dim,
+                   int n_ctx, int pos, float scale, float * out, void * stream);
+const char * sb_attn_last_error(void);
+
 // ------------------------------------------------------------------ models
 // Seeded synthetic SSF writer (the inputs every test and bench runs on; the
 // reference builds SSF files offline, tooling/sml_quantize.py:596-651).

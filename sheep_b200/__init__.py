@@ -73,6 +73,9 @@ def lib():
         "sb_quantize_act": (ip, [vp, vp, ip, vp, vp, vp, vp]),
         "ssfgen_write": (ip, [cp, vp, cp, ip]),
         "sb_ssf_check": (ip, [cp, cp, ip]),
+        "sb_attn_decode": (ip, [vp, vp, vp, vp, vp, vp, vp, ctypes.c_float, ip, ip, ip, ip, ip, ctypes.c_float,
+                                vp, vp]),
+        "sb_attn_last_error": (cp, []),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)

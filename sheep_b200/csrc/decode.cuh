@@ -144,7 +144,8 @@ struct AttnArgs {
     const float * rcos, * rsin;   // [n_ctx][hd/2] RoPE tables
     uint16_t * kc, * vc;     // this layer's cache, [n_ctx][kvd] fp16
     int n_ctx;
-    const int * pos;
+    const int * pos;         // device position, or NULL: pos_imm
+    int pos_imm;
     int chunk;               // positions per CTA
     float scale;             // 1/sqrt(hd)
     float * part;            // [n_head][max_chunks][hd + 2]
@@ -207,7 +208,7 @@ static __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_const
     pdl_wait();
     SB_MARK(g.trace, g.launch_id, 1);
     const int h = blockIdx.x, c = blockIdx.y, hd = g.hd, tid = threadIdx.x;
-    const int pos = *g.pos;
+    const int pos = g.pos ? *g.pos : g.pos_imm;
     const int nchunk = pos / g.chunk + 1;
     if (c >= nchunk) return;
     const int t0 = c * g.chunk, t1 = min(pos + 1, t0 + g.chunk), nt = t1 - t0;

@@ -151,3 +151,75 @@ def test_gemv_cfg0_shapes_stage_reuse():
     finally:
         ts.close()
         orc.close()
+
+
+# ------------------------------------------------------------------ decode attention
+
+def _attn_reference(qkv, kc, vc, cos, sin, nh, nkv, hd, pos, scale, qn=None, kn=None, eps=1e-6):
+    """RoPE by halved pairs, fp16 cache rounding, softmax attention in float64
+    (sml/sml-run.c:180-266, 339-375)."""
+    q = qkv[:nh * hd].reshape(nh, hd).astype(np.float64)
+    k = qkv[nh * hd:(nh + nkv) * hd].reshape(nkv, hd).astype(np.float64)
+    v = qkv[(nh + nkv) * hd:].reshape(nkv, hd).astype(np.float64)
+    if qn is not None:
+        q = q / np.sqrt((q * q).mean(1, keepdims=True) + eps) * qn
+        k = k / np.sqrt((k * k).mean(1, keepdims=True) + eps) * kn
+    half = hd // 2
+
+    def rope(x):
+        a, b = x[:, :half], x[:, half:]
+        c, s = cos[pos].astype(np.float64), sin[pos].astype(np.float64)
+        return np.concatenate([a * c - b * s, a * s + b * c], 1)
+
+    q, k = rope(q), rope(k)
+    k16, v16 = k.astype(np.float16), v.astype(np.float16)
+    K = kc[:pos + 1].reshape(pos + 1, nkv, hd).astype(np.float64)
+    V = vc[:pos + 1].reshape(pos + 1, nkv, hd).astype(np.float64)
+    K[pos], V[pos] = k16, v16
+    rep = nh // nkv
+    out = np.zeros((nh, hd))
+    for h in range(nh):
+        s = K[:, h // rep] @ q[h] * scale
+        p = np.exp(s - s.max())
+        out[h] = (p / p.sum()) @ V[:, h // rep]
+    return out.reshape(-1), k16, v16
+
+
+@pytest.mark.parametrize("hd,nh,nkv,pos,norm", [(128, 12, 2, 0, False), (128, 12, 2, 37, False),
+                                                 (128, 12, 2, 64, False), (128, 12, 2, 200, False),
+                                                 (64, 8, 2, 130, True), (128, 32, 8, 255, False)])
+def test_attention_decode(hd, nh, nkv, pos, norm):
+    torch = _torch()
+    rng = np.random.default_rng(pos + hd)
+    n_ctx = 256
+    qkv = rng.standard_normal((nh + 2 * nkv) * hd).astype(np.float32)
+    kc = rng.standard_normal((n_ctx, nkv * hd)).astype(np.float16)
+    vc = rng.standard_normal((n_ctx, nkv * hd)).astype(np.float16)
+    i = np.arange(hd // 2, dtype=np.float32)
+    freq = np.float32(1e6) ** (-i / np.float32(hd // 2))
+    ang = np.arange(n_ctx, dtype=np.float32)[:, None] * freq[None, :]
+    cos, sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+    qn = (1.0 + 0.1 * rng.standard_normal(hd)).astype(np.float32) if norm else None
+    kn = (1.0 + 0.1 * rng.standard_normal(hd)).astype(np.float32) if norm else None
+    scale = 1.0 / np.sqrt(hd)
+    want, k16, v16 = _attn_reference(qkv, kc, vc, cos, sin, nh, nkv, hd, pos, scale, qn, kn)
+    d = {n: torch.from_numpy(np.ascontiguousarray(a)).cuda() for n, a in
+         dict(qkv=qkv, kc=kc.view(np.uint16), vc=vc.view(np.uint16), cos=cos, sin=sin).items()}
+    dn = {n: (torch.from_numpy(a).cuda() if a is not None else None) for n, a in dict(qn=qn, kn=kn).items()}
+    out = torch.zeros(nh * hd, dtype=torch.float32, device="cuda")
+    L = sheep_b200.lib()
+    ok = L.sb_attn_decode(d["qkv"].data_ptr(), d["kc"].data_ptr(), d["vc"].data_ptr(), d["cos"].data_ptr(),
+                          d["sin"].data_ptr(), dn["qn"].data_ptr() if norm else None,
+                          dn["kn"].data_ptr() if norm else None, 1e-6, nh, nkv, hd, n_ctx, pos, float(scale),
+                          out.data_ptr(), None)
+    assert ok, L.sb_attn_last_error()
+    got = out.cpu().numpy()
+    assert helpers.rel_rms(want, got) <= 1e-5
+    # the cache row at pos: the roped key and the value, fp16 (last-bit ties allowed)
+    kw = d["kc"].cpu().numpy().view(np.float16)[pos].reshape(nkv, hd)
+    vw = d["vc"].cpu().numpy().view(np.float16)[pos].reshape(nkv, hd)
+    assert np.array_equal(vw, v16)
+    assert np.abs(kw.astype(np.float64) - k16.astype(np.float64)).max() <= \
+        np.abs(k16.astype(np.float64)).max() * 2.0 ** -10
+    # positions other than pos untouched
+    assert np.array_equal(d["kc"].cpu().numpy()[:pos], kc.view(np.uint16)[:pos])
