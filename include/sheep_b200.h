@@ -95,6 +95,20 @@ int sb_attn_decode(const float * qkv, uint16_t * kc, uint16_t * vc, const float 
                    const float * q_norm, const float * k_norm, float eps, int n_head, int n_head_kv, int head_dim,
                    int n_ctx, int pos, float scale, float * out, void * stream);
 const char * sb_attn_last_error(void);
+// sb_attn_decode for callers that cannot allocate device memory (a host that
+// owns every allocation up front, or one that must not synchronize the device
+// mid-stream): same arguments and results, but the chunk partials live in a
+// static device array of 1 MiB (+ 256 counters) that every GPU loading the
+// library holds until exit, and nothing is allocated. Rejects, with an error,
+// calls needing more (n_head x chunks x (head_dim + 2) floats > 1 MiB, or > 256
+// heads). All calls share the array: calls that overlap on the GPU race. The
+// first call on a device finds the array's address and clears the counters
+// (synchronizing once), so make it before any stream capture. Asynchronous on
+// `stream`. No counterpart in the reference: an addition of this library.
+int sb_attn_decode_noalloc(const float * qkv, uint16_t * kc, uint16_t * vc, const float * rope_cos,
+                           const float * rope_sin, const float * q_norm, const float * k_norm, float eps, int n_head,
+                           int n_head_kv, int head_dim, int n_ctx, int pos, float scale, float * out, void * stream);
+const char * sb_attn_noalloc_last_error(void);
 
 // ------------------------------------------------------------------ models
 // Seeded synthetic SSF writer (the inputs every test and bench runs on; the

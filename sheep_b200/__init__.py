@@ -76,6 +76,9 @@ def lib():
         "sb_attn_decode": (ip, [vp, vp, vp, vp, vp, vp, vp, ctypes.c_float, ip, ip, ip, ip, ip, ctypes.c_float,
                                 vp, vp]),
         "sb_attn_last_error": (cp, []),
+        "sb_attn_decode_noalloc": (ip, [vp, vp, vp, vp, vp, vp, vp, ctypes.c_float, ip, ip, ip, ip, ip,
+                                        ctypes.c_float, vp, vp]),
+        "sb_attn_noalloc_last_error": (cp, []),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
