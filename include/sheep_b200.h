@@ -110,6 +110,38 @@ int sb_attn_decode_noalloc(const float * qkv, uint16_t * kc, uint16_t * vc, cons
                            int n_head_kv, int head_dim, int n_ctx, int pos, float scale, float * out, void * stream);
 const char * sb_attn_noalloc_last_error(void);
 
+// ------------------------------------------------------------------ MoE FFN
+// One mixture-of-experts FFN layer of an SSF file on the current device:
+// router (fp32, double accumulation), top-k routing with ties to the lower
+// index and softmax weights (renormalized over the chosen experts when
+// moe_flags bit 0 is set), each chosen expert's SwiGLU FFN, and the weighted
+// sum in choice order -- per row, what moe_ffn does (sml/sml-run.c:3071-3125;
+// on the reference's GPU moe_ffn_dev, sml/sml-gpu-fwd.c:492-546). Rows are
+// the FFN's input (already normalized). Refused with a reason: routing other
+// than flags 0/1, shared experts, an expert bias, scaled weights.
+typedef struct sb_moe sb_moe;
+sb_moe * sb_moe_open(const char * path, int layer, int max_tokens, char * why, int nwhy);
+void sb_moe_close(sb_moe * m);
+// out[10]: n_embd, expert hidden size, experts, experts per token, flags,
+// max_tokens, expert width in bits, bytes of one expert as stored (low, high),
+// router bytes.
+void sb_moe_info(const sb_moe * m, int * out);
+// y[n_tok][n_embd] from x[n_tok][n_embd], device pointers, asynchronous on
+// `stream`. Calls on one handle must not overlap (they share its scratch).
+int sb_moe_forward(sb_moe * m, const float * x, int n_tok, float * y, void * stream);
+// The same with host rows (copies included, synchronous); sel and w
+// (n_tok x k: chosen experts and weights) and n_active (distinct experts)
+// may be NULL.
+int sb_moe_forward_host(sb_moe * m, const float * x, int n_tok, float * y, int * sel, float * w, int * n_active);
+// Mean device time (CUDA events) of one forward over rows already on the
+// device, with a buffer larger than L2 rewritten before each timed run.
+int sb_moe_time(sb_moe * m, const float * x_host, int n_tok, int reps, float * ms_avg, int * n_active);
+// Routing alone, device pointers: logits[n_tok][n_expert] -> sel, w
+// [n_tok][k] (sml_moe_route, sml/sml-run.c:2925, for moe_flags 0 and 1).
+int sb_moe_route(const float * logits, int n_tok, int n_expert, int k, unsigned flags, int * sel, float * w,
+                 void * stream);
+const char * sb_moe_last_error(void);
+
 // ------------------------------------------------------------------ models
 // Seeded synthetic SSF writer (the inputs every test and bench runs on; the
 // reference builds SSF files offline, tooling/sml_quantize.py:596-651).

@@ -384,8 +384,9 @@ int so_moe_route(const float * lg, int ne, int k, unsigned moe_flags, int * sel,
     return k;
 }
 
-// sml/sml-run.c:3071-3125 (gated experts, no shared expert)
-static void moe_ffn(so_model * m, int L, const float * xb, float * out) {
+// sml/sml-run.c:3071-3125 (gated experts, no shared expert); the chosen
+// experts and weights go to sel_out / w_out when they are not NULL
+static int moe_ffn(so_model * m, int L, const float * xb, float * out, int * sel_out, float * w_out) {
     const int E = (int) m->n_embd;
     const rec_t * rt = findf(m, "blk.%d.ffn_gate_inp.weight", L, 0);
     const int ne = (int) ((uint64_t) rt->rows * rt->cols / E);
@@ -393,6 +394,10 @@ static void moe_ffn(so_model * m, int L, const float * xb, float * out) {
     matvec_f32(f32p(m, rt), ne, E, xb, lg);
     int sel[16]; float w[16];
     const int k = so_moe_route(lg, ne, (int) m->n_expert_used, m->moe_flags, sel, w);
+    for (int j = 0; j < k; j++) {
+        if (sel_out) sel_out[j] = sel[j];
+        if (w_out) w_out[j] = w[j];
+    }
     const rec_t * u0 = findf(m, "blk.%d.ffn_up.%d.weight", L, 0);
     const int F = (int) u0->rows;
     float * g = (float *) malloc((size_t) F * 4), * u = (float *) malloc((size_t) F * 4);
@@ -406,6 +411,14 @@ static void moe_ffn(so_model * m, int L, const float * xb, float * out) {
         for (int i = 0; i < E; i++) out[i] += w[j] * t[i];
     }
     free(lg); free(g); free(u); free(t);
+    return k;
+}
+
+// The MoE FFN of layer L on one (already normalized) row: returns the experts
+// per token, 0 if layer L has no router.
+int so_moe_ffn(so_model * m, int L, const float * xb, float * out, int * sel, float * w) {
+    if (L < 0 || L >= (int) m->n_layer || !findf(m, "blk.%d.ffn_gate_inp.weight", L, 0)) return 0;
+    return moe_ffn(m, L, xb, out, sel, w);
 }
 
 static void add_bias(float * y, const float * b, int n) { if (b) for (int i = 0; i < n; i++) y[i] += b[i]; }
@@ -448,7 +461,7 @@ int so_forward(so_model * m, int tok, int pos, float * logits) {
         for (int i = 0; i < E; i++) x[i] += hb2[i];
         rms_norm(xb, x, f32p(m, findf(m, "blk.%d.ffn_norm.weight", L, 0)), E, m->eps);
         if (findf(m, "blk.%d.ffn_gate_inp.weight", L, 0)) {
-            moe_ffn(m, L, xb, hb2);
+            moe_ffn(m, L, xb, hb2, NULL, NULL);
             for (int i = 0; i < E; i++) x[i] += hb2[i];
             continue;
         }

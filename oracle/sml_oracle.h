@@ -32,6 +32,10 @@ int so_decode(so_model * m, const int * prompt, int np, int ngen, int * ids, flo
 
 // sml/sml-run.c:2925-3040, the softmax-top-k branch (moe_flags bit 0 = renormalise)
 int so_moe_route(const float * lg, int ne, int k, unsigned moe_flags, int * sel, float * w);
+// sml/sml-run.c:3071-3125: the MoE FFN of layer L on one normalized row, with
+// the chosen experts and weights (either may be NULL); returns k, 0 if layer L
+// has no router.
+int so_moe_ffn(so_model * m, int L, const float * xb, float * out, int * sel, float * w);
 
 #ifdef __cplusplus
 }

@@ -79,6 +79,14 @@ def lib():
         "sb_attn_decode_noalloc": (ip, [vp, vp, vp, vp, vp, vp, vp, ctypes.c_float, ip, ip, ip, ip, ip,
                                         ctypes.c_float, vp, vp]),
         "sb_attn_noalloc_last_error": (cp, []),
+        "sb_moe_open": (vp, [cp, ip, ip, cp, ip]),
+        "sb_moe_close": (None, [vp]),
+        "sb_moe_info": (None, [vp, vp]),
+        "sb_moe_forward": (ip, [vp, vp, ip, vp, vp]),
+        "sb_moe_forward_host": (ip, [vp, vp, ip, vp, vp, vp, vp]),
+        "sb_moe_time": (ip, [vp, vp, ip, ip, fp, vp]),
+        "sb_moe_route": (ip, [vp, ip, ip, ip, ctypes.c_uint, vp, vp, vp]),
+        "sb_moe_last_error": (cp, []),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -229,6 +237,62 @@ class TensorSet:
             self.close()
         except Exception:
             pass
+
+
+class MoeLayer:
+    """One mixture-of-experts FFN layer of an SSF file on the GPU (sb_moe_*)."""
+
+    def __init__(self, path, layer=0, max_tokens=256):
+        why = ctypes.create_string_buffer(512)
+        self.h = lib().sb_moe_open(path.encode(), layer, max_tokens, why, 512)
+        if not self.h:
+            raise RuntimeError(f"sb_moe_open: {why.value.decode()}")
+        info = (ctypes.c_int * 10)()
+        lib().sb_moe_info(self.h, info)
+        self.n_embd, self.n_ff, self.n_expert, self.k, self.flags, self.max_tokens, self.nbits = info[:7]
+        self.expert_bytes = (info[7] & 0xffffffff) | (info[8] << 32)
+        self.router_bytes = info[9]
+
+    def forward(self, x):
+        """y [T, n_embd], sel and w [T, k], distinct experts, from rows x [T, n_embd]."""
+        x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+        T = len(x)
+        y = np.zeros_like(x)
+        sel = np.zeros((T, self.k), np.int32)
+        w = np.zeros((T, self.k), np.float32)
+        na = ctypes.c_int()
+        if not lib().sb_moe_forward_host(self.h, _p(x), T, _p(y), _p(sel), _p(w), ctypes.byref(na)):
+            raise RuntimeError(f"sb_moe_forward_host: {lib().sb_moe_last_error().decode()}")
+        return y, sel, w, na.value
+
+    def forward_dev(self, x_ptr, n_tok, y_ptr, stream=0):
+        if not lib().sb_moe_forward(self.h, x_ptr, n_tok, y_ptr, stream):
+            raise RuntimeError(f"sb_moe_forward: {lib().sb_moe_last_error().decode()}")
+
+    def time(self, x, reps):
+        """(mean device ms of one forward with L2 flushed before each, distinct experts)."""
+        x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+        ms, na = ctypes.c_float(), ctypes.c_int()
+        if not lib().sb_moe_time(self.h, _p(x), len(x), reps, ctypes.byref(ms), ctypes.byref(na)):
+            raise RuntimeError(f"sb_moe_time: {lib().sb_moe_last_error().decode()}")
+        return ms.value, na.value
+
+    def close(self):
+        if self.h:
+            lib().sb_moe_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def moe_route_dev(logits_ptr, n_tok, n_expert, k, flags, sel_ptr, w_ptr, stream=0):
+    """Routing alone on device buffers (sb_moe_route)."""
+    if not lib().sb_moe_route(logits_ptr, n_tok, n_expert, k, flags, sel_ptr, w_ptr, stream):
+        raise RuntimeError(f"sb_moe_route: {lib().sb_moe_last_error().decode()}")
 
 
 # ----------------------------------------------------------------- sml-gpu.h mirror

@@ -6,6 +6,7 @@
 // captured graph per token whose kernels chain by programmatic dependent
 // launch, and the greedy choice made on the device so a generation loop is
 // graph replays with no host round trip.
+#include "moe_host.h"
 #include "tgemv.cuh"
 #include "sheep_b200.h"
 #include "ssf.h"
@@ -38,6 +39,8 @@ struct LayerD {
     const float * qkv_b = nullptr;    // q|k|v biases, or NULL
     const float * qn = nullptr, * kn = nullptr;
     const int32_t * down_iperm = nullptr;
+    bool moe = false;                 // mixture-of-experts FFN in place of gate/up/down
+    MoeLayer ml;
 };
 
 struct sb_engine {
@@ -60,6 +63,7 @@ struct sb_engine {
     unsigned * am_cnt = nullptr;
     float * apart = nullptr;
     unsigned * acnt = nullptr;
+    MoeScratch ms;                    // routing scratch shared by every MoE layer (one token)
     int * err = nullptr;              // bounded waits that gave up
     unsigned long long * trace = nullptr;   // trace build: [launch][cta][8] timestamps
     int n_launch_trace = 0;
@@ -84,6 +88,22 @@ static const float * up_f32(sb_engine * e, const ssf_rec * r) { return upload_f3
 
 // ------------------------------------------------------------------ launch
 
+// Count every launch; in sync mode (SB_SYNC=1) finish it and check its error
+// flag before the next is enqueued.
+static void after_launch(sb_engine * e, cudaError_t r) {
+    e->launches++;
+    if (e->sync_mode && !e->failed) {
+        if (r == cudaSuccess) r = cudaStreamSynchronize(e->st);
+        int err = 0;
+        if (r == cudaSuccess) r = cudaMemcpy(&err, e->err, 4, cudaMemcpyDeviceToHost);
+        if (r != cudaSuccess || err) {
+            snprintf(g_err, sizeof g_err, "kernel %s: %s (check code %d)", e->cur,
+                     r != cudaSuccess ? cudaGetErrorString(r) : "bounds check failed", err);
+            e->failed = true;
+        }
+    }
+}
+
 template <typename... KArgs, typename... Args>
 static cudaError_t launch(sb_engine * e, bool pdl, void (*k)(KArgs...), dim3 grid, dim3 block, size_t smem,
                           Args &&... args) {
@@ -97,18 +117,8 @@ static cudaError_t launch(sb_engine * e, bool pdl, void (*k)(KArgs...), dim3 gri
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = pdl ? 1 : 0;
-    e->launches++;
-    cudaError_t r = cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
-    if (e->sync_mode && !e->failed) {
-        if (r == cudaSuccess) r = cudaStreamSynchronize(e->st);
-        int err = 0;
-        if (r == cudaSuccess) r = cudaMemcpy(&err, e->err, 4, cudaMemcpyDeviceToHost);
-        if (r != cudaSuccess || err) {
-            snprintf(g_err, sizeof g_err, "kernel %s: %s (check code %d)", e->cur,
-                     r != cudaSuccess ? cudaGetErrorString(r) : "bounds check failed", err);
-            e->failed = true;
-        }
-    }
+    const cudaError_t r = cudaLaunchKernelEx(&cfg, k, std::forward<Args>(args)...);
+    after_launch(e, r);
     return r;
 }
 
@@ -177,6 +187,13 @@ static void set_next(TGArgs & g, const TT * nt, int nsm) {
 
 static void launch_tg(sb_engine * e, int mode, const TGArgs & g) {
     const int grid = g.t.ntiles < e->nsm ? g.t.ntiles : e->nsm;
+    if (tg_smem(g) > 200 * 1024) {
+        // the staged activation and one ring stage per consumer warp must fit
+        snprintf(g_err, sizeof g_err, "kernel %s: %zu bytes of shared memory (tiles of %u bytes over %d columns)",
+                 e->cur, tg_smem(g), g.t.tb, g.t.cols);
+        e->failed = true;
+        return;
+    }
     SB_DISPATCH_QT(g.t.nbits, g.t.six, launch_tg_nb, e, mode, g, grid, tg_smem(g));
 }
 
@@ -208,8 +225,15 @@ static void enqueue_token(sb_engine * e) {
         snprintf(e->cur, sizeof e->cur, "L%d.o", l);
         {
             TGArgs g = tg_args(e, y.o, e->att, nullptr, e->x);
-            set_next(g, &y.gateup, e->nsm);
+            set_next(g, y.moe ? nullptr : &y.gateup, e->nsm);
             launch_tg(e, GM_O, g);
+        }
+        if (y.moe) {
+            // router on rmsnorm(x), experts, combine added to x (sml/sml-run.c:3503-3507)
+            snprintf(e->cur, sizeof e->cur, "L%d.moe", l);
+            moe_enqueue(y.ml, e->ms, e->x, 1, y.fn, e->eps, e->x, 1, e->nsm, e->st, true, e->err, e->trace,
+                        e->launches, [&](cudaError_t r, const char *) { after_launch(e, r); });
+            continue;
         }
         snprintf(e->cur, sizeof e->cur, "L%d.ffn", l);
         {
@@ -280,22 +304,24 @@ static bool build(sb_engine * e, char * why, int nwhy) {
     e->bytes_tok += tt_bytes(e->head);
     e->out_norm = up_f32(e, ssf_find(&f, "output_norm.weight"));
     e->L.assign(e->n_layer, LayerD());
+    const MoeLayer * moe0 = nullptr;
     for (int l = 0; l < e->n_layer; l++) {
         LayerD & y = e->L[l];
         auto R = [&](const char * fmt) { return ssf_findf(&f, fmt, l, 0); };
-        if (R("blk.%d.ffn_gate_inp.weight")) { snprintf(why, nwhy, "mixture-of-experts layers"); return false; }
         if (!R("blk.%d.attn_norm.weight") || !R("blk.%d.ffn_norm.weight")) { snprintf(why, nwhy, "layer %d: missing norms", l); return false; }
         const ssf_rec * q = R("blk.%d.attn_q.weight"), * k = R("blk.%d.attn_k.weight"), * v = R("blk.%d.attn_v.weight");
         const ssf_rec * o = R("blk.%d.attn_output.weight"), * gt = R("blk.%d.ffn_gate.weight"), * up = R("blk.%d.ffn_up.weight");
         const ssf_rec * dn = R("blk.%d.ffn_down.weight");
-        if (!q || !k || !v || !o || !gt || !up || !dn) { snprintf(why, nwhy, "layer %d: missing projections", l); return false; }
+        y.moe = R("blk.%d.ffn_gate_inp.weight") != nullptr;
+        if (!q || !k || !v || !o || (!y.moe && (!gt || !up || !dn))) { snprintf(why, nwhy, "layer %d: missing projections", l); return false; }
         if ((int) q->rows != e->qd || (int) k->rows != e->kvd || (int) v->rows != e->kvd || (int) q->cols != e->E ||
-            (int) o->rows != e->E || (int) o->cols != e->qd || (int) gt->cols != e->E || gt->rows != up->rows ||
-            (int) dn->rows != e->E || dn->cols != gt->rows || gt->rows % 8) {
+            (int) o->rows != e->E || (int) o->cols != e->qd ||
+            (!y.moe && ((int) gt->cols != e->E || gt->rows != up->rows || (int) dn->rows != e->E ||
+                        dn->cols != gt->rows || gt->rows % 8))) {
             snprintf(why, nwhy, "layer %d: tensor shapes do not match the header", l);
             return false;
         }
-        const int F = (int) gt->rows;
+        const int F = y.moe ? 0 : (int) gt->rows;
         e->F = F > e->F ? F : e->F;
         // q | k | v as one tensor (they share an input; sml/sml-run.c:1796 groups them)
         if (!upload_tt(e->ar, f, q, e->qd + 2 * e->kvd, 0, min_tiles, 0, [&](int r) {
@@ -303,21 +329,34 @@ static bool build(sb_engine * e, char * why, int nwhy) {
                      : r < e->qd + 2 * e->kvd ? RowSrc{v, r - e->qd - e->kvd} : RowSrc{nullptr, 0}; },
                        y.qkv, why, nwhy))
             return false;
+        if (y.moe) {
+            if (!moe_upload(e->ar, f, l, y.ml, why, nwhy)) return false;
+            if (moe0 && (y.ml.E != moe0->E || y.ml.F != moe0->F || y.ml.ne != moe0->ne || y.ml.k != moe0->k)) {
+                snprintf(why, nwhy, "layer %d: MoE layers differ in shape", l);
+                return false;
+            }
+            if (!moe0) moe0 = &y.ml;
+        }
         // gate / up: a tile of TR rows holds TR/2 gate rows then the same TR/2 up rows
-        const int gtr = pick_tr(2 * F, (int) tile_geom(e->E, 1, (int) gt->nbits, e->six, gt->mq_n != 0).bytes,
-                                min_tiles, 1);
-        if (!upload_tt(e->ar, f, gt, 2 * F, gtr, min_tiles, 1, [&](int r) {
-                const int h = gtr / 2, ti = r / gtr, j = r % gtr, i = ti * h + j % h;
-                return i >= F ? RowSrc{nullptr, 0} : RowSrc{j < h ? gt : up, i}; },
-                       y.gateup, why, nwhy))
-            return false;
         if (!upload_tt(e->ar, f, o, e->E, 0, min_tiles, 0, [&](int r) { return RowSrc{r < e->E ? o : nullptr, r}; },
-                       y.o, why, nwhy) ||
-            !upload_tt(e->ar, f, dn, e->E, 0, min_tiles, 0, [&](int r) { return RowSrc{r < e->E ? dn : nullptr, r}; },
-                       y.down, why, nwhy))
+                       y.o, why, nwhy))
             return false;
-        y.down_iperm = y.down.iperm;
-        e->bytes_tok += tt_bytes(y.qkv) + tt_bytes(y.gateup) + tt_bytes(y.o) + tt_bytes(y.down);
+        if (!y.moe) {
+            const int gtr = pick_tr(2 * F, (int) tile_geom(e->E, 1, (int) gt->nbits, e->six, gt->mq_n != 0).bytes,
+                                    min_tiles, 1);
+            if (!upload_tt(e->ar, f, gt, 2 * F, gtr, min_tiles, 1, [&](int r) {
+                    const int h = gtr / 2, ti = r / gtr, j = r % gtr, i = ti * h + j % h;
+                    return i >= F ? RowSrc{nullptr, 0} : RowSrc{j < h ? gt : up, i}; },
+                           y.gateup, why, nwhy) ||
+                !upload_tt(e->ar, f, dn, e->E, 0, min_tiles, 0, [&](int r) { return RowSrc{r < e->E ? dn : nullptr, r}; },
+                           y.down, why, nwhy))
+                return false;
+            y.down_iperm = y.down.iperm;
+        }
+        // per token: the router and the k chosen experts (as tiles)
+        e->bytes_tok += tt_bytes(y.qkv) + tt_bytes(y.o) +
+                        (y.moe ? y.ml.router_bytes + (uint64_t) y.ml.k * (tt_bytes(y.ml.gu) + tt_bytes(y.ml.dn))
+                               : tt_bytes(y.gateup) + tt_bytes(y.down));
         y.an = up_f32(e, R("blk.%d.attn_norm.weight"));
         y.fn = up_f32(e, R("blk.%d.ffn_norm.weight"));
         const ssf_rec * qb = R("blk.%d.attn_q.bias"), * kb = R("blk.%d.attn_k.bias"), * vb = R("blk.%d.attn_v.bias");
@@ -362,8 +401,9 @@ static bool build(sb_engine * e, char * why, int nwhy) {
     e->apart = (float *) carve(e, (size_t) e->nh * e->max_chunks * (e->hd + 2) * 4);
     e->acnt = (unsigned *) carve(e, (size_t) e->nh * 4);
     e->err = (int *) carve(e, 4);
+    if (moe0) moe_carve(e->ar, *moe0, 1, e->ms);
 #ifdef SB_TRACE
-    e->n_launch_trace = 6 * e->n_layer + 8;
+    e->n_launch_trace = 8 * e->n_layer + 8;
     e->trace = (unsigned long long *) carve(e, (size_t) e->n_launch_trace * kTraceCtas * 8 * 8);
 #endif
     return true;
@@ -384,6 +424,8 @@ static uint64_t rec_bytes(const ssf_rec * r) {
 // Leaves the decode state undefined: call it after generating, not between.
 extern "C" int sb_time_kernel(sb_engine * e, int which, int reps, float * ms_avg, double * bytes_out) {
     if (!e || reps < 1 || e->sync_mode) return 0;
+    if (which == 3 || which == 4)
+        for (const LayerD & y : e->L) if (y.moe) return 0;   // no dense FFN to time
     const ssf_file & f = e->f;
     auto layer_bytes = [&](int l) -> double {
         auto R = [&](const char * fmt) { return ssf_findf(&f, fmt, l, 0); };
@@ -519,7 +561,7 @@ sb_engine * sb_open(const char * path, int n_ctx, char * why, int nwhy) {
         ok = ok && ck(cudaGraphInstantiateWithFlags(&e->g_tok, gr, 0), "instantiate");
         if (gr) cudaGraphDestroy(gr);
     }
-    ok = ok && ck(cudaDeviceSynchronize(), "open");
+    ok = ok && ck(cudaDeviceSynchronize(), "open") && !e->failed;
     if (!ok) {
         snprintf(why, nwhy, "%s", g_err);
         close_all(e); delete e; return nullptr;

@@ -1,0 +1,255 @@
+// Host side of the mixture-of-experts FFN: upload of one layer's router and
+// experts, the routing scratch, and the four launches of one layer.
+//
+// Expert e of layer L is blk.L.ffn_{gate,up,down}.e.weight (the loader's names,
+// sml/sml-run.c:1675-1700); the router blk.L.ffn_gate_inp.weight is fp32 with
+// n_expert x n_embd values. Every expert of a layer is tiled with the same
+// geometry, so one TT describes them all and per-expert tables give the tile
+// bases and column orders.
+#pragma once
+
+#include "moe.cuh"
+#include "upload.h"
+
+#include <cstdio>
+#include <vector>
+
+namespace sb {
+
+struct MoeLayer {
+    int E = 0, F = 0, ne = 0, k = 0;
+    unsigned flags = 0;
+    const float * router = nullptr;                        // [ne][E]
+    TT gu{}, dn{};                                         // geometry (expert 0's tiles)
+    const uint8_t * const * gu_tiles = nullptr;            // device tables, [ne] each
+    const int32_t * const * gu_perm = nullptr;
+    const uint8_t * const * dn_tiles = nullptr;
+    const int32_t * const * dn_iperm = nullptr;
+    uint64_t expert_file_bytes = 0;                        // gate + up + down of one expert, as stored
+    uint64_t router_bytes = 0;
+};
+
+struct MoeScratch {
+    int T = 0;
+    float * xn = nullptr, * hp = nullptr, * yk = nullptr;
+    MoeRoute r{};
+};
+
+inline uint64_t moe_rec_bytes(const ssf_rec * r) {
+    uint64_t b = r->sd_n + r->sq_n + r->md_n + r->mq_n;
+    for (int p = 0; p < SSF_MAX_LEVELS; p++) b += r->codes_n[p];
+    return b;
+}
+
+// Why layer L's MoE cannot run here, or NULL.
+inline const char * moe_unsupported(const ssf_file & f, int L) {
+    const ssf_hdr * h = f.hdr;
+    if (h->moe_flags & ~1u) return "sigmoid, grouped or sparsemixer expert routing";
+    if (h->moe_scale != 0.0f) return "scaled expert weights";
+    if (h->moe_groups > 1) return "grouped expert routing";
+    const char * names[] = {"blk.%d.ffn_gate_shexp.weight", "blk.%d.ffn_up_shexp.weight",
+                            "blk.%d.ffn_down_shexp.weight", "blk.%d.exp_probs_b.weight"};
+    for (const char * n : names) if (ssf_findf(&f, n, L, 0)) return "shared experts or an expert bias";
+    return nullptr;
+}
+
+// Shared memory of the grouped GEMV: eight staged activations and at least
+// one ring stage per consumer warp must fit in kMoeSmem.
+constexpr size_t kMoeSmem = 200 * 1024;
+inline size_t moe_act_bytes(int cols) { return (act_smem_bytes(cols) + 127) / 128 * 128; }
+
+// Rows per expert tile: the most (<= 16, even for gate/up pairs) whose tile
+// stays under 12 KB and whose ring of kConsWarps stages fits beside eight
+// staged activations; 0 if not even the fewest rows fit.
+inline int moe_pick_tr(int cols, int nbits, int six, int has_min, int even) {
+    for (int tr = 16; tr >= (even ? 2 : 1); tr /= 2) {
+        const size_t tb = tile_geom(cols, tr, nbits, six, has_min).bytes;
+        if (tb <= 12288 && 8 * moe_act_bytes(cols) + (size_t) kConsWarps * tb <= kMoeSmem) return tr;
+    }
+    return 0;
+}
+
+// Upload layer L's router and experts (both arena passes run this).
+inline bool moe_upload(Arena & a, const ssf_file & f, int L, MoeLayer & m, char * why, int nwhy) {
+    const ssf_hdr * h = f.hdr;
+    const int E = (int) h->n_embd;
+    const ssf_rec * rt = ssf_findf(&f, "blk.%d.ffn_gate_inp.weight", L, 0);
+    if (!rt) { snprintf(why, nwhy, "layer %d: no router", L); return false; }
+    if (const char * u = moe_unsupported(f, L)) { snprintf(why, nwhy, "layer %d: %s", L, u); return false; }
+    const uint64_t rn = (uint64_t) rt->rows * rt->cols;
+    if (rt->kind != SSF_KIND_F32 || rn % E) { snprintf(why, nwhy, "layer %d: router is not fp32 n_embd wide", L); return false; }
+    if (E % 64 || E > 8192) { snprintf(why, nwhy, "layer %d: n_embd %d (a multiple of 64, at most 8192)", L, E); return false; }
+    m.E = E;
+    m.ne = (int) (rn / E);
+    if (m.ne < 1 || m.ne > kMoeMaxExperts) {
+        snprintf(why, nwhy, "layer %d: %d experts (at most %d)", L, m.ne, kMoeMaxExperts);
+        return false;
+    }
+    int k = (int) h->n_expert_used;
+    if (k <= 0 || k > m.ne) k = m.ne;   // sml/sml-run.c:2928-2930
+    if (k > kMoeMaxK) k = kMoeMaxK;
+    m.k = k;
+    m.flags = h->moe_flags;
+    m.router = upload_f32(a, f, rt);
+    m.router_bytes = rn * 4;
+    std::vector<const uint8_t *> gt(m.ne), dt(m.ne);
+    std::vector<const int32_t *> gp(m.ne), di(m.ne);
+    int gtr = 0, dtr = 0;
+    for (int e = 0; e < m.ne; e++) {
+        char nm[3][96];
+        snprintf(nm[0], sizeof nm[0], "blk.%d.ffn_gate.%d.weight", L, e);
+        snprintf(nm[1], sizeof nm[1], "blk.%d.ffn_up.%d.weight", L, e);
+        snprintf(nm[2], sizeof nm[2], "blk.%d.ffn_down.%d.weight", L, e);
+        const ssf_rec * g = ssf_find(&f, nm[0]), * u = ssf_find(&f, nm[1]), * d = ssf_find(&f, nm[2]);
+        if (!g || !u || !d) { snprintf(why, nwhy, "layer %d: expert %d is incomplete or ungated", L, e); return false; }
+        const int F = (int) g->rows;
+        if ((int) g->cols != E || u->rows != g->rows || (int) d->rows != E || (int) d->cols != F || F % 64 ||
+            (e > 0 && F != m.F)) {
+            snprintf(why, nwhy, "layer %d: expert %d shapes do not match", L, e);
+            return false;
+        }
+        m.F = F;
+        if (e == 0) {
+            gtr = moe_pick_tr(E, (int) g->nbits, f.scale6, g->mq_n != 0, 1);
+            dtr = moe_pick_tr(F, (int) d->nbits, f.scale6, d->mq_n != 0, 0);
+            if (!gtr || !dtr) { snprintf(why, nwhy, "layer %d: expert rows too wide for the tile ring", L); return false; }
+        }
+        TT tg, td;
+        // gate / up interleaved: a tile of gtr rows holds gtr/2 gate rows then the same up rows
+        if (!upload_tt(a, f, g, 2 * F, gtr, 0, 1, [&](int r) {
+                const int hh = gtr / 2, ti = r / gtr, j = r % gtr, i = ti * hh + j % hh;
+                return i >= F ? RowSrc{nullptr, 0} : RowSrc{j < hh ? g : u, i}; }, tg, why, nwhy) ||
+            !upload_tt(a, f, d, E, dtr, 0, 0, [&](int r) { return RowSrc{r < E ? d : nullptr, r}; }, td, why, nwhy))
+            return false;
+        if (e == 0) { m.gu = tg; m.dn = td; }
+        if (tg.nbits != m.gu.nbits || tg.has_min != m.gu.has_min || td.nbits != m.dn.nbits || td.has_min != m.dn.has_min) {
+            snprintf(why, nwhy, "layer %d: experts differ in width or fields", L);
+            return false;
+        }
+        gt[e] = tg.tiles; gp[e] = tg.perm; dt[e] = td.tiles; di[e] = td.iperm;
+        if (e == 0) m.expert_file_bytes = moe_rec_bytes(g) + moe_rec_bytes(u) + moe_rec_bytes(d);
+    }
+    m.gu_tiles = (const uint8_t * const *) a.upload(gt.data(), gt.size() * sizeof(void *));
+    m.gu_perm = (const int32_t * const *) a.upload(gp.data(), gp.size() * sizeof(void *));
+    m.dn_tiles = (const uint8_t * const *) a.upload(dt.data(), dt.size() * sizeof(void *));
+    m.dn_iperm = (const int32_t * const *) a.upload(di.data(), di.size() * sizeof(void *));
+    return true;
+}
+
+// Scratch for up to T tokens through layers shaped like m (carved from the arena).
+inline void moe_carve(Arena & a, const MoeLayer & m, int T, MoeScratch & s) {
+    const size_t ns = (size_t) T * m.k;
+    s.T = T;
+    s.xn = (float *) a.carve((size_t) T * m.E * 4);
+    s.hp = (float *) a.carve(ns * m.F * 4);
+    s.yk = (float *) a.carve(ns * m.E * 4);
+    s.r.logits = (float *) a.carve((size_t) T * m.ne * 4);
+    s.r.sel = (int *) a.carve(ns * 4);
+    s.r.w = (float *) a.carve(ns * 4);
+    s.r.slots = (int *) a.carve(ns * 4);
+    s.r.ch_e = (int *) a.carve(ns * 4);
+    s.r.ch_s0 = (int *) a.carve(ns * 4);
+    s.r.ch_n = (int *) a.carve(ns * 4);
+    s.r.meta = (int *) a.carve(2 * 4);
+    s.r.cnt = (unsigned *) a.carve(4);
+}
+
+// Ring stages for the grouped GEMV: a multiple of the consumer warps, ~96 KB,
+// within kMoeSmem beside eight staged activations (moe_pick_tr ensures one per warp fits).
+inline int moe_stages(const TT & t) {
+    int ns = (int) ((96 * 1024) / t.tb) / kConsWarps * kConsWarps;
+    const int fit = (int) ((kMoeSmem - 8 * moe_act_bytes(t.cols)) / t.tb) / kConsWarps * kConsWarps;
+    if (ns > fit) ns = fit;
+    return ns < kConsWarps ? kConsWarps : ns > kMaxStages ? kMaxStages : ns;
+}
+
+template <int NB, int SIX>
+inline void moe_gemv_w(int mode, int nt, const MoeGArgs & g, int grid, size_t smem, cudaStream_t st, bool pdl,
+                       cudaError_t * r) {
+    if (nt == 1 && mode != MG_PLAIN) {
+        *r = mode == MG_GU ? moe_gemv_launch<MG_GU, NB, SIX, 1>(g, grid, smem, st, pdl)
+                           : moe_gemv_launch<MG_DN, NB, SIX, 1>(g, grid, smem, st, pdl);
+    } else {
+        *r = mode == MG_GU ? moe_gemv_launch<MG_GU, NB, SIX, 8>(g, grid, smem, st, pdl)
+           : mode == MG_DN ? moe_gemv_launch<MG_DN, NB, SIX, 8>(g, grid, smem, st, pdl)
+                           : moe_gemv_launch<MG_PLAIN, NB, SIX, 8>(g, grid, smem, st, pdl);
+    }
+}
+
+// nt: tokens per chunk, 1 or 8 (a batched PLAIN GEMV always runs the 8-token kernel).
+inline cudaError_t moe_gemv(int mode, int nt, const MoeGArgs & g, int grid, cudaStream_t st, bool pdl) {
+    cudaError_t r = cudaErrorInvalidValue;
+    if (mode == MG_PLAIN) nt = 8;
+    SB_DISPATCH_QT(g.t.nbits, g.t.six, moe_gemv_w, mode, nt, g, grid, moe_gemv_smem(g, nt), st, pdl, &r);
+    return r;
+}
+
+// The launches of one MoE FFN over T <= s.T input rows x ([T][E]): router and
+// routing (x RMS-normalized by norm_w first when given), gate/up, down, combine
+// into y ([T][E]; added to it when resid). post(err, name) sees every launch.
+template <class Post>
+inline void moe_enqueue(const MoeLayer & m, const MoeScratch & s, const float * x, int T, const float * norm_w,
+                        float eps, float * y, int resid, int nsm, cudaStream_t st, bool pdl, int * err,
+                        unsigned long long * trace, int launch_id, Post post) {
+    const int nt = T == 1 ? 1 : 8;   // one token per chunk at T = 1: a token never picks an expert twice
+    {
+        MoeRouterArgs r;
+        memset(&r, 0, sizeof r);
+        r.x = x; r.norm_w = norm_w; r.eps = eps; r.xn = norm_w ? s.xn : nullptr; r.wr = m.router;
+        r.T = T; r.E = m.E; r.ne = m.ne; r.k = m.k; r.nt = nt; r.flags = m.flags; r.r = s.r;
+        r.err = err; r.trace = trace; r.launch_id = launch_id;
+        static bool attr = false;
+        if (!attr) {
+            cudaFuncSetAttribute(k_moe_router, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 8192 * 4);
+            attr = true;
+        }
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(m.ne);
+        cfg.blockDim = dim3(kRouterThreads);
+        cfg.dynamicSmemBytes = (size_t) m.E * 4 * (norm_w ? 2 : 1);
+        cfg.stream = st;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = pdl ? 1 : 0;
+        post(cudaLaunchKernelEx(&cfg, k_moe_router, r), "moe.router");
+    }
+    MoeGArgs g;
+    memset(&g, 0, sizeof g);
+    g.slots = s.r.slots; g.ch_e = s.r.ch_e; g.ch_s0 = s.r.ch_s0; g.ch_n = s.r.ch_n; g.meta = s.r.meta;
+    g.err = err; g.trace = trace;
+    {
+        MoeGArgs a = g;
+        a.t = m.gu; a.tiles = m.gu_tiles; a.perm = m.gu_perm; a.scatter = m.dn_iperm;
+        a.in = norm_w ? s.xn : x; a.in_stride = m.E; a.in_div = m.k;
+        a.out = s.hp; a.out_stride = m.F; a.ffn_f = m.F;
+        a.nstage = moe_stages(m.gu);
+        a.launch_id = launch_id + 1;
+        post(moe_gemv(MG_GU, nt, a, nsm, st, pdl), "moe.gate_up");
+    }
+    {
+        MoeGArgs a = g;
+        a.t = m.dn; a.tiles = m.dn_tiles;
+        a.in = s.hp; a.in_stride = m.F; a.in_div = 1;
+        a.out = s.yk; a.out_stride = m.E;
+        a.nstage = moe_stages(m.dn);
+        a.launch_id = launch_id + 2;
+        post(moe_gemv(MG_DN, nt, a, nsm, st, pdl), "moe.down");
+    }
+    {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3((m.E + 255) / 256, T);
+        cfg.blockDim = dim3(256);
+        cfg.stream = st;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[0].val.programmaticStreamSerializationAllowed = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = pdl ? 1 : 0;
+        post(cudaLaunchKernelEx(&cfg, k_moe_comb, (const float *) s.yk, (const float *) s.r.w, T, m.k, m.E, y, resid),
+             "moe.combine");
+    }
+}
+
+}  // namespace sb

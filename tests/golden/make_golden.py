@@ -13,7 +13,10 @@ matvec dispatch of sml-run.c, the sml_dequant_row_* functions):
   - y = W x for two tensors;
   - three dequantized embedding rows.
 For a two-layer model: 8 greedy ids after an 8-token prompt and their logits
-(sml_forward, the prompt stepped a token at a time).
+(sml_forward, the prompt stepped a token at a time). The same for a two-layer
+mixture-of-experts model (16 experts, 4 per token, renormalized softmax), and
+sml_moe_route's choices and weights on seeded logits with planted ties, for
+moe_flags 1 and 0.
 """
 import json
 import os
@@ -38,6 +41,20 @@ def width_spec(nb, six):
 def decode_spec():
     import sheep_b200
     return sheep_b200.spec_for("tiny-q4", seed=77)
+
+
+def moe_spec():
+    import sheep_b200
+    return sheep_b200.spec_for("tiny-q4", seed=91, n_expert=16, n_expert_used=4, moe_flags=1, expert_ff=384)
+
+
+def route_logits():
+    rng = np.random.default_rng(2024)
+    lg = rng.standard_normal((24, 128)).astype(np.float32)
+    for t in range(0, 24, 3):                    # ties: the lower index wins
+        lg[t, rng.integers(0, 128, 6)] = lg[t].max()
+    lg[1, :] = 0.5                               # every expert tied
+    return lg
 
 
 def check_input(n):
@@ -79,6 +96,23 @@ def main():
     ids, lg = helpers.ref("decode", path, prompt=PROMPT, ngen=8, n_ctx=64)
     np.savez_compressed(os.path.join(HERE, "decode_tiny.npz"), ids=ids, logits=lg, prompt=np.array(PROMPT, np.int32))
     index["decode_tiny.npz"] = {"spec": spec, "sha256": helpers.file_sha(path)}
+    spec = moe_spec()
+    path = helpers.model_path(spec)
+    ids, lg = helpers.ref("decode", path, prompt=PROMPT, ngen=8, n_ctx=64)
+    np.savez_compressed(os.path.join(HERE, "decode_moe_tiny.npz"), ids=ids, logits=lg,
+                        prompt=np.array(PROMPT, np.int32))
+    index["decode_moe_tiny.npz"] = {"spec": spec, "sha256": helpers.file_sha(path)}
+    lgs = route_logits()
+    out = {"logits": lgs}
+    for flags in (1, 0):
+        sel = np.zeros((len(lgs), 8), np.int32)
+        w = np.zeros((len(lgs), 8), np.float32)
+        for t in range(len(lgs)):
+            sel[t], w[t] = helpers.ref("route", lg=lgs[t], k=8, flags=flags)
+        out[f"sel_f{flags}"] = sel
+        out[f"w_f{flags}"] = w
+    np.savez_compressed(os.path.join(HERE, "route.npz"), **out)
+    index["route.npz"] = {"k": 8, "n_expert": 128}
     with open(os.path.join(HERE, "index.json"), "w") as f:
         json.dump(index, f, indent=1, sort_keys=True)
     print("wrote", len(index), "fixtures")

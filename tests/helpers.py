@@ -113,6 +113,18 @@ class Oracle:
         self.lib().so_decode(self.m, _p(prompt), len(prompt), ngen, _p(ids), _p(lg))
         return ids, lg
 
+    def moe_ffn(self, layer, x, kmax=16):
+        """The MoE FFN of `layer` on normalized rows x [T, E]: y [T, E], sel and w [T, k]."""
+        x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+        y = np.zeros_like(x)
+        sel = np.zeros((len(x), kmax), np.int32)
+        w = np.zeros((len(x), kmax), np.float32)
+        k = 0
+        for t in range(len(x)):
+            k = self.lib().so_moe_ffn(self.m, layer, _p(x[t]), _p(y[t]), _p(sel[t]), _p(w[t]))
+            assert k > 0, "layer has no router"
+        return y, sel[:, :k], w[:, :k]
+
     def close(self):
         if self.m:
             self.lib().so_close(self.m)

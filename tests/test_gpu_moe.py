@@ -1,0 +1,191 @@
+"""The mixture-of-experts FFN on the GPU against the CPU oracle.
+
+Routing: the chosen experts bit-exact (sml_moe_route's top-k, ties to the lower
+index), weights within 2e-6 relative (the device's expf against the host
+libm's). The layer (router, experts, combine) per row: the same experts, and
+outputs within rel-RMS 3e-3 of the oracle's. The gate/up sums differ from the
+CPU's in their last bits (another summation order); where a hidden value sits
+at a rounding boundary of its int8 code, the down projection sees a code one
+step away -- about 1e-3 of the output for one such flip. Rows without a flip
+agree to 1e-4, and at 16 or more rows most rows must. MoE decode: the
+whole-model tolerances of test_gpu_decode and the reference's greedy ids.
+"""
+import json
+import os
+
+import numpy as np
+import pytest
+
+import sheep_b200
+from tests import helpers
+
+pytestmark = pytest.mark.gpu
+
+GOLD = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+INDEX = json.load(open(os.path.join(GOLD, "index.json")))
+Y_RELRMS = 3e-3          # a few int8 code flips in the hidden vector
+Y_RELRMS_CLEAN = 1e-4    # a row without one
+W_RTOL = 2e-6
+
+
+def _torch():
+    import torch
+    assert torch.cuda.is_available(), "GPU tests need a CUDA device"
+    return torch
+
+
+def _rows(seed, T, E):
+    """fp16 N(0, 1) token rows as the layer's float input."""
+    return np.random.default_rng(seed).standard_normal((T, E)).astype(np.float16).astype(np.float32)
+
+
+def _route_dev(lg, k, flags):
+    torch = _torch()
+    d = torch.from_numpy(np.ascontiguousarray(lg, np.float32)).cuda()
+    T, ne = lg.shape
+    sel = torch.full((T, k), -1, dtype=torch.int32, device="cuda")
+    w = torch.zeros((T, k), dtype=torch.float32, device="cuda")
+    sheep_b200.moe_route_dev(d.data_ptr(), T, ne, k, flags, sel.data_ptr(), w.data_ptr())
+    torch.cuda.synchronize()
+    return sel.cpu().numpy(), w.cpu().numpy()
+
+
+def test_route_against_reference_vectors():
+    g = np.load(os.path.join(GOLD, "route.npz"))
+    for flags in (1, 0):
+        sel, w = _route_dev(g["logits"], 8, flags)
+        assert np.array_equal(sel, g[f"sel_f{flags}"]), flags
+        assert np.allclose(w, g[f"w_f{flags}"], rtol=W_RTOL, atol=0), flags
+
+
+@pytest.mark.parametrize("ne,k", [(128, 8), (256, 16), (60, 6), (8, 8), (1, 1)])
+def test_route_against_oracle(ne, k):
+    rng = np.random.default_rng(ne * 31 + k)
+    lg = rng.standard_normal((300, ne)).astype(np.float32)
+    lg[::7, rng.integers(0, ne, 3)] = lg[::7].max(axis=1, keepdims=True)   # planted ties
+    lg[5::11] = np.float32(-1.25)                                          # all tied
+    for flags in (1, 0):
+        sel, w = _route_dev(lg, k, flags)
+        for t in range(len(lg)):
+            s, ww = helpers.oracle_route(lg[t], k, flags)
+            assert np.array_equal(sel[t], s), (flags, t)
+            assert np.allclose(w[t], ww, rtol=W_RTOL, atol=0), (flags, t)
+
+
+def test_route_rejects_bad_arguments():
+    torch = _torch()
+    d = torch.zeros((4, 300), dtype=torch.float32, device="cuda")
+    sel = torch.zeros((4, 8), dtype=torch.int32, device="cuda")
+    w = torch.zeros((4, 8), dtype=torch.float32, device="cuda")
+    for ne, k, flags in ((300, 8, 1), (128, 17, 1), (128, 0, 1), (128, 8, 2)):
+        with pytest.raises(RuntimeError):
+            sheep_b200.moe_route_dev(d.data_ptr(), 4, ne, k, flags, sel.data_ptr(), w.data_ptr())
+
+
+def _check_layer(path, T, seed, layer=0):
+    m = sheep_b200.MoeLayer(path, layer=layer, max_tokens=max(T, 1))
+    orc = helpers.Oracle(path, n_ctx=64)
+    try:
+        x = _rows(seed, T, m.n_embd)
+        y, sel, w, n_active = m.forward(x)
+        yo, so, wo = orc.moe_ffn(layer, x)
+        assert np.array_equal(sel, so)
+        assert np.allclose(w, wo, rtol=W_RTOL, atol=0)
+        assert n_active == len(np.unique(so))
+        errs = np.array([helpers.rel_rms(yo[t], y[t]) for t in range(T)])
+        assert errs.max() <= Y_RELRMS, errs.max()
+        if T >= 16:
+            assert np.mean(errs <= Y_RELRMS_CLEAN) >= 0.75, np.sort(errs)[-8:]
+        return y
+    finally:
+        m.close()
+        orc.close()
+
+
+def test_layer_cfg2_shape():
+    """The Qwen3-30B-A3B-shaped layer (2048 wide, 128 experts, top 8, FFN 768)
+    at 1, 16, 64 and 256 tokens a step: one token per chunk at T = 1, up to
+    eight at once above."""
+    path = helpers.model_path(sheep_b200.spec_for("qwen3-30b-a3b-moe-layer"))
+    for T in (1, 16, 64, 256):
+        _check_layer(path, T, seed=T)
+
+
+@pytest.mark.parametrize("nb,six", [(nb, six) for six in (0, 1) for nb in (2, 3, 4, 5, 6, 7, 8)])
+def test_layer_every_width(nb, six):
+    spec = sheep_b200.spec_for("tiny-q4", n_layer=1, nbits=nb, scale6=six, minneg=six, n_expert=8,
+                               n_expert_used=2, moe_flags=1, expert_ff=128, seed=700 + 10 * nb + six)
+    path = helpers.model_path(spec)
+    _check_layer(path, 1, seed=1)
+    _check_layer(path, 13, seed=2)
+
+
+def test_layer_softmax_over_all_experts():
+    spec = sheep_b200.spec_for("tiny-q4", n_layer=1, n_expert=16, n_expert_used=4, moe_flags=0, expert_ff=256,
+                               seed=41)
+    _check_layer(helpers.model_path(spec), 9, seed=3)
+
+
+def test_rows_do_not_depend_on_the_batch():
+    """A row's output is the same whichever rows share its step (chunks of
+    eight tokens per expert form differently)."""
+    spec = sheep_b200.spec_for("tiny-q4", n_layer=1, n_expert=16, n_expert_used=4, moe_flags=1, expert_ff=256,
+                               seed=42)
+    path = helpers.model_path(spec)
+    m = sheep_b200.MoeLayer(path, max_tokens=64)
+    try:
+        x = _rows(5, 64, m.n_embd)
+        a = m.forward(x[:16])[0]
+        b = m.forward(x)[0][:16]
+        c = m.forward(x[::-1].copy())[0][::-1][:16]
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+        assert np.array_equal(a.view(np.uint32), c.view(np.uint32))
+    finally:
+        m.close()
+
+
+def test_layer_rejects_bad_arguments():
+    spec = sheep_b200.spec_for("tiny-q4", n_layer=1, n_expert=8, n_expert_used=2, moe_flags=1, expert_ff=128)
+    path = helpers.model_path(spec)
+    with pytest.raises(RuntimeError):
+        sheep_b200.MoeLayer(path, layer=1)
+    with pytest.raises(RuntimeError):
+        sheep_b200.MoeLayer(helpers.model_path(sheep_b200.spec_for("tiny-q4")))   # dense: no router
+    m = sheep_b200.MoeLayer(path, max_tokens=4)
+    try:
+        with pytest.raises(RuntimeError):
+            m.forward(np.zeros((5, m.n_embd), np.float32))
+    finally:
+        m.close()
+
+
+def test_moe_decode_against_oracle():
+    """A two-layer MoE decoder through the engine: teacher-forced logits, then
+    the reference's greedy ids from its own decode."""
+    path = helpers.model_path(INDEX["decode_moe_tiny.npz"]["spec"])
+    g = np.load(os.path.join(GOLD, "decode_moe_tiny.npz"))
+    eng = sheep_b200.Engine(path, n_ctx=96)
+    orc = helpers.Oracle(path, n_ctx=96)
+    try:
+        toks = np.random.default_rng(8).integers(0, 1024, 40)
+        for pos, t in enumerate(toks):
+            lg, lo = eng.step(int(t), pos), orc.forward(int(t), pos)
+            corr = float(np.corrcoef(lo.astype(np.float64), lg.astype(np.float64))[0, 1])
+            assert corr >= 0.999 and helpers.rel_rms(lo, lg) <= 2e-2, (pos, corr)
+            assert helpers.agree_with_ties(lo, lg)[0], pos
+    finally:
+        eng.close()
+        orc.close()
+    eng = sheep_b200.Engine(path, n_ctx=96)
+    try:
+        ids = eng.generate(g["prompt"], 8)
+        assert np.array_equal(ids, g["ids"]), (ids, g["ids"])
+        ids32 = eng.generate(g["prompt"], 32)
+    finally:
+        eng.close()
+    orc = helpers.Oracle(path, n_ctx=96)
+    try:
+        want, _ = orc.decode(g["prompt"], 32)
+    finally:
+        orc.close()
+    assert np.array_equal(ids32, want)

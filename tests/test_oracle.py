@@ -99,3 +99,32 @@ def test_moe_route_matches_reference():
         if helpers.have_ref():
             rs, rw = helpers.ref("route", lg=lg, k=8, flags=1)
             assert np.array_equal(rs, sel) and np.array_equal(rw.view(np.uint32), w.view(np.uint32))
+
+
+def test_oracle_moe_decode_against_reference():
+    """The restatement's MoE branch (router, routing, experts, combine) against
+    the reference's own decode of a two-layer, 16-expert model."""
+    g = np.load(os.path.join(GOLD, "decode_moe_tiny.npz"))
+    path = helpers.model_path(INDEX["decode_moe_tiny.npz"]["spec"])
+    assert helpers.file_sha(path) == INDEX["decode_moe_tiny.npz"]["sha256"]
+    orc = helpers.Oracle(path, n_ctx=64)
+    try:
+        ids, lg = orc.decode(g["prompt"], 8)
+    finally:
+        orc.close()
+    assert np.array_equal(ids, g["ids"])
+    for k in range(8):
+        assert float(np.corrcoef(g["logits"][k], lg[k])[0, 1]) >= 0.9999
+        assert helpers.rel_rms(g["logits"][k], lg[k]) <= 2e-2
+
+
+def test_oracle_route_against_reference_vectors():
+    """Choices bit-exact and weights bit-exact against sml_moe_route's outputs
+    (both flags; ties, and a row where every expert ties)."""
+    g = np.load(os.path.join(GOLD, "route.npz"))
+    for flags in (1, 0):
+        for t, lg in enumerate(g["logits"]):
+            sel, w = helpers.oracle_route(lg, 8, flags)
+            assert np.array_equal(sel, g[f"sel_f{flags}"][t]), (flags, t)
+            assert np.array_equal(w.view(np.uint32), g[f"w_f{flags}"][t].view(np.uint32)), (flags, t)
+    assert list(g["sel_f1"][1]) == list(range(8))
