@@ -126,10 +126,11 @@ class Engine:
         self.h = lib().sb_open(path.encode(), n_ctx, why, 512)
         if not self.h:
             raise RuntimeError(f"sb_open: {why.value.decode()}")
-        info = (ctypes.c_int * 12)()
+        info = (ctypes.c_int * 16)()
         lib().sb_info(self.h, info)
         (self.n_layer, self.n_embd, self.n_head, self.n_head_kv, self.head_dim, self.n_ff,
-         self.n_vocab, self.n_ctx) = info[:8]
+         self.n_vocab, self.n_ctx, self.n_expert, self.n_expert_used) = info[:10]
+        self.persistent = bool(info[12])   # one kernel per token
         self.bytes_per_token = int(lib().sb_bytes_per_token(self.h))
 
     def step(self, tok, pos):
@@ -307,7 +308,7 @@ def sml_gpu_open(path, n_ctx=0, threads=0, gpu_layers=0):
 
 
 def _n_vocab():
-    info = (ctypes.c_int * 12)()
+    info = (ctypes.c_int * 16)()
     lib().sb_info(lib().sml_gpu_engine(), info)
     return info[6]
 

@@ -43,7 +43,7 @@ extern "C" const float * sml_gpu_step(int tok, int pos) {
 }
 
 extern "C" int sml_gpu_layers(int * of) {
-    int info[12] = {0};
+    int info[16] = {0};
     if (g_eng) sb_info(g_eng, info);
     if (of) *of = info[0];
     return info[0];

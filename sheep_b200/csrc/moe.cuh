@@ -396,33 +396,6 @@ SB_DEV void tile_row_nt(const uint8_t * tile, const TileGeom & tg, uint8_t * act
     }
 }
 
-// Quantize a team's 4 values of group grp into a (no export).
-SB_DEV void quant_team_to(float4 v, int grp, int sub, ActS & a, bool store) {
-    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-#pragma unroll
-    for (int o = 4; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    const float sc = __fdiv_rn(amax, 127.0f);
-    const float is = sc > 0.0f ? __fdiv_rn(1.0f, sc) : 0.0f;
-    const float vv[4] = {v.x, v.y, v.z, v.w};
-    uint32_t word = 0;
-    int sum = 0;
-#pragma unroll
-    for (int b = 0; b < 4; b++) {
-        int q = __float2int_rn(__fmul_rn(vv[b], is));
-        q = q > 127 ? 127 : q < -127 ? -127 : q;
-        sum += q;
-        word |= ((uint32_t) (q & 0xff)) << (8 * b);
-    }
-#pragma unroll
-    for (int o = 4; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    if (!store) return;
-    *reinterpret_cast<uint32_t *>(a.q + act_slot_off(a.n, grp, 4 * sub)) = word;
-    if (sub == 0) {
-        a.xs[grp] = sc;
-        a.xsum[grp] = sc * (float) sum;
-    }
-}
-
 // Stage the activations of one chunk (consumer threads, named barrier 1):
 // (token, group) pairs go to teams of 8 lanes, every load of a batch issued
 // before any quantization. Gathered modes read in[row][perm[i]].
@@ -488,19 +461,20 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_moe_gemv(const __grid_constan
     const int q0 = (int) (Q * blockIdx.x / gridDim.x), q1 = (int) (Q * (blockIdx.x + 1) / gridDim.x);
 
     if (warp == kConsWarps) {
-        if (lane == 0) {
-            int cur = -1, issued = 0;
+        // lane j < ns owns ring stage j and issues items q0 + j, q0 + j + ns, ...
+        if (lane < ns) {
+            const int s = lane;
+            const uint32_t tb = t.tb;
+            int cur = -1, lap = 0;
             const uint8_t * base = nullptr;
-            for (int q = q0; q < q1; q++) {
-                const int k = q - q0, s = k % ns, c = q / ntl, i = q - c * ntl;
+            for (int q = q0 + s; q < q1; q += ns, lap++) {
+                const int c = q / ntl, i = q - c * ntl;
                 if (c != cur) { cur = c; base = g.tiles[g.ch_e[c]]; }
-                if (k >= ns && !mbar_wait(&empty[s], ((k / ns) - 1) & 1, g.err, 1)) break;
-                mbar_expect_tx(&full[s], t.tb);
-                bulk_g2s(ring + (size_t) s * t.tb, base + (size_t) i * t.tb, t.tb, &full[s]);
-                issued++;
+                if (lap > 0 && !mbar_wait(&empty[s], (lap - 1) & 1, g.err, 1)) break;
+                mbar_expect_tx(&full[s], tb);
+                bulk_g2s(ring + (size_t) s * tb, base + (size_t) i * tb, tb, &full[s]);
             }
-            for (int k = issued - ns < 0 ? 0 : issued - ns; k < issued; k++)
-                mbar_wait(&full[k % ns], (k / ns) & 1, g.err, 3);
+            if (lap > 0) mbar_wait(&full[s], (lap - 1) & 1, g.err, 3);   // nothing may land after exit
         }
         return;
     }

@@ -3,7 +3,9 @@
 // One CTA per SM takes a contiguous range of tiles (TR whole rows each). A
 // producer warp streams them into a ring of shared-memory stages with
 // cp.async.bulk and mbarrier transaction counts -- it starts before the kernel
-// waits on its predecessor, since weights never depend on it. Eight consumer
+// waits on its predecessor, since weights never depend on it. Lane j of the
+// producer owns stage j and issues its tiles, so the copies of a ring's worth
+// of tiles leave in one warp instruction. Eight consumer
 // warps stage the int8 activation (the mode's prologue: RMSNorm, gather,
 // per-32 quantization), then take whole tiles round-robin: lane l owns row
 // l % TR and every (32/TR)-th unit of it, so a lane's units are independent
@@ -108,6 +110,33 @@ SB_DEV void quant_team(float4 v, int grp, int sub, ActS & a, const TGArgs & g, b
     if (ex) {
         *reinterpret_cast<uint32_t *>(g.act_q + grp * kGroup + 4 * sub) = word;
         if (sub == 0) { g.act_s[grp] = sc; g.act_sum[grp] = sum; }
+    }
+}
+
+// Quantize a team's 4 values of group grp into a (no export).
+SB_DEV void quant_team_to(float4 v, int grp, int sub, ActS & a, bool store) {
+    float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+    for (int o = 4; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float sc = __fdiv_rn(amax, 127.0f);
+    const float is = sc > 0.0f ? __fdiv_rn(1.0f, sc) : 0.0f;
+    const float vv[4] = {v.x, v.y, v.z, v.w};
+    uint32_t word = 0;
+    int sum = 0;
+#pragma unroll
+    for (int b = 0; b < 4; b++) {
+        int q = __float2int_rn(__fmul_rn(vv[b], is));
+        q = q > 127 ? 127 : q < -127 ? -127 : q;
+        sum += q;
+        word |= ((uint32_t) (q & 0xff)) << (8 * b);
+    }
+#pragma unroll
+    for (int o = 4; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (!store) return;
+    *reinterpret_cast<uint32_t *>(a.q + act_slot_off(a.n, grp, 4 * sub)) = word;
+    if (sub == 0) {
+        a.xs[grp] = sc;
+        a.xsum[grp] = sc * (float) sum;
     }
 }
 
@@ -338,18 +367,30 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__
                 const int n1 = (int) ((long) g.next_ntiles * (blockIdx.x + 1) / g.next_grid);
                 if (n1 > n0) prefetch_l2(g.next_tiles + (size_t) n0 * g.next_tb, (size_t) (n1 - n0) * g.next_tb);
             }
-            int issued = 0;
-            for (int i = t0; i < t1; i++) {
-                const int k = i - t0, s = k % ns;
-                if (k >= ns && !mbar_wait(&empty[s], ((k / ns) - 1) & 1, g.err, 1)) break;
-                mbar_expect_tx(&full[s], t.tb);
-                bulk_g2s(ring + (size_t) s * t.tb, t.tiles + (size_t) i * t.tb, t.tb, &full[s]);
-                issued++;
+#ifdef SB_TRACE
+            if (g.trace && blockIdx.x < kTraceCtas) g.trace[((size_t) g.launch_id * kTraceCtas + blockIdx.x) * 8 + 6] = global_ns();
+#endif
+        }
+        __syncwarp();
+        // lane j < ns owns ring stage j and issues its tiles t0 + j, t0 + j + ns, ...:
+        // one warp instruction issues up to ns copies
+        if (lane < ns) {
+            const int s = lane;
+            const uint32_t tb = t.tb;
+            int lap = 0;
+            for (int i = t0 + s; i < t1; i += ns, lap++) {
+                if (lap > 0 && !mbar_wait(&empty[s], (lap - 1) & 1, g.err, 1)) break;
+                mbar_expect_tx(&full[s], tb);
+                bulk_g2s(ring + (size_t) s * tb, t.tiles + (size_t) i * tb, tb, &full[s]);
             }
-            // no copy may still be landing in shared memory when the CTA exits:
-            // wait (bounded) for the last copy into every stage
-            for (int k = issued - ns < 0 ? 0 : issued - ns; k < issued; k++)
-                mbar_wait(&full[k % ns], (k / ns) & 1, g.err, 3);
+            // no copy may still be landing in shared memory when the CTA exits
+            if (lap > 0) mbar_wait(&full[s], (lap - 1) & 1, g.err, 3);
+        }
+        __syncwarp();
+        if (lane == 0) {
+#ifdef SB_TRACE
+            if (g.trace && blockIdx.x < kTraceCtas) g.trace[((size_t) g.launch_id * kTraceCtas + blockIdx.x) * 8 + 7] = global_ns();
+#endif
             mbar_wait(&statics, 0, g.err, 5);
         }
         pdl_wait();

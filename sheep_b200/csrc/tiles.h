@@ -99,11 +99,11 @@ struct TT {
 };
 
 // Rows per tile for a tensor of `rows` x `row_bytes`: as many as keep at least
-// `min_tiles` tiles and a tile at most 12 KB (at least one row), so eight ring
-// stages stay under 96 KB. `even` for fused gate/up tensors whose tiles pair rows.
-__host__ __device__ inline int pick_tr(int rows, int row_bytes, int min_tiles, int even) {
+// `min_tiles` tiles and a tile at most max_bytes (at least one row). `even`
+// for fused gate/up tensors whose tiles pair rows.
+__host__ __device__ inline int pick_tr(int rows, int row_bytes, int min_tiles, int even, int max_bytes = 12288) {
     int tr = 16;
-    while (tr > (even ? 2 : 1) && (rows / tr < min_tiles || (long) tr * row_bytes > 12288)) tr /= 2;
+    while (tr > (even ? 2 : 1) && (rows / tr < min_tiles || (long) tr * row_bytes > max_bytes)) tr /= 2;
     return tr;
 }
 

@@ -167,3 +167,26 @@ def test_cfg0_logits_within_reference_spread():
     finally:
         eng.close()
         orc.close()
+
+
+@pytest.mark.parametrize("cfg", ["tiny-q4", "small-q4-tied"])
+def test_persistent_kernel_equals_kernel_chain(cfg, monkeypatch):
+    """One persistent kernel per token (SB_MEGA=1) and the chain of kernels
+    (the default) run the same arithmetic in the same order: logits bit-equal
+    at every step, greedy ids equal."""
+    path = helpers.model_path(sheep_b200.spec_for(cfg))
+    toks = np.random.default_rng(11).integers(0, 1024, 70)   # two attention chunks
+    outs = []
+    for mega in ("1", "0"):
+        monkeypatch.setenv("SB_MEGA", mega)
+        eng = sheep_b200.Engine(path, n_ctx=128)
+        try:
+            assert eng.persistent == (mega == "1")
+            lg = [eng.step(int(t), pos).copy() for pos, t in enumerate(toks)]
+            ids = eng.generate(toks[:9], 24)
+        finally:
+            eng.close()
+        outs.append((np.array(lg), ids))
+    (a, ia), (b, ib) = outs
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+    assert np.array_equal(ia, ib)
