@@ -16,6 +16,11 @@ e2e: the same tokens through the reference-facing C ABI (sml_gpu_prefill /
 sml_gpu_step with host ids in and host logits out, host argmax), wall clock.
 --impl reference: the reference engine's own CPU decode (oracle/_ref, built
 from its unchanged sources) on the box's host cores, same model and metric.
+extras (single GPU only): configuration 1's GEMV microbench (GB/s of weight
+bytes streamed, Q4 and Q8, batch 1/4/16) and configuration 2's MoE layer
+(Qwen3-30B-A3B shape at 1/16/64/256 tokens a step: tok/s and GB/s of the
+experts actually read plus the router), each run timed alone by CUDA events
+with a 512 MB buffer rewritten before it, so the weights come from HBM.
 """
 import argparse
 import ctypes
@@ -272,6 +277,12 @@ def main():
         cpu = {"value": tps, "unit": "tok/s", "cores": cores, "kind": "reference",
                "sample": f"same model, 16-token prompt stepped, 2 warm-up then {n_cpu} timed greedy tokens"}
 
+    extras = None
+    if rank == 0 and world == 1:
+        peak0, _ = peaks()
+        extras = {"l2": "a 512 MB buffer rewritten before each timed run",
+                  "gemv_cfg1": gemv_microbench(peak0), "moe_cfg2": moe_microbench(peak0)}
+
     if rank == 0:
         peak, peak_kind = peaks()
         achieved = k_bytes / (k_ms / 1000.0) / 1e9
@@ -297,11 +308,56 @@ def main():
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
             "greedy_ids_head": [int(i) for i in ids[W:W + 8]],
+            "extras": extras,
         }
         print(json.dumps(out))
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def fp16_rows(seed, n, cols):
+    """fp16 N(0, 1) activations as float32 rows."""
+    return np.random.default_rng(seed).standard_normal((n, cols)).astype(np.float16).astype(np.float32)
+
+
+def gemv_microbench(peak, reps=20):
+    """Configuration 1: weight GB/s of one GEMV over B activations."""
+    import sheep_b200
+    from sheep_b200 import configs
+    out = []
+    for cfg, quant in (("gemv-4096-q4", "Q4"), ("gemv-4096-q8", "Q8")):
+        ts = sheep_b200.TensorSet(model_path(configs.CONFIGS[cfg], 0, None))
+        try:
+            for name in ("blk.0.attn_q.weight", "blk.0.ffn_gate.weight", "blk.0.ffn_down.weight"):
+                rows, cols, _ = ts.shape(name)
+                nbytes = ts.nbytes(name)
+                for B in (1, 4, 16):
+                    ms = ts.time_gemv(name, fp16_rows(B, B, cols), reps)
+                    gbs = nbytes / (ms / 1000.0) / 1e9
+                    out.append({"quant": quant, "shape": f"{rows}x{cols}", "batch": B, "us": round(ms * 1000.0, 2),
+                                "weight_bytes": nbytes, "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)})
+        finally:
+            ts.close()
+    return out
+
+
+def moe_microbench(peak, reps=20):
+    """Configuration 2: the MoE layer at T tokens a step."""
+    import sheep_b200
+    from sheep_b200 import configs
+    m = sheep_b200.MoeLayer(model_path(configs.CONFIGS["qwen3-30b-a3b-moe-layer"], 0, None), max_tokens=256)
+    out = []
+    try:
+        for T in (1, 16, 64, 256):
+            ms, na = m.time(fp16_rows(100 + T, T, m.n_embd), reps)
+            nbytes = na * m.expert_bytes + m.router_bytes
+            gbs = nbytes / (ms / 1000.0) / 1e9
+            out.append({"tokens": T, "us": round(ms * 1000.0, 2), "tok_s": round(T / (ms / 1000.0), 1),
+                        "experts_read": na, "bytes": nbytes, "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)})
+    finally:
+        m.close()
+    return out
 
 
 def spec_bytes(path):

@@ -66,7 +66,14 @@ unsigned long long sb_tset_bytes(const sb_tset * t, const char * name);
 // y[b] = W x[b], nb vectors, device pointers (x nb x cols, y nb x rows),
 // activation gathered through the tensor's perm and quantized per 32 inside.
 // Replaces sml_g_mv3s / sml_g_qdmv2 (sml/sml-gpu-fast.cu:267-315).
+// nb = 1 runs the streaming GEMV; nb > 1 (up to 4096) the batched one, which
+// reads the weights once per 8 vectors.
 int sb_tset_gemv_dev(sb_tset * t, const char * name, const float * x, int nb, float * y, void * stream);
+// The same with host buffers (copies included, synchronous).
+int sb_tset_gemv_host(sb_tset * t, const char * name, const float * x, int nb, float * y);
+// Mean device time (CUDA events) of one sb_tset_gemv_dev over nb host vectors
+// copied to the device once, a buffer larger than L2 rewritten before each run.
+int sb_tset_time_gemv(sb_tset * t, const char * name, const float * x, int nb, int reps, float * ms_avg);
 // Host-buffer form of one GEMV; q/s/sums (host, may be NULL) receive the int8
 // activation the kernel used. Mirrors what sml-check writes
 // (sml/sml-check.c:194-245).

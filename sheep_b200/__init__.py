@@ -68,6 +68,8 @@ def lib():
         "sb_tset_shape": (ip, [vp, cp, vp, vp, vp]),
         "sb_tset_bytes": (ctypes.c_ulonglong, [vp, cp]),
         "sb_tset_gemv_dev": (ip, [vp, cp, vp, ip, vp, vp]),
+        "sb_tset_gemv_host": (ip, [vp, cp, vp, ip, vp]),
+        "sb_tset_time_gemv": (ip, [vp, cp, vp, ip, ip, fp]),
         "sb_tset_matvec": (ip, [vp, cp, vp, vp, vp, vp, vp]),
         "sb_tset_dequant_rows": (ip, [vp, cp, vp, ip, vp]),
         "sb_quantize_act": (ip, [vp, vp, ip, vp, vp, vp, vp]),
@@ -223,6 +225,24 @@ class TensorSet:
         if not lib().sb_tset_dequant_rows(self.h, name.encode(), _p(rows), len(rows), _p(out)):
             raise RuntimeError("sb_tset_dequant_rows failed")
         return out
+
+    def gemv(self, name, X):
+        """Y [nb, rows] = W X[b] for host rows X [nb, cols] (batched for nb > 1)."""
+        rows, cols, _ = self.shape(name)
+        X = np.ascontiguousarray(np.atleast_2d(X), np.float32)
+        assert X.shape[1] == cols
+        Y = np.zeros((len(X), rows), np.float32)
+        if not lib().sb_tset_gemv_host(self.h, name.encode(), _p(X), len(X), _p(Y)):
+            raise RuntimeError("sb_tset_gemv_host failed")
+        return Y
+
+    def time_gemv(self, name, X, reps):
+        """Mean device ms of one GEMV over the host rows X, L2 flushed before each run."""
+        X = np.ascontiguousarray(np.atleast_2d(X), np.float32)
+        ms = ctypes.c_float()
+        if not lib().sb_tset_time_gemv(self.h, name.encode(), _p(X), len(X), reps, ctypes.byref(ms)):
+            raise RuntimeError("sb_tset_time_gemv failed")
+        return ms.value
 
     def gemv_dev(self, name, x_ptr, nb, y_ptr, stream=0):
         if not lib().sb_tset_gemv_dev(self.h, name.encode(), x_ptr, nb, y_ptr, stream):

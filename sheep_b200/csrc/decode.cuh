@@ -205,9 +205,9 @@ static __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_const
     __shared__ unsigned last_flag;
     pdl_launch_dependents();
     SB_MARK(g.trace, g.launch_id, 0);
-    pdl_wait();
-    SB_MARK(g.trace, g.launch_id, 1);
     const int h = blockIdx.x, c = blockIdx.y, hd = g.hd, tid = threadIdx.x;
+    // the position comes from the previous token; the cached keys and values
+    // before it from earlier tokens: neither waits on the previous kernel
     const int pos = g.pos ? *g.pos : g.pos_imm;
     const int nchunk = pos / g.chunk + 1;
     if (c >= nchunk) return;
@@ -220,15 +220,9 @@ static __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_const
     uint16_t * Ks = reinterpret_cast<uint16_t *>(sm + 4 * hd + g.chunk);   // [chunk][hd + 4]
     uint16_t * Vs = Ks + (size_t) g.chunk * (hd + 4);                        // [chunk][hd]
     const int kst = hd + 4;
-    // every load of this CTA issued before any is used
-    for (int i = tid; i < hd; i += blockDim.x) {
-        q[i] = g.qkv[h * hd + i];
-        kn[i] = g.qkv[g.qd + kvh * hd + i];
-        vn[i] = g.qkv[g.qd + g.kvd + kvh * hd + i];
-        if (i < hd / 2) {
-            cs[i] = g.rcos[(size_t) pos * (hd / 2) + i];
-            sn[i] = g.rsin[(size_t) pos * (hd / 2) + i];
-        }
+    for (int i = tid; i < hd / 2; i += blockDim.x) {
+        cs[i] = g.rcos[(size_t) pos * (hd / 2) + i];
+        sn[i] = g.rsin[(size_t) pos * (hd / 2) + i];
     }
     const int per = hd / 8;   // 16-byte pieces per row
     // in batches of kB pieces per thread: all of a batch's loads before its stores
@@ -255,6 +249,13 @@ static __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_const
                 *reinterpret_cast<uint4 *>(Vs + (size_t) (t - t0) * hd + part * 8) = vv[r];
             }
         }
+    }
+    pdl_wait();
+    SB_MARK(g.trace, g.launch_id, 1);
+    for (int i = tid; i < hd; i += blockDim.x) {
+        q[i] = g.qkv[h * hd + i];
+        kn[i] = g.qkv[g.qd + kvh * hd + i];
+        vn[i] = g.qkv[g.qd + g.kvd + kvh * hd + i];
     }
     __syncthreads();
     SB_MARK(g.trace, g.launch_id, 2);

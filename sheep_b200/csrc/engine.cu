@@ -140,7 +140,7 @@ template <int MODE, int NB, int SIX>
 static void launch_tg_t(sb_engine * e, const TGArgs & g, int grid, size_t smem) {
     static bool attr = false;
     if (!attr) {
-        cudaFuncSetAttribute(k_tgemv<MODE, NB, SIX>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(k_tgemv<MODE, NB, SIX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kSmemBudget);
         attr = true;
     }
     launch(e, true, k_tgemv<MODE, NB, SIX>, dim3(grid), dim3(kTgThreads), smem, g);
@@ -158,17 +158,6 @@ static void launch_tg_nb(sb_engine * e, int mode, const TGArgs & g, int grid, si
     }
 }
 
-// Ring stages: a multiple of the consumer warps (tgemv.cuh), as many as fit
-// in ~96 KB so a CTA of the next kernel can share the SM, at least one per warp.
-static int tg_stages(const TT & t) {
-    int ns = (int) ((96 * 1024) / t.tb) / kConsWarps * kConsWarps;
-    return ns < kConsWarps ? kConsWarps : ns > kMaxStages ? kMaxStages : ns;
-}
-
-static size_t tg_smem(const TGArgs & g) {
-    return tg_ring_off(g.t.cols, g.in_permuted, g.norm_w != nullptr) + (size_t) g.nstage * g.t.tb;
-}
-
 static TGArgs tg_args(sb_engine * e, const TT & t, const float * in, const float * nw, float * out) {
     TGArgs g;
     memset(&g, 0, sizeof g);
@@ -177,7 +166,6 @@ static TGArgs tg_args(sb_engine * e, const TT & t, const float * in, const float
     g.norm_w = nw;
     g.eps = e->eps;
     g.out = out;
-    g.nstage = tg_stages(t);
     g.trace = e->trace;
     g.launch_id = e->launches;
     g.prefetch = 1;
@@ -194,12 +182,13 @@ static void set_next(TGArgs & g, const TT * nt, int nsm) {
     g.next_tb = nt->tb;
 }
 
-static void launch_tg(sb_engine * e, int mode, const TGArgs & g) {
-    const int grid = g.t.ntiles < e->nsm ? g.t.ntiles : e->nsm;
-    if (tg_smem(g) > 200 * 1024) {
-        // the staged activation and one ring stage per consumer warp must fit
-        snprintf(g_err, sizeof g_err, "kernel %s: %zu bytes of shared memory (tiles of %u bytes over %d columns)",
-                 e->cur, tg_smem(g), g.t.tb, g.t.cols);
+static void launch_tg(sb_engine * e, int mode, const TGArgs & g0) {
+    const int grid = g0.t.ntiles < e->nsm ? g0.t.ntiles : e->nsm;
+    TGArgs g = g0;
+    if (!tg_plan(g)) {
+        // not even the staged activation and a two-stage ring fit
+        snprintf(g_err, sizeof g_err, "kernel %s: no shared-memory plan for tiles of %u bytes over %d columns",
+                 e->cur, g.t.tb, g.t.cols);
         e->failed = true;
         return;
     }

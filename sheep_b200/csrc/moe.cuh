@@ -494,7 +494,7 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_moe_gemv(const __grid_constan
         const int k0 = q - q0, k1 = qe - q0;
         for (int k = k0 + (((warp - k0) % kConsWarps) + kConsWarps) % kConsWarps; k < k1; k += kConsWarps) {
             const int s = k % ns, i = q0 + k - c * ntl;
-            const bool ok = !failed && mbar_wait(&full[s], (k / ns) & 1, g.err, 2);
+            const bool ok = !failed && ring_wait(full, empty, k, ns, g.err);
             failed = !ok;
             float acc[NT];
             if (ok) {

@@ -53,18 +53,16 @@ inline const char * moe_unsupported(const ssf_file & f, int L) {
     return nullptr;
 }
 
-// Shared memory of the grouped GEMV: eight staged activations and at least
-// one ring stage per consumer warp must fit in kMoeSmem.
-constexpr size_t kMoeSmem = 200 * 1024;
+// Shared memory of the grouped GEMV: eight staged activations, then the ring.
 inline size_t moe_act_bytes(int cols) { return (act_smem_bytes(cols) + 127) / 128 * 128; }
 
 // Rows per expert tile: the most (<= 16, even for gate/up pairs) whose tile
-// stays under 12 KB and whose ring of kConsWarps stages fits beside eight
-// staged activations; 0 if not even the fewest rows fit.
+// stays under 12 KB and leaves room for a ring beside eight staged
+// activations; 0 if not even the fewest rows fit.
 inline int moe_pick_tr(int cols, int nbits, int six, int has_min, int even) {
     for (int tr = 16; tr >= (even ? 2 : 1); tr /= 2) {
-        const size_t tb = tile_geom(cols, tr, nbits, six, has_min).bytes;
-        if (tb <= 12288 && 8 * moe_act_bytes(cols) + (size_t) kConsWarps * tb <= kMoeSmem) return tr;
+        const uint32_t tb = tile_geom(cols, tr, nbits, six, has_min).bytes;
+        if (tb <= 12288 && ring_stages(8 * moe_act_bytes(cols), tb) >= 2) return tr;
     }
     return 0;
 }
@@ -154,14 +152,8 @@ inline void moe_carve(Arena & a, const MoeLayer & m, int T, MoeScratch & s) {
     s.r.cnt = (unsigned *) a.carve(4);
 }
 
-// Ring stages for the grouped GEMV: a multiple of the consumer warps, ~96 KB,
-// within kMoeSmem beside eight staged activations (moe_pick_tr ensures one per warp fits).
-inline int moe_stages(const TT & t) {
-    int ns = (int) ((96 * 1024) / t.tb) / kConsWarps * kConsWarps;
-    const int fit = (int) ((kMoeSmem - 8 * moe_act_bytes(t.cols)) / t.tb) / kConsWarps * kConsWarps;
-    if (ns > fit) ns = fit;
-    return ns < kConsWarps ? kConsWarps : ns > kMaxStages ? kMaxStages : ns;
-}
+// Ring stages of the grouped GEMV for nt staged activations.
+inline int moe_stages(const TT & t, int nt) { return ring_stages((size_t) nt * moe_act_bytes(t.cols), t.tb); }
 
 template <int NB, int SIX>
 inline void moe_gemv_w(int mode, int nt, const MoeGArgs & g, int grid, size_t smem, cudaStream_t st, bool pdl,
@@ -169,6 +161,8 @@ inline void moe_gemv_w(int mode, int nt, const MoeGArgs & g, int grid, size_t sm
     if (nt == 1 && mode != MG_PLAIN) {
         *r = mode == MG_GU ? moe_gemv_launch<MG_GU, NB, SIX, 1>(g, grid, smem, st, pdl)
                            : moe_gemv_launch<MG_DN, NB, SIX, 1>(g, grid, smem, st, pdl);
+    } else if (mode == MG_PLAIN && nt == 4) {
+        *r = moe_gemv_launch<MG_PLAIN, NB, SIX, 4>(g, grid, smem, st, pdl);
     } else {
         *r = mode == MG_GU ? moe_gemv_launch<MG_GU, NB, SIX, 8>(g, grid, smem, st, pdl)
            : mode == MG_DN ? moe_gemv_launch<MG_DN, NB, SIX, 8>(g, grid, smem, st, pdl)
@@ -176,10 +170,11 @@ inline void moe_gemv_w(int mode, int nt, const MoeGArgs & g, int grid, size_t sm
     }
 }
 
-// nt: tokens per chunk, 1 or 8 (a batched PLAIN GEMV always runs the 8-token kernel).
+// nt: tokens per chunk: 1 or 8 for the expert GEMVs, 8 or 4 for a batched
+// PLAIN GEMV (4 when eight staged activations leave no room for the ring).
 inline cudaError_t moe_gemv(int mode, int nt, const MoeGArgs & g, int grid, cudaStream_t st, bool pdl) {
     cudaError_t r = cudaErrorInvalidValue;
-    if (mode == MG_PLAIN) nt = 8;
+    if (mode == MG_PLAIN && nt != 4) nt = 8;
     SB_DISPATCH_QT(g.t.nbits, g.t.six, moe_gemv_w, mode, nt, g, grid, moe_gemv_smem(g, nt), st, pdl, &r);
     return r;
 }
@@ -224,7 +219,7 @@ inline void moe_enqueue(const MoeLayer & m, const MoeScratch & s, const float * 
         a.t = m.gu; a.tiles = m.gu_tiles; a.perm = m.gu_perm; a.scatter = m.dn_iperm;
         a.in = norm_w ? s.xn : x; a.in_stride = m.E; a.in_div = m.k;
         a.out = s.hp; a.out_stride = m.F; a.ffn_f = m.F;
-        a.nstage = moe_stages(m.gu);
+        a.nstage = moe_stages(m.gu, nt);
         a.launch_id = launch_id + 1;
         post(moe_gemv(MG_GU, nt, a, nsm, st, pdl), "moe.gate_up");
     }
@@ -233,7 +228,7 @@ inline void moe_enqueue(const MoeLayer & m, const MoeScratch & s, const float * 
         a.t = m.dn; a.tiles = m.dn_tiles;
         a.in = s.hp; a.in_stride = m.F; a.in_div = 1;
         a.out = s.yk; a.out_stride = m.E;
-        a.nstage = moe_stages(m.dn);
+        a.nstage = moe_stages(m.dn, nt);
         a.launch_id = launch_id + 2;
         post(moe_gemv(MG_DN, nt, a, nsm, st, pdl), "moe.down");
     }

@@ -11,7 +11,7 @@ cudaError_t moe_gemv_launch(const MoeGArgs & g, int grid, size_t smem, cudaStrea
     static bool attr = false;
     if (!attr) {
         const cudaError_t e = cudaFuncSetAttribute(k_moe_gemv<MODE, NB, SIX, NT>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kSmemBudget);
         if (e != cudaSuccess) return e;
         attr = true;
     }

@@ -5,13 +5,16 @@
 // cp.async.bulk and mbarrier transaction counts -- it starts before the kernel
 // waits on its predecessor, since weights never depend on it. Lane j of the
 // producer owns stage j and issues its tiles, so the copies of a ring's worth
-// of tiles leave in one warp instruction. Eight consumer
-// warps stage the int8 activation (the mode's prologue: RMSNorm, gather,
-// per-32 quantization), then take whole tiles round-robin: lane l owns row
-// l % TR and every (32/TR)-th unit of it, so a lane's units are independent
-// work and the warp reduces once per tile. The ring depth is a multiple of the
-// eight consumer warps, so tile k lands in stage k % ns and stage s is always
-// consumed by warp s % 8, in order -- the mbarrier parity protocol needs that.
+// of tiles leave in one warp instruction. Sixteen consumer warps stage the
+// int8 activation (the mode's prologue: RMSNorm, gather, per-32
+// quantization), then take whole tiles round-robin (tile k to warp k % 16):
+// lane l owns row l % TR and every (32/TR)-th unit of it, so a lane's units are
+// independent work and the warp reduces once per tile. Tile k lands in stage
+// k % ns. mbarrier.try_wait.parity reports a phase done whenever the barrier's
+// parity differs, so no waiter may run a phase ahead: with ns a multiple of 16
+// a stage always has the same consumer warp, which takes it in order; a ring of
+// 8 stages (wide tiles) has each waiter first see the stage's previous lap
+// consumed (ring_wait).
 //
 // Arithmetic per group (sml/sml-kernel.c:2027-2066 and the plane kinds of
 // :1934-2018): y += d*sq*xs*dot(code, xq) + md*(mq-bias)*xs*sum(xq), the dot
@@ -28,7 +31,10 @@ namespace sb {
 constexpr int kConsWarps = 16;
 constexpr int kConsThreads = kConsWarps * 32;
 constexpr int kTgThreads = kConsThreads + 32;   // + one producer warp
-constexpr int kMaxStages = 32;   // a multiple of kConsWarps: stage s belongs to warp s % kConsWarps
+constexpr int kMaxStages = 32;
+// Dynamic shared memory a GEMV may use (the device allows 227 KB per block,
+// less this file's static arrays).
+constexpr size_t kSmemBudget = 225 * 1024;
 
 struct TGArgs {
     TT t;
@@ -42,7 +48,8 @@ struct TGArgs {
     const int32_t * scatter; // FFN: write index of hidden value i
     float * am_val; int * am_idx; unsigned * am_cnt;
     int * tok; int * pos; int * tlog;
-    int nstage;
+    int nstage;              // ring stages: a multiple of 16, or 8
+    int x_smem;              // gathered input copied into shared memory first (else gathered from L2)
     int prefetch;            // L2 prefetch of this CTA's tiles before the wait
     int8_t * act_q; float * act_s; int32_t * act_sum;   // optional export (CTA 0)
     int * err;               // set if a bounded wait gave up
@@ -57,11 +64,12 @@ struct TGArgs {
 
 // Shared memory: [act | perm | norm gain | input x | ring]. perm and the gain
 // are static, so the producer bulk-loads them before the dependency wait; the
-// input is read once, coalesced, after it.
+// input is read once, coalesced, after it (when it fits; wide inputs are
+// gathered from L2 instead).
 struct StageLayout {
     uint32_t perm_off, w_off, x_off, ring_off;
 };
-__host__ __device__ inline StageLayout stage_layout(int n, int has_perm, int has_norm) {
+__host__ __device__ inline StageLayout stage_layout(int n, int has_perm, int has_norm, int has_x) {
     StageLayout L;
     uint32_t off = (uint32_t) ((act_smem_bytes(n) + 127) / 128 * 128);
     L.perm_off = off;
@@ -69,12 +77,60 @@ __host__ __device__ inline StageLayout stage_layout(int n, int has_perm, int has
     L.w_off = off;
     if (has_norm) off += (uint32_t) n * 4;
     L.x_off = off;
-    if (has_perm) off += (uint32_t) n * 4;
+    if (has_perm && has_x) off += (uint32_t) n * 4;
     L.ring_off = (off + 127) / 128 * 128;
     return L;
 }
-__host__ __device__ inline size_t tg_ring_off(int n, int in_permuted, int has_norm) {
-    return stage_layout(n, !in_permuted, has_norm).ring_off;
+__host__ __device__ inline size_t tg_ring_off(int n, int in_permuted, int has_norm, int x_smem) {
+    return stage_layout(n, !in_permuted, has_norm, x_smem).ring_off;
+}
+
+// Ring stages for tiles of tb bytes behind ring_off bytes of staging: the
+// multiple of 16 nearest ~96 KB (16..32) when 16 fit the budget, else 8 if
+// they fit; 0 otherwise. (Fewer than 8 would put four or more warps on one
+// stage, where a parity wait can no longer tell its lap from an older one.)
+__host__ __device__ inline int ring_stages(size_t ring_off, uint32_t tb) {
+    if (ring_off >= kSmemBudget) return 0;
+    const size_t fit = (kSmemBudget - ring_off) / tb;
+    int ns = (int) ((96 * 1024) / tb) / kConsWarps * kConsWarps;
+    ns = ns < kConsWarps ? kConsWarps : ns > kMaxStages ? kMaxStages : ns;
+    while (ns > kConsWarps && (size_t) ns > fit) ns -= kConsWarps;
+    if ((size_t) ns <= fit) return ns;
+    return fit >= 8 ? 8 : 0;
+}
+
+// Staging layout and ring depth of one GEMV launch: the input copied into
+// shared memory with a ring of at least 16 stages if that fits the budget,
+// else gathered from L2 with 16 or 8 stages. False if not even 8 fit.
+__host__ inline bool tg_plan(TGArgs & g) {
+    const int hn = g.norm_w != nullptr;
+    if (g.in_permuted) {
+        g.x_smem = 0;
+        g.nstage = ring_stages(tg_ring_off(g.t.cols, 1, hn, 0), g.t.tb);
+        return g.nstage > 0;
+    }
+    const int ns = ring_stages(tg_ring_off(g.t.cols, 0, hn, 1), g.t.tb);
+    if (ns >= kConsWarps) { g.x_smem = 1; g.nstage = ns; return true; }
+    g.x_smem = 0;
+    g.nstage = ring_stages(tg_ring_off(g.t.cols, 0, hn, 0), g.t.tb);
+    return g.nstage > 0;
+}
+__host__ inline size_t tg_smem(const TGArgs & g) {
+    return tg_ring_off(g.t.cols, g.in_permuted, g.norm_w != nullptr, g.x_smem) + (size_t) g.nstage * g.t.tb;
+}
+
+// Wait for tile k of the ring (stage k % ns, lap k / ns) as consumer warp
+// k % 16. try_wait.parity reports a phase done whenever the barrier's parity
+// differs from the one asked for, so the barrier must be at most one phase
+// from the waiter's. With ns a multiple of 16 the stage's previous lap was this
+// warp's own, so that holds. With ns = 8 two warps alternate on a stage: the
+// waiter first sees the previous lap consumed (empty barrier: at most one
+// phase behind, since its own lap before that is done), which puts the full
+// barrier at this lap or just past it.
+SB_DEV bool ring_wait(uint64_t * full, uint64_t * empty, int k, int ns, int * err) {
+    const int s = k % ns, lap = k / ns;
+    if (ns < kConsWarps && lap > 0 && !mbar_wait(&empty[s], (lap - 1) & 1, err, 2)) return false;
+    return mbar_wait(&full[s], lap & 1, err, 2);
 }
 
 // Quantize groups of 32 with 8 lanes per group, 4 values per lane (4 groups
@@ -161,6 +217,7 @@ SB_DEV void tg_stage(const TGArgs & g, ActS & a, double * red, uint8_t * smem, c
             const int grp = r * nteam + team;
             v[r] = grp < ng ? *reinterpret_cast<const float4 *>(g.in + grp * kGroup + 4 * sub) : make_float4(0.f, 0.f, 0.f, 0.f);
         }
+        SB_MARK(g.trace, g.launch_id, 5);   // thread 0's loads are issued
 #pragma unroll
         for (int r = 0; r < kR; r++) {
             const int grp = r * nteam + team;
@@ -175,19 +232,22 @@ SB_DEV void tg_stage(const TGArgs & g, ActS & a, double * red, uint8_t * smem, c
         return;
     }
     float * xs = reinterpret_cast<float *>(smem + L.x_off);
+    const float * xg = g.x_smem ? xs : g.in;   // where the gather reads x
     const int32_t * perm = reinterpret_cast<const int32_t *>(smem + L.perm_off);
     const float * gw = reinterpret_cast<const float *>(smem + L.w_off);
     double q = 0.0;
-    for (int i = 4 * tid; i < n; i += 4 * kConsThreads) {
-        const float4 f = *reinterpret_cast<const float4 *>(g.in + i);
-        *reinterpret_cast<float4 *>(xs + i) = f;
-        q += (double) f.x * f.x + (double) f.y * f.y + (double) f.z * f.z + (double) f.w * f.w;
-    }
+    if (g.x_smem || g.norm_w)
+        for (int i = 4 * tid; i < n; i += 4 * kConsThreads) {
+            const float4 f = *reinterpret_cast<const float4 *>(g.in + i);
+            if (g.x_smem) *reinterpret_cast<float4 *>(xs + i) = f;
+            q += (double) f.x * f.x + (double) f.y * f.y + (double) f.z * f.z + (double) f.w * f.w;
+        }
     float s = 1.0f;
     if (g.norm_w) {
         q = warp_sum_d(q);
         if (lane == 0) red[w] = q;
     }
+    SB_MARK(g.trace, g.launch_id, 5);   // thread 0's share of x is in
     bar_sync(1, kConsThreads);
     if (g.norm_w) {
         double ss = 0.0;
@@ -204,7 +264,7 @@ SB_DEV void tg_stage(const TGArgs & g, ActS & a, double * red, uint8_t * smem, c
             float vv[4];
 #pragma unroll
             for (int k = 0; k < 4; k++)
-                vv[k] = g.norm_w ? __fmul_rn(__fmul_rn(xs[pi[k]], s), gw[pi[k]]) : xs[pi[k]];
+                vv[k] = g.norm_w ? __fmul_rn(__fmul_rn(xg[pi[k]], s), gw[pi[k]]) : xg[pi[k]];
             quant_team(make_float4(vv[0], vv[1], vv[2], vv[3]), grp, sub, a, g, ex, grp < ng);
         }
     }
@@ -335,13 +395,13 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__
     const int T = t.ntiles;
     const int t0 = (int) ((long) T * blockIdx.x / gridDim.x), t1 = (int) ((long) T * (blockIdx.x + 1) / gridDim.x);
     const int ns = g.nstage;
-    const StageLayout SL = stage_layout(t.cols, !g.in_permuted, g.norm_w != nullptr);
+    const StageLayout SL = stage_layout(t.cols, !g.in_permuted, g.norm_w != nullptr, g.x_smem);
     uint8_t * ring = smem + SL.ring_off;
 #ifdef SB_CHECKED
     uint32_t dsm;
     asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dsm));
     const size_t ring_end = dsm;
-    if (!SB_CHECK(g.err, ns >= kConsWarps && ns % kConsWarps == 0 && ns <= kMaxStages &&
+    if (!SB_CHECK(g.err, (ns == 8 || ns % kConsWarps == 0) && ns <= kMaxStages &&
                            SL.ring_off + (size_t) ns * t.tb <= dsm, 107)) return;
 #else
     const size_t ring_end = ~(size_t) 0;
@@ -410,7 +470,7 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__
     int best_i = 0x7fffffff;
     for (int i = t0 + warp; i < t1; i += kConsWarps) {
         const int k = i - t0, s = k % ns;
-        const bool ok = !failed && mbar_wait(&full[s], (k / ns) & 1, g.err, 2);
+        const bool ok = !failed && ring_wait(full, empty, k, ns, g.err);
         failed = !ok;
         if (k == 0) SB_MARK(g.trace, g.launch_id, 3);
         float acc = 0.0f;

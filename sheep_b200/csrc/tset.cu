@@ -1,6 +1,7 @@
 // A tensor set: every flat tensor of an SSF file on the device, addressable by
 // name, for kernel-level entry points (GEMV microbench, parity tests, MoE
 // layer). The decode engine holds its own copy in its own arena.
+#include "moe_host.h"
 #include "tgemv.cuh"
 #include "sheep_b200.h"
 #include "upload.h"
@@ -8,16 +9,29 @@
 #include <cstdio>
 #include <string>
 #include <unordered_map>
+#include <vector>
 
 using namespace sb;
+
+// A tiled tensor with one-entry tile and column-order tables: the form the
+// grouped GEMV (moe.cuh, PLAIN mode) takes for a batch of vectors.
+struct TTB {
+    TT t;
+    const uint8_t * const * tiles_tab;
+    const int32_t * const * perm_tab;
+};
+
+constexpr int kMaxBatch = 4096;
 
 struct sb_tset {
     ssf_file f{};
     Arena ar;
     std::unordered_map<std::string, QT> q;    // file layout (row dequant)
-    std::unordered_map<std::string, TT> tt;   // tiled (GEMV)
+    std::unordered_map<std::string, TTB> tt;  // tiled (GEMV)
     std::unordered_map<std::string, const float *> f32;
     int * err = nullptr;
+    // batch plan: identity slots, chunks of 8 vectors of the one "expert"
+    int * slots = nullptr, * ch_e = nullptr, * ch_s0 = nullptr, * ch_n = nullptr, * meta = nullptr;
     int nsm = 148;
 };
 
@@ -33,13 +47,23 @@ static bool tset_build(sb_tset * t, char * why, int nwhy) {
         QT qt;
         if (!upload_qt(t->ar, t->f, r, qt, why, nwhy)) return false;
         t->q[nm] = qt;
-        TT tt;
+        TTB tb;
         if (!upload_tt(t->ar, t->f, r, (int) r->rows, 0, 6 * t->nsm, 0,
-                       [&](int v) { return RowSrc{v < (int) r->rows ? r : nullptr, v}; }, tt, why, nwhy))
+                       [&](int v) { return RowSrc{v < (int) r->rows ? r : nullptr, v}; }, tb.t, why, nwhy))
             return false;
-        t->tt[nm] = tt;
+        tb.tiles_tab = (const uint8_t * const *) t->ar.upload(&tb.t.tiles, sizeof(void *));
+        tb.perm_tab = (const int32_t * const *) t->ar.upload(&tb.t.perm, sizeof(void *));
+        t->tt[nm] = tb;
     }
     t->err = (int *) t->ar.carve(4);
+    std::vector<int> ident(kMaxBatch);
+    for (int i = 0; i < kMaxBatch; i++) ident[i] = i;
+    t->slots = (int *) t->ar.upload(ident.data(), ident.size() * 4);
+    const int nch = kMaxBatch / 8;
+    t->ch_e = (int *) t->ar.carve((size_t) nch * 4);
+    t->ch_s0 = (int *) t->ar.carve((size_t) nch * 4);
+    t->ch_n = (int *) t->ar.carve((size_t) nch * 4);
+    t->meta = (int *) t->ar.carve(8);
     return true;
 }
 
@@ -91,15 +115,19 @@ template <int NB, int SIX>
 static void launch_plain(const TGArgs & g, int grid, size_t smem, cudaStream_t st) {
     static bool attr = false;
     if (!attr) {
-        cudaFuncSetAttribute(k_tgemv<GM_PLAIN, NB, SIX>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+        cudaFuncSetAttribute(k_tgemv<GM_PLAIN, NB, SIX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kSmemBudget);
         attr = true;
     }
     k_tgemv<GM_PLAIN, NB, SIX><<<grid, kTgThreads, smem, st>>>(g);
 }
 
-static const TT * find_tt(const sb_tset * t, const char * name) {
+static const TTB * find_ttb(const sb_tset * t, const char * name) {
     auto it = t->tt.find(name);
     return it == t->tt.end() ? nullptr : &it->second;
+}
+static const TT * find_tt(const sb_tset * t, const char * name) {
+    const TTB * b = find_ttb(t, name);
+    return b ? &b->t : nullptr;
 }
 
 static TGArgs plain_args(const sb_tset * t, const TT & tt, const float * x, float * y) {
@@ -109,25 +137,123 @@ static TGArgs plain_args(const sb_tset * t, const TT & tt, const float * x, floa
     g.in = x;
     g.out = y;
     g.err = t->err;
-    int ns = (int) ((96 * 1024) / tt.tb) / kConsWarps * kConsWarps;
-    g.nstage = ns < kConsWarps ? kConsWarps : ns > kMaxStages ? kMaxStages : ns;
     return g;
 }
 
-static void run_plain(const sb_tset * t, const TGArgs & g, cudaStream_t st) {
+static bool run_plain(const sb_tset * t, const TGArgs & g0, cudaStream_t st) {
+    TGArgs g = g0;
+    if (!tg_plan(g)) return false;
     long grid = g.t.ntiles;
     if (grid > t->nsm) grid = t->nsm;
-    const size_t smem = tg_ring_off(g.t.cols, g.in_permuted, g.norm_w != nullptr) + (size_t) g.nstage * g.t.tb;
-    SB_DISPATCH_QT(g.t.nbits, g.t.six, launch_plain, g, (int) grid, smem, st);
+    SB_DISPATCH_QT(g.t.nbits, g.t.six, launch_plain, g, (int) grid, tg_smem(g), st);
+    return true;
 }
 
-// y[b] = W x[b] for nb vectors on device pointers (x: nb x cols, y: nb x rows).
+// The chunks of a batch of nb vectors: ceil(nb / nt) chunks of the one tensor.
+static __global__ void k_batch_plan(int nb, int nt, int * ch_e, int * ch_s0, int * ch_n, int * meta) {
+    const int nch = (nb + nt - 1) / nt;
+    for (int c = threadIdx.x; c < nch; c += blockDim.x) {
+        ch_e[c] = 0;
+        ch_s0[c] = nt * c;
+        ch_n[c] = nb - nt * c < nt ? nb - nt * c : nt;
+    }
+    if (threadIdx.x == 0) { meta[0] = nch; meta[1] = 1; }
+}
+
+// y[b] = W x[b] for nb > 1 vectors: the weights are read once per 8 vectors
+// (per 4 for rows so wide that eight staged vectors leave no room for the
+// ring), or once per vector if even that does not fit.
+static bool run_batch(const sb_tset * t, const TTB & b, const float * x, int nb, float * y, cudaStream_t st) {
+    const int nt = moe_stages(b.t, 8) ? 8 : moe_stages(b.t, 4) ? 4 : 0;
+    if (!nt) {
+        for (int i = 0; i < nb; i++)
+            if (!run_plain(t, plain_args(t, b.t, x + (size_t) i * b.t.cols, y + (size_t) i * b.t.rows), st)) return false;
+        return true;
+    }
+    k_batch_plan<<<1, 128, 0, st>>>(nb, nt, t->ch_e, t->ch_s0, t->ch_n, t->meta);
+    MoeGArgs g;
+    memset(&g, 0, sizeof g);
+    g.t = b.t; g.tiles = b.tiles_tab; g.perm = b.perm_tab;
+    g.in = x; g.in_stride = b.t.cols; g.in_div = 1;
+    g.out = y; g.out_stride = b.t.rows;
+    g.slots = t->slots; g.ch_e = t->ch_e; g.ch_s0 = t->ch_s0; g.ch_n = t->ch_n; g.meta = t->meta;
+    g.nstage = moe_stages(b.t, nt);
+    g.err = t->err;
+    return moe_gemv(MG_PLAIN, nt, g, t->nsm, st, false) == cudaSuccess;
+}
+
+// y[b] = W x[b] for nb vectors on device pointers (x: nb x cols, y: nb x rows):
+// one vector through the streaming GEMV, more through the batched one.
 extern "C" int sb_tset_gemv_dev(sb_tset * t, const char * name, const float * x, int nb, float * y, void * stream) {
-    const TT * q = find_tt(t, name);
-    if (!q || nb < 1) return 0;
-    for (int b = 0; b < nb; b++)
-        run_plain(t, plain_args(t, *q, x + (size_t) b * q->cols, y + (size_t) b * q->rows), (cudaStream_t) stream);
-    return cudaGetLastError() == cudaSuccess;
+    const TTB * b = find_ttb(t, name);
+    if (!b || nb < 1 || nb > kMaxBatch) return 0;
+    const cudaStream_t st = (cudaStream_t) stream;
+    const bool ok = nb == 1 ? run_plain(t, plain_args(t, b->t, x, y), st) : run_batch(t, *b, x, nb, y, st);
+    return ok && cudaGetLastError() == cudaSuccess;
+}
+
+// The same with host buffers (copies included, synchronous).
+extern "C" int sb_tset_gemv_host(sb_tset * t, const char * name, const float * x, int nb, float * y) {
+    const TTB * b = find_ttb(t, name);
+    if (!b || nb < 1 || nb > kMaxBatch) return 0;
+    float * dx = nullptr, * dy = nullptr;
+    bool ok = cudaMalloc(&dx, (size_t) nb * b->t.cols * 4) == cudaSuccess &&
+              cudaMalloc(&dy, (size_t) nb * b->t.rows * 4) == cudaSuccess;
+    int err = 0;
+    if (ok) {
+        cudaMemcpy(dx, x, (size_t) nb * b->t.cols * 4, cudaMemcpyHostToDevice);
+        ok = sb_tset_gemv_dev(t, name, dx, nb, dy, nullptr) && cudaDeviceSynchronize() == cudaSuccess;
+        cudaMemcpy(&err, t->err, 4, cudaMemcpyDeviceToHost);
+        ok = ok && err == 0;
+        if (ok) cudaMemcpy(y, dy, (size_t) nb * b->t.rows * 4, cudaMemcpyDeviceToHost);
+    }
+    cudaFree(dx);
+    cudaFree(dy);
+    return ok ? 1 : 0;
+}
+
+// Mean device time of sb_tset_gemv_dev over nb host vectors (copied once),
+// a buffer larger than L2 rewritten before each timed run so the weights come
+// from HBM: CUDA events around each run.
+extern "C" int sb_tset_time_gemv(sb_tset * t, const char * name, const float * x, int nb, int reps, float * ms_avg) {
+    const TTB * b = find_ttb(t, name);
+    if (!b || nb < 1 || nb > kMaxBatch || reps < 1) return 0;
+    float * dx = nullptr, * dy = nullptr;
+    void * flush = nullptr;
+    const size_t flush_n = (size_t) 512 << 20;
+    cudaStream_t st = nullptr;
+    bool ok = cudaMalloc(&dx, (size_t) nb * b->t.cols * 4) == cudaSuccess &&
+              cudaMalloc(&dy, (size_t) nb * b->t.rows * 4) == cudaSuccess &&
+              cudaMalloc(&flush, flush_n) == cudaSuccess && cudaStreamCreate(&st) == cudaSuccess;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    double total = 0.0;
+    if (ok) {
+        cudaEventCreate(&e0);
+        cudaEventCreate(&e1);
+        cudaMemcpy(dx, x, (size_t) nb * b->t.cols * 4, cudaMemcpyHostToDevice);
+        for (int r = 0; ok && r < 3; r++) ok = sb_tset_gemv_dev(t, name, dx, nb, dy, st);
+        for (int r = 0; ok && r < reps; r++) {
+            cudaMemsetAsync(flush, r & 0xff, flush_n, st);
+            cudaEventRecord(e0, st);
+            ok = sb_tset_gemv_dev(t, name, dx, nb, dy, st);
+            cudaEventRecord(e1, st);
+            ok = ok && cudaEventSynchronize(e1) == cudaSuccess;
+            float ms = 0.0f;
+            cudaEventElapsedTime(&ms, e0, e1);
+            total += ms;
+        }
+        int err = 0;
+        cudaMemcpy(&err, t->err, 4, cudaMemcpyDeviceToHost);
+        ok = ok && err == 0;
+    }
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    if (st) cudaStreamDestroy(st);
+    cudaFree(dx);
+    cudaFree(dy);
+    cudaFree(flush);
+    if (ms_avg) *ms_avg = (float) (total / reps);
+    return ok ? 1 : 0;
 }
 
 // Host-buffer form for tests: y = W x, plus the int8 activation the kernel
@@ -147,9 +273,9 @@ extern "C" int sb_tset_matvec(sb_tset * t, const char * name, const float * x, f
         cudaMemcpy(dx, x, (size_t) n * 4, cudaMemcpyHostToDevice);
         TGArgs g = plain_args(t, *q, dx, dy);
         g.act_q = dq; g.act_s = ds; g.act_sum = dsum;
-        run_plain(t, g, (cudaStream_t) 0);
+        ok = run_plain(t, g, (cudaStream_t) 0);
         int err = 0;
-        ok = cudaDeviceSynchronize() == cudaSuccess;
+        ok = cudaDeviceSynchronize() == cudaSuccess && ok;
         cudaMemcpy(&err, t->err, 4, cudaMemcpyDeviceToHost);
         ok = ok && err == 0;
         if (ok) {

@@ -223,3 +223,47 @@ def test_attention_decode(hd, nh, nkv, pos, norm):
         np.abs(k16.astype(np.float64)).max() * 2.0 ** -10
     # positions other than pos untouched
     assert np.array_equal(d["kc"].cpu().numpy()[:pos], kc.view(np.uint16)[:pos])
+
+
+@pytest.mark.parametrize("nb,six", [(4, 0), (8, 0), (6, 1), (2, 1), (3, 0), (5, 1), (7, 0)])
+def test_batched_gemv_widths(nb, six):
+    """The batched GEMV (weights read once per 8 vectors) against the oracle
+    vector by vector, at batches of 1 (the streaming GEMV), 4, 13 and 16."""
+    path = _width_model(nb, six)
+    ts = sheep_b200.TensorSet(path)
+    orc = helpers.Oracle(path)
+    rng = np.random.default_rng(nb * 7 + six)
+    try:
+        for name in ("blk.0.ffn_down.weight", "blk.0.attn_q.weight"):
+            rows, cols, _ = ts.shape(name)
+            for B in (1, 4, 13, 16):
+                X = rng.standard_normal((B, cols)).astype(np.float16).astype(np.float32)
+                Y = ts.gemv(name, X)
+                for b in range(B):
+                    assert helpers.rel_rms(orc.matvec(name, X[b], rows), Y[b]) <= GEMV_TOL, (name, B, b)
+    finally:
+        ts.close()
+        orc.close()
+
+
+@pytest.mark.parametrize("cfg", ["gemv-4096-q4", "gemv-4096-q8"])
+def test_gemv_microbench_shapes(cfg):
+    """Configuration 1's matrices (4096x4096, 14336x4096, 4096x14336; Q4 and
+    Q8) at batches 1, 4 and 16. The 14336-column rows do not leave room for the
+    input copy and a 16-stage ring: they run with the input gathered from L2
+    and a shorter ring."""
+    path = helpers.model_path(sheep_b200.spec_for(cfg))
+    ts = sheep_b200.TensorSet(path)
+    orc = helpers.Oracle(path)
+    rng = np.random.default_rng(17)
+    try:
+        for name in ("blk.0.attn_q.weight", "blk.0.ffn_gate.weight", "blk.0.ffn_down.weight"):
+            rows, cols, _ = ts.shape(name)
+            for B in (1, 4, 16):
+                X = rng.standard_normal((B, cols)).astype(np.float16).astype(np.float32)
+                Y = ts.gemv(name, X)
+                for b in range(0, B, 3):
+                    assert helpers.rel_rms(orc.matvec(name, X[b], rows), Y[b]) <= GEMV_TOL, (name, B, b)
+    finally:
+        ts.close()
+        orc.close()
