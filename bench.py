@@ -20,7 +20,8 @@ extras (single GPU only): configuration 1's GEMV microbench (GB/s of weight
 bytes streamed, Q4 and Q8, batch 1/4/16) and configuration 2's MoE layer
 (Qwen3-30B-A3B shape at 1/16/64/256 tokens a step: tok/s and GB/s of the
 experts actually read plus the router), each run timed alone by CUDA events
-with a 512 MB buffer rewritten before it, so the weights come from HBM.
+with a 512 MB buffer rewritten before it, so the weights come from HBM; and
+configuration 3's batch-1 decode (Llama-3-8B shape, 4.2 GB per token).
 """
 import argparse
 import ctypes
@@ -280,8 +281,9 @@ def main():
     extras = None
     if rank == 0 and world == 1:
         peak0, _ = peaks()
-        extras = {"l2": "a 512 MB buffer rewritten before each timed run",
-                  "gemv_cfg1": gemv_microbench(peak0), "moe_cfg2": moe_microbench(peak0)}
+        extras = {"l2": "a 512 MB buffer rewritten before each timed run (decode: weights > L2)",
+                  "gemv_cfg1": gemv_microbench(peak0), "moe_cfg2": moe_microbench(peak0),
+                  "decode_cfg3": decode_cfg3(peak0)}
 
     if rank == 0:
         peak, peak_kind = peaks()
@@ -340,6 +342,24 @@ def gemv_microbench(peak, reps=20):
         finally:
             ts.close()
     return out
+
+
+def decode_cfg3(peak, ngen=64):
+    """Configuration 3 (Llama-3-8B shape, 6-bit group fields) at batch 1: the
+    device-resident greedy loop after a 128-token prompt."""
+    import sheep_b200
+    from sheep_b200 import configs
+    path = model_path(configs.CONFIGS["llama3-8b-q4k"], 0, None)
+    eng = sheep_b200.Engine(path, n_ctx=PROMPT_LEN + 8 + ngen + 8)
+    try:
+        prompt = np.random.default_rng(1234).integers(0, eng.n_vocab, PROMPT_LEN).astype(np.int32)
+        _, ms = eng.generate(prompt, ngen + 1, timed=True, warmup=8)
+        tps = ngen / (ms / 1000.0)
+        gbs = eng.bytes_per_token * tps / 1e9
+        return {"tok_s": round(tps, 1), "ms_per_token": round(ms / ngen, 4), "bytes_per_token": eng.bytes_per_token,
+                "gbs": round(gbs, 1), "frac": round(gbs / peak, 4), "tokens": ngen}
+    finally:
+        eng.close()
 
 
 def moe_microbench(peak, reps=20):
