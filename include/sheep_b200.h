@@ -150,6 +150,16 @@ int sb_moe_route(const float * logits, int n_tok, int n_expert, int k, unsigned 
                  void * stream);
 const char * sb_moe_last_error(void);
 
+// ------------------------------------------------------------------ tensor cores
+// C[M][N] (int32) = A[M][K] * B[N][K]^T on the 5th-generation tensor cores
+// (tcgen05.mma kind::i8, accumulator in tensor memory): A and B signed 8-bit,
+// row-major; M a multiple of 128, N one of 16/32/64/128/256, K a multiple of
+// 32; device pointers, 16-byte aligned. *err (device) receives a code if a
+// bounded wait gave up. Asynchronous on `stream`. The integer core of the
+// batched path (the reference's int8 tiles, sml_g_tcm9, sml/sml-gpu-fast.cu:3149).
+int sb_tc_imma(const int8_t * A, const int8_t * B, int32_t * C, int M, int N, int K, int * err, void * stream);
+const char * sb_tc_last_error(void);
+
 // ------------------------------------------------------------------ models
 // Seeded synthetic SSF writer (the inputs every test and bench runs on; the
 // reference builds SSF files offline, tooling/sml_quantize.py:596-651).

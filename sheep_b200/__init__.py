@@ -89,6 +89,8 @@ def lib():
         "sb_moe_time": (ip, [vp, vp, ip, ip, fp, vp]),
         "sb_moe_route": (ip, [vp, ip, ip, ip, ctypes.c_uint, vp, vp, vp]),
         "sb_moe_last_error": (cp, []),
+        "sb_tc_imma": (ip, [vp, vp, vp, ip, ip, ip, vp, vp]),
+        "sb_tc_last_error": (cp, []),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
