@@ -74,6 +74,16 @@ int sb_tset_gemv_host(sb_tset * t, const char * name, const float * x, int nb, f
 // Mean device time (CUDA events) of one sb_tset_gemv_dev over nb host vectors
 // copied to the device once, a buffer larger than L2 rewritten before each run.
 int sb_tset_time_gemv(sb_tset * t, const char * name, const float * x, int nb, int reps, float * ms_avg);
+// The batched path on the tensor cores, with the reference's batched
+// arithmetic (sml_g_requant8 + the int8 tiles, sml/sml-gpu-fast.cu:1804-1880,
+// 2025-2031): the weights re-quantized once to int8 with one scale per row per
+// 256 (kept on the device), x quantized per 256, int32 superblock dots from
+// tcgen05, one float epilogue per superblock. Device pointers, nb <= 4096.
+int sb_tset_gemm_tc(sb_tset * t, const char * name, const float * x, int nb, float * y, void * stream);
+int sb_tset_gemm_tc_host(sb_tset * t, const char * name, const float * x, int nb, float * y);
+int sb_tset_time_gemm_tc(sb_tset * t, const char * name, const float * x, int nb, int reps, float * ms_avg);
+// The re-quantized weights, host buffers: w8 rows x (nsb*256), s8 rows x nsb (nsb = ceil(cols/256)).
+int sb_tset_requant8_host(sb_tset * t, const char * name, int8_t * w8, float * s8);
 // Host-buffer form of one GEMV; q/s/sums (host, may be NULL) receive the int8
 // activation the kernel used. Mirrors what sml-check writes
 // (sml/sml-check.c:194-245).

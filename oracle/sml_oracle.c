@@ -284,6 +284,95 @@ static void matvec_rec(const so_model * m, const rec_t * r, const float * x, flo
     free(xg); free(q); free(xs); free(sums);
 }
 
+// ------------------------------------------------------------- batched path
+
+// The batched path's weights (sml_g_requant8, sml/sml-gpu-fast.cu:1804-1880):
+// per row and 256-weight superblock, bound = the largest |w| its groups can
+// take, max(|m|, |s*cmax + m|) with s = d*sq, m = md*(mq - bias) and s*cmax + m
+// fused; s8 = bound/127; w8 = rint(fma(code, s*inv, m*inv)) with inv = 127/bound.
+// Generalized from the reference's 4- and 6-bit codes with 8-bit fields to every
+// width (cmax = 2^nbits - 1) and the file's min bias. w8: rows x (nsb * 256),
+// zero past the last group; s8: rows x nsb.
+int so_requant8(so_model * m, const char * name, int8_t * w8, float * s8) {
+    const rec_t * r = find(m, name);
+    if (!r || r->kind != 1 || r->layout != 1) return 0;
+    const int n = (int) r->cols, ng = n / G, nsb = (ng + 7) / 8, K = nsb * 256;
+    const float cmax = (float) ((1 << r->nbits) - 1);
+#pragma omp parallel for schedule(static)
+    for (int row = 0; row < (int) r->rows; row++) {
+        uint8_t * c = (uint8_t *) malloc((size_t) n);
+        row_codes(m, r, row, c);
+        int8_t * wr = w8 + (size_t) row * K;
+        memset(wr, 0, (size_t) K);
+        for (int sb = 0; sb < nsb; sb++) {
+            const int g0 = sb * 8, g1 = g0 + 8 < ng ? g0 + 8 : ng;
+            float bound = 0.0f;
+            for (int g = g0; g < g1; g++) {
+                float st, mn;
+                group_grid(m, r, row, g, &st, &mn);
+                const float top = fmaf(st, cmax, mn);
+                const float am = fabsf(mn), at = fabsf(top), b = am > at ? am : at;
+                bound = b > bound ? b : bound;
+            }
+            s8[(size_t) row * nsb + sb] = bound / 127.0f;
+            const float inv = bound > 0.0f ? 127.0f / bound : 0.0f;
+            for (int g = g0; g < g1; g++) {
+                float st, mn;
+                group_grid(m, r, row, g, &st, &mn);
+                const float ka = st * inv, kb = mn * inv;
+                for (int j = 0; j < G; j++) wr[g * G + j] = (int8_t) rintf(fmaf((float) c[g * G + j], ka, kb));
+            }
+        }
+        free(c);
+    }
+    return 1;
+}
+
+// The batched product (sml_g_tcm3/tcm9 epilogue, sml/sml-gpu-fast.cu:2025-2031):
+// each row of X gathered through the tensor's column order and quantized per 256
+// (one scale per superblock, sml_quantize_act_sb, sml/sml-kernel.c:164-189),
+// then y[t][row] = sum over superblocks, in order, of
+// fma(s8 * xs, dot(w8, xq), acc). X: T x cols, Y: T x rows.
+int so_gemm_sb(so_model * m, const char * name, const float * X, int T, float * Y) {
+    const rec_t * r = find(m, name);
+    if (!r || r->kind != 1 || r->layout != 1 || T < 1) return 0;
+    const int n = (int) r->cols, ng = n / G, nsb = (ng + 7) / 8, K = nsb * 256, rows = (int) r->rows;
+    int8_t * w8 = (int8_t *) malloc((size_t) rows * K);
+    float * s8 = (float *) malloc((size_t) rows * nsb * 4);
+    so_requant8(m, name, w8, s8);
+    const int32_t * perm = (const int32_t *) (m->base + r->perm_off);
+    int8_t * q = (int8_t *) malloc((size_t) K);
+    float * xs = (float *) malloc((size_t) nsb * 4), * xg = (float *) malloc((size_t) n * 4);
+    for (int t = 0; t < T; t++) {
+        for (int i = 0; i < n; i++) xg[i] = X[(size_t) t * n + perm[i]];
+        memset(q, 0, (size_t) K);
+        for (int sb = 0; sb < nsb; sb++) {
+            const int i0 = sb * 256, i1 = (sb * 8 + 8 < ng ? sb * 8 + 8 : ng) * G;
+            float amax = 0.0f;
+            for (int i = i0; i < i1; i++) { const float v = fabsf(xg[i]); if (v > amax) amax = v; }
+            const float sc = amax / 127.0f, is = sc > 0.0f ? 1.0f / sc : 0.0f;
+            xs[sb] = sc;
+            for (int i = i0; i < i1; i++) {
+                int v = (int) lrintf(xg[i] * is);
+                q[i] = (int8_t) (v > 127 ? 127 : v < -127 ? -127 : v);
+            }
+        }
+#pragma omp parallel for schedule(static)
+        for (int row = 0; row < rows; row++) {
+            const int8_t * wr = w8 + (size_t) row * K;
+            float acc = 0.0f;
+            for (int sb = 0; sb < nsb; sb++) {
+                int32_t d = 0;
+                for (int i = sb * 256; i < sb * 256 + 256; i++) d += (int32_t) wr[i] * (int32_t) q[i];
+                acc = fmaf(s8[(size_t) row * nsb + sb] * xs[sb], (float) d, acc);
+            }
+            Y[(size_t) t * rows + row] = acc;
+        }
+    }
+    free(w8); free(s8); free(q); free(xs); free(xg);
+    return 1;
+}
+
 static void matvec_f32(const float * w, int rows, int n, const float * x, float * y) {
     for (int i = 0; i < rows; i++) {                         // sml/sml-run.c:3076-3081
         double s = 0.0;

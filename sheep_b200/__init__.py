@@ -70,6 +70,10 @@ def lib():
         "sb_tset_gemv_dev": (ip, [vp, cp, vp, ip, vp, vp]),
         "sb_tset_gemv_host": (ip, [vp, cp, vp, ip, vp]),
         "sb_tset_time_gemv": (ip, [vp, cp, vp, ip, ip, fp]),
+        "sb_tset_gemm_tc": (ip, [vp, cp, vp, ip, vp, vp]),
+        "sb_tset_gemm_tc_host": (ip, [vp, cp, vp, ip, vp]),
+        "sb_tset_time_gemm_tc": (ip, [vp, cp, vp, ip, ip, fp]),
+        "sb_tset_requant8_host": (ip, [vp, cp, vp, vp]),
         "sb_tset_matvec": (ip, [vp, cp, vp, vp, vp, vp, vp]),
         "sb_tset_dequant_rows": (ip, [vp, cp, vp, ip, vp]),
         "sb_quantize_act": (ip, [vp, vp, ip, vp, vp, vp, vp]),
@@ -245,6 +249,32 @@ class TensorSet:
         if not lib().sb_tset_time_gemv(self.h, name.encode(), _p(X), len(X), reps, ctypes.byref(ms)):
             raise RuntimeError("sb_tset_time_gemv failed")
         return ms.value
+
+    def gemm_tc(self, name, X):
+        """Y [nb, rows]: the batched path on the tensor cores (int8 per-256 arithmetic)."""
+        rows, cols, _ = self.shape(name)
+        X = np.ascontiguousarray(np.atleast_2d(X), np.float32)
+        Y = np.zeros((len(X), rows), np.float32)
+        if not lib().sb_tset_gemm_tc_host(self.h, name.encode(), _p(X), len(X), _p(Y)):
+            raise RuntimeError("sb_tset_gemm_tc_host failed")
+        return Y
+
+    def time_gemm_tc(self, name, X, reps):
+        X = np.ascontiguousarray(np.atleast_2d(X), np.float32)
+        ms = ctypes.c_float()
+        if not lib().sb_tset_time_gemm_tc(self.h, name.encode(), _p(X), len(X), reps, ctypes.byref(ms)):
+            raise RuntimeError("sb_tset_time_gemm_tc failed")
+        return ms.value
+
+    def requant8(self, name):
+        """(w8 [rows, nsb*256] int8, s8 [rows, nsb] float32) of the tensor-core path."""
+        rows, cols, _ = self.shape(name)
+        nsb = (cols // 32 + 7) // 8
+        w8 = np.zeros((rows, nsb * 256), np.int8)
+        s8 = np.zeros((rows, nsb), np.float32)
+        if not lib().sb_tset_requant8_host(self.h, name.encode(), _p(w8), _p(s8)):
+            raise RuntimeError("sb_tset_requant8_host failed")
+        return w8, s8
 
     def gemv_dev(self, name, x_ptr, nb, y_ptr, stream=0):
         if not lib().sb_tset_gemv_dev(self.h, name.encode(), x_ptr, nb, y_ptr, stream):

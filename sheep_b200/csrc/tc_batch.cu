@@ -1,0 +1,245 @@
+// The batched path on the tensor cores: y[t] = W x[t] for T >= 16 rows of x,
+// with the reference's batched arithmetic (sml_g_requant8 and the int8 tiles,
+// sml/sml-gpu-fast.cu:1804-1880, 2025-2031): the weights re-quantized to int8
+// with one fp32 scale per row per 256 (the group scale and min folded in), x
+// quantized per 256, the int32 dot of a superblock from tcgen05.mma, and one
+// float epilogue per superblock, acc = fma(s8 * xs, dot, acc), superblocks in
+// order -- so results equal the CPU restatement bit for bit.
+//
+//   k_requant8   one warp per (row, superblock): the bound of its groups, s8,
+//                and the 256 int8 weights, written as the GEMM's A operand:
+//                a 32 KB block per (128 rows, superblock) in the core-matrix
+//                layout of tc.cuh. Done once per tensor, kept on the device
+//                (the reference re-makes it per call).
+//   k_quant_sb   one warp per (token, superblock): the B operand, a block of
+//                N x 256 bytes per (N tokens, superblock), and the scale.
+//   k_tcgemm<N>  one CTA per (128 rows, N tokens), six warps: a producer
+//                (bulk copies of both blocks of a superblock into a 4-stage
+//                ring), an MMA issuer (8 MMAs of K = 32 per superblock into
+//                one of two TMEM accumulators, then commits), and four
+//                epilogue warps (TMEM lanes 0..127 = rows) that apply the
+//                superblock's scales while the next superblock multiplies.
+#include "tc.cuh"
+#include "decode.cuh"
+#include "sheep_b200.h"
+#include "tc_batch.h"
+
+#include <cstdio>
+
+namespace sb {
+
+constexpr int kTcStages = 4;
+constexpr uint32_t kTcABytes = 128 * 256;
+
+template <int NB, int SIX>
+__global__ void __launch_bounds__(256) k_requant8(const __grid_constant__ QT t, uint8_t * wblk, float * s8,
+                                                  int rows_pad, int nsb) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long item = (long) blockIdx.x * 8 + warp;
+    if (item >= (long) rows_pad * nsb) return;
+    const int r = (int) (item / nsb), sb = (int) (item % nsb);
+    const int ng = t.cols / kGroup, g = sb * 8 + (lane >> 2), part = lane & 3;
+    const bool live = r < t.rows && g < ng;
+    const float cmax = (float) ((1 << NB) - 1);
+    float s = 0.0f, m = 0.0f, bound = 0.0f;
+    if (live) {
+        s = __fmul_rn(h2f(t.sd[(size_t) r * t.nsb + sb]), (float) field_at<SIX>(t.sq, t.frow, r, g));
+        if (t.has_min)
+            m = __fmul_rn(h2f(t.md[(size_t) r * t.nsb + sb]), __fsub_rn((float) field_at<SIX>(t.mq, t.frow, r, g), t.mbias));
+        const float top = __fmaf_rn(s, cmax, m);
+        bound = fmaxf(fabsf(m), fabsf(top));
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) bound = fmaxf(bound, __shfl_xor_sync(0xffffffffu, bound, o));
+    if (lane == 0) s8[(size_t) sb * rows_pad + r] = __fdiv_rn(bound, 127.0f);
+    const float inv = bound > 0.0f ? __fdiv_rn(127.0f, bound) : 0.0f;
+    const float ka = __fmul_rn(s, inv), kb = __fmul_rn(m, inv);
+    uint32_t w[2] = {0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int i = g * kGroup + part * 8 + j;
+        const int q = live ? __float2int_rn(__fmaf_rn((float) code_at<NB>(t, r, i), ka, kb)) : 0;
+        w[j >> 2] |= ((uint32_t) (q & 0xff)) << (8 * (j & 3));
+    }
+    const int k = (lane >> 2) * kGroup + part * 8;
+    *reinterpret_cast<uint2 *>(wblk + ((size_t) (r >> 7) * nsb + sb) * kTcABytes + tc_off(128, r & 127, k)) =
+        make_uint2(w[0], w[1]);
+}
+
+__global__ void __launch_bounds__(256) k_quant_sb(const float * x, const int32_t * perm, int T, int cols, int nsb,
+                                                  int T_pad, int N, uint8_t * xblk, float * xs) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const long item = (long) blockIdx.x * 8 + warp;
+    if (item >= (long) T_pad * nsb) return;
+    const int tok = (int) (item / nsb), sb = (int) (item % nsb);
+    const int k0 = lane * 8;
+    float v[8];
+    float amax = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int i = sb * 256 + k0 + j;
+        v[j] = tok < T && i < cols ? x[(size_t) tok * cols + perm[i]] : 0.0f;
+        amax = fmaxf(amax, fabsf(v[j]));
+    }
+    amax = warp_max(amax);
+    const float sc = __fdiv_rn(amax, 127.0f);
+    const float is = sc > 0.0f ? __fdiv_rn(1.0f, sc) : 0.0f;
+    uint32_t w[2] = {0u, 0u};
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        int q = __float2int_rn(__fmul_rn(v[j], is));
+        q = q > 127 ? 127 : q < -127 ? -127 : q;
+        w[j >> 2] |= ((uint32_t) (q & 0xff)) << (8 * (j & 3));
+    }
+    *reinterpret_cast<uint2 *>(xblk + ((size_t) (tok / N) * nsb + sb) * (size_t) (N * 256) + tc_off(N, tok % N, k0)) =
+        make_uint2(w[0], w[1]);
+    if (lane == 0) xs[(size_t) sb * T_pad + tok] = sc;
+}
+
+// A wait that gives up at once when another role of the CTA already has.
+SB_DEV bool tc_wait(uint64_t * bar, uint32_t parity, int * err, int code, volatile int * fail) {
+    if (*fail) return false;
+    if (mbar_wait(bar, parity, err, code)) return true;
+    *fail = 1;
+    return false;
+}
+
+template <int N>
+__global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArgs g) {
+    extern __shared__ __align__(1024) uint8_t tsm[];
+    __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], accf[2], acce[2];
+    __shared__ uint32_t tslot;
+    __shared__ volatile int fail;
+    constexpr uint32_t BB = N * 256, SB = kTcABytes + BB;
+    constexpr uint32_t ncols = tc_cols(2 * N);
+    constexpr uint32_t idesc = tc_idesc_s8(128, N);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int mb = blockIdx.x, tb = blockIdx.y;
+    if (warp == 1) tmem_alloc(&tslot, ncols);
+    if (tid == 0) {
+        for (int s = 0; s < kTcStages; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
+        for (int b = 0; b < 2; b++) { mbar_init(&accf[b], 1); mbar_init(&acce[b], 4); }
+        fail = 0;
+        mbar_fence_init();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tslot;
+    if (warp == 1) tmem_relinquish();
+
+    if (warp == 0) {
+        // ---------------- producer: both operand blocks of every superblock
+        if (lane == 0) {
+            for (int sb = 0; sb < g.nsb; sb++) {
+                const int s = sb % kTcStages, lap = sb / kTcStages;
+                if (lap > 0 && !tc_wait(&empty[s], (lap - 1) & 1, g.err, 40, &fail)) break;
+                mbar_expect_tx(&full[s], SB);
+                bulk_g2s(tsm + (size_t) s * SB, g.wblk + ((size_t) mb * g.nsb + sb) * kTcABytes, kTcABytes, &full[s]);
+                bulk_g2s(tsm + (size_t) s * SB + kTcABytes, g.xblk + ((size_t) tb * g.nsb + sb) * BB, BB, &full[s]);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer: 8 x K=32 per superblock into accumulator sb % 2
+        if (lane == 0) {
+            for (int sb = 0; sb < g.nsb; sb++) {
+                const int s = sb % kTcStages, buf = sb & 1;
+                if (!tc_wait(&full[s], (sb / kTcStages) & 1, g.err, 41, &fail)) break;
+                if (sb >= 2 && !tc_wait(&acce[buf], ((sb >> 1) - 1) & 1, g.err, 42, &fail)) break;
+                tc_fence_after();
+                const uint8_t * As = tsm + (size_t) s * SB, * Bs = As + kTcABytes;
+#pragma unroll
+                for (int j = 0; j < 8; j++)
+                    tc_mma_s8(tmem + (uint32_t) (buf * N), tc_desc(As + tc_off(128, 0, 32 * j), 16 * 128, 128),
+                              tc_desc(Bs + tc_off(N, 0, 32 * j), (N / 8) * 128, 128), idesc, j > 0);
+                tc_commit(&empty[s]);     // the stage may be refilled once these MMAs are done
+                tc_commit(&accf[buf]);    // and the accumulator read
+            }
+        }
+    } else {
+        // ---------------- epilogue: TMEM lanes (rows) 32 q .. 32 q + 31
+        const int q = warp & 3, row = 32 * q + lane, r = mb * 128 + row;
+        float acc[N];
+#pragma unroll
+        for (int t = 0; t < N; t++) acc[t] = 0.0f;
+        bool ok = true;
+        for (int sb = 0; sb < g.nsb; sb++) {
+            const int buf = sb & 1;
+            const float s8v = g.s8[(size_t) sb * g.rows_pad + r];
+            const float * xsp = g.xs + (size_t) sb * g.T_pad + (size_t) tb * N;
+            ok = ok && tc_wait(&accf[buf], (sb >> 1) & 1, g.err, 43, &fail);
+            tc_fence_after();
+            uint32_t d[N];
+#pragma unroll
+            for (int c = 0; c < N; c += 8) {
+                uint32_t r8[8];
+                tmem_ld8(tmem + ((uint32_t) (32 * q) << 16) + (uint32_t) (buf * N + c), r8);
+#pragma unroll
+                for (int k = 0; k < 8; k++) d[c + k] = r8[k];
+            }
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acce[buf]);
+#pragma unroll
+            for (int t = 0; t < N; t++)
+                acc[t] = __fmaf_rn(__fmul_rn(s8v, __ldg(xsp + t)), (float) (int) d[t], acc[t]);
+        }
+        if (ok && r < g.rows)
+#pragma unroll
+            for (int t = 0; t < N; t++) {
+                const int tok = tb * N + t;
+                if (tok < g.T) g.y[(size_t) tok * g.rows + r] = acc[t];
+            }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem, ncols);
+    }
+}
+
+template <int NB, int SIX>
+static void launch_requant(const QT & t, uint8_t * wblk, float * s8, int rows_pad, int nsb, cudaStream_t st,
+                           cudaError_t * r) {
+    const long items = (long) rows_pad * nsb;
+    k_requant8<NB, SIX><<<(unsigned) ((items + 7) / 8), 256, 0, st>>>(t, wblk, s8, rows_pad, nsb);
+    *r = cudaGetLastError();
+}
+
+cudaError_t tc_requant(const QT & t, const TcPlan & p, cudaStream_t st) {
+    cudaError_t r = cudaErrorInvalidValue;
+    SB_DISPATCH_QT(t.nbits, t.six, launch_requant, t, p.wblk, p.s8, p.rows_pad, p.nsb, st, &r);
+    return r;
+}
+
+int tc_tile_n(int T) { return T <= 16 ? 16 : T <= 32 ? 32 : 64; }
+
+template <int N>
+static cudaError_t launch_gemm(const TcArgs & a, cudaStream_t st) {
+    constexpr int smem = kTcStages * (int) (kTcABytes + N * 256);
+    static bool attr = false;
+    if (!attr) {
+        const cudaError_t e = cudaFuncSetAttribute(k_tcgemm<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    k_tcgemm<N><<<dim3(a.rows_pad / 128, a.T_pad / N), 192, smem, st>>>(a);
+    return cudaGetLastError();
+}
+
+cudaError_t tc_gemm(const QT & t, const TcPlan & p, const float * x, int T, uint8_t * xblk, float * xs, float * y,
+                    int * err, cudaStream_t st) {
+    const int N = tc_tile_n(T), T_pad = (T + N - 1) / N * N;
+    const long items = (long) T_pad * p.nsb;
+    k_quant_sb<<<(unsigned) ((items + 7) / 8), 256, 0, st>>>(x, t.perm, T, t.cols, p.nsb, T_pad, N, xblk, xs);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    TcArgs a;
+    a.wblk = p.wblk; a.s8 = p.s8; a.xblk = xblk; a.xs = xs; a.y = y;
+    a.rows = t.rows; a.rows_pad = p.rows_pad; a.nsb = p.nsb; a.T = T; a.T_pad = T_pad; a.err = err;
+    return N == 16 ? launch_gemm<16>(a, st) : N == 32 ? launch_gemm<32>(a, st) : launch_gemm<64>(a, st);
+}
+
+}  // namespace sb

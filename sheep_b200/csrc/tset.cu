@@ -2,6 +2,7 @@
 // name, for kernel-level entry points (GEMV microbench, parity tests, MoE
 // layer). The decode engine holds its own copy in its own arena.
 #include "moe_host.h"
+#include "tc_batch.h"
 #include "tgemv.cuh"
 #include "sheep_b200.h"
 #include "upload.h"
@@ -32,6 +33,11 @@ struct sb_tset {
     int * err = nullptr;
     // batch plan: identity slots, chunks of 8 vectors of the one "expert"
     int * slots = nullptr, * ch_e = nullptr, * ch_s0 = nullptr, * ch_n = nullptr, * meta = nullptr;
+    // tensor-core batched path: per-tensor int8 re-quantization, made on first use
+    std::unordered_map<std::string, TcPlan> tc;
+    uint8_t * tc_x = nullptr;
+    float * tc_xs = nullptr;
+    size_t tc_x_cap = 0, tc_xs_cap = 0;
     int nsm = 148;
 };
 
@@ -87,6 +93,9 @@ extern "C" sb_tset * sb_tset_open(const char * path, char * why, int nwhy) {
 extern "C" void sb_tset_close(sb_tset * t) {
     if (!t) return;
     cudaDeviceSynchronize();
+    for (auto & kv : t->tc) { cudaFree(kv.second.wblk); cudaFree(kv.second.s8); }
+    cudaFree(t->tc_x);
+    cudaFree(t->tc_xs);
     t->ar.release();
     ssf_close(&t->f);
     delete t;
@@ -321,4 +330,138 @@ extern "C" int sb_quantize_act(const float * x, const int32_t * perm, int n, int
     const int ng = n / SSF_GROUP;
     k_quant_act<<<(ng + 7) / 8, 256, 0, (cudaStream_t) stream>>>(x, perm, n, q, s, sums);
     return cudaGetLastError() == cudaSuccess;
+}
+
+// ------------------------------------------------------------------ tensor-core batched path
+
+// The tensor's re-quantized form (made and kept on first use).
+static const TcPlan * tc_plan(sb_tset * t, const char * name, const QT ** qo) {
+    const QT * q = find_qt(t, name);
+    if (!q) return nullptr;
+    *qo = q;
+    auto it = t->tc.find(name);
+    if (it != t->tc.end()) return &it->second;
+    TcPlan p;
+    p.nsb = (q->cols / SSF_GROUP + 7) / 8;
+    p.rows_pad = (q->rows + 127) / 128 * 128;
+    if (cudaMalloc(&p.wblk, (size_t) p.rows_pad * p.nsb * 256) != cudaSuccess) return nullptr;
+    if (cudaMalloc(&p.s8, (size_t) p.nsb * p.rows_pad * 4) != cudaSuccess) { cudaFree(p.wblk); return nullptr; }
+    if (tc_requant(*q, p, nullptr) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+        cudaFree(p.wblk);
+        cudaFree(p.s8);
+        return nullptr;
+    }
+    return &t->tc.emplace(name, p).first->second;
+}
+
+// Scratch for the activations of T rows (grown as needed; frees synchronize).
+static bool tc_scratch(sb_tset * t, int nsb, int T) {
+    const int N = tc_tile_n(T), T_pad = (T + N - 1) / N * N;
+    const size_t xb = (size_t) T_pad * nsb * 256, sb = (size_t) T_pad * nsb * 4;
+    if (xb > t->tc_x_cap) {
+        cudaFree(t->tc_x);
+        t->tc_x = nullptr;
+        t->tc_x_cap = 0;
+        if (cudaMalloc(&t->tc_x, xb) != cudaSuccess) return false;
+        t->tc_x_cap = xb;
+    }
+    if (sb > t->tc_xs_cap) {
+        cudaFree(t->tc_xs);
+        t->tc_xs = nullptr;
+        t->tc_xs_cap = 0;
+        if (cudaMalloc(&t->tc_xs, sb) != cudaSuccess) return false;
+        t->tc_xs_cap = sb;
+    }
+    return true;
+}
+
+extern "C" int sb_tset_gemm_tc(sb_tset * t, const char * name, const float * x, int nb, float * y, void * stream) {
+    const QT * q = nullptr;
+    if (!t || nb < 1 || nb > kMaxBatch) return 0;
+    const TcPlan * p = tc_plan(t, name, &q);
+    if (!p || !tc_scratch(t, p->nsb, nb)) return 0;
+    return tc_gemm(*q, *p, x, nb, t->tc_x, t->tc_xs, y, t->err, (cudaStream_t) stream) == cudaSuccess;
+}
+
+extern "C" int sb_tset_gemm_tc_host(sb_tset * t, const char * name, const float * x, int nb, float * y) {
+    const QT * q = find_qt(t, name);
+    if (!q || nb < 1 || nb > kMaxBatch) return 0;
+    float * dx = nullptr, * dy = nullptr;
+    bool ok = cudaMalloc(&dx, (size_t) nb * q->cols * 4) == cudaSuccess &&
+              cudaMalloc(&dy, (size_t) nb * q->rows * 4) == cudaSuccess;
+    int err = 0;
+    if (ok) {
+        cudaMemcpy(dx, x, (size_t) nb * q->cols * 4, cudaMemcpyHostToDevice);
+        ok = sb_tset_gemm_tc(t, name, dx, nb, dy, nullptr) && cudaDeviceSynchronize() == cudaSuccess;
+        cudaMemcpy(&err, t->err, 4, cudaMemcpyDeviceToHost);
+        ok = ok && err == 0;
+        if (ok) cudaMemcpy(y, dy, (size_t) nb * q->rows * 4, cudaMemcpyDeviceToHost);
+    }
+    cudaFree(dx);
+    cudaFree(dy);
+    return ok ? 1 : 0;
+}
+
+// Mean device time of sb_tset_gemm_tc (activation quantization + product; the
+// weights' re-quantization, made once, is not timed) over nb host rows copied
+// once, a buffer larger than L2 rewritten before each run.
+extern "C" int sb_tset_time_gemm_tc(sb_tset * t, const char * name, const float * x, int nb, int reps, float * ms_avg) {
+    const QT * q = find_qt(t, name);
+    if (!q || nb < 1 || nb > kMaxBatch || reps < 1) return 0;
+    float * dx = nullptr, * dy = nullptr;
+    void * flush = nullptr;
+    const size_t flush_n = (size_t) 512 << 20;
+    cudaStream_t st = nullptr;
+    bool ok = cudaMalloc(&dx, (size_t) nb * q->cols * 4) == cudaSuccess &&
+              cudaMalloc(&dy, (size_t) nb * q->rows * 4) == cudaSuccess &&
+              cudaMalloc(&flush, flush_n) == cudaSuccess && cudaStreamCreate(&st) == cudaSuccess;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    double total = 0.0;
+    if (ok) {
+        cudaEventCreate(&e0);
+        cudaEventCreate(&e1);
+        cudaMemcpy(dx, x, (size_t) nb * q->cols * 4, cudaMemcpyHostToDevice);
+        for (int r = 0; ok && r < 3; r++) ok = sb_tset_gemm_tc(t, name, dx, nb, dy, st);
+        for (int r = 0; ok && r < reps; r++) {
+            cudaMemsetAsync(flush, r & 0xff, flush_n, st);
+            cudaEventRecord(e0, st);
+            ok = sb_tset_gemm_tc(t, name, dx, nb, dy, st);
+            cudaEventRecord(e1, st);
+            ok = ok && cudaEventSynchronize(e1) == cudaSuccess;
+            float ms = 0.0f;
+            cudaEventElapsedTime(&ms, e0, e1);
+            total += ms;
+        }
+        int err = 0;
+        cudaMemcpy(&err, t->err, 4, cudaMemcpyDeviceToHost);
+        ok = ok && err == 0;
+    }
+    if (e0) cudaEventDestroy(e0);
+    if (e1) cudaEventDestroy(e1);
+    if (st) cudaStreamDestroy(st);
+    cudaFree(dx);
+    cudaFree(dy);
+    cudaFree(flush);
+    if (ms_avg) *ms_avg = (float) (total / reps);
+    return ok ? 1 : 0;
+}
+
+// The re-quantized weights in natural layout (host): w8 rows x (nsb * 256), s8 rows x nsb.
+extern "C" int sb_tset_requant8_host(sb_tset * t, const char * name, int8_t * w8, float * s8) {
+    const QT * q = nullptr;
+    const TcPlan * p = tc_plan(t, name, &q);
+    if (!p) return 0;
+    const int nsb = p->nsb, K = nsb * 256;
+    std::vector<uint8_t> blk((size_t) p->rows_pad * nsb * 256);
+    std::vector<float> sc((size_t) nsb * p->rows_pad);
+    if (cudaMemcpy(blk.data(), p->wblk, blk.size(), cudaMemcpyDeviceToHost) != cudaSuccess ||
+        cudaMemcpy(sc.data(), p->s8, sc.size() * 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return 0;
+    for (int r = 0; r < q->rows; r++)
+        for (int sb = 0; sb < nsb; sb++) {
+            s8[(size_t) r * nsb + sb] = sc[(size_t) sb * p->rows_pad + r];
+            const uint8_t * b = blk.data() + ((size_t) (r >> 7) * nsb + sb) * 32768;
+            for (int k = 0; k < 256; k++) w8[(size_t) r * K + sb * 256 + k] = (int8_t) b[tc_off(128, r & 127, k)];
+        }
+    return 1;
 }

@@ -125,6 +125,19 @@ class Oracle:
             assert k > 0, "layer has no router"
         return y, sel[:, :k], w[:, :k]
 
+    def requant8(self, name, rows, cols):
+        nsb = (cols // 32 + 7) // 8
+        w8 = np.zeros((rows, nsb * 256), np.int8)
+        s8 = np.zeros((rows, nsb), np.float32)
+        assert self.lib().so_requant8(self.m, name.encode(), _p(w8), _p(s8))
+        return w8, s8
+
+    def gemm_sb(self, name, X, rows):
+        X = np.ascontiguousarray(np.atleast_2d(X), np.float32)
+        Y = np.zeros((len(X), rows), np.float32)
+        assert self.lib().so_gemm_sb(self.m, name.encode(), _p(X), len(X), _p(Y))
+        return Y
+
     def close(self):
         if self.m:
             self.lib().so_close(self.m)
