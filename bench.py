@@ -282,7 +282,8 @@ def main():
     if rank == 0 and world == 1:
         peak0, _ = peaks()
         extras = {"l2": "a 512 MB buffer rewritten before each timed run (decode: weights > L2)",
-                  "gemv_cfg1": gemv_microbench(peak0), "moe_cfg2": moe_microbench(peak0),
+                  "gemv_cfg1": gemv_microbench(peak0), "gemm_tc_cfg1": gemm_tc_microbench(peak0),
+                  "moe_cfg2": moe_microbench(peak0),
                   "decode_cfg3": decode_cfg3(peak0)}
 
     if rank == 0:
@@ -360,6 +361,29 @@ def decode_cfg3(peak, ngen=64):
                 "gbs": round(gbs, 1), "frac": round(gbs / peak, 4), "tokens": ngen}
     finally:
         eng.close()
+
+
+def gemm_tc_microbench(peak, reps=20):
+    """Configuration 1's matrices at 16/64/256 rows of x on the tensor cores
+    (the batched path's int8 arithmetic): TOPS of the int8 products and GB/s
+    of the re-quantized int8 weights read."""
+    import sheep_b200
+    from sheep_b200 import configs
+    out = []
+    for cfg, quant in (("gemv-4096-q4", "Q4"), ("gemv-4096-q8", "Q8")):
+        ts = sheep_b200.TensorSet(model_path(configs.CONFIGS[cfg], 0, None))
+        try:
+            for name in ("blk.0.attn_q.weight", "blk.0.ffn_gate.weight", "blk.0.ffn_down.weight"):
+                rows, cols, _ = ts.shape(name)
+                for B in (16, 64, 256):
+                    ms = ts.time_gemm_tc(name, fp16_rows(B, B, cols), reps)
+                    w8 = rows * ((cols // 32 + 7) // 8) * 256
+                    out.append({"quant": quant, "shape": f"{rows}x{cols}", "batch": B, "us": round(ms * 1000.0, 2),
+                                "int8_tops": round(2.0 * rows * cols * B / (ms / 1000.0) / 1e12, 1),
+                                "int8_weight_gbs": round(w8 / (ms / 1000.0) / 1e9, 1)})
+        finally:
+            ts.close()
+    return out
 
 
 def moe_microbench(peak, reps=20):
