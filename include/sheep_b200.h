@@ -79,9 +79,13 @@ int sb_tset_time_gemv(sb_tset * t, const char * name, const float * x, int nb, i
 // 2025-2031): the weights re-quantized once to int8 with one scale per row per
 // 256 (kept on the device), x quantized per 256, int32 superblock dots from
 // tcgen05, one float epilogue per superblock. Device pointers, nb <= 4096.
-int sb_tset_gemm_tc(sb_tset * t, const char * name, const float * x, int nb, float * y, void * stream);
-int sb_tset_gemm_tc_host(sb_tset * t, const char * name, const float * x, int nb, float * y);
-int sb_tset_time_gemm_tc(sb_tset * t, const char * name, const float * x, int nb, int reps, float * ms_avg);
+// split > 1 cuts the superblocks into that many equal runs whose sums are added
+// in run order (the reference's split-K, sml_g_tcm3 + sml_g_splitk_sum,
+// sml/sml-gpu-fast.cu:1907-2065); split must leave no run empty
+// (ceil(nsb / ceil(nsb / split)) == split), else the call fails.
+int sb_tset_gemm_tc(sb_tset * t, const char * name, const float * x, int nb, int split, float * y, void * stream);
+int sb_tset_gemm_tc_host(sb_tset * t, const char * name, const float * x, int nb, int split, float * y);
+int sb_tset_time_gemm_tc(sb_tset * t, const char * name, const float * x, int nb, int split, int reps, float * ms_avg);
 // The re-quantized weights, host buffers: w8 rows x (nsb*256), s8 rows x nsb (nsb = ceil(cols/256)).
 int sb_tset_requant8_host(sb_tset * t, const char * name, int8_t * w8, float * s8);
 // Host-buffer form of one GEMV; q/s/sums (host, may be NULL) receive the int8
@@ -169,6 +173,39 @@ const char * sb_moe_last_error(void);
 // batched path (the reference's int8 tiles, sml_g_tcm9, sml/sml-gpu-fast.cu:3149).
 int sb_tc_imma(const int8_t * A, const int8_t * B, int32_t * C, int M, int N, int K, int * err, void * stream);
 const char * sb_tc_last_error(void);
+
+// ------------------------------------------------------------------ batched serving
+// n_seq conversations decoding together, one token each per step and one read
+// of the weights per step: the GPU form of sml_forward_multi
+// (sml/sml-run.c:2559-2604), driven like sml-batched (sml/sml-batched.c:43-146).
+// Every product runs on the tensor cores with the batched arithmetic of
+// sb_tset_gemm_tc; attention, norms, RoPE and the greedy choice are each
+// sequence's own, over its own fp16 KV cache of n_ctx positions. Dense
+// decoders only (an MoE file is refused with the reason in `why`).
+typedef struct sb_batch sb_batch;
+sb_batch * sb_batch_open(const char * path, int n_seq, int n_ctx, char * why, int nwhy);
+void sb_batch_close(sb_batch * b);
+// out (int[16]): [0] n_seq [1] n_ctx [2] n_vocab [3..7] superblock slices of
+// the q|k|v, o, gate|up, down and head products [8,9] the file's weight bytes
+// per step (lo, hi 32 bits) [10,11] the int8 weight bytes per step [12] kernel
+// launches per step [13] tokens per tensor-core tile.
+void sb_batch_info(const sb_batch * b, int * out);
+// One token per slot: tokens[s] at absolute position pos[s] (pos[s] < 0 idles
+// slot s: its logits are not meaningful). Host arrays of n_seq. Returns a host
+// pointer to [n_seq][n_vocab] logits owned by the library, NULL on failure
+// (positions >= n_ctx or ids out of range included). Replaces the reference's
+// sml_forward_multi(cs, tokens, pos, ns, depth, logits_out).
+const float * sb_forward_multi(sb_batch * b, const int * tokens, const int * pos);
+// Greedy generation on the device: prompts [n_seq][np] stepped from position
+// 0, then nwarm + ngen tokens per slot, each chosen on the GPU and fed back by
+// graph replay; ids [n_seq][nwarm + ngen]. ms (if not NULL) receives the device
+// time of the last ngen - 1 steps. np + nwarm + ngen - 1 <= n_ctx.
+int sb_batch_generate(sb_batch * b, const int * prompts, int np, int nwarm, int ngen, int * ids, float * ms);
+const float * sb_batch_device_logits(const sb_batch * b);
+// The cached key and value rows of `slot` at `pos` in `layer`: n_kv * head_dim
+// fp16 each (head-major), host buffers.
+int sb_batch_kv(const sb_batch * b, int layer, int slot, int pos, uint16_t * k, uint16_t * v);
+const char * sb_batch_last_error(void);
 
 // ------------------------------------------------------------------ models
 // Seeded synthetic SSF writer (the inputs every test and bench runs on; the

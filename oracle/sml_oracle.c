@@ -328,49 +328,65 @@ int so_requant8(so_model * m, const char * name, int8_t * w8, float * s8) {
     return 1;
 }
 
-// The batched product (sml_g_tcm3/tcm9 epilogue, sml/sml-gpu-fast.cu:2025-2031):
-// each row of X gathered through the tensor's column order and quantized per 256
-// (one scale per superblock, sml_quantize_act_sb, sml/sml-kernel.c:164-189),
-// then y[t][row] = sum over superblocks, in order, of
-// fma(s8 * xs, dot(w8, xq), acc). X: T x cols, Y: T x rows.
-int so_gemm_sb(so_model * m, const char * name, const float * X, int T, float * Y) {
-    const rec_t * r = find(m, name);
-    if (!r || r->kind != 1 || r->layout != 1 || T < 1) return 0;
-    const int n = (int) r->cols, ng = n / G, nsb = (ng + 7) / 8, K = nsb * 256, rows = (int) r->rows;
-    int8_t * w8 = (int8_t *) malloc((size_t) rows * K);
-    float * s8 = (float *) malloc((size_t) rows * nsb * 4);
-    so_requant8(m, name, w8, s8);
-    const int32_t * perm = (const int32_t *) (m->base + r->perm_off);
-    int8_t * q = (int8_t *) malloc((size_t) K);
+// The batched product for one activation row (sml_g_tcm3/tcm9 epilogue,
+// sml/sml-gpu-fast.cu:2025-2031): the row gathered through the tensor's column
+// order and quantized per 256 (one scale per superblock, sml_quantize_act_sb,
+// sml/sml-kernel.c:164-189), then y[row] = sum over superblocks, in order, of
+// fma(s8 * xs, dot(w8, xq), acc). With split > 1 (sml_g_tcm3 +
+// sml_g_splitk_sum, sml/sml-gpu-fast.cu:1919-1921, 2057-2065) the superblocks
+// are cut into runs of ceil(nsb / split), each run accumulated from zero as
+// above, and y = ((0 + run 0) + run 1) + ...
+static void sb_row(const int8_t * w8, const float * s8, const int32_t * perm, int n, int rows, const float * x,
+                   int split, float * y) {
+    const int ng = n / G, nsb = (ng + 7) / 8, K = nsb * 256, per = (nsb + split - 1) / split;
+    int8_t * q = (int8_t *) calloc((size_t) K, 1);
     float * xs = (float *) malloc((size_t) nsb * 4), * xg = (float *) malloc((size_t) n * 4);
-    for (int t = 0; t < T; t++) {
-        for (int i = 0; i < n; i++) xg[i] = X[(size_t) t * n + perm[i]];
-        memset(q, 0, (size_t) K);
-        for (int sb = 0; sb < nsb; sb++) {
-            const int i0 = sb * 256, i1 = (sb * 8 + 8 < ng ? sb * 8 + 8 : ng) * G;
-            float amax = 0.0f;
-            for (int i = i0; i < i1; i++) { const float v = fabsf(xg[i]); if (v > amax) amax = v; }
-            const float sc = amax / 127.0f, is = sc > 0.0f ? 1.0f / sc : 0.0f;
-            xs[sb] = sc;
-            for (int i = i0; i < i1; i++) {
-                int v = (int) lrintf(xg[i] * is);
-                q[i] = (int8_t) (v > 127 ? 127 : v < -127 ? -127 : v);
-            }
+    for (int i = 0; i < n; i++) xg[i] = x[perm[i]];
+    for (int sb = 0; sb < nsb; sb++) {
+        const int i0 = sb * 256, i1 = (sb * 8 + 8 < ng ? sb * 8 + 8 : ng) * G;
+        float amax = 0.0f;
+        for (int i = i0; i < i1; i++) { const float v = fabsf(xg[i]); if (v > amax) amax = v; }
+        const float sc = amax / 127.0f, is = sc > 0.0f ? 1.0f / sc : 0.0f;
+        xs[sb] = sc;
+        for (int i = i0; i < i1; i++) {
+            int v = (int) lrintf(xg[i] * is);
+            q[i] = (int8_t) (v > 127 ? 127 : v < -127 ? -127 : v);
         }
+    }
 #pragma omp parallel for schedule(static)
-        for (int row = 0; row < rows; row++) {
-            const int8_t * wr = w8 + (size_t) row * K;
+    for (int row = 0; row < rows; row++) {
+        const int8_t * wr = w8 + (size_t) row * K;
+        float yv = 0.0f;
+        for (int s0 = 0; s0 < nsb; s0 += per) {
             float acc = 0.0f;
-            for (int sb = 0; sb < nsb; sb++) {
+            for (int sb = s0; sb < s0 + per && sb < nsb; sb++) {
                 int32_t d = 0;
                 for (int i = sb * 256; i < sb * 256 + 256; i++) d += (int32_t) wr[i] * (int32_t) q[i];
                 acc = fmaf(s8[(size_t) row * nsb + sb] * xs[sb], (float) d, acc);
             }
-            Y[(size_t) t * rows + row] = acc;
+            yv = per >= nsb ? acc : yv + acc;
         }
+        y[row] = yv;
     }
-    free(w8); free(s8); free(q); free(xs); free(xg);
+    free(q); free(xs); free(xg);
+}
+
+// The batched product over T rows of X (T x cols) into Y (T x rows).
+int so_gemm_sb_split(so_model * m, const char * name, const float * X, int T, int split, float * Y) {
+    const rec_t * r = find(m, name);
+    if (!r || r->kind != 1 || r->layout != 1 || T < 1 || split < 1) return 0;
+    const int n = (int) r->cols, nsb = (n / G + 7) / 8, rows = (int) r->rows;
+    int8_t * w8 = (int8_t *) malloc((size_t) rows * nsb * 256);
+    float * s8 = (float *) malloc((size_t) rows * nsb * 4);
+    so_requant8(m, name, w8, s8);
+    const int32_t * perm = (const int32_t *) (m->base + r->perm_off);
+    for (int t = 0; t < T; t++) sb_row(w8, s8, perm, n, rows, X + (size_t) t * n, split, Y + (size_t) t * rows);
+    free(w8); free(s8);
     return 1;
+}
+
+int so_gemm_sb(so_model * m, const char * name, const float * X, int T, float * Y) {
+    return so_gemm_sb_split(m, name, X, T, 1, Y);
 }
 
 static void matvec_f32(const float * w, int rows, int n, const float * x, float * y) {
@@ -417,12 +433,13 @@ static void qk_norm(float * v, const float * w, int nh, int hd, float eps) {
 }
 
 // sml/sml-run.c:180-266 (scores, max-subtracted softmax with expf, weighted V)
-static void attn_head(const so_model * m, int L, int h, int pos, const float * q, float * out, float * sc) {
+static void attn_head(const so_model * m, const uint16_t * kc, const uint16_t * vc, int L, int h, int pos,
+                      const float * q, float * out, float * sc) {
     const int hd = m->hd, kvd = (int) m->n_kv * hd, rep = (int) (m->n_head / m->n_kv);
     const size_t base = (size_t) L * m->n_ctx * kvd + (size_t) (h / rep) * hd;
     const float inv = 1.0f / sqrtf((float) hd);
     for (int t = 0; t <= pos; t++) {
-        const uint16_t * k = m->kc + base + (size_t) t * kvd;
+        const uint16_t * k = kc + base + (size_t) t * kvd;
         float s = 0.0f;
         for (int i = 0; i < hd; i++) s += q[i] * f16(k[i]);
         sc[t] = s * inv;
@@ -435,7 +452,7 @@ static void attn_head(const so_model * m, int L, int h, int pos, const float * q
     for (int t = 0; t <= pos; t++) sc[t] *= is;
     for (int i = 0; i < hd; i++) out[i] = 0.0f;
     for (int t = 0; t <= pos; t++) {
-        const uint16_t * v = m->vc + base + (size_t) t * kvd;
+        const uint16_t * v = vc + base + (size_t) t * kvd;
         for (int i = 0; i < hd; i++) out[i] += sc[t] * f16(v[i]);
     }
 }
@@ -512,8 +529,17 @@ int so_moe_ffn(so_model * m, int L, const float * xb, float * out, int * sel, fl
 
 static void add_bias(float * y, const float * b, int n) { if (b) for (int i = 0; i < n; i++) y[i] += b[i]; }
 
-// sml/sml-run.c:3243-3523, the dense / MoE decoder branch
-int so_forward(so_model * m, int tok, int pos, float * logits) {
+// The products of one step, by kind: 0 q/k/v, 1 o, 2 gate/up, 3 down, 4 head.
+typedef void (*lin_fn)(void * ctx, so_model * m, const rec_t * r, int kind, const float * x, float * y);
+
+static void lin_decode(void * ctx, so_model * m, const rec_t * r, int kind, const float * x, float * y) {
+    (void) ctx; (void) kind;
+    matvec_rec(m, r, x, y, 0, (int) r->rows);
+}
+
+// sml/sml-run.c:3243-3523, the dense / MoE decoder branch, over the caches kc/vc
+static int forward_core(so_model * m, uint16_t * kc, uint16_t * vc, int tok, int pos, float * logits, lin_fn lin,
+                        void * lctx) {
     if (pos >= m->n_ctx || tok < 0 || tok >= (int) m->n_vocab) return 0;
     const int E = (int) m->n_embd, hd = m->hd, nh = (int) m->n_head, nkv = (int) m->n_kv;
     const int qd = nh * hd, kvd = nkv * hd;
@@ -531,9 +557,9 @@ int so_forward(so_model * m, int tok, int pos, float * logits) {
     for (int i = 0; i < E; i++) x[pe[i]] = xb[i];
     for (int L = 0; L < (int) m->n_layer; L++) {
         rms_norm(xb, x, f32p(m, findf(m, "blk.%d.attn_norm.weight", L, 0)), E, m->eps);
-        matvec_rec(m, findf(m, "blk.%d.attn_q.weight", L, 0), xb, q, 0, qd);
-        matvec_rec(m, findf(m, "blk.%d.attn_k.weight", L, 0), xb, k, 0, kvd);
-        matvec_rec(m, findf(m, "blk.%d.attn_v.weight", L, 0), xb, v, 0, kvd);
+        lin(lctx, m, findf(m, "blk.%d.attn_q.weight", L, 0), 0, xb, q);
+        lin(lctx, m, findf(m, "blk.%d.attn_k.weight", L, 0), 0, xb, k);
+        lin(lctx, m, findf(m, "blk.%d.attn_v.weight", L, 0), 0, xb, v);
         add_bias(q, f32p(m, findf(m, "blk.%d.attn_q.bias", L, 0)), qd);
         add_bias(k, f32p(m, findf(m, "blk.%d.attn_k.bias", L, 0)), kvd);
         add_bias(v, f32p(m, findf(m, "blk.%d.attn_v.bias", L, 0)), kvd);
@@ -544,9 +570,9 @@ int so_forward(so_model * m, int tok, int pos, float * logits) {
         rope(m, q, nh, pos);
         rope(m, k, nkv, pos);
         const size_t at = ((size_t) L * m->n_ctx + pos) * kvd;   // :3414-3415
-        for (int i = 0; i < kvd; i++) { m->kc[at + i] = to_f16(k[i]); m->vc[at + i] = to_f16(v[i]); }
-        for (int h = 0; h < nh; h++) attn_head(m, L, h, pos, q + (size_t) h * hd, att + (size_t) h * hd, sc);
-        matvec_rec(m, findf(m, "blk.%d.attn_output.weight", L, 0), att, hb2, 0, E);
+        for (int i = 0; i < kvd; i++) { kc[at + i] = to_f16(k[i]); vc[at + i] = to_f16(v[i]); }
+        for (int h = 0; h < nh; h++) attn_head(m, kc, vc, L, h, pos, q + (size_t) h * hd, att + (size_t) h * hd, sc);
+        lin(lctx, m, findf(m, "blk.%d.attn_output.weight", L, 0), 1, att, hb2);
         for (int i = 0; i < E; i++) x[i] += hb2[i];
         rms_norm(xb, x, f32p(m, findf(m, "blk.%d.ffn_norm.weight", L, 0)), E, m->eps);
         if (findf(m, "blk.%d.ffn_gate_inp.weight", L, 0)) {
@@ -555,19 +581,23 @@ int so_forward(so_model * m, int tok, int pos, float * logits) {
             continue;
         }
         const int F = (int) m->n_ff;
-        matvec_rec(m, findf(m, "blk.%d.ffn_gate.weight", L, 0), xb, hb, 0, F);
-        matvec_rec(m, findf(m, "blk.%d.ffn_up.weight", L, 0), xb, hb2, 0, F);
+        lin(lctx, m, findf(m, "blk.%d.ffn_gate.weight", L, 0), 2, xb, hb);
+        lin(lctx, m, findf(m, "blk.%d.ffn_up.weight", L, 0), 2, xb, hb2);
         silu_mul(hb, hb2, F);
-        matvec_rec(m, findf(m, "blk.%d.ffn_down.weight", L, 0), hb, xb, 0, E);
+        lin(lctx, m, findf(m, "blk.%d.ffn_down.weight", L, 0), 3, hb, xb);
         for (int i = 0; i < E; i++) x[i] += xb[i];
     }
     rms_norm(xb, x, f32p(m, find(m, "output_norm.weight")), E, m->eps);
     const rec_t * head = find(m, "output.weight");
-    matvec_rec(m, head ? head : emb, xb, logits, 0, (int) m->n_vocab);
+    lin(lctx, m, head ? head : emb, 4, xb, logits);
     free(x); free(xb); free(q); free(k); free(v); free(att); free(hb); free(hb2); free(sc);
     int best = 0;                                                  // sml/sml-run.c:3539-3544
     for (int i = 1; i < (int) m->n_vocab; i++) if (logits[i] > logits[best]) best = i;
     return best;
+}
+
+int so_forward(so_model * m, int tok, int pos, float * logits) {
+    return forward_core(m, m->kc, m->vc, tok, pos, logits, lin_decode, NULL);
 }
 
 int so_decode(so_model * m, const int * prompt, int np, int ngen, int * ids, float * logits) {
@@ -581,5 +611,90 @@ int so_decode(so_model * m, const int * prompt, int np, int ngen, int * ids, flo
         if (g + 1 < ngen) t = so_forward(m, t, np + g, lg);
     }
     free(lg);
+    return 1;
+}
+
+// ------------------------------------------------------------- batched serving
+
+// sml_forward_multi (sml/sml-run.c:2559-2604): ns sequences, one token each,
+// each with its own cache and position. mode 0: every sequence through the
+// decode arithmetic (SML_MULTI=exact); mode 1: every product on the batched
+// path's arithmetic (so_gemm_sb_split with the splits set per kind, the
+// re-quantized weights made once per tensor).
+typedef struct { const rec_t * r; int8_t * w8; float * s8; } tc_cache_t;
+
+struct so_batch {
+    so_model * m;
+    int ns, mode;
+    int split[5];
+    uint16_t * kc, * vc;
+    tc_cache_t * cache;
+    int ncache, capcache;
+};
+
+static void lin_batched(void * ctx, so_model * m, const rec_t * r, int kind, const float * x, float * y) {
+    so_batch * b = (so_batch *) ctx;
+    tc_cache_t * c = NULL;
+    for (int i = 0; i < b->ncache; i++) if (b->cache[i].r == r) c = &b->cache[i];
+    const int n = (int) r->cols, nsb = (n / G + 7) / 8;
+    if (!c) {
+        if (b->ncache == b->capcache) {
+            b->capcache = b->capcache ? 2 * b->capcache : 64;
+            b->cache = (tc_cache_t *) realloc(b->cache, (size_t) b->capcache * sizeof *b->cache);
+        }
+        c = &b->cache[b->ncache++];
+        c->r = r;
+        c->w8 = (int8_t *) malloc((size_t) r->rows * nsb * 256);
+        c->s8 = (float *) malloc((size_t) r->rows * nsb * 4);
+        char nm[65];
+        memcpy(nm, r->name, 64);
+        nm[64] = 0;
+        so_requant8(m, nm, c->w8, c->s8);
+    }
+    sb_row(c->w8, c->s8, (const int32_t *) (m->base + r->perm_off), n, (int) r->rows, x, b->split[kind], y);
+}
+
+so_batch * so_batch_open(so_model * m, int ns, int mode) {
+    so_batch * b = (so_batch *) calloc(1, sizeof *b);
+    b->m = m;
+    b->ns = ns;
+    b->mode = mode;
+    for (int k = 0; k < 5; k++) b->split[k] = 1;
+    const size_t per = (size_t) m->n_layer * m->n_ctx * m->n_kv * m->hd;
+    b->kc = (uint16_t *) calloc(per * ns, 2);
+    b->vc = (uint16_t *) calloc(per * ns, 2);
+    return b;
+}
+
+void so_batch_set_splits(so_batch * b, const int * split5) {
+    for (int k = 0; k < 5; k++) b->split[k] = split5[k] > 0 ? split5[k] : 1;
+}
+
+int so_batch_step(so_batch * b, const int * tok, const int * pos, float * logits) {
+    so_model * m = b->m;
+    const size_t per = (size_t) m->n_layer * m->n_ctx * m->n_kv * m->hd;
+    for (int s = 0; s < b->ns; s++)
+        if (pos[s] >= m->n_ctx || (pos[s] >= 0 && (tok[s] < 0 || tok[s] >= (int) m->n_vocab))) return 0;
+    for (int s = 0; s < b->ns; s++)
+        if (pos[s] >= 0)
+            forward_core(m, b->kc + per * s, b->vc + per * s, tok[s], pos[s], logits + (size_t) s * m->n_vocab,
+                         b->mode ? lin_batched : lin_decode, b);
+    return 1;
+}
+
+void so_batch_close(so_batch * b) {
+    if (!b) return;
+    for (int i = 0; i < b->ncache; i++) { free(b->cache[i].w8); free(b->cache[i].s8); }
+    free(b->cache); free(b->kc); free(b->vc);
+    free(b);
+}
+
+int so_batch_kv(const so_batch * b, int layer, int slot, int pos, uint16_t * k, uint16_t * v) {
+    const so_model * m = b->m;
+    if (layer < 0 || layer >= (int) m->n_layer || slot < 0 || slot >= b->ns || pos < 0 || pos >= m->n_ctx) return 0;
+    const size_t kvd = (size_t) m->n_kv * m->hd, per = (size_t) m->n_layer * m->n_ctx * kvd;
+    const size_t at = per * slot + ((size_t) layer * m->n_ctx + pos) * kvd;
+    memcpy(k, b->kc + at, kvd * 2);
+    memcpy(v, b->vc + at, kvd * 2);
     return 1;
 }

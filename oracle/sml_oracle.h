@@ -41,6 +41,22 @@ int so_moe_ffn(so_model * m, int L, const float * xb, float * out, int * sel, fl
 // tiles' epilogue, sml/sml-gpu-fast.cu:1804-1880, 2025-2031).
 int so_requant8(so_model * m, const char * name, int8_t * w8, float * s8);
 int so_gemm_sb(so_model * m, const char * name, const float * X, int T, float * Y);
+// The same with the superblocks cut into `split` runs summed in order (split-K).
+int so_gemm_sb_split(so_model * m, const char * name, const float * X, int T, int split, float * Y);
+
+// Batched serving (sml_forward_multi, sml/sml-run.c:2559-2604): ns sequences,
+// each with its own KV cache. mode 0: each through the decode arithmetic;
+// mode 1: every product with the batched path's arithmetic, superblock slices
+// per kind (q|k|v, o, gate|up, down, head) from so_batch_set_splits. A step
+// fills logits [ns][n_vocab] for the slots with pos >= 0 (the rest untouched)
+// and returns 1, or 0 for a position or id out of range.
+typedef struct so_batch so_batch;
+so_batch * so_batch_open(so_model * m, int ns, int mode);
+void so_batch_set_splits(so_batch * b, const int * split5);
+int so_batch_step(so_batch * b, const int * tok, const int * pos, float * logits);
+void so_batch_close(so_batch * b);
+// Slot `slot`'s cached key and value rows at `pos` in `layer` (n_kv * hd fp16 each).
+int so_batch_kv(const so_batch * b, int layer, int slot, int pos, uint16_t * k, uint16_t * v);
 
 #ifdef __cplusplus
 }

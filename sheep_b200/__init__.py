@@ -70,9 +70,9 @@ def lib():
         "sb_tset_gemv_dev": (ip, [vp, cp, vp, ip, vp, vp]),
         "sb_tset_gemv_host": (ip, [vp, cp, vp, ip, vp]),
         "sb_tset_time_gemv": (ip, [vp, cp, vp, ip, ip, fp]),
-        "sb_tset_gemm_tc": (ip, [vp, cp, vp, ip, vp, vp]),
-        "sb_tset_gemm_tc_host": (ip, [vp, cp, vp, ip, vp]),
-        "sb_tset_time_gemm_tc": (ip, [vp, cp, vp, ip, ip, fp]),
+        "sb_tset_gemm_tc": (ip, [vp, cp, vp, ip, ip, vp, vp]),
+        "sb_tset_gemm_tc_host": (ip, [vp, cp, vp, ip, ip, vp]),
+        "sb_tset_time_gemm_tc": (ip, [vp, cp, vp, ip, ip, ip, fp]),
         "sb_tset_requant8_host": (ip, [vp, cp, vp, vp]),
         "sb_tset_matvec": (ip, [vp, cp, vp, vp, vp, vp, vp]),
         "sb_tset_dequant_rows": (ip, [vp, cp, vp, ip, vp]),
@@ -95,6 +95,14 @@ def lib():
         "sb_moe_last_error": (cp, []),
         "sb_tc_imma": (ip, [vp, vp, vp, ip, ip, ip, vp, vp]),
         "sb_tc_last_error": (cp, []),
+        "sb_batch_open": (vp, [cp, ip, ip, cp, ip]),
+        "sb_batch_close": (None, [vp]),
+        "sb_batch_info": (None, [vp, vp]),
+        "sb_forward_multi": (fp, [vp, vp, vp]),
+        "sb_batch_generate": (ip, [vp, vp, ip, ip, ip, vp, fp]),
+        "sb_batch_device_logits": (vp, [vp]),
+        "sb_batch_last_error": (cp, []),
+        "sb_batch_kv": (ip, [vp, ip, ip, ip, vp, vp]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -250,19 +258,20 @@ class TensorSet:
             raise RuntimeError("sb_tset_time_gemv failed")
         return ms.value
 
-    def gemm_tc(self, name, X):
-        """Y [nb, rows]: the batched path on the tensor cores (int8 per-256 arithmetic)."""
+    def gemm_tc(self, name, X, split=1):
+        """Y [nb, rows]: the batched path on the tensor cores (int8 per-256
+        arithmetic); split > 1 sums that many runs of superblocks in run order."""
         rows, cols, _ = self.shape(name)
         X = np.ascontiguousarray(np.atleast_2d(X), np.float32)
         Y = np.zeros((len(X), rows), np.float32)
-        if not lib().sb_tset_gemm_tc_host(self.h, name.encode(), _p(X), len(X), _p(Y)):
+        if not lib().sb_tset_gemm_tc_host(self.h, name.encode(), _p(X), len(X), split, _p(Y)):
             raise RuntimeError("sb_tset_gemm_tc_host failed")
         return Y
 
-    def time_gemm_tc(self, name, X, reps):
+    def time_gemm_tc(self, name, X, reps, split=1):
         X = np.ascontiguousarray(np.atleast_2d(X), np.float32)
         ms = ctypes.c_float()
-        if not lib().sb_tset_time_gemm_tc(self.h, name.encode(), _p(X), len(X), reps, ctypes.byref(ms)):
+        if not lib().sb_tset_time_gemm_tc(self.h, name.encode(), _p(X), len(X), split, reps, ctypes.byref(ms)):
             raise RuntimeError("sb_tset_time_gemm_tc failed")
         return ms.value
 
@@ -340,6 +349,65 @@ class MoeLayer:
             self.close()
         except Exception:
             pass
+
+
+class Batch:
+    """n_seq conversations decoding together on the GPU (sb_batch_*): the
+    reference's sml_forward_multi with every product on the tensor cores."""
+
+    def __init__(self, path, n_seq, n_ctx):
+        why = ctypes.create_string_buffer(512)
+        self.h = lib().sb_batch_open(path.encode(), n_seq, n_ctx, why, 512)
+        if not self.h:
+            raise RuntimeError(f"sb_batch_open: {why.value.decode()}")
+        info = (ctypes.c_int * 16)()
+        lib().sb_batch_info(self.h, info)
+        self.n_seq, self.n_ctx, self.n_vocab = info[0], info[1], info[2]
+        self.splits = list(info[3:8])
+        self.file_bytes = (info[8] & 0xffffffff) | (info[9] << 32)
+        self.int8_bytes = (info[10] & 0xffffffff) | (info[11] << 32)
+        self.launches = info[12]
+        self.tile_tokens = info[13]
+
+    def forward_multi(self, tokens, pos):
+        """logits [n_seq, n_vocab] for tokens[s] at pos[s] (pos < 0: idle slot)."""
+        t = np.ascontiguousarray(tokens, np.int32)
+        p = np.ascontiguousarray(pos, np.int32)
+        assert len(t) == self.n_seq and len(p) == self.n_seq
+        r = lib().sb_forward_multi(self.h, _p(t), _p(p))
+        if not r:
+            raise RuntimeError(f"sb_forward_multi: {lib().sb_batch_last_error().decode()}")
+        return np.ctypeslib.as_array(r, shape=(self.n_seq * self.n_vocab,)).reshape(self.n_seq, self.n_vocab).copy()
+
+    def generate(self, prompts, ngen, nwarm=0, timed=False):
+        """ids [n_seq, nwarm + ngen] greedy from prompts [n_seq, np] (and the
+        device ms of the last ngen - 1 steps when timed)."""
+        P = np.ascontiguousarray(prompts, np.int32)
+        ids = np.zeros((self.n_seq, nwarm + ngen), np.int32)
+        ms = ctypes.c_float()
+        if not lib().sb_batch_generate(self.h, _p(P), P.shape[1], nwarm, ngen, _p(ids),
+                                       ctypes.byref(ms) if timed else None):
+            raise RuntimeError(f"sb_batch_generate: {lib().sb_batch_last_error().decode()}")
+        return (ids, ms.value) if timed else ids
+
+    def kv(self, layer, slot, pos, n_kv_dim):
+        """(k, v) cached fp16 rows (as uint16) of slot at pos in layer."""
+        k = np.zeros(n_kv_dim, np.uint16)
+        v = np.zeros(n_kv_dim, np.uint16)
+        if not lib().sb_batch_kv(self.h, layer, slot, pos, _p(k), _p(v)):
+            raise RuntimeError(f"sb_batch_kv: {lib().sb_batch_last_error().decode()}")
+        return k, v
+
+    def close(self):
+        if self.h:
+            lib().sb_batch_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
 
 
 def moe_route_dev(logits_ptr, n_tok, n_expert, k, flags, sel_ptr, w_ptr, stream=0):

@@ -287,23 +287,6 @@ static void enqueue_token(sb_engine * e) {
 
 // ------------------------------------------------------------------ open
 
-static const char * unsupported(const ssf_file & f) {
-    const ssf_hdr * h = f.hdr;
-    if (h->flags & SSF_FLAG_HADAMARD) return "Hadamard-rotated weights";
-    if (h->flags & SSF_FLAG_EXACT) return "an exact-weight (f32) file";
-    if (h->norm_type != 0) return "LayerNorm";
-    if (h->rope_type != 0) return "interleaved RoPE";
-    if (h->arch_bits) return "architecture flags beyond a plain decoder";
-    if (h->logit_softcap != 0.0f || h->attn_softcap != 0.0f) return "soft-capping";
-    if (h->n_swa) return "sliding-window attention";
-    if (h->emb_scale != 0.0f || h->res_scale != 0.0f || h->logit_scale != 0.0f) return "embedding/residual/logit scales";
-    if (h->clip_qkv != 0.0f) return "Q/K/V clamping";
-    const char * names[] = {"position_embd.weight", "token_embd_norm.weight", "output.bias", "rope_freqs",
-                            "attn_window", "attn_rope"};
-    for (const char * n : names) if (ssf_find(&f, n)) return n;
-    return nullptr;
-}
-
 static void close_all(sb_engine * e) {
     if (e->g_tok) cudaGraphExecDestroy(e->g_tok);
     if (e->st) cudaStreamDestroy(e->st);
@@ -446,12 +429,6 @@ static bool build(sb_engine * e, char * why, int nwhy) {
     return true;
 }
 
-// Algorithmic bytes of one record: codes and fields as the file stores them.
-static uint64_t rec_bytes(const ssf_rec * r) {
-    uint64_t b = r->sd_n + r->sq_n + r->md_n + r->mq_n;
-    for (int p = 0; p < SSF_MAX_LEVELS; p++) b += r->codes_n[p];
-    return b;
-}
 
 // Average duration of one kernel class of the token, each launch alone on the
 // engine's stream (no programmatic overlap), timed by CUDA events, cycling
@@ -467,14 +444,14 @@ extern "C" int sb_time_kernel(sb_engine * e, int which, int reps, float * ms_avg
     auto layer_bytes = [&](int l) -> double {
         auto R = [&](const char * fmt) { return ssf_findf(&f, fmt, l, 0); };
         switch (which) {
-        case 0: return (double) (rec_bytes(R("blk.%d.attn_q.weight")) + rec_bytes(R("blk.%d.attn_k.weight")) +
-                                 rec_bytes(R("blk.%d.attn_v.weight")));
-        case 2: return (double) rec_bytes(R("blk.%d.attn_output.weight"));
-        case 3: return (double) (rec_bytes(R("blk.%d.ffn_gate.weight")) + rec_bytes(R("blk.%d.ffn_up.weight")));
-        case 4: return (double) rec_bytes(R("blk.%d.ffn_down.weight"));
+        case 0: return (double) (ssf_rec_bytes(R("blk.%d.attn_q.weight")) + ssf_rec_bytes(R("blk.%d.attn_k.weight")) +
+                                 ssf_rec_bytes(R("blk.%d.attn_v.weight")));
+        case 2: return (double) ssf_rec_bytes(R("blk.%d.attn_output.weight"));
+        case 3: return (double) (ssf_rec_bytes(R("blk.%d.ffn_gate.weight")) + ssf_rec_bytes(R("blk.%d.ffn_up.weight")));
+        case 4: return (double) ssf_rec_bytes(R("blk.%d.ffn_down.weight"));
         default: {
             const ssf_rec * h = ssf_find(&f, "output.weight");
-            return (double) rec_bytes(h ? h : ssf_find(&f, "token_embd.weight"));
+            return (double) ssf_rec_bytes(h ? h : ssf_find(&f, "token_embd.weight"));
         }
         }
     };
@@ -617,7 +594,7 @@ sb_engine * sb_open(const char * path, int n_ctx, char * why, int nwhy) {
     sb_engine * e = new sb_engine();
     if (!ssf_open(&e->f, path, why, nwhy)) { delete e; return nullptr; }
     const ssf_hdr * h = e->f.hdr;
-    if (const char * u = unsupported(e->f)) {
+    if (const char * u = ssf_unsupported(e->f)) {
         snprintf(why, nwhy, "%s: not on the GPU yet", u);
         close_all(e);
         delete e;
@@ -651,20 +628,7 @@ sb_engine * sb_open(const char * path, int n_ctx, char * why, int nwhy) {
         close_all(e); delete e; return nullptr;
     }
     if (!build(e, why, nwhy)) { close_all(e); delete e; return nullptr; }
-    // RoPE tables exactly as the CPU builds them (sml/sml-run.c:1383-1393)
-    {
-        const int half = e->hd / 2;
-        std::vector<float> c((size_t) e->n_ctx * half), s((size_t) e->n_ctx * half);
-        for (int p = 0; p < e->n_ctx; p++)
-            for (int i = 0; i < half; i++) {
-                const float fr = powf(e->theta, -(float) i / (float) half);
-                const float a = (float) p * fr;
-                c[(size_t) p * half + i] = cosf(a);
-                s[(size_t) p * half + i] = sinf(a);
-            }
-        cudaMemcpy(e->rcos, c.data(), c.size() * 4, cudaMemcpyHostToDevice);
-        cudaMemcpy(e->rsin, s.data(), s.size() * 4, cudaMemcpyHostToDevice);
-    }
+    upload_rope(e->rcos, e->rsin, e->n_ctx, e->hd, e->theta);
     if (!ck(cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking), "stream") ||
         !ck(cudaMallocHost(&e->h_logits, (size_t) e->V * 4), "pinned logits") ||
         !ck(cudaMallocHost(&e->h_io, 64 * 4), "pinned io")) {

@@ -359,8 +359,11 @@ SB_DEV void mk_norm_rope(float * v, const float * w, float eps, int hd, const fl
     const int half = hd / 2;
     for (int i = tid; i < half; i += kConsThreads) {
         const float a = v[i], b = v[i + half];
-        v[i] = a * cs[i] - b * sn[i];
-        v[i + half] = a * sn[i] + b * cs[i];
+        // both products rounded, then the sum: no fused multiply-add, as the CPU
+        // restatement computes it (sml/sml-run.c:363-366, built without contraction),
+        // so keys are bit-equal before their fp16 rounding
+        v[i] = __fsub_rn(__fmul_rn(a, cs[i]), __fmul_rn(b, sn[i]));
+        v[i + half] = __fadd_rn(__fmul_rn(a, sn[i]), __fmul_rn(b, cs[i]));
     }
     bar_sync(1, kConsThreads);
 }

@@ -11,14 +11,19 @@
 //                a 32 KB block per (128 rows, superblock) in the core-matrix
 //                layout of tc.cuh. Done once per tensor, kept on the device
 //                (the reference re-makes it per call).
-//   k_quant_sb   one warp per (token, superblock): the B operand, a block of
+//   k_quant_rows one CTA per token (row of x), one warp per superblock: the
+//                row gathered through the tensor's column order (optionally
+//                RMS-normalized, or SiLU(gate) * up), the B operand, a block of
 //                N x 256 bytes per (N tokens, superblock), and the scale.
-//   k_tcgemm<N>  one CTA per (128 rows, N tokens), six warps: a producer
-//                (bulk copies of both blocks of a superblock into a 4-stage
-//                ring), an MMA issuer (8 MMAs of K = 32 per superblock into
-//                one of two TMEM accumulators, then commits), and four
-//                epilogue warps (TMEM lanes 0..127 = rows) that apply the
-//                superblock's scales while the next superblock multiplies.
+//   k_tcgemm<N>  one CTA per (128 rows, N tokens, slice of the superblocks),
+//                six warps: a producer (bulk copies of both blocks of a
+//                superblock into a 4-stage ring), an MMA issuer (8 MMAs of
+//                K = 32 per superblock into one of two TMEM accumulators, then
+//                commits), and four epilogue warps (TMEM lanes 0..127 = rows)
+//                that apply the superblock's scales while the next superblock
+//                multiplies. Slices meet in a partial-sum buffer and the last
+//                CTA of a tile adds them in slice order (split-K). The
+//                epilogue may add a bias or accumulate into y (a residual).
 #include "tc.cuh"
 #include "decode.cuh"
 #include "sheep_b200.h"
@@ -33,11 +38,11 @@ constexpr uint32_t kTcABytes = 128 * 256;
 
 template <int NB, int SIX>
 __global__ void __launch_bounds__(256) k_requant8(const __grid_constant__ QT t, uint8_t * wblk, float * s8,
-                                                  int rows_pad, int nsb) {
+                                                  int rows_pad, int nsb, int row_off, int rows_here) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const long item = (long) blockIdx.x * 8 + warp;
-    if (item >= (long) rows_pad * nsb) return;
-    const int r = (int) (item / nsb), sb = (int) (item % nsb);
+    if (item >= (long) rows_here * nsb) return;
+    const int r = (int) (item / nsb), sb = (int) (item % nsb);   // r: row of t; row_off + r: row of the plan
     const int ng = t.cols / kGroup, g = sb * 8 + (lane >> 2), part = lane & 3;
     const bool live = r < t.rows && g < ng;
     const float cmax = (float) ((1 << NB) - 1);
@@ -51,7 +56,7 @@ __global__ void __launch_bounds__(256) k_requant8(const __grid_constant__ QT t, 
     }
 #pragma unroll
     for (int o = 16; o; o >>= 1) bound = fmaxf(bound, __shfl_xor_sync(0xffffffffu, bound, o));
-    if (lane == 0) s8[(size_t) sb * rows_pad + r] = __fdiv_rn(bound, 127.0f);
+    if (lane == 0) s8[(size_t) sb * rows_pad + row_off + r] = __fdiv_rn(bound, 127.0f);
     const float inv = bound > 0.0f ? __fdiv_rn(127.0f, bound) : 0.0f;
     const float ka = __fmul_rn(s, inv), kb = __fmul_rn(m, inv);
     uint32_t w[2] = {0u, 0u};
@@ -62,38 +67,65 @@ __global__ void __launch_bounds__(256) k_requant8(const __grid_constant__ QT t, 
         w[j >> 2] |= ((uint32_t) (q & 0xff)) << (8 * (j & 3));
     }
     const int k = (lane >> 2) * kGroup + part * 8;
-    *reinterpret_cast<uint2 *>(wblk + ((size_t) (r >> 7) * nsb + sb) * kTcABytes + tc_off(128, r & 127, k)) =
+    const int pr = row_off + r;
+    *reinterpret_cast<uint2 *>(wblk + ((size_t) (pr >> 7) * nsb + sb) * kTcABytes + tc_off(128, pr & 127, k)) =
         make_uint2(w[0], w[1]);
 }
 
-__global__ void __launch_bounds__(256) k_quant_sb(const float * x, const int32_t * perm, int T, int cols, int nsb,
-                                                  int T_pad, int N, uint8_t * xblk, float * xs) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const long item = (long) blockIdx.x * 8 + warp;
-    if (item >= (long) T_pad * nsb) return;
-    const int tok = (int) (item / nsb), sb = (int) (item % nsb);
-    const int k0 = lane * 8;
-    float v[8];
-    float amax = 0.0f;
-#pragma unroll
-    for (int j = 0; j < 8; j++) {
-        const int i = sb * 256 + k0 + j;
-        v[j] = tok < T && i < cols ? x[(size_t) tok * cols + perm[i]] : 0.0f;
-        amax = fmaxf(amax, fabsf(v[j]));
+// One CTA per row of x (token): the row's values in the tensor's column order
+// (plain; RMS-normalized with a gain, the norm's sum of squares in double as
+// the decode GEMVs take it; or SiLU(gate) * up from a row holding gate | up),
+// quantized per 256 into the B operand blocks (N tokens per block) and the
+// per-superblock scales. Rows past T are zeros.
+template <int MODE>
+__global__ void __launch_bounds__(256) k_quant_rows(const TcQuantArgs a) {
+    __shared__ double red[8];
+    const int tok = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool live = tok < a.T;
+    const float * row = a.x + (size_t) tok * a.ldx;
+    float s = 1.0f;
+    if (MODE == TQ_NORM) {
+        double q = 0.0;
+        if (live)
+            for (int i = threadIdx.x; i < a.cols; i += 256) q += (double) row[i] * (double) row[i];
+        q = warp_sum_d(q);
+        if (lane == 0) red[warp] = q;
+        __syncthreads();
+        double ss = 0.0;
+        for (int k = 0; k < 8; k++) ss += red[k];
+        s = __fdiv_rn(1.0f, sqrtf(__fadd_rn((float) (ss / a.cols), a.eps)));
     }
-    amax = warp_max(amax);
-    const float sc = __fdiv_rn(amax, 127.0f);
-    const float is = sc > 0.0f ? __fdiv_rn(1.0f, sc) : 0.0f;
-    uint32_t w[2] = {0u, 0u};
+    for (int sb = warp; sb < a.nsb; sb += 8) {
+        const int k0 = lane * 8;
+        float v[8];
+        float amax = 0.0f;
 #pragma unroll
-    for (int j = 0; j < 8; j++) {
-        int q = __float2int_rn(__fmul_rn(v[j], is));
-        q = q > 127 ? 127 : q < -127 ? -127 : q;
-        w[j >> 2] |= ((uint32_t) (q & 0xff)) << (8 * (j & 3));
+        for (int j = 0; j < 8; j++) {
+            const int i = sb * 256 + k0 + j;
+            float x = 0.0f;
+            if (live && i < a.cols) {
+                const int p = a.perm[i];
+                if (MODE == TQ_PLAIN) x = row[p];
+                else if (MODE == TQ_NORM) x = __fmul_rn(__fmul_rn(row[p], s), a.gain[p]);
+                else x = silu_mul(row[p], row[a.up_off + p]);
+            }
+            v[j] = x;
+            amax = fmaxf(amax, fabsf(x));
+        }
+        amax = warp_max(amax);
+        const float sc = __fdiv_rn(amax, 127.0f);
+        const float is = sc > 0.0f ? __fdiv_rn(1.0f, sc) : 0.0f;
+        uint32_t w[2] = {0u, 0u};
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            int q = __float2int_rn(__fmul_rn(v[j], is));
+            q = q > 127 ? 127 : q < -127 ? -127 : q;
+            w[j >> 2] |= ((uint32_t) (q & 0xff)) << (8 * (j & 3));
+        }
+        *reinterpret_cast<uint2 *>(a.xblk + ((size_t) (tok / a.N) * a.nsb + sb) * (size_t) (a.N * 256) +
+                                   tc_off(a.N, tok % a.N, k0)) = make_uint2(w[0], w[1]);
+        if (lane == 0) a.xs[(size_t) sb * a.T_pad + tok] = sc;
     }
-    *reinterpret_cast<uint2 *>(xblk + ((size_t) (tok / N) * nsb + sb) * (size_t) (N * 256) + tc_off(N, tok % N, k0)) =
-        make_uint2(w[0], w[1]);
-    if (lane == 0) xs[(size_t) sb * T_pad + tok] = sc;
 }
 
 // A wait that gives up at once when another role of the CTA already has.
@@ -110,11 +142,15 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
     __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], accf[2], acce[2];
     __shared__ uint32_t tslot;
     __shared__ volatile int fail;
+    __shared__ volatile bool last;
     constexpr uint32_t BB = N * 256, SB = kTcABytes + BB;
     constexpr uint32_t ncols = tc_cols(2 * N);
     constexpr uint32_t idesc = tc_idesc_s8(128, N);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int mb = blockIdx.x, tb = blockIdx.y;
+    const int mb = blockIdx.x, tb = blockIdx.y, z = blockIdx.z;
+    // this CTA's superblocks: slice z of the deep sum
+    const int per = (g.nsb + g.split - 1) / g.split;
+    const int s0 = z * per, ns = min(g.nsb, s0 + per) - s0;
     if (warp == 1) tmem_alloc(&tslot, ncols);
     if (tid == 0) {
         for (int s = 0; s < kTcStages; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
@@ -131,8 +167,8 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
     if (warp == 0) {
         // ---------------- producer: both operand blocks of every superblock
         if (lane == 0) {
-            for (int sb = 0; sb < g.nsb; sb++) {
-                const int s = sb % kTcStages, lap = sb / kTcStages;
+            for (int i = 0; i < ns; i++) {
+                const int s = i % kTcStages, lap = i / kTcStages, sb = s0 + i;
                 if (lap > 0 && !tc_wait(&empty[s], (lap - 1) & 1, g.err, 40, &fail)) break;
                 mbar_expect_tx(&full[s], SB);
                 bulk_g2s(tsm + (size_t) s * SB, g.wblk + ((size_t) mb * g.nsb + sb) * kTcABytes, kTcABytes, &full[s]);
@@ -142,10 +178,10 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
     } else if (warp == 1) {
         // ---------------- MMA issuer: 8 x K=32 per superblock into accumulator sb % 2
         if (lane == 0) {
-            for (int sb = 0; sb < g.nsb; sb++) {
-                const int s = sb % kTcStages, buf = sb & 1;
-                if (!tc_wait(&full[s], (sb / kTcStages) & 1, g.err, 41, &fail)) break;
-                if (sb >= 2 && !tc_wait(&acce[buf], ((sb >> 1) - 1) & 1, g.err, 42, &fail)) break;
+            for (int i = 0; i < ns; i++) {
+                const int s = i % kTcStages, buf = i & 1;
+                if (!tc_wait(&full[s], (i / kTcStages) & 1, g.err, 41, &fail)) break;
+                if (i >= 2 && !tc_wait(&acce[buf], ((i >> 1) - 1) & 1, g.err, 42, &fail)) break;
                 tc_fence_after();
                 const uint8_t * As = tsm + (size_t) s * SB, * Bs = As + kTcABytes;
 #pragma unroll
@@ -163,11 +199,11 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
 #pragma unroll
         for (int t = 0; t < N; t++) acc[t] = 0.0f;
         bool ok = true;
-        for (int sb = 0; sb < g.nsb; sb++) {
-            const int buf = sb & 1;
+        for (int i = 0; i < ns; i++) {
+            const int buf = i & 1, sb = s0 + i;
             const float s8v = g.s8[(size_t) sb * g.rows_pad + r];
             const float * xsp = g.xs + (size_t) sb * g.T_pad + (size_t) tb * N;
-            ok = ok && tc_wait(&accf[buf], (sb >> 1) & 1, g.err, 43, &fail);
+            ok = ok && tc_wait(&accf[buf], (i >> 1) & 1, g.err, 43, &fail);
             tc_fence_after();
             uint32_t d[N];
 #pragma unroll
@@ -185,12 +221,42 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
             for (int t = 0; t < N; t++)
                 acc[t] = __fmaf_rn(__fmul_rn(s8v, __ldg(xsp + t)), (float) (int) d[t], acc[t]);
         }
-        if (ok && r < g.rows)
+        if (g.split > 1) {
+            // slices meet in part[z][token][row]; the last CTA of the tile adds
+            // them in slice order, so the sum does not depend on arrival order
+            // (sml_g_splitk_sum, sml/sml-gpu-fast.cu:2057-2065)
+#pragma unroll
+            for (int t = 0; t < N; t++)
+                g.part[((size_t) z * g.T_pad + tb * N + t) * g.rows_pad + r] = acc[t];
+            __threadfence();
+            bar_sync(1, 128);
+            if (warp == 2 && lane == 0)
+                last = atomicAdd(&g.cnt[mb * gridDim.y + tb], 1u) == (unsigned) (g.split - 1);
+            bar_sync(1, 128);
+            if (!last) ok = false;
+            else {
+                __threadfence();
+#pragma unroll
+                for (int t = 0; t < N; t++) {
+                    float s = 0.0f;
+                    for (int k = 0; k < g.split; k++)
+                        s = __fadd_rn(s, __ldcg(g.part + ((size_t) k * g.T_pad + tb * N + t) * g.rows_pad + r));
+                    acc[t] = s;
+                }
+                if (warp == 2 && lane == 0) g.cnt[mb * gridDim.y + tb] = 0;
+            }
+        }
+        if (ok && r < g.rows) {
+            const float b = g.bias ? g.bias[r] : 0.0f;
 #pragma unroll
             for (int t = 0; t < N; t++) {
                 const int tok = tb * N + t;
-                if (tok < g.T) g.y[(size_t) tok * g.rows + r] = acc[t];
+                if (tok < g.T) {
+                    float * yp = g.y + (size_t) tok * g.ldy + r;
+                    *yp = g.accumulate ? __fadd_rn(*yp, acc[t]) : g.bias ? __fadd_rn(acc[t], b) : acc[t];
+                }
             }
+        }
     }
     tc_fence_before();
     __syncthreads();
@@ -201,20 +267,29 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
 }
 
 template <int NB, int SIX>
-static void launch_requant(const QT & t, uint8_t * wblk, float * s8, int rows_pad, int nsb, cudaStream_t st,
-                           cudaError_t * r) {
-    const long items = (long) rows_pad * nsb;
-    k_requant8<NB, SIX><<<(unsigned) ((items + 7) / 8), 256, 0, st>>>(t, wblk, s8, rows_pad, nsb);
+static void launch_requant(const QT & t, uint8_t * wblk, float * s8, int rows_pad, int nsb, int row_off,
+                           cudaStream_t st, cudaError_t * r) {
+    const long items = (long) t.rows * nsb;
+    k_requant8<NB, SIX><<<(unsigned) ((items + 7) / 8), 256, 0, st>>>(t, wblk, s8, rows_pad, nsb, row_off, t.rows);
     *r = cudaGetLastError();
 }
 
-cudaError_t tc_requant(const QT & t, const TcPlan & p, cudaStream_t st) {
+cudaError_t tc_requant(const QT & t, const TcPlan & p, int row_off, cudaStream_t st) {
     cudaError_t r = cudaErrorInvalidValue;
-    SB_DISPATCH_QT(t.nbits, t.six, launch_requant, t, p.wblk, p.s8, p.rows_pad, p.nsb, st, &r);
+    if (row_off + t.rows > p.rows_pad || (t.cols / kGroup + 7) / 8 != p.nsb) return r;
+    SB_DISPATCH_QT(t.nbits, t.six, launch_requant, t, p.wblk, p.s8, p.rows_pad, p.nsb, row_off, st, &r);
     return r;
 }
 
 int tc_tile_n(int T) { return T <= 16 ? 16 : T <= 32 ? 32 : 64; }
+int tc_tokens_pad(int T) { const int N = tc_tile_n(T); return (T + N - 1) / N * N; }
+
+cudaError_t tc_quant(int mode, const TcQuantArgs & a, cudaStream_t st) {
+    if (mode == TQ_NORM) k_quant_rows<TQ_NORM><<<a.T_pad, 256, 0, st>>>(a);
+    else if (mode == TQ_SILU) k_quant_rows<TQ_SILU><<<a.T_pad, 256, 0, st>>>(a);
+    else k_quant_rows<TQ_PLAIN><<<a.T_pad, 256, 0, st>>>(a);
+    return cudaGetLastError();
+}
 
 template <int N>
 static cudaError_t launch_gemm(const TcArgs & a, cudaStream_t st) {
@@ -225,21 +300,38 @@ static cudaError_t launch_gemm(const TcArgs & a, cudaStream_t st) {
         if (e != cudaSuccess) return e;
         attr = true;
     }
-    k_tcgemm<N><<<dim3(a.rows_pad / 128, a.T_pad / N), 192, smem, st>>>(a);
+    k_tcgemm<N><<<dim3(a.rows_pad / 128, a.T_pad / N, a.split), 192, smem, st>>>(a);
     return cudaGetLastError();
+}
+
+int tc_split(int nsb, int split) {
+    if (split < 1) split = 1;
+    if (split > nsb) split = nsb;
+    const int per = (nsb + split - 1) / split;
+    return (nsb + per - 1) / per;
+}
+
+cudaError_t tc_mma(const TcArgs & a, cudaStream_t st) {
+    if (a.split < 1 || a.split != tc_split(a.nsb, a.split) || (a.split > 1 && (!a.part || !a.cnt)))
+        return cudaErrorInvalidValue;
+    const int N = tc_tile_n(a.T);
+    return N == 16 ? launch_gemm<16>(a, st) : N == 32 ? launch_gemm<32>(a, st) : launch_gemm<64>(a, st);
 }
 
 cudaError_t tc_gemm(const QT & t, const TcPlan & p, const float * x, int T, uint8_t * xblk, float * xs, float * y,
                     int * err, cudaStream_t st) {
-    const int N = tc_tile_n(T), T_pad = (T + N - 1) / N * N;
-    const long items = (long) T_pad * p.nsb;
-    k_quant_sb<<<(unsigned) ((items + 7) / 8), 256, 0, st>>>(x, t.perm, T, t.cols, p.nsb, T_pad, N, xblk, xs);
-    cudaError_t e = cudaGetLastError();
+    TcQuantArgs q;
+    memset(&q, 0, sizeof q);
+    q.x = x; q.ldx = t.cols; q.perm = t.perm; q.cols = t.cols; q.T = T; q.T_pad = tc_tokens_pad(T);
+    q.N = tc_tile_n(T); q.nsb = p.nsb; q.xblk = xblk; q.xs = xs;
+    cudaError_t e = tc_quant(TQ_PLAIN, q, st);
     if (e != cudaSuccess) return e;
     TcArgs a;
-    a.wblk = p.wblk; a.s8 = p.s8; a.xblk = xblk; a.xs = xs; a.y = y;
-    a.rows = t.rows; a.rows_pad = p.rows_pad; a.nsb = p.nsb; a.T = T; a.T_pad = T_pad; a.err = err;
-    return N == 16 ? launch_gemm<16>(a, st) : N == 32 ? launch_gemm<32>(a, st) : launch_gemm<64>(a, st);
+    memset(&a, 0, sizeof a);
+    a.wblk = p.wblk; a.s8 = p.s8; a.xblk = xblk; a.xs = xs; a.y = y; a.ldy = t.rows;
+    a.rows = t.rows; a.rows_pad = p.rows_pad; a.nsb = p.nsb; a.T = T; a.T_pad = q.T_pad; a.err = err;
+    a.split = 1;
+    return tc_mma(a, st);
 }
 
 }  // namespace sb

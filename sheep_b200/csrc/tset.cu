@@ -36,8 +36,9 @@ struct sb_tset {
     // tensor-core batched path: per-tensor int8 re-quantization, made on first use
     std::unordered_map<std::string, TcPlan> tc;
     uint8_t * tc_x = nullptr;
-    float * tc_xs = nullptr;
-    size_t tc_x_cap = 0, tc_xs_cap = 0;
+    float * tc_xs = nullptr, * tc_part = nullptr;
+    unsigned * tc_cnt = nullptr;
+    size_t tc_x_cap = 0, tc_xs_cap = 0, tc_part_cap = 0, tc_cnt_cap = 0;
     int nsm = 148;
 };
 
@@ -96,6 +97,8 @@ extern "C" void sb_tset_close(sb_tset * t) {
     for (auto & kv : t->tc) { cudaFree(kv.second.wblk); cudaFree(kv.second.s8); }
     cudaFree(t->tc_x);
     cudaFree(t->tc_xs);
+    cudaFree(t->tc_part);
+    cudaFree(t->tc_cnt);
     t->ar.release();
     ssf_close(&t->f);
     delete t;
@@ -346,7 +349,7 @@ static const TcPlan * tc_plan(sb_tset * t, const char * name, const QT ** qo) {
     p.rows_pad = (q->rows + 127) / 128 * 128;
     if (cudaMalloc(&p.wblk, (size_t) p.rows_pad * p.nsb * 256) != cudaSuccess) return nullptr;
     if (cudaMalloc(&p.s8, (size_t) p.nsb * p.rows_pad * 4) != cudaSuccess) { cudaFree(p.wblk); return nullptr; }
-    if (tc_requant(*q, p, nullptr) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+    if (tc_requant(*q, p, 0, nullptr) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
         cudaFree(p.wblk);
         cudaFree(p.s8);
         return nullptr;
@@ -354,36 +357,48 @@ static const TcPlan * tc_plan(sb_tset * t, const char * name, const QT ** qo) {
     return &t->tc.emplace(name, p).first->second;
 }
 
-// Scratch for the activations of T rows (grown as needed; frees synchronize).
-static bool tc_scratch(sb_tset * t, int nsb, int T) {
-    const int N = tc_tile_n(T), T_pad = (T + N - 1) / N * N;
-    const size_t xb = (size_t) T_pad * nsb * 256, sb = (size_t) T_pad * nsb * 4;
-    if (xb > t->tc_x_cap) {
-        cudaFree(t->tc_x);
-        t->tc_x = nullptr;
-        t->tc_x_cap = 0;
-        if (cudaMalloc(&t->tc_x, xb) != cudaSuccess) return false;
-        t->tc_x_cap = xb;
-    }
-    if (sb > t->tc_xs_cap) {
-        cudaFree(t->tc_xs);
-        t->tc_xs = nullptr;
-        t->tc_xs_cap = 0;
-        if (cudaMalloc(&t->tc_xs, sb) != cudaSuccess) return false;
-        t->tc_xs_cap = sb;
-    }
+// Grow a device buffer to at least n bytes (zeroed when grown; frees synchronize).
+template <typename P>
+static bool grow(P *& buf, size_t & cap, size_t n) {
+    if (n <= cap) return true;
+    cudaFree(buf);
+    buf = nullptr;
+    cap = 0;
+    if (cudaMalloc(&buf, n) != cudaSuccess || cudaMemset(buf, 0, n) != cudaSuccess) return false;
+    cap = n;
     return true;
 }
 
-extern "C" int sb_tset_gemm_tc(sb_tset * t, const char * name, const float * x, int nb, float * y, void * stream) {
-    const QT * q = nullptr;
-    if (!t || nb < 1 || nb > kMaxBatch) return 0;
-    const TcPlan * p = tc_plan(t, name, &q);
-    if (!p || !tc_scratch(t, p->nsb, nb)) return 0;
-    return tc_gemm(*q, *p, x, nb, t->tc_x, t->tc_xs, y, t->err, (cudaStream_t) stream) == cudaSuccess;
+// Scratch for the activations of T rows and the partial sums of `split` slices.
+static bool tc_scratch(sb_tset * t, const TcPlan & p, int T, int split) {
+    const int N = tc_tile_n(T), T_pad = tc_tokens_pad(T);
+    return grow(t->tc_x, t->tc_x_cap, (size_t) T_pad * p.nsb * 256) &&
+           grow(t->tc_xs, t->tc_xs_cap, (size_t) T_pad * p.nsb * 4) &&
+           (split <= 1 || (grow(t->tc_part, t->tc_part_cap, (size_t) split * T_pad * p.rows_pad * 4) &&
+                           grow(t->tc_cnt, t->tc_cnt_cap, (size_t) (p.rows_pad / 128) * (T_pad / N) * 4)));
 }
 
-extern "C" int sb_tset_gemm_tc_host(sb_tset * t, const char * name, const float * x, int nb, float * y) {
+extern "C" int sb_tset_gemm_tc(sb_tset * t, const char * name, const float * x, int nb, int split, float * y,
+                               void * stream) {
+    const QT * q = nullptr;
+    if (!t || nb < 1 || nb > kMaxBatch || split < 1) return 0;
+    const TcPlan * p = tc_plan(t, name, &q);
+    if (!p || split != tc_split(p->nsb, split) || !tc_scratch(t, *p, nb, split)) return 0;
+    const cudaStream_t st = (cudaStream_t) stream;
+    TcQuantArgs qa;
+    memset(&qa, 0, sizeof qa);
+    qa.x = x; qa.ldx = q->cols; qa.perm = q->perm; qa.cols = q->cols; qa.T = nb; qa.T_pad = tc_tokens_pad(nb);
+    qa.N = tc_tile_n(nb); qa.nsb = p->nsb; qa.xblk = t->tc_x; qa.xs = t->tc_xs;
+    if (tc_quant(TQ_PLAIN, qa, st) != cudaSuccess) return 0;
+    TcArgs a;
+    memset(&a, 0, sizeof a);
+    a.wblk = p->wblk; a.s8 = p->s8; a.xblk = t->tc_x; a.xs = t->tc_xs; a.y = y; a.ldy = q->rows;
+    a.rows = q->rows; a.rows_pad = p->rows_pad; a.nsb = p->nsb; a.T = nb; a.T_pad = qa.T_pad; a.err = t->err;
+    a.split = split; a.part = t->tc_part; a.cnt = t->tc_cnt;
+    return tc_mma(a, st) == cudaSuccess;
+}
+
+extern "C" int sb_tset_gemm_tc_host(sb_tset * t, const char * name, const float * x, int nb, int split, float * y) {
     const QT * q = find_qt(t, name);
     if (!q || nb < 1 || nb > kMaxBatch) return 0;
     float * dx = nullptr, * dy = nullptr;
@@ -392,7 +407,7 @@ extern "C" int sb_tset_gemm_tc_host(sb_tset * t, const char * name, const float 
     int err = 0;
     if (ok) {
         cudaMemcpy(dx, x, (size_t) nb * q->cols * 4, cudaMemcpyHostToDevice);
-        ok = sb_tset_gemm_tc(t, name, dx, nb, dy, nullptr) && cudaDeviceSynchronize() == cudaSuccess;
+        ok = sb_tset_gemm_tc(t, name, dx, nb, split, dy, nullptr) && cudaDeviceSynchronize() == cudaSuccess;
         cudaMemcpy(&err, t->err, 4, cudaMemcpyDeviceToHost);
         ok = ok && err == 0;
         if (ok) cudaMemcpy(y, dy, (size_t) nb * q->rows * 4, cudaMemcpyDeviceToHost);
@@ -405,7 +420,8 @@ extern "C" int sb_tset_gemm_tc_host(sb_tset * t, const char * name, const float 
 // Mean device time of sb_tset_gemm_tc (activation quantization + product; the
 // weights' re-quantization, made once, is not timed) over nb host rows copied
 // once, a buffer larger than L2 rewritten before each run.
-extern "C" int sb_tset_time_gemm_tc(sb_tset * t, const char * name, const float * x, int nb, int reps, float * ms_avg) {
+extern "C" int sb_tset_time_gemm_tc(sb_tset * t, const char * name, const float * x, int nb, int split, int reps,
+                                    float * ms_avg) {
     const QT * q = find_qt(t, name);
     if (!q || nb < 1 || nb > kMaxBatch || reps < 1) return 0;
     float * dx = nullptr, * dy = nullptr;
@@ -421,11 +437,11 @@ extern "C" int sb_tset_time_gemm_tc(sb_tset * t, const char * name, const float 
         cudaEventCreate(&e0);
         cudaEventCreate(&e1);
         cudaMemcpy(dx, x, (size_t) nb * q->cols * 4, cudaMemcpyHostToDevice);
-        for (int r = 0; ok && r < 3; r++) ok = sb_tset_gemm_tc(t, name, dx, nb, dy, st);
+        for (int r = 0; ok && r < 3; r++) ok = sb_tset_gemm_tc(t, name, dx, nb, split, dy, st);
         for (int r = 0; ok && r < reps; r++) {
             cudaMemsetAsync(flush, r & 0xff, flush_n, st);
             cudaEventRecord(e0, st);
-            ok = sb_tset_gemm_tc(t, name, dx, nb, dy, st);
+            ok = sb_tset_gemm_tc(t, name, dx, nb, split, dy, st);
             cudaEventRecord(e1, st);
             ok = ok && cudaEventSynchronize(e1) == cudaSuccess;
             float ms = 0.0f;

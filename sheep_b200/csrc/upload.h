@@ -10,6 +10,7 @@
 #include "ssf.h"
 #include "tiles.h"
 
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <unordered_map>
@@ -223,6 +224,47 @@ inline bool upload_tt(Arena & a, const ssf_file & f, const ssf_rec * first, int 
     }
     cudaMemcpy(dev, host.data(), total, cudaMemcpyHostToDevice);
     return true;
+}
+
+// Features of a file the decode kernels do not implement (the reference's GPU
+// open refuses by name the same way, sml/sml-gpu-fwd.c:1833-1840), or NULL.
+inline const char * ssf_unsupported(const ssf_file & f) {
+    const ssf_hdr * h = f.hdr;
+    if (h->flags & SSF_FLAG_HADAMARD) return "Hadamard-rotated weights";
+    if (h->flags & SSF_FLAG_EXACT) return "an exact-weight (f32) file";
+    if (h->norm_type != 0) return "LayerNorm";
+    if (h->rope_type != 0) return "interleaved RoPE";
+    if (h->arch_bits) return "architecture flags beyond a plain decoder";
+    if (h->logit_softcap != 0.0f || h->attn_softcap != 0.0f) return "soft-capping";
+    if (h->n_swa) return "sliding-window attention";
+    if (h->emb_scale != 0.0f || h->res_scale != 0.0f || h->logit_scale != 0.0f) return "embedding/residual/logit scales";
+    if (h->clip_qkv != 0.0f) return "Q/K/V clamping";
+    const char * names[] = {"position_embd.weight", "token_embd_norm.weight", "output.bias", "rope_freqs",
+                            "attn_window", "attn_rope"};
+    for (const char * n : names) if (ssf_find(&f, n)) return n;
+    return nullptr;
+}
+
+// RoPE tables [n_ctx][hd/2] exactly as the CPU builds them (sml/sml-run.c:1383-1393).
+inline void upload_rope(float * dcos, float * dsin, int n_ctx, int hd, float theta) {
+    const int half = hd / 2;
+    std::vector<float> c((size_t) n_ctx * half), s((size_t) n_ctx * half);
+    for (int p = 0; p < n_ctx; p++)
+        for (int i = 0; i < half; i++) {
+            const float fr = powf(theta, -(float) i / (float) half);
+            const float a = (float) p * fr;
+            c[(size_t) p * half + i] = cosf(a);
+            s[(size_t) p * half + i] = sinf(a);
+        }
+    cudaMemcpy(dcos, c.data(), c.size() * 4, cudaMemcpyHostToDevice);
+    cudaMemcpy(dsin, s.data(), s.size() * 4, cudaMemcpyHostToDevice);
+}
+
+// Bytes of one record as the file stores it: codes and fields.
+inline uint64_t ssf_rec_bytes(const ssf_rec * r) {
+    uint64_t b = r->sd_n + r->sq_n + r->md_n + r->mq_n;
+    for (int p = 0; p < SSF_MAX_LEVELS; p++) b += r->codes_n[p];
+    return b;
 }
 
 }  // namespace sb

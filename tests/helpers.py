@@ -138,10 +138,55 @@ class Oracle:
         assert self.lib().so_gemm_sb(self.m, name.encode(), _p(X), len(X), _p(Y))
         return Y
 
+    def gemm_sb_split(self, name, X, rows, split):
+        X = np.ascontiguousarray(np.atleast_2d(X), np.float32)
+        Y = np.zeros((len(X), rows), np.float32)
+        assert self.lib().so_gemm_sb_split(self.m, name.encode(), _p(X), len(X), split, _p(Y))
+        return Y
+
     def close(self):
         if self.m:
             self.lib().so_close(self.m)
             self.m = None
+
+
+class OracleBatch:
+    """so_batch_*: ns sequences with their own caches; mode 0 the decode
+    arithmetic, mode 1 the batched (tensor-core) arithmetic."""
+
+    def __init__(self, orc, ns, mode, splits=None):
+        L = Oracle.lib()
+        L.so_batch_open.restype = ctypes.c_void_p
+        L.so_batch_open.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int]
+        L.so_batch_step.argtypes = [ctypes.c_void_p] * 4
+        L.so_batch_set_splits.argtypes = [ctypes.c_void_p, ctypes.c_void_p]
+        L.so_batch_close.argtypes = [ctypes.c_void_p]
+        self.orc, self.ns = orc, ns
+        self.b = ctypes.c_void_p(L.so_batch_open(orc.m, ns, mode))
+        if splits is not None:
+            sp = np.ascontiguousarray(splits, np.int32)
+            L.so_batch_set_splits(self.b, _p(sp))
+
+    def step(self, tokens, pos):
+        t = np.ascontiguousarray(tokens, np.int32)
+        p = np.ascontiguousarray(pos, np.int32)
+        lg = np.zeros((self.ns, self.orc.n_vocab), np.float32)
+        assert Oracle.lib().so_batch_step(self.b, _p(t), _p(p), _p(lg))
+        return lg
+
+    def kv(self, layer, slot, pos, n_kv_dim):
+        k = np.zeros(n_kv_dim, np.uint16)
+        v = np.zeros(n_kv_dim, np.uint16)
+        L = Oracle.lib()
+        L.so_batch_kv.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                  ctypes.c_void_p]
+        assert L.so_batch_kv(self.b, layer, slot, pos, _p(k), _p(v))
+        return k, v
+
+    def close(self):
+        if self.b:
+            Oracle.lib().so_batch_close(self.b)
+            self.b = None
 
 
 def oracle_quant(x):

@@ -128,3 +128,37 @@ def test_oracle_route_against_reference_vectors():
             assert np.array_equal(sel, g[f"sel_f{flags}"][t]), (flags, t)
             assert np.array_equal(w.view(np.uint32), g[f"w_f{flags}"][t].view(np.uint32)), (flags, t)
     assert list(g["sel_f1"][1]) == list(range(8))
+
+
+def test_oracle_batch_bookkeeping():
+    """The batched restatement keeps one cache per slot: in the decode
+    arithmetic (mode 0), ragged slots equal each sequence decoded alone, bit
+    for bit; the batched arithmetic (mode 1) stays near them."""
+    path = helpers.model_path(INDEX["decode_tiny.npz"]["spec"])
+    rng = np.random.default_rng(3)
+    ns, steps = 3, 7
+    starts = [0, 2, 3]
+    toks = rng.integers(0, 256, (ns, steps)).astype(np.int32)
+    orc = helpers.Oracle(path, n_ctx=32)
+    try:
+        ob0 = helpers.OracleBatch(orc, ns, 0)
+        ob1 = helpers.OracleBatch(orc, ns, 1, [1, 2, 1, 2, 1])
+        got0, got1 = {}, {}
+        for t in range(steps):
+            pos = np.array([t - s if t >= s else -1 for s in starts], np.int32)
+            tok = np.array([toks[s, max(p, 0)] for s, p in enumerate(pos)], np.int32)
+            l0, l1 = ob0.step(tok, pos), ob1.step(tok, pos)
+            for s in range(ns):
+                if pos[s] >= 0:
+                    got0[(s, pos[s])] = l0[s].copy()
+                    got1[(s, pos[s])] = l1[s].copy()
+        ob0.close()
+        ob1.close()
+        for s in range(ns):
+            for p in range(steps - starts[s]):
+                solo = orc.forward(int(toks[s, p]), p)   # the model's own cache, re-filled per sequence
+                assert np.array_equal(solo.view(np.uint32), got0[(s, p)].view(np.uint32)), (s, p)
+                assert helpers.rel_rms(solo, got1[(s, p)]) <= 6e-2
+            # the next sequence re-uses positions 0.. of the model's cache
+    finally:
+        orc.close()
