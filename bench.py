@@ -284,7 +284,7 @@ def main():
         extras = {"l2": "a 512 MB buffer rewritten before each timed run (decode: weights > L2)",
                   "gemv_cfg1": gemv_microbench(peak0), "gemm_tc_cfg1": gemm_tc_microbench(peak0),
                   "moe_cfg2": moe_microbench(peak0),
-                  "decode_cfg3": decode_cfg3(peak0)}
+                  "decode_cfg3": decode_cfg3(peak0), "decode_cfg3_batch64": decode_cfg3_batch(peak0)}
 
     if rank == 0:
         peak, peak_kind = peaks()
@@ -361,6 +361,47 @@ def decode_cfg3(peak, ngen=64):
                 "gbs": round(gbs, 1), "frac": round(gbs / peak, 4), "tokens": ngen}
     finally:
         eng.close()
+
+
+def decode_cfg3_batch(peak, n_seq=64, prompt=2048, ngen=256, nwarm=4):
+    """Configuration 3 as batched serving: n_seq sequences, each a `prompt`-id
+    random prompt stepped through the batched engine, then ngen greedy tokens
+    per sequence decoded together (one weight read per step, every product on
+    the tensor cores). Timed: the last ngen - 1 steps (CUDA events). Bytes per
+    step: the weights once (the file's Q4 bytes, the metric's algorithmic
+    figure, and the int8 re-quantized bytes the products actually read) plus
+    every sequence's KV cache up to its position."""
+    import sheep_b200
+    from sheep_b200 import configs
+    spec = configs.CONFIGS["llama3-8b-q4k"]
+    path = model_path(spec, 0, None)
+    n_ctx = prompt + nwarm + ngen
+    t0 = time.time()
+    b = sheep_b200.Batch(path, n_seq, n_ctx)
+    t_open = time.time() - t0
+    try:
+        prompts = np.random.default_rng(64).integers(0, b.n_vocab, (n_seq, prompt)).astype(np.int32)
+        t0 = time.time()
+        ids, ms = b.generate(prompts, ngen, nwarm=nwarm, timed=True)
+        t_run = time.time() - t0
+        steps = ngen - 1
+        tps = n_seq * steps / (ms / 1000.0)
+        kv_row = spec["n_layer"] * 2 * spec["n_head_kv"] * spec["head_dim"] * 2   # bytes per position per sequence
+        first = prompt + nwarm + 1                        # positions of the timed steps: first .. first + steps - 1
+        kv_step = n_seq * kv_row * (first + (steps - 1) / 2.0 + 1)   # mean cached positions read per step
+        alg = b.file_bytes + kv_step
+        real = b.int8_bytes + kv_step
+        return {"n_seq": n_seq, "prompt": prompt, "generated": ngen, "tok_s": round(tps, 1),
+                "ms_per_step": round(ms / steps, 4), "bytes_per_step_alg": int(alg),
+                "gbs_alg": round(alg * steps / (ms / 1000.0) / 1e9, 1),
+                "frac_alg": round(alg * steps / (ms / 1000.0) / 1e9 / peak, 4),
+                "bytes_per_step_read": int(real), "gbs_read": round(real * steps / (ms / 1000.0) / 1e9, 1),
+                "frac_read": round(real * steps / (ms / 1000.0) / 1e9 / peak, 4),
+                "splits_qkv_o_gu_down_head": b.splits, "launches_per_step": b.launches,
+                "open_s": round(t_open, 1), "run_s": round(t_run, 1),
+                "ids_distinct": int(len(np.unique(ids)))}
+    finally:
+        b.close()
 
 
 def gemm_tc_microbench(peak, reps=20):

@@ -95,7 +95,7 @@ struct sb_batch {
     uint8_t * xblk = nullptr;
     float * xs = nullptr, * part = nullptr, * apart = nullptr;
     unsigned * cnt = nullptr, * acnt = nullptr;
-    int max_chunks = 0;
+    int attn_split = 1, attn_hg = 4, attn_groups = 1;
     int * err = nullptr;
     cudaStream_t st = nullptr;
     cudaGraphExec_t g = nullptr;
@@ -267,10 +267,23 @@ static bool b_build(sb_batch * b, char * why, int nwhy) {
     b->xs = (float *) b->ar.carve((size_t) Tp * nsb_max * 4);
     b->part = (float *) b->ar.carve(part ? part * 4 : 16);
     b->cnt = (unsigned *) b->ar.carve(tiles * 4);
-    b->max_chunks = (b->n_ctx + kBChunk - 1) / kBChunk;
+    // attention: head groups of attn_hg query heads; the positions of a
+    // (sequence, group) split over attn_split CTAs so that the grid fills the
+    // SMs' resident slots in whole waves (two CTAs per SM up to hd 128)
     const int rep = b->nh / b->nkv;
-    b->apart = (float *) b->ar.carve((size_t) B * b->nkv * b->max_chunks * rep * (b->hd + 2) * 4);
-    b->acnt = (unsigned *) b->ar.carve((size_t) B * b->nkv * 4);
+    b->attn_hg = battn_hg(rep);
+    b->attn_groups = (rep + b->attn_hg - 1) / b->attn_hg;
+    {
+        const int pairs = B * b->nkv * b->attn_groups, slots = (b->hd <= 128 ? 2 : 1) * b->nsm;
+        double best = 1e30;
+        for (int n = 1; n <= 16; n++) {
+            const double cost = (double) ((pairs * n + slots - 1) / slots) / n + 0.02 * n;
+            if (cost < best - 1e-9) { best = cost; b->attn_split = n; }
+        }
+    }
+    b->apart = (float *) b->ar.carve((size_t) B * b->nkv * b->attn_groups * b->attn_split * b->attn_hg *
+                                     (b->hd + 2) * 4);
+    b->acnt = (unsigned *) b->ar.carve((size_t) B * b->nkv * b->attn_groups * 4);
     b->err = (int *) b->ar.carve(4);
     return true;
 }
@@ -303,6 +316,21 @@ static void b_mma(sb_batch * b, const BGemm & gm, float * y, int ldy, const floa
     b_after(b, tc_mma(a, b->st));
 }
 
+// Launch (or, with attr, set the shared-memory limit of) k_battn<hd, hg>.
+static cudaError_t b_attn_launch(int hd, int hg, dim3 grid, size_t smem, cudaStream_t st, const BAttnArgs & a,
+                                 bool attr) {
+#define SB_BATTN(HD, HG)                                                                                   \
+    if (hd == HD && hg == HG) {                                                                             \
+        if (attr) return cudaFuncSetAttribute(k_battn<HD, HG>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                              (int) smem);                                                  \
+        k_battn<HD, HG><<<grid, kBThreads, smem, st>>>(a);                                                  \
+        return cudaGetLastError();                                                                          \
+    }
+    SB_BATTN(64, 4) SB_BATTN(64, 8) SB_BATTN(128, 4) SB_BATTN(128, 8) SB_BATTN(256, 4) SB_BATTN(256, 8)
+#undef SB_BATTN
+    return cudaErrorInvalidValue;
+}
+
 static void b_attn(sb_batch * b, const BLayer & y, int l) {
     BAttnArgs a;
     memset(&a, 0, sizeof a);
@@ -312,18 +340,11 @@ static void b_attn(sb_batch * b, const BLayer & y, int l) {
     const size_t per_layer = (size_t) b->B * b->nkv * b->n_ctx * b->hd;
     a.kc = b->kc + (size_t) l * per_layer;
     a.vc = b->vc + (size_t) l * per_layer;
-    a.n_ctx = b->n_ctx; a.pos = b->pos; a.max_chunks = b->max_chunks; a.scale = b->scale;
+    a.n_ctx = b->n_ctx; a.pos = b->pos; a.nsplit = b->attn_split; a.hgroups = b->attn_groups; a.scale = b->scale;
     a.part = b->apart; a.cnt = b->acnt; a.out = b->att; a.ldo = b->qd; a.err = b->err;
-    const dim3 grid(b->max_chunks, b->nkv, b->B);
-    const size_t smem = battn_smem(b->hd, b->nh / b->nkv);
-    cudaError_t r;
-    switch (b->hd) {
-    case 64: k_battn<64><<<grid, kBThreads, smem, b->st>>>(a); break;
-    case 128: k_battn<128><<<grid, kBThreads, smem, b->st>>>(a); break;
-    default: k_battn<256><<<grid, kBThreads, smem, b->st>>>(a); break;
-    }
-    r = cudaGetLastError();
-    b_after(b, r);
+    const dim3 grid(b->attn_split, b->nkv * b->attn_groups, b->B);
+    const size_t smem = battn_smem(b->hd, b->attn_hg);
+    b_after(b, b_attn_launch(b->hd, b->attn_hg, grid, smem, b->st, a, false));
 }
 
 static void b_enqueue(sb_batch * b) {
@@ -416,10 +437,9 @@ extern "C" sb_batch * sb_batch_open(const char * path, int n_seq, int n_ctx, cha
     }
     if (!b_build(b, why, nwhy)) return b_fail(b, why, nwhy, nullptr);
     upload_rope(b->rcos, b->rsin, b->n_ctx, b->hd, b->theta);
-    const int smem = (int) battn_smem(b->hd, b->nh / b->nkv);
-    cudaError_t ar = b->hd == 64 ? cudaFuncSetAttribute(k_battn<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)
-                   : b->hd == 128 ? cudaFuncSetAttribute(k_battn<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem)
-                   : cudaFuncSetAttribute(k_battn<256>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    BAttnArgs none;
+    memset(&none, 0, sizeof none);
+    const cudaError_t ar = b_attn_launch(b->hd, b->attn_hg, dim3(1), battn_smem(b->hd, b->attn_hg), b->st, none, true);
     if (!bck(ar, "attention shared memory") || !bck(cudaMallocHost(&b->h_logits, (size_t) b->B * b->V * 4), "pinned logits") ||
         !bck(cudaMallocHost(&b->h_io, (size_t) 2 * b->B * 4), "pinned io"))
         return b_fail(b, why, nwhy, g_berr);

@@ -5,8 +5,10 @@
 //
 //   k_bembed    the B embedding rows, dequantized and scattered to natural order
 //   k_battn     RoPE, the KV write and split-position attention, one CTA per
-//               (128 positions, KV head, sequence) serving every query head
-//               of the KV head's group, so each cached byte is read once
+//               (run of positions, KV head, sequence) streaming 64-position
+//               chunks through a bulk-copy ring with an online softmax, and
+//               serving up to 8 query heads of the KV head, so each cached
+//               byte is read once per step (GQA groups of <= 8)
 //   k_bargmax   the greedy choice per sequence, fed back as its next token
 //
 // The CPU body these follow is sml_forward_multi / forward_slots
@@ -18,7 +20,7 @@
 
 namespace sb {
 
-constexpr int kBChunk = 128;     // positions per attention CTA
+constexpr int kBChunk = 64;      // positions per attention ring stage
 constexpr int kBThreads = 256;
 constexpr int kBMaxRep = 32;     // query heads per KV head
 constexpr int kMaxBatchSeqs = 256;
@@ -48,57 +50,71 @@ struct BAttnArgs {
     uint16_t * kc, * vc;     // this layer's cache: [B][n_kv][n_ctx][hd] fp16
     int n_ctx;
     const int * pos;         // [B]; < 0: an idle slot
-    int max_chunks;
+    int nsplit;              // CTAs sharing one (sequence, head group)'s positions
+    int hgroups;             // head groups per KV head (ceil(rep / HG))
     float scale;             // 1/sqrt(hd)
-    float * part;            // [B][n_kv][max_chunks][rep][hd + 2]: max, sum, weighted values
-    unsigned * cnt;          // [B][n_kv] arrivals, zero between steps
+    float * part;            // [B][n_kv * hgroups][nsplit][HG][hd + 2]: max, sum, weighted values
+    unsigned * cnt;          // [B][n_kv * hgroups] arrivals, zero between steps
     float * out;             // [B][ldo] attention output (head-major)
     int ldo;
     int * err;
 };
 
-// Shared memory of k_battn: the chunk's keys and values, the group's rotated
-// queries, the new key and value, the RoPE row and the scores.
-__host__ __device__ inline size_t battn_smem(int hd, int rep) {
-    const int rp = (rep + 3) / 4 * 4;
-    return (size_t) 2 * kBChunk * hd * 2 + (size_t) (rp * hd + 3 * hd) * 4 + (size_t) kBChunk * rp * 4 + 16;
+// Ring stages of 64 positions' keys and values, and query heads per CTA.
+__host__ __device__ constexpr int battn_stages(int hd) { return hd <= 128 ? 3 : 2; }
+__host__ __device__ inline int battn_hg(int rep) { return rep <= 4 ? 4 : 8; }
+
+// Shared memory of k_battn: the ring (reused at the end for the warps' sums),
+// the group's rotated queries, the new key and value, the RoPE row, the scores.
+__host__ __device__ inline size_t battn_smem(int hd, int hg) {
+    const size_t ring = (size_t) battn_stages(hd) * 2 * kBChunk * hd * 2;
+    const size_t ro = (size_t) (kBThreads / 32) * hg * hd * 4;
+    return (ring > ro ? ring : ro) + (size_t) (hg * hd + 3 * hd) * 4 + (size_t) kBChunk * hg * 4 + 16;
 }
 
-// One CTA per (chunk of 128 positions, KV head, sequence).
-//  1. one thread starts bulk copies of the chunk's keys and values (contiguous
-//     in the cache layout) while every thread loads the group's queries and the
-//     new key/value, applies the Q/K norms and RoPE (sml/sml-run.c:295-375);
-//  2. the chunk owning `pos` writes the new key/value (fp16, round to nearest
-//     even) into its copy and into the cache;
-//  3. scores: a team of 8 lanes (16 for hd 256) per position, each lane 16 B
-//     column pieces of the key row (a team reads 128 contiguous bytes) against
-//     the queries of 4 heads held in registers, summed across the team;
-//  4. per head, the max-subtracted softmax of the chunk (expf);
-//  5. weighted values: each warp a stride of positions, each lane hd/32
-//     columns, the 4 heads' weights of a position read as one float4; the
-//     warps' sums added in warp order;
-//  6. chunks meet in `part`; the last CTA of the (sequence, KV head) combines
-//     them in chunk order (flash-decoding partials, as k_attn).
-template <int HD>
-__global__ void __launch_bounds__(kBThreads) k_battn(const __grid_constant__ BAttnArgs g) {
+// One CTA per (split of the positions, KV head x head group, sequence); the
+// HG query heads of the group share every key and value the CTA reads.
+//  1. thread 0 starts bulk copies of the split's first chunks of 64 positions
+//     (keys and values contiguous in the cache layout) into a ring, while every
+//     thread loads the group's queries and the new key/value and applies the
+//     Q/K norms and RoPE (sml/sml-run.c:295-375);
+//  2. per chunk, once it has landed: the chunk owning `pos` takes the new key
+//     and value (fp16, round to nearest even; the head group 0 CTA also writes
+//     them to the cache); scores by teams of 8 lanes (16 for hd 256) per
+//     position, each lane 16-byte column pieces of the key row against 4 heads'
+//     queries in registers, summed across the team; the online softmax per
+//     head (running max and sum, expf; sml/sml-run.c:180-266 takes it over all
+//     positions at once); weighted values, each warp a stride of positions and
+//     each lane hd/32 columns, its running sums rescaled by the max's change;
+//     then the stage is refilled with the chunk `stages` ahead;
+//  3. the warps' sums added in warp order; one split alone writes the output,
+//     several meet in `part` and the last to arrive combines them in split
+//     order (flash-decoding partials).
+template <int HD, int HG>
+__global__ void __launch_bounds__(kBThreads, 2) k_battn(const __grid_constant__ BAttnArgs g) {
+    constexpr int S = battn_stages(HD);
     constexpr int LPP = HD <= 128 ? 8 : 16;   // lanes per position in the scores
     constexpr int NCH = HD / 8;                // 16-byte pieces per key row
     constexpr int CPL = NCH / LPP;             // pieces per lane (1 or 2)
     constexpr int PPW = 32 / LPP;              // positions per warp step
     constexpr int DV = HD / 32;                // columns per lane in the weighted sum
+    constexpr int NW = kBThreads / 32;
+    constexpr size_t RING = (size_t) S * 2 * kBChunk * HD * 2;
+    constexpr size_t RO = (size_t) NW * HG * HD * 4;
     extern __shared__ __align__(16) uint8_t bsm[];
-    __shared__ __align__(8) uint64_t bar;
-    __shared__ double red[kBThreads / 32];
-    __shared__ float hm[kBMaxRep], hl[kBMaxRep];
+    __shared__ __align__(8) uint64_t full[S];
+    __shared__ double red[NW];
+    __shared__ float hm[HG], hl[HG], ha[HG];
     __shared__ unsigned last_flag;
-    const int c = blockIdx.x, kvh = blockIdx.y, b = blockIdx.z;
+    const int split = blockIdx.x, gy = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int rep = g.n_head / g.n_kv, rp = (rep + 3) / 4 * 4;
+    const int rep = g.n_head / g.n_kv;
+    const int kvh = gy / g.hgroups, h0 = (gy % g.hgroups) * HG, nh = min(HG, rep - h0);
     const int pos = g.pos[b];
-    float * outb = g.out + (size_t) b * g.ldo + (size_t) kvh * rep * HD;
+    float * outb = g.out + (size_t) b * g.ldo + ((size_t) kvh * rep + h0) * HD;
     if (pos < 0) {
-        if (c == 0)
-            for (int i = tid; i < rep * HD; i += kBThreads) outb[i] = 0.0f;
+        if (split == 0)
+            for (int i = tid; i < nh * HD; i += kBThreads) outb[i] = 0.0f;
         return;
     }
     if (pos >= g.n_ctx || rep > kBMaxRep) {
@@ -106,121 +122,142 @@ __global__ void __launch_bounds__(kBThreads) k_battn(const __grid_constant__ BAt
         return;
     }
     const int nchunk = pos / kBChunk + 1;
-    if (c >= nchunk) return;
-    const int t0 = c * kBChunk, nt = min(pos + 1, t0 + kBChunk) - t0;
-    uint16_t * Ks = reinterpret_cast<uint16_t *>(bsm);          // [kBChunk][HD]
-    uint16_t * Vs = Ks + kBChunk * HD;                           // [kBChunk][HD]
-    float * qs = reinterpret_cast<float *>(Vs + kBChunk * HD);   // [rp][HD]
-    float * kn = qs + rp * HD, * vn = kn + HD, * cs = vn + HD, * sn = cs + HD / 2;
-    float * sc = sn + HD / 2;                                    // [kBChunk][rp]
-    float * ro = reinterpret_cast<float *>(bsm);                 // [8 warps][4][HD], over Ks after the scores
+    const int per = (nchunk + g.nsplit - 1) / g.nsplit;
+    const int nact = (nchunk + per - 1) / per;   // splits with positions
+    const int c0 = split * per, c1 = min(nchunk, c0 + per);
+    if (c0 >= nchunk) return;
+    const int nmine = c1 - c0;
+    uint16_t * ring = reinterpret_cast<uint16_t *>(bsm);
+    float * qs = reinterpret_cast<float *>(bsm + (RING > RO ? RING : RO));   // [HG][HD]
+    float * kn = qs + HG * HD, * vn = kn + HD, * cs = vn + HD, * sn = cs + HD / 2;
+    float * sc = sn + HD / 2;                                                // [kBChunk][HG]
+    float * ro = reinterpret_cast<float *>(bsm);                             // [NW][HG][HD] at the end
     const size_t row0 = ((size_t) b * g.n_kv + kvh) * g.n_ctx;
 
     if (tid == 0) {
-        mbar_init(&bar, 1);
+        for (int s = 0; s < S; s++) mbar_init(&full[s], 1);
         mbar_fence_init();
     }
     __syncthreads();
-    if (tid == 0) {
+    auto issue = [&](int j) {   // chunk c0 + j into stage j % S
+        const int t0 = (c0 + j) * kBChunk, nt = min(pos + 1, t0 + kBChunk) - t0;
+        uint16_t * Ks = ring + (size_t) (j % S) * 2 * kBChunk * HD;
         const uint32_t bytes = (uint32_t) nt * HD * 2;
-        mbar_expect_tx(&bar, 2 * bytes);
-        bulk_g2s(Ks, g.kc + (row0 + t0) * HD, bytes, &bar);
-        bulk_g2s(Vs, g.vc + (row0 + t0) * HD, bytes, &bar);
-    }
+        mbar_expect_tx(&full[j % S], 2 * bytes);
+        bulk_g2s(Ks, g.kc + (row0 + t0) * HD, bytes, &full[j % S]);
+        bulk_g2s(Ks + kBChunk * HD, g.vc + (row0 + t0) * HD, bytes, &full[j % S]);
+    };
+    if (tid == 0)
+        for (int j = 0; j < S && j < nmine; j++) issue(j);
     const float * qrow = g.qkv + (size_t) b * g.ldq;
     for (int i = tid; i < HD / 2; i += kBThreads) {
         cs[i] = g.rcos[(size_t) pos * (HD / 2) + i];
         sn[i] = g.rsin[(size_t) pos * (HD / 2) + i];
     }
-    for (int i = tid; i < rp * HD; i += kBThreads)
-        qs[i] = i < rep * HD ? qrow[(size_t) kvh * rep * HD + i] : 0.0f;
+    for (int i = tid; i < HG * HD; i += kBThreads)
+        qs[i] = i < nh * HD ? qrow[((size_t) kvh * rep + h0) * HD + i] : 0.0f;
     for (int i = tid; i < HD; i += kBThreads) {
         kn[i] = qrow[g.koff + kvh * HD + i];
         vn[i] = qrow[g.voff + kvh * HD + i];
     }
+    if (tid < HG) { hm[tid] = -INFINITY; hl[tid] = 0.0f; }
     __syncthreads();
-    for (int h = 0; h < rep; h++) norm_rope(qs + h * HD, g.qn, g.eps, HD, cs, sn, red);
+    for (int h = 0; h < nh; h++) norm_rope(qs + h * HD, g.qn, g.eps, HD, cs, sn, red);
     norm_rope(kn, g.kn, g.eps, HD, cs, sn, red);
-    const bool landed = mbar_wait(&bar, 0, g.err, 212);
-    if (pos < t0 + nt && landed) {
-        const int r = pos - t0;
-        for (int i = tid; i < HD; i += kBThreads) {
-            const uint16_t kh = f2h(kn[i]), vh = f2h(vn[i]);
-            Ks[r * HD + i] = kh;
-            Vs[r * HD + i] = vh;
-            g.kc[(row0 + pos) * HD + i] = kh;
-            g.vc[(row0 + pos) * HD + i] = vh;
-        }
-    }
-    __syncthreads();
-    if (!landed) return;
 
-    // ---- scores (sml/sml-run.c:180-235: dot * 1/sqrt(hd))
+    float o[HG][DV];
+#pragma unroll
+    for (int h = 0; h < HG; h++)
+#pragma unroll
+        for (int d = 0; d < DV; d++) o[h][d] = 0.0f;
     const int team = lane / LPP, tl = lane % LPP;
-    for (int hg = 0; hg < rp; hg += 4) {
-        float qr[4][CPL * 8];
+    bool ok = true;
+    for (int j = 0; j < nmine; j++) {
+        const int c = c0 + j, t0 = c * kBChunk, nt = min(pos + 1, t0 + kBChunk) - t0;
+        uint16_t * Ks = ring + (size_t) (j % S) * 2 * kBChunk * HD, * Vs = Ks + kBChunk * HD;
+        ok = mbar_wait(&full[j % S], (uint32_t) (j / S) & 1u, g.err, 212) && ok;
+        if (c == nchunk - 1 && ok) {
+            const int r = pos - t0;
+            for (int i = tid; i < HD; i += kBThreads) {
+                const uint16_t kh = f2h(kn[i]), vh = f2h(vn[i]);
+                Ks[r * HD + i] = kh;
+                Vs[r * HD + i] = vh;
+                if (h0 == 0) {
+                    g.kc[(row0 + pos) * HD + i] = kh;
+                    g.vc[(row0 + pos) * HD + i] = vh;
+                }
+            }
+        }
+        ok = __syncthreads_and(ok) != 0;   // one verdict for the whole CTA
+        if (!ok) break;
+        // ---- scores (sml/sml-run.c:180-235: dot * 1/sqrt(hd))
 #pragma unroll
-        for (int h = 0; h < 4; h++)
+        for (int hg = 0; hg < HG; hg += 4) {
+            float qr[4][CPL * 8];
 #pragma unroll
-            for (int k = 0; k < CPL; k++)
+            for (int h = 0; h < 4; h++)
 #pragma unroll
-                for (int j = 0; j < 8; j++) qr[h][k * 8 + j] = qs[(hg + h) * HD + (tl + k * LPP) * 8 + j];
-        for (int p0 = 0; p0 < nt; p0 += (kBThreads / 32) * PPW) {
-            const int p = p0 + warp * PPW + team;
-            float s[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-            if (p < nt) {
+                for (int k = 0; k < CPL; k++)
 #pragma unroll
-                for (int k = 0; k < CPL; k++) {
-                    const uint4 w = *reinterpret_cast<const uint4 *>(Ks + p * HD + (tl + k * LPP) * 8);
-                    const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+                    for (int jj = 0; jj < 8; jj++) qr[h][k * 8 + jj] = qs[(hg + h) * HD + (tl + k * LPP) * 8 + jj];
+            for (int p0 = 0; p0 < nt; p0 += NW * PPW) {
+                const int p = p0 + warp * PPW + team;
+                float s4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+                if (p < nt) {
 #pragma unroll
-                    for (int j = 0; j < 4; j++) {
-                        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&wv[j]));
+                    for (int k = 0; k < CPL; k++) {
+                        const uint4 w = *reinterpret_cast<const uint4 *>(Ks + p * HD + (tl + k * LPP) * 8);
+                        const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-                        for (int h = 0; h < 4; h++) {
-                            s[h] = fmaf(qr[h][k * 8 + 2 * j], f.x, s[h]);
-                            s[h] = fmaf(qr[h][k * 8 + 2 * j + 1], f.y, s[h]);
+                        for (int jj = 0; jj < 4; jj++) {
+                            const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&wv[jj]));
+#pragma unroll
+                            for (int h = 0; h < 4; h++) {
+                                s4[h] = fmaf(qr[h][k * 8 + 2 * jj], f.x, s4[h]);
+                                s4[h] = fmaf(qr[h][k * 8 + 2 * jj + 1], f.y, s4[h]);
+                            }
                         }
                     }
                 }
+#pragma unroll
+                for (int off = LPP / 2; off; off >>= 1)
+#pragma unroll
+                    for (int h = 0; h < 4; h++) s4[h] += __shfl_xor_sync(0xffffffffu, s4[h], off);
+                if (p < nt && tl == 0)
+                    *reinterpret_cast<float4 *>(sc + p * HG + hg) =
+                        make_float4(s4[0] * g.scale, s4[1] * g.scale, s4[2] * g.scale, s4[3] * g.scale);
             }
-#pragma unroll
-            for (int o = LPP / 2; o; o >>= 1)
-#pragma unroll
-                for (int h = 0; h < 4; h++) s[h] += __shfl_xor_sync(0xffffffffu, s[h], o);
-            if (p < nt && tl == 0)
-                *reinterpret_cast<float4 *>(sc + p * rp + hg) =
-                    make_float4(s[0] * g.scale, s[1] * g.scale, s[2] * g.scale, s[3] * g.scale);
         }
-    }
-    __syncthreads();
-
-    // ---- softmax of the chunk, per head (max-subtracted, expf)
-    for (int h = warp; h < rep; h += kBThreads / 32) {
-        float m = -INFINITY;
-        for (int p = lane; p < nt; p += 32) m = fmaxf(m, sc[p * rp + h]);
-        m = warp_max(m);
-        float l = 0.0f;
-        for (int p = lane; p < nt; p += 32) {
-            const float e = expf(sc[p * rp + h] - m);
-            sc[p * rp + h] = e;
-            l += e;
+        __syncthreads();
+        // ---- online softmax, one warp per head
+        if (warp < nh) {
+            float mc = -INFINITY;
+            for (int p = lane; p < nt; p += 32) mc = fmaxf(mc, sc[p * HG + warp]);
+            mc = warp_max(mc);
+            const float mo = hm[warp], mn = fmaxf(mo, mc);
+            float l = 0.0f;
+            for (int p = lane; p < nt; p += 32) {
+                const float e = expf(sc[p * HG + warp] - mn);
+                sc[p * HG + warp] = e;
+                l += e;
+            }
+            l = warp_sum(l);
+            if (lane == 0) {
+                const float a = expf(mo - mn);
+                ha[warp] = a;
+                hl[warp] = hl[warp] * a + l;
+                hm[warp] = mn;
+            }
         }
-        l = warp_sum(l);
-        if (lane == 0) { hm[h] = m; hl[h] = l; }
-    }
-    __syncthreads();
-
-    // ---- weighted values
-    float * pb = g.part + ((row0 / g.n_ctx) * g.max_chunks + c) * (size_t) rep * (HD + 2);
-    for (int hg = 0; hg < rp; hg += 4) {
-        float o[4][DV];
+        __syncthreads();
+        // ---- weighted values
 #pragma unroll
-        for (int h = 0; h < 4; h++)
+        for (int h = 0; h < HG; h++) {
+            const float a = h < nh ? ha[h] : 0.0f;
 #pragma unroll
-            for (int d = 0; d < DV; d++) o[h][d] = 0.0f;
-        for (int p = warp; p < nt; p += kBThreads / 32) {
-            const float4 pr = *reinterpret_cast<const float4 *>(sc + p * rp + hg);
+            for (int d = 0; d < DV; d++) o[h][d] *= a;
+        }
+        for (int p = warp; p < nt; p += NW) {
             float v[DV];
             if constexpr (DV == 2) {
                 const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(Vs + p * HD + lane * 2));
@@ -235,57 +272,64 @@ __global__ void __launch_bounds__(kBThreads) k_battn(const __grid_constant__ BAt
                 }
             }
 #pragma unroll
-            for (int d = 0; d < DV; d++) {
-                o[0][d] = fmaf(pr.x, v[d], o[0][d]);
-                o[1][d] = fmaf(pr.y, v[d], o[1][d]);
-                o[2][d] = fmaf(pr.z, v[d], o[2][d]);
-                o[3][d] = fmaf(pr.w, v[d], o[3][d]);
+            for (int hg = 0; hg < HG; hg += 4) {
+                const float4 pr = *reinterpret_cast<const float4 *>(sc + p * HG + hg);
+#pragma unroll
+                for (int d = 0; d < DV; d++) {
+                    o[hg][d] = fmaf(pr.x, v[d], o[hg][d]);
+                    o[hg + 1][d] = fmaf(pr.y, v[d], o[hg + 1][d]);
+                    o[hg + 2][d] = fmaf(pr.z, v[d], o[hg + 2][d]);
+                    o[hg + 3][d] = fmaf(pr.w, v[d], o[hg + 3][d]);
+                }
             }
         }
-        __syncthreads();   // the keys (under ro) are no longer read; the previous group's sums are taken
-#pragma unroll
-        for (int h = 0; h < 4; h++)
-#pragma unroll
-            for (int d = 0; d < DV; d++) ro[(warp * 4 + h) * HD + lane * DV + d] = o[h][d];
-        __syncthreads();
-        for (int i = tid; i < 4 * HD; i += kBThreads) {
-            const int h = i / HD, d = i % HD;
-            if (hg + h >= rep) continue;
-            float s = 0.0f;
-#pragma unroll
-            for (int w = 0; w < kBThreads / 32; w++) s += ro[(w * 4 + h) * HD + d];
-            if (nchunk == 1) outb[(hg + h) * HD + d] = s / hl[hg + h];
-            else pb[(hg + h) * (HD + 2) + 2 + d] = s;
-        }
+        __syncthreads();   // the stage and the scores are free
+        if (tid == 0 && j + S < nmine) issue(j + S);
     }
-    if (nchunk == 1) return;
-    if (tid < rep) {
+    if (!ok) return;
+    // ---- the warps' sums, in warp order (the ring is free: every copy landed)
+#pragma unroll
+    for (int h = 0; h < HG; h++)
+#pragma unroll
+        for (int d = 0; d < DV; d++) ro[(warp * HG + h) * HD + lane * DV + d] = o[h][d];
+    __syncthreads();
+    const size_t grp = (size_t) b * g.n_kv * g.hgroups + gy;
+    float * pb = g.part + (grp * g.nsplit + split) * HG * (HD + 2);
+    for (int i = tid; i < nh * HD; i += kBThreads) {
+        const int h = i / HD, d = i % HD;
+        float s = 0.0f;
+#pragma unroll
+        for (int w = 0; w < NW; w++) s += ro[(w * HG + h) * HD + d];
+        if (nact == 1) outb[h * HD + d] = s / hl[h];
+        else pb[h * (HD + 2) + 2 + d] = s;
+    }
+    if (nact == 1) return;
+    if (tid < nh) {
         pb[tid * (HD + 2)] = hm[tid];
         pb[tid * (HD + 2) + 1] = hl[tid];
     }
     __threadfence();
     __syncthreads();
-    unsigned * cnt = g.cnt + (size_t) b * g.n_kv + kvh;
-    if (tid == 0) last_flag = atomicAdd(cnt, 1u) == (unsigned) nchunk - 1;
+    if (tid == 0) last_flag = atomicAdd(&g.cnt[grp], 1u) == (unsigned) nact - 1;
     __syncthreads();
     if (!last_flag) return;
     __threadfence();
-    // the last chunk combines every chunk of the group, in chunk order
-    const volatile float * P = g.part + (row0 / g.n_ctx) * g.max_chunks * (size_t) rep * (HD + 2);
-    const size_t cst = (size_t) rep * (HD + 2);
-    for (int i = tid; i < rep * HD; i += kBThreads) {
+    // the last split combines every split of the group, in split order
+    const float * P = g.part + grp * g.nsplit * HG * (HD + 2);
+    const size_t sst = (size_t) HG * (HD + 2);
+    for (int i = tid; i < nh * HD; i += kBThreads) {
         const int h = i / HD, d = i % HD;
         float M = -INFINITY;
-        for (int k = 0; k < nchunk; k++) M = fmaxf(M, P[k * cst + h * (HD + 2)]);
-        float L = 0.0f, o = 0.0f;
-        for (int k = 0; k < nchunk; k++) {
-            const float e = expf(P[k * cst + h * (HD + 2)] - M);
-            L += P[k * cst + h * (HD + 2) + 1] * e;
-            o += P[k * cst + h * (HD + 2) + 2 + d] * e;
+        for (int k = 0; k < nact; k++) M = fmaxf(M, __ldcg(P + k * sst + h * (HD + 2)));
+        float L = 0.0f, ov = 0.0f;
+        for (int k = 0; k < nact; k++) {
+            const float e = expf(__ldcg(P + k * sst + h * (HD + 2)) - M);
+            L += __ldcg(P + k * sst + h * (HD + 2) + 1) * e;
+            ov += __ldcg(P + k * sst + h * (HD + 2) + 2 + d) * e;
         }
-        outb[h * HD + d] = o / L;
+        outb[h * HD + d] = ov / L;
     }
-    if (tid == 0) *cnt = 0;
+    if (tid == 0) g.cnt[grp] = 0;
 }
 
 // Greedy choice per sequence: the first index of the largest logit

@@ -72,11 +72,12 @@ __global__ void __launch_bounds__(256) k_requant8(const __grid_constant__ QT t, 
         make_uint2(w[0], w[1]);
 }
 
-// One CTA per row of x (token): the row's values in the tensor's column order
-// (plain; RMS-normalized with a gain, the norm's sum of squares in double as
-// the decode GEMVs take it; or SiLU(gate) * up from a row holding gate | up),
-// quantized per 256 into the B operand blocks (N tokens per block) and the
-// per-superblock scales. Rows past T are zeros.
+// One CTA per (row of x, 8 superblocks), one warp per superblock: the row's
+// values in the tensor's column order (plain; RMS-normalized with a gain, the
+// norm's sum of squares over the whole row in double as the decode GEMVs take
+// it; or SiLU(gate) * up from a row holding gate | up), quantized per 256 into
+// the B operand blocks (N tokens per block) and the per-superblock scales.
+// Rows past T are zeros.
 template <int MODE>
 __global__ void __launch_bounds__(256) k_quant_rows(const TcQuantArgs a) {
     __shared__ double red[8];
@@ -95,7 +96,8 @@ __global__ void __launch_bounds__(256) k_quant_rows(const TcQuantArgs a) {
         for (int k = 0; k < 8; k++) ss += red[k];
         s = __fdiv_rn(1.0f, sqrtf(__fadd_rn((float) (ss / a.cols), a.eps)));
     }
-    for (int sb = warp; sb < a.nsb; sb += 8) {
+    const int sb = blockIdx.y * 8 + warp;
+    if (sb < a.nsb) {
         const int k0 = lane * 8;
         float v[8];
         float amax = 0.0f;
@@ -236,25 +238,33 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
             if (!last) ok = false;
             else {
                 __threadfence();
+                // slice-outer: a slice's N loads are independent and issue together
 #pragma unroll
-                for (int t = 0; t < N; t++) {
-                    float s = 0.0f;
-                    for (int k = 0; k < g.split; k++)
-                        s = __fadd_rn(s, __ldcg(g.part + ((size_t) k * g.T_pad + tb * N + t) * g.rows_pad + r));
-                    acc[t] = s;
+                for (int t = 0; t < N; t++) acc[t] = 0.0f;
+                for (int k = 0; k < g.split; k++) {
+                    const float * pk = g.part + ((size_t) k * g.T_pad + tb * N) * g.rows_pad + r;
+#pragma unroll
+                    for (int t = 0; t < N; t++) acc[t] = __fadd_rn(acc[t], __ldcg(pk + (size_t) t * g.rows_pad));
                 }
                 if (warp == 2 && lane == 0) g.cnt[mb * gridDim.y + tb] = 0;
             }
         }
         if (ok && r < g.rows) {
-            const float b = g.bias ? g.bias[r] : 0.0f;
+            const int nt = min(N, g.T - tb * N);
+            float * yr = g.y + (size_t) tb * N * g.ldy + r;
+            if (g.accumulate) {
+                // every token's old value read before any is written (they never alias)
+                float old[N];
 #pragma unroll
-            for (int t = 0; t < N; t++) {
-                const int tok = tb * N + t;
-                if (tok < g.T) {
-                    float * yp = g.y + (size_t) tok * g.ldy + r;
-                    *yp = g.accumulate ? __fadd_rn(*yp, acc[t]) : g.bias ? __fadd_rn(acc[t], b) : acc[t];
-                }
+                for (int t = 0; t < N; t++) old[t] = t < nt ? yr[(size_t) t * g.ldy] : 0.0f;
+#pragma unroll
+                for (int t = 0; t < N; t++)
+                    if (t < nt) yr[(size_t) t * g.ldy] = __fadd_rn(old[t], acc[t]);
+            } else {
+                const float b = g.bias ? g.bias[r] : 0.0f;
+#pragma unroll
+                for (int t = 0; t < N; t++)
+                    if (t < nt) yr[(size_t) t * g.ldy] = g.bias ? __fadd_rn(acc[t], b) : acc[t];
             }
         }
     }
@@ -285,9 +295,10 @@ int tc_tile_n(int T) { return T <= 16 ? 16 : T <= 32 ? 32 : 64; }
 int tc_tokens_pad(int T) { const int N = tc_tile_n(T); return (T + N - 1) / N * N; }
 
 cudaError_t tc_quant(int mode, const TcQuantArgs & a, cudaStream_t st) {
-    if (mode == TQ_NORM) k_quant_rows<TQ_NORM><<<a.T_pad, 256, 0, st>>>(a);
-    else if (mode == TQ_SILU) k_quant_rows<TQ_SILU><<<a.T_pad, 256, 0, st>>>(a);
-    else k_quant_rows<TQ_PLAIN><<<a.T_pad, 256, 0, st>>>(a);
+    const dim3 grid(a.T_pad, (a.nsb + 7) / 8);
+    if (mode == TQ_NORM) k_quant_rows<TQ_NORM><<<grid, 256, 0, st>>>(a);
+    else if (mode == TQ_SILU) k_quant_rows<TQ_SILU><<<grid, 256, 0, st>>>(a);
+    else k_quant_rows<TQ_PLAIN><<<grid, 256, 0, st>>>(a);
     return cudaGetLastError();
 }
 
