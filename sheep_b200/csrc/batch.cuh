@@ -332,6 +332,312 @@ __global__ void __launch_bounds__(kBThreads, 2) k_battn(const __grid_constant__ 
     if (tid == 0) g.cnt[grp] = 0;
 }
 
+// ---------------------------------------------------------------- attention on the tensor cores
+
+// Warp-level f16 MMA (m16n8k16, fp32 accumulate), ldmatrix and 16-byte async
+// copies. Decode attention has 1-16 query heads per KV head, so the product is
+// M = heads (padded to 16) by N = positions: the warp-level form keeps scores
+// in registers and hands them to the value product as its A fragments.
+SB_DEV void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+SB_DEV void ldsm4(uint32_t addr, uint32_t & r0, uint32_t & r1, uint32_t & r2, uint32_t & r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr) : "memory");
+}
+SB_DEV void ldsm4t(uint32_t addr, uint32_t & r0, uint32_t & r1, uint32_t & r2, uint32_t & r3) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr) : "memory");
+}
+// 16 bytes global -> shared, bypassing L1; src_bytes 0 fills zeros.
+SB_DEV void cp_async16(uint32_t dst, const void * src, uint32_t src_bytes) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" :: "r"(dst), "l"(src), "r"(src_bytes) : "memory");
+}
+SB_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+SB_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
+SB_DEV uint32_t pack_h2(float a, float b) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+// x = hi + lo in fp16 (hi = fp16(x), lo = fp16(x - hi)): two MMAs with the
+// exact fp16 keys/values give the fp32 product to ~2^-22 of x.
+SB_DEV void split_h2(float a, float b, uint32_t & hi, uint32_t & lo) {
+    const __half2 h = __floats2half2_rn(a, b);
+    const float2 f = __half22float2(h);
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = pack_h2(a - f.x, b - f.y);
+}
+
+constexpr int kMChunk = 64;      // positions per ring stage
+constexpr int kMStages = 3;
+constexpr int kMThreads = 128;   // 4 warps, 16 positions of each chunk apiece
+constexpr int kMHeads = 16;      // query heads per CTA (the MMA's M)
+
+__host__ __device__ inline int battn_mma_q(int rep) { return (rep < kMHeads ? rep : kMHeads + 3) / 4 * 4; }
+__host__ __device__ inline size_t battn_mma_smem(int hd, int rep) {
+    const size_t ring = (size_t) kMStages * 2 * kMChunk * (hd + 8) * 2;
+    const size_t comb = (size_t) (kMThreads / 32) * kMHeads * hd * 4;
+    const int nq = rep < kMHeads ? (rep + 3) / 4 * 4 : kMHeads;
+    return (ring > comb ? ring : comb) + (size_t) (nq * hd + 3 * hd) * 4 + 16;
+}
+
+// One CTA per (split of the positions, KV head x group of up to 16 query heads,
+// sequence), 4 warps. Chunks of 64 positions stream into a 3-stage ring by
+// 16-byte async copies into rows padded by 16 bytes (ldmatrix without bank
+// conflicts; rows past the position are zero-filled). Per chunk each warp
+// takes 16 positions:
+//   scores  S[head][pos] = Q K^T over hd/16 K steps, Q as fp16 hi + lo
+//           fragments in registers, K fragments by ldmatrix (2 x 8 positions);
+//   softmax the warp's own running max and sum per head (rows g and g+8 of
+//           the fragment), expf, its accumulators rescaled;
+//   values  O[head][d] += P V with P (hi + lo) taken straight from the score
+//           accumulators, V fragments by ldmatrix.trans.
+// The 4 warps' (max, sum, O) merge at the end, then the splits as in k_battn.
+template <int HD>
+__global__ void __launch_bounds__(kMThreads, 2) k_battn_mma(const __grid_constant__ BAttnArgs g) {
+    constexpr int RS = HD + 8;           // padded row, halves
+    constexpr int KS = HD / 16;          // K steps of the scores
+    constexpr int NT = HD / 8;           // n-tiles of the output
+    constexpr int NW = kMThreads / 32;
+    constexpr int PIECES = HD / 8;       // 16-byte pieces per row
+    constexpr size_t STAGE = (size_t) 2 * kMChunk * RS;   // halves
+    constexpr size_t RING = (size_t) kMStages * STAGE * 2;
+    constexpr size_t COMB = (size_t) NW * kMHeads * HD * 4;
+    extern __shared__ __align__(16) uint8_t bsm[];
+    __shared__ double red[NW];
+    __shared__ float wm[NW][kMHeads], wl[NW][kMHeads];
+    __shared__ unsigned last_flag;
+    const int split = blockIdx.x, gy = blockIdx.y, b = blockIdx.z;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int gq = lane >> 2, tq = lane & 3;   // fragment row / column pair
+    const int rep = g.n_head / g.n_kv;
+    const int kvh = gy / g.hgroups, h0 = (gy % g.hgroups) * kMHeads, nh = min(kMHeads, rep - h0);
+    const int nq = (nh + 3) / 4 * 4;           // query rows kept in shared memory
+    const int pos = g.pos[b];
+    float * outb = g.out + (size_t) b * g.ldo + ((size_t) kvh * rep + h0) * HD;
+    if (pos < 0) {
+        if (split == 0)
+            for (int i = tid; i < nh * HD; i += kMThreads) outb[i] = 0.0f;
+        return;
+    }
+    if (pos >= g.n_ctx || rep > kBMaxRep) {
+        if (tid == 0) atomicExch(g.err, 213);
+        return;
+    }
+    const int nchunk = pos / kMChunk + 1;
+    const int per = (nchunk + g.nsplit - 1) / g.nsplit;
+    const int nact = (nchunk + per - 1) / per;
+    const int c0 = split * per, c1 = min(nchunk, c0 + per);
+    if (c0 >= nchunk) return;
+    const int nmine = c1 - c0;
+    uint16_t * ring = reinterpret_cast<uint16_t *>(bsm);
+    float * qs = reinterpret_cast<float *>(bsm + (RING > COMB ? RING : COMB));   // [nq][HD]
+    float * kn = qs + nq * HD, * vn = kn + HD, * cs = vn + HD, * sn = cs + HD / 2;
+    float * comb = reinterpret_cast<float *>(bsm);                                 // [NW][16][HD] at the end
+    const size_t row0 = ((size_t) b * g.n_kv + kvh) * g.n_ctx;
+
+    auto issue = [&](int j) {   // chunk c0 + j into stage j % kMStages
+        const int t0 = (c0 + j) * kMChunk, nt = min(pos + 1, t0 + kMChunk) - t0;
+        uint16_t * Ks = ring + (size_t) (j % kMStages) * STAGE;
+        for (int i = tid; i < 2 * kMChunk * PIECES; i += kMThreads) {
+            const int kv = i / (kMChunk * PIECES), rem = i % (kMChunk * PIECES);
+            const int r = rem / PIECES, pc = rem % PIECES;
+            const uint16_t * src = (kv ? g.vc : g.kc) + (row0 + t0 + min(r, nt - 1)) * HD + pc * 8;
+            cp_async16(smem_u32(Ks + (size_t) kv * kMChunk * RS + r * RS + pc * 8), src, r < nt ? 16u : 0u);
+        }
+    };
+#pragma unroll
+    for (int j = 0; j < kMStages; j++) {
+        if (j < nmine) issue(j);
+        cp_async_commit();
+    }
+    const float * qrow = g.qkv + (size_t) b * g.ldq;
+    for (int i = tid; i < HD / 2; i += kMThreads) {
+        cs[i] = g.rcos[(size_t) pos * (HD / 2) + i];
+        sn[i] = g.rsin[(size_t) pos * (HD / 2) + i];
+    }
+    for (int i = tid; i < nq * HD; i += kMThreads)
+        qs[i] = i < nh * HD ? qrow[((size_t) kvh * rep + h0) * HD + i] : 0.0f;
+    for (int i = tid; i < HD; i += kMThreads) {
+        kn[i] = qrow[g.koff + kvh * HD + i];
+        vn[i] = qrow[g.voff + kvh * HD + i];
+    }
+    __syncthreads();
+    for (int h = 0; h < nh; h++) norm_rope(qs + h * HD, g.qn, g.eps, HD, cs, sn, red);
+    norm_rope(kn, g.kn, g.eps, HD, cs, sn, red);
+    // Q fragments (rows gq and gq + 8 are heads; columns the K step's dims)
+    uint32_t qa[KS][4], ql[KS][4];
+#pragma unroll
+    for (int ks = 0; ks < KS; ks++) {
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int row = gq + (e & 1) * 8, col = ks * 16 + 2 * tq + (e >> 1) * 8;
+            const float x0 = row < nq ? qs[row * HD + col] : 0.0f, x1 = row < nq ? qs[row * HD + col + 1] : 0.0f;
+            split_h2(x0, x1, qa[ks][e], ql[ks][e]);
+        }
+    }
+    float m2[2] = {-INFINITY, -INFINITY}, l2[2] = {0.0f, 0.0f};
+    float o[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; n++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) o[n][e] = 0.0f;
+    const int pw = warp * 16;   // the warp's positions in each chunk
+    for (int j = 0; j < nmine; j++) {
+        const int c = c0 + j, t0 = c * kMChunk, nt = min(pos + 1, t0 + kMChunk) - t0;
+        uint16_t * Ks = ring + (size_t) (j % kMStages) * STAGE, * Vs = Ks + kMChunk * RS;
+        cp_async_wait<kMStages - 1>();
+        __syncthreads();
+        if (c == nchunk - 1) {
+            // the new key and value, fp16 round to nearest even, over the stale row
+            const int r = pos - t0;
+            for (int i = tid; i < HD; i += kMThreads) {
+                const uint16_t kh = f2h(kn[i]), vh = f2h(vn[i]);
+                Ks[r * RS + i] = kh;
+                Vs[r * RS + i] = vh;
+                if (h0 == 0) {
+                    g.kc[(row0 + pos) * HD + i] = kh;
+                    g.vc[(row0 + pos) * HD + i] = vh;
+                }
+            }
+            __syncthreads();
+        }
+        if (pw < nt) {
+            // ---- scores of positions pw .. pw + 15 (two n-tiles of 8)
+            float sc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+            const uint32_t kaddr = smem_u32(Ks + (pw + ((lane >> 4) << 3) + (lane & 7)) * RS + ((lane >> 3) & 1) * 8);
+#pragma unroll
+            for (int ks = 0; ks < KS; ks++) {
+                uint32_t b0, b1, b2, b3;
+                ldsm4(kaddr + ks * 32, b0, b1, b2, b3);
+                mma16816(sc[0], qa[ks], b0, b1);
+                mma16816(sc[0], ql[ks], b0, b1);
+                mma16816(sc[1], qa[ks], b2, b3);
+                mma16816(sc[1], ql[ks], b2, b3);
+            }
+            // ---- online softmax per head row (gq: e = 0,1; gq + 8: e = 2,3)
+            float pr[2][4];
+#pragma unroll
+            for (int rr = 0; rr < 2; rr++) {
+                float mx = -INFINITY;
+#pragma unroll
+                for (int n = 0; n < 2; n++)
+#pragma unroll
+                    for (int e = 0; e < 2; e++) {
+                        const int col = pw + n * 8 + 2 * tq + e;
+                        const float v = col < nt ? sc[n][2 * rr + e] * g.scale : -INFINITY;
+                        sc[n][2 * rr + e] = v;
+                        mx = fmaxf(mx, v);
+                    }
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+                const float mn = fmaxf(m2[rr], mx);
+                const float alpha = m2[rr] == -INFINITY ? 0.0f : expf(m2[rr] - mn);
+                float sum = 0.0f;
+#pragma unroll
+                for (int n = 0; n < 2; n++)
+#pragma unroll
+                    for (int e = 0; e < 2; e++) {
+                        const float v = sc[n][2 * rr + e];
+                        const float pe = v == -INFINITY ? 0.0f : expf(v - mn);
+                        pr[n][2 * rr + e] = pe;
+                        sum += pe;
+                    }
+                sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+                sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+                l2[rr] = l2[rr] * alpha + sum;
+                m2[rr] = mn;
+#pragma unroll
+                for (int n = 0; n < NT; n++) {
+                    o[n][2 * rr] *= alpha;
+                    o[n][2 * rr + 1] *= alpha;
+                }
+            }
+            // ---- values: P (16 heads x 16 positions) from the score fragments
+            uint32_t pa[4], pl[4];
+            split_h2(pr[0][0], pr[0][1], pa[0], pl[0]);
+            split_h2(pr[0][2], pr[0][3], pa[1], pl[1]);
+            split_h2(pr[1][0], pr[1][1], pa[2], pl[2]);
+            split_h2(pr[1][2], pr[1][3], pa[3], pl[3]);
+            const uint32_t vaddr = smem_u32(Vs + (pw + ((lane >> 3) & 1) * 8 + (lane & 7)) * RS + (lane >> 4) * 8);
+#pragma unroll
+            for (int n = 0; n < NT; n += 2) {
+                uint32_t b0, b1, b2, b3;
+                ldsm4t(vaddr + n * 16, b0, b1, b2, b3);
+                mma16816(o[n], pa, b0, b1);
+                mma16816(o[n], pl, b0, b1);
+                mma16816(o[n + 1], pa, b2, b3);
+                mma16816(o[n + 1], pl, b2, b3);
+            }
+        }
+        __syncthreads();   // the stage is free
+        if (j + kMStages < nmine) issue(j + kMStages);
+        cp_async_commit();
+    }
+    cp_async_wait<0>();
+    __syncthreads();
+    // ---- the warps' partial softmax states merge (the ring is free)
+    if (tq == 0) {
+        wm[warp][gq] = m2[0]; wm[warp][gq + 8] = m2[1];
+        wl[warp][gq] = l2[0]; wl[warp][gq + 8] = l2[1];
+    }
+#pragma unroll
+    for (int n = 0; n < NT; n++) {
+        comb[(warp * kMHeads + gq) * HD + n * 8 + 2 * tq] = o[n][0];
+        comb[(warp * kMHeads + gq) * HD + n * 8 + 2 * tq + 1] = o[n][1];
+        comb[(warp * kMHeads + gq + 8) * HD + n * 8 + 2 * tq] = o[n][2];
+        comb[(warp * kMHeads + gq + 8) * HD + n * 8 + 2 * tq + 1] = o[n][3];
+    }
+    __syncthreads();
+    const size_t grp = (size_t) b * g.n_kv * g.hgroups + gy;
+    float * pb = g.part + (grp * g.nsplit + split) * kMHeads * (HD + 2);
+    for (int i = tid; i < nh * HD; i += kMThreads) {
+        const int h = i / HD, d = i % HD;
+        float M = -INFINITY;
+#pragma unroll
+        for (int w = 0; w < NW; w++) M = fmaxf(M, wm[w][h]);
+        float L = 0.0f, ov = 0.0f;
+#pragma unroll
+        for (int w = 0; w < NW; w++) {
+            if (wm[w][h] == -INFINITY) continue;
+            const float e = expf(wm[w][h] - M);
+            L += wl[w][h] * e;
+            ov += comb[(w * kMHeads + h) * HD + d] * e;
+        }
+        if (nact == 1) outb[h * HD + d] = ov / L;
+        else {
+            pb[h * (HD + 2) + 2 + d] = ov;
+            if (d == 0) { pb[h * (HD + 2)] = M; pb[h * (HD + 2) + 1] = L; }
+        }
+    }
+    if (nact == 1) return;
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last_flag = atomicAdd(&g.cnt[grp], 1u) == (unsigned) nact - 1;
+    __syncthreads();
+    if (!last_flag) return;
+    __threadfence();
+    const float * P = g.part + grp * g.nsplit * kMHeads * (HD + 2);
+    const size_t sst = (size_t) kMHeads * (HD + 2);
+    for (int i = tid; i < nh * HD; i += kMThreads) {
+        const int h = i / HD, d = i % HD;
+        float M = -INFINITY;
+        for (int k = 0; k < nact; k++) M = fmaxf(M, __ldcg(P + k * sst + h * (HD + 2)));
+        float L = 0.0f, ov = 0.0f;
+        for (int k = 0; k < nact; k++) {
+            const float e = expf(__ldcg(P + k * sst + h * (HD + 2)) - M);
+            L += __ldcg(P + k * sst + h * (HD + 2) + 1) * e;
+            ov += __ldcg(P + k * sst + h * (HD + 2) + 2 + d) * e;
+        }
+        outb[h * HD + d] = ov / L;
+    }
+    if (tid == 0) g.cnt[grp] = 0;
+}
+
 // Greedy choice per sequence: the first index of the largest logit
 // (sml/sml-run.c:3539-3544). It becomes the slot's next token, is logged at
 // the slot's next position, and the position advances; idle slots stay idle.
