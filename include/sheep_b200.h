@@ -173,6 +173,10 @@ const char * sb_moe_last_error(void);
 // batched path (the reference's int8 tiles, sml_g_tcm9, sml/sml-gpu-fast.cu:3149).
 int sb_tc_imma(const int8_t * A, const int8_t * B, int32_t * C, int M, int N, int K, int * err, void * stream);
 const char * sb_tc_last_error(void);
+// Global-timer marks of the last batched tensor-core product, per CTA (8 words:
+// start, first accumulator read, main loop done, slices added, stored, exit);
+// filled only by the trace build (-DSB_TRACE), else returns 0.
+int sb_tc_trace(unsigned long long * out, int cap_ctas);
 
 // ------------------------------------------------------------------ batched serving
 // n_seq conversations decoding together, one token each per step and one read

@@ -95,6 +95,7 @@ def lib():
         "sb_moe_last_error": (cp, []),
         "sb_tc_imma": (ip, [vp, vp, vp, ip, ip, ip, vp, vp]),
         "sb_tc_last_error": (cp, []),
+        "sb_tc_trace": (ip, [vp, ip]),
         "sb_batch_open": (vp, [cp, ip, ip, cp, ip]),
         "sb_batch_close": (None, [vp]),
         "sb_batch_info": (None, [vp, vp]),

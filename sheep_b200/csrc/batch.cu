@@ -65,7 +65,7 @@ int round128(int n) { return (n + 127) / 128 * 128; }
 int pick_split(int tiles, int nsb, int nsm) {
     int best = 1;
     double bc = 1e30;
-    for (int s = 1; s <= nsb && s <= 16; s++) {
+    for (int s = 1; s <= nsb && s <= kTcMaxSplit; s++) {
         if (tc_split(nsb, s) != s) continue;
         const int per = (nsb + s - 1) / s;
         const int waves = (tiles * s + nsm - 1) / nsm;
@@ -93,8 +93,8 @@ struct sb_batch {
     float * rcos = nullptr, * rsin = nullptr;
     int * tok = nullptr, * pos = nullptr, * tlog = nullptr;
     uint8_t * xblk = nullptr;
-    float * xs = nullptr, * part = nullptr, * apart = nullptr;
-    unsigned * cnt = nullptr, * acnt = nullptr;
+    float * xs = nullptr, * apart = nullptr;
+    unsigned * acnt = nullptr;
     int attn_split = 1, attn_hg = 4, attn_groups = 1;
     bool attn_mma = true;
     int * err = nullptr;
@@ -244,13 +244,6 @@ static bool b_build(sb_batch * b, char * why, int nwhy) {
     int wide = b->E > b->qd ? b->E : b->qd;
     wide = wide > b->F ? wide : b->F;
     const int nsb_max = (wide / SSF_GROUP + 7) / 8;
-    size_t part = 0, tiles = 0;
-    auto need = [&](const BGemm & gm) {
-        if (gm.split > 1) part = std::max(part, (size_t) gm.split * Tp * gm.p.rows_pad);
-        tiles = std::max(tiles, (size_t) (gm.p.rows_pad / 128) * (Tp / b->N));
-    };
-    need(b->head);
-    for (const BLayer & y : b->L) { need(y.qkv); need(y.o); need(y.gu); need(y.dn); }
     b->x = (float *) b->ar.carve((size_t) B * b->E * 4);
     b->qkv = (float *) b->ar.carve((size_t) B * b->qkv_rows * 4);
     b->att = (float *) b->ar.carve((size_t) B * b->qd * 4);
@@ -266,8 +259,6 @@ static bool b_build(sb_batch * b, char * why, int nwhy) {
     b->tlog = (int *) b->ar.carve((size_t) B * (b->n_ctx + 1) * 4);
     b->xblk = (uint8_t *) b->ar.carve((size_t) Tp * nsb_max * 256);
     b->xs = (float *) b->ar.carve((size_t) Tp * nsb_max * 4);
-    b->part = (float *) b->ar.carve(part ? part * 4 : 16);
-    b->cnt = (unsigned *) b->ar.carve(tiles * 4);
     // attention: head groups of attn_hg query heads; the positions of a
     // (sequence, group) split over attn_split CTAs so that the grid fills the
     // SMs' resident slots in whole waves (two CTAs per SM up to hd 128)
@@ -314,7 +305,7 @@ static void b_mma(sb_batch * b, const BGemm & gm, float * y, int ldy, const floa
     a.wblk = gm.p.wblk; a.s8 = gm.p.s8; a.xblk = b->xblk; a.xs = b->xs;
     a.y = y; a.ldy = ldy; a.bias = bias; a.accumulate = accumulate;
     a.rows = gm.rows; a.rows_pad = gm.p.rows_pad; a.nsb = gm.p.nsb; a.T = b->B; a.T_pad = b->T_pad;
-    a.split = gm.split; a.part = b->part; a.cnt = b->cnt; a.err = b->err;
+    a.split = gm.split; a.err = b->err;
     b_after(b, tc_mma(a, b->st));
 }
 

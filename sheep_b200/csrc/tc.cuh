@@ -85,4 +85,19 @@ SB_DEV void tmem_ld8(uint32_t taddr, uint32_t (&r)[8]) {
 }
 SB_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Thread-block clusters: a barrier over every thread of the cluster (release /
+// acquire: shared-memory stores before it are visible after it), and stores
+// into another CTA's shared memory by its rank in the cluster.
+SB_DEV void cluster_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+SB_DEV uint32_t cluster_map(const void * smem_ptr, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(smem_ptr)), "r"(rank));
+    return r;
+}
+SB_DEV void st_cluster(uint32_t addr, float v) {
+    asm volatile("st.shared::cluster.f32 [%0], %1;" :: "r"(addr), "f"(v) : "memory");
+}
+
 }  // namespace sb

@@ -18,12 +18,13 @@
 //   k_tcgemm<N>  one CTA per (128 rows, N tokens, slice of the superblocks),
 //                six warps: a producer (bulk copies of both blocks of a
 //                superblock into a 4-stage ring), an MMA issuer (8 MMAs of
-//                K = 32 per superblock into one of two TMEM accumulators, then
+//                K = 32 per superblock into one of four TMEM accumulators, then
 //                commits), and four epilogue warps (TMEM lanes 0..127 = rows)
 //                that apply the superblock's scales while the next superblock
-//                multiplies. Slices meet in a partial-sum buffer and the last
-//                CTA of a tile adds them in slice order (split-K). The
-//                epilogue may add a bias or accumulate into y (a residual).
+//                multiplies. The slices of a tile run as one thread-block
+//                cluster and meet in the leader CTA's shared memory, where
+//                they are added in slice order (split-K). The epilogue may add
+//                a bias or accumulate into y (a residual).
 #include "tc.cuh"
 #include "decode.cuh"
 #include "sheep_b200.h"
@@ -34,6 +35,22 @@
 namespace sb {
 
 constexpr int kTcStages = 4;
+constexpr int kTcAcc = 4;        // TMEM accumulators: the MMAs run up to 3 superblocks ahead of the epilogue
+
+
+#ifdef SB_TRACE
+// Trace build: global-timer marks of the last tensor-core product, per CTA
+// (blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z) < kTcTraceCtas).
+constexpr int kTcTraceCtas = 1024;
+__device__ unsigned long long g_tc_trace[kTcTraceCtas * 8];
+#define TC_MARK(slot)                                                                                   \
+    do {                                                                                                \
+        const unsigned cta_ = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);          \
+        if (cta_ < (unsigned) kTcTraceCtas) g_tc_trace[cta_ * 8 + (slot)] = global_ns();              \
+    } while (0)
+#else
+#define TC_MARK(slot) do { } while (0)
+#endif
 constexpr uint32_t kTcABytes = 128 * 256;
 
 template <int NB, int SIX>
@@ -141,12 +158,14 @@ SB_DEV bool tc_wait(uint64_t * bar, uint32_t parity, int * err, int code, volati
 template <int N>
 __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArgs g) {
     extern __shared__ __align__(1024) uint8_t tsm[];
-    __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], accf[2], acce[2];
+    __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], accf[kTcAcc], acce[kTcAcc];
     __shared__ uint32_t tslot;
     __shared__ volatile int fail;
-    __shared__ volatile bool last;
-    constexpr uint32_t BB = N * 256, SB = kTcABytes + BB;
-    constexpr uint32_t ncols = tc_cols(2 * N);
+    // a stage: A block | B block | the rows' s8 (128 floats) | the tokens' xs (N floats)
+    constexpr uint32_t BB = N * 256, SB = kTcABytes + BB + 512 + N * 4;
+    static_assert((size_t) kTcStages * SB >= (size_t) (kTcMaxSplit - 1) * 128 * N * 4,
+                  "a cluster's partial tiles must fit in the leader's ring");
+    constexpr uint32_t ncols = tc_cols(kTcAcc * N);
     constexpr uint32_t idesc = tc_idesc_s8(128, N);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int mb = blockIdx.x, tb = blockIdx.y, z = blockIdx.z;
@@ -155,8 +174,9 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
     const int s0 = z * per, ns = min(g.nsb, s0 + per) - s0;
     if (warp == 1) tmem_alloc(&tslot, ncols);
     if (tid == 0) {
-        for (int s = 0; s < kTcStages; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
-        for (int b = 0; b < 2; b++) { mbar_init(&accf[b], 1); mbar_init(&acce[b], 4); }
+        // a stage is free once its MMAs are done (commit) and the 4 epilogue warps read its scales
+        for (int s = 0; s < kTcStages; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 5); }
+        for (int b = 0; b < kTcAcc; b++) { mbar_init(&accf[b], 1); mbar_init(&acce[b], 4); }
         fail = 0;
         mbar_fence_init();
     }
@@ -165,6 +185,10 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
     tc_fence_after();
     const uint32_t tmem = tslot;
     if (warp == 1) tmem_relinquish();
+    if (tid == 0) TC_MARK(0);
+    const int q = warp & 3, row = 32 * q + lane, r = mb * 128 + row;   // epilogue warps: TMEM lane = row
+    float acc[N];
+    bool ok = true;
 
     if (warp == 0) {
         // ---------------- producer: both operand blocks of every superblock
@@ -175,15 +199,19 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
                 mbar_expect_tx(&full[s], SB);
                 bulk_g2s(tsm + (size_t) s * SB, g.wblk + ((size_t) mb * g.nsb + sb) * kTcABytes, kTcABytes, &full[s]);
                 bulk_g2s(tsm + (size_t) s * SB + kTcABytes, g.xblk + ((size_t) tb * g.nsb + sb) * BB, BB, &full[s]);
+                bulk_g2s(tsm + (size_t) s * SB + kTcABytes + BB, g.s8 + (size_t) sb * g.rows_pad + mb * 128, 512,
+                         &full[s]);
+                bulk_g2s(tsm + (size_t) s * SB + kTcABytes + BB + 512, g.xs + (size_t) sb * g.T_pad + tb * N, N * 4,
+                         &full[s]);
             }
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer: 8 x K=32 per superblock into accumulator sb % 2
         if (lane == 0) {
             for (int i = 0; i < ns; i++) {
-                const int s = i % kTcStages, buf = i & 1;
+                const int s = i % kTcStages, buf = i % kTcAcc;
                 if (!tc_wait(&full[s], (i / kTcStages) & 1, g.err, 41, &fail)) break;
-                if (i >= 2 && !tc_wait(&acce[buf], ((i >> 1) - 1) & 1, g.err, 42, &fail)) break;
+                if (i >= kTcAcc && !tc_wait(&acce[buf], (i / kTcAcc - 1) & 1, g.err, 42, &fail)) break;
                 tc_fence_after();
                 const uint8_t * As = tsm + (size_t) s * SB, * Bs = As + kTcABytes;
 #pragma unroll
@@ -196,16 +224,24 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
         }
     } else {
         // ---------------- epilogue: TMEM lanes (rows) 32 q .. 32 q + 31
-        const int q = warp & 3, row = 32 * q + lane, r = mb * 128 + row;
-        float acc[N];
-#pragma unroll
         for (int t = 0; t < N; t++) acc[t] = 0.0f;
-        bool ok = true;
         for (int i = 0; i < ns; i++) {
-            const int buf = i & 1, sb = s0 + i;
-            const float s8v = g.s8[(size_t) sb * g.rows_pad + r];
-            const float * xsp = g.xs + (size_t) sb * g.T_pad + (size_t) tb * N;
-            ok = ok && tc_wait(&accf[buf], (i >> 1) & 1, g.err, 43, &fail);
+            const int buf = i % kTcAcc, s = i % kTcStages;
+            // the stage's scales: landed with its operands, and the stage is held
+            // (empty needs this warp's arrival) until they are read
+            ok = ok && tc_wait(&full[s], (i / kTcStages) & 1, g.err, 44, &fail);
+            const float * ssc = reinterpret_cast<const float *>(tsm + (size_t) s * SB + kTcABytes + BB);
+            const float s8v = ssc[row];
+            float xsv[N];
+#pragma unroll
+            for (int t = 0; t < N; t += 4) {
+                const float4 v4 = *reinterpret_cast<const float4 *>(ssc + 128 + t);
+                xsv[t] = v4.x; xsv[t + 1] = v4.y; xsv[t + 2] = v4.z; xsv[t + 3] = v4.w;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+            ok = ok && tc_wait(&accf[buf], (i / kTcAcc) & 1, g.err, 43, &fail);
+            if (i == 0 && tid == 64) TC_MARK(1);
             tc_fence_after();
             uint32_t d[N];
 #pragma unroll
@@ -220,35 +256,38 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
             __syncwarp();
             if (lane == 0) mbar_arrive(&acce[buf]);
 #pragma unroll
-            for (int t = 0; t < N; t++)
-                acc[t] = __fmaf_rn(__fmul_rn(s8v, __ldg(xsp + t)), (float) (int) d[t], acc[t]);
+            for (int t = 0; t < N; t++) acc[t] = __fmaf_rn(__fmul_rn(s8v, xsv[t]), (float) (int) d[t], acc[t]);
         }
-        if (g.split > 1) {
-            // slices meet in part[z][token][row]; the last CTA of the tile adds
-            // them in slice order, so the sum does not depend on arrival order
-            // (sml_g_splitk_sum, sml/sml-gpu-fast.cu:2057-2065)
+        if (tid == 64) TC_MARK(2);
+    }
+    if (g.split > 1) {
+        // The slices of a tile are one cluster (rank = z). Once every CTA is past
+        // its main loop (the leader's ring is idle), slices 1.. store their sums
+        // into the leader's ring as [slice - 1][token][row]; the leader adds them
+        // in slice order, so the sum does not depend on arrival order
+        // (sml_g_splitk_sum, sml/sml-gpu-fast.cu:2057-2065).
+        cluster_sync();
+        float * pbuf = reinterpret_cast<float *>(tsm);
+        if (warp >= 2 && z > 0) {
+            const uint32_t base = cluster_map(pbuf + (size_t) (z - 1) * N * 128 + row, 0);
 #pragma unroll
-            for (int t = 0; t < N; t++)
-                g.part[((size_t) z * g.T_pad + tb * N + t) * g.rows_pad + r] = acc[t];
-            __threadfence();
-            bar_sync(1, 128);
-            if (warp == 2 && lane == 0)
-                last = atomicAdd(&g.cnt[mb * gridDim.y + tb], 1u) == (unsigned) (g.split - 1);
-            bar_sync(1, 128);
-            if (!last) ok = false;
-            else {
-                __threadfence();
-                // slice-outer: a slice's N loads are independent and issue together
+            for (int t = 0; t < N; t++) st_cluster(base + (uint32_t) (t * 128 * 4), acc[t]);
+        }
+        cluster_sync();
+        if (warp >= 2) {
+            if (z == 0) {
+                for (int k = 1; k < g.split; k++) {
+                    const float * pk = pbuf + (size_t) (k - 1) * N * 128 + row;
 #pragma unroll
-                for (int t = 0; t < N; t++) acc[t] = 0.0f;
-                for (int k = 0; k < g.split; k++) {
-                    const float * pk = g.part + ((size_t) k * g.T_pad + tb * N) * g.rows_pad + r;
-#pragma unroll
-                    for (int t = 0; t < N; t++) acc[t] = __fadd_rn(acc[t], __ldcg(pk + (size_t) t * g.rows_pad));
+                    for (int t = 0; t < N; t++) acc[t] = __fadd_rn(acc[t], pk[t * 128]);
                 }
-                if (warp == 2 && lane == 0) g.cnt[mb * gridDim.y + tb] = 0;
+            } else {
+                ok = false;   // only the leader writes the tile
             }
         }
+    }
+    if (warp >= 2) {
+        if (tid == 64) TC_MARK(3);
         if (ok && r < g.rows) {
             const int nt = min(N, g.T - tb * N);
             float * yr = g.y + (size_t) tb * N * g.ldy + r;
@@ -268,12 +307,14 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
             }
         }
     }
+    if (tid == 64) TC_MARK(4);
     tc_fence_before();
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem, ncols);
     }
+    if (tid == 0) TC_MARK(5);
 }
 
 template <int NB, int SIX>
@@ -304,15 +345,26 @@ cudaError_t tc_quant(int mode, const TcQuantArgs & a, cudaStream_t st) {
 
 template <int N>
 static cudaError_t launch_gemm(const TcArgs & a, cudaStream_t st) {
-    constexpr int smem = kTcStages * (int) (kTcABytes + N * 256);
+    constexpr int smem = kTcStages * (int) (kTcABytes + N * 256 + 512 + N * 4);
     static bool attr = false;
     if (!attr) {
         const cudaError_t e = cudaFuncSetAttribute(k_tcgemm<N>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
         if (e != cudaSuccess) return e;
         attr = true;
     }
-    k_tcgemm<N><<<dim3(a.rows_pad / 128, a.T_pad / N, a.split), 192, smem, st>>>(a);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.rows_pad / 128, a.T_pad / N, a.split);
+    cfg.blockDim = dim3(192);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 1;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = (unsigned) a.split;   // one tile's slices
+    cfg.attrs = at;
+    cfg.numAttrs = a.split > 1 ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_tcgemm<N>, a);
 }
 
 int tc_split(int nsb, int split) {
@@ -323,8 +375,7 @@ int tc_split(int nsb, int split) {
 }
 
 cudaError_t tc_mma(const TcArgs & a, cudaStream_t st) {
-    if (a.split < 1 || a.split != tc_split(a.nsb, a.split) || (a.split > 1 && (!a.part || !a.cnt)))
-        return cudaErrorInvalidValue;
+    if (a.split < 1 || a.split > kTcMaxSplit || a.split != tc_split(a.nsb, a.split)) return cudaErrorInvalidValue;
     const int N = tc_tile_n(a.T);
     return N == 16 ? launch_gemm<16>(a, st) : N == 32 ? launch_gemm<32>(a, st) : launch_gemm<64>(a, st);
 }
@@ -346,3 +397,17 @@ cudaError_t tc_gemm(const QT & t, const TcPlan & p, const float * x, int T, uint
 }
 
 }  // namespace sb
+
+// The global-timer marks of the last tensor-core product (trace build only):
+// per CTA [start, first accumulator read, main loop done, slices added,
+// stored, exit, -, -]; returns the CTAs copied (0 without SB_TRACE).
+extern "C" int sb_tc_trace(unsigned long long * out, int cap_ctas) {
+#ifdef SB_TRACE
+    const int n = cap_ctas < sb::kTcTraceCtas ? cap_ctas : sb::kTcTraceCtas;
+    if (cudaMemcpyFromSymbol(out, sb::g_tc_trace, (size_t) n * 8 * 8) != cudaSuccess) return 0;
+    return n;
+#else
+    (void) out; (void) cap_ctas;
+    return 0;
+#endif
+}

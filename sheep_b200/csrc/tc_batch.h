@@ -24,9 +24,7 @@ struct TcArgs {
     int accumulate;           // y += product (else y = product + bias)
     int ldy;
     int rows, rows_pad, nsb, T, T_pad;
-    int split;                // slices of the superblocks (tc_split); > 1 needs part and cnt
-    float * part;             // [split][T_pad][rows_pad] partial sums
-    unsigned * cnt;           // [rows_pad / 128][T_pad / N] arrivals, zero between calls
+    int split;                // slices of the superblocks (tc_split), 1..kTcMaxSplit
     int * err;
 };
 
@@ -54,7 +52,10 @@ int tc_tile_n(int T);
 int tc_tokens_pad(int T);
 cudaError_t tc_quant(int mode, const TcQuantArgs & a, cudaStream_t st);
 // The number of non-empty slices when nsb superblocks are cut into `split`
-// equal runs (a launch's split must be a value this returns).
+// equal runs (a launch's split must be a value this returns, at most
+// kTcMaxSplit: a tile's slices form one cluster whose partial tiles fit in the
+// leader's shared memory).
+constexpr int kTcMaxSplit = 7;
 int tc_split(int nsb, int split);
 cudaError_t tc_mma(const TcArgs & a, cudaStream_t st);
 // y[T][rows] = W x[t] for x[T][cols] (device pointers): tc_quant + tc_mma.

@@ -36,9 +36,8 @@ struct sb_tset {
     // tensor-core batched path: per-tensor int8 re-quantization, made on first use
     std::unordered_map<std::string, TcPlan> tc;
     uint8_t * tc_x = nullptr;
-    float * tc_xs = nullptr, * tc_part = nullptr;
-    unsigned * tc_cnt = nullptr;
-    size_t tc_x_cap = 0, tc_xs_cap = 0, tc_part_cap = 0, tc_cnt_cap = 0;
+    float * tc_xs = nullptr;
+    size_t tc_x_cap = 0, tc_xs_cap = 0;
     int nsm = 148;
 };
 
@@ -97,8 +96,6 @@ extern "C" void sb_tset_close(sb_tset * t) {
     for (auto & kv : t->tc) { cudaFree(kv.second.wblk); cudaFree(kv.second.s8); }
     cudaFree(t->tc_x);
     cudaFree(t->tc_xs);
-    cudaFree(t->tc_part);
-    cudaFree(t->tc_cnt);
     t->ar.release();
     ssf_close(&t->f);
     delete t;
@@ -372,10 +369,10 @@ static bool grow(P *& buf, size_t & cap, size_t n) {
 // Scratch for the activations of T rows and the partial sums of `split` slices.
 static bool tc_scratch(sb_tset * t, const TcPlan & p, int T, int split) {
     const int N = tc_tile_n(T), T_pad = tc_tokens_pad(T);
+    (void) split;
+    (void) N;
     return grow(t->tc_x, t->tc_x_cap, (size_t) T_pad * p.nsb * 256) &&
-           grow(t->tc_xs, t->tc_xs_cap, (size_t) T_pad * p.nsb * 4) &&
-           (split <= 1 || (grow(t->tc_part, t->tc_part_cap, (size_t) split * T_pad * p.rows_pad * 4) &&
-                           grow(t->tc_cnt, t->tc_cnt_cap, (size_t) (p.rows_pad / 128) * (T_pad / N) * 4)));
+           grow(t->tc_xs, t->tc_xs_cap, (size_t) T_pad * p.nsb * 4);
 }
 
 extern "C" int sb_tset_gemm_tc(sb_tset * t, const char * name, const float * x, int nb, int split, float * y,
@@ -394,7 +391,7 @@ extern "C" int sb_tset_gemm_tc(sb_tset * t, const char * name, const float * x, 
     memset(&a, 0, sizeof a);
     a.wblk = p->wblk; a.s8 = p->s8; a.xblk = t->tc_x; a.xs = t->tc_xs; a.y = y; a.ldy = q->rows;
     a.rows = q->rows; a.rows_pad = p->rows_pad; a.nsb = p->nsb; a.T = nb; a.T_pad = qa.T_pad; a.err = t->err;
-    a.split = split; a.part = t->tc_part; a.cnt = t->tc_cnt;
+    a.split = split;
     return tc_mma(a, st) == cudaSuccess;
 }
 
