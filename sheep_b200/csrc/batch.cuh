@@ -508,17 +508,23 @@ __global__ void __launch_bounds__(kMThreads, 2) k_battn_mma(const __grid_constan
         }
         if (pw < nt) {
             // ---- scores of positions pw .. pw + 15 (two n-tiles of 8)
+            // hi and lo parts in their own accumulators: four independent MMA chains
             float sc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+            float sl[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
             const uint32_t kaddr = smem_u32(Ks + (pw + ((lane >> 4) << 3) + (lane & 7)) * RS + ((lane >> 3) & 1) * 8);
 #pragma unroll
             for (int ks = 0; ks < KS; ks++) {
                 uint32_t b0, b1, b2, b3;
                 ldsm4(kaddr + ks * 32, b0, b1, b2, b3);
                 mma16816(sc[0], qa[ks], b0, b1);
-                mma16816(sc[0], ql[ks], b0, b1);
+                mma16816(sl[0], ql[ks], b0, b1);
                 mma16816(sc[1], qa[ks], b2, b3);
-                mma16816(sc[1], ql[ks], b2, b3);
+                mma16816(sl[1], ql[ks], b2, b3);
             }
+#pragma unroll
+            for (int n = 0; n < 2; n++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) sc[n][e] += sl[n][e];
             // ---- online softmax per head row (gq: e = 0,1; gq + 8: e = 2,3)
             float pr[2][4];
 #pragma unroll
