@@ -21,7 +21,10 @@ bytes streamed, Q4 and Q8, batch 1/4/16) and configuration 2's MoE layer
 (Qwen3-30B-A3B shape at 1/16/64/256 tokens a step: tok/s and GB/s of the
 experts actually read plus the router), each run timed alone by CUDA events
 with a 512 MB buffer rewritten before it, so the weights come from HBM; and
-configuration 3's batch-1 decode (Llama-3-8B shape, 4.2 GB per token).
+configuration 3's batch-1 decode (Llama-3-8B shape, 4.2 GB per token) and its
+batched serving at 64 slots (2048-id prompts, 256 generated ids each).
+extras with N > 1 GPUs: configuration 2's MoE layer spread over the N GPUs
+(expert parallelism, sb_moe_open_ep), the max over ranks at 1/16/64/256 tokens.
 """
 import argparse
 import ctypes
@@ -279,6 +282,13 @@ def main():
                "sample": f"same model, 16-token prompt stepped, 2 warm-up then {n_cpu} timed greedy tokens"}
 
     extras = None
+    if world > 1:
+        # every rank: configuration 2's MoE layer spread over the GPUs (expert
+        # parallelism, the library's NCCL all-reduce between down and combine)
+        peak0, _ = peaks()
+        ep = moe_ep_microbench(peak0, dist, world, rank, max_over_ranks)
+        if rank == 0:
+            extras = {"moe_cfg2_ep": ep}
     if rank == 0 and world == 1:
         peak0, _ = peaks()
         extras = {"l2": "a 512 MB buffer rewritten before each timed run (decode: weights > L2)",
@@ -424,6 +434,37 @@ def gemm_tc_microbench(peak, reps=20):
                                 "int8_weight_gbs": round(w8 / (ms / 1000.0) / 1e9, 1)})
         finally:
             ts.close()
+    return out
+
+
+def moe_ep_microbench(peak, dist, world, rank, max_over_ranks, reps=20):
+    """Configuration 2's MoE layer over `world` GPUs (expert parallelism): every
+    rank holds 128/world experts and passes all T tokens; timed per rank by
+    CUDA events with L2 flushed, the max over ranks reported. Bytes: the chosen
+    experts summed over the ranks (each rank reads only those it holds) plus
+    every rank's router."""
+    import sheep_b200
+    from sheep_b200 import configs
+    nid = sdist.share_nccl_id(dist)
+    m = sheep_b200.MoeLayer(model_path(configs.CONFIGS["qwen3-30b-a3b-moe-layer"], 0, None), max_tokens=256,
+                            ep=(world, rank, nid))
+    out = []
+    try:
+        for T in (1, 16, 64, 256):
+            ms, na = m.time(fp16_rows(100 + T, T, m.n_embd), reps)
+            ms = max_over_ranks(ms)
+            import torch
+            t = torch.tensor([float(na)], dtype=torch.float64, device="cuda")
+            if dist is not None:
+                dist.all_reduce(t)
+            na_all = int(t.item())
+            nbytes = na_all * m.expert_bytes + world * m.router_bytes
+            gbs = nbytes / (ms / 1000.0) / 1e9
+            out.append({"tokens": T, "gpus": world, "us": round(ms * 1000.0, 2), "tok_s": round(T / (ms / 1000.0), 1),
+                        "experts_read": na_all, "bytes": nbytes, "gbs": round(gbs, 1),
+                        "frac_of_n_gpus": round(gbs / (peak * world), 4)})
+    finally:
+        m.close()
     return out
 
 

@@ -143,10 +143,22 @@ const char * sb_attn_noalloc_last_error(void);
 // than flags 0/1, shared experts, an expert bias, scaled weights.
 typedef struct sb_moe sb_moe;
 sb_moe * sb_moe_open(const char * path, int layer, int max_tokens, char * why, int nwhy);
+// Expert parallelism over `world` GPUs (one process each): every process calls
+// sb_moe_open_ep with the same 128-byte NCCL id (made by one of them with
+// sb_nccl_unique_id and shared by the host); this one holds experts
+// [rank*ne/world, (rank+1)*ne/world). Every process passes all tokens; the
+// router runs everywhere, each GPU runs the expert FFNs of the choices it holds,
+// the per-choice outputs are summed over the GPUs (NCCL all-reduce; each row is
+// one GPU's, zeros elsewhere, so the sum is exact) and combined in choice order
+// on every GPU: y equals the single-GPU layer's bit for bit. NCCL is loaded at
+// run time (libnccl.so.2); without it these return 0 / NULL with the reason.
+sb_moe * sb_moe_open_ep(const char * path, int layer, int max_tokens, int world, int rank, const void * nccl_id,
+                        char * why, int nwhy);
+int sb_nccl_unique_id(void * id128);
 void sb_moe_close(sb_moe * m);
-// out[10]: n_embd, expert hidden size, experts, experts per token, flags,
+// out[14]: n_embd, expert hidden size, experts, experts per token, flags,
 // max_tokens, expert width in bits, bytes of one expert as stored (low, high),
-// router bytes.
+// router bytes, GPUs, rank, first and one-past-last expert held here.
 void sb_moe_info(const sb_moe * m, int * out);
 // y[n_tok][n_embd] from x[n_tok][n_embd], device pointers, asynchronous on
 // `stream`. Calls on one handle must not overlap (they share its scratch).

@@ -520,6 +520,23 @@ static int moe_ffn(so_model * m, int L, const float * xb, float * out, int * sel
     return k;
 }
 
+// One expert's FFN of layer L on one normalized row: down(silu(gate x) * up x)
+// (the body of the choice loop of moe_ffn, sml/sml-run.c:3098-3121, before its
+// weighting). 0 if the expert does not exist.
+int so_moe_expert(so_model * m, int L, int e, const float * xb, float * out) {
+    const rec_t * g = findf(m, "blk.%d.ffn_gate.%d.weight", L, e), * u = findf(m, "blk.%d.ffn_up.%d.weight", L, e);
+    const rec_t * d = findf(m, "blk.%d.ffn_down.%d.weight", L, e);
+    if (!g || !u || !d) return 0;
+    const int F = (int) g->rows, E = (int) m->n_embd;
+    float * gv = (float *) malloc((size_t) F * 4), * uv = (float *) malloc((size_t) F * 4);
+    matvec_rec(m, g, xb, gv, 0, F);
+    matvec_rec(m, u, xb, uv, 0, F);
+    silu_mul(gv, uv, F);
+    matvec_rec(m, d, gv, out, 0, E);
+    free(gv); free(uv);
+    return 1;
+}
+
 // The MoE FFN of layer L on one (already normalized) row: returns the experts
 // per token, 0 if layer L has no router.
 int so_moe_ffn(so_model * m, int L, const float * xb, float * out, int * sel, float * w) {

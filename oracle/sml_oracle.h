@@ -36,6 +36,8 @@ int so_moe_route(const float * lg, int ne, int k, unsigned moe_flags, int * sel,
 // the chosen experts and weights (either may be NULL); returns k, 0 if layer L
 // has no router.
 int so_moe_ffn(so_model * m, int L, const float * xb, float * out, int * sel, float * w);
+// One expert's FFN output (unweighted) of layer L on a normalized row.
+int so_moe_expert(so_model * m, int L, int e, const float * xb, float * out);
 // The batched path: the int8 re-quantization of a tensor (w8: rows x nsb*256,
 // s8: rows x nsb) and the product over T rows of X (sml_g_requant8 and the int8
 // tiles' epilogue, sml/sml-gpu-fast.cu:1804-1880, 2025-2031).

@@ -93,6 +93,8 @@ def lib():
         "sb_moe_time": (ip, [vp, vp, ip, ip, fp, vp]),
         "sb_moe_route": (ip, [vp, ip, ip, ip, ctypes.c_uint, vp, vp, vp]),
         "sb_moe_last_error": (cp, []),
+        "sb_moe_open_ep": (vp, [cp, ip, ip, ip, ip, vp, cp, ip]),
+        "sb_nccl_unique_id": (ip, [vp]),
         "sb_tc_imma": (ip, [vp, vp, vp, ip, ip, ip, vp, vp]),
         "sb_tc_last_error": (cp, []),
         "sb_tc_trace": (ip, [vp, ip]),
@@ -302,19 +304,35 @@ class TensorSet:
             pass
 
 
-class MoeLayer:
-    """One mixture-of-experts FFN layer of an SSF file on the GPU (sb_moe_*)."""
+def nccl_unique_id():
+    """128 bytes for sb_moe_open_ep, made by one process and shared by the host."""
+    buf = ctypes.create_string_buffer(128)
+    if not lib().sb_nccl_unique_id(buf):
+        raise RuntimeError(f"sb_nccl_unique_id: {lib().sb_moe_last_error().decode()}")
+    return buf.raw
 
-    def __init__(self, path, layer=0, max_tokens=256):
+
+class MoeLayer:
+    """One mixture-of-experts FFN layer of an SSF file on the GPU (sb_moe_*).
+    With ep=(world, rank, nccl_id) the experts are spread over `world` GPUs
+    (one process each, every process passing all tokens)."""
+
+    def __init__(self, path, layer=0, max_tokens=256, ep=None):
         why = ctypes.create_string_buffer(512)
-        self.h = lib().sb_moe_open(path.encode(), layer, max_tokens, why, 512)
+        if ep is None:
+            self.h = lib().sb_moe_open(path.encode(), layer, max_tokens, why, 512)
+        else:
+            world, rank, nid = ep
+            idbuf = ctypes.create_string_buffer(bytes(nid), 128)
+            self.h = lib().sb_moe_open_ep(path.encode(), layer, max_tokens, world, rank, idbuf, why, 512)
         if not self.h:
             raise RuntimeError(f"sb_moe_open: {why.value.decode()}")
-        info = (ctypes.c_int * 10)()
+        info = (ctypes.c_int * 16)()
         lib().sb_moe_info(self.h, info)
         self.n_embd, self.n_ff, self.n_expert, self.k, self.flags, self.max_tokens, self.nbits = info[:7]
         self.expert_bytes = (info[7] & 0xffffffff) | (info[8] << 32)
         self.router_bytes = info[9]
+        self.world, self.rank, self.e_lo, self.e_hi = info[10:14]
 
     def forward(self, x):
         """y [T, n_embd], sel and w [T, k], distinct experts, from rows x [T, n_embd]."""

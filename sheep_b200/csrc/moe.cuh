@@ -54,6 +54,7 @@ struct MoeRouterArgs {
     const float * wr;                // [ne][E] router weights
     int T, E, ne, k, nt;             // nt: most tokens in one chunk
     unsigned flags;                  // bit 0: softmax over the chosen experts only
+    int e_lo, e_hi;                  // experts this GPU holds: only their slots are dispatched
     MoeRoute r;
     int * err;
     unsigned long long * trace;
@@ -164,7 +165,11 @@ SB_DEV void moe_dispatch(const MoeRouterArgs & g) {
     const int tid = threadIdx.x, ne = g.ne, ns = g.T * g.k;
     for (int e = tid; e < ne; e += blockDim.x) { cnt[e] = 0; fill[e] = 0; }
     __syncthreads();
-    for (int s = tid; s < ns; s += blockDim.x) atomicAdd(&cnt[g.r.sel[s]], 1);
+    // slots of experts held elsewhere (expert parallelism) are not dispatched here
+    for (int s = tid; s < ns; s += blockDim.x) {
+        const int e = g.r.sel[s];
+        if (e >= g.e_lo && e < g.e_hi) atomicAdd(&cnt[e], 1);
+    }
     __syncthreads();
     for (int e = tid; e < ne; e += blockDim.x) nch[e] = (cnt[e] + g.nt - 1) / g.nt;
     __syncthreads();
@@ -173,7 +178,7 @@ SB_DEV void moe_dispatch(const MoeRouterArgs & g) {
     __syncthreads();
     for (int s = tid; s < ns; s += blockDim.x) {
         const int e = g.r.sel[s];
-        g.r.slots[off[e] + atomicAdd(&fill[e], 1)] = s;
+        if (e >= g.e_lo && e < g.e_hi) g.r.slots[off[e] + atomicAdd(&fill[e], 1)] = s;
     }
     __syncthreads();
     for (int e = tid; e < ne; e += blockDim.x) {

@@ -10,6 +10,9 @@
 #include "sheep_b200.h"
 #include "ssf.h"
 
+#include <dlfcn.h>
+#include <nccl.h>
+
 #include <cstdio>
 #include <cstring>
 
@@ -19,8 +22,40 @@ static thread_local char g_err[512];
 
 extern "C" const char * sb_moe_last_error(void) { return g_err; }
 
+// NCCL, loaded when an expert-parallel layer is opened (single-GPU users need
+// no NCCL; in a process that already loaded one, dlopen returns that one).
+struct NcclApi {
+    ncclResult_t (*get_id)(ncclUniqueId *);
+    ncclResult_t (*init_rank)(ncclComm_t *, int, ncclUniqueId, int);
+    ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
+    ncclResult_t (*destroy)(ncclComm_t);
+    const char * (*error)(ncclResult_t);
+};
+
+static const NcclApi * nccl_api() {
+    static NcclApi api;
+    static int state = 0;   // 0 untried, 1 loaded, -1 unavailable
+    if (state) return state > 0 ? &api : nullptr;
+    state = -1;
+    void * h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return nullptr;
+    api.get_id = (ncclResult_t (*)(ncclUniqueId *)) dlsym(h, "ncclGetUniqueId");
+    api.init_rank = (ncclResult_t (*)(ncclComm_t *, int, ncclUniqueId, int)) dlsym(h, "ncclCommInitRank");
+    api.all_reduce = (ncclResult_t (*)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
+                                       cudaStream_t)) dlsym(h, "ncclAllReduce");
+    api.destroy = (ncclResult_t (*)(ncclComm_t)) dlsym(h, "ncclCommDestroy");
+    api.error = (const char * (*)(ncclResult_t)) dlsym(h, "ncclGetErrorString");
+    if (!api.get_id || !api.init_rank || !api.all_reduce || !api.destroy || !api.error) return nullptr;
+    state = 1;
+    return &api;
+}
+
 struct sb_moe {
     ssf_file f{};
+    int world = 1, rank = 0;              // expert parallelism: this GPU holds experts [rank*ne/world, ...)
+    ncclComm_t comm = nullptr;
+    MoeExchange ex{};
     Arena ar;
     MoeLayer m;
     MoeScratch s;
@@ -39,6 +74,7 @@ static bool ck(cudaError_t e, const char * what) {
 }
 
 static void moe_free(sb_moe * h) {
+    if (h->comm) nccl_api()->destroy(h->comm);
     if (h->st) cudaStreamDestroy(h->st);
     if (h->flush) cudaFree(h->flush);
     h->ar.release();
@@ -47,7 +83,15 @@ static void moe_free(sb_moe * h) {
 }
 
 static bool moe_build(sb_moe * h, char * why, int nwhy) {
-    if (!moe_upload(h->ar, h->f, h->layer, h->m, why, nwhy)) return false;
+    int e_lo = 0, e_hi = 0;
+    if (h->world > 1) {
+        const ssf_rec * rt = ssf_findf(&h->f, "blk.%d.ffn_gate_inp.weight", h->layer, 0);
+        const int ne = rt ? (int) ((uint64_t) rt->rows * rt->cols / h->f.hdr->n_embd) : 0;
+        if (ne < h->world) { snprintf(why, nwhy, "%d experts cannot spread over %d GPUs", ne, h->world); return false; }
+        e_lo = (int) ((long) ne * h->rank / h->world);
+        e_hi = (int) ((long) ne * (h->rank + 1) / h->world);
+    }
+    if (!moe_upload(h->ar, h->f, h->layer, h->m, why, nwhy, e_lo, e_hi)) return false;
     moe_carve(h->ar, h->m, h->tmax, h->s);
     h->x = (float *) h->ar.carve((size_t) h->tmax * h->m.E * 4);
     h->y = (float *) h->ar.carve((size_t) h->tmax * h->m.E * 4);
@@ -55,10 +99,28 @@ static bool moe_build(sb_moe * h, char * why, int nwhy) {
     return true;
 }
 
-extern "C" sb_moe * sb_moe_open(const char * path, int layer, int max_tokens, char * why, int nwhy) {
+static cudaError_t ep_sum(void * ctx, float * buf, size_t n, cudaStream_t st) {
+    sb_moe * h = (sb_moe *) ctx;
+    const ncclResult_t r = nccl_api()->all_reduce(buf, buf, n, ncclFloat, ncclSum, h->comm, st);
+    if (r != ncclSuccess) {
+        snprintf(g_err, sizeof g_err, "ncclAllReduce: %s", nccl_api()->error(r));
+        return cudaErrorUnknown;
+    }
+    return cudaSuccess;
+}
+
+static sb_moe * moe_open(const char * path, int layer, int max_tokens, int world, int rank, const void * id,
+                         char * why, int nwhy) {
     g_err[0] = 0;
     if (max_tokens < 1 || max_tokens > 4096) { snprintf(why, nwhy, "max_tokens must be 1..4096"); return nullptr; }
+    if (world < 1 || world > 64 || rank < 0 || rank >= world || (world > 1 && !id)) {
+        snprintf(why, nwhy, "world %d / rank %d / id", world, rank);
+        return nullptr;
+    }
+    if (world > 1 && !nccl_api()) { snprintf(why, nwhy, "NCCL (libnccl.so.2) could not be loaded"); return nullptr; }
     sb_moe * h = new sb_moe();
+    h->world = world;
+    h->rank = rank;
     if (!ssf_open(&h->f, path, why, nwhy)) { delete h; return nullptr; }
     if (layer < 0 || layer >= (int) h->f.hdr->n_layer) {
         snprintf(why, nwhy, "layer %d out of range", layer);
@@ -83,7 +145,42 @@ extern "C" sb_moe * sb_moe_open(const char * path, int layer, int max_tokens, ch
         moe_free(h);
         return nullptr;
     }
+    if (world > 1) {
+        ncclUniqueId uid;
+        memcpy(&uid, id, sizeof uid);
+        const ncclResult_t r = nccl_api()->init_rank(&h->comm, world, uid, rank);
+        if (r != ncclSuccess) {
+            snprintf(why, nwhy, "ncclCommInitRank: %s", nccl_api()->error(r));
+            h->comm = nullptr;
+            moe_free(h);
+            return nullptr;
+        }
+        h->ex.sum = ep_sum;
+        h->ex.ctx = h;
+    }
     return h;
+}
+
+extern "C" sb_moe * sb_moe_open(const char * path, int layer, int max_tokens, char * why, int nwhy) {
+    return moe_open(path, layer, max_tokens, 1, 0, nullptr, why, nwhy);
+}
+
+// Expert parallelism: `world` processes (one GPU each) call this with the same
+// id; this one holds experts [rank*ne/world, (rank+1)*ne/world).
+extern "C" sb_moe * sb_moe_open_ep(const char * path, int layer, int max_tokens, int world, int rank,
+                                   const void * nccl_id, char * why, int nwhy) {
+    return moe_open(path, layer, max_tokens, world, rank, nccl_id, why, nwhy);
+}
+
+extern "C" int sb_nccl_unique_id(void * id128) {
+    g_err[0] = 0;
+    const NcclApi * api = nccl_api();
+    if (!api || !id128) { snprintf(g_err, sizeof g_err, "NCCL (libnccl.so.2) could not be loaded"); return 0; }
+    ncclUniqueId uid;
+    const ncclResult_t r = api->get_id(&uid);
+    if (r != ncclSuccess) { snprintf(g_err, sizeof g_err, "ncclGetUniqueId: %s", api->error(r)); return 0; }
+    memcpy(id128, &uid, sizeof uid);
+    return 1;
 }
 
 extern "C" void sb_moe_close(sb_moe * h) {
@@ -100,12 +197,19 @@ extern "C" void sb_moe_info(const sb_moe * h, int * out) {
     out[5] = h->tmax; out[6] = h->m.gu.nbits;
     out[7] = (int) (h->m.expert_file_bytes & 0xffffffffu); out[8] = (int) (h->m.expert_file_bytes >> 32);
     out[9] = (int) h->m.router_bytes;
+    out[10] = h->world; out[11] = h->rank; out[12] = h->m.e_lo; out[13] = h->m.e_hi;
 }
 
 static bool enqueue(sb_moe * h, const float * x, int T, float * y, cudaStream_t st) {
     bool ok = true;
     moe_enqueue(h->m, h->s, x, T, nullptr, 0.0f, y, 0, h->nsm, st, true, h->err, nullptr, 0,
-                [&](cudaError_t e, const char * name) { if (ok && !ck(e, name)) ok = false; });
+                [&](cudaError_t e, const char * name) {
+                    if (ok && e != cudaSuccess) {
+                        if (e != cudaErrorUnknown || !g_err[0]) ck(e, name);   // an NCCL failure set its own message
+                        ok = false;
+                    }
+                },
+                h->world > 1 ? &h->ex : nullptr);
     return ok;
 }
 

@@ -18,6 +18,7 @@ namespace sb {
 
 struct MoeLayer {
     int E = 0, F = 0, ne = 0, k = 0;
+    int e_lo = 0, e_hi = 0;                                // experts held on this GPU (all, unless expert-parallel)
     unsigned flags = 0;
     const float * router = nullptr;                        // [ne][E]
     TT gu{}, dn{};                                         // geometry (expert 0's tiles)
@@ -67,8 +68,11 @@ inline int moe_pick_tr(int cols, int nbits, int six, int has_min, int even) {
     return 0;
 }
 
-// Upload layer L's router and experts (both arena passes run this).
-inline bool moe_upload(Arena & a, const ssf_file & f, int L, MoeLayer & m, char * why, int nwhy) {
+// Upload layer L's router and experts [e_lo, e_hi) (all when e_hi <= 0); both
+// arena passes run this. Every expert's shapes are checked; only the held ones
+// are uploaded.
+inline bool moe_upload(Arena & a, const ssf_file & f, int L, MoeLayer & m, char * why, int nwhy, int e_lo = 0,
+                       int e_hi = 0) {
     const ssf_hdr * h = f.hdr;
     const int E = (int) h->n_embd;
     const ssf_rec * rt = ssf_findf(&f, "blk.%d.ffn_gate_inp.weight", L, 0);
@@ -90,6 +94,9 @@ inline bool moe_upload(Arena & a, const ssf_file & f, int L, MoeLayer & m, char 
     m.flags = h->moe_flags;
     m.router = upload_f32(a, f, rt);
     m.router_bytes = rn * 4;
+    m.e_lo = e_hi > 0 ? e_lo : 0;
+    m.e_hi = e_hi > 0 ? (e_hi < m.ne ? e_hi : m.ne) : m.ne;
+    if (m.e_lo < 0 || m.e_lo >= m.e_hi) { snprintf(why, nwhy, "layer %d: empty expert range", L); return false; }
     std::vector<const uint8_t *> gt(m.ne), dt(m.ne);
     std::vector<const int32_t *> gp(m.ne), di(m.ne);
     int gtr = 0, dtr = 0;
@@ -111,6 +118,11 @@ inline bool moe_upload(Arena & a, const ssf_file & f, int L, MoeLayer & m, char 
             gtr = moe_pick_tr(E, (int) g->nbits, f.scale6, g->mq_n != 0, 1);
             dtr = moe_pick_tr(F, (int) d->nbits, f.scale6, d->mq_n != 0, 0);
             if (!gtr || !dtr) { snprintf(why, nwhy, "layer %d: expert rows too wide for the tile ring", L); return false; }
+            m.expert_file_bytes = moe_rec_bytes(g) + moe_rec_bytes(u) + moe_rec_bytes(d);
+        }
+        if (e < m.e_lo || e >= m.e_hi) {   // held by another GPU
+            gt[e] = nullptr; gp[e] = nullptr; dt[e] = nullptr; di[e] = nullptr;
+            continue;
         }
         TT tg, td;
         // gate / up interleaved: a tile of gtr rows holds gtr/2 gate rows then the same up rows
@@ -119,13 +131,12 @@ inline bool moe_upload(Arena & a, const ssf_file & f, int L, MoeLayer & m, char 
                 return i >= F ? RowSrc{nullptr, 0} : RowSrc{j < hh ? g : u, i}; }, tg, why, nwhy) ||
             !upload_tt(a, f, d, E, dtr, 0, 0, [&](int r) { return RowSrc{r < E ? d : nullptr, r}; }, td, why, nwhy))
             return false;
-        if (e == 0) { m.gu = tg; m.dn = td; }
+        if (e == m.e_lo) { m.gu = tg; m.dn = td; }
         if (tg.nbits != m.gu.nbits || tg.has_min != m.gu.has_min || td.nbits != m.dn.nbits || td.has_min != m.dn.has_min) {
             snprintf(why, nwhy, "layer %d: experts differ in width or fields", L);
             return false;
         }
         gt[e] = tg.tiles; gp[e] = tg.perm; dt[e] = td.tiles; di[e] = td.iperm;
-        if (e == 0) m.expert_file_bytes = moe_rec_bytes(g) + moe_rec_bytes(u) + moe_rec_bytes(d);
     }
     m.gu_tiles = (const uint8_t * const *) a.upload(gt.data(), gt.size() * sizeof(void *));
     m.gu_perm = (const int32_t * const *) a.upload(gp.data(), gp.size() * sizeof(void *));
@@ -179,19 +190,32 @@ inline cudaError_t moe_gemv(int mode, int nt, const MoeGArgs & g, int grid, cuda
     return r;
 }
 
+// Expert parallelism: the per-choice down outputs ([T*k][E]) are summed over
+// the GPUs between the down GEMV and the combine. Each row is written by the one
+// GPU holding its expert and is zero on the others, so the sum is exact and the
+// combine then runs in choice order as on one GPU.
+struct MoeExchange {
+    cudaError_t (*sum)(void * ctx, float * buf, size_t n, cudaStream_t st);
+    void * ctx;
+};
+
 // The launches of one MoE FFN over T <= s.T input rows x ([T][E]): router and
 // routing (x RMS-normalized by norm_w first when given), gate/up, down, combine
 // into y ([T][E]; added to it when resid). post(err, name) sees every launch.
+// With ex (expert parallelism) the per-choice outputs are zeroed first and
+// summed across GPUs before the combine.
 template <class Post>
 inline void moe_enqueue(const MoeLayer & m, const MoeScratch & s, const float * x, int T, const float * norm_w,
                         float eps, float * y, int resid, int nsm, cudaStream_t st, bool pdl, int * err,
-                        unsigned long long * trace, int launch_id, Post post) {
+                        unsigned long long * trace, int launch_id, Post post, const MoeExchange * ex = nullptr) {
     const int nt = T == 1 ? 1 : 8;   // one token per chunk at T = 1: a token never picks an expert twice
+    if (ex) post(cudaMemsetAsync(s.yk, 0, (size_t) T * m.k * m.E * 4, st), "moe.zero");
     {
         MoeRouterArgs r;
         memset(&r, 0, sizeof r);
         r.x = x; r.norm_w = norm_w; r.eps = eps; r.xn = norm_w ? s.xn : nullptr; r.wr = m.router;
         r.T = T; r.E = m.E; r.ne = m.ne; r.k = m.k; r.nt = nt; r.flags = m.flags; r.r = s.r;
+        r.e_lo = m.e_lo; r.e_hi = m.e_hi;
         r.err = err; r.trace = trace; r.launch_id = launch_id;
         static bool attr = false;
         if (!attr) {
@@ -232,6 +256,7 @@ inline void moe_enqueue(const MoeLayer & m, const MoeScratch & s, const float * 
         a.launch_id = launch_id + 2;
         post(moe_gemv(MG_DN, nt, a, nsm, st, pdl), "moe.down");
     }
+    if (ex) post(ex->sum(ex->ctx, s.yk, (size_t) T * m.k * m.E, st), "moe.exchange");
     {
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3((m.E + 255) / 256, T);

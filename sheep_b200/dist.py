@@ -1,9 +1,11 @@
 """Multi-GPU plumbing for the bench: one process per GPU (torchrun), the
 decode path run as independent replicas (batch-1 decode of one sequence does
-not shard), times reduced as the max over ranks.
+not shard), times reduced as the max over ranks; and the host side of the
+expert-parallel MoE layer (sb_moe_open_ep): the NCCL id every rank must share
+and the experts each rank holds.
 
-torch.distributed carries only the barrier and the max; no data of the decode
-path crosses ranks.
+torch.distributed carries only the barrier, the max and the id; the MoE layer's
+data crosses ranks in the library's own NCCL all-reduce.
 """
 import os
 
@@ -41,3 +43,21 @@ def replica_throughput(steps, seconds_max, world):
     """Whole-job tokens/s of `world` replicas that each ran `steps` tokens,
     the slowest taking `seconds_max` (weak scaling)."""
     return world * steps / seconds_max
+
+
+def expert_range(n_expert, world, rank):
+    """The experts rank `rank` of `world` holds: [lo, hi) (as sb_moe_open_ep)."""
+    return n_expert * rank // world, n_expert * (rank + 1) // world
+
+
+def share_nccl_id(dist, device="cuda"):
+    """The 128-byte NCCL id made by rank 0 (sb_nccl_unique_id), broadcast to every rank."""
+    import torch
+    import sheep_b200
+    _, rank, _ = rank_info()
+    t = torch.zeros(128, dtype=torch.uint8, device=device)
+    if rank == 0:
+        t.copy_(torch.frombuffer(bytearray(sheep_b200.nccl_unique_id()), dtype=torch.uint8))
+    if dist is not None:
+        dist.broadcast(t, src=0)
+    return bytes(t.cpu().numpy().tobytes())

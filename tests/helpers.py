@@ -125,6 +125,13 @@ class Oracle:
             assert k > 0, "layer has no router"
         return y, sel[:, :k], w[:, :k]
 
+    def moe_expert(self, layer, e, x):
+        """One expert's unweighted FFN output on a normalized row."""
+        x = np.ascontiguousarray(x, np.float32)
+        y = np.zeros_like(x)
+        assert self.lib().so_moe_expert(self.m, layer, e, _p(x), _p(y))
+        return y
+
     def requant8(self, name, rows, cols):
         nsb = (cols // 32 + 7) // 8
         w8 = np.zeros((rows, nsb * 256), np.int8)
