@@ -99,5 +99,9 @@ SB_DEV uint32_t cluster_map(const void * smem_ptr, uint32_t rank) {
 SB_DEV void st_cluster(uint32_t addr, float v) {
     asm volatile("st.shared::cluster.f32 [%0], %1;" :: "r"(addr), "f"(v) : "memory");
 }
+SB_DEV void st_cluster4(uint32_t addr, float a, float b, float c, float d) {
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" :: "r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+                 : "memory");
+}
 
 }  // namespace sb

@@ -263,23 +263,31 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
     if (g.split > 1) {
         // The slices of a tile are one cluster (rank = z). Once every CTA is past
         // its main loop (the leader's ring is idle), slices 1.. store their sums
-        // into the leader's ring as [slice - 1][token][row]; the leader adds them
-        // in slice order, so the sum does not depend on arrival order
-        // (sml_g_splitk_sum, sml/sml-gpu-fast.cu:2057-2065).
+        // into the leader's ring as [slice - 1][token / 4][row][4] (four tokens
+        // per 16-byte store; a warp's 32 rows are 512 contiguous bytes); the
+        // leader adds them in slice order, so the sum does not depend on arrival
+        // order (sml_g_splitk_sum, sml/sml-gpu-fast.cu:2057-2065).
         cluster_sync();
         float * pbuf = reinterpret_cast<float *>(tsm);
         if (warp >= 2 && z > 0) {
-            const uint32_t base = cluster_map(pbuf + (size_t) (z - 1) * N * 128 + row, 0);
+            const uint32_t base = cluster_map(pbuf + (size_t) (z - 1) * N * 128 + row * 4, 0);
 #pragma unroll
-            for (int t = 0; t < N; t++) st_cluster(base + (uint32_t) (t * 128 * 4), acc[t]);
+            for (int t = 0; t < N; t += 4)
+                st_cluster4(base + (uint32_t) (t * 128 * 4), acc[t], acc[t + 1], acc[t + 2], acc[t + 3]);
         }
         cluster_sync();
         if (warp >= 2) {
             if (z == 0) {
                 for (int k = 1; k < g.split; k++) {
-                    const float * pk = pbuf + (size_t) (k - 1) * N * 128 + row;
+                    const float * pk = pbuf + (size_t) (k - 1) * N * 128 + row * 4;
 #pragma unroll
-                    for (int t = 0; t < N; t++) acc[t] = __fadd_rn(acc[t], pk[t * 128]);
+                    for (int t = 0; t < N; t += 4) {
+                        const float4 v = *reinterpret_cast<const float4 *>(pk + t * 128);
+                        acc[t] = __fadd_rn(acc[t], v.x);
+                        acc[t + 1] = __fadd_rn(acc[t + 1], v.y);
+                        acc[t + 2] = __fadd_rn(acc[t + 2], v.z);
+                        acc[t + 3] = __fadd_rn(acc[t + 3], v.w);
+                    }
                 }
             } else {
                 ok = false;   // only the leader writes the tile
