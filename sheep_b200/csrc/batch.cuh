@@ -571,13 +571,16 @@ __global__ void __launch_bounds__(kMThreads, 2) k_battn_mma(const __grid_constan
             split_h2(pr[1][2], pr[1][3], pa[3], pl[3]);
             const uint32_t vaddr = smem_u32(Vs + (pw + ((lane >> 3) & 1) * 8 + (lane & 7)) * RS + (lane >> 4) * 8);
 #pragma unroll
-            for (int n = 0; n < NT; n += 2) {
-                uint32_t b0, b1, b2, b3;
-                ldsm4t(vaddr + n * 16, b0, b1, b2, b3);
-                mma16816(o[n], pa, b0, b1);
-                mma16816(o[n], pl, b0, b1);
-                mma16816(o[n + 1], pa, b2, b3);
-                mma16816(o[n + 1], pl, b2, b3);
+            // four output tiles at a time: their hi MMAs, then their lo MMAs, so
+            // the two MMAs into one accumulator are four apart
+            for (int n = 0; n < NT; n += 4) {
+                uint32_t b[8];
+                ldsm4t(vaddr + n * 16, b[0], b[1], b[2], b[3]);
+                ldsm4t(vaddr + (n + 2) * 16, b[4], b[5], b[6], b[7]);
+#pragma unroll
+                for (int i = 0; i < 4; i++) mma16816(o[n + i], pa, b[2 * i], b[2 * i + 1]);
+#pragma unroll
+                for (int i = 0; i < 4; i++) mma16816(o[n + i], pl, b[2 * i], b[2 * i + 1]);
             }
         }
         __syncthreads();   // the stage is free
