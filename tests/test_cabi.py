@@ -136,3 +136,19 @@ def _ref_open(path):
     if h:
         L.refh_close(ctypes.c_void_p(h))
     return bool(h)
+
+
+def test_nccl_id_without_gpu():
+    """The expert-parallel layer's NCCL id comes from the library with NCCL
+    loaded at run time and no GPU needed; each call makes a new one."""
+    import sheep_b200
+    a, b = sheep_b200.nccl_unique_id(), sheep_b200.nccl_unique_id()
+    assert len(a) == 128 and len(b) == 128 and a != b
+
+
+def test_expert_ranges_cover_every_expert_once():
+    from sheep_b200 import dist as sd
+    for ne in (8, 16, 60, 128, 256):
+        for world in (1, 2, 3, 4, 8):
+            got = [e for r in range(world) for e in range(*sd.expert_range(ne, world, r))]
+            assert got == list(range(ne))
