@@ -331,18 +331,54 @@ static __global__ void __launch_bounds__(kAttnThreads) k_attn(const __grid_const
     __syncthreads();
     if (!last_flag) return;
     __threadfence();
-    // the last chunk of this head combines every chunk, in chunk order
-    const volatile float * P = g.part + (size_t) h * g.max_chunks * (hd + 2);
-    float M = -INFINITY;
-    for (int k = 0; k < nchunk; k++) M = fmaxf(M, P[k * (hd + 2)]);
-    float Lsum = 0.0f;
-    for (int k = 0; k < nchunk; k++) Lsum += P[k * (hd + 2) + 1] * expf(P[k * (hd + 2)] - M);
-    for (int i = tid; i < hd; i += blockDim.x) {
-        float o = 0.0f;
-        for (int k = 0; k < nchunk; k++) o += P[k * (hd + 2) + 2 + i] * expf(P[k * (hd + 2)] - M);
-        g.out[h * hd + i] = o / Lsum;
+#ifdef SB_TRACE
+    if (g.trace && tid == 0 && h < kTraceCtas) g.trace[((size_t) g.launch_id * kTraceCtas + h) * 8 + 6] = global_ns();
+#endif
+    // the last chunk of this head combines every chunk, in chunk order. The
+    // partials are read through L2 (after the fence above) with plain loads; up
+    // to 8 chunks, a thread issues every load it needs (each chunk's max and sum,
+    // and its own output element's partials) before using any, so the combine
+    // costs one round trip. The arithmetic is the same for any chunk count.
+    const float * P = g.part + (size_t) h * g.max_chunks * (hd + 2);
+    if (nchunk <= 8) {
+        float mk[8], lk[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) {
+            mk[k] = k < nchunk ? __ldcg(P + k * (hd + 2)) : -INFINITY;
+            lk[k] = k < nchunk ? __ldcg(P + k * (hd + 2) + 1) : 0.0f;
+        }
+        for (int i = tid; i < hd; i += blockDim.x) {
+            float pk[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) pk[k] = k < nchunk ? __ldcg(P + k * (hd + 2) + 2 + i) : 0.0f;
+            float M = -INFINITY;
+#pragma unroll
+            for (int k = 0; k < 8; k++) if (k < nchunk) M = fmaxf(M, mk[k]);
+            float Lsum = 0.0f, o = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                if (k < nchunk) Lsum += lk[k] * expf(mk[k] - M);
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                if (k < nchunk) o += pk[k] * expf(mk[k] - M);
+            g.out[h * hd + i] = o / Lsum;
+        }
+    } else {
+        float M = -INFINITY;
+        for (int k = 0; k < nchunk; k++) M = fmaxf(M, __ldcg(P + k * (hd + 2)));
+        float Lsum = 0.0f;
+        for (int k = 0; k < nchunk; k++) Lsum += __ldcg(P + k * (hd + 2) + 1) * expf(__ldcg(P + k * (hd + 2)) - M);
+        for (int i = tid; i < hd; i += blockDim.x) {
+            float o = 0.0f;
+            for (int k = 0; k < nchunk; k++) o += __ldcg(P + k * (hd + 2) + 2 + i) * expf(__ldcg(P + k * (hd + 2)) - M);
+            g.out[h * hd + i] = o / Lsum;
+        }
     }
     if (tid == 0) g.cnt[h] = 0;
+#ifdef SB_TRACE
+    __syncthreads();
+    if (g.trace && tid == 0 && h < kTraceCtas) g.trace[((size_t) g.launch_id * kTraceCtas + h) * 8 + 7] = global_ns();
+#endif
 }
 
 }  // namespace sb
