@@ -445,6 +445,7 @@ def moe_ep_microbench(peak, dist, world, rank, max_over_ranks, reps=20):
     every rank's router."""
     import sheep_b200
     from sheep_b200 import configs
+    from sheep_b200 import dist as sdist
     nid = sdist.share_nccl_id(dist)
     m = sheep_b200.MoeLayer(model_path(configs.CONFIGS["qwen3-30b-a3b-moe-layer"], 0, None), max_tokens=256,
                             ep=(world, rank, nid))
