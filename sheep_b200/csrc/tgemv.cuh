@@ -460,6 +460,14 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__
     // ---------------- consumers
     pdl_wait();
     SB_MARK(g.trace, g.launch_id, 1);
+    // o / down add into the residual stream: the rows of the warp's first tile
+    // are read now, so that add waits on no L2 round trip after the tile (each
+    // row is this warp's alone; earlier kernels' writes are visible past the wait)
+    float res0 = 0.0f;
+    if (MODE == GM_O || MODE == GM_DOWN) {
+        const int r = (t0 + warp) * t.TR + lane;
+        if (t0 + warp < t1 && lane < t.TR && r < t.rows) res0 = g.out[r];
+    }
     ActS a = act_carve(smem, t.cols);
     bool failed = false;   // after one wait gives up, the rest are skipped
     tg_stage(g, a, red, smem, SL, &statics, failed);
@@ -498,7 +506,7 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__
                 if (g.bias) y += g.bias[r];
                 g.out[r] = y;
             } else if (MODE == GM_O || MODE == GM_DOWN) {
-                g.out[r] += y;
+                g.out[r] = (k < kConsWarps ? res0 : g.out[r]) + y;
             } else if (MODE == GM_HEAD) {
                 g.out[r] = y;
                 if (y > best_v || (y == best_v && r < best_i)) { best_v = y; best_i = r; }
