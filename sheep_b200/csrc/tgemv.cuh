@@ -458,6 +458,21 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__
     }
 
     // ---------------- consumers
+    // static epilogue data of the warp's first tile (the hidden vector's order,
+    // the q|k|v and gate/up biases: uploaded weights, which no kernel writes)
+    // is read before the dependency wait, so the tile's epilogue waits on no load
+    int sc0 = 0;
+    float gb0 = 0.0f, ub0 = 0.0f;
+    if (MODE == GM_FFN) {
+        const int idx = (t0 + warp) * (t.TR / 2) + lane;
+        if (t0 + warp < t1 && lane < t.TR / 2 && idx < g.ffn_f) {
+            sc0 = g.scatter[idx];
+            if (g.bias) { gb0 = g.bias[idx]; ub0 = g.bias[g.ffn_f + idx]; }
+        }
+    } else if (MODE == GM_QKV) {
+        const int r = (t0 + warp) * t.TR + lane;
+        if (g.bias && t0 + warp < t1 && lane < t.TR && r < t.rows) gb0 = g.bias[r];
+    }
     pdl_wait();
     SB_MARK(g.trace, g.launch_id, 1);
     // o / down add into the residual stream: the rows of the warp's first tile
@@ -492,10 +507,12 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__
             const float up = __shfl_down_sync(0xffffffffu, acc, TR / 2);
             const int idx = i * (TR / 2) + lane;
             if (lane < TR / 2 && idx < g.ffn_f) {
+                const bool first = k < kConsWarps;
                 float gv = acc, uv = up;
-                if (g.bias) { gv += g.bias[idx]; uv += g.bias[g.ffn_f + idx]; }
-                if (SB_CHECK(g.err, g.scatter[idx] >= 0 && g.scatter[idx] < g.ffn_f, 108))
-                    g.out[g.scatter[idx]] = silu_mul(gv, uv);
+                if (g.bias) { gv += first ? gb0 : g.bias[idx]; uv += first ? ub0 : g.bias[g.ffn_f + idx]; }
+                const int sc = first ? sc0 : g.scatter[idx];
+                if (SB_CHECK(g.err, sc >= 0 && sc < g.ffn_f, 108))
+                    g.out[sc] = silu_mul(gv, uv);
             }
             continue;
         }
@@ -503,7 +520,7 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__
         if (lane < TR && r < t.rows) {
             float y = acc;
             if (MODE == GM_QKV || MODE == GM_PLAIN) {
-                if (g.bias) y += g.bias[r];
+                if (g.bias) y += (MODE == GM_QKV && k < kConsWarps) ? gb0 : g.bias[r];
                 g.out[r] = y;
             } else if (MODE == GM_O || MODE == GM_DOWN) {
                 g.out[r] = (k < kConsWarps ? res0 : g.out[r]) + y;
