@@ -169,6 +169,44 @@ SB_DEV void quant_team(float4 v, int grp, int sub, ActS & a, const TGArgs & g, b
     }
 }
 
+// quant_team with four lanes per group, 8 values per lane (v0 then v1 are
+// the group's values 8*sub .. 8*sub+7): half the shuffles and divisions per
+// group. amax and the integer sum are exact, so the codes, scale and sum are
+// quant_team's.
+SB_DEV void quant_quad(float4 v0, float4 v1, int grp, int sub, ActS & a, const TGArgs & g, bool ex, bool store) {
+    float amax = fmaxf(fmaxf(fmaxf(fabsf(v0.x), fabsf(v0.y)), fmaxf(fabsf(v0.z), fabsf(v0.w))),
+                       fmaxf(fmaxf(fabsf(v1.x), fabsf(v1.y)), fmaxf(fabsf(v1.z), fabsf(v1.w))));
+#pragma unroll
+    for (int o = 2; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float sc = __fdiv_rn(amax, 127.0f);
+    const float is = sc > 0.0f ? __frcp_rn(sc) : 0.0f;
+    const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+    uint32_t w[2] = {0u, 0u};
+    int sum = 0;
+#pragma unroll
+    for (int b = 0; b < 8; b++) {
+        int q = __float2int_rn(__fmul_rn(vv[b], is));
+        q = q > 127 ? 127 : q < -127 ? -127 : q;
+        sum += q;
+        w[b >> 2] |= ((uint32_t) (q & 0xff)) << (8 * (b & 3));
+    }
+#pragma unroll
+    for (int o = 2; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    if (!store) return;
+    // values 8*sub .. 8*sub+7 sit in one 16-byte slot row: one 8-byte store
+    *reinterpret_cast<uint2 *>(a.q + act_slot_off(a.n, grp, 8 * sub)) = make_uint2(w[0], w[1]);
+    if (sub == 0) {
+        a.xs[grp] = sc;
+        a.xsum[grp] = sc * (float) sum;
+    }
+    if (ex) {
+        uint32_t * d = reinterpret_cast<uint32_t *>(g.act_q + grp * kGroup + 8 * sub);
+        d[0] = w[0];
+        d[1] = w[1];
+        if (sub == 0) { g.act_s[grp] = sc; g.act_sum[grp] = sum; }
+    }
+}
+
 // Quantize a team's 4 values of group grp into a (no export).
 SB_DEV void quant_team_to(float4 v, int grp, int sub, ActS & a, bool store) {
     float amax = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
@@ -209,24 +247,37 @@ SB_DEV void tg_stage(const TGArgs & g, ActS & a, double * red, uint8_t * smem, c
     const int team = tid >> 3, sub = tid & 7, nteam = kConsThreads / 8;
     const bool ex = g.act_q && blockIdx.x == 0;
     if (g.in_permuted) {
-        // every round's load issued before any group is quantized
-        constexpr int kR = 8;   // rounds held in registers: n <= 8 * nteam * 32
-        float4 v[kR];
+        // every round's load issued before any group is quantized; four lanes
+        // per group, 32 bytes each
+        constexpr int kR = 4;   // rounds held in registers: n <= 4 * nquad * 32
+        const int quad = tid >> 2, qs = tid & 3, nquad = kConsThreads / 4;
+        float4 v[kR][2];
 #pragma unroll
         for (int r = 0; r < kR; r++) {
-            const int grp = r * nteam + team;
-            v[r] = grp < ng ? *reinterpret_cast<const float4 *>(g.in + grp * kGroup + 4 * sub) : make_float4(0.f, 0.f, 0.f, 0.f);
+            const int grp = r * nquad + quad;
+            if (grp < ng) {
+                const float4 * p = reinterpret_cast<const float4 *>(g.in + grp * kGroup + 8 * qs);
+                v[r][0] = p[0];
+                v[r][1] = p[1];
+            } else {
+                v[r][0] = v[r][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
         }
         SB_MARK(g.trace, g.launch_id, 5);   // thread 0's loads are issued
 #pragma unroll
         for (int r = 0; r < kR; r++) {
-            const int grp = r * nteam + team;
-            if (r * nteam < ng) quant_team(v[r], grp, sub, a, g, ex, grp < ng);
+            const int grp = r * nquad + quad;
+            if (r * nquad < ng) quant_quad(v[r][0], v[r][1], grp, qs, a, g, ex, grp < ng);
         }
-        for (int base = kR * nteam; base < ng; base += nteam) {
-            const int grp = base + team;
-            const float4 w4 = grp < ng ? *reinterpret_cast<const float4 *>(g.in + grp * kGroup + 4 * sub) : make_float4(0.f, 0.f, 0.f, 0.f);
-            quant_team(w4, grp, sub, a, g, ex, grp < ng);
+        for (int base = kR * nquad; base < ng; base += nquad) {
+            const int grp = base + quad;
+            float4 w0 = make_float4(0.f, 0.f, 0.f, 0.f), w1 = w0;
+            if (grp < ng) {
+                const float4 * p = reinterpret_cast<const float4 *>(g.in + grp * kGroup + 8 * qs);
+                w0 = p[0];
+                w1 = p[1];
+            }
+            quant_quad(w0, w1, grp, qs, a, g, ex, grp < ng);
         }
         bar_sync(1, kConsThreads);
         return;
