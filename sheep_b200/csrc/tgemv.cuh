@@ -240,7 +240,7 @@ SB_DEV void quant_team_to(float4 v, int grp, int sub, ActS & a, bool store) {
 // sml/sml-run.c:147-152); teams of 8 lanes then quantize groups, reading
 // x[perm[i]] and the gain from shared memory (both bulk-loaded by the producer
 // before the wait; `statics` completes when they land). Pre-permuted input:
-// each team reads its group with 16-byte loads.
+// quads of 4 lanes, each lane reading its 8 values with two 16-byte loads.
 SB_DEV void tg_stage(const TGArgs & g, ActS & a, double * red, uint8_t * smem, const StageLayout & L,
                      uint64_t * statics, bool & failed) {
     const int n = g.t.cols, ng = n / kGroup, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
@@ -472,7 +472,20 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__
             mbar_expect_tx(&statics, sb);
             if (!g.in_permuted) bulk_g2s(smem + SL.perm_off, t.perm, (uint32_t) t.cols * 4, &statics);
             if (g.norm_w) bulk_g2s(smem + SL.w_off, g.norm_w, (uint32_t) t.cols * 4, &statics);
-            if (g.prefetch && t1 > t0) prefetch_l2(t.tiles + (size_t) t0 * t.tb, (size_t) (t1 - t0) * t.tb);
+        }
+        __syncwarp();
+        // lane j < ns owns ring stage j and issues its tiles t0 + j, t0 + j + ns, ...:
+        // one warp instruction issues the first lap's ns copies, ahead of the
+        // L2 prefetches, which the copy engine would otherwise work through first
+        const uint32_t tb = t.tb;
+        if (lane < ns && t0 + lane < t1) {
+            mbar_expect_tx(&full[lane], tb);
+            bulk_g2s(ring + (size_t) lane * tb, t.tiles + (size_t) (t0 + lane) * tb, tb, &full[lane]);
+        }
+        __syncwarp();
+        if (lane == 0) {
+            // the tiles past the first lap, and the next kernel's share
+            if (g.prefetch && t1 > t0 + ns) prefetch_l2(t.tiles + (size_t) (t0 + ns) * tb, (size_t) (t1 - t0 - ns) * tb);
             if (g.next_tiles && (int) blockIdx.x < g.next_grid) {
                 const int n0 = (int) ((long) g.next_ntiles * blockIdx.x / g.next_grid);
                 const int n1 = (int) ((long) g.next_ntiles * (blockIdx.x + 1) / g.next_grid);
@@ -483,14 +496,11 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__
 #endif
         }
         __syncwarp();
-        // lane j < ns owns ring stage j and issues its tiles t0 + j, t0 + j + ns, ...:
-        // one warp instruction issues up to ns copies
         if (lane < ns) {
             const int s = lane;
-            const uint32_t tb = t.tb;
-            int lap = 0;
-            for (int i = t0 + s; i < t1; i += ns, lap++) {
-                if (lap > 0 && !mbar_wait(&empty[s], (lap - 1) & 1, g.err, 1)) break;
+            int lap = t0 + s < t1 ? 1 : 0;
+            for (int i = t0 + s + ns; i < t1; i += ns, lap++) {
+                if (!mbar_wait(&empty[s], (lap - 1) & 1, g.err, 1)) break;
                 mbar_expect_tx(&full[s], tb);
                 bulk_g2s(ring + (size_t) s * tb, t.tiles + (size_t) i * tb, tb, &full[s]);
             }
