@@ -169,40 +169,52 @@ SB_DEV void quant_team(float4 v, int grp, int sub, ActS & a, const TGArgs & g, b
     }
 }
 
-// quant_team with four lanes per group, 8 values per lane (v0 then v1 are
-// the group's values 8*sub .. 8*sub+7): half the shuffles and divisions per
-// group. amax and the integer sum are exact, so the codes, scale and sum are
-// quant_team's.
-SB_DEV void quant_quad(float4 v0, float4 v1, int grp, int sub, ActS & a, const TGArgs & g, bool ex, bool store) {
-    float amax = fmaxf(fmaxf(fmaxf(fabsf(v0.x), fabsf(v0.y)), fmaxf(fabsf(v0.z), fabsf(v0.w))),
-                       fmaxf(fmaxf(fabsf(v1.x), fabsf(v1.y)), fmaxf(fabsf(v1.z), fabsf(v1.w))));
+// quant_team with LPG lanes per group (4 or 2), 32/LPG values per lane (v[k]
+// holds the group's values (32/LPG)*sub + 4k .. +3): fewer shuffles and
+// divisions per group than 8 lanes of 4. amax and the integer sum are exact
+// whatever the lane split, so the codes, scale and sum are quant_team's (the
+// reciprocal by __frcp_rn is the same IEEE value as 1.0f/s). A lane's codes
+// land as 8-byte stores in the slot layout (8 consecutive values share one
+// 16-byte slot row).
+template <int LPG>
+SB_DEV void quant_lanes(const float4 (&v)[8 / LPG], int grp, int sub, ActS & a, const TGArgs & g, bool ex, bool store) {
+    constexpr int NV = 8 / LPG;   // float4s per lane
+    float amax = 0.0f;
 #pragma unroll
-    for (int o = 2; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    for (int k = 0; k < NV; k++)
+        amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v[k].x), fabsf(v[k].y)), fmaxf(fabsf(v[k].z), fabsf(v[k].w))));
+#pragma unroll
+    for (int o = LPG / 2; o; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
     const float sc = __fdiv_rn(amax, 127.0f);
     const float is = sc > 0.0f ? __frcp_rn(sc) : 0.0f;
-    const float vv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-    uint32_t w[2] = {0u, 0u};
+    uint32_t w[NV];
     int sum = 0;
 #pragma unroll
-    for (int b = 0; b < 8; b++) {
-        int q = __float2int_rn(__fmul_rn(vv[b], is));
-        q = q > 127 ? 127 : q < -127 ? -127 : q;
-        sum += q;
-        w[b >> 2] |= ((uint32_t) (q & 0xff)) << (8 * (b & 3));
+    for (int k = 0; k < NV; k++) {
+        const float vv[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+        w[k] = 0u;
+#pragma unroll
+        for (int b = 0; b < 4; b++) {
+            int q = __float2int_rn(__fmul_rn(vv[b], is));
+            q = q > 127 ? 127 : q < -127 ? -127 : q;
+            sum += q;
+            w[k] |= ((uint32_t) (q & 0xff)) << (8 * b);
+        }
     }
 #pragma unroll
-    for (int o = 2; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    for (int o = LPG / 2; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
     if (!store) return;
-    // values 8*sub .. 8*sub+7 sit in one 16-byte slot row: one 8-byte store
-    *reinterpret_cast<uint2 *>(a.q + act_slot_off(a.n, grp, 8 * sub)) = make_uint2(w[0], w[1]);
+#pragma unroll
+    for (int k = 0; k < NV; k += 2)
+        *reinterpret_cast<uint2 *>(a.q + act_slot_off(a.n, grp, 4 * NV * sub + 4 * k)) = make_uint2(w[k], w[k + 1]);
     if (sub == 0) {
         a.xs[grp] = sc;
         a.xsum[grp] = sc * (float) sum;
     }
     if (ex) {
-        uint32_t * d = reinterpret_cast<uint32_t *>(g.act_q + grp * kGroup + 8 * sub);
-        d[0] = w[0];
-        d[1] = w[1];
+        uint32_t * d = reinterpret_cast<uint32_t *>(g.act_q + grp * kGroup + 4 * NV * sub);
+#pragma unroll
+        for (int k = 0; k < NV; k++) d[k] = w[k];
         if (sub == 0) { g.act_s[grp] = sc; g.act_sum[grp] = sum; }
     }
 }
@@ -240,44 +252,40 @@ SB_DEV void quant_team_to(float4 v, int grp, int sub, ActS & a, bool store) {
 // sml/sml-run.c:147-152); teams of 8 lanes then quantize groups, reading
 // x[perm[i]] and the gain from shared memory (both bulk-loaded by the producer
 // before the wait; `statics` completes when they land). Pre-permuted input:
-// quads of 4 lanes, each lane reading its 8 values with two 16-byte loads.
+// pairs of lanes, each lane reading its 16 values with four 16-byte loads.
 SB_DEV void tg_stage(const TGArgs & g, ActS & a, double * red, uint8_t * smem, const StageLayout & L,
                      uint64_t * statics, bool & failed) {
     const int n = g.t.cols, ng = n / kGroup, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int team = tid >> 3, sub = tid & 7, nteam = kConsThreads / 8;
     const bool ex = g.act_q && blockIdx.x == 0;
     if (g.in_permuted) {
-        // every round's load issued before any group is quantized; four lanes
-        // per group, 32 bytes each
-        constexpr int kR = 4;   // rounds held in registers: n <= 4 * nquad * 32
-        const int quad = tid >> 2, qs = tid & 3, nquad = kConsThreads / 4;
-        float4 v[kR][2];
+        // every round's load issued before any group is quantized; two lanes
+        // per group, 64 bytes each
+        constexpr int kLpg = 2, kNv = 8 / kLpg, kR = 2;   // rounds held in registers: n <= 2 * npair * 32
+        const int pair = tid / kLpg, ps = tid % kLpg, npair = kConsThreads / kLpg;
+        float4 v[kR][kNv];
 #pragma unroll
         for (int r = 0; r < kR; r++) {
-            const int grp = r * nquad + quad;
-            if (grp < ng) {
-                const float4 * p = reinterpret_cast<const float4 *>(g.in + grp * kGroup + 8 * qs);
-                v[r][0] = p[0];
-                v[r][1] = p[1];
-            } else {
-                v[r][0] = v[r][1] = make_float4(0.f, 0.f, 0.f, 0.f);
-            }
+            const int grp = r * npair + pair;
+#pragma unroll
+            for (int k = 0; k < kNv; k++)
+                v[r][k] = grp < ng ? reinterpret_cast<const float4 *>(g.in + grp * kGroup + 4 * kNv * ps)[k]
+                                   : make_float4(0.f, 0.f, 0.f, 0.f);
         }
         SB_MARK(g.trace, g.launch_id, 5);   // thread 0's loads are issued
 #pragma unroll
         for (int r = 0; r < kR; r++) {
-            const int grp = r * nquad + quad;
-            if (r * nquad < ng) quant_quad(v[r][0], v[r][1], grp, qs, a, g, ex, grp < ng);
+            const int grp = r * npair + pair;
+            if (r * npair < ng) quant_lanes<kLpg>(v[r], grp, ps, a, g, ex, grp < ng);
         }
-        for (int base = kR * nquad; base < ng; base += nquad) {
-            const int grp = base + quad;
-            float4 w0 = make_float4(0.f, 0.f, 0.f, 0.f), w1 = w0;
-            if (grp < ng) {
-                const float4 * p = reinterpret_cast<const float4 *>(g.in + grp * kGroup + 8 * qs);
-                w0 = p[0];
-                w1 = p[1];
-            }
-            quant_quad(w0, w1, grp, qs, a, g, ex, grp < ng);
+        for (int base = kR * npair; base < ng; base += npair) {
+            const int grp = base + pair;
+            float4 w4[kNv];
+#pragma unroll
+            for (int k = 0; k < kNv; k++)
+                w4[k] = grp < ng ? reinterpret_cast<const float4 *>(g.in + grp * kGroup + 4 * kNv * ps)[k]
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+            quant_lanes<kLpg>(w4, grp, ps, a, g, ex, grp < ng);
         }
         bar_sync(1, kConsThreads);
         return;
