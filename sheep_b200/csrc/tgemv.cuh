@@ -169,7 +169,7 @@ SB_DEV void quant_team(float4 v, int grp, int sub, ActS & a, const TGArgs & g, b
     }
 }
 
-// quant_team with LPG lanes per group (4 or 2), 32/LPG values per lane (v[k]
+// quant_team with LPG lanes per group (4, 2 or 1), 32/LPG values per lane (v[k]
 // holds the group's values (32/LPG)*sub + 4k .. +3): fewer shuffles and
 // divisions per group than 8 lanes of 4. amax and the integer sum are exact
 // whatever the lane split, so the codes, scale and sum are quant_team's (the
@@ -252,40 +252,40 @@ SB_DEV void quant_team_to(float4 v, int grp, int sub, ActS & a, bool store) {
 // sml/sml-run.c:147-152); teams of 8 lanes then quantize groups, reading
 // x[perm[i]] and the gain from shared memory (both bulk-loaded by the producer
 // before the wait; `statics` completes when they land). Pre-permuted input:
-// pairs of lanes, each lane reading its 16 values with four 16-byte loads.
+// one lane per group, reading its 32 values with eight 16-byte loads.
 SB_DEV void tg_stage(const TGArgs & g, ActS & a, double * red, uint8_t * smem, const StageLayout & L,
                      uint64_t * statics, bool & failed) {
     const int n = g.t.cols, ng = n / kGroup, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const int team = tid >> 3, sub = tid & 7, nteam = kConsThreads / 8;
     const bool ex = g.act_q && blockIdx.x == 0;
     if (g.in_permuted) {
-        // every round's load issued before any group is quantized; two lanes
-        // per group, 64 bytes each
-        constexpr int kLpg = 2, kNv = 8 / kLpg, kR = 2;   // rounds held in registers: n <= 2 * npair * 32
-        const int pair = tid / kLpg, ps = tid % kLpg, npair = kConsThreads / kLpg;
+        // every round's load issued before any group is quantized; one lane
+        // per group, 128 bytes each
+        constexpr int kLpg = 1, kNv = 8 / kLpg, kR = 1;   // rounds held in registers: n <= nlg * 32
+        const int lg = tid / kLpg, ls = tid % kLpg, nlg = kConsThreads / kLpg;   // lane group, lane in it
         float4 v[kR][kNv];
 #pragma unroll
         for (int r = 0; r < kR; r++) {
-            const int grp = r * npair + pair;
+            const int grp = r * nlg + lg;
 #pragma unroll
             for (int k = 0; k < kNv; k++)
-                v[r][k] = grp < ng ? reinterpret_cast<const float4 *>(g.in + grp * kGroup + 4 * kNv * ps)[k]
+                v[r][k] = grp < ng ? reinterpret_cast<const float4 *>(g.in + grp * kGroup + 4 * kNv * ls)[k]
                                    : make_float4(0.f, 0.f, 0.f, 0.f);
         }
         SB_MARK(g.trace, g.launch_id, 5);   // thread 0's loads are issued
 #pragma unroll
         for (int r = 0; r < kR; r++) {
-            const int grp = r * npair + pair;
-            if (r * npair < ng) quant_lanes<kLpg>(v[r], grp, ps, a, g, ex, grp < ng);
+            const int grp = r * nlg + lg;
+            if (r * nlg < ng) quant_lanes<kLpg>(v[r], grp, ls, a, g, ex, grp < ng);
         }
-        for (int base = kR * npair; base < ng; base += npair) {
-            const int grp = base + pair;
+        for (int base = kR * nlg; base < ng; base += nlg) {
+            const int grp = base + lg;
             float4 w4[kNv];
 #pragma unroll
             for (int k = 0; k < kNv; k++)
-                w4[k] = grp < ng ? reinterpret_cast<const float4 *>(g.in + grp * kGroup + 4 * kNv * ps)[k]
+                w4[k] = grp < ng ? reinterpret_cast<const float4 *>(g.in + grp * kGroup + 4 * kNv * ls)[k]
                                  : make_float4(0.f, 0.f, 0.f, 0.f);
-            quant_lanes<kLpg>(w4, grp, ps, a, g, ex, grp < ng);
+            quant_lanes<kLpg>(w4, grp, ls, a, g, ex, grp < ng);
         }
         bar_sync(1, kConsThreads);
         return;
