@@ -2,9 +2,13 @@
 // the checker for the CUDA engine. Not linked into the product.
 //
 // Each step cites the reference line it restates. Written as plain loops from
-// the algorithm (codes unpacked to integers, one integer dot per group, one
-// float epilogue per group), not as a copy of the reference's vector code, so
-// agreement between the two means the format was read the same way twice.
+// the algorithm (codes unpacked to integers, one integer dot per group), with
+// the reference's float operations in the reference's order: its vector
+// kernels' accumulator chains and horizontal sums, the fused multiply-adds gcc
+// forms from them under its default contraction (-ffp-contract=fast), the
+// attention's chains, the SiLU's own exponential. The restatement therefore
+// equals the reference build bit for bit (logits included), which the tests
+// check against vectors the reference wrote.
 #include "sml_oracle.h"
 
 #include <fcntl.h>
@@ -255,9 +259,85 @@ int so_dequant_row(so_model * m, const char * name, int row, float * out) {
     return 1;
 }
 
-// Per group: y += step*xs*dot(code, xq) + min*xs*sum(xq)   (sml/sml-kernel.c:2049-2063)
+// One plane's unsigned values of one row (permuted column order).
+static void row_plane(const so_model * m, const rec_t * r, int row, int p, uint8_t * c) {
+    static const int kinds[9][3] = {{0},{0},{2},{2,1},{4},{4,1},{2,4},{4,2,1},{4,4}};
+    const int n = (int) r->cols, kd = kinds[r->nbits][p];
+    const uint8_t * pl = m->base + r->codes_off[p];
+    for (int i = 0; i < n; i++) {
+        const int g = i / G, j = i % G;
+        int v;
+        if (kd == 4) {
+            const uint8_t b = pl[(size_t) row * (n / 2) + (g / 4) * 64 + ((g % 4) >= 2 ? 32 : 0) + j];
+            v = (g & 1) ? (b >> 4) & 15 : b & 15;
+        } else if (kd == 2) {
+            const uint8_t b = pl[(size_t) row * (n / 4) + (g / 4) * 32 + j];
+            v = (b >> (2 * (g % 4))) & 3;
+        } else {
+            const uint8_t b = pl[(size_t) row * (n / 8) + g * 4 + j / 8];
+            v = (b >> (j % 8)) & 1;
+        }
+        c[i] = (uint8_t) v;
+    }
+}
+
+// The reference's float epilogues, each restated in its own order (a group's
+// integer dot is exact whatever the order; the float sums are not):
+//
+// ep_flat -- matvec_flat4_l8 (sml/sml-kernel.c:572-718), which the decode
+//   copy's sml_matvec_rows_il4/il6 (:836-905) and the fused 6-bit kernel
+//   (:919-1005) repeat "in the same order" (:816): eight accumulators,
+//   accumulator L taking groups 8k+L in k order, each group two fused
+//   multiply-adds, acc = fma(d*sq, xs*dot, acc) then fma(md*(mq - bias), xs*sum,
+//   acc) (gcc contracts the intrinsics' add(acc, mul(..)) under its default
+//   -ffp-contract=fast); a 4-group tail in four more (:664-705); the horizontal
+//   sum ((a0+a4)+(a1+a5)) + ((a2+a6)+(a3+a7)), plus the tail's (t0+t1)+(t2+t3)
+//   (:707-716).
+// ep_ladder -- sml_matvec_rows (:298-370): four accumulators (groups 4p+L), the
+//   dot scaled by 2^shift, the same two fused steps; sum (a0+a1)+(a2+a3).
+// ep_bits1 -- sml_matvec_bits1 (:1036-1063): one scalar sum over the groups
+//   whose bit word is not zero, tot = fma(d*sq*xs, dot, tot), no min term,
+//   added to y as y + tot*2^shift.
+static float ep_flat(const int32_t * d, int ng, const float * st, const float * mn, const float * xs,
+                     const int32_t * sums) {
+    const int nblk = ng / 8;
+    float a[8] = {0}, t[4] = {0};
+    for (int g = 0; g < ng; g++) {
+        float * acc = g < nblk * 8 ? &a[g % 8] : &t[g % 4];
+        *acc = fmaf(st[g], xs[g] * (float) d[g], *acc);
+        if (mn) *acc = fmaf(mn[g], xs[g] * (float) sums[g], *acc);
+    }
+    float tot = ((a[0] + a[4]) + (a[1] + a[5])) + ((a[2] + a[6]) + (a[3] + a[7]));
+    if (ng > nblk * 8) tot += (t[0] + t[1]) + (t[2] + t[3]);
+    return tot;
+}
+
+static float ep_ladder(const int32_t * d, int ng, float mul, const float * st, const float * mn, const float * xs,
+                       const int32_t * sums) {
+    float a[4] = {0};
+    for (int g = 0; g < ng; g++) {
+        a[g % 4] = fmaf(st[g], xs[g] * ((float) d[g] * mul), a[g % 4]);
+        if (mn) a[g % 4] = fmaf(mn[g], xs[g] * (float) sums[g], a[g % 4]);
+    }
+    return (a[0] + a[1]) + (a[2] + a[3]);
+}
+
+static float ep_bits1(const int32_t * d, const uint8_t * nz, int ng, const float * st, const float * xs) {
+    float tot = 0.0f;
+    for (int g = 0; g < ng; g++)
+        if (nz[g]) tot = fmaf(st[g] * xs[g], (float) d[g], tot);
+    return tot;
+}
+
+// y[row0..row1) = W x, x gathered through the tensor's column order and
+// quantized per 32 (sml/sml-run.c:711-760), each width through the kernels
+// the reference's decode dispatch picks (issue_rows_act, sml/sml-run.c:612-680):
+// Q2 ladder; Q3 ladder + bit plane x4; Q4 flat; Q5 flat + bit plane x16; Q6 the
+// fused flat form (two passes -- ladder x16 with the min, then flat without --
+// when the groups are not whole 8-group blocks, :929-936); Q7 as Q6 + bit plane
+// x64; Q8 flat over lo + 16 hi. y starts at 0 and each pass adds its sum.
 static void matvec_rec(const so_model * m, const rec_t * r, const float * x, float * y, int row0, int row1) {
-    const int n = (int) r->cols, ng = n / G;
+    const int n = (int) r->cols, ng = n / G, nb = (int) r->nbits;
     const int32_t * perm = (const int32_t *) (m->base + r->perm_off);
     float * xg = (float *) malloc((size_t) n * 4);
     int8_t * q = (int8_t *) malloc((size_t) n);
@@ -265,21 +345,55 @@ static void matvec_rec(const so_model * m, const rec_t * r, const float * x, flo
     int32_t * sums = (int32_t *) malloc((size_t) ng * 4);
     for (int i = 0; i < n; i++) xg[i] = x[perm[i]];          // sml/sml-kernel.c:253-255
     so_quantize_act(xg, n, q, xs, sums);
+    const int np = nb == 2 || nb == 4 ? 1 : nb == 7 ? 3 : 2;
 #pragma omp parallel for schedule(static)
     for (int row = row0; row < row1; row++) {
-        uint8_t * c = (uint8_t *) malloc((size_t) n);
-        row_codes(m, r, row, c);
-        float acc = 0.0f;
+        uint8_t * c = (uint8_t *) malloc((size_t) n * 3);
+        int32_t * d = (int32_t *) malloc((size_t) ng * 3 * 4);
+        float * st = (float *) malloc((size_t) ng * 4), * mn = (float *) malloc((size_t) ng * 4);
+        uint8_t * nz = (uint8_t *) malloc((size_t) ng);
+        for (int p = 0; p < np; p++) row_plane(m, r, row, p, c + (size_t) p * n);
+        for (int p = 0; p < np; p++)
+            for (int g = 0; g < ng; g++) {
+                int32_t s = 0;
+                for (int j = 0; j < G; j++) s += (int32_t) c[(size_t) p * n + g * G + j] * (int32_t) q[g * G + j];
+                d[p * ng + g] = s;
+            }
         for (int g = 0; g < ng; g++) {
-            int32_t d = 0;
-            for (int j = 0; j < G; j++) d += (int32_t) c[g * G + j] * (int32_t) q[g * G + j];
-            float st, mn;
-            group_grid(m, r, row, g, &st, &mn);
-            acc += st * xs[g] * (float) d;
-            if (r->mq_n) acc += mn * xs[g] * (float) sums[g];
+            group_grid(m, r, row, g, &st[g], &mn[g]);
+            nz[g] = 0;
+            if (np > 1) for (int j = 0; j < G; j++) nz[g] |= c[(size_t) (np - 1) * n + g * G + j];
+        }
+        const float * mnp = r->mq_n ? mn : NULL;
+        const int whole = ng % 8 == 0;
+        float acc = 0.0f;
+        int32_t * comb = (int32_t *) malloc((size_t) ng * 4);
+        switch (nb) {
+        case 2: acc = 0.0f + ep_ladder(d, ng, 1.0f, st, mnp, xs, sums); break;
+        case 3: acc = 0.0f + ep_ladder(d, ng, 1.0f, st, mnp, xs, sums);
+                acc = acc + ep_bits1(d + ng, nz, ng, st, xs) * 4.0f; break;
+        case 4: acc = 0.0f + ep_flat(d, ng, st, mnp, xs, sums); break;
+        case 5: acc = 0.0f + ep_flat(d, ng, st, mnp, xs, sums);
+                acc = acc + ep_bits1(d + ng, nz, ng, st, xs) * 16.0f; break;
+        case 6: case 7: {
+            const int32_t * nib = nb == 6 ? d + ng : d, * two = nb == 6 ? d : d + ng;
+            if (whole) {
+                for (int g = 0; g < ng; g++) comb[g] = nib[g] + 16 * two[g];
+                acc = 0.0f + ep_flat(comb, ng, st, mnp, xs, sums);
+            } else {
+                acc = 0.0f + ep_ladder(two, ng, 16.0f, st, mnp, xs, sums);
+                acc = acc + ep_flat(nib, ng, st, NULL, xs, sums);
+            }
+            if (nb == 7) acc = acc + ep_bits1(d + 2 * ng, nz, ng, st, xs) * 64.0f;
+            break;
+        }
+        default:
+            for (int g = 0; g < ng; g++) comb[g] = d[g] + 16 * d[ng + g];
+            acc = 0.0f + ep_flat(comb, ng, st, mnp, xs, sums);
+            break;
         }
         y[row] = acc;
-        free(c);
+        free(comb); free(c); free(d); free(st); free(mn); free(nz);
     }
     free(xg); free(q); free(xs); free(sums);
 }
@@ -414,15 +528,31 @@ static void rms_norm(float * out, const float * x, const float * w, int n, float
     for (int i = 0; i < n; i++) out[i] = x[i] * s * w[i];
 }
 
-// sml/sml-run.c:339-375, halved pairs (i, i + half)
+// sml/sml-run.c:339-375, halved pairs (i, i + half). Which product of each
+// pair gcc fuses into the subtraction / addition (its default
+// -ffp-contract=fast) is set by ROPE_FUSE, pinned against the reference build.
+#ifndef ROPE_FUSE
+#define ROPE_FUSE 1
+#endif
 static void rope(const so_model * m, float * v, int nh, int pos) {
     const float * cs = m->cos_t + (size_t) pos * m->half, * sn = m->sin_t + (size_t) pos * m->half;
     for (int h = 0; h < nh; h++) {
         float * x = v + (size_t) h * m->hd;
         for (int i = 0; i < m->half; i++) {
             const float a = x[i], b = x[i + m->half];
-            x[i] = a * cs[i] - b * sn[i];
-            x[i + m->half] = a * sn[i] + b * cs[i];
+#if ROPE_FUSE == 0
+            x[i] = fmaf(-b, sn[i], a * cs[i]);
+            x[i + m->half] = fmaf(b, cs[i], a * sn[i]);
+#elif ROPE_FUSE == 1
+            x[i] = fmaf(a, cs[i], -(b * sn[i]));
+            x[i + m->half] = fmaf(a, sn[i], b * cs[i]);
+#elif ROPE_FUSE == 2
+            x[i] = fmaf(-b, sn[i], a * cs[i]);
+            x[i + m->half] = fmaf(a, sn[i], b * cs[i]);
+#else
+            x[i] = fmaf(a, cs[i], -(b * sn[i]));
+            x[i + m->half] = fmaf(b, cs[i], a * sn[i]);
+#endif
         }
     }
 }
@@ -432,7 +562,12 @@ static void qk_norm(float * v, const float * w, int nh, int hd, float eps) {
     for (int h = 0; h < nh; h++) rms_norm(v + (size_t) h * hd, v + (size_t) h * hd, w, hd, eps);
 }
 
-// sml/sml-run.c:180-266 (scores, max-subtracted softmax with expf, weighted V)
+// attn_row (sml/sml-run.c:180-266), the AVX2 arm's order: a position's score
+// as eight fused multiply-add chains (chain l over dims l, l+8, ...), reduced
+// ((c0+c4)+(c1+c5)) + ((c2+c6)+(c3+c7)) (sml_hsum256 :111-119), times 1/sqrt(hd);
+// softmax with libm expf, the sum in position order, then times 1/sum
+// (:280-288); the output per dim one fused multiply-add chain over the
+// positions in order (:236-253; hd % 64 == 0, else the same per dim, :256-265).
 static void attn_head(const so_model * m, const uint16_t * kc, const uint16_t * vc, int L, int h, int pos,
                       const float * q, float * out, float * sc) {
     const int hd = m->hd, kvd = (int) m->n_kv * hd, rep = (int) (m->n_head / m->n_kv);
@@ -440,8 +575,9 @@ static void attn_head(const so_model * m, const uint16_t * kc, const uint16_t * 
     const float inv = 1.0f / sqrtf((float) hd);
     for (int t = 0; t <= pos; t++) {
         const uint16_t * k = kc + base + (size_t) t * kvd;
-        float s = 0.0f;
-        for (int i = 0; i < hd; i++) s += q[i] * f16(k[i]);
+        float c[8] = {0};
+        for (int i = 0; i < hd; i++) c[i % 8] = fmaf(q[i], f16(k[i]), c[i % 8]);
+        const float s = ((c[0] + c[4]) + (c[1] + c[5])) + ((c[2] + c[6]) + (c[3] + c[7]));
         sc[t] = s * inv;
     }
     float mx = sc[0];
@@ -453,13 +589,37 @@ static void attn_head(const so_model * m, const uint16_t * kc, const uint16_t * 
     for (int i = 0; i < hd; i++) out[i] = 0.0f;
     for (int t = 0; t <= pos; t++) {
         const uint16_t * v = vc + base + (size_t) t * kvd;
-        for (int i = 0; i < hd; i++) out[i] += sc[t] * f16(v[i]);
+        for (int i = 0; i < hd; i++) out[i] = fmaf(sc[t], f16(v[i]), out[i]);
     }
 }
 
-// sml/sml-run.c:437-455 (portable arm): silu(g) * u with libm expf
+// The AVX2 arm's exp of silu_mul (sml_exp_ps, sml/sml-run.c:392-413): x clamped
+// to [-88, 88], f = x*log2(e), r = f rounded to nearest even, 2^(f-r) by a
+// degree-5 polynomial in Horner form (each step one fused multiply-add under
+// gcc's contraction), times 2^r through the exponent field.
+static float exp_ps1(float x) {
+    x = fminf(fmaxf(x, -88.0f), 88.0f);
+    const float f = x * 1.44269504088896341f;
+    const float r = rintf(f);
+    const float g = f - r;
+    float p = 1.3697664e-3f;
+    p = fmaf(p, g, 8.3013611e-3f);
+    p = fmaf(p, g, 5.5826318e-2f);
+    p = fmaf(p, g, 2.4022652e-1f);
+    p = fmaf(p, g, 6.9314718e-1f);
+    p = fmaf(p, g, 1.0f);
+    uint32_t e = (uint32_t) ((int) r + 127) << 23;
+    float s;
+    memcpy(&s, &e, 4);
+    return p * s;
+}
+
+// silu_mul (sml/sml-run.c:436-446): blocks of 8 through the vector exp,
+// (g / (1 + exp(0 - g))) * u; a tail past the last block of 8 with libm expf.
 static void silu_mul(float * g, const float * u, int n) {
-    for (int i = 0; i < n; i++) g[i] = (g[i] / (1.0f + expf(-g[i]))) * u[i];
+    const int n8 = n / 8 * 8;
+    for (int i = 0; i < n8; i++) g[i] = (g[i] / (1.0f + exp_ps1(0.0f - g[i]))) * u[i];
+    for (int i = n8; i < n; i++) g[i] = (g[i] / (1.0f + expf(-g[i]))) * u[i];
 }
 
 // sml/sml-run.c:3009-3030: top-k on the logits (ties to the lower index), then
@@ -514,7 +674,7 @@ static int moe_ffn(so_model * m, int L, const float * xb, float * out, int * sel
         matvec_rec(m, findf(m, "blk.%d.ffn_up.%d.weight", L, sel[j]), xb, u, 0, F);
         silu_mul(g, u, F);
         matvec_rec(m, findf(m, "blk.%d.ffn_down.%d.weight", L, sel[j]), g, t, 0, E);
-        for (int i = 0; i < E; i++) out[i] += w[j] * t[i];
+        for (int i = 0; i < E; i++) out[i] = fmaf(w[j], t[i], out[i]);   // acc += w*t, contracted
     }
     free(lg); free(g); free(u); free(t);
     return k;
