@@ -21,7 +21,7 @@ sb_engine * sb_open(const char * path, int n_ctx, char * why, int nwhy);
 void        sb_close(sb_engine * e);
 // out[0..12]: n_layer, n_embd, n_head, n_head_kv, head_dim, n_ff, n_vocab,
 // n_ctx, n_expert, n_expert_used, weight bytes per token (low, high 32 bits),
-// 1 if a token runs as one persistent kernel (else a chain of kernels)
+// 0 (reserved)
 void        sb_info(const sb_engine * e, int * out);
 uint64_t    sb_bytes_per_token(const sb_engine * e);
 // sml/sml-gpu.h:17 semantics on a handle: logits in host memory, NULL on failure.

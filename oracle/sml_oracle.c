@@ -528,31 +528,18 @@ static void rms_norm(float * out, const float * x, const float * w, int n, float
     for (int i = 0; i < n; i++) out[i] = x[i] * s * w[i];
 }
 
-// sml/sml-run.c:339-375, halved pairs (i, i + half). Which product of each
-// pair gcc fuses into the subtraction / addition (its default
-// -ffp-contract=fast) is set by ROPE_FUSE, pinned against the reference build.
-#ifndef ROPE_FUSE
-#define ROPE_FUSE 1
-#endif
+// sml/sml-run.c:339-375, halved pairs (i, i + half), as gcc's default
+// contraction builds the two lines: x[i] = fma(a, cos, -(b*sin)),
+// x[i + half] = fma(a, sin, b*cos) (the form the reference build's decode
+// matches bit for bit; the other pairings do not).
 static void rope(const so_model * m, float * v, int nh, int pos) {
     const float * cs = m->cos_t + (size_t) pos * m->half, * sn = m->sin_t + (size_t) pos * m->half;
     for (int h = 0; h < nh; h++) {
         float * x = v + (size_t) h * m->hd;
         for (int i = 0; i < m->half; i++) {
             const float a = x[i], b = x[i + m->half];
-#if ROPE_FUSE == 0
-            x[i] = fmaf(-b, sn[i], a * cs[i]);
-            x[i + m->half] = fmaf(b, cs[i], a * sn[i]);
-#elif ROPE_FUSE == 1
             x[i] = fmaf(a, cs[i], -(b * sn[i]));
             x[i + m->half] = fmaf(a, sn[i], b * cs[i]);
-#elif ROPE_FUSE == 2
-            x[i] = fmaf(-b, sn[i], a * cs[i]);
-            x[i + m->half] = fmaf(a, sn[i], b * cs[i]);
-#else
-            x[i] = fmaf(a, cs[i], -(b * sn[i]));
-            x[i + m->half] = fmaf(b, cs[i], a * sn[i]);
-#endif
         }
     }
 }

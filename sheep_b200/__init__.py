@@ -149,7 +149,6 @@ class Engine:
         lib().sb_info(self.h, info)
         (self.n_layer, self.n_embd, self.n_head, self.n_head_kv, self.head_dim, self.n_ff,
          self.n_vocab, self.n_ctx, self.n_expert, self.n_expert_used) = info[:10]
-        self.persistent = bool(info[12])   # one kernel per token
         self.bytes_per_token = int(lib().sb_bytes_per_token(self.h))
 
     def step(self, tok, pos):

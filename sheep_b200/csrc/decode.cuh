@@ -16,6 +16,7 @@
 // complete after its predecessor has.
 #pragma once
 
+#include "expf_libm.h"
 #include "qgemv.cuh"
 
 namespace sb {
@@ -36,14 +37,30 @@ SB_DEV ActS act_carve(uint8_t * smem, int n) {
     return a;
 }
 
+// The reference's exponential for SiLU (sml_exp_ps, sml/sml-run.c:392-413, the
+// AVX2 build's): x clamped to [-88, 88], f = x*log2(e), r = f rounded to
+// nearest even, 2^(f - r) by a degree-5 polynomial in Horner form (each step
+// one fused multiply-add, as gcc contracts the intrinsics' add(mul(p, g), c)),
+// scaled by 2^r through the exponent field. Restated with the same constants so
+// the hidden vector equals the reference's bit for bit.
+SB_DEV float exp_silu(float x) {
+    x = fminf(fmaxf(x, -88.0f), 88.0f);
+    const float f = __fmul_rn(x, 1.44269504088896341f);
+    const float r = rintf(f);
+    const float g = __fsub_rn(f, r);
+    float p = 1.3697664e-3f;
+    p = __fmaf_rn(p, g, 8.3013611e-3f);
+    p = __fmaf_rn(p, g, 5.5826318e-2f);
+    p = __fmaf_rn(p, g, 2.4022652e-1f);
+    p = __fmaf_rn(p, g, 6.9314718e-1f);
+    p = __fmaf_rn(p, g, 1.0f);
+    return __fmul_rn(p, __int_as_float(((int) r + 127) << 23));
+}
+
 SB_DEV float silu_mul(float g, float u) {
-    // sml/sml-run.c:450-455: (g / (1 + expf(-g))) * u. The exponential is taken
-    // in double and rounded once, the correctly rounded float in all but
-    // vanishing cases (the host's libm expf differs from it on 0.06 % of
-    // arguments; the single-precision device expf is allowed 2 ulp), so the
-    // hidden vector follows the CPU's to the last bit as far as it can.
-    const float e = (float) exp(-(double) g);
-    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, e)), u);
+    // silu_mul (sml/sml-run.c:436-446), the vector arm every hidden width that
+    // is a multiple of 8 takes: (g / (1 + exp(0 - g))) * u, IEEE division
+    return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, exp_silu(__fsub_rn(0.0f, g)))), u);
 }
 
 // ---------------------------------------------------------------- embedding
@@ -157,6 +174,7 @@ struct AttnArgs {
     unsigned * cnt;          // [n_head]
     int max_chunks;
     float * out;             // [qd] attention output
+    const ExpfEntry * xtab;  // expf_libm.h table (k_attn_seq), or NULL: exp rounded from double
     int * err;
     unsigned long long * trace;
     int launch_id;
@@ -184,13 +202,196 @@ SB_DEV void norm_rope(float * v, const float * w, float eps, int hd, const float
     const int half = hd / 2;
     for (int i = threadIdx.x; i < half; i += blockDim.x) {
         const float a = v[i], b = v[i + half];
-        // both products rounded, then the sum: no fused multiply-add, as the CPU
-        // restatement computes it (sml/sml-run.c:363-366, built without contraction),
-        // so keys are bit-equal before their fp16 rounding
-        v[i] = __fsub_rn(__fmul_rn(a, cs[i]), __fmul_rn(b, sn[i]));
-        v[i + half] = __fadd_rn(__fmul_rn(a, sn[i]), __fmul_rn(b, cs[i]));
+        // as the reference's build computes it (sml/sml-run.c:363-366 under gcc's
+        // contraction): v[i] = fma(a, cos, -(b sin)), v[i + half] = fma(a, sin, b cos)
+        v[i] = __fmaf_rn(a, cs[i], -__fmul_rn(b, sn[i]));
+        v[i + half] = __fmaf_rn(a, sn[i], __fmul_rn(b, cs[i]));
     }
     __syncthreads();
+}
+
+// The host libm's expf on the device (expf_libm.h): exp in double rounded
+// once, corrected from the table where the host's expf differs.
+SB_DEV float expf_libm(float x, const ExpfEntry * tab) {
+    float y = __double2float_rn(exp((double) x));
+    if (tab && x < 0.0f) {
+        const uint32_t k = __float_as_uint(x), mask = (1u << kExpfBits) - 1u;
+        uint32_t h = expf_slot(k);
+        for (int i = 0; i < 64; i++) {   // the table is at most half full: a run ends well before
+            const ExpfEntry e = tab[h];
+            if (e.x == k) { y = __uint_as_float(e.y); break; }
+            if (e.x == 0xffffffffu) break;
+            h = (h + 1) & mask;
+        }
+    }
+    return y;
+}
+
+// RoPE by halved pairs as the reference's build computes it
+// (sml/sml-run.c:363-366 under gcc's contraction): v[i] = fma(a, cos, -(b sin)),
+// v[i + half] = fma(a, sin, b cos), a = v[i], b = v[i + half].
+SB_DEV void rope_ref(float * v, int hd, const float * cs, const float * sn) {
+    const int half = hd / 2;
+    for (int i = threadIdx.x; i < half; i += blockDim.x) {
+        const float a = v[i], b = v[i + half];
+        v[i] = __fmaf_rn(a, cs[i], -__fmul_rn(b, sn[i]));
+        v[i + half] = __fmaf_rn(a, sn[i], __fmul_rn(b, cs[i]));
+    }
+}
+
+// Per-head RMS norm of Q or K (sml/sml-run.c:329-333): the sum of squares in
+// double, s = 1/sqrtf((float)(ss/hd) + eps), v = (v*s)*w.
+SB_DEV void head_norm(float * v, const float * w, float eps, int hd, double * red) {
+    const int lane = threadIdx.x & 31, wp = threadIdx.x >> 5;
+    double s = 0.0;
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) s += (double) v[i] * (double) v[i];
+    s = warp_sum_d(s);
+    if (lane == 0) red[wp] = s;
+    __syncthreads();
+    double ss = 0.0;
+    for (int k = 0; k < (int) (blockDim.x >> 5); k++) ss += red[k];
+    const float f = __fdiv_rn(1.0f, sqrtf(__fadd_rn((float) (ss / hd), eps)));
+    __syncthreads();
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) v[i] = __fmul_rn(__fmul_rn(v[i], f), w[i]);
+    __syncthreads();
+}
+
+constexpr int kSeqThreads = 256;
+constexpr int kSeqChunk = 64;     // positions of V per shared-memory stage
+
+// Shared memory of k_attn_seq: q, k, v, cos, sin, the scores of n_ctx
+// positions, the new key and value as fp16, two V stages.
+__host__ __device__ inline size_t attn_seq_smem_bytes(int hd, int n_ctx) {
+    return (size_t) (4 * hd + ((n_ctx + 3) & ~3)) * 4 + (size_t) 2 * hd * 2 + (size_t) 2 * kSeqChunk * hd * 2;
+}
+
+// Decode attention of one query head per CTA, in the reference's float order
+// (attn_row, sml/sml-run.c:180-266, AVX2 arm):
+//   score(t) = (((c0+c4)+(c1+c5)) + ((c2+c6)+(c3+c7))) * scale, chain c_l the
+//              fused multiply-adds over dims l, l+8, ... (one thread per position);
+//   softmax    max, e_t = expf(s_t - max) (the host libm's, expf_libm), their sum
+//              in position order (one thread), p_t = e_t * (1/sum);
+//   out[d]     = fma chain over positions 0..pos in order (one thread per dim),
+//              V streamed through two shared-memory stages of 64 positions.
+// Before that: Q/K norm if any, RoPE (rope_ref), the new key/value rounded to
+// fp16 and written to the cache by the group's first head; the new position's
+// key and value are taken from shared memory, never re-read from the cache.
+static __global__ void __launch_bounds__(kSeqThreads) k_attn_seq(const __grid_constant__ AttnArgs g) {
+    extern __shared__ __align__(16) float sm[];
+    __shared__ double red[kSeqThreads / 32];
+    __shared__ float wred[kSeqThreads / 32];
+    __shared__ float s_inv;
+    pdl_launch_dependents();
+    SB_MARK(g.trace, g.launch_id, 0);
+    const int h = blockIdx.x, hd = g.hd, tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
+    const int pos = g.pos ? *g.pos : g.pos_imm;
+    if (!SB_CHECK(g.err, pos >= 0 && pos < g.n_ctx && (hd & 7) == 0 && hd <= 256, 211)) { pdl_wait(); return; }
+    const int rep = g.n_head / g.n_kv, kvh = h / rep, np = pos + 1;
+    float * q = sm, * kn = sm + hd, * vn = sm + 2 * hd, * cs = sm + 3 * hd, * sn = cs + hd / 2;
+    float * sc = sm + 4 * hd;
+    uint16_t * kh = reinterpret_cast<uint16_t *>(sc + ((g.n_ctx + 3) & ~3)), * vh = kh + hd;
+    uint16_t * vs = vh + hd;   // [2][kSeqChunk][hd]
+    for (int i = tid; i < hd / 2; i += blockDim.x) {
+        cs[i] = g.rcos[(size_t) pos * (hd / 2) + i];
+        sn[i] = g.rsin[(size_t) pos * (hd / 2) + i];
+    }
+    pdl_wait();
+    SB_MARK(g.trace, g.launch_id, 1);
+    for (int i = tid; i < hd; i += blockDim.x) {
+        q[i] = g.qkv[h * hd + i];
+        kn[i] = g.qkv[g.qd + kvh * hd + i];
+        vn[i] = g.qkv[g.qd + g.kvd + kvh * hd + i];
+    }
+    __syncthreads();
+    if (g.qn) head_norm(q, g.qn, g.eps, hd, red);
+    if (g.kn) head_norm(kn, g.kn, g.eps, hd, red);
+    rope_ref(q, hd, cs, sn);
+    rope_ref(kn, hd, cs, sn);
+    __syncthreads();
+    const size_t row0 = (size_t) kvh * hd;
+    for (int i = tid; i < hd; i += blockDim.x) {
+        kh[i] = f2h(kn[i]);
+        vh[i] = f2h(vn[i]);
+        if (h % rep == 0) { g.kc[(size_t) pos * g.kvd + row0 + i] = kh[i]; g.vc[(size_t) pos * g.kvd + row0 + i] = vh[i]; }
+    }
+    __syncthreads();
+    SB_MARK(g.trace, g.launch_id, 2);
+    // scores, one position per thread
+    float m = -INFINITY;
+    for (int t = tid; t < np; t += blockDim.x) {
+        float c[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        const uint16_t * kr = t == pos ? kh : g.kc + (size_t) t * g.kvd + row0;
+        for (int i0 = 0; i0 < hd; i0 += 8) {
+            const uint4 w = *reinterpret_cast<const uint4 *>(kr + i0);
+            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+            for (int l = 0; l < 4; l++) {
+                c[2 * l] = __fmaf_rn(q[i0 + 2 * l], h2f((uint16_t) (ww[l] & 0xffffu)), c[2 * l]);
+                c[2 * l + 1] = __fmaf_rn(q[i0 + 2 * l + 1], h2f((uint16_t) (ww[l] >> 16)), c[2 * l + 1]);
+            }
+        }
+        const float s = __fadd_rn(__fadd_rn(__fadd_rn(c[0], c[4]), __fadd_rn(c[1], c[5])),
+                                  __fadd_rn(__fadd_rn(c[2], c[6]), __fadd_rn(c[3], c[7])));
+        sc[t] = __fmul_rn(s, g.scale);
+        m = fmaxf(m, sc[t]);
+    }
+    m = warp_max(m);
+    if (lane == 0) wred[wp] = m;
+    __syncthreads();
+    m = wred[0];
+    for (int k = 1; k < (int) (blockDim.x >> 5); k++) m = fmaxf(m, wred[k]);
+    for (int t = tid; t < np; t += blockDim.x) sc[t] = expf_libm(__fsub_rn(sc[t], m), g.xtab);
+    // the first V stage's loads go out before the sequential sum
+    const int per = hd / 8, nck = (np + kSeqChunk - 1) / kSeqChunk;
+    constexpr int kPer = kSeqChunk * 256 / 8 / kSeqThreads;   // 16-byte pieces per thread at hd 256
+    const int nper = kSeqChunk * per / kSeqThreads;
+    auto load_chunk = [&](int c, uint4 (&r)[kPer]) {
+#pragma unroll
+        for (int k = 0; k < kPer; k++) {
+            if (k >= nper) break;
+            const int idx = tid + k * kSeqThreads, t = c * kSeqChunk + idx / per;
+            r[k] = make_uint4(0u, 0u, 0u, 0u);
+            if (idx < kSeqChunk * per && t < pos) r[k] = *reinterpret_cast<const uint4 *>(g.vc + (size_t) t * g.kvd + row0 + (idx % per) * 8);
+        }
+    };
+    auto store_chunk = [&](int c, const uint4 (&r)[kPer]) {
+        uint16_t * dst = vs + (size_t) (c & 1) * kSeqChunk * hd;
+#pragma unroll
+        for (int k = 0; k < kPer; k++) {
+            if (k >= nper) break;
+            const int idx = tid + k * kSeqThreads, t = c * kSeqChunk + idx / per;
+            if (idx < kSeqChunk * per && t <= pos)
+                *reinterpret_cast<uint4 *>(dst + (size_t) (idx / per) * hd + (idx % per) * 8) =
+                    t == pos ? *reinterpret_cast<const uint4 *>(vh + (idx % per) * 8) : r[k];
+        }
+    };
+    uint4 rv[kPer];
+    load_chunk(0, rv);
+    __syncthreads();
+    if (tid == 0) {
+        float sum = 0.0f;
+        for (int t = 0; t < np; t++) sum = __fadd_rn(sum, sc[t]);
+        s_inv = __fdiv_rn(1.0f, sum);
+    }
+    store_chunk(0, rv);
+    __syncthreads();
+    SB_MARK(g.trace, g.launch_id, 3);
+    const float inv = s_inv;
+    for (int t = tid; t < np; t += blockDim.x) sc[t] = __fmul_rn(sc[t], inv);
+    __syncthreads();
+    float o = 0.0f;
+    for (int c = 0; c < nck; c++) {
+        if (c + 1 < nck) load_chunk(c + 1, rv);
+        if (tid < hd) {
+            const uint16_t * src = vs + (size_t) (c & 1) * kSeqChunk * hd + tid;
+            const int t0 = c * kSeqChunk, nt = min(kSeqChunk, np - t0);
+            for (int t = 0; t < nt; t++) o = __fmaf_rn(sc[t0 + t], h2f(src[(size_t) t * hd]), o);
+        }
+        if (c + 1 < nck) store_chunk(c + 1, rv);
+        __syncthreads();
+    }
+    if (tid < hd) g.out[h * hd + tid] = o;
+    SB_MARK(g.trace, g.launch_id, 4);
 }
 
 // Shared memory of k_attn for head width hd and `chunk` positions.

@@ -6,7 +6,7 @@
 // captured graph per token whose kernels chain by programmatic dependent
 // launch, and the greedy choice made on the device so a generation loop is
 // graph replays with no host round trip.
-#include "mega.cuh"
+#include "decode.cuh"
 #include "moe_host.h"
 #include "tgemv.cuh"
 #include "sheep_b200.h"
@@ -62,21 +62,11 @@ struct sb_engine {
     float * am_val = nullptr;
     int * am_idx = nullptr;
     unsigned * am_cnt = nullptr;
-    float * apart = nullptr;
-    unsigned * acnt = nullptr;
+    const ExpfEntry * xtab = nullptr;  // the host libm's expf corrections (expf_libm.h)
     MoeScratch ms;                    // routing scratch shared by every MoE layer (one token)
-    // one persistent kernel per token (mega.cuh) when the model allows it
-    bool mega = false;
-    MegaArgs ma{};
-    MegaLayer * d_mlayers = nullptr;
-    unsigned * bar = nullptr;         // grid barrier arrivals
-    unsigned * seq = nullptr;         // tokens run (the persistent kernel's tag base)
-    tagged_t * tx = nullptr, * tqkv = nullptr, * tpart = nullptr, * thp = nullptr;   // its versioned buffers
-    size_t mega_smem = 0;
     int * err = nullptr;              // bounded waits that gave up
     unsigned long long * trace = nullptr;   // trace build: [launch][cta][8] timestamps
     int n_launch_trace = 0;
-    int attn_chunk = 64, max_chunks = 0;
     int nsm = 148;
     cudaStream_t st = nullptr;
     cudaGraphExec_t g_tok = nullptr;
@@ -195,36 +185,8 @@ static void launch_tg(sb_engine * e, int mode, const TGArgs & g0) {
     SB_DISPATCH_QT(g.t.nbits, g.t.six, launch_tg_nb, e, mode, g, grid, tg_smem(g));
 }
 
-template <int NB, int SIX>
-static void launch_mega_w(sb_engine * e, cudaError_t * r) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(e->nsm);
-    cfg.blockDim = dim3(kTgThreads);
-    cfg.dynamicSmemBytes = e->mega_smem;
-    cfg.stream = e->st;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeCooperative;
-    at[0].val.cooperative = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    MegaArgs a = e->ma;
-    a.trace = e->trace;
-    *r = cudaLaunchKernelEx(&cfg, k_token<NB, SIX>, a);
-}
-
 // One token: embed, every layer, head and argmax. Enqueued on e->st (captured).
 static void enqueue_token(sb_engine * e) {
-    if (e->mega) {
-        snprintf(e->cur, sizeof e->cur, "token");
-        cudaError_t r = cudaErrorInvalidValue;
-        SB_DISPATCH_QT(e->emb.nbits, e->emb.six, launch_mega_w, e, &r);
-        if (r != cudaSuccess) {
-            snprintf(g_err, sizeof g_err, "k_token launch: %s", cudaGetErrorString(r));
-            e->failed = true;
-        }
-        after_launch(e, r);
-        return;
-    }
     snprintf(e->cur, sizeof e->cur, "embed");
     SB_DISPATCH_QT(e->emb.nbits, e->emb.six, launch_embed, e, e->emb);
     for (int l = 0; l < e->n_layer; l++) {
@@ -243,11 +205,11 @@ static void enqueue_token(sb_engine * e) {
         a.rcos = e->rcos; a.rsin = e->rsin;
         a.kc = e->kc + (size_t) l * e->n_ctx * e->kvd;
         a.vc = e->vc + (size_t) l * e->n_ctx * e->kvd;
-        a.n_ctx = e->n_ctx; a.pos = e->pos; a.chunk = e->attn_chunk; a.scale = e->scale;
-        a.part = e->apart; a.cnt = e->acnt; a.max_chunks = e->max_chunks; a.out = e->att; a.err = e->err;
+        a.n_ctx = e->n_ctx; a.pos = e->pos; a.scale = e->scale;
+        a.out = e->att; a.err = e->err; a.xtab = e->xtab;
         a.trace = e->trace; a.launch_id = e->launches;
         snprintf(e->cur, sizeof e->cur, "L%d.attn", l);
-        launch(e, true, k_attn, dim3(e->nh, e->max_chunks), dim3(kAttnThreads), attn_smem_bytes(e->hd, e->attn_chunk), a);
+        launch(e, true, k_attn_seq, dim3(e->nh), dim3(kSeqThreads), attn_seq_smem_bytes(e->hd, e->n_ctx), a);
         snprintf(e->cur, sizeof e->cur, "L%d.o", l);
         {
             TGArgs g = tg_args(e, y.o, e->att, nullptr, e->x);
@@ -409,18 +371,12 @@ static bool build(sb_engine * e, char * why, int nwhy) {
     e->am_val = (float *) carve(e, (size_t) 4 * e->nsm * 4);
     e->am_idx = (int *) carve(e, (size_t) 4 * e->nsm * 4);
     e->am_cnt = (unsigned *) carve(e, 4);
-    e->attn_chunk = e->hd <= 128 ? 64 : 32;   // the chunk's keys and values fit in 48 KB
-    e->max_chunks = (e->n_ctx + e->attn_chunk - 1) / e->attn_chunk;
-    e->apart = (float *) carve(e, (size_t) e->nh * e->max_chunks * (e->hd + 2) * 4);
-    e->acnt = (unsigned *) carve(e, (size_t) e->nh * 4);
+    {
+        const std::vector<ExpfEntry> & xt = expf_libm_table();
+        if (xt.empty()) { snprintf(why, nwhy, "this libm's expf differs from the rounded exponential too often"); return false; }
+        e->xtab = (const ExpfEntry *) e->ar.upload(xt.data(), xt.size() * sizeof(ExpfEntry));
+    }
     e->err = (int *) carve(e, 4);
-    e->bar = (unsigned *) carve(e, 4);
-    e->seq = (unsigned *) carve(e, 4);
-    e->d_mlayers = (MegaLayer *) carve(e, (size_t) e->n_layer * sizeof(MegaLayer));
-    e->tx = (tagged_t *) carve(e, (size_t) e->E * 8);
-    e->tqkv = (tagged_t *) carve(e, (size_t) (e->qd + 2 * e->kvd) * 8);
-    e->tpart = (tagged_t *) carve(e, (size_t) e->nh * e->max_chunks * (e->hd + 2) * 8);
-    e->thp = (tagged_t *) carve(e, (size_t) (e->F > 0 ? e->F : 1) * 8);
     if (moe0) moe_carve(e->ar, *moe0, 1, e->ms);
 #ifdef SB_TRACE
     e->n_launch_trace = 8 * e->n_layer + 8;
@@ -501,94 +457,6 @@ extern "C" int sb_trace(const sb_engine * e, unsigned long long * out, int cap) 
     return e->n_launch_trace;
 }
 
-// ------------------------------------------------------------------ persistent token kernel
-
-template <int NB, int SIX>
-static void mega_setup_w(sb_engine * e, bool * ok) {
-    *ok = false;
-    cudaFuncAttributes fa;
-    if (cudaFuncGetAttributes(&fa, k_token<NB, SIX>) != cudaSuccess) return;
-    int dev = 0, optin = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    const size_t maxdyn = (size_t) optin - fa.sharedSizeBytes;
-    MegaArgs & a = e->ma;
-    auto r128 = [](size_t v) { return (v + 127) / 128 * 128; };
-    const int nmax = e->E > e->qd ? e->E : e->qd;
-    const int amax = e->F > nmax ? e->F : nmax;
-    // [x kept (E) | act + input + combine weights, or attention | statics | ring]
-    a.work_off = (uint32_t) r128((size_t) e->E * 4);
-    a.xin_off = (uint32_t) (a.work_off + r128(act_smem_bytes(amax)));
-    size_t work_end = a.xin_off + (size_t) (nmax + 2 * e->nh * e->max_chunks + e->nh) * 4;
-    const size_t attn_end = a.work_off + attn_smem_bytes(e->hd, e->attn_chunk);
-    if (attn_end > work_end) work_end = attn_end;
-    a.stat_off = (uint32_t) r128(work_end);
-    a.ring_off = (uint32_t) r128(a.stat_off + (size_t) 2 * nmax * 4);
-    uint32_t sb = e->head.tb;
-    for (const LayerD & y : e->L)
-        for (const TT * t : {&y.qkv, &y.o, &y.gateup, &y.down}) sb = t->tb > sb ? t->tb : sb;
-    a.stage_bytes = sb;
-    // the byte ring: the rest of shared memory, at least four of the largest tiles
-    if (a.ring_off + 4 * (size_t) sb > maxdyn) return;
-    a.ring_bytes = (uint32_t) ((maxdyn - a.ring_off) / 16 * 16);
-    e->mega_smem = a.ring_off + a.ring_bytes;
-    if (cudaFuncSetAttribute(k_token<NB, SIX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) e->mega_smem) !=
-        cudaSuccess)
-        return;
-    int per_sm = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_token<NB, SIX>, kTgThreads, e->mega_smem) !=
-            cudaSuccess || per_sm < 1)
-        return;
-    *ok = true;
-}
-
-// SB_MEGA=1 runs a token as the persistent kernel (mega.cuh) when every
-// projection shares one width and field layout (the kernel is instantiated per
-// width), there is no MoE layer, and its shared memory fits. It computes the
-// same logits as the kernel chain; on cfg0 it is not yet faster (its grid
-// barriers cost more than the chain's programmatic launches), so the chain is
-// the default.
-static bool mega_setup(sb_engine * e) {
-    const char * env = getenv("SB_MEGA");
-    if (!env || atoi(env) != 1) return false;
-    const int nb = e->emb.nbits, six = e->emb.six;
-    if (e->head.nbits != nb || e->head.six != six) return false;
-    if (e->E > 8192 || e->nh > kConsThreads) return false;   // the staging loops' bounds
-    for (const LayerD & y : e->L) {
-        if (y.moe) return false;
-        for (const TT * t : {&y.qkv, &y.o, &y.gateup, &y.down})
-            if (t->nbits != nb || t->six != six) return false;
-    }
-    std::vector<MegaLayer> ml(e->n_layer);
-    for (int l = 0; l < e->n_layer; l++) {
-        const LayerD & y = e->L[l];
-        MegaLayer & m = ml[l];
-        m.qkv = y.qkv; m.o = y.o; m.gu = y.gateup; m.dn = y.down;
-        m.an = y.an; m.fn = y.fn; m.qkv_b = y.qkv_b; m.qn = y.qn; m.kn = y.kn;
-        m.dn_iperm = y.down_iperm;
-        m.kc = e->kc + (size_t) l * e->n_ctx * e->kvd;
-        m.vc = e->vc + (size_t) l * e->n_ctx * e->kvd;
-    }
-    if (cudaMemcpy(e->d_mlayers, ml.data(), ml.size() * sizeof(MegaLayer), cudaMemcpyHostToDevice) != cudaSuccess)
-        return false;
-    MegaArgs & a = e->ma;
-    memset(&a, 0, sizeof a);
-    a.L = e->d_mlayers; a.n_layer = e->n_layer;
-    a.emb = e->emb; a.head = e->head; a.out_norm = e->out_norm;
-    a.x = e->tx; a.qkv = e->tqkv; a.part = e->tpart; a.hp = e->thp; a.logits = e->logits;
-    a.E = e->E; a.nh = e->nh; a.nkv = e->nkv; a.hd = e->hd; a.qd = e->qd; a.kvd = e->kvd; a.F = e->F; a.V = e->V;
-    a.n_ctx = e->n_ctx; a.eps = e->eps; a.scale = e->scale;
-    a.rcos = e->rcos; a.rsin = e->rsin;
-    a.attn_chunk = e->attn_chunk; a.max_chunks = e->max_chunks;
-    a.tok = e->tok; a.pos = e->pos; a.tlog = e->tlog;
-    a.am_val = e->am_val; a.am_idx = e->am_idx; a.am_cnt = e->am_cnt;
-    a.bar = e->bar; a.seq = e->seq; a.err = e->err;
-
-    bool ok = false;
-    SB_DISPATCH_QT(nb, six, mega_setup_w, e, &ok);
-    return ok;
-}
-
 sb_engine * sb_open(const char * path, int n_ctx, char * why, int nwhy) {
     g_err[0] = 0;
     sb_engine * e = new sb_engine();
@@ -621,6 +489,17 @@ sb_engine * sb_open(const char * path, int n_ctx, char * why, int nwhy) {
     int dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&e->nsm, cudaDevAttrMultiProcessorCount, dev);
+    {
+        // decode attention keeps a score per position in shared memory
+        int optin = 0;
+        cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+        const size_t as = attn_seq_smem_bytes(e->hd, e->n_ctx);
+        if (as + 1024 > (size_t) optin ||
+            cudaFuncSetAttribute(k_attn_seq, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) as) != cudaSuccess) {
+            snprintf(why, nwhy, "n_ctx %d: attention scores do not fit in shared memory", e->n_ctx);
+            close_all(e); delete e; return nullptr;
+        }
+    }
     // pass 1 sizes the arena, pass 2 fills it
     if (!build(e, why, nwhy)) { close_all(e); delete e; return nullptr; }
     if (!e->ar.allocate()) {
@@ -635,7 +514,6 @@ sb_engine * sb_open(const char * path, int n_ctx, char * why, int nwhy) {
         snprintf(why, nwhy, "%s", g_err);
         close_all(e); delete e; return nullptr;
     }
-    e->mega = mega_setup(e);
     // capture one token (SB_SYNC=1: no graph, every kernel synchronized and checked)
     const char * sm = getenv("SB_SYNC");
     e->sync_mode = sm && atoi(sm) != 0;
@@ -672,7 +550,7 @@ void sb_info(const sb_engine * e, int * out) {
     for (const LayerD & y : e->L) if (y.moe) { ne = y.ml.ne; k = y.ml.k; }
     out[6] = e->V; out[7] = e->n_ctx; out[8] = ne; out[9] = k;
     out[10] = (int) (e->bytes_tok & 0xffffffffu); out[11] = (int) (e->bytes_tok >> 32);
-    out[12] = e->mega ? 1 : 0;
+    out[12] = 0;
 }
 
 uint64_t sb_bytes_per_token(const sb_engine * e) { return e->bytes_tok; }

@@ -16,11 +16,14 @@
 // 8 stages (wide tiles) has each waiter first see the stage's previous lap
 // consumed (ring_wait).
 //
-// Arithmetic per group (sml/sml-kernel.c:2027-2066 and the plane kinds of
-// :1934-2018): y += d*sq*xs*dot(code, xq) + md*(mq-bias)*xs*sum(xq), the dot
-// exact in integers (dp4a), the float epilogue summed per unit then per row.
-// Every row is finished by exactly one warp, in a fixed order of additions, so
-// results do not depend on timing.
+// Arithmetic: the reference's, in the reference's float order (tile_exact
+// below). Each group's dot is exact in integers (dp4a) whatever lanes compute
+// it; the float epilogue then runs as the reference's vector kernels run it --
+// eight accumulator chains per row (chain L takes groups 8k+L in k order, two
+// fused multiply-adds per group) and their fixed horizontal sum, or the
+// ladder's four chains, or the bit plane's single chain -- so a row's result
+// equals the reference build's bit for bit (sml/sml-kernel.c:298-370,
+// :572-718, :836-1005, :1036-1063).
 #pragma once
 
 #include "decode.cuh"
@@ -62,14 +65,26 @@ struct TGArgs {
     uint32_t next_tb;
 };
 
-// Shared memory: [act | perm | norm gain | input x | ring]. perm and the gain
-// are static, so the producer bulk-loads them before the dependency wait; the
-// input is read once, coalesced, after it (when it fits; wide inputs are
-// gathered from L2 instead).
+// Shared memory: [act | perm | norm gain | input x | group dots | ring]. perm
+// and the gain are static, so the producer bulk-loads them before the
+// dependency wait; the input is read once, coalesced, after it (when it fits;
+// wide inputs are gathered from L2 instead). The group dots are each consumer
+// warp's scratch for the integer dots of its current tile (tile_exact).
 struct StageLayout {
-    uint32_t perm_off, w_off, x_off, ring_off;
+    uint32_t perm_off, w_off, x_off, d_off, ring_off;
 };
-__host__ __device__ inline StageLayout stage_layout(int n, int has_perm, int has_norm, int has_x) {
+
+// Integer dot arrays a width's epilogue needs per group: the main code, the
+// bit plane (Q3, Q5, Q7: its own chain), the 2-bit plane of Q6/Q7 kept apart
+// for rows whose groups are not whole 8-group blocks.
+__host__ __device__ constexpr int dot_arrays(int nb) { return nb == 3 || nb == 5 || nb == 6 ? 2 : nb == 7 ? 3 : 1; }
+
+// Bytes of every consumer warp's dot scratch for tiles of t.
+__host__ __device__ inline uint32_t tg_dot_bytes(const TT & t) {
+    return (uint32_t) kConsWarps * dot_arrays(t.nbits) * t.TR * (t.cols / kGroup) * 4u;
+}
+
+__host__ __device__ inline StageLayout stage_layout(int n, int has_perm, int has_norm, int has_x, uint32_t dbytes) {
     StageLayout L;
     uint32_t off = (uint32_t) ((act_smem_bytes(n) + 127) / 128 * 128);
     L.perm_off = off;
@@ -78,11 +93,13 @@ __host__ __device__ inline StageLayout stage_layout(int n, int has_perm, int has
     if (has_norm) off += (uint32_t) n * 4;
     L.x_off = off;
     if (has_perm && has_x) off += (uint32_t) n * 4;
+    L.d_off = (off + 15) / 16 * 16;
+    off = L.d_off + dbytes;
     L.ring_off = (off + 127) / 128 * 128;
     return L;
 }
-__host__ __device__ inline size_t tg_ring_off(int n, int in_permuted, int has_norm, int x_smem) {
-    return stage_layout(n, !in_permuted, has_norm, x_smem).ring_off;
+__host__ __device__ inline size_t tg_ring_off(const TT & t, int in_permuted, int has_norm, int x_smem) {
+    return stage_layout(t.cols, !in_permuted, has_norm, x_smem, tg_dot_bytes(t)).ring_off;
 }
 
 // Ring stages for tiles of tb bytes behind ring_off bytes of staging: the
@@ -106,17 +123,17 @@ __host__ inline bool tg_plan(TGArgs & g) {
     const int hn = g.norm_w != nullptr;
     if (g.in_permuted) {
         g.x_smem = 0;
-        g.nstage = ring_stages(tg_ring_off(g.t.cols, 1, hn, 0), g.t.tb);
+        g.nstage = ring_stages(tg_ring_off(g.t, 1, hn, 0), g.t.tb);
         return g.nstage > 0;
     }
-    const int ns = ring_stages(tg_ring_off(g.t.cols, 0, hn, 1), g.t.tb);
+    const int ns = ring_stages(tg_ring_off(g.t, 0, hn, 1), g.t.tb);
     if (ns >= kConsWarps) { g.x_smem = 1; g.nstage = ns; return true; }
     g.x_smem = 0;
-    g.nstage = ring_stages(tg_ring_off(g.t.cols, 0, hn, 0), g.t.tb);
+    g.nstage = ring_stages(tg_ring_off(g.t, 0, hn, 0), g.t.tb);
     return g.nstage > 0;
 }
 __host__ inline size_t tg_smem(const TGArgs & g) {
-    return tg_ring_off(g.t.cols, g.in_permuted, g.norm_w != nullptr, g.x_smem) + (size_t) g.nstage * g.t.tb;
+    return tg_ring_off(g.t, g.in_permuted, g.norm_w != nullptr, g.x_smem) + (size_t) g.nstage * g.t.tb;
 }
 
 // Wait for tile k of the ring (stage k % ns, lap k / ns) as consumer warp
@@ -440,6 +457,234 @@ SB_DEV float tile_row(const uint8_t * tile, const TileGeom & tg, const ActS & a,
     return acc;
 }
 
+// ---------------------------------------------------------------- exact epilogue
+//
+// tile_exact: the rows of one tile, each as the reference computes it.
+//
+// Phase A: the warp's lanes take the tile's units as tile_row does (lane l: row
+// l % TR, units l / TR + k * (32 / TR)) and compute each unit's 4 group dots
+// per dot array, exact in integers. The two halves of a group (units 2p and
+// 2p+1) sit in lanes l and l ^ TR and are added by one shuffle; the even lane
+// stores the 4 full dots into the warp's scratch D[array][row][group].
+//
+// Phase B: eight lanes per row (up to four rows per pass) run the reference's
+// float epilogue over those dots:
+//   flat   (matvec_flat4_l8 / il4 / il6 / flat6, sml/sml-kernel.c:572-1005):
+//          lane L: acc = fma(d*sq, xs*dot, acc); acc = fma(md*(mq-bias), xs*sum,
+//          acc) for groups 8k+L in k order; a 4-group tail in lanes 0-3;
+//          then ((a0+a4)+(a1+a5)) + ((a2+a6)+(a3+a7)) (+ (t0+t1)+(t2+t3));
+//   ladder (sml_matvec_rows :298-370): lanes 0-3, groups 4p+L, the dot times
+//          2^shift, sum (a0+a1)+(a2+a3);
+//   bits1  (sml_matvec_bits1 :1036-1063): lane 0, every group whose bit word is
+//          not zero, tot = fma(d*sq*xs, dot, tot).
+// A width's result is y = 0 + its first pass, + later passes, as the
+// reference's dispatch adds them into a zeroed y (sml/sml-run.c:612-680, :755).
+// The row's value ends in lane 8*(row % 4) of its pass.
+
+// Array of plane p's dot for width NB, and its factor when planes share one.
+template <int NB> SB_DEV int plane_arr(int p) {
+    switch (NB) {
+    case 3: case 5: return p;          // main plane, bit plane
+    case 6: return p == 0 ? 1 : 0;     // 2-bit plane apart, nibbles main
+    case 7: return p;                  // nibbles, 2-bit, bit
+    default: return 0;                 // Q2, Q4: one plane; Q8: lo + 16 hi
+    }
+}
+
+template <int NB>
+SB_DEV void tile_dots_exact(const uint8_t * tile, const TileGeom & tg, const ActS & a, int * D, int ng) {
+    constexpr int ND = dot_arrays(NB);
+    int kinds[3], shifts[3];
+    plane_kinds(NB, kinds, shifts);
+    const int lane = threadIdx.x & 31, TR = tg.TR, j = lane % TR, v = lane / TR, VS = 32 / TR;
+    const int nit = (tg.U + VS - 1) / VS;
+    for (int it = 0; it < nit; it++) {
+        const int u = v + it * VS;
+        const bool ok = u < tg.U;
+        int dd[ND][4];
+#pragma unroll
+        for (int r = 0; r < ND; r++) dd[r][0] = dd[r][1] = dd[r][2] = dd[r][3] = 0;
+        if (ok) {
+            uint4 av[4];
+#pragma unroll
+            for (int k = 0; k < 4; k++) av[k] = *reinterpret_cast<const uint4 *>(a.q + k * (a.n >> 2) + 16 * u);
+            const uint32_t a0[4] = {av[0].x, av[0].y, av[0].z, av[0].w}, a1[4] = {av[1].x, av[1].y, av[1].z, av[1].w};
+            const uint32_t a2[4] = {av[2].x, av[2].y, av[2].z, av[2].w}, a3[4] = {av[3].x, av[3].y, av[3].z, av[3].w};
+            const int at = u * TR + j;
+#pragma unroll
+            for (int p = 0; p < 3; p++) {
+                if (!kinds[p]) break;
+                const int r = plane_arr<NB>(p);
+                const int f = (NB == 8 && p == 1) ? 4 : 0;   // Q8: hi nibbles x16 into the main dot
+                const uint8_t * sec = tile + tg.pl_off[p];
+                int s4[4] = {0, 0, 0, 0};
+                if (kinds[p] == 4) {
+                    const uint4 w0 = *reinterpret_cast<const uint4 *>(sec + 16 * at);
+                    const uint4 w1 = *reinterpret_cast<const uint4 *>(sec + tg.pl_sec[p] + 16 * at);
+                    const uint32_t x0[4] = {w0.x, w0.y, w0.z, w0.w}, x1[4] = {w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+                    for (int w = 0; w < 4; w++) {
+                        s4[0] = __dp4a((int) (x0[w] & 0x0f0f0f0fu), (int) a0[w], s4[0]);
+                        s4[1] = __dp4a((int) ((x0[w] >> 4) & 0x0f0f0f0fu), (int) a1[w], s4[1]);
+                        s4[2] = __dp4a((int) (x1[w] & 0x0f0f0f0fu), (int) a2[w], s4[2]);
+                        s4[3] = __dp4a((int) ((x1[w] >> 4) & 0x0f0f0f0fu), (int) a3[w], s4[3]);
+                    }
+                } else if (kinds[p] == 2) {
+                    const uint4 w = *reinterpret_cast<const uint4 *>(sec + 16 * at);
+                    const uint32_t x[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                    for (int ww = 0; ww < 4; ww++) {
+                        s4[0] = __dp4a((int) (x[ww] & 0x03030303u), (int) a0[ww], s4[0]);
+                        s4[1] = __dp4a((int) ((x[ww] >> 2) & 0x03030303u), (int) a1[ww], s4[1]);
+                        s4[2] = __dp4a((int) ((x[ww] >> 4) & 0x03030303u), (int) a2[ww], s4[2]);
+                        s4[3] = __dp4a((int) ((x[ww] >> 6) & 0x03030303u), (int) a3[ww], s4[3]);
+                    }
+                } else {
+                    const uint2 w = *reinterpret_cast<const uint2 *>(sec + 8 * at);
+                    const uint32_t h[4] = {w.x & 0xffffu, w.x >> 16, w.y & 0xffffu, w.y >> 16};
+                    const uint32_t * ak[4] = {a0, a1, a2, a3};
+#pragma unroll
+                    for (int k = 0; k < 4; k++)
+#pragma unroll
+                        for (int ww = 0; ww < 4; ww++)
+                            s4[k] = __dp4a((int) nib_to_bytes((h[k] >> (4 * ww)) & 15u), (int) ak[k][ww], s4[k]);
+                }
+#pragma unroll
+                for (int k = 0; k < 4; k++) dd[r][k] += s4[k] << f;
+            }
+        }
+#pragma unroll
+        for (int r = 0; r < ND; r++)
+#pragma unroll
+            for (int k = 0; k < 4; k++) dd[r][k] += __shfl_xor_sync(0xffffffffu, dd[r][k], TR);
+        if (ok && !(v & 1)) {
+#pragma unroll
+            for (int r = 0; r < ND; r++)
+                *reinterpret_cast<int4 *>(D + (r * TR + j) * ng + 4 * (u >> 1)) =
+                    make_int4(dd[r][0], dd[r][1], dd[r][2], dd[r][3]);
+        }
+    }
+}
+
+// Group g's step d*sq and min md*(mq - bias) of tile row j, each a rounded
+// product as the reference forms them (sml/sml-kernel.c:655-661).
+// Field i (0..3) of a quad's packed step or min fields: a byte each, or 6 bits
+// of a 3-byte little-endian word (sml/sml-kernel.h:65-96).
+template <int SIX>
+SB_DEV float tile_field1(const uint8_t * f, int i) {
+    if (SIX) {
+        const uint32_t b = (uint32_t) f[0] | ((uint32_t) f[1] << 8) | ((uint32_t) f[2] << 16);
+        return (float) ((b >> (6 * i)) & 63u);
+    }
+    return (float) f[i];
+}
+template <int SIX>
+SB_DEV float tile_step(const uint8_t * tile, const TileGeom & tg, int j, int g) {
+    const float sq = tile_field1<SIX>(tile + tg.sq_off + ((g >> 2) * tg.TR + j) * tg.f_w, g & 3);
+    return __fmul_rn(h2f(*reinterpret_cast<const uint16_t *>(tile + tg.sd_off + ((g >> 3) * tg.TR + j) * 2)), sq);
+}
+template <int SIX>
+SB_DEV float tile_min(const uint8_t * tile, const TileGeom & tg, int j, int g, float mbias) {
+    const float mq = tile_field1<SIX>(tile + tg.mq_off + ((g >> 2) * tg.TR + j) * tg.f_w, g & 3);
+    return __fmul_rn(h2f(*reinterpret_cast<const uint16_t *>(tile + tg.md_off + ((g >> 3) * tg.TR + j) * 2)),
+                     __fsub_rn(mq, mbias));
+}
+
+// dot of group g from arrays (flat: a + 16 b when b != NULL)
+SB_DEV int dot_at(const int * da, const int * db, int g) { return db ? da[g] + 16 * db[g] : da[g]; }
+
+template <int SIX>
+SB_DEV float chain_flat(const uint8_t * tile, const TileGeom & tg, const ActS & a, const int * da, const int * db,
+                        int ng, int j, int L, bool with_min, float mbias) {
+    const int nblk = ng >> 3;
+    float acc = 0.0f, tac = 0.0f;
+    for (int k = 0; k < nblk; k++) {
+        const int g = 8 * k + L;
+        acc = __fmaf_rn(tile_step<SIX>(tile, tg, j, g), __fmul_rn(a.xs[g], (float) dot_at(da, db, g)), acc);
+        if (with_min) acc = __fmaf_rn(tile_min<SIX>(tile, tg, j, g, mbias), a.xsum[g], acc);
+    }
+    const bool tail = (ng & 7) != 0;
+    if (tail && L < 4) {
+        const int g = 8 * nblk + L;
+        tac = __fmaf_rn(tile_step<SIX>(tile, tg, j, g), __fmul_rn(a.xs[g], (float) dot_at(da, db, g)), tac);
+        if (with_min) tac = __fmaf_rn(tile_min<SIX>(tile, tg, j, g, mbias), a.xsum[g], tac);
+    }
+    const float s = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4, 8));
+    const float t = __fadd_rn(s, __shfl_down_sync(0xffffffffu, s, 1, 8));
+    float tot = __fadd_rn(t, __shfl_down_sync(0xffffffffu, t, 2, 8));
+    const float v = __fadd_rn(tac, __shfl_down_sync(0xffffffffu, tac, 1, 8));
+    const float tt = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 2, 8));
+    if (tail) tot = __fadd_rn(tot, tt);
+    return tot;
+}
+
+template <int SIX>
+SB_DEV float chain_ladder(const uint8_t * tile, const TileGeom & tg, const ActS & a, const int * d, float mul,
+                          int ng, int j, int L, bool with_min, float mbias) {
+    float acc = 0.0f;
+    if (L < 4)
+        for (int p = 0; p < (ng >> 2); p++) {
+            const int g = 4 * p + L;
+            acc = __fmaf_rn(tile_step<SIX>(tile, tg, j, g), __fmul_rn(a.xs[g], __fmul_rn((float) d[g], mul)), acc);
+            if (with_min) acc = __fmaf_rn(tile_min<SIX>(tile, tg, j, g, mbias), a.xsum[g], acc);
+        }
+    const float s = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 1, 8));
+    return __fadd_rn(s, __shfl_down_sync(0xffffffffu, s, 2, 8));
+}
+
+// The bit plane's chain, lane 0 of the row: groups whose 32 bits are not all zero.
+template <int SIX>
+SB_DEV float chain_bits1(const uint8_t * tile, const TileGeom & tg, const ActS & a, const int * d, int plane,
+                         int ng, int j, int L) {
+    float tot = 0.0f;
+    if (L == 0) {
+        const uint8_t * sec = tile + tg.pl_off[plane];
+        for (int g = 0; g < ng; g++) {
+            const int u0 = 2 * (g >> 2), i = g & 3;
+            const uint16_t b0 = *reinterpret_cast<const uint16_t *>(sec + (u0 * tg.TR + j) * 8 + 2 * i);
+            const uint16_t b1 = *reinterpret_cast<const uint16_t *>(sec + ((u0 + 1) * tg.TR + j) * 8 + 2 * i);
+            if (b0 | b1) tot = __fmaf_rn(__fmul_rn(tile_step<SIX>(tile, tg, j, g), a.xs[g]), (float) d[g], tot);
+        }
+    }
+    return tot;
+}
+
+// Rows of one tile: returns row l's value in lane l < TR.
+template <int NB, int SIX>
+SB_DEV float tile_exact(const uint8_t * tile, const TileGeom & tg, const ActS & a, int * D, bool has_min, float mbias) {
+    const int ng = a.n / kGroup, TR = tg.TR, lane = threadIdx.x & 31, jj = lane >> 3, L = lane & 7;
+    tile_dots_exact<NB>(tile, tg, a, D, ng);
+    __syncwarp();
+    float mine = 0.0f;
+    for (int r0 = 0; r0 < TR; r0 += 4) {
+        const int j = r0 + jj < TR ? r0 + jj : TR - 1;   // lanes past the last row repeat it and are dropped
+        const int * d0 = D + j * ng, * d1 = D + (TR + j) * ng, * d2 = D + (2 * TR + j) * ng;
+        float y = 0.0f;
+        switch (NB) {
+        case 2: y = __fadd_rn(0.0f, chain_ladder<SIX>(tile, tg, a, d0, 1.0f, ng, j, L, has_min, mbias)); break;
+        case 3: y = __fadd_rn(0.0f, chain_ladder<SIX>(tile, tg, a, d0, 1.0f, ng, j, L, has_min, mbias));
+                y = __fadd_rn(y, __fmul_rn(chain_bits1<SIX>(tile, tg, a, d1, 1, ng, j, L), 4.0f)); break;
+        case 5: y = __fadd_rn(0.0f, chain_flat<SIX>(tile, tg, a, d0, nullptr, ng, j, L, has_min, mbias));
+                y = __fadd_rn(y, __fmul_rn(chain_bits1<SIX>(tile, tg, a, d1, 1, ng, j, L), 16.0f)); break;
+        case 6: case 7:
+            if ((ng & 7) == 0) {
+                y = __fadd_rn(0.0f, chain_flat<SIX>(tile, tg, a, d0, d1, ng, j, L, has_min, mbias));
+            } else {
+                y = __fadd_rn(0.0f, chain_ladder<SIX>(tile, tg, a, d1, 16.0f, ng, j, L, has_min, mbias));
+                y = __fadd_rn(y, chain_flat<SIX>(tile, tg, a, d0, nullptr, ng, j, L, false, mbias));
+            }
+            if (NB == 7) y = __fadd_rn(y, __fmul_rn(chain_bits1<SIX>(tile, tg, a, d2, 2, ng, j, L), 64.0f));
+            break;
+        default: y = __fadd_rn(0.0f, chain_flat<SIX>(tile, tg, a, d0, nullptr, ng, j, L, has_min, mbias)); break;
+        }
+        // row r0 + (lane - r0) takes the value from lane 8 * (lane - r0)
+        const int src = lane - r0;
+        const float got = __shfl_sync(0xffffffffu, y, (src >= 0 && src < 4 ? src : 0) * 8);
+        if (src >= 0 && src < 4) mine = got;
+    }
+    return mine;
+}
+
 template <int MODE, int NB, int SIX>
 __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__ TGArgs g) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -454,7 +699,7 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__
     const int T = t.ntiles;
     const int t0 = (int) ((long) T * blockIdx.x / gridDim.x), t1 = (int) ((long) T * (blockIdx.x + 1) / gridDim.x);
     const int ns = g.nstage;
-    const StageLayout SL = stage_layout(t.cols, !g.in_permuted, g.norm_w != nullptr, g.x_smem);
+    const StageLayout SL = stage_layout(t.cols, !g.in_permuted, g.norm_w != nullptr, g.x_smem, tg_dot_bytes(t));
     uint8_t * ring = smem + SL.ring_off;
 #ifdef SB_CHECKED
     uint32_t dsm;
@@ -557,20 +802,22 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__
     tg_stage(g, a, red, smem, SL, &statics, failed);
     SB_MARK(g.trace, g.launch_id, 2);
     const TileGeom tg = tile_geom(t.cols, t.TR, NB, SIX, t.has_min);
-    const int TR = t.TR, j = lane % TR, v = lane / TR, VS = 32 / TR;
+    const int TR = t.TR;
+    // this warp's scratch for the group dots of its current tile
+    int * D = reinterpret_cast<int *>(smem + SL.d_off) + (size_t) warp * (tg_dot_bytes(t) / kConsWarps / 4);
     float best_v = -INFINITY;
     int best_i = 0x7fffffff;
     for (int i = t0 + warp; i < t1; i += kConsWarps) {
         const int k = i - t0, s = k % ns;
-        const bool ok = !failed && ring_wait(full, empty, k, ns, g.err);
+        // one verdict for the warp: the tile's lanes meet in shuffles
+        const bool ok = __all_sync(0xffffffffu, !failed && ring_wait(full, empty, k, ns, g.err));
         failed = !ok;
         if (k == 0) SB_MARK(g.trace, g.launch_id, 3);
         float acc = 0.0f;
         if (ok && SB_CHECK(g.err, tg.bytes == t.tb && (size_t) (s + 1) * t.tb + SL.ring_off <= ring_end, 106))
-            acc = tile_row<NB, SIX>(ring + (size_t) s * t.tb, tg, a, j, v, VS, t.has_min, t.mbias, g.err);
+            acc = tile_exact<NB, SIX>(ring + (size_t) s * t.tb, tg, a, D, t.has_min, t.mbias);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
-        for (int o = 16; o >= TR; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
         if (MODE == GM_FFN) {
             // rows 0..TR/2-1 of the tile are gate rows, TR/2..TR-1 the matching up rows
             const float up = __shfl_down_sync(0xffffffffu, acc, TR / 2);
@@ -578,7 +825,10 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__
             if (lane < TR / 2 && idx < g.ffn_f) {
                 const bool first = k < kConsWarps;
                 float gv = acc, uv = up;
-                if (g.bias) { gv += first ? gb0 : g.bias[idx]; uv += first ? ub0 : g.bias[g.ffn_f + idx]; }
+                if (g.bias) {
+                    gv = __fadd_rn(gv, first ? gb0 : g.bias[idx]);
+                    uv = __fadd_rn(uv, first ? ub0 : g.bias[g.ffn_f + idx]);
+                }
                 const int sc = first ? sc0 : g.scatter[idx];
                 if (SB_CHECK(g.err, sc >= 0 && sc < g.ffn_f, 108))
                     g.out[sc] = silu_mul(gv, uv);
@@ -589,10 +839,10 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__
         if (lane < TR && r < t.rows) {
             float y = acc;
             if (MODE == GM_QKV || MODE == GM_PLAIN) {
-                if (g.bias) y += (MODE == GM_QKV && k < kConsWarps) ? gb0 : g.bias[r];
+                if (g.bias) y = __fadd_rn(y, (MODE == GM_QKV && k < kConsWarps) ? gb0 : g.bias[r]);
                 g.out[r] = y;
             } else if (MODE == GM_O || MODE == GM_DOWN) {
-                g.out[r] = (k < kConsWarps ? res0 : g.out[r]) + y;
+                g.out[r] = __fadd_rn(k < kConsWarps ? res0 : g.out[r], y);
             } else if (MODE == GM_HEAD) {
                 g.out[r] = y;
                 if (y > best_v || (y == best_v && r < best_i)) { best_v = y; best_i = r; }
