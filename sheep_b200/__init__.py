@@ -182,7 +182,7 @@ class Engine:
     def launches_per_token(self):
         return lib().sb_launches_per_token(self.h)
 
-    KERNELS = {"qkv": 0, "o": 2, "ffn": 3, "down": 4, "head": 5}
+    KERNELS = {"qkv": 0, "attn": 1, "o": 2, "ffn": 3, "down": 4, "head": 5}
 
     def time_kernel(self, which, reps):
         """(avg ms per launch, weight bytes per launch) of one kernel class, each

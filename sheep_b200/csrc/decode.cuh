@@ -175,6 +175,7 @@ struct AttnArgs {
     int max_chunks;
     float * out;             // [qd] attention output
     const ExpfEntry * xtab;  // expf_libm.h table (k_attn_seq), or NULL: exp rounded from double
+    float xnear;             // ... consulted within this distance of a rounding midpoint
     int * err;
     unsigned long long * trace;
     int launch_id;
@@ -211,17 +212,26 @@ SB_DEV void norm_rope(float * v, const float * w, float eps, int hd, const float
 }
 
 // The host libm's expf on the device (expf_libm.h): exp in double rounded
-// once, corrected from the table where the host's expf differs.
-SB_DEV float expf_libm(float x, const ExpfEntry * tab) {
-    float y = __double2float_rn(exp((double) x));
+// once; where that double lies within `near` float ulps of a rounding midpoint
+// (about 0.2 % of arguments), the table says whether the host's expf rounds the
+// other way.
+SB_DEV float expf_libm(float x, const ExpfEntry * tab, float near) {
+    const double d = exp((double) x);
+    float y = __double2float_rn(d);
     if (tab && x < 0.0f) {
-        const uint32_t k = __float_as_uint(x), mask = (1u << kExpfBits) - 1u;
-        uint32_t h = expf_slot(k);
-        for (int i = 0; i < 64; i++) {   // the table is at most half full: a run ends well before
-            const ExpfEntry e = tab[h];
-            if (e.x == k) { y = __uint_as_float(e.y); break; }
-            if (e.x == 0xffffffffu) break;
-            h = (h + 1) & mask;
+        const double r = d - (double) y;   // exact: d and y agree to a float ulp
+        const uint32_t yb = __float_as_uint(y);
+        const float nb = __uint_as_float(r > 0.0 ? yb + 1u : yb - 1u);   // neighbour on d's side (y > 0)
+        const double side = fabs((double) nb - (double) y);
+        if (r != 0.0 && 0.5 * side - fabs(r) < (double) near * side) {
+            const uint32_t k = __float_as_uint(x), mask = (1u << kExpfBits) - 1u;
+            uint32_t h = expf_slot(k);
+            for (int i = 0; i < 64; i++) {   // the table is at most half full: a run ends well before
+                const ExpfEntry e = tab[h];
+                if (e.x == k) { y = __uint_as_float(e.y); break; }
+                if (e.x == 0xffffffffu) break;
+                h = (h + 1) & mask;
+            }
         }
     }
     return y;
@@ -257,12 +267,20 @@ SB_DEV void head_norm(float * v, const float * w, float eps, int hd, double * re
 }
 
 constexpr int kSeqThreads = 256;
-constexpr int kSeqChunk = 64;     // positions of V per shared-memory stage
+constexpr int kSeqCap = 192;      // cached positions whose K and V rows are staged in shared memory
+                                  // (96 KB at head size 128: the CTA still fits beside a GEMV's)
 
-// Shared memory of k_attn_seq: q, k, v, cos, sin, the scores of n_ctx
-// positions, the new key and value as fp16, two V stages.
+SB_DEV void cp_async16(void * dst, const void * src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_u32(dst)), "l"(src) : "memory");
+}
+SB_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Shared memory of k_attn_seq: q, k, v, cos, sin, a score per position, and
+// the K and V rows of the first kSeqCap positions (K rows padded by 16 bytes so
+// a warp's 16-byte reads of 32 rows fall in distinct banks).
+__host__ __device__ inline int attn_seq_cap(int n_ctx) { return n_ctx < kSeqCap ? n_ctx : kSeqCap; }
 __host__ __device__ inline size_t attn_seq_smem_bytes(int hd, int n_ctx) {
-    return (size_t) (4 * hd + ((n_ctx + 3) & ~3)) * 4 + (size_t) 2 * hd * 2 + (size_t) 2 * kSeqChunk * hd * 2;
+    return (size_t) (4 * hd + ((n_ctx + 3) & ~3)) * 4 + (size_t) attn_seq_cap(n_ctx) * (2 * hd + 8) * 2;
 }
 
 // Decode attention of one query head per CTA, in the reference's float order
@@ -271,26 +289,43 @@ __host__ __device__ inline size_t attn_seq_smem_bytes(int hd, int n_ctx) {
 //              fused multiply-adds over dims l, l+8, ... (one thread per position);
 //   softmax    max, e_t = expf(s_t - max) (the host libm's, expf_libm), their sum
 //              in position order (one thread), p_t = e_t * (1/sum);
-//   out[d]     = fma chain over positions 0..pos in order (one thread per dim),
-//              V streamed through two shared-memory stages of 64 positions.
-// Before that: Q/K norm if any, RoPE (rope_ref), the new key/value rounded to
-// fp16 and written to the cache by the group's first head; the new position's
-// key and value are taken from shared memory, never re-read from the cache.
-static __global__ void __launch_bounds__(kSeqThreads) k_attn_seq(const __grid_constant__ AttnArgs g) {
+//   out[d]     = fma chain over positions 0..pos in order (one thread per dim).
+// The cached rows (positions before pos, up to kSeqCap of them) do not depend on
+// the previous kernel: they are copied into shared memory (cp.async) before
+// the dependency wait; positions past kSeqCap are read from the cache in place.
+// After the wait: Q/K norm if any, RoPE (rope_ref), the new key/value rounded
+// to fp16, written to the cache by the group's first head and into this CTA's
+// staged rows. The serial loops (the softmax sum, each dim's chain) load a
+// block of 32 positions before its arithmetic.
+template <int HD>
+__global__ void __launch_bounds__(kSeqThreads) k_attn_seq(const __grid_constant__ AttnArgs g) {
     extern __shared__ __align__(16) float sm[];
     __shared__ double red[kSeqThreads / 32];
     __shared__ float wred[kSeqThreads / 32];
     __shared__ float s_inv;
     pdl_launch_dependents();
     SB_MARK(g.trace, g.launch_id, 0);
-    const int h = blockIdx.x, hd = g.hd, tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
+    constexpr int hd = HD;
+    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
     const int pos = g.pos ? *g.pos : g.pos_imm;
-    if (!SB_CHECK(g.err, pos >= 0 && pos < g.n_ctx && (hd & 7) == 0 && hd <= 256, 211)) { pdl_wait(); return; }
+    if (!SB_CHECK(g.err, pos >= 0 && pos < g.n_ctx && g.hd == HD, 211)) { pdl_wait(); return; }
     const int rep = g.n_head / g.n_kv, kvh = h / rep, np = pos + 1;
+    const int cap = attn_seq_cap(g.n_ctx), nst = pos < cap ? pos : cap;   // staged cached rows
+    const int ks = hd + 8;                                                // K row stride (halves)
     float * q = sm, * kn = sm + hd, * vn = sm + 2 * hd, * cs = sm + 3 * hd, * sn = cs + hd / 2;
     float * sc = sm + 4 * hd;
-    uint16_t * kh = reinterpret_cast<uint16_t *>(sc + ((g.n_ctx + 3) & ~3)), * vh = kh + hd;
-    uint16_t * vs = vh + hd;   // [2][kSeqChunk][hd]
+    uint16_t * Ks = reinterpret_cast<uint16_t *>(sc + ((g.n_ctx + 3) & ~3));   // [cap][hd + 8]
+    uint16_t * Vs = Ks + (size_t) cap * ks;                                     // [cap][hd]
+    const size_t row0 = (size_t) kvh * hd;
+    {
+        const int per = hd / 8;
+        for (int idx = tid; idx < nst * per; idx += kSeqThreads) {
+            const int t = idx / per, part = idx % per;
+            const size_t at = (size_t) t * g.kvd + row0 + part * 8;
+            cp_async16(Ks + (size_t) t * ks + part * 8, g.kc + at);
+            cp_async16(Vs + (size_t) t * hd + part * 8, g.vc + at);
+        }
+    }
     for (int i = tid; i < hd / 2; i += blockDim.x) {
         cs[i] = g.rcos[(size_t) pos * (hd / 2) + i];
         sn[i] = g.rsin[(size_t) pos * (hd / 2) + i];
@@ -308,89 +343,109 @@ static __global__ void __launch_bounds__(kSeqThreads) k_attn_seq(const __grid_co
     rope_ref(q, hd, cs, sn);
     rope_ref(kn, hd, cs, sn);
     __syncthreads();
-    const size_t row0 = (size_t) kvh * hd;
+    // the new row (rows past the staged ones are read from the cache, so a
+    // position beyond kSeqCap must reach it before the scores: a fence and the
+    // barrier below order the stores)
     for (int i = tid; i < hd; i += blockDim.x) {
-        kh[i] = f2h(kn[i]);
-        vh[i] = f2h(vn[i]);
-        if (h % rep == 0) { g.kc[(size_t) pos * g.kvd + row0 + i] = kh[i]; g.vc[(size_t) pos * g.kvd + row0 + i] = vh[i]; }
+        const uint16_t kh = f2h(kn[i]), vh = f2h(vn[i]);
+        if (pos < cap) { Ks[(size_t) pos * ks + i] = kh; Vs[(size_t) pos * hd + i] = vh; }
+        if (h % rep == 0 || pos >= cap) { g.kc[(size_t) pos * g.kvd + row0 + i] = kh; g.vc[(size_t) pos * g.kvd + row0 + i] = vh; }
     }
+    if (pos >= cap) __threadfence_block();
+    cp_async_wait_all();
     __syncthreads();
     SB_MARK(g.trace, g.launch_id, 2);
     // scores, one position per thread
     float m = -INFINITY;
     for (int t = tid; t < np; t += blockDim.x) {
         float c[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        const uint16_t * kr = t == pos ? kh : g.kc + (size_t) t * g.kvd + row0;
+        const uint16_t * kr = t < cap ? Ks + (size_t) t * ks : g.kc + (size_t) t * g.kvd + row0;
+#pragma unroll
         for (int i0 = 0; i0 < hd; i0 += 8) {
             const uint4 w = *reinterpret_cast<const uint4 *>(kr + i0);
-            const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int l = 0; l < 4; l++) {
-                c[2 * l] = __fmaf_rn(q[i0 + 2 * l], h2f((uint16_t) (ww[l] & 0xffffu)), c[2 * l]);
-                c[2 * l + 1] = __fmaf_rn(q[i0 + 2 * l + 1], h2f((uint16_t) (ww[l] >> 16)), c[2 * l + 1]);
-            }
+            const float4 qa = *reinterpret_cast<const float4 *>(q + i0), qb = *reinterpret_cast<const float4 *>(q + i0 + 4);
+            c[0] = __fmaf_rn(qa.x, h2f((uint16_t) (w.x & 0xffffu)), c[0]);
+            c[1] = __fmaf_rn(qa.y, h2f((uint16_t) (w.x >> 16)), c[1]);
+            c[2] = __fmaf_rn(qa.z, h2f((uint16_t) (w.y & 0xffffu)), c[2]);
+            c[3] = __fmaf_rn(qa.w, h2f((uint16_t) (w.y >> 16)), c[3]);
+            c[4] = __fmaf_rn(qb.x, h2f((uint16_t) (w.z & 0xffffu)), c[4]);
+            c[5] = __fmaf_rn(qb.y, h2f((uint16_t) (w.z >> 16)), c[5]);
+            c[6] = __fmaf_rn(qb.z, h2f((uint16_t) (w.w & 0xffffu)), c[6]);
+            c[7] = __fmaf_rn(qb.w, h2f((uint16_t) (w.w >> 16)), c[7]);
         }
         const float s = __fadd_rn(__fadd_rn(__fadd_rn(c[0], c[4]), __fadd_rn(c[1], c[5])),
                                   __fadd_rn(__fadd_rn(c[2], c[6]), __fadd_rn(c[3], c[7])));
         sc[t] = __fmul_rn(s, g.scale);
         m = fmaxf(m, sc[t]);
     }
+    SB_MARK(g.trace, g.launch_id, 5);
     m = warp_max(m);
     if (lane == 0) wred[wp] = m;
     __syncthreads();
     m = wred[0];
     for (int k = 1; k < (int) (blockDim.x >> 5); k++) m = fmaxf(m, wred[k]);
-    for (int t = tid; t < np; t += blockDim.x) sc[t] = expf_libm(__fsub_rn(sc[t], m), g.xtab);
-    // the first V stage's loads go out before the sequential sum
-    const int per = hd / 8, nck = (np + kSeqChunk - 1) / kSeqChunk;
-    constexpr int kPer = kSeqChunk * 256 / 8 / kSeqThreads;   // 16-byte pieces per thread at hd 256
-    const int nper = kSeqChunk * per / kSeqThreads;
-    auto load_chunk = [&](int c, uint4 (&r)[kPer]) {
-#pragma unroll
-        for (int k = 0; k < kPer; k++) {
-            if (k >= nper) break;
-            const int idx = tid + k * kSeqThreads, t = c * kSeqChunk + idx / per;
-            r[k] = make_uint4(0u, 0u, 0u, 0u);
-            if (idx < kSeqChunk * per && t < pos) r[k] = *reinterpret_cast<const uint4 *>(g.vc + (size_t) t * g.kvd + row0 + (idx % per) * 8);
-        }
-    };
-    auto store_chunk = [&](int c, const uint4 (&r)[kPer]) {
-        uint16_t * dst = vs + (size_t) (c & 1) * kSeqChunk * hd;
-#pragma unroll
-        for (int k = 0; k < kPer; k++) {
-            if (k >= nper) break;
-            const int idx = tid + k * kSeqThreads, t = c * kSeqChunk + idx / per;
-            if (idx < kSeqChunk * per && t <= pos)
-                *reinterpret_cast<uint4 *>(dst + (size_t) (idx / per) * hd + (idx % per) * 8) =
-                    t == pos ? *reinterpret_cast<const uint4 *>(vh + (idx % per) * 8) : r[k];
-        }
-    };
-    uint4 rv[kPer];
-    load_chunk(0, rv);
+    for (int t = tid; t < np; t += blockDim.x) sc[t] = expf_libm(__fsub_rn(sc[t], m), g.xtab, g.xnear);
     __syncthreads();
+    SB_MARK(g.trace, g.launch_id, 6);
     if (tid == 0) {
+        // the sum in position order, each block of 32 loaded (as float4) before it is added
         float sum = 0.0f;
-        for (int t = 0; t < np; t++) sum = __fadd_rn(sum, sc[t]);
+        int t = 0;
+        for (; t + 32 <= np; t += 32) {
+            float4 e[8];
+#pragma unroll
+            for (int u = 0; u < 8; u++) e[u] = *reinterpret_cast<const float4 *>(sc + t + 4 * u);
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                sum = __fadd_rn(sum, e[u].x); sum = __fadd_rn(sum, e[u].y);
+                sum = __fadd_rn(sum, e[u].z); sum = __fadd_rn(sum, e[u].w);
+            }
+        }
+        for (; t < np; t++) sum = __fadd_rn(sum, sc[t]);
         s_inv = __fdiv_rn(1.0f, sum);
     }
-    store_chunk(0, rv);
     __syncthreads();
     SB_MARK(g.trace, g.launch_id, 3);
     const float inv = s_inv;
     for (int t = tid; t < np; t += blockDim.x) sc[t] = __fmul_rn(sc[t], inv);
     __syncthreads();
-    float o = 0.0f;
-    for (int c = 0; c < nck; c++) {
-        if (c + 1 < nck) load_chunk(c + 1, rv);
-        if (tid < hd) {
-            const uint16_t * src = vs + (size_t) (c & 1) * kSeqChunk * hd + tid;
-            const int t0 = c * kSeqChunk, nt = min(kSeqChunk, np - t0);
-            for (int t = 0; t < nt; t++) o = __fmaf_rn(sc[t0 + t], h2f(src[(size_t) t * hd]), o);
+    SB_MARK(g.trace, g.launch_id, 7);
+    if (tid < hd / 2) {
+        // two dims per thread (one 4-byte load of V per position), two chains
+        const int d = 2 * tid;
+        float o0 = 0.0f, o1 = 0.0f;
+        const int ns = np < cap ? np : cap;
+        const uint32_t * vcol = reinterpret_cast<const uint32_t *>(Vs + d);
+        int t = 0;
+        for (; t + 32 <= ns; t += 32) {
+            float4 p[8];
+            uint32_t v[32];
+#pragma unroll
+            for (int u = 0; u < 8; u++) p[u] = *reinterpret_cast<const float4 *>(sc + t + 4 * u);
+#pragma unroll
+            for (int u = 0; u < 32; u++) v[u] = vcol[(size_t) (t + u) * (hd / 2)];
+#pragma unroll
+            for (int u = 0; u < 8; u++) {
+                const float pp[4] = {p[u].x, p[u].y, p[u].z, p[u].w};
+#pragma unroll
+                for (int w = 0; w < 4; w++) {
+                    const uint32_t vv = v[4 * u + w];
+                    o0 = __fmaf_rn(pp[w], h2f((uint16_t) (vv & 0xffffu)), o0);
+                    o1 = __fmaf_rn(pp[w], h2f((uint16_t) (vv >> 16)), o1);
+                }
+            }
         }
-        if (c + 1 < nck) store_chunk(c + 1, rv);
-        __syncthreads();
+        for (; t < ns; t++) {
+            const uint32_t vv = vcol[(size_t) t * (hd / 2)];
+            o0 = __fmaf_rn(sc[t], h2f((uint16_t) (vv & 0xffffu)), o0);
+            o1 = __fmaf_rn(sc[t], h2f((uint16_t) (vv >> 16)), o1);
+        }
+        for (; t < np; t++) {
+            o0 = __fmaf_rn(sc[t], h2f(g.vc[(size_t) t * g.kvd + row0 + d]), o0);
+            o1 = __fmaf_rn(sc[t], h2f(g.vc[(size_t) t * g.kvd + row0 + d + 1]), o1);
+        }
+        *reinterpret_cast<float2 *>(g.out + h * hd + d) = make_float2(o0, o1);
     }
-    if (tid < hd) g.out[h * hd + tid] = o;
     SB_MARK(g.trace, g.launch_id, 4);
 }
 

@@ -63,6 +63,7 @@ struct sb_engine {
     int * am_idx = nullptr;
     unsigned * am_cnt = nullptr;
     const ExpfEntry * xtab = nullptr;  // the host libm's expf corrections (expf_libm.h)
+    float xnear = 0.0f;                // ... looked up within this midpoint distance
     MoeScratch ms;                    // routing scratch shared by every MoE layer (one token)
     int * err = nullptr;              // bounded waits that gave up
     unsigned long long * trace = nullptr;   // trace build: [launch][cta][8] timestamps
@@ -185,6 +186,23 @@ static void launch_tg(sb_engine * e, int mode, const TGArgs & g0) {
     SB_DISPATCH_QT(g.t.nbits, g.t.six, launch_tg_nb, e, mode, g, grid, tg_smem(g));
 }
 
+// Decode attention of layer l (k_attn_seq, one CTA per query head).
+static void launch_attn(sb_engine * e, int l) {
+    const LayerD & y = e->L[l];
+    AttnArgs a;
+    memset(&a, 0, sizeof a);
+    a.qkv = e->qkv; a.n_head = e->nh; a.n_kv = e->nkv; a.hd = e->hd; a.qd = e->qd; a.kvd = e->kvd;
+    a.qn = y.qn; a.kn = y.kn; a.eps = e->eps;
+    a.rcos = e->rcos; a.rsin = e->rsin;
+    a.kc = e->kc + (size_t) l * e->n_ctx * e->kvd;
+    a.vc = e->vc + (size_t) l * e->n_ctx * e->kvd;
+    a.n_ctx = e->n_ctx; a.pos = e->pos; a.scale = e->scale;
+    a.out = e->att; a.err = e->err; a.xtab = e->xtab; a.xnear = e->xnear;
+    a.trace = e->trace; a.launch_id = e->launches;
+    auto k = e->hd == 64 ? k_attn_seq<64> : e->hd == 128 ? k_attn_seq<128> : k_attn_seq<256>;
+    launch(e, true, k, dim3(e->nh), dim3(kSeqThreads), attn_seq_smem_bytes(e->hd, e->n_ctx), a);
+}
+
 // One token: embed, every layer, head and argmax. Enqueued on e->st (captured).
 static void enqueue_token(sb_engine * e) {
     snprintf(e->cur, sizeof e->cur, "embed");
@@ -198,18 +216,8 @@ static void enqueue_token(sb_engine * e) {
             set_next(g, &y.o, e->nsm);
             launch_tg(e, GM_QKV, g);
         }
-        AttnArgs a;
-        memset(&a, 0, sizeof a);
-        a.qkv = e->qkv; a.n_head = e->nh; a.n_kv = e->nkv; a.hd = e->hd; a.qd = e->qd; a.kvd = e->kvd;
-        a.qn = y.qn; a.kn = y.kn; a.eps = e->eps;
-        a.rcos = e->rcos; a.rsin = e->rsin;
-        a.kc = e->kc + (size_t) l * e->n_ctx * e->kvd;
-        a.vc = e->vc + (size_t) l * e->n_ctx * e->kvd;
-        a.n_ctx = e->n_ctx; a.pos = e->pos; a.scale = e->scale;
-        a.out = e->att; a.err = e->err; a.xtab = e->xtab;
-        a.trace = e->trace; a.launch_id = e->launches;
         snprintf(e->cur, sizeof e->cur, "L%d.attn", l);
-        launch(e, true, k_attn_seq, dim3(e->nh), dim3(kSeqThreads), attn_seq_smem_bytes(e->hd, e->n_ctx), a);
+        launch_attn(e, l);
         snprintf(e->cur, sizeof e->cur, "L%d.o", l);
         {
             TGArgs g = tg_args(e, y.o, e->att, nullptr, e->x);
@@ -372,9 +380,10 @@ static bool build(sb_engine * e, char * why, int nwhy) {
     e->am_idx = (int *) carve(e, (size_t) 4 * e->nsm * 4);
     e->am_cnt = (unsigned *) carve(e, 4);
     {
-        const std::vector<ExpfEntry> & xt = expf_libm_table();
-        if (xt.empty()) { snprintf(why, nwhy, "this libm's expf differs from the rounded exponential too often"); return false; }
-        e->xtab = (const ExpfEntry *) e->ar.upload(xt.data(), xt.size() * sizeof(ExpfEntry));
+        const ExpfTable & xt = expf_libm_table();
+        if (xt.slots.empty()) { snprintf(why, nwhy, "this libm's expf differs from the rounded exponential too often"); return false; }
+        e->xtab = (const ExpfEntry *) e->ar.upload(xt.slots.data(), xt.slots.size() * sizeof(ExpfEntry));
+        e->xnear = xt.near;
     }
     e->err = (int *) carve(e, 4);
     if (moe0) moe_carve(e->ar, *moe0, 1, e->ms);
@@ -389,8 +398,8 @@ static bool build(sb_engine * e, char * why, int nwhy) {
 // Average duration of one kernel class of the token, each launch alone on the
 // engine's stream (no programmatic overlap), timed by CUDA events, cycling
 // over the layers so the weights come from HBM rather than L2 (a layer's
-// gate/up is 16 MB, the 28 layers 445 MB). which: 0 q|k|v, 2 o, 3 gate/up,
-// 4 down, 5 head. bytes_out: the file's bytes of the weights one launch reads.
+// gate/up is 16 MB, the 28 layers 445 MB). which: 0 q|k|v, 1 attention (at
+// the engine's current position), 2 o, 3 gate/up, 4 down, 5 head. bytes_out: the file's bytes of the weights one launch reads.
 // Leaves the decode state undefined: call it after generating, not between.
 extern "C" int sb_time_kernel(sb_engine * e, int which, int reps, float * ms_avg, double * bytes_out) {
     if (!e || reps < 1 || e->sync_mode) return 0;
@@ -402,6 +411,7 @@ extern "C" int sb_time_kernel(sb_engine * e, int which, int reps, float * ms_avg
         switch (which) {
         case 0: return (double) (ssf_rec_bytes(R("blk.%d.attn_q.weight")) + ssf_rec_bytes(R("blk.%d.attn_k.weight")) +
                                  ssf_rec_bytes(R("blk.%d.attn_v.weight")));
+        case 1: return (double) e->kvd * 2 * 2 * (e->n_ctx);   // an upper bound: the whole cache of one layer
         case 2: return (double) ssf_rec_bytes(R("blk.%d.attn_output.weight"));
         case 3: return (double) (ssf_rec_bytes(R("blk.%d.ffn_gate.weight")) + ssf_rec_bytes(R("blk.%d.ffn_up.weight")));
         case 4: return (double) ssf_rec_bytes(R("blk.%d.ffn_down.weight"));
@@ -421,6 +431,7 @@ extern "C" int sb_time_kernel(sb_engine * e, int which, int reps, float * ms_avg
         TGArgs g;
         switch (which) {
         case 0: g = tg_args(e, y.qkv, e->x, y.an, e->qkv); g.bias = y.qkv_b; launch_tg(e, GM_QKV, g); break;
+        case 1: launch_attn(e, l); break;
         case 2: g = tg_args(e, y.o, e->att, nullptr, e->x); launch_tg(e, GM_O, g); break;
         case 3: g = tg_args(e, y.gateup, e->x, y.fn, e->hp); g.ffn_f = e->F; g.scatter = y.down_iperm;
                 launch_tg(e, GM_FFN, g); break;
@@ -494,9 +505,10 @@ sb_engine * sb_open(const char * path, int n_ctx, char * why, int nwhy) {
         int optin = 0;
         cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
         const size_t as = attn_seq_smem_bytes(e->hd, e->n_ctx);
-        if (as + 1024 > (size_t) optin ||
-            cudaFuncSetAttribute(k_attn_seq, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) as) != cudaSuccess) {
-            snprintf(why, nwhy, "n_ctx %d: attention scores do not fit in shared memory", e->n_ctx);
+        if (as + 1024 > (size_t) optin || (e->hd != 64 && e->hd != 128 && e->hd != 256) ||
+            cudaFuncSetAttribute(e->hd == 64 ? k_attn_seq<64> : e->hd == 128 ? k_attn_seq<128> : k_attn_seq<256>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int) as) != cudaSuccess) {
+            snprintf(why, nwhy, "head size %d at n_ctx %d: no decode attention for it (sizes 64, 128, 256; scores in shared memory)", e->hd, e->n_ctx);
             close_all(e); delete e; return nullptr;
         }
     }

@@ -14,7 +14,12 @@
 // routing only ever take exp of x - max <= 0.
 //
 // The table is an open-addressing hash of 2^kExpfBits slots (x bits, expf(x)
-// bits), empty slots keyed 0xffffffff (a NaN: never an argument).
+// bits), empty slots keyed 0xffffffff (a NaN: never an argument). libm's
+// expf only rounds differently where the exact exp(x) lies very near a float
+// rounding midpoint (glibc's worst case here: 0.0016 of a float ulp), so the
+// device looks an argument up only when its double exp lies within `near` ulp
+// of one -- about 0.2 % of arguments; the build checks that every entry
+// qualifies.
 #pragma once
 
 #include <cstdint>
@@ -29,8 +34,14 @@ struct ExpfEntry { uint32_t x, y; };
 // Slot of key k (multiplicative hash); probes continue linearly.
 __host__ __device__ inline uint32_t expf_slot(uint32_t k) { return (k * 0x9E3779B1u) >> (32 - kExpfBits); }
 
-// The table for this process's libm (built on first use, then shared), or an
-// empty vector if more entries than half the slots were found.
-const std::vector<ExpfEntry> & expf_libm_table();
+struct ExpfTable {
+    std::vector<ExpfEntry> slots;   // empty if the table could not be built
+    float near;                     // midpoint distance (float ulps) below which to look up
+};
+
+// The table for this process's libm (built on first use, then shared). Empty
+// if more entries than half the slots were found, or an entry lies farther
+// from its midpoint than the lookup threshold could allow.
+const ExpfTable & expf_libm_table();
 
 }  // namespace sb

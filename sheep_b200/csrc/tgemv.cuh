@@ -593,21 +593,45 @@ SB_DEV float tile_min(const uint8_t * tile, const TileGeom & tg, int j, int g, f
 // dot of group g from arrays (flat: a + 16 b when b != NULL)
 SB_DEV int dot_at(const int * da, const int * db, int g) { return db ? da[g] + 16 * db[g] : da[g]; }
 
+// One group's two terms of the flat epilogue: step*(xs*dot) and min, xs*sum.
+template <int SIX>
+SB_DEV void flat_terms(const uint8_t * tile, const TileGeom & tg, const ActS & a, const int * da, const int * db,
+                       int j, int g, bool with_min, float mbias, float & st, float & t1, float & mn, float & xm) {
+    st = tile_step<SIX>(tile, tg, j, g);
+    t1 = __fmul_rn(a.xs[g], (float) dot_at(da, db, g));
+    mn = with_min ? tile_min<SIX>(tile, tg, j, g, mbias) : 0.0f;
+    xm = with_min ? a.xsum[g] : 0.0f;
+}
+
 template <int SIX>
 SB_DEV float chain_flat(const uint8_t * tile, const TileGeom & tg, const ActS & a, const int * da, const int * db,
                         int ng, int j, int L, bool with_min, float mbias) {
     const int nblk = ng >> 3;
     float acc = 0.0f, tac = 0.0f;
-    for (int k = 0; k < nblk; k++) {
-        const int g = 8 * k + L;
-        acc = __fmaf_rn(tile_step<SIX>(tile, tg, j, g), __fmul_rn(a.xs[g], (float) dot_at(da, db, g)), acc);
-        if (with_min) acc = __fmaf_rn(tile_min<SIX>(tile, tg, j, g, mbias), a.xsum[g], acc);
+    int k = 0;
+    // four steps' operands are loaded before their fused multiply-adds
+    for (; k + 4 <= nblk; k += 4) {
+        float st[4], t1[4], mn[4], xm[4];
+#pragma unroll
+        for (int u = 0; u < 4; u++) flat_terms<SIX>(tile, tg, a, da, db, j, 8 * (k + u) + L, with_min, mbias, st[u], t1[u], mn[u], xm[u]);
+#pragma unroll
+        for (int u = 0; u < 4; u++) {
+            acc = __fmaf_rn(st[u], t1[u], acc);
+            if (with_min) acc = __fmaf_rn(mn[u], xm[u], acc);
+        }
+    }
+    for (; k < nblk; k++) {
+        float st, t1, mn, xm;
+        flat_terms<SIX>(tile, tg, a, da, db, j, 8 * k + L, with_min, mbias, st, t1, mn, xm);
+        acc = __fmaf_rn(st, t1, acc);
+        if (with_min) acc = __fmaf_rn(mn, xm, acc);
     }
     const bool tail = (ng & 7) != 0;
     if (tail && L < 4) {
-        const int g = 8 * nblk + L;
-        tac = __fmaf_rn(tile_step<SIX>(tile, tg, j, g), __fmul_rn(a.xs[g], (float) dot_at(da, db, g)), tac);
-        if (with_min) tac = __fmaf_rn(tile_min<SIX>(tile, tg, j, g, mbias), a.xsum[g], tac);
+        float st, t1, mn, xm;
+        flat_terms<SIX>(tile, tg, a, da, db, j, 8 * nblk + L, with_min, mbias, st, t1, mn, xm);
+        tac = __fmaf_rn(st, t1, tac);
+        if (with_min) tac = __fmaf_rn(mn, xm, tac);
     }
     const float s = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4, 8));
     const float t = __fadd_rn(s, __shfl_down_sync(0xffffffffu, s, 1, 8));
