@@ -9,6 +9,8 @@
 //                            (sml/sml-run.c:1236, :3243), prompt stepped a token
 //                            at a time as SML_SEQ_PROMPT=1 does (sml/sml-cli.c:481)
 //   refh_quantize_act        sml_quantize_act (sml/sml-kernel.c:41)
+//   refh_quantize_act_sb     sml_quantize_act_sb (sml/sml-kernel.c:116), the
+//                            batched path's per-256 activation
 //   refh_matvec              gather + quantize + the per-width dispatch of
 //                            issue_rows_act (sml/sml-run.c:612-680), issued the
 //                            way sml/sml-check.c:166-245 issues it
@@ -89,6 +91,11 @@ int refh_decode(void * p, const int * prompt, int np, int ngen, int * ids_out, f
 void refh_quantize_act(const float * x, int n, int8_t * q, float * scale, int32_t * sums) {
     sml_act a = { q, scale, sums, n };
     sml_quantize_act(&a, x, n);
+}
+
+void refh_quantize_act_sb(const float * x, int n, int8_t * q, float * scale, int32_t * sums) {
+    sml_act a = { q, scale, sums, n };
+    sml_quantize_act_sb(&a, x, n);
 }
 
 // y[row0..row1) = W x for one tensor, x in the model's natural column order.

@@ -103,6 +103,29 @@ void so_quantize_act(const float * x, int n, int8_t * q, float * scale, int32_t 
     }
 }
 
+// sml/sml-kernel.c:161-189 (scalar arm of sml_quantize_act_sb)
+void so_quantize_act_sb(const float * x, int n, int8_t * q, float * scale, int32_t * sums) {
+    const int ng = n / G;
+    for (int g0 = 0; g0 < ng; g0 += 8) {
+        const int g1 = g0 + 8 < ng ? g0 + 8 : ng;
+        float amax = 0.0f;
+        for (int i = g0 * G; i < g1 * G; i++) { const float v = fabsf(x[i]); if (v > amax) amax = v; }
+        const float s = amax / 127.0f;
+        const float is = s > 0.0f ? 1.0f / s : 0.0f;
+        for (int g = g0; g < g1; g++) {
+            int32_t sum = 0;
+            for (int i = 0; i < G; i++) {
+                int v = (int) lrintf(x[g * G + i] * is);
+                v = v > 127 ? 127 : v < -127 ? -127 : v;
+                q[g * G + i] = (int8_t) v;
+                sum += v;
+            }
+            scale[g] = s;
+            sums[g] = sum;
+        }
+    }
+}
+
 // ------------------------------------------------------------- model
 
 struct so_model {
@@ -456,16 +479,13 @@ static void sb_row(const int8_t * w8, const float * s8, const int32_t * perm, in
     int8_t * q = (int8_t *) calloc((size_t) K, 1);
     float * xs = (float *) malloc((size_t) nsb * 4), * xg = (float *) malloc((size_t) n * 4);
     for (int i = 0; i < n; i++) xg[i] = x[perm[i]];
-    for (int sb = 0; sb < nsb; sb++) {
-        const int i0 = sb * 256, i1 = (sb * 8 + 8 < ng ? sb * 8 + 8 : ng) * G;
-        float amax = 0.0f;
-        for (int i = i0; i < i1; i++) { const float v = fabsf(xg[i]); if (v > amax) amax = v; }
-        const float sc = amax / 127.0f, is = sc > 0.0f ? 1.0f / sc : 0.0f;
-        xs[sb] = sc;
-        for (int i = i0; i < i1; i++) {
-            int v = (int) lrintf(xg[i] * is);
-            q[i] = (int8_t) (v > 127 ? 127 : v < -127 ? -127 : v);
-        }
+    {
+        // the per-256 activation (sml_quantize_act_sb); past n the codes stay 0
+        float * gs = (float *) malloc((size_t) ng * 4);
+        int32_t * gsum = (int32_t *) malloc((size_t) ng * 4);
+        so_quantize_act_sb(xg, n, q, gs, gsum);
+        for (int sb = 0; sb < nsb; sb++) xs[sb] = gs[sb * 8];
+        free(gs); free(gsum);
     }
 #pragma omp parallel for schedule(static)
     for (int row = 0; row < rows; row++) {

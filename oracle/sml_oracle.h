@@ -12,6 +12,10 @@ extern "C" {
 
 // sml/sml-kernel.c:89-109 (scalar arm of sml_quantize_act)
 void so_quantize_act(const float * x, int n, int8_t * q, float * scale, int32_t * sums);
+// sml/sml-kernel.c:116-190 (sml_quantize_act_sb): one scale per 256 values
+// (a partial last superblock on its own), written into each of its groups;
+// codes and per-group sums as sml_quantize_act.
+void so_quantize_act_sb(const float * x, int n, int8_t * q, float * scale, int32_t * sums);
 
 typedef struct so_model so_model;
 

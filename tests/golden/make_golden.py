@@ -16,7 +16,9 @@ For a two-layer model: 8 greedy ids after an 8-token prompt and their logits
 (sml_forward, the prompt stepped a token at a time). The same for a two-layer
 mixture-of-experts model (16 experts, 4 per token, renormalized softmax), and
 sml_moe_route's choices and weights on seeded logits with planted ties, for
-moe_flags 1 and 0.
+moe_flags 1 and 0. sml_quantize_act_sb's per-256 activation (the batched
+path's) on seeded vectors with a zero superblock, exact .5 ties, saturation
+and a partial last superblock.
 """
 import json
 import os
@@ -55,6 +57,21 @@ def route_logits():
         lg[t, rng.integers(0, 128, 6)] = lg[t].max()
     lg[1, :] = 0.5                               # every expert tied
     return lg
+
+
+def act_sb_inputs():
+    rng = np.random.default_rng(77)
+    xs = []
+    for n in (256, 1024, 1408, 4096):      # 1408: a partial (4-group) last superblock
+        x = rng.standard_normal(n).astype(np.float32)
+        xs.append(x)
+    x = np.zeros(1408, np.float32)
+    x[256:512] = np.float32(0.5) * np.arange(256, dtype=np.float32) - 64.0   # .5 ties at amax 63.5 -> 127/63.5 = 2
+    x[512:768] = 127.0
+    x[513] = -1e6                                                             # one huge value: everything else rounds to 0
+    x[1280:] = rng.standard_normal(128).astype(np.float32) * 1e-30            # tiny, still nonzero
+    xs.append(x)
+    return xs
 
 
 def check_input(n):
@@ -112,6 +129,12 @@ def main():
         out[f"sel_f{flags}"] = sel
         out[f"w_f{flags}"] = w
     np.savez_compressed(os.path.join(HERE, "route.npz"), **out)
+    out = {}
+    for i, x in enumerate(act_sb_inputs()):
+        q, s, sums = helpers.ref("quant_sb", x=x)
+        out[f"x{i}"], out[f"q{i}"], out[f"s{i}"], out[f"sums{i}"] = x, q, s, sums
+    np.savez_compressed(os.path.join(HERE, "act_sb.npz"), **out)
+    index["act_sb.npz"] = {"inputs": len(act_sb_inputs())}
     index["route.npz"] = {"k": 8, "n_expert": 128}
     with open(os.path.join(HERE, "index.json"), "w") as f:
         json.dump(index, f, indent=1, sort_keys=True)

@@ -206,6 +206,16 @@ def oracle_quant(x):
     return q, s, sums
 
 
+def oracle_quant_sb(x):
+    x = np.ascontiguousarray(x, np.float32)
+    n = len(x)
+    q = np.zeros(n, np.int8)
+    s = np.zeros(n // 32, np.float32)
+    sums = np.zeros(n // 32, np.int32)
+    Oracle.lib().so_quantize_act_sb(_p(x), n, _p(q), _p(s), _p(sums))
+    return q, s, sums
+
+
 def oracle_route(lg, k, flags=1):
     lg = np.ascontiguousarray(lg, np.float32)
     sel = np.zeros(16, np.int32)
@@ -226,12 +236,37 @@ def _ref_lib():
 
 def _ref_task(kind, path, args):
     L = _ref_lib()
-    if kind == "quant":
+    if kind in ("quant", "quant_sb"):
         x = np.ascontiguousarray(args["x"], np.float32)
         n = len(x)
         q, s, sums = np.zeros(n, np.int8), np.zeros(n // 32, np.float32), np.zeros(n // 32, np.int32)
-        L.refh_quantize_act(_p(x), n, _p(q), _p(s), _p(sums))
+        (L.refh_quantize_act if kind == "quant" else L.refh_quantize_act_sb)(_p(x), n, _p(q), _p(s), _p(sums))
         return q, s, sums
+    if kind == "multi":
+        # sml_forward_multi over ns conversations, each its own context; steps
+        # of (tokens, positions), a position < 0 leaving that slot out of the
+        # call. env: SML_MULTI etc. as the reference reads them.
+        for k, v in args.get("env", {}).items():
+            os.environ[k] = v
+        ns, nv = args["ns"], args["n_vocab"]
+        L.refh_forward_multi.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int, ctypes.c_void_p]
+        hs = [L.refh_open(path.encode(), args.get("n_ctx", 64), args.get("threads", 4), 1) for _ in range(ns)]
+        outs = []
+        try:
+            for tok, pos in args["steps"]:
+                idx = [i for i in range(ns) if pos[i] >= 0]
+                lg = np.zeros((len(idx), nv), np.float32)
+                sub = (ctypes.c_void_p * len(idx))(*[hs[i] for i in idx])
+                tk = np.ascontiguousarray([tok[i] for i in idx], np.int32)
+                ps = np.ascontiguousarray([pos[i] for i in idx], np.int32)
+                L.refh_forward_multi(sub, _p(tk), _p(ps), len(idx), _p(lg))
+                full = np.zeros((ns, nv), np.float32)
+                full[idx] = lg
+                outs.append(full)
+        finally:
+            for h in hs:
+                L.refh_close(ctypes.c_void_p(h))
+        return np.array(outs)
     if kind == "route":
         lg = np.ascontiguousarray(args["lg"], np.float32)
         sel, w = np.zeros(16, np.int32), np.zeros(16, np.float32)

@@ -165,3 +165,40 @@ def test_oracle_batch_bookkeeping():
             # the next sequence re-uses positions 0.. of the model's cache
     finally:
         orc.close()
+
+
+def test_quantize_act_sb_against_reference_vectors():
+    """The batched path's per-256 activation (sml_quantize_act_sb) against the
+    reference's own outputs: codes, per-group scales and sums bit for bit,
+    including a zero superblock, .5 ties, one huge value, tiny values and a
+    partial last superblock."""
+    g = np.load(os.path.join(GOLD, "act_sb.npz"))
+    for i in range(INDEX["act_sb.npz"]["inputs"]):
+        q, s, sums = helpers.oracle_quant_sb(g[f"x{i}"])
+        assert np.array_equal(q, g[f"q{i}"]), i
+        assert np.array_equal(s.view(np.uint32), g[f"s{i}"].view(np.uint32)), i
+        assert np.array_equal(sums, g[f"sums{i}"]), i
+
+
+@pytest.mark.skipif(not helpers.have_ref(), reason="reference CPU build (oracle/_ref) not present")
+def test_oracle_batch_equals_reference_forward_multi():
+    """The restatement's multi-sequence step in the decode arithmetic (mode 0)
+    against the reference's sml_forward_multi with SML_MULTI=exact (each
+    conversation through the decode kernels, sml/sml-run.c:2579-2597):
+    ragged starts, idle slots, five conversations -- logits bit for bit."""
+    path = helpers.model_path(INDEX["decode_tiny.npz"]["spec"])
+    ns, nsteps, starts = 5, 9, [0, 1, 2, 0, 4]
+    toks = np.random.default_rng(3).integers(0, 1024, (nsteps, ns)).astype(np.int32)
+    steps = [(toks[t].tolist(), [t - s if t >= s else -1 for s in starts]) for t in range(nsteps)]
+    ref = helpers.ref("multi", path, ns=ns, n_vocab=1024, steps=steps, n_ctx=32, env={"SML_MULTI": "exact"})
+    orc = helpers.Oracle(path, n_ctx=32)
+    ob0 = helpers.OracleBatch(orc, ns, 0)
+    try:
+        for t, (tok, pos) in enumerate(steps):
+            lg = ob0.step(np.array(tok, np.int32), np.array(pos, np.int32))
+            for s in range(ns):
+                if pos[s] >= 0:
+                    assert np.array_equal(lg[s].view(np.uint32), ref[t][s].view(np.uint32)), (t, s)
+    finally:
+        ob0.close()
+        orc.close()
