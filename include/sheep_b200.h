@@ -93,6 +93,12 @@ int sb_tset_requant8_host(sb_tset * t, const char * name, int8_t * w8, float * s
 // (sml/sml-check.c:194-245).
 int sb_tset_matvec(sb_tset * t, const char * name, const float * x, float * y, int8_t * q, float * s,
                    int32_t * sums);
+// sb_tset_matvec with xp already in the tensor's column order (xp[i] =
+// x[perm[i]]): the staging of the decode chain's down projection, whose input
+// the gate/up epilogue writes in that order. The exported int8 activation is
+// the per-32 quantization of xp.
+int sb_tset_matvec_permuted(sb_tset * t, const char * name, const float * xp, float * y, int8_t * q, float * s,
+                            int32_t * sums);
 // Rows dequantized on the GPU, permuted column order (sml_dequant_row_flat*,
 // sml/sml-kernel.c:2134-2260; the embedding path sml_g_embed,
 // sml/sml-gpu-fast.cu:461). Host buffers.
@@ -123,10 +129,12 @@ const char * sb_attn_last_error(void);
 // static device array of 1 MiB (+ 256 counters) that every GPU loading the
 // library holds until exit, and nothing is allocated. Rejects, with an error,
 // calls needing more (n_head x chunks x (head_dim + 2) floats > 1 MiB, or > 256
-// heads). All calls share the array: calls that overlap on the GPU race. The
-// first call on a device finds the array's address and clears the counters
-// (synchronizing once), so make it before any stream capture. Asynchronous on
-// `stream`. No counterpart in the reference: an addition of this library.
+// heads). All calls on one device share that device's array: calls that
+// overlap on the GPU race. The first call on a device finds the array's address
+// and clears the counters (synchronizing once), so make it before any stream
+// capture, and do not reset the device afterwards. Asynchronous on `stream`.
+// The error text is per calling thread. No counterpart in the reference: an
+// addition of this library.
 int sb_attn_decode_noalloc(const float * qkv, uint16_t * kc, uint16_t * vc, const float * rope_cos,
                            const float * rope_sin, const float * q_norm, const float * k_norm, float eps, int n_head,
                            int n_head_kv, int head_dim, int n_ctx, int pos, float scale, float * out, void * stream);

@@ -75,6 +75,7 @@ def lib():
         "sb_tset_time_gemm_tc": (ip, [vp, cp, vp, ip, ip, ip, fp]),
         "sb_tset_requant8_host": (ip, [vp, cp, vp, vp]),
         "sb_tset_matvec": (ip, [vp, cp, vp, vp, vp, vp, vp]),
+        "sb_tset_matvec_permuted": (ip, [vp, cp, vp, vp, vp, vp, vp]),
         "sb_tset_dequant_rows": (ip, [vp, cp, vp, ip, vp]),
         "sb_quantize_act": (ip, [vp, vp, ip, vp, vp, vp, vp]),
         "ssfgen_write": (ip, [cp, vp, cp, ip]),
@@ -222,7 +223,9 @@ class TensorSet:
     def nbytes(self, name):
         return int(lib().sb_tset_bytes(self.h, name.encode()))
 
-    def matvec(self, name, x):
+    def matvec(self, name, x, permuted=False):
+        """y = W x and the int8 activation the kernel staged; permuted=True takes
+        x already in the tensor's column order (the down projection's staging)."""
         rows, cols, _ = self.shape(name)
         x = np.ascontiguousarray(x, dtype=np.float32)
         assert x.shape == (cols,)
@@ -230,7 +233,8 @@ class TensorSet:
         q = np.zeros(cols, np.int8)
         s = np.zeros(cols // 32, np.float32)
         sums = np.zeros(cols // 32, np.int32)
-        if not lib().sb_tset_matvec(self.h, name.encode(), _p(x), _p(y), _p(q), _p(s), _p(sums)):
+        fn = lib().sb_tset_matvec_permuted if permuted else lib().sb_tset_matvec
+        if not fn(self.h, name.encode(), _p(x), _p(y), _p(q), _p(s), _p(sums)):
             raise RuntimeError(f"sb_tset_matvec failed: {lib().sb_last_error().decode()}")
         return y, q, s, sums
 

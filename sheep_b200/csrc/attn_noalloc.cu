@@ -15,12 +15,18 @@
 // on the GPU (other streams, other threads) race and give wrong results: issue
 // them one after another on one stream.
 //
+// "Shared" means per device: each GPU has its own copy of the array, so calls
+// on different devices do not race on it.
+//
 // In host code the array's name is not a device address; the address comes from
 // cudaGetSymbolAddress once per device, with that device current. The first call
 // on a device does that set-up and clears the counters (a cudaMemset, which
 // synchronizes), so make the first call before any stream capture. The kernel
 // leaves the counters at zero when it finishes, and the partials are written
-// before they are read, so later calls need no clearing.
+// before they are read, so later calls need no clearing. The address and the
+// cleared counters are kept for the life of the process: do not reset the
+// device (cudaDeviceReset) after the first call -- a new context would hold a
+// new copy of the array that this file has neither looked up nor cleared.
 #include "decode.cuh"
 #include "sheep_b200.h"
 
@@ -40,7 +46,7 @@ static __device__ __align__(256) unsigned char g_attn_scratch[kScratchBytes];
 
 std::mutex g_setup;
 void * g_addr[kMaxDevices];
-char g_err[256];
+thread_local char g_err[256];   // per calling thread, as sb_attn_last_error
 
 // The array's device address on the current device (set up on first use).
 bool scratch_address(void ** out) {

@@ -267,8 +267,23 @@ extern "C" int sb_tset_time_gemv(sb_tset * t, const char * name, const float * x
 
 // Host-buffer form for tests: y = W x, plus the int8 activation the kernel
 // quantized (natural group order) when q/s/sums are not NULL.
+static int matvec_host(sb_tset * t, const char * name, const float * x, int permuted, float * y, int8_t * qx,
+                       float * qs, int32_t * qsum);
+
 extern "C" int sb_tset_matvec(sb_tset * t, const char * name, const float * x, float * y, int8_t * qx, float * qs,
                               int32_t * qsum) {
+    return matvec_host(t, name, x, 0, y, qx, qs, qsum);
+}
+
+// The same with x already in the tensor's column order (the staging the
+// decode chain's down projection uses: no gather, one lane per group).
+extern "C" int sb_tset_matvec_permuted(sb_tset * t, const char * name, const float * xp, float * y, int8_t * qx,
+                                       float * qs, int32_t * qsum) {
+    return matvec_host(t, name, xp, 1, y, qx, qs, qsum);
+}
+
+static int matvec_host(sb_tset * t, const char * name, const float * x, int permuted, float * y, int8_t * qx,
+                       float * qs, int32_t * qsum) {
     const TT * q = find_tt(t, name);
     if (!q) return 0;
     const int n = q->cols, ng = n / SSF_GROUP;
@@ -282,6 +297,7 @@ extern "C" int sb_tset_matvec(sb_tset * t, const char * name, const float * x, f
         cudaMemcpy(dx, x, (size_t) n * 4, cudaMemcpyHostToDevice);
         TGArgs g = plain_args(t, *q, dx, dy);
         g.act_q = dq; g.act_s = ds; g.act_sum = dsum;
+        g.in_permuted = permuted;
         ok = run_plain(t, g, (cudaStream_t) 0);
         int err = 0;
         ok = cudaDeviceSynchronize() == cudaSuccess && ok;
