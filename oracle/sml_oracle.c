@@ -687,6 +687,16 @@ static int moe_ffn(so_model * m, int L, const float * xb, float * out, int * sel
     return k;
 }
 
+void so_moe_combine(int T, int k, int E, const float * w, const float * yk, float * y) {
+    for (int t = 0; t < T; t++) {
+        float * yt = y + (size_t) t * E;
+        for (int i = 0; i < E; i++) yt[i] = 0.0f;
+        for (int j = 0; j < k; j++)
+            for (int i = 0; i < E; i++)
+                yt[i] = fmaf(w[(size_t) t * k + j], yk[((size_t) t * k + j) * E + i], yt[i]);
+    }
+}
+
 // One expert's FFN of layer L on one normalized row: down(silu(gate x) * up x)
 // (the body of the choice loop of moe_ffn, sml/sml-run.c:3098-3121, before its
 // weighting). 0 if the expert does not exist.

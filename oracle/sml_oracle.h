@@ -40,6 +40,10 @@ int so_moe_route(const float * lg, int ne, int k, unsigned moe_flags, int * sel,
 // the chosen experts and weights (either may be NULL); returns k, 0 if layer L
 // has no router.
 int so_moe_ffn(so_model * m, int L, const float * xb, float * out, int * sel, float * w);
+// The combine of moe_ffn (sml/sml-run.c:3120): for each of T rows, the k
+// per-choice expert outputs yk [T][k][E] weighted by w [T][k] and summed in
+// choice order into y [T][E] from 0, y = fma(w, yk, y).
+void so_moe_combine(int T, int k, int E, const float * w, const float * yk, float * y);
 // One expert's FFN output (unweighted) of layer L on a normalized row.
 int so_moe_expert(so_model * m, int L, int e, const float * xb, float * out);
 // The batched path: the int8 re-quantization of a tensor (w8: rows x nsb*256,

@@ -74,9 +74,11 @@ def _ep_worker(rank, world, port, out):
     tk = torch.from_numpy(yk)
     d.all_reduce(tk)
     yk = tk.numpy()
+    # the combine in choice order, as the layer computes it (fused multiply-adds)
     y = np.zeros_like(y_full)
-    for j in range(sel.shape[1]):   # choice order, float32, no fused multiply-add
-        y = (y + (w[:, j:j + 1] * yk[:, j]).astype(np.float32)).astype(np.float32)
+    wk = np.ascontiguousarray(w, np.float32)
+    yk = np.ascontiguousarray(yk, np.float32)
+    orc.lib().so_moe_combine(len(x), sel.shape[1], orc.info[1], helpers._p(wk), helpers._p(yk), helpers._p(y))
     out[rank] = (bool(np.array_equal(y.view(np.uint32), y_full.view(np.uint32))), (lo, hi))
     orc.close()
     d.barrier()
