@@ -67,8 +67,10 @@ def profiled_traffic(name):
         return None
 
 
-def model_path(spec, rank, dist):
-    import sheep_b200
+def model_path(spec, rank, dist, own_process=False):
+    """The synthetic SSF of `spec` (written once, cached by content). With
+    own_process the writer runs in a separate Python process, so the caller
+    (the reference arm) never maps this repository's engine library."""
     d = os.path.join(tempfile.gettempdir(), "sheep_b200_bench")
     os.makedirs(d, exist_ok=True)
     import hashlib
@@ -76,11 +78,23 @@ def model_path(spec, rank, dist):
     path = os.path.join(d, key + ".ssf")
     if rank == 0 and not os.path.exists(path):
         tmp = path + f".tmp{os.getpid()}"
-        sheep_b200.write_model(tmp, **spec)
+        if own_process:
+            code = ("import json, sys; sys.path.insert(0, %r); import sheep_b200; "
+                    "sheep_b200.write_model(%r, **json.loads(%r))" % (ROOT, tmp, json.dumps(spec)))
+            subprocess.run([sys.executable, "-c", code], check=True)
+        else:
+            import sheep_b200
+            sheep_b200.write_model(tmp, **spec)
         os.replace(tmp, path)
     if dist is not None:
         dist.barrier()
     return path
+
+
+def bench_config(W, K):
+    """The workload, identical in both arms."""
+    return {"workload": WORKLOAD, "quant": "SSF v8 flat Q4", "batch": 1, "prompt": PROMPT_LEN,
+            "seq_len": PROMPT_LEN + W + K}
 
 
 class Clocks:
@@ -133,7 +147,8 @@ class Clocks:
 
 def cpu_decode(path, n_prompt, nwarm, ngen, threads):
     """Reference CPU decode (oracle/_ref): prompt stepped, then greedy tokens;
-    returns (tok/s over the timed ngen tokens, seconds). Runs in the caller's process."""
+    returns (tok/s over the timed ngen tokens, seconds, the greedy ids after the
+    prompt). Runs in the caller's process."""
     L = ctypes.CDLL(REF_LIB)
     L.refh_open.restype = ctypes.c_void_p
     L.refh_open.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.c_int]
@@ -148,17 +163,20 @@ def cpu_decode(path, n_prompt, nwarm, ngen, threads):
     tok = 0
     for i, t in enumerate(prompt):
         tok = L.refh_forward(h, int(t), i, lp)
+    ids = [int(tok)]
     pos = n_prompt
     for _ in range(nwarm):
         tok = L.refh_forward(h, int(tok), pos, lp)
+        ids.append(int(tok))
         pos += 1
     t0 = time.perf_counter()
     for _ in range(ngen):
         tok = L.refh_forward(h, int(tok), pos, lp)
+        ids.append(int(tok))
         pos += 1
     dt = time.perf_counter() - t0
     L.refh_close(h)
-    return ngen / dt, dt
+    return ngen / dt, dt, ids
 
 
 def _cpu_child(args):
@@ -202,20 +220,22 @@ def main():
             print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libsmlref.so was not built "
                               "(the reference tree was absent at build time)"}))
             return
-        path = model_path(spec, 0, None)
+        path = model_path(spec, 0, None, own_process=True)
         cores = host_cores()
-        tps, dt = cpu_decode_isolated(path, PROMPT_LEN, W, K, cores)
-        sample = f"{PROMPT_LEN}-token prompt stepped, {W} warm-up tokens, {K} timed greedy tokens"
+        # at least 32 greedy ids (warm-up + timed) for the ids line
+        wr = max(W, 32 - K)
+        tps, dt, ids = cpu_decode_isolated(path, PROMPT_LEN, wr, K, cores)
+        sample = f"{PROMPT_LEN}-token prompt stepped, {wr} warm-up tokens, {K} timed greedy tokens"
         print(json.dumps({
             "metric": METRIC, "value": tps, "unit": "tok/s", "n_gpus": a.gpus, "steps": K, "warmup": W,
             "ms_per_step": 1000.0 / tps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "s8xu4->s32, f32 epilogue", "data": "synthetic (seeded N(0,0.02) weights, RTN Q4)",
             "impl": "reference",
-            "config": {"workload": WORKLOAD, "model": "qwen2.5-1.5b-shape", "quant": "SSF v8 flat Q4",
-                       "global_batch": 1, "seq_len": PROMPT_LEN + W + K},
+            "config": bench_config(W, K),
             "cpu_baseline": {"value": tps, "unit": "tok/s", "cores": cores, "kind": "reference",
                              "sample": sample},
             "e2e": {"value": tps, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "greedy_ids_32": ids[:32],
         }))
         return
 
@@ -225,7 +245,7 @@ def main():
         torch.cuda.set_device(0)
     import sheep_b200
     path = model_path(spec, rank, dist)
-    n_ctx = PROMPT_LEN + W + K + 8
+    n_ctx = max(PROMPT_LEN + W + K + 8, PROMPT_LEN + 40)
     eng = sheep_b200.Engine(path, n_ctx=n_ctx)
     prompt = np.random.default_rng(1234).integers(0, eng.n_vocab, PROMPT_LEN).astype(np.int32)
 
@@ -239,7 +259,7 @@ def main():
         return sdist.max_over_ranks(dist, v)
 
     # ---- device-resident decode: K tokens after the prompt and W warm-up tokens
-    eng.generate(prompt, 4)   # first replay of the graph, outside the timed region
+    ids32 = eng.generate(prompt, 32)   # the first 32 greedy ids; first replays, outside the timed region
     barrier()
     with Clocks(local) as clk:
         ids, ms = eng.generate(prompt, K + 1, timed=True, warmup=W)   # K + 1 ids = K timed replays
@@ -277,9 +297,9 @@ def main():
     if rank == 0 and world == 1 and os.path.exists(REF_LIB):
         cores = host_cores()
         n_cpu = 24
-        tps, _ = cpu_decode_isolated(path, 16, 2, n_cpu, cores)
+        tps, _, _ = cpu_decode_isolated(path, PROMPT_LEN, 2, n_cpu, cores)
         cpu = {"value": tps, "unit": "tok/s", "cores": cores, "kind": "reference",
-               "sample": f"same model, 16-token prompt stepped, 2 warm-up then {n_cpu} timed greedy tokens"}
+               "sample": f"same model and prompt ({PROMPT_LEN} ids stepped), 2 warm-up then {n_cpu} timed greedy tokens"}
 
     extras = None
     if world > 1:
@@ -304,9 +324,9 @@ def main():
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
             "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "s8xu4->s32, f32 epilogue", "data": "synthetic (seeded N(0,0.02) weights, RTN Q4)",
-            "config": {"workload": WORKLOAD, "model": "qwen2.5-1.5b-shape", "quant": "SSF v8 flat Q4",
-                       "global_batch": world, "seq_len": PROMPT_LEN + W + K, "parallelism": f"replicas{world}",
-                       "l2": "weights 0.89 GB/token > 126 MB L2: no flush"},
+            "config": bench_config(W, K),
+            "parallelism": f"replicas{world}: one decode per GPU, value summed over GPUs",
+            "l2": "weights 0.89 GB/token > 126 MB L2: no flush",
             "roofline": {"kernel": "k_tgemv<FFN> (fused gate/up dequant-GEMV + SiLU), launched alone",
                          "bound": "hbm", "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
                          "unit": "GB/s", "frac": achieved / peak,
@@ -320,7 +340,7 @@ def main():
             "gpu_launches": launches * K,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
-            "greedy_ids_head": [int(i) for i in ids[W:W + 8]],
+            "greedy_ids_32": [int(i) for i in ids32[:32]],
             "extras": extras,
         }
         print(json.dumps(out))

@@ -9,8 +9,9 @@
 //               + md[r,g/8]*(mq[r,g] - bias) * xs[g] * sum(xq[g,:])
 //
 // with xq, xs, sums the per-32 int8 activation of sml_quantize_act
-// (sml/sml-kernel.c:89-109). The integer dots are exact (dp4a); only the
-// float epilogue's summation order differs from the CPU.
+// (sml/sml-kernel.c:89-109). The integer dots are exact (dp4a); the float
+// epilogue's order is the reference's in the decode GEMV (tgemv.cuh) and per
+// unit in the batched GEMV (moe.cuh).
 //
 // Work unit: one lane takes 64 weights of a row -- groups 4p..4p+3, columns
 // c0..c0+15 (c0 = 0 or 16) -- which is 2 x 16 bytes of the nibble plane,
@@ -67,27 +68,6 @@ struct ActS {
 
 SB_DEV int act_slot_off(int n, int g, int j) {
     return (g & 3) * (n >> 2) + 16 * (2 * (g >> 2) + (j >> 4)) + (j & 15);
-}
-
-// Quantize one group of 32 values (one value per lane) exactly as
-// sml_quantize_act does: amax, s = amax/127, is = 1/s (0 if s = 0),
-// q = clamp(rint(v*is), +-127). IEEE division and round-to-nearest-even.
-SB_DEV void quant_group_warp(float v, int g, int lane, ActS & a, int8_t * qglob, float * sglob, int32_t * sumglob) {
-    const float amax = warp_max(fabsf(v));
-    const float s = __fdiv_rn(amax, 127.0f);
-    const float is = s > 0.0f ? __fdiv_rn(1.0f, s) : 0.0f;
-    int q = __float2int_rn(__fmul_rn(v, is));
-    q = q > 127 ? 127 : q < -127 ? -127 : q;
-    const int sum = warp_sum_i(q);
-    a.q[act_slot_off(a.n, g, lane)] = (int8_t) q;
-    if (lane == 0) {
-        a.xs[g] = s;
-        a.xsum[g] = s * (float) sum;
-    }
-    if (qglob) {
-        qglob[g * kGroup + lane] = (int8_t) q;
-        if (lane == 0) { sglob[g] = s; sumglob[g] = sum; }
-    }
 }
 
 // Widths and field sizes as one switch, so every kernel instantiates all 14.

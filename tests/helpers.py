@@ -28,7 +28,9 @@ MODEL_DIR = os.path.join(tempfile.gettempdir(), "sheep_b200_models")
 
 def build_oracle():
     subprocess.run(["make", "-s", "-C", ORACLE_DIR, "oracle"], check=True)
-    subprocess.run(["make", "-s", "-C", ORACLE_DIR, "ref"], check=True)
+    ref = os.environ.get("SML_REFERENCE")
+    if ref:
+        subprocess.run(["make", "-s", "-C", ORACLE_DIR, "ref", "REF=" + ref], check=True)
 
 
 def have_ref():
