@@ -19,6 +19,20 @@ typedef struct sb_engine sb_engine;
 
 sb_engine * sb_open(const char * path, int n_ctx, char * why, int nwhy);
 void        sb_close(sb_engine * e);
+
+// Tensor-parallel decode over tp GPUs of one node, one process per GPU (the
+// reference is single-device, cuDeviceGet(&dev, 0) at sml/sml-gpu-fwd.c:1877;
+// this is the row-split GEMV with an exchange north of it): attention, q|k|v
+// and o replicated on every rank; gate/up, down and the head split by rows;
+// each GEMV stores its rows into every rank's copy of the vector over NVLink
+// and raises a flag the consuming kernel waits on. Results equal one GPU's bit
+// for bit. Open on every rank (the current device is the rank's GPU), pass
+// each rank's handle to every rank (rank order), then connect; every rank must
+// then make the same calls in the same order (steps, prefill, generation).
+#define SB_TP_HANDLE_BYTES 64
+sb_engine * sb_open_tp(const char * path, int n_ctx, int tp, int rank, char * why, int nwhy);
+int         sb_tp_handle(const sb_engine * e, void * out);   // SB_TP_HANDLE_BYTES of this rank's exchange region
+int         sb_tp_connect(sb_engine * e, const void * handles, char * why, int nwhy);
 // out[0..12]: n_layer, n_embd, n_head, n_head_kv, head_dim, n_ff, n_vocab,
 // n_ctx, n_expert, n_expert_used, weight bytes per token (low, high 32 bits),
 // 0 (reserved)

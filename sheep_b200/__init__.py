@@ -51,6 +51,9 @@ def lib():
         "sml_gpu_engine": (vp, []),
         "sml_gpu_close": (None, []),
         "sb_open": (vp, [cp, ip, cp, ip]),
+        "sb_open_tp": (vp, [cp, ip, ip, ip, cp, ip]),
+        "sb_tp_handle": (ip, [vp, vp]),
+        "sb_tp_connect": (ip, [vp, vp, cp, ip]),
         "sb_close": (None, [vp]),
         "sb_info": (None, [vp, vp]),
         "sb_bytes_per_token": (ctypes.c_uint64, [vp]),
@@ -141,11 +144,28 @@ def ssf_check(path):
 class Engine:
     """A model on the GPU with its KV cache (the handle form of sml-gpu.h)."""
 
-    def __init__(self, path, n_ctx=256):
+    def __init__(self, path, n_ctx=256, tp=None):
+        """tp=(world, rank, dist): this rank of a tensor-parallel engine over
+        `world` GPUs (dist: an initialised torch.distributed, used once to pass
+        the ranks' exchange handles around); every rank must construct it."""
         why = ctypes.create_string_buffer(512)
-        self.h = lib().sb_open(path.encode(), n_ctx, why, 512)
+        if tp is None or tp[0] == 1:
+            self.h = lib().sb_open(path.encode(), n_ctx, why, 512)
+        else:
+            world, rank, dist = tp
+            self.h = lib().sb_open_tp(path.encode(), n_ctx, world, rank, why, 512)
         if not self.h:
             raise RuntimeError(f"sb_open: {why.value.decode()}")
+        if tp is not None and tp[0] > 1:
+            world, rank, dist = tp
+            hb = ctypes.create_string_buffer(64)
+            if not lib().sb_tp_handle(self.h, hb):
+                raise RuntimeError(f"sb_tp_handle: {lib().sb_last_error().decode()}")
+            allh = [None] * world
+            dist.all_gather_object(allh, bytes(hb.raw))
+            joined = ctypes.create_string_buffer(b"".join(allh), 64 * world)
+            if not lib().sb_tp_connect(self.h, joined, why, 512):
+                raise RuntimeError(f"sb_tp_connect: {why.value.decode()}")
         info = (ctypes.c_int * 16)()
         lib().sb_info(self.h, info)
         (self.n_layer, self.n_embd, self.n_head, self.n_head_kv, self.head_dim, self.n_ff,

@@ -120,10 +120,11 @@ SB_DEV float dequant_at(const QT & t, int row, int i) {
 // natural order (sml/sml-run.c:3332-3336). tok is read from device memory so a
 // captured graph replays the greedy loop without the host.
 template <int NB, int SIX>
-__global__ void k_embed(const __grid_constant__ QT t, const int * dtok, float * x, int * err) {
+__global__ void k_embed(const __grid_constant__ QT t, const int * dtok, float * x, int * err, unsigned * seq) {
     pdl_launch_dependents();
     pdl_wait();
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (seq && i == 0) *seq += 1u;   // tokens run (a tensor-parallel engine's exchange events count by it)
     if (i >= t.cols) return;
     const int tok = *dtok;
     if (!SB_CHECK(err, tok >= 0 && tok < t.rows, 301)) return;
@@ -449,6 +450,11 @@ __global__ void __launch_bounds__(kSeqThreads) k_attn_seq(const __grid_constant_
     SB_MARK(g.trace, g.launch_id, 4);
 }
 
+// Greedy choice over the whole logit vector of a tensor-parallel engine, once
+// every rank's rows have arrived: the first largest logit (ties to the lower
+// index, sml/sml-run.c:3539-3544) becomes the next token; the position
+// advances and the choice is logged.
+constexpr int kArgmaxThreads = 1024;
 // Shared memory of k_attn for head width hd and `chunk` positions.
 __host__ __device__ inline size_t attn_smem_bytes(int hd, int chunk) {
     return (size_t) (4 * hd + chunk) * 4 + (size_t) chunk * (hd + 4) * 2 + (size_t) chunk * hd * 2;

@@ -39,9 +39,30 @@ struct LayerD {
     const float * an = nullptr, * fn = nullptr;
     const float * qkv_b = nullptr;    // q|k|v biases, or NULL
     const float * qn = nullptr, * kn = nullptr;
-    const int32_t * down_iperm = nullptr;
+    const int32_t * down_iperm = nullptr;   // gate/up value i -> its place in down's column order
     bool moe = false;                 // mixture-of-experts FFN in place of gate/up/down
     MoeLayer ml;
+};
+
+// Tensor parallelism (tp > 1 ranks, one process per GPU): attention, q|k|v and
+// o are replicated; gate/up, down and the head are split by rows. Rank r
+// computes the hidden values of down's column positions [F r/tp, F (r+1)/tp)
+// (whole groups of 32), down's rows [E r/tp, ..) and the head's rows
+// [V r/tp, ..); each GEMV stores its rows into every rank's copy of the vector
+// (peer pointers into each rank's exchange region, CUDA IPC) and its last CTA
+// raises the event in every rank's flag array; the kernel that reads the whole
+// vector waits for every peer's event first. Each row is still computed whole
+// by one rank, in the same arithmetic, so the ranks' results equal one GPU's
+// bit for bit. Events per token: hidden(l) = 2l, x(l) = 2l+1 after layer l's
+// down, logits = 2 n_layer.
+struct TpState {
+    int n = 1, rank = 0;
+    uint8_t * reg = nullptr;          // this rank's exchange region (cudaMalloc: IPC-exported)
+    size_t reg_bytes = 0;
+    void * peer[kMaxTp] = {};         // every rank's region as mapped here (this rank's = reg)
+    size_t off_x = 0, off_hp = 0, off_lg = 0;   // vectors in the region (flags at 0)
+    unsigned * arrive = nullptr;      // per raising kernel kind: FFN, down, head
+    unsigned * tok_seq = nullptr;
 };
 
 struct sb_engine {
@@ -78,6 +99,7 @@ struct sb_engine {
     float * h_logits = nullptr;
     int * h_io = nullptr;
     uint64_t bytes_tok = 0;
+    TpState tp;
 };
 
 // ------------------------------------------------------------------ arena
@@ -124,7 +146,8 @@ static cudaError_t launch(sb_engine * e, bool pdl, void (*k)(KArgs...), dim3 gri
 
 template <int NB, int SIX>
 static void launch_embed(sb_engine * e, const QT & t) {
-    launch(e, true, k_embed<NB, SIX>, dim3((t.cols + 255) / 256), dim3(256), 0, t, (const int *) e->tok, e->x, e->err);
+    launch(e, true, k_embed<NB, SIX>, dim3((t.cols + 255) / 256), dim3(256), 0, t, (const int *) e->tok, e->x, e->err,
+           e->tp.tok_seq);
 }
 
 template <int MODE, int NB, int SIX>
@@ -173,6 +196,29 @@ static void set_next(TGArgs & g, const TT * nt, int nsm) {
     g.next_tb = nt->tb;
 }
 
+// The exchange of one GEMV launch: `out` is this launch's output pointer in
+// this rank's region (its rows go to the same offset in every peer's).
+static void set_tp(sb_engine * e, TGArgs & g, int kind, int ev_raise, int ev_wait, float * out) {
+    TpState & t = e->tp;
+    if (t.n <= 1) return;
+    TpX & x = g.tp;
+    x.n = t.n; x.rank = t.rank;
+    for (int p = 0; p < t.n; p++) {
+        x.peer_out[p] = nullptr;
+        x.peer_flag[p] = nullptr;
+        if (p == t.rank) continue;
+        if (out) x.peer_out[p] = (float *) ((uint8_t *) t.peer[p] + ((uint8_t *) out - t.reg));
+        if (ev_raise >= 0) x.peer_flag[p] = (unsigned *) t.peer[p] + t.rank;
+    }
+    x.arrive = t.arrive + kind;
+    x.flags = (const unsigned *) t.reg;
+    x.tok_seq = t.tok_seq;
+    x.ev_per_tok = 2u * e->n_layer + 1u;
+    x.ev_raise = ev_raise;
+    x.ev_wait = ev_wait;
+    x.err = e->err;
+}
+
 static void launch_tg(sb_engine * e, int mode, const TGArgs & g0) {
     const int grid = g0.t.ntiles < e->nsm ? g0.t.ntiles : e->nsm;
     TGArgs g = g0;
@@ -214,6 +260,7 @@ static void enqueue_token(sb_engine * e) {
             TGArgs g = tg_args(e, y.qkv, e->x, y.an, e->qkv);
             g.bias = y.qkv_b;
             set_next(g, &y.o, e->nsm);
+            set_tp(e, g, 0, -1, l > 0 ? 2 * (l - 1) + 1 : -1, nullptr);   // x of the previous layer
             launch_tg(e, GM_QKV, g);
         }
         snprintf(e->cur, sizeof e->cur, "L%d.attn", l);
@@ -234,25 +281,43 @@ static void enqueue_token(sb_engine * e) {
         snprintf(e->cur, sizeof e->cur, "L%d.ffn", l);
         {
             TGArgs g = tg_args(e, y.gateup, e->x, y.fn, e->hp);
-            g.ffn_f = e->F;
+            g.ffn_f = y.gateup.rows / 2;
+            g.ffn_n = e->F;
             g.scatter = y.down_iperm;
             set_next(g, &y.down, e->nsm);
+            set_tp(e, g, 0, 2 * l, -1, e->hp);
             launch_tg(e, GM_FFN, g);
         }
         snprintf(e->cur, sizeof e->cur, "L%d.down", l);
         {
-            TGArgs g = tg_args(e, y.down, e->hp, nullptr, e->x);
+            // a tensor-parallel rank's rows are x's rows [E r/tp, ..)
+            float * xo = e->x + (size_t) e->E * e->tp.rank / e->tp.n;
+            TGArgs g = tg_args(e, y.down, e->hp, nullptr, xo);
             g.in_permuted = 1;
             set_next(g, l + 1 < e->n_layer ? &e->L[l + 1].qkv : nullptr, e->nsm);
+            set_tp(e, g, 1, 2 * l + 1, 2 * l, xo);
             launch_tg(e, GM_DOWN, g);
         }
     }
     snprintf(e->cur, sizeof e->cur, "head");
-    TGArgs g = tg_args(e, e->head, e->x, e->out_norm, e->logits);
+    float * lo = e->logits + (size_t) e->V * e->tp.rank / e->tp.n;
+    TGArgs g = tg_args(e, e->head, e->x, e->out_norm, lo);
     g.prefetch = 0;   // larger than L2: streamed, not staged
-    g.am_val = e->am_val; g.am_idx = e->am_idx; g.am_cnt = e->am_cnt;
-    g.tok = e->tok; g.pos = e->pos; g.tlog = e->tlog;
+    if (e->tp.n <= 1) {
+        g.am_val = e->am_val; g.am_idx = e->am_idx; g.am_cnt = e->am_cnt;
+        g.tok = e->tok; g.pos = e->pos; g.tlog = e->tlog;
+    }
+    set_tp(e, g, 2, 2 * e->n_layer, 2 * (e->n_layer - 1) + 1, lo);
     launch_tg(e, GM_HEAD, g);
+    if (e->tp.n > 1) {
+        // the greedy choice over every rank's logits
+        snprintf(e->cur, sizeof e->cur, "argmax");
+        TGArgs w;
+        memset(&w, 0, sizeof w);
+        set_tp(e, w, 2, -1, 2 * e->n_layer, nullptr);
+        launch(e, true, k_tp_argmax, dim3(1), dim3(kArgmaxThreads), 0, (const float *) e->logits, e->V, w.tp,
+               e->tok, e->pos, e->tlog);
+    }
 }
 
 // ------------------------------------------------------------------ open
@@ -260,6 +325,9 @@ static void enqueue_token(sb_engine * e) {
 static void close_all(sb_engine * e) {
     if (e->g_tok) cudaGraphExecDestroy(e->g_tok);
     if (e->st) cudaStreamDestroy(e->st);
+    for (int p = 0; p < e->tp.n; p++)
+        if (p != e->tp.rank && e->tp.peer[p]) cudaIpcCloseMemHandle(e->tp.peer[p]);
+    if (e->tp.reg) cudaFree(e->tp.reg);
     e->ar.release();
     if (e->h_logits) cudaFreeHost(e->h_logits);
     if (e->h_io) cudaFreeHost(e->h_io);
@@ -282,9 +350,15 @@ static bool build(sb_engine * e, char * why, int nwhy) {
         return pick_tr(rows, (int) tile_geom((int) r->cols, 1, (int) r->nbits, e->six, r->mq_n != 0).bytes, min_tiles,
                        even, kTileCap);
     };
-    if (!upload_tt(e->ar, f, hr, (int) hr->rows, tr_for(hr, (int) hr->rows, 0), min_tiles, 0,
-                   [&](int v) { return RowSrc{v < (int) hr->rows ? hr : nullptr, v}; }, e->head, why, nwhy))
-        return false;
+    const int tp = e->tp.n, rk = e->tp.rank;
+    if ((int) hr->rows % tp || e->E % tp) { snprintf(why, nwhy, "vocab or width not divisible by %d ranks", tp); return false; }
+    {
+        // this rank's head rows [V r/tp, V (r+1)/tp)
+        const int hn = (int) hr->rows / tp, h0 = hn * rk;
+        if (!upload_tt(e->ar, f, hr, hn, tr_for(hr, hn, 0), min_tiles, 0,
+                       [&](int v) { return RowSrc{v < hn ? hr : nullptr, h0 + v}; }, e->head, why, nwhy))
+            return false;
+    }
     e->bytes_tok += tt_bytes(e->head);
     e->out_norm = up_f32(e, ssf_find(&f, "output_norm.weight"));
     e->L.assign(e->n_layer, LayerD());
@@ -313,6 +387,7 @@ static bool build(sb_engine * e, char * why, int nwhy) {
                      : r < e->qd + 2 * e->kvd ? RowSrc{v, r - e->qd - e->kvd} : RowSrc{nullptr, 0}; },
                        y.qkv, why, nwhy))
             return false;
+        if (y.moe && tp > 1) { snprintf(why, nwhy, "layer %d: tensor parallelism over MoE layers is not built", l); return false; }
         if (y.moe) {
             if (!moe_upload(e->ar, f, l, y.ml, why, nwhy)) return false;
             if (moe0 && (y.ml.E != moe0->E || y.ml.F != moe0->F || y.ml.ne != moe0->ne || y.ml.k != moe0->k)) {
@@ -326,15 +401,35 @@ static bool build(sb_engine * e, char * why, int nwhy) {
                        y.o, why, nwhy))
             return false;
         if (!y.moe) {
-            const int gtr = tr_for(gt, 2 * F, 1);
-            if (!upload_tt(e->ar, f, gt, 2 * F, gtr, min_tiles, 1, [&](int r) {
-                    const int h = gtr / 2, ti = r / gtr, j = r % gtr, i = ti * h + j % h;
-                    return i >= F ? RowSrc{nullptr, 0} : RowSrc{j < h ? gt : up, i}; },
-                           y.gateup, why, nwhy) ||
-                !upload_tt(e->ar, f, dn, e->E, tr_for(dn, e->E, 0), min_tiles, 0, [&](int r) { return RowSrc{r < e->E ? dn : nullptr, r}; },
-                           y.down, why, nwhy))
-                return false;
-            y.down_iperm = y.down.iperm;
+            if (tp == 1) {
+                const int gtr = tr_for(gt, 2 * F, 1);
+                if (!upload_tt(e->ar, f, gt, 2 * F, gtr, min_tiles, 1, [&](int r) {
+                        const int h = gtr / 2, ti = r / gtr, j = r % gtr, i = ti * h + j % h;
+                        return i >= F ? RowSrc{nullptr, 0} : RowSrc{j < h ? gt : up, i}; },
+                               y.gateup, why, nwhy) ||
+                    !upload_tt(e->ar, f, dn, e->E, tr_for(dn, e->E, 0), min_tiles, 0,
+                               [&](int r) { return RowSrc{r < e->E ? dn : nullptr, r}; }, y.down, why, nwhy))
+                    return false;
+                y.down_iperm = y.down.iperm;
+            } else {
+                // this rank: down's column positions [F r/tp, ..) -- whole groups -- i.e. hidden
+                // values perm[j]; their gate/up rows interleaved by tile as above, each value
+                // written at its position j of the whole (permuted) hidden vector
+                if (F % (32 * tp)) { snprintf(why, nwhy, "layer %d: FFN %d not in whole groups per rank", l, F); return false; }
+                const int fn = F / tp, j0 = fn * rk, en = e->E / tp, e0 = en * rk;
+                const int32_t * dperm = (const int32_t *) (f.base + dn->perm_off);
+                const int gtr = tr_for(gt, 2 * fn, 1);
+                std::vector<int32_t> sc(fn);
+                for (int m = 0; m < fn; m++) sc[m] = j0 + m;
+                if (!upload_tt(e->ar, f, gt, 2 * fn, gtr, min_tiles, 1, [&](int r) {
+                        const int h = gtr / 2, ti = r / gtr, j = r % gtr, m = ti * h + j % h;
+                        return m >= fn ? RowSrc{nullptr, 0} : RowSrc{j < h ? gt : up, dperm[j0 + m]}; },
+                               y.gateup, why, nwhy) ||
+                    !upload_tt(e->ar, f, dn, en, tr_for(dn, en, 0), min_tiles, 0,
+                               [&](int r) { return RowSrc{r < en ? dn : nullptr, e0 + r}; }, y.down, why, nwhy))
+                    return false;
+                y.down_iperm = (const int32_t *) e->ar.upload(sc.data(), sc.size() * 4);
+            }
         }
         // per token: the router and the k chosen experts (as tiles)
         e->bytes_tok += tt_bytes(y.qkv) + tt_bytes(y.o) +
@@ -358,17 +453,34 @@ static bool build(sb_engine * e, char * why, int nwhy) {
         y.qn = up_f32(e, qn);
         y.kn = up_f32(e, kn);
     }
-    if (e->emb.cols != e->E || e->emb.rows != e->V || e->head.cols != e->E || e->head.rows != e->V) {
+    if (e->emb.cols != e->E || e->emb.rows != e->V || e->head.cols != e->E || e->head.rows != e->V / tp) {
         snprintf(why, nwhy, "embedding or head shape does not match the header");
         return false;
     }
     // decode state
     const size_t kv = (size_t) e->n_layer * e->n_ctx * e->kvd * 2;
-    e->x = (float *) carve(e, (size_t) e->E * 4);
     e->qkv = (float *) carve(e, (size_t) (e->qd + 2 * e->kvd) * 4);
     e->att = (float *) carve(e, (size_t) e->qd * 4);
-    e->hp = (float *) carve(e, (size_t) (e->F > 0 ? e->F : 1) * 4);
-    e->logits = (float *) carve(e, (size_t) e->V * 4);
+    if (tp == 1) {
+        e->x = (float *) carve(e, (size_t) e->E * 4);
+        e->hp = (float *) carve(e, (size_t) (e->F > 0 ? e->F : 1) * 4);
+        e->logits = (float *) carve(e, (size_t) e->V * 4);
+    } else {
+        // the exchanged vectors live in the region the peers map: [flags | x | hidden | logits]
+        TpState & t = e->tp;
+        auto r256 = [](size_t v) { return (v + 255) / 256 * 256; };
+        t.off_x = 256;
+        t.off_hp = t.off_x + r256((size_t) e->E * 4);
+        t.off_lg = t.off_hp + r256((size_t) (e->F > 0 ? e->F : 1) * 4);
+        t.reg_bytes = t.off_lg + r256((size_t) e->V * 4);
+        if (t.reg) {
+            e->x = (float *) (t.reg + t.off_x);
+            e->hp = (float *) (t.reg + t.off_hp);
+            e->logits = (float *) (t.reg + t.off_lg);
+        }
+        t.arrive = (unsigned *) carve(e, 4 * 4);
+        t.tok_seq = (unsigned *) carve(e, 4);
+    }
     e->kc = (uint16_t *) carve(e, kv);
     e->vc = (uint16_t *) carve(e, kv);
     e->rcos = (float *) carve(e, (size_t) e->n_ctx * (e->hd / 2) * 4);
@@ -433,7 +545,8 @@ extern "C" int sb_time_kernel(sb_engine * e, int which, int reps, float * ms_avg
         case 0: g = tg_args(e, y.qkv, e->x, y.an, e->qkv); g.bias = y.qkv_b; launch_tg(e, GM_QKV, g); break;
         case 1: launch_attn(e, l); break;
         case 2: g = tg_args(e, y.o, e->att, nullptr, e->x); launch_tg(e, GM_O, g); break;
-        case 3: g = tg_args(e, y.gateup, e->x, y.fn, e->hp); g.ffn_f = e->F; g.scatter = y.down_iperm;
+        case 3: g = tg_args(e, y.gateup, e->x, y.fn, e->hp); g.ffn_f = y.gateup.rows / 2; g.ffn_n = e->F;
+                g.scatter = y.down_iperm;
                 launch_tg(e, GM_FFN, g); break;
         case 4: g = tg_args(e, y.down, e->hp, nullptr, e->x); g.in_permuted = 1; launch_tg(e, GM_DOWN, g); break;
         default: g = tg_args(e, e->head, e->x, e->out_norm, e->logits); g.prefetch = 0;
@@ -468,9 +581,14 @@ extern "C" int sb_trace(const sb_engine * e, unsigned long long * out, int cap) 
     return e->n_launch_trace;
 }
 
-sb_engine * sb_open(const char * path, int n_ctx, char * why, int nwhy) {
+// Open, upload and plan (everything but the token graph). tp > 1: this rank's
+// slices and its exchange region.
+static sb_engine * open_engine(const char * path, int n_ctx, int tp, int rank, char * why, int nwhy) {
     g_err[0] = 0;
+    if (tp < 1 || tp > kMaxTp || rank < 0 || rank >= tp) { snprintf(why, nwhy, "rank %d of %d", rank, tp); return nullptr; }
     sb_engine * e = new sb_engine();
+    e->tp.n = tp;
+    e->tp.rank = rank;
     if (!ssf_open(&e->f, path, why, nwhy)) { delete e; return nullptr; }
     const ssf_hdr * h = e->f.hdr;
     if (const char * u = ssf_unsupported(e->f)) {
@@ -512,12 +630,18 @@ sb_engine * sb_open(const char * path, int n_ctx, char * why, int nwhy) {
             close_all(e); delete e; return nullptr;
         }
     }
-    // pass 1 sizes the arena, pass 2 fills it
+    // pass 1 sizes the arena (and the exchange region), pass 2 fills them
     if (!build(e, why, nwhy)) { close_all(e); delete e; return nullptr; }
     if (!e->ar.allocate()) {
         snprintf(why, nwhy, "cudaMalloc of %.2f GB for the model failed", e->ar.size / 1e9);
         close_all(e); delete e; return nullptr;
     }
+    if (tp > 1 && (!ck(cudaMalloc(&e->tp.reg, e->tp.reg_bytes), "exchange region") ||
+                   !ck(cudaMemset(e->tp.reg, 0, e->tp.reg_bytes), "exchange region"))) {
+        snprintf(why, nwhy, "%s", g_err);
+        close_all(e); delete e; return nullptr;
+    }
+    e->tp.peer[rank] = e->tp.reg;
     if (!build(e, why, nwhy)) { close_all(e); delete e; return nullptr; }
     upload_rope(e->rcos, e->rsin, e->n_ctx, e->hd, e->theta);
     if (!ck(cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking), "stream") ||
@@ -526,9 +650,13 @@ sb_engine * sb_open(const char * path, int n_ctx, char * why, int nwhy) {
         snprintf(why, nwhy, "%s", g_err);
         close_all(e); delete e; return nullptr;
     }
-    // capture one token (SB_SYNC=1: no graph, every kernel synchronized and checked)
+    return e;
+}
+
+// Capture one token (SB_SYNC=1: no graph, every kernel synchronized and checked).
+static bool capture(sb_engine * e) {
     const char * sm = getenv("SB_SYNC");
-    e->sync_mode = sm && atoi(sm) != 0;
+    e->sync_mode = sm && atoi(sm) != 0 && e->tp.n == 1;
     cudaGraph_t gr = nullptr;
     e->launches = 0;
     bool ok = true;
@@ -541,12 +669,46 @@ sb_engine * sb_open(const char * path, int n_ctx, char * why, int nwhy) {
         ok = ok && ck(cudaGraphInstantiateWithFlags(&e->g_tok, gr, 0), "instantiate");
         if (gr) cudaGraphDestroy(gr);
     }
-    ok = ok && ck(cudaDeviceSynchronize(), "open") && !e->failed;
-    if (!ok) {
+    return ok && ck(cudaDeviceSynchronize(), "open") && !e->failed;
+}
+
+sb_engine * sb_open(const char * path, int n_ctx, char * why, int nwhy) {
+    sb_engine * e = open_engine(path, n_ctx, 1, 0, why, nwhy);
+    if (e && !capture(e)) {
         snprintf(why, nwhy, "%s", g_err);
         close_all(e); delete e; return nullptr;
     }
     return e;
+}
+
+sb_engine * sb_open_tp(const char * path, int n_ctx, int tp, int rank, char * why, int nwhy) {
+    if (tp == 1) return sb_open(path, n_ctx, why, nwhy);
+    return open_engine(path, n_ctx, tp, rank, why, nwhy);
+}
+
+int sb_tp_handle(const sb_engine * e, void * out) {
+    if (!e || e->tp.n <= 1 || !out) return 0;
+    cudaIpcMemHandle_t h;
+    if (!ck(cudaIpcGetMemHandle(&h, e->tp.reg), "cudaIpcGetMemHandle")) return 0;
+    static_assert(sizeof h == SB_TP_HANDLE_BYTES, "IPC handle size");
+    memcpy(out, &h, sizeof h);
+    return 1;
+}
+
+int sb_tp_connect(sb_engine * e, const void * handles, char * why, int nwhy) {
+    if (!e || e->tp.n <= 1 || !handles || e->g_tok) { snprintf(why, nwhy, "not a tensor-parallel engine awaiting its peers"); return 0; }
+    TpState & t = e->tp;
+    for (int p = 0; p < t.n; p++) {
+        if (p == t.rank) continue;
+        cudaIpcMemHandle_t h;
+        memcpy(&h, (const uint8_t *) handles + (size_t) p * SB_TP_HANDLE_BYTES, sizeof h);
+        if (!ck(cudaIpcOpenMemHandle(&t.peer[p], h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle")) {
+            snprintf(why, nwhy, "rank %d: %s", p, g_err);
+            return 0;
+        }
+    }
+    if (!capture(e)) { snprintf(why, nwhy, "%s", g_err); return 0; }
+    return 1;
 }
 
 void sb_close(sb_engine * e) {
@@ -583,12 +745,25 @@ static bool run_token(sb_engine * e) {
     return !e->failed;
 }
 
+// After a synchronize: the kernels' error flag (a bounded wait that gave up, a
+// failed check) makes the call fail with its code.
+static bool check_err(sb_engine * e) {
+    int err = 0;
+    if (!ck(cudaMemcpy(&err, e->err, 4, cudaMemcpyDeviceToHost), "error flag")) return false;
+    if (err) {
+        snprintf(g_err, sizeof g_err, "a kernel reported error code %d (%s)", err,
+                 err == 7 ? "a tensor-parallel peer's event did not arrive" : "a bounded wait or check");
+        return false;
+    }
+    return true;
+}
+
 const float * sb_step(sb_engine * e, int tok, int pos) {
     if (!e || pos < 0 || pos >= e->n_ctx || tok < 0 || tok >= e->V) return nullptr;
     if (!set_tok_pos(e, tok, pos)) return nullptr;
     if (!run_token(e)) return nullptr;
     if (!ck(cudaMemcpyAsync(e->h_logits, e->logits, (size_t) e->V * 4, cudaMemcpyDeviceToHost, e->st), "logits")) return nullptr;
-    if (!ck(cudaStreamSynchronize(e->st), "step")) return nullptr;
+    if (!ck(cudaStreamSynchronize(e->st), "step") || !check_err(e)) return nullptr;
     return e->h_logits;
 }
 
@@ -605,10 +780,10 @@ const float * sb_prefill(sb_engine * e, const int * ids, int pos0, int n) {
             !ck(cudaMemcpyAsync(e->pos, &e->h_io[slot + 1], 4, cudaMemcpyHostToDevice, e->st), "pos") ||
             !run_token(e))
             return nullptr;
-        if (i % 30 == 29) { if (!ck(cudaStreamSynchronize(e->st), "prefill")) return nullptr; }
+        if (i % 30 == 29) { if (!ck(cudaStreamSynchronize(e->st), "prefill") || !check_err(e)) return nullptr; }
     }
     if (!ck(cudaMemcpyAsync(e->h_logits, e->logits, (size_t) e->V * 4, cudaMemcpyDeviceToHost, e->st), "logits")) return nullptr;
-    if (!ck(cudaStreamSynchronize(e->st), "prefill")) return nullptr;
+    if (!ck(cudaStreamSynchronize(e->st), "prefill") || !check_err(e)) return nullptr;
     return e->h_logits;
 }
 
@@ -635,7 +810,7 @@ static int generate(sb_engine * e, const int * prompt, int np, int nwarm, int ng
     if (ms) cudaEventRecord(b, e->st);
     if (!ck(cudaMemcpyAsync(out_ids, e->tlog + np - 1, (size_t) total * 4, cudaMemcpyDeviceToHost, e->st), "ids"))
         return 0;
-    if (!ck(cudaStreamSynchronize(e->st), "generate")) return 0;
+    if (!ck(cudaStreamSynchronize(e->st), "generate") || !check_err(e)) return 0;
     if (ms) {
         cudaEventElapsedTime(ms, a, b);
         cudaEventDestroy(a);

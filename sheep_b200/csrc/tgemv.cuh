@@ -39,6 +39,61 @@ constexpr int kMaxStages = 32;
 // less this file's static arrays).
 constexpr size_t kSmemBudget = 225 * 1024;
 
+// Tensor-parallel exchange of one GEMV (tp_exchange.h's protocol): rows
+// written into every peer's copy of the output buffer, then one flag per
+// peer raised by the kernel's last CTA; and, before staging, a wait on the
+// peers' flags of the event this kernel's input depends on.
+constexpr int kMaxTp = 8;
+struct TpX {
+    int n, rank;                       // ranks; this one
+    float * peer_out[kMaxTp];          // the output pointer as each peer maps it (NULL for this rank)
+    unsigned * peer_flag[kMaxTp];      // flag slot [rank] in each peer's flag array (NULL for this rank)
+    unsigned * arrive;                 // arrivals of this kernel's CTAs (last one raises; it resets)
+    const unsigned * flags;            // this rank's flag array [n]: event counts per source rank
+    const unsigned * tok_seq;          // tokens run so far (the embedding kernel counts them)
+    unsigned ev_per_tok;               // exchange events per token
+    int ev_raise, ev_wait;             // this kernel's event to raise / to wait for (-1: none)
+    int * err;
+};
+
+// Value a flag reaches once event ev of the current token is raised.
+SB_DEV unsigned tp_target(const TpX & x, int ev) { return *x.tok_seq * x.ev_per_tok + (unsigned) ev + 1u; }
+
+// Wait, as one thread, until every peer has raised event x.ev_wait (bounded:
+// 2 s of the global timer, then an error code and on).
+SB_DEV void tp_wait(const TpX & x) {
+    if (x.n <= 1 || x.ev_wait < 0) return;
+    const unsigned want = tp_target(x, x.ev_wait);
+    for (int p = 0; p < x.n; p++) {
+        if (p == x.rank) continue;
+        const unsigned * f = x.flags + p;
+        unsigned v;
+        asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+        if ((int) (v - want) >= 0) continue;
+        const unsigned long long t0 = global_ns();
+        for (;;) {
+            asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+            if ((int) (v - want) >= 0) break;
+            if (global_ns() - t0 > kWaitNs) { if (x.err) atomicExch(x.err, 7); break; }
+        }
+    }
+}
+
+// After this CTA's rows are stored everywhere: the last CTA of the grid raises
+// event x.ev_raise in every peer (system-scope release after a system fence).
+SB_DEV void tp_arrive(const TpX & x) {
+    if (x.n <= 1 || x.ev_raise < 0) return;
+    __threadfence_system();
+    const unsigned total = gridDim.x * gridDim.y;
+    if (atomicAdd(x.arrive, 1u) == total - 1u) {
+        __threadfence_system();
+        *x.arrive = 0u;
+        const unsigned v = tp_target(x, x.ev_raise);
+        for (int p = 0; p < x.n; p++)
+            if (x.peer_flag[p]) asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(x.peer_flag[p]), "r"(v) : "memory");
+    }
+}
+
 struct TGArgs {
     TT t;
     const float * in;        // input activation
@@ -46,7 +101,8 @@ struct TGArgs {
     float eps;
     int in_permuted;         // `in` already in t.perm order
     const float * bias;      // per logical row (QKV: q|k|v concatenated); FFN: [gate bias | up bias]
-    int ffn_f;               // FFN: hidden size
+    int ffn_f;               // FFN: hidden values this launch computes (rows / 2)
+    int ffn_n;               // FFN: size of the output (the whole hidden vector; > ffn_f on a tensor-parallel rank)
     float * out;
     const int32_t * scatter; // FFN: write index of hidden value i
     float * am_val; int * am_idx; unsigned * am_cnt;
@@ -63,6 +119,7 @@ struct TGArgs {
     const uint8_t * next_tiles;
     int next_ntiles, next_grid;
     uint32_t next_tb;
+    TpX tp;                  // tensor-parallel exchange (tp.n > 1)
 };
 
 // Shared memory: [act | perm | norm gain | input x | group dots | ring]. perm
@@ -823,6 +880,11 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__
     }
     ActS a = act_carve(smem, t.cols);
     bool failed = false;   // after one wait gives up, the rest are skipped
+    if (g.tp.n > 1 && g.tp.ev_wait >= 0) {
+        // the input's other rows come from the peers: wait for their event
+        if (threadIdx.x == 0) tp_wait(g.tp);
+        bar_sync(1, kConsThreads);
+    }
     tg_stage(g, a, red, smem, SL, &statics, failed);
     SB_MARK(g.trace, g.launch_id, 2);
     const TileGeom tg = tile_geom(t.cols, t.TR, NB, SIX, t.has_min);
@@ -854,8 +916,12 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__
                     uv = __fadd_rn(uv, first ? ub0 : g.bias[g.ffn_f + idx]);
                 }
                 const int sc = first ? sc0 : g.scatter[idx];
-                if (SB_CHECK(g.err, sc >= 0 && sc < g.ffn_f, 108))
-                    g.out[sc] = silu_mul(gv, uv);
+                if (SB_CHECK(g.err, sc >= 0 && sc < g.ffn_n, 108)) {
+                    const float h = silu_mul(gv, uv);
+                    g.out[sc] = h;
+                    for (int p = 0; p < g.tp.n; p++)
+                        if (g.tp.peer_out[p]) g.tp.peer_out[p][sc] = h;
+                }
             }
             continue;
         }
@@ -866,17 +932,27 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__
                 if (g.bias) y = __fadd_rn(y, (MODE == GM_QKV && k < kConsWarps) ? gb0 : g.bias[r]);
                 g.out[r] = y;
             } else if (MODE == GM_O || MODE == GM_DOWN) {
-                g.out[r] = __fadd_rn(k < kConsWarps ? res0 : g.out[r], y);
+                y = __fadd_rn(k < kConsWarps ? res0 : g.out[r], y);
+                g.out[r] = y;
             } else if (MODE == GM_HEAD) {
                 g.out[r] = y;
                 if (y > best_v || (y == best_v && r < best_i)) { best_v = y; best_i = r; }
             }
+            for (int p = 0; p < g.tp.n; p++)
+                if (g.tp.peer_out[p]) g.tp.peer_out[p][r] = y;
         }
     }
 
+    if (g.tp.n > 1) {
+        // every consumer's stores to the peers, then the grid's last CTA raises
+        // the event (tp_arrive fences at system scope)
+        __threadfence_system();
+        bar_sync(1, kConsThreads);
+        if (threadIdx.x == 0) tp_arrive(g.tp);
+    }
     bar_sync(1, kConsThreads);
     SB_MARK(g.trace, g.launch_id, 4);
-    if (MODE == GM_HEAD) {
+    if (MODE == GM_HEAD && g.am_cnt) {
         // greedy argmax, ties to the lower index (sml/sml-run.c:3539-3544)
 #pragma unroll
         for (int o = 16; o; o >>= 1) {
@@ -910,6 +986,39 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__
                 *g.pos = p + 1;
             }
         }
+    }
+}
+
+static __global__ void __launch_bounds__(kArgmaxThreads) k_tp_argmax(const float * logits, int V,
+                                                                      const __grid_constant__ TpX x, int * tok,
+                                                                      int * pos, int * tlog) {
+    __shared__ float bv_s[kArgmaxThreads / 32];
+    __shared__ int bi_s[kArgmaxThreads / 32];
+    pdl_launch_dependents();
+    pdl_wait();
+    if (threadIdx.x == 0) tp_wait(x);
+    __syncthreads();
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const float v = logits[i];
+        if (v > bv) { bv = v; bi = i; }   // increasing i: the first largest stays
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    if ((threadIdx.x & 31) == 0) { bv_s[threadIdx.x >> 5] = bv; bi_s[threadIdx.x >> 5] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int) (blockDim.x >> 5); w++)
+            if (bv_s[w] > bv || (bv_s[w] == bv && bi_s[w] < bi)) { bv = bv_s[w]; bi = bi_s[w]; }
+        const int p = *pos;
+        if (tlog) tlog[p] = bi;
+        *tok = bi;
+        *pos = p + 1;
     }
 }
 
