@@ -10,8 +10,9 @@ so nothing is flushed between steps.
 
 value: device-resident greedy loop (one CUDA-graph replay per token, the
 token chosen on the GPU), CUDA events over K tokens after a 128-token prompt
-and W warm-up tokens, max over ranks, summed over ranks (N independent
-replicas: the path does not shard at batch 1).
+and W warm-up tokens. With N GPUs the one stream is split over them (tensor
+parallelism: attention replicated, gate/up, down and head rows split, rows
+exchanged over NVLink by the GEMVs), the max over ranks; strong scaling.
 e2e: the same tokens through the reference-facing C ABI (sml_gpu_prefill /
 sml_gpu_step with host ids in and host logits out, host argmax), wall clock.
 --impl reference: the reference engine's own CPU decode (oracle/_ref, built
@@ -23,8 +24,9 @@ experts actually read plus the router), each run timed alone by CUDA events
 with a 512 MB buffer rewritten before it, so the weights come from HBM; and
 configuration 3's batch-1 decode (Llama-3-8B shape, 4.2 GB per token) and its
 batched serving at 64 slots (2048-id prompts, 256 generated ids each).
-extras with N > 1 GPUs: configuration 2's MoE layer spread over the N GPUs
-(expert parallelism, sb_moe_open_ep), the max over ranks at 1/16/64/256 tokens.
+extras with N > 1 GPUs: configuration 3 split the same way over the N GPUs,
+and configuration 2's MoE layer spread over them (expert parallelism,
+sb_moe_open_ep), the max over ranks at 1/16/64/256 tokens.
 """
 import argparse
 import ctypes
@@ -246,7 +248,9 @@ def main():
     import sheep_b200
     path = model_path(spec, rank, dist)
     n_ctx = max(PROMPT_LEN + W + K + 8, PROMPT_LEN + 40)
-    eng = sheep_b200.Engine(path, n_ctx=n_ctx)
+    # N > 1: one decode stream split over the N GPUs (tensor parallelism)
+    tp = (world, rank, dist) if world > 1 else None
+    eng = sheep_b200.Engine(path, n_ctx=n_ctx, tp=tp)
     prompt = np.random.default_rng(1234).integers(0, eng.n_vocab, PROMPT_LEN).astype(np.int32)
 
     def barrier():
@@ -265,33 +269,48 @@ def main():
         ids, ms = eng.generate(prompt, K + 1, timed=True, warmup=W)   # K + 1 ids = K timed replays
         barrier()
     ms = max_over_ranks(ms)
-    value = sdist.replica_throughput(K, ms / 1000.0, world)
+    value = K / (ms / 1000.0)
     launches = eng.launches_per_token
+    bytes_rank = float(eng.bytes_per_token)
 
-    # ---- the dominant kernel (fused gate/up GEMV) alone, for the roofline
+    # ---- the dominant kernel (fused gate/up GEMV, this rank's rows) alone, for the roofline
     k_ms, k_bytes = eng.time_kernel("ffn", 2 * eng.n_layer)
-    eng.close()
     barrier()
 
-    # ---- end to end through the reference-facing C ABI, host buffers
-    ok, why = sheep_b200.sml_gpu_open(path, n_ctx)
-    if not ok:
-        raise RuntimeError(why)
-    lg = sheep_b200.sml_gpu_prefill(prompt, 0)
+    # ---- end to end through the reference-facing API, host buffers: host ids
+    # in, host logits out, host argmax (sml_gpu_step; with N GPUs its handle
+    # form sb_step on every rank)
+    if world == 1:
+        eng.close()
+        ok, why = sheep_b200.sml_gpu_open(path, n_ctx)
+        if not ok:
+            raise RuntimeError(why)
+        prefill, step = (lambda ids_, p0: sheep_b200.sml_gpu_prefill(ids_, p0)), sheep_b200.sml_gpu_step
+    else:
+        prefill, step = eng.prefill, eng.step
+    lg = prefill(prompt, 0)
     pos = PROMPT_LEN
     for _ in range(W):
-        lg = sheep_b200.sml_gpu_step(int(np.argmax(lg)), pos)
+        lg = step(int(np.argmax(lg)), pos)
         pos += 1
     barrier()
     t0 = time.perf_counter()
     for _ in range(K):
-        lg = sheep_b200.sml_gpu_step(int(np.argmax(lg)), pos)
+        lg = step(int(np.argmax(lg)), pos)
         pos += 1
     e2e_s = time.perf_counter() - t0
-    sheep_b200.sml_gpu_close()
+    if world == 1:
+        sheep_b200.sml_gpu_close()
+    else:
+        eng.close()
     e2e_s = max_over_ranks(e2e_s)
-    e2e = sdist.replica_throughput(K, e2e_s, world)
+    e2e = K / e2e_s
     nv = len(lg)
+    bytes_all = bytes_rank
+    if dist is not None:
+        t = torch.tensor([bytes_rank], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t)
+        bytes_all = float(t.item())
 
     cpu = None
     if rank == 0 and world == 1 and os.path.exists(REF_LIB):
@@ -303,12 +322,14 @@ def main():
 
     extras = None
     if world > 1:
-        # every rank: configuration 2's MoE layer spread over the GPUs (expert
-        # parallelism, the library's NCCL all-reduce between down and combine)
+        # every rank: configuration 3 split the same way, and configuration 2's
+        # MoE layer spread over the GPUs (expert parallelism, the library's NCCL
+        # all-reduce between down and combine)
         peak0, _ = peaks()
+        d3 = decode_cfg3(peak0, tp=(world, rank, dist), max_over_ranks=max_over_ranks)
         ep = moe_ep_microbench(peak0, dist, world, rank, max_over_ranks)
         if rank == 0:
-            extras = {"moe_cfg2_ep": ep}
+            extras = {"decode_cfg3_tp": d3, "moe_cfg2_ep": ep}
     if rank == 0 and world == 1:
         peak0, _ = peaks()
         extras = {"l2": "a 512 MB buffer rewritten before each timed run (decode: weights > L2)",
@@ -322,10 +343,12 @@ def main():
         traffic = profiled_traffic("tgemv_ffn_cfg0")
         out = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W,
-            "ms_per_step": ms / K, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "ms_per_step": ms / K, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
             "dtype": "s8xu4->s32, f32 epilogue", "data": "synthetic (seeded N(0,0.02) weights, RTN Q4)",
             "config": bench_config(W, K),
-            "parallelism": f"replicas{world}: one decode per GPU, value summed over GPUs",
+            "parallelism": ("one GPU" if world == 1 else
+                            f"tp{world}: one decode stream; gate/up, down and head rows split over {world} GPUs, "
+                            "attention replicated, rows exchanged over NVLink by the GEMVs"),
             "l2": "weights 0.89 GB/token > 126 MB L2: no flush",
             "roofline": {"kernel": "k_tgemv<FFN> (fused gate/up dequant-GEMV + SiLU), launched alone",
                          "bound": "hbm", "achieved": achieved, "peak": peak, "peak_kind": peak_kind,
@@ -334,10 +357,13 @@ def main():
                          "launch_us": k_ms * 1000.0},
             "token_roofline": {"bytes_per_token": float(spec_bytes(path)),
                                "achieved_gbs": float(spec_bytes(path)) / (ms / K / 1000.0) / 1e9,
-                               "frac": float(spec_bytes(path)) / (ms / K / 1000.0) / 1e9 / peak},
-            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4 * nv,
-                    "path": "sml_gpu_step (host ids in, host logits out, host argmax)"},
-            "gpu_launches": launches * K,
+                               "frac": float(spec_bytes(path)) / (ms / K / 1000.0) / 1e9 / peak,
+                               "bytes_read_all_gpus": bytes_all,
+                               "frac_of_n_gpus": bytes_all / (ms / K / 1000.0) / 1e9 / (peak * world)},
+            "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8 * world, "d2h_bytes_per_step": 4 * nv * world,
+                    "path": "sml_gpu_step (host ids in, host logits out, host argmax)" if world == 1 else
+                            "sb_step on every rank (host ids in, host logits out, host argmax)"},
+            "gpu_launches": launches * K * world,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
             "greedy_ids_32": [int(i) for i in ids32[:32]],
@@ -375,20 +401,32 @@ def gemv_microbench(peak, reps=20):
     return out
 
 
-def decode_cfg3(peak, ngen=64):
+def decode_cfg3(peak, ngen=64, tp=None, max_over_ranks=None):
     """Configuration 3 (Llama-3-8B shape, 6-bit group fields) at batch 1: the
-    device-resident greedy loop after a 128-token prompt."""
+    device-resident greedy loop after a 128-token prompt; with tp=(world, rank,
+    dist) one stream split over the GPUs (every rank calls this)."""
     import sheep_b200
     from sheep_b200 import configs
-    path = model_path(configs.CONFIGS["llama3-8b-q4k"], 0, None)
-    eng = sheep_b200.Engine(path, n_ctx=PROMPT_LEN + 8 + ngen + 8)
+    rank, dist = (tp[1], tp[2]) if tp else (0, None)
+    path = model_path(configs.CONFIGS["llama3-8b-q4k"], rank, dist)
+    eng = sheep_b200.Engine(path, n_ctx=PROMPT_LEN + 8 + ngen + 8, tp=tp)
     try:
         prompt = np.random.default_rng(1234).integers(0, eng.n_vocab, PROMPT_LEN).astype(np.int32)
-        _, ms = eng.generate(prompt, ngen + 1, timed=True, warmup=8)
+        ids, ms = eng.generate(prompt, ngen + 1, timed=True, warmup=8)
+        if max_over_ranks:
+            ms = max_over_ranks(ms)
         tps = ngen / (ms / 1000.0)
-        gbs = eng.bytes_per_token * tps / 1e9
-        return {"tok_s": round(tps, 1), "ms_per_token": round(ms / ngen, 4), "bytes_per_token": eng.bytes_per_token,
-                "gbs": round(gbs, 1), "frac": round(gbs / peak, 4), "tokens": ngen}
+        nb = float(eng.bytes_per_token)
+        world = tp[0] if tp else 1
+        if dist is not None:
+            import torch
+            t = torch.tensor([nb], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t)
+            nb = float(t.item())
+        gbs = nb * tps / 1e9
+        return {"tok_s": round(tps, 1), "ms_per_token": round(ms / ngen, 4), "gpus": world,
+                "bytes_per_token_all_gpus": int(nb), "gbs": round(gbs, 1), "frac_of_n_gpus": round(gbs / (peak * world), 4),
+                "tokens": ngen, "greedy_ids_head": [int(i) for i in ids[:8]]}
     finally:
         eng.close()
 

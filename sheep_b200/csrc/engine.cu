@@ -61,8 +61,8 @@ struct TpState {
     size_t reg_bytes = 0;
     void * peer[kMaxTp] = {};         // every rank's region as mapped here (this rank's = reg)
     size_t off_x = 0, off_hp = 0, off_lg = 0;   // vectors in the region (flags at 0)
-    unsigned * arrive = nullptr;      // per raising kernel kind: FFN, down, head
     unsigned * tok_seq = nullptr;
+    std::vector<unsigned> cum;        // arrivals per token up to each event (tp_counts)
 };
 
 struct sb_engine {
@@ -197,26 +197,41 @@ static void set_next(TGArgs & g, const TT * nt, int nsm) {
 }
 
 // The exchange of one GEMV launch: `out` is this launch's output pointer in
-// this rank's region (its rows go to the same offset in every peer's).
-static void set_tp(sb_engine * e, TGArgs & g, int kind, int ev_raise, int ev_wait, float * out) {
+// this rank's region (its rows go to the same offset in every peer's); raise:
+// its CTAs arrive at the peers; wait_ev: the event (index into tp.cum) whose
+// arrivals it waits for, -1 none.
+static void set_tp(sb_engine * e, TGArgs & g, bool raise, int wait_ev, float * out) {
     TpState & t = e->tp;
     if (t.n <= 1) return;
     TpX & x = g.tp;
     x.n = t.n; x.rank = t.rank;
     for (int p = 0; p < t.n; p++) {
         x.peer_out[p] = nullptr;
-        x.peer_flag[p] = nullptr;
+        x.peer_cnt[p] = nullptr;
         if (p == t.rank) continue;
         if (out) x.peer_out[p] = (float *) ((uint8_t *) t.peer[p] + ((uint8_t *) out - t.reg));
-        if (ev_raise >= 0) x.peer_flag[p] = (unsigned *) t.peer[p] + t.rank;
+        if (raise) x.peer_cnt[p] = (unsigned *) t.peer[p] + t.rank;
     }
-    x.arrive = t.arrive + kind;
-    x.flags = (const unsigned *) t.reg;
+    x.cnt = (const unsigned *) t.reg;
     x.tok_seq = t.tok_seq;
-    x.ev_per_tok = 2u * e->n_layer + 1u;
-    x.ev_raise = ev_raise;
-    x.ev_wait = ev_wait;
+    x.c_tok = t.cum.empty() ? 0u : t.cum.back();
+    x.wait_count = wait_ev >= 0 ? t.cum[wait_ev] : 0u;
+    x.raise = raise ? 1 : 0;
     x.err = e->err;
+}
+
+// Arrivals per token up to each event (hidden(l) = 2l, x(l) = 2l+1, logits =
+// 2 n_layer): the raising kernels' CTA counts, in the order they run.
+static void tp_counts(sb_engine * e) {
+    TpState & t = e->tp;
+    t.cum.clear();
+    unsigned c = 0;
+    auto grid = [&](const TT & tt) { return (unsigned) (tt.ntiles < e->nsm ? tt.ntiles : e->nsm); };
+    for (const LayerD & y : e->L) {
+        c += grid(y.gateup); t.cum.push_back(c);
+        c += grid(y.down); t.cum.push_back(c);
+    }
+    c += grid(e->head); t.cum.push_back(c);
 }
 
 static void launch_tg(sb_engine * e, int mode, const TGArgs & g0) {
@@ -260,7 +275,7 @@ static void enqueue_token(sb_engine * e) {
             TGArgs g = tg_args(e, y.qkv, e->x, y.an, e->qkv);
             g.bias = y.qkv_b;
             set_next(g, &y.o, e->nsm);
-            set_tp(e, g, 0, -1, l > 0 ? 2 * (l - 1) + 1 : -1, nullptr);   // x of the previous layer
+            set_tp(e, g, false, l > 0 ? 2 * (l - 1) + 1 : -1, nullptr);   // x of the previous layer
             launch_tg(e, GM_QKV, g);
         }
         snprintf(e->cur, sizeof e->cur, "L%d.attn", l);
@@ -285,7 +300,7 @@ static void enqueue_token(sb_engine * e) {
             g.ffn_n = e->F;
             g.scatter = y.down_iperm;
             set_next(g, &y.down, e->nsm);
-            set_tp(e, g, 0, 2 * l, -1, e->hp);
+            set_tp(e, g, true, -1, e->hp);
             launch_tg(e, GM_FFN, g);
         }
         snprintf(e->cur, sizeof e->cur, "L%d.down", l);
@@ -295,7 +310,7 @@ static void enqueue_token(sb_engine * e) {
             TGArgs g = tg_args(e, y.down, e->hp, nullptr, xo);
             g.in_permuted = 1;
             set_next(g, l + 1 < e->n_layer ? &e->L[l + 1].qkv : nullptr, e->nsm);
-            set_tp(e, g, 1, 2 * l + 1, 2 * l, xo);
+            set_tp(e, g, true, 2 * l, xo);
             launch_tg(e, GM_DOWN, g);
         }
     }
@@ -307,14 +322,14 @@ static void enqueue_token(sb_engine * e) {
         g.am_val = e->am_val; g.am_idx = e->am_idx; g.am_cnt = e->am_cnt;
         g.tok = e->tok; g.pos = e->pos; g.tlog = e->tlog;
     }
-    set_tp(e, g, 2, 2 * e->n_layer, 2 * (e->n_layer - 1) + 1, lo);
+    set_tp(e, g, true, 2 * (e->n_layer - 1) + 1, lo);
     launch_tg(e, GM_HEAD, g);
     if (e->tp.n > 1) {
         // the greedy choice over every rank's logits
         snprintf(e->cur, sizeof e->cur, "argmax");
         TGArgs w;
         memset(&w, 0, sizeof w);
-        set_tp(e, w, 2, -1, 2 * e->n_layer, nullptr);
+        set_tp(e, w, false, 2 * e->n_layer, nullptr);
         launch(e, true, k_tp_argmax, dim3(1), dim3(kArgmaxThreads), 0, (const float *) e->logits, e->V, w.tp,
                e->tok, e->pos, e->tlog);
     }
@@ -478,7 +493,6 @@ static bool build(sb_engine * e, char * why, int nwhy) {
             e->hp = (float *) (t.reg + t.off_hp);
             e->logits = (float *) (t.reg + t.off_lg);
         }
-        t.arrive = (unsigned *) carve(e, 4 * 4);
         t.tok_seq = (unsigned *) carve(e, 4);
     }
     e->kc = (uint16_t *) carve(e, kv);
@@ -655,6 +669,7 @@ static sb_engine * open_engine(const char * path, int n_ctx, int tp, int rank, c
 
 // Capture one token (SB_SYNC=1: no graph, every kernel synchronized and checked).
 static bool capture(sb_engine * e) {
+    if (e->tp.n > 1) tp_counts(e);
     const char * sm = getenv("SB_SYNC");
     e->sync_mode = sm && atoi(sm) != 0 && e->tp.n == 1;
     cudaGraph_t gr = nullptr;

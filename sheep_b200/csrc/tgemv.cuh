@@ -39,34 +39,34 @@ constexpr int kMaxStages = 32;
 // less this file's static arrays).
 constexpr size_t kSmemBudget = 225 * 1024;
 
-// Tensor-parallel exchange of one GEMV (tp_exchange.h's protocol): rows
-// written into every peer's copy of the output buffer, then one flag per
-// peer raised by the kernel's last CTA; and, before staging, a wait on the
-// peers' flags of the event this kernel's input depends on.
+// Tensor-parallel exchange of one GEMV: rows written into every peer's copy
+// of the output buffer, then every CTA adds one to a counter per source rank
+// in every peer (a system-scope release after a block barrier); and, before
+// staging, a wait until each peer's counter has reached the count its event
+// completes. The counters only grow: a token's raising kernels add c_tok in
+// all (their CTA counts, summed on the host), so event e of the current token
+// is complete at (tokens before it) * c_tok + the count up to e.
 constexpr int kMaxTp = 8;
 struct TpX {
     int n, rank;                       // ranks; this one
     float * peer_out[kMaxTp];          // the output pointer as each peer maps it (NULL for this rank)
-    unsigned * peer_flag[kMaxTp];      // flag slot [rank] in each peer's flag array (NULL for this rank)
-    unsigned * arrive;                 // arrivals of this kernel's CTAs (last one raises; it resets)
-    const unsigned * flags;            // this rank's flag array [n]: event counts per source rank
-    const unsigned * tok_seq;          // tokens run so far (the embedding kernel counts them)
-    unsigned ev_per_tok;               // exchange events per token
-    int ev_raise, ev_wait;             // this kernel's event to raise / to wait for (-1: none)
+    unsigned * peer_cnt[kMaxTp];       // counter [rank] in each peer's counter array (NULL for this rank)
+    const unsigned * cnt;              // this rank's counter array [n]: CTAs arrived per source rank
+    const unsigned * tok_seq;          // tokens run so far, this one included (the embedding kernel counts)
+    unsigned c_tok;                    // arrivals per token per source
+    unsigned wait_count;               // arrivals, within a token, that complete the awaited event (0: none)
+    int raise;                         // this kernel's CTAs arrive at the peers
     int * err;
 };
 
-// Value a flag reaches once event ev of the current token is raised.
-SB_DEV unsigned tp_target(const TpX & x, int ev) { return *x.tok_seq * x.ev_per_tok + (unsigned) ev + 1u; }
-
-// Wait, as one thread, until every peer has raised event x.ev_wait (bounded:
-// 2 s of the global timer, then an error code and on).
+// Wait, as one thread, until every peer's arrivals complete the awaited
+// event (bounded: 2 s of the global timer, then an error code and on).
 SB_DEV void tp_wait(const TpX & x) {
-    if (x.n <= 1 || x.ev_wait < 0) return;
-    const unsigned want = tp_target(x, x.ev_wait);
+    if (x.n <= 1 || !x.wait_count) return;
+    const unsigned want = (*x.tok_seq - 1u) * x.c_tok + x.wait_count;
     for (int p = 0; p < x.n; p++) {
         if (p == x.rank) continue;
-        const unsigned * f = x.flags + p;
+        const unsigned * f = x.cnt + p;
         unsigned v;
         asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
         if ((int) (v - want) >= 0) continue;
@@ -79,19 +79,14 @@ SB_DEV void tp_wait(const TpX & x) {
     }
 }
 
-// After this CTA's rows are stored everywhere: the last CTA of the grid raises
-// event x.ev_raise in every peer (system-scope release after a system fence).
+// After every thread of the CTA has stored its rows everywhere and passed a
+// block barrier: one thread adds this CTA's arrival in every peer (release at
+// system scope: the CTA's stores, ordered before it by the barrier, are seen
+// before the count).
 SB_DEV void tp_arrive(const TpX & x) {
-    if (x.n <= 1 || x.ev_raise < 0) return;
-    __threadfence_system();
-    const unsigned total = gridDim.x * gridDim.y;
-    if (atomicAdd(x.arrive, 1u) == total - 1u) {
-        __threadfence_system();
-        *x.arrive = 0u;
-        const unsigned v = tp_target(x, x.ev_raise);
-        for (int p = 0; p < x.n; p++)
-            if (x.peer_flag[p]) asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(x.peer_flag[p]), "r"(v) : "memory");
-    }
+    if (x.n <= 1 || !x.raise) return;
+    for (int p = 0; p < x.n; p++)
+        if (x.peer_cnt[p]) asm volatile("red.release.sys.global.add.u32 [%0], 1;" :: "l"(x.peer_cnt[p]) : "memory");
 }
 
 struct TGArgs {
@@ -880,7 +875,7 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__
     }
     ActS a = act_carve(smem, t.cols);
     bool failed = false;   // after one wait gives up, the rest are skipped
-    if (g.tp.n > 1 && g.tp.ev_wait >= 0) {
+    if (g.tp.n > 1 && g.tp.wait_count) {
         // the input's other rows come from the peers: wait for their event
         if (threadIdx.x == 0) tp_wait(g.tp);
         bar_sync(1, kConsThreads);
@@ -943,10 +938,8 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__
         }
     }
 
-    if (g.tp.n > 1) {
-        // every consumer's stores to the peers, then the grid's last CTA raises
-        // the event (tp_arrive fences at system scope)
-        __threadfence_system();
+    if (g.tp.n > 1 && g.tp.raise) {
+        // every consumer's stores to the peers, then this CTA's arrival
         bar_sync(1, kConsThreads);
         if (threadIdx.x == 0) tp_arrive(g.tp);
     }
