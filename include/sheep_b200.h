@@ -40,8 +40,13 @@ void        sb_info(const sb_engine * e, int * out);
 uint64_t    sb_bytes_per_token(const sb_engine * e);
 // sml/sml-gpu.h:17 semantics on a handle: logits in host memory, NULL on failure.
 const float * sb_step(sb_engine * e, int tok, int pos);
-// sml/sml-gpu.h:14 semantics on a handle.
+// sml/sml-gpu.h:14 semantics on a handle. The prompt mode (sml_gpu_prompt_mode's
+// levels, sml/sml-gpu-fwd.c:2420) decides how: 0 or 1 (the handle's default 0)
+// step every token through the decode path; 2 reads all but the last in
+// chunks of 64 on the tensor cores (int8 re-quantized weights made on first
+// use, per-256 activations; attention the decode kernel's), then steps the last.
 const float * sb_prefill(sb_engine * e, const int * ids, int pos0, int n);
+int sb_set_prompt_mode(sb_engine * e, int level);   // returns the level set (0..2)
 // Greedy decode with the choice made on the device (the reference's
 // graph-replay benchmark loop, sml/sml-gpu-fwd.c:2626-2662): host prompt in,
 // ngen host ids out. Returns 1, or 0 on failure.

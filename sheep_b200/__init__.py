@@ -53,6 +53,7 @@ def lib():
         "sb_open": (vp, [cp, ip, cp, ip]),
         "sb_open_tp": (vp, [cp, ip, ip, ip, cp, ip]),
         "sb_tp_handle": (ip, [vp, vp]),
+        "sb_set_prompt_mode": (ip, [vp, ip]),
         "sb_tp_connect": (ip, [vp, vp, cp, ip]),
         "sb_close": (None, [vp]),
         "sb_info": (None, [vp, vp]),
@@ -177,6 +178,11 @@ class Engine:
         if not p:
             raise RuntimeError(f"sb_step failed: {lib().sb_last_error().decode()}")
         return np.ctypeslib.as_array(p, shape=(self.n_vocab,)).copy()
+
+    def prompt_mode(self, level):
+        """sml_gpu_prompt_mode on this engine: 0/1 step the prompt, 2 reads it in
+        tensor-core chunks (all but the last token). Returns the level set."""
+        return lib().sb_set_prompt_mode(self.h, int(level))
 
     def prefill(self, ids, pos0=0):
         ids = np.ascontiguousarray(ids, dtype=np.int32)

@@ -29,6 +29,7 @@ extern "C" int sml_gpu_open(const char * path, int n_ctx, int threads, int gpu_l
         if (why && nwhy > 0) snprintf(why, (size_t) nwhy, "%s", buf[0] ? buf : "this model cannot use the GPU path");
         return 0;
     }
+    sb_set_prompt_mode(g_eng, g_prompt_level);
     return 1;
 }
 
@@ -49,7 +50,15 @@ extern "C" int sml_gpu_layers(int * of) {
     return info[0];
 }
 
-extern "C" void sml_gpu_prompt_mode(int level) { g_prompt_level = level; }
+// sml/sml-gpu-fwd.c:2420-2423: level >= 1 lets prompts be read in batches,
+// >= 2 on the tensor cores. Here levels 0 and 1 step the prompt a token at a
+// time through the decode path (exact: it writes what reading a token at a
+// time writes); level 2, the default as in the reference, reads all but the
+// last token in tensor-core chunks (the batched arithmetic).
+extern "C" void sml_gpu_prompt_mode(int level) {
+    g_prompt_level = level;
+    if (g_eng) sb_set_prompt_mode(g_eng, level);
+}
 
 extern "C" int sml_gpu_decode_cpu(int on) {
     (void) on;

@@ -177,6 +177,8 @@ struct AttnArgs {
     float * out;             // [qd] attention output
     const ExpfEntry * xtab;  // expf_libm.h table (k_attn_seq), or NULL: exp rounded from double
     float xnear;             // ... consulted within this distance of a rounding midpoint
+    int qkv_ld, out_ld;      // k_attn_seq over a prompt chunk: token blockIdx.y at qkv + y*qkv_ld,
+                             // position pos_imm + y, output out + y*out_ld
     int * err;
     unsigned long long * trace;
     int launch_id;
@@ -308,7 +310,9 @@ __global__ void __launch_bounds__(kSeqThreads) k_attn_seq(const __grid_constant_
     SB_MARK(g.trace, g.launch_id, 0);
     constexpr int hd = HD;
     const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, wp = tid >> 5;
-    const int pos = g.pos ? *g.pos : g.pos_imm;
+    const int pos = g.pos ? *g.pos : g.pos_imm + (int) blockIdx.y;
+    const float * qkv = g.qkv + (size_t) blockIdx.y * g.qkv_ld;
+    float * gout = g.out + (size_t) blockIdx.y * g.out_ld;
     if (!SB_CHECK(g.err, pos >= 0 && pos < g.n_ctx && g.hd == HD, 211)) { pdl_wait(); return; }
     const int rep = g.n_head / g.n_kv, kvh = h / rep, np = pos + 1;
     const int cap = attn_seq_cap(g.n_ctx), nst = pos < cap ? pos : cap;   // staged cached rows
@@ -334,9 +338,9 @@ __global__ void __launch_bounds__(kSeqThreads) k_attn_seq(const __grid_constant_
     pdl_wait();
     SB_MARK(g.trace, g.launch_id, 1);
     for (int i = tid; i < hd; i += blockDim.x) {
-        q[i] = g.qkv[h * hd + i];
-        kn[i] = g.qkv[g.qd + kvh * hd + i];
-        vn[i] = g.qkv[g.qd + g.kvd + kvh * hd + i];
+        q[i] = qkv[h * hd + i];
+        kn[i] = qkv[g.qd + kvh * hd + i];
+        vn[i] = qkv[g.qd + g.kvd + kvh * hd + i];
     }
     __syncthreads();
     if (g.qn) head_norm(q, g.qn, g.eps, hd, red);
@@ -445,9 +449,48 @@ __global__ void __launch_bounds__(kSeqThreads) k_attn_seq(const __grid_constant_
             o0 = __fmaf_rn(sc[t], h2f(g.vc[(size_t) t * g.kvd + row0 + d]), o0);
             o1 = __fmaf_rn(sc[t], h2f(g.vc[(size_t) t * g.kvd + row0 + d + 1]), o1);
         }
-        *reinterpret_cast<float2 *>(g.out + h * hd + d) = make_float2(o0, o1);
+        *reinterpret_cast<float2 *>(gout + h * hd + d) = make_float2(o0, o1);
     }
     SB_MARK(g.trace, g.launch_id, 4);
+}
+
+// A prompt chunk's embedding rows: token t's row dequantized and scattered to
+// natural order into x + t*E (as k_embed, one row per blockIdx.y).
+template <int NB, int SIX>
+__global__ void k_embed_rows(const __grid_constant__ QT t, const int * tok, float * x, int * err) {
+    const int i = blockIdx.x * blockDim.x + threadIdx.x, r = blockIdx.y;
+    if (i >= t.cols) return;
+    const int tk = tok[r];
+    if (tk < 0 || tk >= t.rows) { if (i == 0) atomicExch(err, 303); return; }
+    x[(size_t) r * t.cols + t.perm[i]] = dequant_at<NB, SIX>(t, tk, i);
+}
+
+// A prompt chunk's keys and values into the cache before its attention: token
+// blockIdx.y (position pos0 + y), KV head blockIdx.x; K normed if kn, RoPE'd
+// (rope_ref) and V as they are, both rounded to fp16 -- the values k_attn_seq
+// computes for its own position, so every later read of these rows sees what
+// the token's own attention writes.
+template <int HD>
+__global__ void __launch_bounds__(128) k_chunk_kv(const float * qkv, int ldq, int qd, int kvd, const float * kn,
+                                                   float eps, const float * rcos, const float * rsin, uint16_t * kc,
+                                                   uint16_t * vc, int pos0) {
+    __shared__ float k[HD], cs[HD / 2], sn[HD / 2];
+    __shared__ double red[4];
+    const int kvh = blockIdx.x, t = blockIdx.y, pos = pos0 + t;
+    const float * row = qkv + (size_t) t * ldq;
+    for (int i = threadIdx.x; i < HD / 2; i += blockDim.x) {
+        cs[i] = rcos[(size_t) pos * (HD / 2) + i];
+        sn[i] = rsin[(size_t) pos * (HD / 2) + i];
+    }
+    for (int i = threadIdx.x; i < HD; i += blockDim.x) k[i] = row[qd + kvh * HD + i];
+    __syncthreads();
+    if (kn) head_norm(k, kn, eps, HD, red);
+    rope_ref(k, HD, cs, sn);
+    __syncthreads();
+    for (int i = threadIdx.x; i < HD; i += blockDim.x) {
+        kc[(size_t) pos * kvd + kvh * HD + i] = f2h(k[i]);
+        vc[(size_t) pos * kvd + kvh * HD + i] = f2h(row[qd + kvd + kvh * HD + i]);
+    }
 }
 
 // Greedy choice over the whole logit vector of a tensor-parallel engine, once

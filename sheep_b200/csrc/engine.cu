@@ -8,6 +8,7 @@
 // graph replays with no host round trip.
 #include "decode.cuh"
 #include "moe_host.h"
+#include "tc_batch.h"
 #include "tgemv.cuh"
 #include "sheep_b200.h"
 #include "ssf.h"
@@ -65,6 +66,28 @@ struct TpState {
     std::vector<unsigned> cum;        // arrivals per token up to each event (tp_counts)
 };
 
+// Prompt reading on the tensor cores (sml_gpu_prompt_mode level 2; the
+// reference's gpu_prefill, sml/sml-gpu-fwd.c:1418, with its tensor-core
+// product sml_g_tcm3/tcm9): a prompt's tokens but the last go through in
+// chunks of up to kPfChunk, every product the batched path's int8 arithmetic
+// (tc_batch.cu: weights re-quantized once, made on first use), each token's
+// keys and values written to the decode cache first (k_chunk_kv) and its
+// attention then the decode kernel's own (k_attn_seq over (head, token)); the
+// last token is stepped through the decode graph, so the logits returned are
+// the decode arithmetic's over the cache the chunks filled.
+constexpr int kPfChunk = 64;
+struct PfGemm { TcPlan p; const int32_t * perm = nullptr; int rows = 0, cols = 0, split = 1; };
+struct PfLayer { PfGemm qkv, o, gu, dn; };
+struct PfState {
+    bool tried = false, ok = false;
+    Arena ar;
+    std::vector<PfLayer> L;
+    int Fp = 0, qkv_ld = 0;
+    float * x = nullptr, * qkv = nullptr, * att = nullptr, * hid = nullptr, * xs = nullptr;
+    uint8_t * xblk = nullptr;
+    int * tok = nullptr, * h_tok = nullptr;
+};
+
 struct sb_engine {
     ssf_file f{};
     int n_layer = 0, E = 0, nh = 0, nkv = 0, hd = 0, qd = 0, kvd = 0, F = 0, V = 0, n_ctx = 0;
@@ -100,6 +123,8 @@ struct sb_engine {
     int * h_io = nullptr;
     uint64_t bytes_tok = 0;
     TpState tp;
+    int prompt_level = 0;             // sml_gpu_prompt_mode: >= 2 reads prompts on the tensor cores
+    PfState pf;
 };
 
 // ------------------------------------------------------------------ arena
@@ -343,6 +368,8 @@ static void close_all(sb_engine * e) {
     for (int p = 0; p < e->tp.n; p++)
         if (p != e->tp.rank && e->tp.peer[p]) cudaIpcCloseMemHandle(e->tp.peer[p]);
     if (e->tp.reg) cudaFree(e->tp.reg);
+    e->pf.ar.release();
+    if (e->pf.h_tok) cudaFreeHost(e->pf.h_tok);
     e->ar.release();
     if (e->h_logits) cudaFreeHost(e->h_logits);
     if (e->h_io) cudaFreeHost(e->h_io);
@@ -782,9 +809,183 @@ const float * sb_step(sb_engine * e, int tok, int pos) {
     return e->h_logits;
 }
 
+// ------------------------------------------------------------------ prompt chunks
+
+static int pf_split(int tiles, int nsb, int nsm) {
+    // superblock slices that fill the SMs: the fewest waves times the
+    // superblocks a CTA walks (plus about two per CTA)
+    int best = 1;
+    double bc = 1e30;
+    for (int sp = 1; sp <= nsb && sp <= kTcMaxSplit; sp++) {
+        if (tc_split(nsb, sp) != sp) continue;
+        const int per = (nsb + sp - 1) / sp, waves = (tiles * sp + nsm - 1) / nsm;
+        const double cost = waves * (per + 2.0) + (sp > 1 ? 0.25 : 0.0);
+        if (cost < bc - 1e-9) { bc = cost; best = sp; }
+    }
+    return best;
+}
+
+// One product of the chunk path: the tensors `recs` stacked (segments on 128
+// rows), re-quantized for the tensor cores (sizing pass: carve only).
+static bool pf_gemm(sb_engine * e, PfGemm & gm, const std::vector<const ssf_rec *> & recs, char * why, int nwhy) {
+    Arena & ar = e->pf.ar;
+    const ssf_rec * r0 = recs[0];
+    int rows_pad = 0;
+    for (const ssf_rec * r : recs) rows_pad += ((int) r->rows + 127) / 128 * 128;
+    gm.rows = recs.size() == 1 ? (int) r0->rows : rows_pad;
+    gm.cols = (int) r0->cols;
+    QT meta;
+    if (!upload_qt_meta(ar, e->f, r0, meta, why, nwhy)) return false;
+    gm.perm = meta.perm;
+    gm.p.rows_pad = rows_pad;
+    gm.p.nsb = (gm.cols / SSF_GROUP + 7) / 8;
+    gm.p.wblk = (uint8_t *) ar.carve((size_t) rows_pad * gm.p.nsb * 256);
+    gm.p.s8 = (float *) ar.carve((size_t) gm.p.nsb * rows_pad * 4);
+    gm.split = pf_split(rows_pad / 128, gm.p.nsb, e->nsm);
+    if (!gm.p.wblk) return true;
+    int off = 0;
+    for (const ssf_rec * r : recs) {
+        Arena tmp;
+        QT t;
+        bool ok = upload_qt(tmp, e->f, r, t, why, nwhy) && tmp.allocate() && upload_qt(tmp, e->f, r, t, why, nwhy);
+        ok = ok && tc_requant(t, gm.p, off, e->st) == cudaSuccess && cudaStreamSynchronize(e->st) == cudaSuccess;
+        tmp.release();
+        if (!ok) { if (!why[0]) snprintf(why, nwhy, "%.64s: re-quantization failed", r->name); return false; }
+        off += ((int) r->rows + 127) / 128 * 128;
+    }
+    return true;
+}
+
+static bool pf_layout(sb_engine * e, char * why, int nwhy) {
+    PfState & P = e->pf;
+    const ssf_file & f = e->f;
+    P.L.assign(e->n_layer, PfLayer());
+    for (int l = 0; l < e->n_layer; l++) {
+        auto R = [&](const char * fmt) { return ssf_findf(&f, fmt, l, 0); };
+        PfLayer & y = P.L[l];
+        if (!pf_gemm(e, y.qkv, {R("blk.%d.attn_q.weight"), R("blk.%d.attn_k.weight"), R("blk.%d.attn_v.weight")}, why, nwhy) ||
+            !pf_gemm(e, y.o, {R("blk.%d.attn_output.weight")}, why, nwhy) ||
+            !pf_gemm(e, y.gu, {R("blk.%d.ffn_gate.weight"), R("blk.%d.ffn_up.weight")}, why, nwhy) ||
+            !pf_gemm(e, y.dn, {R("blk.%d.ffn_down.weight")}, why, nwhy))
+            return false;
+    }
+    P.Fp = (e->F + 127) / 128 * 128;
+    P.qkv_ld = P.L[0].qkv.p.rows_pad;
+    int wide = e->E > e->qd ? e->E : e->qd;
+    wide = wide > e->F ? wide : e->F;
+    const int nsb = (wide / SSF_GROUP + 7) / 8;
+    P.x = (float *) P.ar.carve((size_t) kPfChunk * e->E * 4);
+    P.qkv = (float *) P.ar.carve((size_t) kPfChunk * P.qkv_ld * 4);
+    P.att = (float *) P.ar.carve((size_t) kPfChunk * e->qd * 4);
+    P.hid = (float *) P.ar.carve((size_t) kPfChunk * 2 * P.Fp * 4);
+    P.xblk = (uint8_t *) P.ar.carve((size_t) kPfChunk * nsb * 256);
+    P.xs = (float *) P.ar.carve((size_t) nsb * kPfChunk * 4);
+    P.tok = (int *) P.ar.carve((size_t) kPfChunk * 4);
+    return true;
+}
+
+// Make the chunk path on first use: dense decoders on one GPU whose q|k|v
+// segments need no padding (the fused product's rows are then the decode
+// engine's q|k|v order, biases included).
+static bool pf_ready(sb_engine * e) {
+    PfState & P = e->pf;
+    if (P.tried) return P.ok;
+    P.tried = true;
+    if (e->tp.n > 1 || e->qd % 128 || e->kvd % 128 || e->F <= 0) return false;
+    for (const LayerD & y : e->L) if (y.moe) return false;
+    char why[256] = {0};
+    if (!pf_layout(e, why, sizeof why) || !P.ar.allocate() || !pf_layout(e, why, sizeof why) ||
+        cudaMallocHost(&P.h_tok, kPfChunk * 4) != cudaSuccess) {
+        P.ar.release();
+        snprintf(g_err, sizeof g_err, "tensor-core prompt path unavailable: %s", why[0] ? why : "allocation failed");
+        return false;
+    }
+    P.ok = true;
+    return true;
+}
+
+template <int NB, int SIX>
+static void pf_embed(sb_engine * e, int T) {
+    k_embed_rows<NB, SIX><<<dim3((e->E + 255) / 256, T), 256, 0, e->st>>>(e->emb, e->pf.tok, e->pf.x, e->err);
+}
+
+// Positions pos0 .. pos0 + n - 1 of the prompt through the chunk path (the
+// cache rows written; no logits).
+static bool prefill_chunks(sb_engine * e, const int * ids, int pos0, int n) {
+    PfState & P = e->pf;
+    for (int c0 = 0; c0 < n; c0 += kPfChunk) {
+        const int T = n - c0 < kPfChunk ? n - c0 : kPfChunk, Tp = tc_tokens_pad(T), N = tc_tile_n(T);
+        if (!ck(cudaStreamSynchronize(e->st), "prefill")) return false;   // the staging buffer is reused
+        memcpy(P.h_tok, ids + c0, (size_t) T * 4);
+        if (!ck(cudaMemcpyAsync(P.tok, P.h_tok, (size_t) T * 4, cudaMemcpyHostToDevice, e->st), "prompt ids")) return false;
+        SB_DISPATCH_QT(e->emb.nbits, e->emb.six, pf_embed, e, T);
+        auto quant = [&](int mode, const PfGemm & gm, const float * x, int ldx, const float * gain, int up_off) {
+            TcQuantArgs q;
+            memset(&q, 0, sizeof q);
+            q.x = x; q.ldx = ldx; q.up_off = up_off; q.perm = gm.perm; q.gain = gain; q.eps = e->eps;
+            q.cols = gm.cols; q.T = T; q.T_pad = Tp; q.N = N; q.nsb = gm.p.nsb; q.xblk = P.xblk; q.xs = P.xs;
+            return tc_quant(mode, q, e->st);
+        };
+        auto mma = [&](const PfGemm & gm, float * y, int ldy, const float * bias, int acc) {
+            TcArgs a;
+            memset(&a, 0, sizeof a);
+            a.wblk = gm.p.wblk; a.s8 = gm.p.s8; a.xblk = P.xblk; a.xs = P.xs; a.y = y; a.ldy = ldy; a.bias = bias;
+            a.accumulate = acc; a.rows = gm.rows; a.rows_pad = gm.p.rows_pad; a.nsb = gm.p.nsb; a.T = T; a.T_pad = Tp;
+            a.split = gm.split; a.err = e->err;
+            return tc_mma(a, e->st);
+        };
+        for (int l = 0; l < e->n_layer; l++) {
+            const LayerD & y = e->L[l];
+            const PfLayer & z = P.L[l];
+            uint16_t * kc = e->kc + (size_t) l * e->n_ctx * e->kvd, * vc = e->vc + (size_t) l * e->n_ctx * e->kvd;
+            cudaError_t r = quant(TQ_NORM, z.qkv, P.x, e->E, y.an, 0);
+            if (r == cudaSuccess) r = mma(z.qkv, P.qkv, P.qkv_ld, y.qkv_b, 0);
+            if (r == cudaSuccess) {
+                auto kk = e->hd == 64 ? k_chunk_kv<64> : e->hd == 128 ? k_chunk_kv<128> : k_chunk_kv<256>;
+                kk<<<dim3(e->nkv, T), 128, 0, e->st>>>(P.qkv, P.qkv_ld, e->qd, e->kvd, y.kn, e->eps, e->rcos, e->rsin,
+                                                      kc, vc, pos0 + c0);
+                r = cudaGetLastError();
+            }
+            if (r == cudaSuccess) {
+                AttnArgs a;
+                memset(&a, 0, sizeof a);
+                a.qkv = P.qkv; a.qkv_ld = P.qkv_ld; a.n_head = e->nh; a.n_kv = e->nkv; a.hd = e->hd; a.qd = e->qd;
+                a.kvd = e->kvd; a.qn = y.qn; a.kn = y.kn; a.eps = e->eps; a.rcos = e->rcos; a.rsin = e->rsin;
+                a.kc = kc; a.vc = vc; a.n_ctx = e->n_ctx; a.pos = nullptr; a.pos_imm = pos0 + c0; a.scale = e->scale;
+                a.out = P.att; a.out_ld = e->qd; a.err = e->err; a.xtab = e->xtab; a.xnear = e->xnear;
+                auto ka = e->hd == 64 ? k_attn_seq<64> : e->hd == 128 ? k_attn_seq<128> : k_attn_seq<256>;
+                ka<<<dim3(e->nh, T), kSeqThreads, attn_seq_smem_bytes(e->hd, e->n_ctx), e->st>>>(a);
+                r = cudaGetLastError();
+            }
+            if (r == cudaSuccess) r = quant(TQ_PLAIN, z.o, P.att, e->qd, nullptr, 0);
+            if (r == cudaSuccess) r = mma(z.o, P.x, e->E, nullptr, 1);
+            if (r == cudaSuccess) r = quant(TQ_NORM, z.gu, P.x, e->E, y.fn, 0);
+            if (r == cudaSuccess) r = mma(z.gu, P.hid, 2 * P.Fp, nullptr, 0);
+            if (r == cudaSuccess) r = quant(TQ_SILU, z.dn, P.hid, 2 * P.Fp, nullptr, P.Fp);
+            if (r == cudaSuccess) r = mma(z.dn, P.x, e->E, nullptr, 1);
+            if (!ck(r, "prompt chunk")) return false;
+        }
+    }
+    return true;
+}
+
+int sb_set_prompt_mode(sb_engine * e, int level) {
+    if (!e) return 0;
+    e->prompt_level = level < 0 ? 0 : level > 2 ? 2 : level;
+    return e->prompt_level;
+}
+
 const float * sb_prefill(sb_engine * e, const int * ids, int pos0, int n) {
     if (!e || n <= 0 || pos0 < 0 || pos0 + n > e->n_ctx) return nullptr;
-    for (int i = 0; i < n; i++) {
+    for (int i = 0; i < n; i++)
+        if (ids[i] < 0 || ids[i] >= e->V) return nullptr;
+    int i0 = 0;
+    if (e->prompt_level >= 2 && n >= 2 && pf_ready(e)) {
+        // every token but the last through the chunk path, then the last stepped
+        if (!prefill_chunks(e, ids, pos0, n - 1)) return nullptr;
+        i0 = n - 1;
+    }
+    for (int i = i0; i < n; i++) {
         if (ids[i] < 0 || ids[i] >= e->V) return nullptr;
         // each token's id must reach the device before its graph runs; every
         // staging slot is its own pinned word, reused only after a sync
