@@ -332,10 +332,13 @@ def main():
             extras = {"decode_cfg3_tp": d3, "moe_cfg2_ep": ep}
     if rank == 0 and world == 1:
         peak0, _ = peaks()
+        from sheep_b200 import configs as cf
         extras = {"l2": "a 512 MB buffer rewritten before each timed run (decode: weights > L2)",
                   "gemv_cfg1": gemv_microbench(peak0), "gemm_tc_cfg1": gemm_tc_microbench(peak0),
                   "moe_cfg2": moe_microbench(peak0),
-                  "decode_cfg3": decode_cfg3(peak0), "decode_cfg3_batch64": decode_cfg3_batch(peak0)}
+                  "decode_cfg3": decode_cfg3(peak0), "decode_cfg3_batch64": decode_cfg3_batch(peak0),
+                  "prefill_cfg0": prefill_bench(model_path(cf.CONFIGS["qwen2.5-1.5b-q4"], 0, None), PROMPT_LEN),
+                  "prefill_cfg3": prefill_bench(model_path(cf.CONFIGS["llama3-8b-q4k"], 0, None), 2048)}
 
     if rank == 0:
         peak, peak_kind = peaks()
@@ -378,6 +381,38 @@ def main():
 def fp16_rows(seed, n, cols):
     """fp16 N(0, 1) activations as float32 rows."""
     return np.random.default_rng(seed).standard_normal((n, cols)).astype(np.float16).astype(np.float32)
+
+
+def prefill_bench(path, n_prompt, ngen=12):
+    """Prompt reading: tok/s of sb_prefill over a random n_prompt-id prompt,
+    stepped (prompt level 0) and in tensor-core chunks (level 2), each after one
+    untimed read; and the 12 greedy ids after the prompt both ways (the
+    reference server's check of a batched prompt path)."""
+    import sheep_b200
+    eng = sheep_b200.Engine(path, n_ctx=n_prompt + ngen + 8)
+    out = {"prompt": n_prompt}
+    try:
+        prompt = np.random.default_rng(2048).integers(0, eng.n_vocab, n_prompt).astype(np.int32)
+        ids = {}
+        for level in (0, 2):
+            eng.prompt_mode(level)
+            eng.prefill(prompt, 0)
+            t0 = time.perf_counter()
+            lg = eng.prefill(prompt, 0)
+            dt = time.perf_counter() - t0
+            got, pos = [], n_prompt
+            for _ in range(ngen):
+                got.append(int(np.argmax(lg)))
+                lg = eng.step(got[-1], pos)
+                pos += 1
+            ids[level] = got
+            out[f"level{level}_tok_s"] = round(n_prompt / dt, 1)
+            out[f"level{level}_ms"] = round(dt * 1000.0, 2)
+        out["ids_after_prompt_equal"] = int(sum(a == b for a, b in zip(ids[0], ids[2])))
+        out["ids_compared"] = ngen
+    finally:
+        eng.close()
+    return out
 
 
 def gemv_microbench(peak, reps=20):

@@ -47,6 +47,11 @@ const float * sb_step(sb_engine * e, int tok, int pos);
 // use, per-256 activations; attention the decode kernel's), then steps the last.
 const float * sb_prefill(sb_engine * e, const int * ids, int pos0, int n);
 int sb_set_prompt_mode(sb_engine * e, int level);   // returns the level set (0..2)
+// The cached key and value rows of (layer, pos) (n_head_kv * head_dim fp16
+// each), for checks; and the superblock slices of the tensor-core prompt
+// products (q|k|v, o, gate|up, down, and 1 for the unused head).
+int sb_kv_rows(const sb_engine * e, int layer, int pos, uint16_t * k, uint16_t * v);
+int sb_prompt_splits(sb_engine * e, int * out5);
 // Greedy decode with the choice made on the device (the reference's
 // graph-replay benchmark loop, sml/sml-gpu-fwd.c:2626-2662): host prompt in,
 // ngen host ids out. Returns 1, or 0 on failure.

@@ -54,6 +54,8 @@ def lib():
         "sb_open_tp": (vp, [cp, ip, ip, ip, cp, ip]),
         "sb_tp_handle": (ip, [vp, vp]),
         "sb_set_prompt_mode": (ip, [vp, ip]),
+        "sb_kv_rows": (ip, [vp, ip, ip, vp, vp]),
+        "sb_prompt_splits": (ip, [vp, vp]),
         "sb_tp_connect": (ip, [vp, vp, cp, ip]),
         "sb_close": (None, [vp]),
         "sb_info": (None, [vp, vp]),
@@ -183,6 +185,20 @@ class Engine:
         """sml_gpu_prompt_mode on this engine: 0/1 step the prompt, 2 reads it in
         tensor-core chunks (all but the last token). Returns the level set."""
         return lib().sb_set_prompt_mode(self.h, int(level))
+
+    def kv_rows(self, layer, pos):
+        """The cached key and value rows of (layer, pos), fp16 bit patterns."""
+        kvd = self.n_head_kv * self.head_dim
+        k, v = np.zeros(kvd, np.uint16), np.zeros(kvd, np.uint16)
+        if not lib().sb_kv_rows(self.h, int(layer), int(pos), _p(k), _p(v)):
+            raise RuntimeError("sb_kv_rows failed")
+        return k, v
+
+    def prompt_splits(self):
+        out = (ctypes.c_int * 5)()
+        if not lib().sb_prompt_splits(self.h, out):
+            raise RuntimeError(f"no tensor-core prompt path: {lib().sb_last_error().decode()}")
+        return list(out)
 
     def prefill(self, ids, pos0=0):
         ids = np.ascontiguousarray(ids, dtype=np.int32)

@@ -969,6 +969,20 @@ static bool prefill_chunks(sb_engine * e, const int * ids, int pos0, int n) {
     return true;
 }
 
+int sb_kv_rows(const sb_engine * e, int layer, int pos, uint16_t * k, uint16_t * v) {
+    if (!e || layer < 0 || layer >= e->n_layer || pos < 0 || pos >= e->n_ctx || !k || !v) return 0;
+    const size_t at = ((size_t) layer * e->n_ctx + pos) * e->kvd;
+    return cudaMemcpy(k, e->kc + at, (size_t) e->kvd * 2, cudaMemcpyDeviceToHost) == cudaSuccess &&
+           cudaMemcpy(v, e->vc + at, (size_t) e->kvd * 2, cudaMemcpyDeviceToHost) == cudaSuccess;
+}
+
+int sb_prompt_splits(sb_engine * e, int * out5) {
+    if (!e || !out5 || !pf_ready(e)) return 0;
+    const PfLayer & z = e->pf.L[0];
+    out5[0] = z.qkv.split; out5[1] = z.o.split; out5[2] = z.gu.split; out5[3] = z.dn.split; out5[4] = 1;
+    return 1;
+}
+
 int sb_set_prompt_mode(sb_engine * e, int level) {
     if (!e) return 0;
     e->prompt_level = level < 0 ? 0 : level > 2 ? 2 : level;

@@ -98,3 +98,42 @@ def test_prefill_continues_a_cached_prefix():
     # in the whole one: the same up to the batched arithmetic's noise
     assert helpers.rel_rms(whole, parts) <= 6e-2
     assert int(np.argmax(whole)) == int(np.argmax(parts)) or helpers.agree_with_ties(whole, parts)[0]
+
+
+@pytest.mark.parametrize("cfg,over", [("tiny-q4", {}), ("small-q4-tied", dict(qk_norm=1))])
+def test_prefill_cache_rows_equal_batched_restatement(cfg, over):
+    """The chunk path is the batched arithmetic exactly: the cache rows it
+    writes equal the CPU restatement's (so_batch mode 1: the same int8 products
+    with the same superblock slices, the same per-256 activations, the
+    reference-order attention) bit for bit -- every layer of a prompt read in
+    two chunks, and layer 0 of a continuation at pos0."""
+    spec = sheep_b200.spec_for(cfg, **over)
+    path = helpers.model_path(spec)
+    prompt = np.random.default_rng(73).integers(0, spec["n_vocab"], 75).astype(np.int32)
+    eng = sheep_b200.Engine(path, n_ctx=96)
+    try:
+        eng.prompt_mode(2)
+        splits = eng.prompt_splits()
+        eng.prefill(prompt[:67], 0)      # rows 0..65 in chunks of 64 and 2, 66 stepped
+        eng.prefill(prompt[67:], 67)     # rows 67..73 in one chunk, 74 stepped
+        kvd = spec["n_head_kv"] * spec["head_dim"]
+        got = {(l, p): eng.kv_rows(l, p) for l in range(spec["n_layer"]) for p in range(75)}
+    finally:
+        eng.close()
+    orc = helpers.Oracle(path, 96)
+    ob = helpers.OracleBatch(orc, 1, 1, splits)
+    try:
+        for p, t in enumerate(prompt):
+            ob.step(np.array([t], np.int32), np.array([p], np.int32))
+        # rows 66 and 74 the decode arithmetic wrote (the restatement writes them
+        # in the batched one); a later row of layer >= 1 attends to row 66 of
+        # the layer below, so past it only layer 0 (the token's own row) compares
+        for l in range(spec["n_layer"]):
+            for p in range(75):
+                if p in (66, 74) or (l > 0 and p > 66):
+                    continue
+                k, v = ob.kv(l, 0, p, kvd)
+                assert np.array_equal(got[(l, p)][0], k) and np.array_equal(got[(l, p)][1], v), (l, p)
+    finally:
+        ob.close()
+        orc.close()
