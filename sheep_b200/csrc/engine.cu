@@ -315,7 +315,8 @@ static void enqueue_token(sb_engine * e) {
             // router on rmsnorm(x), experts, combine added to x (sml/sml-run.c:3503-3507)
             snprintf(e->cur, sizeof e->cur, "L%d.moe", l);
             moe_enqueue(y.ml, e->ms, e->x, 1, y.fn, e->eps, e->x, 1, e->nsm, e->st, true, e->err, e->trace,
-                        e->launches, [&](cudaError_t r, const char *) { after_launch(e, r); });
+                        e->launches, [&](cudaError_t r, const char *) { after_launch(e, r); }, nullptr, e->xtab,
+                        e->xnear);
             continue;
         }
         snprintf(e->cur, sizeof e->cur, "L%d.ffn", l);

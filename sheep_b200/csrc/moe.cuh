@@ -14,7 +14,8 @@
 //                  chunks of at most NT tokens of one expert.
 //   k_moe_gemv     the tile ring of tgemv.cuh over work items (chunk, tile):
 //                  the weights of a chunk's expert are read once for all of its
-//                  tokens; each lane keeps NT row sums. GU mode fuses SiLU and
+//                  tokens; each lane keeps NT row sums (one token per chunk:
+//                  the reference's float order, tile_exact). GU mode fuses SiLU and
 //                  scatters the hidden vector into the expert's down order; DN
 //                  mode writes one output row per slot; PLAIN is a batched GEMV
 //                  of one tensor over T input rows.
@@ -55,6 +56,8 @@ struct MoeRouterArgs {
     int T, E, ne, k, nt;             // nt: most tokens in one chunk
     unsigned flags;                  // bit 0: softmax over the chosen experts only
     int e_lo, e_hi;                  // experts this GPU holds: only their slots are dispatched
+    const ExpfEntry * xtab;          // the host libm's expf (expf_libm.h), or NULL
+    float xnear;
     MoeRoute r;
     int * err;
     unsigned long long * trace;
@@ -83,8 +86,10 @@ struct MoeGArgs {
 // Route one token with one warp (sml/sml-run.c:3009-3030, the plain softmax
 // branch): k rounds of a warp argmax over the experts not yet taken, ties to
 // the lower index; weights exp(l_j - l_0) / sum over the chosen (flags bit 0)
-// or the softmax over every expert, sums in double.
-SB_DEV void route_warp(const float * lg, int ne, int k, unsigned flags, int * sel, float * w, int lane) {
+// or the softmax over every expert, sums in double; exp as the host libm
+// rounds it when xtab is given (expf_libm.h), else rounded from double.
+SB_DEV void route_warp(const float * lg, int ne, int k, unsigned flags, int * sel, float * w, int lane,
+                       const ExpfEntry * xtab = nullptr, float xnear = 0.0f) {
     constexpr int kQ = kMoeMaxExperts / 32;
     float v[kQ];
 #pragma unroll
@@ -116,7 +121,7 @@ SB_DEV void route_warp(const float * lg, int ne, int k, unsigned flags, int * se
     if (flags & 1u) {
         double sum = 0.0;
         float wf[kMoeMaxK];
-        for (int j = 0; j < k; j++) { wf[j] = expf(ls[j] - ls[0]); sum += (double) wf[j]; }
+        for (int j = 0; j < k; j++) { wf[j] = expf_libm(__fsub_rn(ls[j], ls[0]), xtab, xnear); sum += (double) wf[j]; }
         if (lane == 0)
             for (int j = 0; j < k; j++) { sel[j] = s[j]; w[j] = (float) ((double) wf[j] / sum); }
     } else {
@@ -126,10 +131,10 @@ SB_DEV void route_warp(const float * lg, int ne, int k, unsigned flags, int * se
         mx = warp_max(mx);
         double sum = 0.0;
 #pragma unroll
-        for (int q = 0; q < kQ; q++) if (q * 32 + lane < ne) sum += (double) expf(v[q] - mx);
+        for (int q = 0; q < kQ; q++) if (q * 32 + lane < ne) sum += (double) expf_libm(__fsub_rn(v[q], mx), xtab, xnear);
         sum = warp_sum_d(sum);
         if (lane == 0)
-            for (int j = 0; j < k; j++) { sel[j] = s[j]; w[j] = (float) ((double) expf(ls[j] - mx) / sum); }
+            for (int j = 0; j < k; j++) { sel[j] = s[j]; w[j] = (float) ((double) expf_libm(__fsub_rn(ls[j], mx), xtab, xnear) / sum); }
     }
 }
 
@@ -263,7 +268,7 @@ static __global__ void __launch_bounds__(kRouterThreads) k_moe_router(const __gr
     SB_MARK(g.trace, g.launch_id, 1);
     for (int t = warp; t < g.T; t += kRouterThreads / 32)
         route_warp(g.r.logits + (size_t) t * g.ne, g.ne, g.k, g.flags, g.r.sel + (size_t) t * g.k,
-                   g.r.w + (size_t) t * g.k, lane);
+                   g.r.w + (size_t) t * g.k, lane, g.xtab, g.xnear);
     __syncthreads();
     moe_dispatch(g);
     if (tid == 0) *g.r.cnt = 0;
@@ -277,8 +282,9 @@ static __global__ void k_moe_route(const float * lg, int T, int ne, int k, unsig
     route_warp(lg + (size_t) t * ne, ne, k, flags, sel + (size_t) t * k, w + (size_t) t * k, threadIdx.x & 31);
 }
 
-// y[t][i] = sum_j w[t][j] * yk[t*k + j][i] in choice order (sml/sml-run.c:3121),
-// added to y[t][i] when resid (the layer's residual add).
+// y[t][i] = sum_j w[t][j] * yk[t*k + j][i] in choice order from 0, each step
+// one fused multiply-add as gcc contracts acc += w*t (sml/sml-run.c:3120),
+// added to y[t][i] when resid (the layer's residual add, x + xb).
 static __global__ void k_moe_comb(const float * yk, const float * w, int T, int k, int E, float * y, int resid) {
     pdl_launch_dependents();
     pdl_wait();
@@ -286,7 +292,7 @@ static __global__ void k_moe_comb(const float * yk, const float * w, int T, int 
     if (i >= E || t >= T) return;
     float acc = 0.0f;
     for (int j = 0; j < k; j++)
-        acc = __fadd_rn(acc, __fmul_rn(w[(size_t) t * k + j], yk[((size_t) t * k + j) * E + i]));
+        acc = __fmaf_rn(w[(size_t) t * k + j], yk[((size_t) t * k + j) * E + i], acc);
     float * o = y + (size_t) t * E + i;
     *o = resid ? __fadd_rn(*o, acc) : acc;
 }
@@ -347,8 +353,10 @@ SB_DEV int dp4a_us(uint32_t a, uint32_t b, int c) {
 
 // Lane share of tile row j for up to NT activations at once (the activations
 // of one chunk, act_b bytes apart): the codes and fields of a unit are read
-// once and used for every token. Same integers and the same float epilogue as
-// tile_row, token by token.
+// once and used for every token. The integers are exact; the float epilogue
+// is summed per unit (lane l: row l % TR, units l / TR + k * (32 / TR)) and
+// the lanes' shares are added by the caller -- another order than the
+// reference's, within its rounding (the one-token path is exact: tile_exact).
 template <int NB, int SIX, int NT>
 SB_DEV void tile_row_nt(const uint8_t * tile, const TileGeom & tg, uint8_t * act0, uint32_t act_b, int n, int ntok,
                         int j, int u0, int step, bool has_min, float mbias, float (&acc)[NT]) {
@@ -453,7 +461,11 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_moe_gemv(const __grid_constan
     const TT & t = g.t;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, ns = g.nstage, n = t.cols;
     const uint32_t act_b = (uint32_t) ((act_smem_bytes(n) + 127) / 128 * 128);
-    uint8_t * ring = smem + (size_t) NT * act_b;
+    // one token per chunk: the rows in the reference's float order (tile_exact),
+    // each warp's group dots in a scratch after the activation
+    const uint32_t dscr = NT == 1 ? (tg_dot_bytes(t) + 127) / 128 * 128 : 0u;
+    int * D = reinterpret_cast<int *>(smem + (size_t) NT * act_b) + (size_t) warp * (tg_dot_bytes(t) / kConsWarps / 4);
+    uint8_t * ring = smem + (size_t) NT * act_b + dscr;
     if (threadIdx.x == 0) {
         for (int s = 0; s < ns; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         mbar_fence_init();
@@ -499,13 +511,13 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_moe_gemv(const __grid_constan
         const int k0 = q - q0, k1 = qe - q0;
         for (int k = k0 + (((warp - k0) % kConsWarps) + kConsWarps) % kConsWarps; k < k1; k += kConsWarps) {
             const int s = k % ns, i = q0 + k - c * ntl;
-            const bool ok = !failed && ring_wait(full, empty, k, ns, g.err);
+            const bool ok = __all_sync(0xffffffffu, !failed && ring_wait(full, empty, k, ns, g.err));
             failed = !ok;
             float acc[NT];
             if (ok) {
                 if (NT == 1) {
                     ActS a = act_carve(smem, n);
-                    acc[0] = tile_row<NB, SIX>(ring + (size_t) s * t.tb, tg, a, j, v, VS, t.has_min, t.mbias, g.err);
+                    acc[0] = tile_exact<NB, SIX>(ring + (size_t) s * t.tb, tg, a, D, t.has_min, t.mbias);
                 } else {
                     tile_row_nt<NB, SIX, NT>(ring + (size_t) s * t.tb, tg, smem, act_b, n, ntok, j, v, VS,
                                              t.has_min, t.mbias, acc);
@@ -520,7 +532,8 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_moe_gemv(const __grid_constan
             for (int tt = 0; tt < NT; tt++) {
                 if (tt >= ntok) break;
                 float a = acc[tt];
-                for (int o = 16; o >= TR; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
+                if (NT > 1)
+                    for (int o = 16; o >= TR; o >>= 1) a += __shfl_xor_sync(0xffffffffu, a, o);
                 if (MODE == MG_GU) {
                     const float up = __shfl_down_sync(0xffffffffu, a, TR / 2);
                     const int idx = i * (TR / 2) + lane;
@@ -542,8 +555,14 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_moe_gemv(const __grid_constan
 template <int MODE, int NB, int SIX, int NT>
 cudaError_t moe_gemv_launch(const MoeGArgs & g, int grid, size_t smem, cudaStream_t st, bool pdl);
 
+// The group-dot scratch of the one-token (exact) expert GEMV.
+__host__ __device__ inline size_t moe_dot_smem(const TT & t, int nt) {
+    return nt == 1 ? (tg_dot_bytes(t) + 127) / 128 * 128 : 0;
+}
+
 __host__ inline size_t moe_gemv_smem(const MoeGArgs & g, int nt) {
-    return (size_t) nt * ((act_smem_bytes(g.t.cols) + 127) / 128 * 128) + (size_t) g.nstage * g.t.tb;
+    return (size_t) nt * ((act_smem_bytes(g.t.cols) + 127) / 128 * 128) + moe_dot_smem(g.t, nt) +
+           (size_t) g.nstage * g.t.tb;
 }
 
 }  // namespace sb

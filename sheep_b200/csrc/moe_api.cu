@@ -61,6 +61,8 @@ struct sb_moe {
     MoeScratch s;
     float * x = nullptr, * y = nullptr;   // device rows [T][E]
     int * err = nullptr;
+    const ExpfEntry * xtab = nullptr;     // the host libm's expf corrections (expf_libm.h)
+    float xnear = 0.0f;
     int nsm = 148, tmax = 0, layer = 0;
     cudaStream_t st = nullptr;
     void * flush = nullptr;               // timing: a buffer larger than L2, rewritten between runs
@@ -96,6 +98,10 @@ static bool moe_build(sb_moe * h, char * why, int nwhy) {
     h->x = (float *) h->ar.carve((size_t) h->tmax * h->m.E * 4);
     h->y = (float *) h->ar.carve((size_t) h->tmax * h->m.E * 4);
     h->err = (int *) h->ar.carve(4);
+    const ExpfTable & xt = expf_libm_table();
+    if (xt.slots.empty()) { snprintf(why, nwhy, "this libm's expf differs from the rounded exponential too often"); return false; }
+    h->xtab = (const ExpfEntry *) h->ar.upload(xt.slots.data(), xt.slots.size() * sizeof(ExpfEntry));
+    h->xnear = xt.near;
     return true;
 }
 
@@ -209,7 +215,7 @@ static bool enqueue(sb_moe * h, const float * x, int T, float * y, cudaStream_t 
                         ok = false;
                     }
                 },
-                h->world > 1 ? &h->ex : nullptr);
+                h->world > 1 ? &h->ex : nullptr, h->xtab, h->xnear);
     return ok;
 }
 

@@ -164,7 +164,9 @@ inline void moe_carve(Arena & a, const MoeLayer & m, int T, MoeScratch & s) {
 }
 
 // Ring stages of the grouped GEMV for nt staged activations.
-inline int moe_stages(const TT & t, int nt) { return ring_stages((size_t) nt * moe_act_bytes(t.cols), t.tb); }
+inline int moe_stages(const TT & t, int nt) {
+    return ring_stages((size_t) nt * moe_act_bytes(t.cols) + moe_dot_smem(t, nt), t.tb);
+}
 
 template <int NB, int SIX>
 inline void moe_gemv_w(int mode, int nt, const MoeGArgs & g, int grid, size_t smem, cudaStream_t st, bool pdl,
@@ -207,7 +209,8 @@ struct MoeExchange {
 template <class Post>
 inline void moe_enqueue(const MoeLayer & m, const MoeScratch & s, const float * x, int T, const float * norm_w,
                         float eps, float * y, int resid, int nsm, cudaStream_t st, bool pdl, int * err,
-                        unsigned long long * trace, int launch_id, Post post, const MoeExchange * ex = nullptr) {
+                        unsigned long long * trace, int launch_id, Post post, const MoeExchange * ex = nullptr,
+                        const ExpfEntry * xtab = nullptr, float xnear = 0.0f) {
     const int nt = T == 1 ? 1 : 8;   // one token per chunk at T = 1: a token never picks an expert twice
     if (ex) post(cudaMemsetAsync(s.yk, 0, (size_t) T * m.k * m.E * 4, st), "moe.zero");
     {
@@ -216,6 +219,7 @@ inline void moe_enqueue(const MoeLayer & m, const MoeScratch & s, const float * 
         r.x = x; r.norm_w = norm_w; r.eps = eps; r.xn = norm_w ? s.xn : nullptr; r.wr = m.router;
         r.T = T; r.E = m.E; r.ne = m.ne; r.k = m.k; r.nt = nt; r.flags = m.flags; r.r = s.r;
         r.e_lo = m.e_lo; r.e_hi = m.e_hi;
+        r.xtab = xtab; r.xnear = xnear;
         r.err = err; r.trace = trace; r.launch_id = launch_id;
         static bool attr = false;
         if (!attr) {

@@ -468,53 +468,13 @@ SB_DEV void tile_fields(const uint8_t * f, int (&v)[4]) {
     }
 }
 
-// Lane share of tile row j: units u = u0, u0 + step, ...
-template <int NB, int SIX>
-SB_DEV float tile_row(const uint8_t * tile, const TileGeom & tg, const ActS & a, int j, int u0, int step,
-                      bool has_min, float mbias, int * err) {
-    float acc = 0.0f;
-    if (!SB_CHECK(err, j < tg.TR && u0 >= 0 && step > 0, 101)) return 0.0f;
-    for (int u = u0; u < tg.U; u += step) {
-        if (!SB_CHECK(err, (u * tg.TR + j) * 16 + 16 <= (int) tg.pl_sec[0] || tg.pl_kind[0] != 4, 102)) return acc;
-        if (!SB_CHECK(err, 3 * (a.n >> 2) + 16 * u + 16 <= a.n, 103)) return acc;
-        if (!SB_CHECK(err, ((u >> 1) * tg.TR + j) * (int) tg.f_w + (int) tg.f_w + (int) tg.sq_off <= (int) tg.bytes, 104)) return acc;
-        if (!SB_CHECK(err, ((u >> 2) * tg.TR + j) * 2 + 2 + (int) tg.sd_off <= (int) tg.bytes, 105)) return acc;
-        uint4 av[4];
-#pragma unroll
-        for (int k = 0; k < 4; k++) av[k] = *reinterpret_cast<const uint4 *>(a.q + k * (a.n >> 2) + 16 * u);
-        int d[4];
-        tile_dots<NB>(tile, tg, j, u, av, d);
-        const int pq = u >> 1;
-        const float4 xs = *reinterpret_cast<const float4 *>(a.xs + 4 * pq);
-        int sq[4];
-        tile_fields<SIX>(tile + tg.sq_off + (pq * tg.TR + j) * tg.f_w, sq);
-        const float sd = h2f(*reinterpret_cast<const uint16_t *>(tile + tg.sd_off + ((u >> 2) * tg.TR + j) * 2));
-        float t1 = (float) sq[0] * xs.x * (float) d[0];
-        t1 += (float) sq[1] * xs.y * (float) d[1];
-        t1 += (float) sq[2] * xs.z * (float) d[2];
-        t1 += (float) sq[3] * xs.w * (float) d[3];
-        acc += sd * t1;
-        if (has_min && (u & 1) == 0) {
-            const float4 xm = *reinterpret_cast<const float4 *>(a.xsum + 4 * pq);
-            int mq[4];
-            tile_fields<SIX>(tile + tg.mq_off + (pq * tg.TR + j) * tg.f_w, mq);
-            const float md = h2f(*reinterpret_cast<const uint16_t *>(tile + tg.md_off + ((u >> 2) * tg.TR + j) * 2));
-            float t2 = ((float) mq[0] - mbias) * xm.x;
-            t2 += ((float) mq[1] - mbias) * xm.y;
-            t2 += ((float) mq[2] - mbias) * xm.z;
-            t2 += ((float) mq[3] - mbias) * xm.w;
-            acc += md * t2;
-        }
-    }
-    return acc;
-}
-
 // ---------------------------------------------------------------- exact epilogue
 //
 // tile_exact: the rows of one tile, each as the reference computes it.
 //
-// Phase A: the warp's lanes take the tile's units as tile_row does (lane l: row
-// l % TR, units l / TR + k * (32 / TR)) and compute each unit's 4 group dots
+// Phase A: the warp's lanes take the tile's units (lane l: row l % TR, units
+// l / TR + k * (32 / TR), so a warp's reads are consecutive 16-byte words) and
+// compute each unit's 4 group dots
 // per dot array, exact in integers. The two halves of a group (units 2p and
 // 2p+1) sit in lanes l and l ^ TR and are added by one shuffle; the even lane
 // stores the 4 full dots into the warp's scratch D[array][row][group].
