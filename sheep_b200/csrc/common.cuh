@@ -131,14 +131,26 @@ SB_DEV void bulk_g2s(void * dst, const void * src, uint32_t bytes, uint64_t * ba
 // Named barrier over the first `n` threads (a subset of the block).
 SB_DEV void bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(n) : "memory"); }
 
-// Timestamps of the trace build (-DSB_TRACE): thread 0 of each CTA writes the
-// global timer into trace[(launch * kTraceCtas + blockIdx) * 8 + slot].
+// Timestamps of the trace build (-DSB_TRACE): thread 0 of each CTA writes
+// trace[(launch * kTraceCtas + blockIdx) * 8 + slot]: slot 0 the global timer
+// at entry, later slots that time plus the SM cycles since, at the nominal
+// 1965 MHz (finer than the global timer's steps).
 constexpr int kTraceCtas = 160;
 #ifdef SB_TRACE
+SB_DEV unsigned long long & trace_ns0() { __shared__ unsigned long long v; return v; }
+SB_DEV long long & trace_clk0() { __shared__ long long v; return v; }
+SB_DEV unsigned long long trace_now(int slot) {
+    if (slot == 0) {
+        trace_clk0() = clock64();
+        trace_ns0() = global_ns();
+        return trace_ns0();
+    }
+    return trace_ns0() + (unsigned long long) ((clock64() - trace_clk0()) * 1000 / 1965);
+}
 #define SB_MARK(tr, launch, slot)                                                              \
     do {                                                                                       \
         if ((tr) && threadIdx.x == 0 && blockIdx.y == 0 && blockIdx.x < kTraceCtas)            \
-            (tr)[((size_t) (launch) * kTraceCtas + blockIdx.x) * 8 + (slot)] = global_ns();    \
+            (tr)[((size_t) (launch) * kTraceCtas + blockIdx.x) * 8 + (slot)] = trace_now(slot); \
     } while (0)
 #else
 #define SB_MARK(tr, launch, slot) do { } while (0)

@@ -175,26 +175,16 @@ static void launch_embed(sb_engine * e, const QT & t) {
            e->tp.tok_seq);
 }
 
-template <int MODE, int NB, int SIX>
-static void launch_tg_t(sb_engine * e, const TGArgs & g, int grid, size_t smem) {
+template <int NB, int SIX>
+static void launch_tg_nb(sb_engine * e, int mode, const TGArgs & g0, int grid, size_t smem) {
     static bool attr = false;
     if (!attr) {
-        cudaFuncSetAttribute(k_tgemv<MODE, NB, SIX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kSmemBudget);
+        cudaFuncSetAttribute(k_tgemv<NB, SIX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kSmemBudget);
         attr = true;
     }
-    launch(e, true, k_tgemv<MODE, NB, SIX>, dim3(grid), dim3(kTgThreads), smem, g);
-}
-
-template <int NB, int SIX>
-static void launch_tg_nb(sb_engine * e, int mode, const TGArgs & g, int grid, size_t smem) {
-    switch (mode) {
-    case GM_QKV: launch_tg_t<GM_QKV, NB, SIX>(e, g, grid, smem); break;
-    case GM_O: launch_tg_t<GM_O, NB, SIX>(e, g, grid, smem); break;
-    case GM_FFN: launch_tg_t<GM_FFN, NB, SIX>(e, g, grid, smem); break;
-    case GM_DOWN: launch_tg_t<GM_DOWN, NB, SIX>(e, g, grid, smem); break;
-    case GM_HEAD: launch_tg_t<GM_HEAD, NB, SIX>(e, g, grid, smem); break;
-    default: launch_tg_t<GM_PLAIN, NB, SIX>(e, g, grid, smem); break;
-    }
+    TGArgs g = g0;
+    g.mode = mode;
+    launch(e, true, k_tgemv<NB, SIX>, dim3(grid), dim3(kTgThreads), smem, g);
 }
 
 static TGArgs tg_args(sb_engine * e, const TT & t, const float * in, const float * nw, float * out) {
@@ -389,9 +379,18 @@ static bool build(sb_engine * e, char * why, int nwhy) {
     if (!hr) hr = er;   // tied head (Qwen2.5): the embedding is streamed as the head
     const int min_tiles = 6 * e->nsm;
     constexpr int kTileCap = 12288;
-    auto tr_for = [&](const ssf_rec * r, int rows, int even) {
-        return pick_tr(rows, (int) tile_geom((int) r->cols, 1, (int) r->nbits, e->six, r->mq_n != 0).bytes, min_tiles,
-                       even, kTileCap);
+    // in_perm: the input arrives in the tensor's column order (no gather);
+    // has_norm: an RMSNorm gain is staged with it
+    auto tr_for = [&](const ssf_rec * r, int rows, int even, int in_perm = 0, int has_norm = 1) {
+        const int n = (int) r->cols, six = e->six, hm = r->mq_n != 0;
+        int tr = pick_tr(rows, (int) tile_geom(n, 1, (int) r->nbits, six, hm).bytes, min_tiles, even, kTileCap);
+        // short 4-bit rows: at least 4 a tile where a ring of 8 such tiles
+        // fits, so tile_q4 keeps all 32 lanes of a warp busy (long rows keep
+        // one or two a tile: more tiles in flight, tile_q4s splits the chains)
+        if (r->nbits == 4 && tr < 4 && rows >= 4 && n <= 4096 &&
+            ring_stages(stage_layout(n, !in_perm, has_norm, 0, 0).ring_off, tile_geom(n, 4, 4, six, hm).bytes) > 0)
+            tr = 4;
+        return tr;
     };
     const int tp = e->tp.n, rk = e->tp.rank;
     if ((int) hr->rows % tp || e->E % tp) { snprintf(why, nwhy, "vocab or width not divisible by %d ranks", tp); return false; }
@@ -440,7 +439,7 @@ static bool build(sb_engine * e, char * why, int nwhy) {
             if (!moe0) moe0 = &y.ml;
         }
         // gate / up: a tile of TR rows holds TR/2 gate rows then the same TR/2 up rows
-        if (!upload_tt(e->ar, f, o, e->E, tr_for(o, e->E, 0), min_tiles, 0, [&](int r) { return RowSrc{r < e->E ? o : nullptr, r}; },
+        if (!upload_tt(e->ar, f, o, e->E, tr_for(o, e->E, 0, 0, 0), min_tiles, 0, [&](int r) { return RowSrc{r < e->E ? o : nullptr, r}; },
                        y.o, why, nwhy))
             return false;
         if (!y.moe) {
@@ -450,7 +449,7 @@ static bool build(sb_engine * e, char * why, int nwhy) {
                         const int h = gtr / 2, ti = r / gtr, j = r % gtr, i = ti * h + j % h;
                         return i >= F ? RowSrc{nullptr, 0} : RowSrc{j < h ? gt : up, i}; },
                                y.gateup, why, nwhy) ||
-                    !upload_tt(e->ar, f, dn, e->E, tr_for(dn, e->E, 0), min_tiles, 0,
+                    !upload_tt(e->ar, f, dn, e->E, tr_for(dn, e->E, 0, 1, 0), min_tiles, 0,
                                [&](int r) { return RowSrc{r < e->E ? dn : nullptr, r}; }, y.down, why, nwhy))
                     return false;
                 y.down_iperm = y.down.iperm;
@@ -468,7 +467,7 @@ static bool build(sb_engine * e, char * why, int nwhy) {
                         const int h = gtr / 2, ti = r / gtr, j = r % gtr, m = ti * h + j % h;
                         return m >= fn ? RowSrc{nullptr, 0} : RowSrc{j < h ? gt : up, dperm[j0 + m]}; },
                                y.gateup, why, nwhy) ||
-                    !upload_tt(e->ar, f, dn, en, tr_for(dn, en, 0), min_tiles, 0,
+                    !upload_tt(e->ar, f, dn, en, tr_for(dn, en, 0, 1, 0), min_tiles, 0,
                                [&](int r) { return RowSrc{r < en ? dn : nullptr, e0 + r}; }, y.down, why, nwhy))
                     return false;
                 y.down_iperm = (const int32_t *) e->ar.upload(sc.data(), sc.size() * 4);

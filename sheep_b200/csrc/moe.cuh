@@ -344,12 +344,6 @@ SB_DEV void unit_codes(const uint8_t * tile, const TileGeom & tg, int j, int u, 
     }
 }
 
-// Unsigned code bytes times signed activation bytes, accumulated (PTX dp4a.u32.s32).
-SB_DEV int dp4a_us(uint32_t a, uint32_t b, int c) {
-    int d;
-    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
-    return d;
-}
 
 // Lane share of tile row j for up to NT activations at once (the activations
 // of one chunk, act_b bytes apart): the codes and fields of a unit are read
@@ -517,7 +511,7 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_moe_gemv(const __grid_constan
             if (ok) {
                 if (NT == 1) {
                     ActS a = act_carve(smem, n);
-                    acc[0] = tile_exact<NB, SIX>(ring + (size_t) s * t.tb, tg, a, D, t.has_min, t.mbias);
+                    acc[0] = tile_rows<NB, SIX>(ring + (size_t) s * t.tb, tg, a, D, t.has_min, t.mbias);
                 } else {
                     tile_row_nt<NB, SIX, NT>(ring + (size_t) s * t.tb, tg, smem, act_b, n, ntok, j, v, VS,
                                              t.has_min, t.mbias, acc);

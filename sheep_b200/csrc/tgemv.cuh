@@ -97,6 +97,8 @@ struct TGArgs {
     int in_permuted;         // `in` already in t.perm order
     const float * bias;      // per logical row (QKV: q|k|v concatenated); FFN: [gate bias | up bias]
     int ffn_f;               // FFN: hidden values this launch computes (rows / 2)
+    int mode;                // GemvMode: the epilogue (one kernel serves every mode, so
+                             // consecutive GEMVs of a token run the same code)
     int ffn_n;               // FFN: size of the output (the whole hidden vector; > ffn_f on a tensor-parallel rank)
     float * out;
     const int32_t * scatter; // FFN: write index of hidden value i
@@ -133,6 +135,7 @@ __host__ __device__ constexpr int dot_arrays(int nb) { return nb == 3 || nb == 5
 
 // Bytes of every consumer warp's dot scratch for tiles of t.
 __host__ __device__ inline uint32_t tg_dot_bytes(const TT & t) {
+    if (t.nbits == 4) return 0u;   // tile_q4 keeps its dots in registers
     return (uint32_t) kConsWarps * dot_arrays(t.nbits) * t.TR * (t.cols / kGroup) * 4u;
 }
 
@@ -721,8 +724,187 @@ SB_DEV float tile_exact(const uint8_t * tile, const TileGeom & tg, const ActS & 
     return mine;
 }
 
-template <int MODE, int NB, int SIX>
+// ---------------------------------------------------------------- Q4 rows, one pass
+//
+// 4-bit tiles in the float order of tile_exact's flat epilogue (eight chains
+// per row, chain L over groups 8k + L; the tree ((a0+a4)+(a1+a5))+((a2+a6)+
+// (a3+a7)); a 4-group tail), with every group dot computed by the lane that
+// uses it: no scratch, no second pass. Group g = 4p + i of row j: piece i/2 of
+// units 2p and 2p+1 (groups 4p, 4p+1 in the low and high nibbles of piece 0,
+// 4p+2, 4p+3 of piece 1); its 32 activation codes are 32 bytes at array i,
+// offset 32p. A high-nibble group's dot is taken on the masked bytes (16x the
+// code, unsigned) and shifted back down: exact, since it is a multiple of 16.
+
+// Unsigned code bytes times signed activation bytes, accumulated (PTX dp4a.u32.s32).
+SB_DEV int dp4a_us(uint32_t a, uint32_t b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+
+// The integer dot of group g (= 4p + i) of the row whose unit-2p piece word is
+// at pc, against activation words a0, a1.
+SB_DEV int q4_dot(const uint8_t * pc, int TR, uint32_t mask, int dsh, const uint4 & a0, const uint4 & a1) {
+    const uint4 c0 = *reinterpret_cast<const uint4 *>(pc);
+    const uint4 c1 = *reinterpret_cast<const uint4 *>(pc + 16 * TR);
+    int d = dp4a_us(c0.x & mask, a0.x, 0);
+    d = dp4a_us(c0.y & mask, a0.y, d);
+    d = dp4a_us(c0.z & mask, a0.z, d);
+    d = dp4a_us(c0.w & mask, a0.w, d);
+    d = dp4a_us(c1.x & mask, a1.x, d);
+    d = dp4a_us(c1.y & mask, a1.y, d);
+    d = dp4a_us(c1.z & mask, a1.z, d);
+    d = dp4a_us(c1.w & mask, a1.w, d);
+    return d >> dsh;
+}
+
+// tile_q4 (TR = 4, 8, 16): lane 4L + r runs chain L of rows r, r+4, ... (TR/4
+// rows); a group's activation words are loaded once for them. A quarter warp
+// (chains L, L+1 of one piece, four rows) reads four consecutive 16-byte words.
+// Row j's value ends in lane j.
+template <int SIX, int TR>
+SB_DEV float tile_q4(const uint8_t * tile, const TileGeom & tg, const ActS & a, bool has_min, float mbias) {
+    constexpr int R = TR / 4;
+    const int lane = threadIdx.x & 31, r = lane & 3, L = lane >> 2, i = L & 3;
+    const int n = a.n, nblk = (n / kGroup) >> 3;
+    const uint32_t mask = (i & 1) ? 0xf0f0f0f0u : 0x0f0f0f0fu;
+    const int dsh = (i & 1) ? 4 : 0;
+    const uint8_t * pc0 = tile + tg.pl_off[0] + (i >> 1) * tg.pl_sec[0] + 16 * r;
+    const int8_t * aq = a.q + i * (n >> 2);
+    const uint32_t fw = tg.f_w;
+    float acc[R];
+#pragma unroll
+    for (int m = 0; m < R; m++) acc[m] = 0.0f;
+    // one chain step (group g) of every row the lane holds
+    auto step = [&](int g, float (&ac)[R]) {
+        const int p = g >> 2, k = g >> 3;
+        const uint4 a0 = *reinterpret_cast<const uint4 *>(aq + 32 * p);
+        const uint4 a1 = *reinterpret_cast<const uint4 *>(aq + 32 * p + 16);
+        const float xs = a.xs[g], xm = has_min ? a.xsum[g] : 0.0f;
+#pragma unroll
+        for (int m = 0; m < R; m++) {
+            const int j = r + 4 * m;
+            const int d = q4_dot(pc0 + 16 * (2 * p * TR + 4 * m), TR, mask, dsh, a0, a1);
+            const float st = __fmul_rn(h2f(*reinterpret_cast<const uint16_t *>(tile + tg.sd_off + (k * TR + j) * 2)),
+                                       tile_field1<SIX>(tile + tg.sq_off + (p * TR + j) * fw, i));
+            ac[m] = __fmaf_rn(st, __fmul_rn(xs, (float) d), ac[m]);
+            if (has_min) {
+                const float mn = __fmul_rn(h2f(*reinterpret_cast<const uint16_t *>(tile + tg.md_off + (k * TR + j) * 2)),
+                                           __fsub_rn(tile_field1<SIX>(tile + tg.mq_off + (p * TR + j) * fw, i), mbias));
+                ac[m] = __fmaf_rn(mn, xm, ac[m]);
+            }
+        }
+    };
+    for (int k = 0; k < nblk; k++) step(8 * k + L, acc);
+    float tac[R];
+#pragma unroll
+    for (int m = 0; m < R; m++) tac[m] = 0.0f;
+    const bool tail = ((n / kGroup) & 7) != 0;
+    if (tail && L < 4) step(8 * nblk + L, tac);
+    float mine = 0.0f;
+#pragma unroll
+    for (int m = 0; m < R; m++) {
+        // chain L + 4 is 16 lanes up, L + 1 four, L + 2 eight
+        const float s = __fadd_rn(acc[m], __shfl_down_sync(0xffffffffu, acc[m], 16));
+        const float t = __fadd_rn(s, __shfl_down_sync(0xffffffffu, s, 4));
+        float tot = __fadd_rn(t, __shfl_down_sync(0xffffffffu, t, 8));
+        const float v = __fadd_rn(tac[m], __shfl_down_sync(0xffffffffu, tac[m], 4));
+        const float tt = __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 8));
+        if (tail) tot = __fadd_rn(tot, tt);
+        // row r + 4m sits in lane r
+        const float y = __shfl_sync(0xffffffffu, __fadd_rn(0.0f, tot), lane & 3);
+        if ((lane >> 2) == m) mine = y;
+    }
+    return mine;
+}
+
+// tile_q4s (TR = 1, 2): a row's chains are short of lanes, so each takes S =
+// 4/TR lanes: lane 8*TR*q + 8j + L computes step k0 + q of chain L of row j
+// for each chunk of S steps (the next chunk's terms are formed while the
+// current one is summed), and the chain's own lane (q = 0) adds the S steps in
+// order, their terms fetched by shuffles. A quarter warp (the eight chains of
+// one row and step) reads the four words of two pieces and two unit pairs.
+// Row j's value ends in lane j.
+template <int SIX, int TR>
+SB_DEV float tile_q4s(const uint8_t * tile, const TileGeom & tg, const ActS & a, bool has_min, float mbias) {
+    constexpr int S = 4 / TR;
+    const int lane = threadIdx.x & 31, L = lane & 7, j = (lane >> 3) % TR, q = lane / (8 * TR), i = L & 3;
+    const int n = a.n, ng = n / kGroup, nblk = ng >> 3;
+    const uint32_t mask = (i & 1) ? 0xf0f0f0f0u : 0x0f0f0f0fu;
+    const int dsh = (i & 1) ? 4 : 0;
+    const uint8_t * pc0 = tile + tg.pl_off[0] + (i >> 1) * tg.pl_sec[0] + 16 * j;
+    const int8_t * aq = a.q + i * (n >> 2);
+    const uint32_t fw = tg.f_w;
+    // the terms of group g of row j: step, xs * dot, min
+    auto terms = [&](int g, float & st, float & t1, float & mn) {
+        const int p = g >> 2, k = g >> 3;
+        const uint4 a0 = *reinterpret_cast<const uint4 *>(aq + 32 * p);
+        const uint4 a1 = *reinterpret_cast<const uint4 *>(aq + 32 * p + 16);
+        const int d = q4_dot(pc0 + 16 * (2 * p * TR), TR, mask, dsh, a0, a1);
+        st = __fmul_rn(h2f(*reinterpret_cast<const uint16_t *>(tile + tg.sd_off + (k * TR + j) * 2)),
+                       tile_field1<SIX>(tile + tg.sq_off + (p * TR + j) * fw, i));
+        t1 = __fmul_rn(a.xs[g], (float) d);
+        mn = has_min ? __fmul_rn(h2f(*reinterpret_cast<const uint16_t *>(tile + tg.md_off + (k * TR + j) * 2)),
+                                 __fsub_rn(tile_field1<SIX>(tile + tg.mq_off + (p * TR + j) * fw, i), mbias))
+                     : 0.0f;
+    };
+    float acc = 0.0f;
+    float st = 0.0f, t1 = 0.0f, mn = 0.0f;
+    if (q < nblk) terms(8 * q + L, st, t1, mn);
+    for (int k0 = 0; k0 < nblk; k0 += S) {
+        const float cst = st, ct1 = t1, cmn = mn;
+        if (k0 + S + q < nblk) terms(8 * (k0 + S + q) + L, st, t1, mn);
+#pragma unroll
+        for (int qq = 0; qq < S; qq++) {
+            const int src = (lane & (8 * TR - 1)) + 8 * TR * qq;
+            const float a_st = __shfl_sync(0xffffffffu, cst, src);
+            const float a_t1 = __shfl_sync(0xffffffffu, ct1, src);
+            const float a_mn = __shfl_sync(0xffffffffu, cmn, src);
+            if (k0 + qq < nblk) {
+                acc = __fmaf_rn(a_st, a_t1, acc);
+                if (has_min) acc = __fmaf_rn(a_mn, a.xsum[8 * (k0 + qq) + L], acc);
+            }
+        }
+    }
+    const float s = __fadd_rn(acc, __shfl_down_sync(0xffffffffu, acc, 4));
+    const float t = __fadd_rn(s, __shfl_down_sync(0xffffffffu, s, 1));
+    float tot = __fadd_rn(t, __shfl_down_sync(0xffffffffu, t, 2));
+    if (ng & 7) {
+        float tac = 0.0f;
+        if (q == 0 && L < 4) {
+            const int g = 8 * nblk + L;
+            float a_st, a_t1, a_mn;
+            terms(g, a_st, a_t1, a_mn);
+            tac = __fmaf_rn(a_st, a_t1, tac);
+            if (has_min) tac = __fmaf_rn(a_mn, a.xsum[g], tac);
+        }
+        const float v = __fadd_rn(tac, __shfl_down_sync(0xffffffffu, tac, 1));
+        tot = __fadd_rn(tot, __fadd_rn(v, __shfl_down_sync(0xffffffffu, v, 2)));
+    }
+    // row j sits in lane 8j
+    return __shfl_sync(0xffffffffu, __fadd_rn(0.0f, tot), 8 * (lane < TR ? lane : 0));
+}
+
+// 4-bit tiles take tile_q4 (no dot scratch: tg_dot_bytes is 0 for them);
+// every other width tile_exact.
+template <int NB, int SIX>
+SB_DEV float tile_rows(const uint8_t * tile, const TileGeom & tg, const ActS & a, int * D, bool has_min, float mbias) {
+    if constexpr (NB == 4) {
+        switch (tg.TR) {
+        case 16: return tile_q4<SIX, 16>(tile, tg, a, has_min, mbias);
+        case 8: return tile_q4<SIX, 8>(tile, tg, a, has_min, mbias);
+        case 4: return tile_q4<SIX, 4>(tile, tg, a, has_min, mbias);
+        case 2: return tile_q4s<SIX, 2>(tile, tg, a, has_min, mbias);
+        default: return tile_q4s<SIX, 1>(tile, tg, a, has_min, mbias);
+        }
+    } else {
+        return tile_exact<NB, SIX>(tile, tg, a, D, has_min, mbias);
+    }
+}
+
+template <int NB, int SIX>
 __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__ TGArgs g) {
+    const int MODE = g.mode;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages], statics;
     __shared__ double red[kConsWarps];
@@ -856,7 +1038,7 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__
         if (k == 0) SB_MARK(g.trace, g.launch_id, 3);
         float acc = 0.0f;
         if (ok && SB_CHECK(g.err, tg.bytes == t.tb && (size_t) (s + 1) * t.tb + SL.ring_off <= ring_end, 106))
-            acc = tile_exact<NB, SIX>(ring + (size_t) s * t.tb, tg, a, D, t.has_min, t.mbias);
+            acc = tile_rows<NB, SIX>(ring + (size_t) s * t.tb, tg, a, D, t.has_min, t.mbias);
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
         if (MODE == GM_FFN) {

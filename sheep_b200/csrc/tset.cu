@@ -121,13 +121,15 @@ extern "C" unsigned long long sb_tset_bytes(const sb_tset * t, const char * name
 }
 
 template <int NB, int SIX>
-static void launch_plain(const TGArgs & g, int grid, size_t smem, cudaStream_t st) {
+static void launch_plain(const TGArgs & g0, int grid, size_t smem, cudaStream_t st) {
     static bool attr = false;
     if (!attr) {
-        cudaFuncSetAttribute(k_tgemv<GM_PLAIN, NB, SIX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kSmemBudget);
+        cudaFuncSetAttribute(k_tgemv<NB, SIX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) kSmemBudget);
         attr = true;
     }
-    k_tgemv<GM_PLAIN, NB, SIX><<<grid, kTgThreads, smem, st>>>(g);
+    TGArgs g = g0;
+    g.mode = GM_PLAIN;
+    k_tgemv<NB, SIX><<<grid, kTgThreads, smem, st>>>(g);
 }
 
 static const TTB * find_ttb(const sb_tset * t, const char * name) {
