@@ -334,11 +334,14 @@ def main():
         peak0, _ = peaks()
         from sheep_b200 import configs as cf
         extras = {"l2": "a 512 MB buffer rewritten before each timed run (decode: weights > L2)",
-                  "gemv_cfg1": gemv_microbench(peak0), "gemm_tc_cfg1": gemm_tc_microbench(peak0),
-                  "moe_cfg2": moe_microbench(peak0),
-                  "decode_cfg3": decode_cfg3(peak0), "decode_cfg3_batch64": decode_cfg3_batch(peak0),
-                  "prefill_cfg0": prefill_bench(model_path(cf.CONFIGS["qwen2.5-1.5b-q4"], 0, None), PROMPT_LEN),
-                  "prefill_cfg3": prefill_bench(model_path(cf.CONFIGS["llama3-8b-q4k"], 0, None), 2048)}
+                  "gemv_cfg1": extra(gemv_microbench, peak0), "gemm_tc_cfg1": extra(gemm_tc_microbench, peak0),
+                  "moe_cfg2": extra(moe_microbench, peak0),
+                  "decode_cfg3": extra(decode_cfg3, peak0), "decode_cfg3_batch64": extra(decode_cfg3_batch, peak0),
+                  "decode_cfg4": extra(decode_cfg4, peak0),
+                  "prefill_cfg0": extra(lambda: prefill_bench(model_path(cf.CONFIGS["qwen2.5-1.5b-q4"], 0, None),
+                                                              PROMPT_LEN)),
+                  "prefill_cfg3": extra(lambda: prefill_bench(model_path(cf.CONFIGS["llama3-8b-q4k"], 0, None),
+                                                              2048))}
 
     if rank == 0:
         peak, peak_kind = peaks()
@@ -376,6 +379,15 @@ def main():
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def extra(fn, *args):
+    """One extra measurement; a failure is reported in its place instead of
+    ending the run (the headline line is printed either way)."""
+    try:
+        return fn(*args)
+    except Exception as e:   # noqa: BLE001 -- any failure of an extra is data, not a crash
+        return {"error": f"{type(e).__name__}: {e}"[:300]}
 
 
 def fp16_rows(seed, n, cols):
@@ -462,6 +474,38 @@ def decode_cfg3(peak, ngen=64, tp=None, max_over_ranks=None):
         return {"tok_s": round(tps, 1), "ms_per_token": round(ms / ngen, 4), "gpus": world,
                 "bytes_per_token_all_gpus": int(nb), "gbs": round(gbs, 1), "frac_of_n_gpus": round(gbs / (peak * world), 4),
                 "tokens": ngen, "greedy_ids_head": [int(i) for i in ids[:8]]}
+    finally:
+        eng.close()
+
+
+def decode_cfg4(peak, prompt=1024, ngen=64, nwarm=8):
+    """Configuration 4 (Qwen3-235B-A22B shape, 94 MoE layers, ~136 GB of Q4)
+    at batch 1 on one GPU: a `prompt`-id random prompt stepped, then the
+    device-resident greedy loop. The file holds everything but the experts
+    (writer mode direct=2); the engine draws the experts' tiles on the device
+    (sb_draw_experts), so a token reads the bytes a full file would give: the
+    attention projections, the router, the 8 chosen experts of every layer and
+    the head."""
+    import sheep_b200
+    from sheep_b200 import configs
+    path = model_path(configs.CONFIGS["qwen3-235b-a22b-q4"], 0, None)
+    sheep_b200.draw_experts(235)
+    t0 = time.time()
+    try:
+        eng = sheep_b200.Engine(path, n_ctx=prompt + nwarm + ngen + 8)
+    finally:
+        sheep_b200.draw_experts(0)
+    open_s = time.time() - t0
+    try:
+        p = np.random.default_rng(1234).integers(0, eng.n_vocab, prompt).astype(np.int32)
+        ids, ms = eng.generate(p, ngen + 1, timed=True, warmup=nwarm)
+        tps = ngen / (ms / 1000.0)
+        nb = float(eng.bytes_per_token)
+        gbs = nb * tps / 1e9
+        return {"tok_s": round(tps, 1), "ms_per_token": round(ms / ngen, 4), "prompt": prompt, "tokens": ngen,
+                "bytes_per_token": int(nb), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
+                "experts": "drawn on the device (direct=2 file)", "open_s": round(open_s, 1),
+                "launches_per_token": eng.launches_per_token, "greedy_ids_head": [int(i) for i in ids[:8]]}
     finally:
         eng.close()
 

@@ -236,7 +236,9 @@ void sb_batch_close(sb_batch * b);
 // out (int[16]): [0] n_seq [1] n_ctx [2] n_vocab [3..7] superblock slices of
 // the q|k|v, o, gate|up, down and head products [8,9] the file's weight bytes
 // per step (lo, hi 32 bits) [10,11] the int8 weight bytes per step [12] kernel
-// launches per step [13] tokens per tensor-core tile.
+// launches per step [13] tokens per tensor-core tile [14,15] every MoE
+// layer's experts and router as stored (lo, hi 32 bits; 0 for a dense model;
+// the gate|up and down splits read 0 when layer 0 is a MoE layer).
 void sb_batch_info(const sb_batch * b, int * out);
 // One token per slot: tokens[s] at absolute position pos[s] (pos[s] < 0 idles
 // slot s: its logits are not meaningful). Host arrays of n_seq. Returns a host
@@ -269,9 +271,24 @@ typedef struct {
     uint64_t seed;
     float    sigma;
     int      threads;
+    // 0: every weight drawn N(0, sigma) and quantized; 1: quantized tensors'
+    // group ranges and codes drawn directly from the seed (same layout and
+    // value scale, several times faster); 2: as 1, but the MoE experts' bytes
+    // are not written (the file is sparse there): an engine opened after
+    // sb_draw_experts(seed) draws them on the device. For the ~130 GB
+    // configuration, whose experts are 97 % of its bytes.
+    uint32_t direct;
 } ssfgen_spec;
 
 int ssfgen_write(const char * path, const ssfgen_spec * s, char * why, int nwhy);
+
+// Engines opened after this call (sb_open, sb_open_tp) fill their MoE experts'
+// tiles on the device from `seed` instead of reading them from the file: for
+// files written with direct = 2, which leave those bytes out. Code and field
+// bytes uniform, superblock scales fixed (weights within about +-2 sigma); the
+// tiles have the size and layout the file's experts would give. 0 restores
+// reading from the file. A benchmark facility: such weights match no file.
+void sb_draw_experts(uint64_t seed);
 
 // The loader's validation alone, no GPU needed: 1, or 0 with the reason
 // (the acceptance rules of sml/sml-model.c:24-75 and :174-260, v8+ files).

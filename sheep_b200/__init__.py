@@ -27,7 +27,8 @@ class SsfSpec(ctypes.Structure):
                [(n, ctypes.c_uint32) for n in
                 "tied qkv_bias qk_norm nbits emb_nbits scale6 minneg "
                 "n_expert n_expert_used moe_flags expert_ff perm_mode".split()] + \
-               [("seed", ctypes.c_uint64), ("sigma", ctypes.c_float), ("threads", ctypes.c_int)]
+               [("seed", ctypes.c_uint64), ("sigma", ctypes.c_float), ("threads", ctypes.c_int),
+                ("direct", ctypes.c_uint32)]
 
 
 def lib():
@@ -86,6 +87,7 @@ def lib():
         "sb_quantize_act": (ip, [vp, vp, ip, vp, vp, vp, vp]),
         "ssfgen_write": (ip, [cp, vp, cp, ip]),
         "sb_ssf_check": (ip, [cp, cp, ip]),
+        "sb_draw_experts": (None, [ctypes.c_uint64]),
         "sb_attn_decode": (ip, [vp, vp, vp, vp, vp, vp, vp, ctypes.c_float, ip, ip, ip, ip, ip, ctypes.c_float,
                                 vp, vp]),
         "sb_attn_last_error": (cp, []),
@@ -135,6 +137,13 @@ def write_model(path, **spec):
     if not lib().ssfgen_write(path.encode(), ctypes.byref(s), why, 512):
         raise RuntimeError(why.value.decode())
     return path
+
+
+def draw_experts(seed):
+    """Engines opened after this fill their MoE experts on the device from
+    `seed` (files written with direct=2 leave those bytes out); 0 restores
+    reading them from the file (sb_draw_experts)."""
+    lib().sb_draw_experts(int(seed))
 
 
 def ssf_check(path):
@@ -432,6 +441,7 @@ class Batch:
         self.int8_bytes = (info[10] & 0xffffffff) | (info[11] << 32)
         self.launches = info[12]
         self.tile_tokens = info[13]
+        self.expert_bytes = (info[14] & 0xffffffff) | (info[15] << 32)
 
     def forward_multi(self, tokens, pos):
         """logits [n_seq, n_vocab] for tokens[s] at pos[s] (pos < 0: idle slot)."""

@@ -9,7 +9,7 @@ round-to-nearest; norms are 1.
 
 _BASE = dict(rope_theta=1e6, rms_eps=1e-6, tied=0, qkv_bias=0, qk_norm=0, nbits=4, emb_nbits=4,
              scale6=0, minneg=0, n_expert=0, n_expert_used=0, moe_flags=0, expert_ff=0,
-             perm_mode=1, seed=1234, sigma=0.02, threads=0)
+             perm_mode=1, seed=1234, sigma=0.02, threads=0, direct=0)
 
 CONFIGS = {
     # 0: Qwen2.5-1.5B shape, v8 Q4, tied head, q/k/v biases
@@ -27,6 +27,14 @@ CONFIGS = {
     # 3: Llama-3-8B shape, v9 6-bit fields ("Q4_K-style")
     "llama3-8b-q4k": dict(_BASE, n_layer=32, n_embd=4096, n_head=32, n_head_kv=8, head_dim=128,
                           n_ff=14336, n_vocab=128256, rope_theta=5e5, rms_eps=1e-5, scale6=1, minneg=1),
+    # 4: Qwen3-235B-A22B shape: 94 MoE layers, 64/4 heads with Q/K norm, 128
+    # experts top-8 (softmax, renormalised), expert FFN 1536, untied head;
+    # ~136 GB of Q4: codes and group ranges drawn directly, and the experts'
+    # bytes (97 %) left out of the file for the engine to draw on the device
+    # (sb_draw_experts); direct=1 writes them (shallow parity models)
+    "qwen3-235b-a22b-q4": dict(_BASE, n_layer=94, n_embd=4096, n_head=64, n_head_kv=4, head_dim=128,
+                               n_ff=1536, n_vocab=151936, n_expert=128, n_expert_used=8, moe_flags=1,
+                               expert_ff=1536, qk_norm=1, direct=2),
 }
 
 # Small models for parity tests (same code paths, seconds on the CPU oracle).

@@ -12,12 +12,18 @@
 //              -> quant -> o GEMM (x +=) -> quant(norm) -> gate|up GEMM
 //              -> quant(silu) -> down GEMM (x +=)
 //   quant(norm) -> head GEMM -> k_bargmax (next token, position + 1)
+// A mixture-of-experts layer replaces the gate|up/down products by the MoE
+// FFN over the n_seq rows (moe_host.h: router with its RMSNorm, grouped
+// gate/up and down GEMVs over the chosen experts' Q4 tiles, choice-order
+// combine added to x), as the CPU's batched step runs moe_ffn per row
+// (sml/sml-run.c:3182 moe_ffn_batch).
 //
 // HBM layout: the int8 weights as 32 KB (128 rows x 256 columns) blocks in the
 // tensor cores' operand layout, q|k|v and gate|up each one tensor (segments
 // padded to 128 rows); the KV cache [layer][seq][kv head][n_ctx][hd] fp16, so a
 // chunk of one head's positions is one contiguous bulk copy.
 #include "batch.cuh"
+#include "moe_host.h"
 #include "tc_batch.h"
 #include "sheep_b200.h"
 #include "ssf.h"
@@ -56,6 +62,8 @@ struct BGemm {
 struct BLayer {
     BGemm qkv, o, gu, dn;
     const float * an = nullptr, * fn = nullptr, * qkv_b = nullptr, * qn = nullptr, * kn = nullptr;
+    bool moe = false;                 // MoE FFN in place of gate|up / down
+    MoeLayer ml;
 };
 
 int round128(int n) { return (n + 127) / 128 * 128; }
@@ -107,6 +115,8 @@ struct sb_batch {
     float * h_logits = nullptr;
     int * h_io = nullptr;             // [2][n_seq] staging of tokens and positions
     uint64_t bytes_file = 0, bytes_i8 = 0;
+    MoeScratch ms;                    // routing scratch for n_seq rows, shared by the MoE layers
+    uint64_t bytes_experts = 0;       // every MoE layer's experts and router, as stored
 };
 
 static void b_after(sb_batch * b, cudaError_t r) {
@@ -190,31 +200,42 @@ static bool b_build(sb_batch * b, char * why, int nwhy) {
     b->out_norm = b_f32(b, ssf_find(&f, "output_norm.weight"));
     b->L.assign(b->n_layer, BLayer());
     b->F = 0;
+    b->bytes_experts = 0;
+    const MoeLayer * moe0 = nullptr;
+    bool dense_seen = false;
     for (int l = 0; l < b->n_layer; l++) {
         BLayer & y = b->L[l];
         auto R = [&](const char * fmt) { return ssf_findf(&f, fmt, l, 0); };
-        if (R("blk.%d.ffn_gate_inp.weight")) {
-            snprintf(why, nwhy, "layer %d: mixture-of-experts layers are not on the batched path", l);
-            return false;
-        }
+        y.moe = R("blk.%d.ffn_gate_inp.weight") != nullptr;
         const ssf_rec * q = R("blk.%d.attn_q.weight"), * k = R("blk.%d.attn_k.weight"), * v = R("blk.%d.attn_v.weight");
         const ssf_rec * o = R("blk.%d.attn_output.weight"), * gt = R("blk.%d.ffn_gate.weight");
         const ssf_rec * up = R("blk.%d.ffn_up.weight"), * dn = R("blk.%d.ffn_down.weight");
-        if (!q || !k || !v || !o || !gt || !up || !dn || !R("blk.%d.attn_norm.weight") || !R("blk.%d.ffn_norm.weight")) {
+        if (!q || !k || !v || !o || (!y.moe && (!gt || !up || !dn)) || !R("blk.%d.attn_norm.weight") ||
+            !R("blk.%d.ffn_norm.weight")) {
             snprintf(why, nwhy, "layer %d: missing tensors", l);
             return false;
         }
         if ((int) q->rows != b->qd || (int) k->rows != b->kvd || (int) v->rows != b->kvd || (int) q->cols != b->E ||
-            (int) o->rows != b->E || (int) o->cols != b->qd || (int) gt->cols != b->E || gt->rows != up->rows ||
-            (int) dn->rows != b->E || dn->cols != gt->rows) {
+            (int) o->rows != b->E || (int) o->cols != b->qd ||
+            (!y.moe && ((int) gt->cols != b->E || gt->rows != up->rows || (int) dn->rows != b->E || dn->cols != gt->rows))) {
             snprintf(why, nwhy, "layer %d: tensor shapes do not match the header", l);
             return false;
         }
-        if (l == 0) b->F = (int) gt->rows;
-        if ((int) gt->rows != b->F) { snprintf(why, nwhy, "layer %d: FFN widths differ", l); return false; }
-        if (!b_gemm(b, y.qkv, {q, k, v}, why, nwhy) || !b_gemm(b, y.o, {o}, why, nwhy) ||
-            !b_gemm(b, y.gu, {gt, up}, why, nwhy) || !b_gemm(b, y.dn, {dn}, why, nwhy))
-            return false;
+        if (!b_gemm(b, y.qkv, {q, k, v}, why, nwhy) || !b_gemm(b, y.o, {o}, why, nwhy)) return false;
+        if (y.moe) {
+            if (!moe_upload(b->ar, f, l, y.ml, why, nwhy)) return false;
+            if (moe0 && (y.ml.E != moe0->E || y.ml.F != moe0->F || y.ml.ne != moe0->ne || y.ml.k != moe0->k)) {
+                snprintf(why, nwhy, "layer %d: MoE shapes differ between layers", l);
+                return false;
+            }
+            if (!moe0) moe0 = &y.ml;
+            b->bytes_experts += (uint64_t) y.ml.ne * y.ml.expert_file_bytes + y.ml.router_bytes;
+        } else {
+            if (!dense_seen) b->F = (int) gt->rows;
+            dense_seen = true;
+            if ((int) gt->rows != b->F) { snprintf(why, nwhy, "layer %d: FFN widths differ", l); return false; }
+            if (!b_gemm(b, y.gu, {gt, up}, why, nwhy) || !b_gemm(b, y.dn, {dn}, why, nwhy)) return false;
+        }
         y.an = b_f32(b, R("blk.%d.attn_norm.weight"));
         y.fn = b_f32(b, R("blk.%d.ffn_norm.weight"));
         const ssf_rec * qb = R("blk.%d.attn_q.bias"), * kb = R("blk.%d.attn_k.bias"), * vb = R("blk.%d.attn_v.bias");
@@ -239,6 +260,7 @@ static bool b_build(sb_batch * b, char * why, int nwhy) {
         return false;
     }
     b->Fp = round128(b->F);
+    if (moe0) moe_carve(b->ar, *moe0, b->B, b->ms);
     // step state
     const int B = b->B, Tp = b->T_pad;
     int wide = b->E > b->qd ? b->E : b->qd;
@@ -360,6 +382,13 @@ static void b_enqueue(sb_batch * b) {
         snprintf(b->cur, sizeof b->cur, "L%d.o", l);
         b_quant(b, TQ_PLAIN, y.o, b->att, b->qd, nullptr, 0);
         b_mma(b, y.o, b->x, b->E, nullptr, 1);
+        if (y.moe) {
+            // router on rmsnorm(x) per row, the chosen experts, combine added to x
+            snprintf(b->cur, sizeof b->cur, "L%d.moe", l);
+            moe_enqueue(y.ml, b->ms, b->x, b->B, y.fn, b->eps, b->x, 1, b->nsm, b->st, false, b->err, nullptr,
+                        b->launches, [&](cudaError_t r, const char *) { b_after(b, r); });
+            continue;
+        }
         snprintf(b->cur, sizeof b->cur, "L%d.ffn", l);
         b_quant(b, TQ_NORM, y.gu, b->x, b->E, y.fn, 0);
         b_mma(b, y.gu, b->hid, 2 * b->Fp, nullptr, 0);
@@ -428,6 +457,9 @@ extern "C" sb_batch * sb_batch_open(const char * path, int n_seq, int n_ctx, cha
     cudaDeviceGetAttribute(&b->nsm, cudaDevAttrMultiProcessorCount, dev);
     if (!bck(cudaStreamCreateWithFlags(&b->st, cudaStreamNonBlocking), "stream"))
         return b_fail(b, why, nwhy, g_berr);
+    // MoE experts drawn on the device (sb_draw_experts) rather than read
+    b->ar.draw_seed = draw_experts_seed();
+    b->ar.minneg = b->f.minneg;
     // pass 1 sizes the arena, pass 2 fills it (and re-quantizes every product's weights)
     if (!b_build(b, why, nwhy)) return b_fail(b, why, nwhy, nullptr);
     if (!b->ar.allocate()) {
@@ -478,11 +510,13 @@ extern "C" void sb_batch_close(sb_batch * b) {
 extern "C" void sb_batch_info(const sb_batch * b, int * out) {
     out[0] = b->B; out[1] = b->n_ctx; out[2] = b->V;
     const BLayer & y = b->L[0];
-    out[3] = y.qkv.split; out[4] = y.o.split; out[5] = y.gu.split; out[6] = y.dn.split; out[7] = b->head.split;
+    out[3] = y.qkv.split; out[4] = y.o.split; out[5] = y.moe ? 0 : y.gu.split; out[6] = y.moe ? 0 : y.dn.split;
+    out[7] = b->head.split;
     out[8] = (int) (b->bytes_file & 0xffffffffu); out[9] = (int) (b->bytes_file >> 32);
     out[10] = (int) (b->bytes_i8 & 0xffffffffu); out[11] = (int) (b->bytes_i8 >> 32);
     out[12] = b->launches;
     out[13] = b->N;
+    out[14] = (int) (b->bytes_experts & 0xffffffffu); out[15] = (int) (b->bytes_experts >> 32);
 }
 
 // One step of every slot on the stream (graph replay or, with SB_SYNC=1, eager

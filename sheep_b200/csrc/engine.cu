@@ -671,6 +671,9 @@ static sb_engine * open_engine(const char * path, int n_ctx, int tp, int rank, c
             close_all(e); delete e; return nullptr;
         }
     }
+    // MoE experts drawn on the device (sb_draw_experts) rather than read
+    e->ar.draw_seed = draw_experts_seed();
+    e->ar.minneg = e->minneg;
     // pass 1 sizes the arena (and the exchange region), pass 2 fills them
     if (!build(e, why, nwhy)) { close_all(e); delete e; return nullptr; }
     if (!e->ar.allocate()) {

@@ -100,6 +100,12 @@ inline bool moe_upload(Arena & a, const ssf_file & f, int L, MoeLayer & m, char 
     std::vector<const uint8_t *> gt(m.ne), dt(m.ne);
     std::vector<const int32_t *> gp(m.ne), di(m.ne);
     int gtr = 0, dtr = 0;
+    // experts drawn on the device when the arena asks for it (sb_draw_experts)
+    struct Drawing {
+        Arena & a;
+        explicit Drawing(Arena & a_) : a(a_) { a.drawing = a.draw_seed != 0; }
+        ~Drawing() { a.drawing = false; }
+    } drawing(a);
     for (int e = 0; e < m.ne; e++) {
         char nm[3][96];
         snprintf(nm[0], sizeof nm[0], "blk.%d.ffn_gate.%d.weight", L, e);

@@ -102,6 +102,7 @@ typedef struct {
     int rows, cols, nbits;
     int init;
     int perm_group;           // index into the perm list (quant only)
+    int expert;               // a MoE expert's gate/up/down
     uint64_t stream;          // RNG stream id
     ssf_rec rec;
 } tdesc;
@@ -139,9 +140,10 @@ static int add_perm(tlist * L, int cols) {
     return L->n_perm++;
 }
 
-static void qt(tlist * L, const char * name, int rows, int cols, int nbits, int pg) {
+static tdesc * qt(tlist * L, const char * name, int rows, int cols, int nbits, int pg) {
     tdesc * d = add_t(L, name, SSF_KIND_QUANT, rows, cols, nbits, INIT_GAUSS);
     d->perm_group = pg;
+    return d;
 }
 
 static void build_list(tlist * L, const ssfgen_spec * s) {
@@ -176,11 +178,11 @@ static void build_list(tlist * L, const ssfgen_spec * s) {
             for (int e = 0; e < (int) s->n_expert; e++) {
                 const int pgu = add_perm(L, E), pdn = add_perm(L, F);
                 snprintf(nm, sizeof nm, "blk.%d.ffn_gate.%d.weight", l, e);
-                qt(L, nm, F, E, (int) s->nbits, pgu);
+                qt(L, nm, F, E, (int) s->nbits, pgu)->expert = 1;
                 snprintf(nm, sizeof nm, "blk.%d.ffn_up.%d.weight", l, e);
-                qt(L, nm, F, E, (int) s->nbits, pgu);
+                qt(L, nm, F, E, (int) s->nbits, pgu)->expert = 1;
                 snprintf(nm, sizeof nm, "blk.%d.ffn_down.%d.weight", l, e);
-                qt(L, nm, E, F, (int) s->nbits, pdn);
+                qt(L, nm, E, F, (int) s->nbits, pdn)->expert = 1;
             }
         } else {
             const int F = (int) s->n_ff;
@@ -261,12 +263,20 @@ typedef struct {
     int six, minneg;
     float sigma;
     uint64_t seed;
+    int direct;               // 1, 2: quantized tensors' ranges and codes drawn directly (quant_row);
+                              // 2: MoE experts' bytes not written (holes of a sparse file)
 } qctx;
 
 // Quantize one row of n weights (already drawn) into its planes and fields.
+// With rd (direct draws) w is not read: each group's range is drawn as
+// [-sigma (1.6 + 0.8 u), sigma (1.6 + 0.8 v)] (about the extremes of 32
+// normal draws), its fields follow from that range exactly as below, and its
+// codes are uniform on [0, 2^nbits - 1]. Same layout and value scale, without
+// drawing and rounding every weight: the ~130 GB configuration is written
+// this way.
 static void quant_row(const qctx * q, const float * w, int n, int nbits,
                       uint16_t * sd, uint8_t * sqf, uint16_t * md, uint8_t * mqf,
-                      uint8_t * planes[3], uint8_t * codes_tmp) {
+                      uint8_t * planes[3], uint8_t * codes_tmp, rng_t * rd) {
     const int ng = n / SSF_GROUP, nsb = ssf_nscale(n);
     const int nmax = (1 << nbits) - 1;
     const int fmax = q->six ? 63 : 255;
@@ -277,10 +287,16 @@ static void quant_row(const qctx * q, const float * w, int n, int nbits,
         const int g0 = s * SSF_GPS, g1 = g0 + SSF_GPS < ng ? g0 + SSF_GPS : ng;
         float step[SSF_GPS], mn[SSF_GPS], smax = 0.0f, mabs = 0.0f;
         for (int g = g0; g < g1; g++) {
-            float lo = w[g * SSF_GROUP], hi = lo;
-            for (int j = 1; j < SSF_GROUP; j++) {
-                const float v = w[g * SSF_GROUP + j];
-                lo = v < lo ? v : lo; hi = v > hi ? v : hi;
+            float lo, hi;
+            if (rd) {
+                lo = -q->sigma * (1.6f + 0.8f * rng_unit(rd));
+                hi = q->sigma * (1.6f + 0.8f * rng_unit(rd));
+            } else {
+                lo = hi = w[g * SSF_GROUP];
+                for (int j = 1; j < SSF_GROUP; j++) {
+                    const float v = w[g * SSF_GROUP + j];
+                    lo = v < lo ? v : lo; hi = v > hi ? v : hi;
+                }
             }
             if (q->minneg && lo > 0.0f) lo = 0.0f;
             step[g - g0] = (hi - lo) / (float) nmax;
@@ -305,7 +321,12 @@ static void quant_row(const qctx * q, const float * w, int n, int nbits,
             sqv[g - g0] = sv;
             mqv[g - g0] = mv;
             const float es = dd * (float) sv, em = mdd * ((float) mv - mbias);
-            for (int j = 0; j < SSF_GROUP; j++) {
+            if (rd) {
+                for (int j = 0; j < SSF_GROUP; j += 8) {
+                    const uint64_t b = rng_next(rd);
+                    for (int k = 0; k < 8; k++) codes_tmp[g * SSF_GROUP + j + k] = (uint8_t) ((b >> (8 * k)) & (uint64_t) nmax);
+                }
+            } else for (int j = 0; j < SSF_GROUP; j++) {
                 int c = es > 0.0f ? (int) lrintf((w[g * SSF_GROUP + j] - em) / es) : 0;
                 c = c < 0 ? 0 : c > nmax ? nmax : c;
                 codes_tmp[g * SSF_GROUP + j] = (uint8_t) c;
@@ -398,9 +419,10 @@ static int write_quant(int fd, const qctx * q, const tdesc * d) {
                 const int i = row - r0;
                 uint8_t * planes[3];
                 for (int p = 0; p < np; p++) planes[p] = pl[p] + (size_t) i * plane_row_bytes(kinds[p], n);
-                draw_row(q, d->stream, row, w, n, q->sigma);
+                rng_t rd = { mix64(q->seed * 0x100000001b3ull ^ 0x6469726563740000ull ^ (d->stream << 32) ^ (uint64_t) row) };
+                if (!q->direct) draw_row(q, d->stream, row, w, n, q->sigma);
                 quant_row(q, w, n, d->nbits, sd + (size_t) i * nsb, sqf + (size_t) i * frow,
-                          md + (size_t) i * nsb, mqf + (size_t) i * frow, planes, ct);
+                          md + (size_t) i * nsb, mqf + (size_t) i * frow, planes, ct, q->direct ? &rd : NULL);
             }
             free(w);
             free(ct);
@@ -491,11 +513,13 @@ int ssfgen_write(const char * path, const ssfgen_spec * s, char * why, int nwhy)
     free(head);
     for (int i = 0; ok && i < L.n; i++)
         ok = pwrite_all(fd, &L.t[i].rec, sizeof(ssf_rec), SSF_HEADER_BYTES + (uint64_t) i * sizeof(ssf_rec));
-    const qctx q = { six, six && s->minneg, s->sigma > 0.0f ? s->sigma : 0.02f, s->seed };
+    const qctx q = { six, six && s->minneg, s->sigma > 0.0f ? s->sigma : 0.02f, s->seed, (int) s->direct };
     for (int p = 0; ok && p < L.n_perm; p++)
         ok = write_perm(fd, &q, p, L.perm_cols[p], L.perm_off[p], (int) s->perm_mode);
-    for (int i = 0; ok && i < L.n; i++)
+    for (int i = 0; ok && i < L.n; i++) {
+        if (q.direct == 2 && L.t[i].expert) continue;   // left as a hole: drawn on the device at open
         ok = L.t[i].kind == SSF_KIND_F32 ? write_f32(fd, &q, &L.t[i]) : write_quant(fd, &q, &L.t[i]);
+    }
     ok = (close(fd) == 0) && ok;
     free(L.t); free(L.perm_cols); free(L.perm_off);
     if (!ok) snprintf(why, (size_t) nwhy, "write to %s failed", path);

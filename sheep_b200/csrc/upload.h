@@ -22,10 +22,24 @@
 
 namespace sb {
 
+// Tiles filled on the device instead of from the file (draw.cu): uniform code
+// and field bytes, fixed superblock scales; false on a misaligned buffer or a
+// failed launch.
+bool draw_tiles(uint8_t * dev, size_t total, const TileGeom & g, int nbits, int six, int minneg, int has_min,
+                uint64_t seed, float sigma);
+// The seed set by sb_draw_experts (0: experts come from the file).
+uint64_t draw_experts_seed();
+
 struct Arena {
     uint8_t * base = nullptr;
     size_t used = 0, size = 0;
     std::unordered_map<uint64_t, std::pair<const int32_t *, const int32_t *>> perms;
+    // while set, upload_tt draws tiles on the device (seeded by draw_seed and
+    // the tiles' arena offset) instead of copying them from the file
+    bool drawing = false;
+    uint64_t draw_seed = 0;
+    int minneg = 0;
+    bool draw_failed = false;
 
     void * carve(size_t n) {
         const size_t at = (used + 255) / 256 * 256;
@@ -206,6 +220,15 @@ inline bool upload_tt(Arena & a, const ssf_file & f, const ssf_rec * first, int 
     uint8_t * dev = (uint8_t *) a.carve(total);
     t.tiles = dev;
     if (!dev) return true;   // sizing pass
+    if (a.drawing) {
+        if (!draw_tiles(dev, total, tg, t.nbits, t.six, a.minneg, t.has_min,
+                        a.draw_seed ^ (uint64_t) (dev - a.base), 0.02f)) {
+            snprintf(why, nwhy, "%.64s: drawing tiles on the device failed", first->name);
+            a.draw_failed = true;
+            return false;
+        }
+        return true;
+    }
     std::vector<uint8_t> host(total, 0);
     bool bad = false;
 #pragma omp parallel for schedule(dynamic, 16)
