@@ -338,6 +338,7 @@ def main():
                   "moe_cfg2": extra(moe_microbench, peak0),
                   "decode_cfg3": extra(decode_cfg3, peak0), "decode_cfg3_batch64": extra(decode_cfg3_batch, peak0),
                   "decode_cfg4": extra(decode_cfg4, peak0),
+                  "decode_cfg4_batch64": extra(decode_cfg4_batch, peak0),
                   "prefill_cfg0": extra(lambda: prefill_bench(model_path(cf.CONFIGS["qwen2.5-1.5b-q4"], 0, None),
                                                               PROMPT_LEN)),
                   "prefill_cfg3": extra(lambda: prefill_bench(model_path(cf.CONFIGS["llama3-8b-q4k"], 0, None),
@@ -551,6 +552,49 @@ def decode_cfg3_batch(peak, n_seq=64, prompt=2048, ngen=256, nwarm=4):
         b.close()
 
 
+def decode_cfg4_batch(peak, n_seq=64, prompt=1024, ngen=32, nwarm=2):
+    """Configuration 4 as batched serving on one GPU: n_seq sequences of a
+    `prompt`-id random prompt stepped through the batched engine, then ngen
+    greedy tokens each decoded together: per MoE layer the router and the
+    chosen experts of all n_seq rows on the tensor cores (f16, codes decoded
+    in shared memory), the attention products on the int8 tensor-core path.
+    Experts drawn on the device (the direct=2 file). Bytes per step: the
+    attention and head weights once (as stored), every expert (at 64 rows x 8
+    choices almost all of the 128 are chosen in every layer) and the KV caches
+    up to each position."""
+    import sheep_b200
+    from sheep_b200 import configs
+    spec = configs.CONFIGS["qwen3-235b-a22b-q4"]
+    path = model_path(spec, 0, None)
+    n_ctx = prompt + nwarm + ngen
+    sheep_b200.draw_experts(235)
+    t0 = time.time()
+    try:
+        b = sheep_b200.Batch(path, n_seq, n_ctx)
+    finally:
+        sheep_b200.draw_experts(0)
+    t_open = time.time() - t0
+    try:
+        prompts = np.random.default_rng(65).integers(0, b.n_vocab, (n_seq, prompt)).astype(np.int32)
+        t0 = time.time()
+        ids, ms = b.generate(prompts, ngen, nwarm=nwarm, timed=True)
+        t_run = time.time() - t0
+        steps = ngen - 1
+        tps = n_seq * steps / (ms / 1000.0)
+        kv_row = spec["n_layer"] * 2 * spec["n_head_kv"] * spec["head_dim"] * 2
+        first = prompt + nwarm + 1
+        kv_step = n_seq * kv_row * (first + (steps - 1) / 2.0 + 1)
+        alg = b.file_bytes + b.expert_bytes + kv_step
+        return {"n_seq": n_seq, "prompt": prompt, "generated": ngen, "tok_s": round(tps, 1),
+                "ms_per_step": round(ms / steps, 3), "bytes_per_step_alg": int(alg),
+                "gbs_alg": round(alg * steps / (ms / 1000.0) / 1e9, 1),
+                "frac_alg": round(alg * steps / (ms / 1000.0) / 1e9 / peak, 4),
+                "experts": "drawn on the device (direct=2 file); expert products on the tensor cores",
+                "launches_per_step": b.launches, "open_s": round(t_open, 1), "run_s": round(t_run, 1)}
+    finally:
+        b.close()
+
+
 def gemm_tc_microbench(peak, reps=20):
     """Configuration 1's matrices at 16/64/256 rows of x on the tensor cores
     (the batched path's int8 arithmetic): TOPS of the int8 products and GB/s
@@ -614,11 +658,16 @@ def moe_microbench(peak, reps=20):
     out = []
     try:
         for T in (1, 16, 64, 256):
-            ms, na = m.time(fp16_rows(100 + T, T, m.n_embd), reps)
-            nbytes = na * m.expert_bytes + m.router_bytes
-            gbs = nbytes / (ms / 1000.0) / 1e9
-            out.append({"tokens": T, "us": round(ms * 1000.0, 2), "tok_s": round(T / (ms / 1000.0), 1),
-                        "experts_read": na, "bytes": nbytes, "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)})
+            # 16+ rows: the tensor-core path (the default), then the integer kernels
+            for tc in ((True, False) if T >= 16 else (False,)):
+                m.tensor_cores(tc)
+                ms, na = m.time(fp16_rows(100 + T, T, m.n_embd), reps)
+                nbytes = na * m.expert_bytes + m.router_bytes
+                gbs = nbytes / (ms / 1000.0) / 1e9
+                out.append({"tokens": T, "path": "tensor cores (f16)" if tc else "integer (dp4a)",
+                            "us": round(ms * 1000.0, 2), "tok_s": round(T / (ms / 1000.0), 1),
+                            "experts_read": na, "bytes": nbytes, "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)})
+            m.tensor_cores(True)
     finally:
         m.close()
     return out

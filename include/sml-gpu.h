@@ -30,9 +30,11 @@ const float * sml_gpu_step(int tok, int pos);
 // sml/sml-gpu.h:20 -- layers on the card, and (in *of) of how many.
 int sml_gpu_layers(int * of);
 
-// sml/sml-gpu.h:26 -- how a prompt is read. Every level reads it through the
-// decode graph here, a token at a time, so the level is recorded and has no
-// other effect.
+// sml/sml-gpu.h:26 -- how a prompt is read (sml/sml-gpu-fwd.c:2420-2423):
+// 0 and 1 step every token through the decode graph (the decode arithmetic,
+// bit for bit); 2, the default, reads all but the last token in chunks of 64
+// on the tensor cores (int8 re-quantized weights, per-256 activations) and
+// steps the last. Applies to the open model and to later opens.
 void sml_gpu_prompt_mode(int level);
 
 // sml/sml-gpu.h:28 -- no CPU decode exists in this engine: always returns 0.

@@ -102,6 +102,7 @@ def lib():
         "sb_moe_time": (ip, [vp, vp, ip, ip, fp, vp]),
         "sb_moe_route": (ip, [vp, ip, ip, ip, ctypes.c_uint, vp, vp, vp]),
         "sb_moe_last_error": (cp, []),
+        "sb_moe_set_tensor_cores": (ip, [vp, ip]),
         "sb_moe_open_ep": (vp, [cp, ip, ip, ip, ip, vp, cp, ip]),
         "sb_nccl_unique_id": (ip, [vp]),
         "sb_tc_imma": (ip, [vp, vp, vp, ip, ip, ip, vp, vp]),
@@ -399,6 +400,11 @@ class MoeLayer:
         if not lib().sb_moe_forward_host(self.h, _p(x), T, _p(y), _p(sel), _p(w), ctypes.byref(na)):
             raise RuntimeError(f"sb_moe_forward_host: {lib().sb_moe_last_error().decode()}")
         return y, sel, w, na.value
+
+    def tensor_cores(self, on):
+        """Calls of 16+ rows on the tensor cores (on, the default) or on the
+        integer kernels; returns whether this handle can use the tensor cores."""
+        return bool(lib().sb_moe_set_tensor_cores(self.h, 1 if on else 0))
 
     def forward_dev(self, x_ptr, n_tok, y_ptr, stream=0):
         if not lib().sb_moe_forward(self.h, x_ptr, n_tok, y_ptr, stream):

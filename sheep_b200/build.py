@@ -16,6 +16,8 @@ OBJ = os.path.join(HERE, "_build")
 LIB = os.path.join(HERE, "lib", "libsheep_b200.so")
 LIB_CHECKED = os.path.join(HERE, "lib", "libsheep_b200_checked.so")
 LIB_TRACE = os.path.join(HERE, "lib", "libsheep_b200_trace.so")
+CLI_SRC = os.path.join(HERE, "cli", "sml_gpu_fwd.c")
+CLI = os.path.join(HERE, "lib", "sml-gpu-fwd")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr", "-Xcompiler", "-fopenmp",
@@ -77,6 +79,8 @@ def build(verbose=False, force=False, checked=False, trace=False):
     cu, c = _sources()
     deps = _deps()
     if not force and not _stale(lib, deps):
+        if lib == LIB:
+            build_cli(verbose)
         return lib
     extra = (["-DSB_CHECKED"] if checked else []) + (["-DSB_TRACE"] if trace else [])
     nvcc, cc = _nvcc(), _cc()
@@ -97,7 +101,20 @@ def build(verbose=False, force=False, checked=False, trace=False):
         for l in logs:
             if l.strip():
                 print(l)
+    if lib == LIB:
+        build_cli(verbose, force=True)
     return lib
+
+
+def build_cli(verbose=False, force=False):
+    """The sml-gpu-fwd command line (sheep_b200/cli), linked against the
+    in-tree library (found next to it at run time)."""
+    deps = [CLI_SRC, LIB] + [os.path.join(ROOT, "include", f) for f in os.listdir(os.path.join(ROOT, "include"))]
+    if not force and not _stale(CLI, deps):
+        return CLI
+    _run([_cc(), "-O2", "-std=gnu11", "-Wall", "-I" + os.path.join(ROOT, "include"), CLI_SRC, "-o", CLI,
+          "-L" + os.path.dirname(LIB), "-lsheep_b200", "-Wl,-rpath,$ORIGIN", "-lm"], verbose)
+    return CLI
 
 
 if __name__ == "__main__":

@@ -386,7 +386,8 @@ static void b_enqueue(sb_batch * b) {
             // router on rmsnorm(x) per row, the chosen experts, combine added to x
             snprintf(b->cur, sizeof b->cur, "L%d.moe", l);
             moe_enqueue(y.ml, b->ms, b->x, b->B, y.fn, b->eps, b->x, 1, b->nsm, b->st, false, b->err, nullptr,
-                        b->launches, [&](cudaError_t r, const char *) { b_after(b, r); });
+                        b->launches, [&](cudaError_t r, const char *) { b_after(b, r); }, nullptr, nullptr, 0.0f,
+                        true);
             continue;
         }
         snprintf(b->cur, sizeof b->cur, "L%d.ffn", l);

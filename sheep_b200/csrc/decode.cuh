@@ -277,6 +277,9 @@ SB_DEV void cp_async16(void * dst, const void * src) {
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_u32(dst)), "l"(src) : "memory");
 }
 SB_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+SB_DEV void cp_async_group() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+SB_DEV void cp_async_wait_group() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
 
 // Shared memory of k_attn_seq: q, k, v, cos, sin, a score per position, and
 // the K and V rows of the first kSeqCap positions (K rows padded by 16 bytes so
@@ -295,7 +298,9 @@ __host__ __device__ inline size_t attn_seq_smem_bytes(int hd, int n_ctx) {
 //   out[d]     = fma chain over positions 0..pos in order (one thread per dim).
 // The cached rows (positions before pos, up to kSeqCap of them) do not depend on
 // the previous kernel: they are copied into shared memory (cp.async) before
-// the dependency wait; positions past kSeqCap are read from the cache in place.
+// the dependency wait; past kSeqCap, keys are read from the cache in place and
+// values pass through the keys' staging area (free once the scores are done)
+// in double-buffered blocks of kSeqCap / 2 rows.
 // After the wait: Q/K norm if any, RoPE (rope_ref), the new key/value rounded
 // to fp16, written to the cache by the group's first head and into this CTA's
 // staged rows. The serial loops (the softmax sum, each dim's chain) load a
@@ -415,20 +420,21 @@ __global__ void __launch_bounds__(kSeqThreads) k_attn_seq(const __grid_constant_
     for (int t = tid; t < np; t += blockDim.x) sc[t] = __fmul_rn(sc[t], inv);
     __syncthreads();
     SB_MARK(g.trace, g.launch_id, 7);
-    if (tid < hd / 2) {
-        // two dims per thread (one 4-byte load of V per position), two chains
-        const int d = 2 * tid;
-        float o0 = 0.0f, o1 = 0.0f;
-        const int ns = np < cap ? np : cap;
-        const uint32_t * vcol = reinterpret_cast<const uint32_t *>(Vs + d);
-        int t = 0;
-        for (; t + 32 <= ns; t += 32) {
+    // two dims per thread (one 4-byte load of V per position), two chains over
+    // the positions in order: rows [t0, t1) of a staged block V0 (row t at
+    // V0 + (t - t0) * hd), a block of 32 loaded before its arithmetic
+    const int d = 2 * tid;
+    float o0 = 0.0f, o1 = 0.0f;
+    auto chain = [&](const uint16_t * V0, int t0, int t1) {
+        const uint32_t * vcol = reinterpret_cast<const uint32_t *>(V0 + d);
+        int t = t0;
+        for (; t + 32 <= t1; t += 32) {
             float4 p[8];
             uint32_t v[32];
 #pragma unroll
             for (int u = 0; u < 8; u++) p[u] = *reinterpret_cast<const float4 *>(sc + t + 4 * u);
 #pragma unroll
-            for (int u = 0; u < 32; u++) v[u] = vcol[(size_t) (t + u) * (hd / 2)];
+            for (int u = 0; u < 32; u++) v[u] = vcol[(size_t) (t - t0 + u) * (hd / 2)];
 #pragma unroll
             for (int u = 0; u < 8; u++) {
                 const float pp[4] = {p[u].x, p[u].y, p[u].z, p[u].w};
@@ -440,17 +446,43 @@ __global__ void __launch_bounds__(kSeqThreads) k_attn_seq(const __grid_constant_
                 }
             }
         }
-        for (; t < ns; t++) {
-            const uint32_t vv = vcol[(size_t) t * (hd / 2)];
+        for (; t < t1; t++) {
+            const uint32_t vv = vcol[(size_t) (t - t0) * (hd / 2)];
             o0 = __fmaf_rn(sc[t], h2f((uint16_t) (vv & 0xffffu)), o0);
             o1 = __fmaf_rn(sc[t], h2f((uint16_t) (vv >> 16)), o1);
         }
-        for (; t < np; t++) {
-            o0 = __fmaf_rn(sc[t], h2f(g.vc[(size_t) t * g.kvd + row0 + d]), o0);
-            o1 = __fmaf_rn(sc[t], h2f(g.vc[(size_t) t * g.kvd + row0 + d + 1]), o1);
+    };
+    const int ns = np < cap ? np : cap;
+    if (tid < hd / 2) chain(Vs, 0, ns);
+    if (np > cap) {
+        // rows past the staged ones: blocks of VB rows through the keys' area
+        // (2 VB rows of hd fit in its cap rows of hd + 8), the next block's
+        // copies issued before this block's chains
+        const int VB = cap / 2, per = hd / 8;
+        auto issue = [&](uint16_t * buf, int t0) {
+            const int n = (np - t0 < VB ? np - t0 : VB) * per;
+            for (int idx = tid; idx < n; idx += kSeqThreads) {
+                const int r = idx / per, part = idx % per;
+                cp_async16(buf + (size_t) r * hd + part * 8, g.vc + (size_t) (t0 + r) * g.kvd + row0 + part * 8);
+            }
+            cp_async_group();
+        };
+        issue(Ks, cap);
+        int b = 0;
+        for (int t0 = cap; t0 < np; t0 += VB, b ^= 1) {
+            uint16_t * cur = Ks + (size_t) b * VB * hd;
+            if (t0 + VB < np) {
+                issue(Ks + (size_t) (b ^ 1) * VB * hd, t0 + VB);
+                cp_async_wait_group<1>();
+            } else {
+                cp_async_wait_group<0>();
+            }
+            __syncthreads();
+            if (tid < hd / 2) chain(cur, t0, t0 + VB < np ? t0 + VB : np);
+            __syncthreads();   // this buffer is refilled two blocks on
         }
-        *reinterpret_cast<float2 *>(gout + h * hd + d) = make_float2(o0, o1);
     }
+    if (tid < hd / 2) *reinterpret_cast<float2 *>(gout + h * hd + d) = make_float2(o0, o1);
     SB_MARK(g.trace, g.launch_id, 4);
 }
 

@@ -64,6 +64,7 @@ struct sb_moe {
     const ExpfEntry * xtab = nullptr;     // the host libm's expf corrections (expf_libm.h)
     float xnear = 0.0f;
     int nsm = 148, tmax = 0, layer = 0;
+    bool tc = true;                       // calls of 16+ rows on the tensor cores (moe_tc.cu)
     cudaStream_t st = nullptr;
     void * flush = nullptr;               // timing: a buffer larger than L2, rewritten between runs
     size_t flush_n = 0;
@@ -215,8 +216,14 @@ static bool enqueue(sb_moe * h, const float * x, int T, float * y, cudaStream_t 
                         ok = false;
                     }
                 },
-                h->world > 1 ? &h->ex : nullptr, h->xtab, h->xnear);
+                h->world > 1 ? &h->ex : nullptr, h->xtab, h->xnear, h->tc);
     return ok;
+}
+
+extern "C" int sb_moe_set_tensor_cores(sb_moe * h, int on) {
+    if (!h) return 0;
+    h->tc = on != 0;
+    return h->s.tc_chunks > 0 ? 1 : 0;
 }
 
 extern "C" int sb_moe_forward(sb_moe * h, const float * x, int n_tok, float * y, void * stream) {

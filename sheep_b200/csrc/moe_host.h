@@ -34,7 +34,21 @@ struct MoeScratch {
     int T = 0;
     float * xn = nullptr, * hp = nullptr, * yk = nullptr;
     MoeRoute r{};
+    uint8_t * xb = nullptr;           // tensor-core path (moe_tc.cu): the chunks' fp16 B operands
+    int tc_chunks = 0;                // chunks the B operands are sized for (0: no tensor-core path)
 };
+
+// The tensor-core path (moe_tc.cu) for calls of 16 or more rows: whether the
+// layer's experts suit it (four-bit codes, 8-bit group fields, widths in
+// multiples of 128), the most chunks T rows can make, the B-operand scratch
+// for them, and its launches (gather, gate/up, down) after the router.
+bool moe_tc_ok(const MoeLayer & m);
+int moe_tc_chunks(const MoeLayer & m, int T);
+size_t moe_tc_scratch(const MoeLayer & m, int T);
+cudaError_t moe_tc_enqueue(const MoeLayer & m, const MoeScratch & s, const float * in, int T, int nch_max,
+                           cudaStream_t st, bool pdl, int * err);
+constexpr int kMoeTcRows = 16;        // rows per call from which the tensor-core path runs
+constexpr int kMoeTcChunk = 64;       // most rows of one expert per chunk on it
 
 inline uint64_t moe_rec_bytes(const ssf_rec * r) {
     uint64_t b = r->sd_n + r->sq_n + r->md_n + r->mq_n;
@@ -167,6 +181,13 @@ inline void moe_carve(Arena & a, const MoeLayer & m, int T, MoeScratch & s) {
     s.r.ch_n = (int *) a.carve(ns * 4);
     s.r.meta = (int *) a.carve(2 * 4);
     s.r.cnt = (unsigned *) a.carve(4);
+    if (T >= kMoeTcRows && moe_tc_ok(m)) {
+        s.tc_chunks = moe_tc_chunks(m, T);
+        s.xb = (uint8_t *) a.carve(moe_tc_scratch(m, T));
+    } else {
+        s.tc_chunks = 0;
+        s.xb = nullptr;
+    }
 }
 
 // Ring stages of the grouped GEMV for nt staged activations.
@@ -211,13 +232,17 @@ struct MoeExchange {
 // routing (x RMS-normalized by norm_w first when given), gate/up, down, combine
 // into y ([T][E]; added to it when resid). post(err, name) sees every launch.
 // With ex (expert parallelism) the per-choice outputs are zeroed first and
-// summed across GPUs before the combine.
+// summed across GPUs before the combine. With tc, calls of kMoeTcRows rows or
+// more run the expert products on the tensor cores (moe_tc.cu) when the
+// scratch was carved for it.
 template <class Post>
 inline void moe_enqueue(const MoeLayer & m, const MoeScratch & s, const float * x, int T, const float * norm_w,
                         float eps, float * y, int resid, int nsm, cudaStream_t st, bool pdl, int * err,
                         unsigned long long * trace, int launch_id, Post post, const MoeExchange * ex = nullptr,
-                        const ExpfEntry * xtab = nullptr, float xnear = 0.0f) {
-    const int nt = T == 1 ? 1 : 8;   // one token per chunk at T = 1: a token never picks an expert twice
+                        const ExpfEntry * xtab = nullptr, float xnear = 0.0f, bool tc = false) {
+    const bool use_tc = tc && s.tc_chunks > 0 && T >= kMoeTcRows;
+    // one token per chunk at T = 1: a token never picks an expert twice
+    const int nt = use_tc ? kMoeTcChunk : T == 1 ? 1 : 8;
     if (ex) post(cudaMemsetAsync(s.yk, 0, (size_t) T * m.k * m.E * 4, st), "moe.zero");
     {
         MoeRouterArgs r;
@@ -248,23 +273,27 @@ inline void moe_enqueue(const MoeLayer & m, const MoeScratch & s, const float * 
     memset(&g, 0, sizeof g);
     g.slots = s.r.slots; g.ch_e = s.r.ch_e; g.ch_s0 = s.r.ch_s0; g.ch_n = s.r.ch_n; g.meta = s.r.meta;
     g.err = err; g.trace = trace;
-    {
-        MoeGArgs a = g;
-        a.t = m.gu; a.tiles = m.gu_tiles; a.perm = m.gu_perm; a.scatter = m.dn_iperm;
-        a.in = norm_w ? s.xn : x; a.in_stride = m.E; a.in_div = m.k;
-        a.out = s.hp; a.out_stride = m.F; a.ffn_f = m.F;
-        a.nstage = moe_stages(m.gu, nt);
-        a.launch_id = launch_id + 1;
-        post(moe_gemv(MG_GU, nt, a, nsm, st, pdl), "moe.gate_up");
-    }
-    {
-        MoeGArgs a = g;
-        a.t = m.dn; a.tiles = m.dn_tiles;
-        a.in = s.hp; a.in_stride = m.F; a.in_div = 1;
-        a.out = s.yk; a.out_stride = m.E;
-        a.nstage = moe_stages(m.dn, nt);
-        a.launch_id = launch_id + 2;
-        post(moe_gemv(MG_DN, nt, a, nsm, st, pdl), "moe.down");
+    if (use_tc) {
+        post(moe_tc_enqueue(m, s, norm_w ? s.xn : x, T, s.tc_chunks, st, pdl, err), "moe.tensor_cores");
+    } else {
+        {
+            MoeGArgs a = g;
+            a.t = m.gu; a.tiles = m.gu_tiles; a.perm = m.gu_perm; a.scatter = m.dn_iperm;
+            a.in = norm_w ? s.xn : x; a.in_stride = m.E; a.in_div = m.k;
+            a.out = s.hp; a.out_stride = m.F; a.ffn_f = m.F;
+            a.nstage = moe_stages(m.gu, nt);
+            a.launch_id = launch_id + 1;
+            post(moe_gemv(MG_GU, nt, a, nsm, st, pdl), "moe.gate_up");
+        }
+        {
+            MoeGArgs a = g;
+            a.t = m.dn; a.tiles = m.dn_tiles;
+            a.in = s.hp; a.in_stride = m.F; a.in_div = 1;
+            a.out = s.yk; a.out_stride = m.E;
+            a.nstage = moe_stages(m.dn, nt);
+            a.launch_id = launch_id + 2;
+            post(moe_gemv(MG_DN, nt, a, nsm, st, pdl), "moe.down");
+        }
     }
     if (ex) post(ex->sum(ex->ctx, s.yk, (size_t) T * m.k * m.E, st), "moe.exchange");
     {

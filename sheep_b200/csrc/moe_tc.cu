@@ -24,12 +24,13 @@
 //   k_moe_tc<DN>   per (chunk, 128 down rows): the MMA over the hidden width;
 //                  fp32 rows per choice ([T*k][E]), summed by k_moe_comb.
 //
-// A k_moe_tc CTA: warp 4 copies (cp.async.bulk) the 128 rows' group fields for
-// the whole width once, then per 128 columns the rows' code bytes and the B
-// block into a 3-stage ring; warps 0-3 (one A row per thread) decode a stage's
-// codes into its fp16 A block; warp 5 issues the 8 MMAs of K = 16 per stage
-// and commits; after the last, warps 0-3 read the accumulator (TMEM lane =
-// row) for the epilogue. Every wait is bounded and reports an error code.
+// A k_moe_tc CTA: warps 0-3 copy (16-byte asynchronous copies) the 128 rows'
+// group fields for the whole width once, then per 128 columns the rows' code
+// bytes and the B block into a 3-stage ring two chunks ahead, and decode a
+// stage's codes into its fp16 A block (one A row per thread); warp 4 issues
+// the 8 MMAs of K = 16 per stage and commits; after the last, warps 0-3 read
+// the accumulator (TMEM lane = row) for the epilogue. Every wait is bounded
+// and reports an error code.
 #include "moe_host.h"
 #include "tc.cuh"
 
@@ -39,7 +40,7 @@ namespace sb {
 
 constexpr int kXN = 64;                 // most rows of a chunk (the MMA's N)
 constexpr int kXStages = 3;
-constexpr int kXThreads = 192;
+constexpr int kXThreads = 160;
 constexpr uint32_t kXABytes = 128 * 256;          // 128 rows x 128 fp16
 constexpr uint32_t kXBBytes = kXN * 256;          // 64 rows x 128 fp16
 constexpr uint32_t kXCodeBytes = 128 * 64;        // 128 rows x 128 four-bit codes
@@ -125,14 +126,25 @@ SB_DEV bool xt_wait(uint64_t * bar, uint32_t parity, int * err, int code, volati
     return false;
 }
 
+// 16-byte asynchronous copies global -> shared (bypassing L1), in commit groups.
+SB_DEV void xa_cp16(void * dst, const void * src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_u32(dst)), "l"(src) : "memory");
+}
+SB_DEV void xa_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+SB_DEV void xa_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
+
 // MODE: MG_GU (gate / up interleaved tiles, TR/2 gate rows then TR/2 up rows)
-// or MG_DN. Four-bit codes with 8-bit group fields.
+// or MG_DN. Four-bit codes with 8-bit group fields. Warps 0-3 copy (16-byte
+// asynchronous copies, two chunks ahead), decode and run the epilogue; warp 4
+// owns the tensor memory and issues the MMAs.
 template <int MODE>
 __global__ void __launch_bounds__(kXThreads, 1) k_moe_tc(const __grid_constant__ MoeTcArgs g) {
     extern __shared__ __align__(1024) uint8_t xsm[];
-    __shared__ __align__(8) uint64_t full_raw[kXStages], full_a[kXStages], empty[kXStages], fields_full, done;
+    __shared__ __align__(8) uint64_t full_a[kXStages], empty[kXStages], done;
     __shared__ uint32_t tslot;
     __shared__ volatile int fail;
+    __shared__ volatile int cfail[2];
     pdl_launch_dependents();
     const TT & t = g.t;
     const int K = t.cols, TR = t.TR, nkc = K / 128;
@@ -144,19 +156,19 @@ __global__ void __launch_bounds__(kXThreads, 1) k_moe_tc(const __grid_constant__
     uint8_t * fields = xsm + (size_t) kXStages * stage_b;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int mb = blockIdx.x, c = blockIdx.y;
-    if (warp == 5) tmem_alloc(&tslot, 64);
+    if (warp == 4) tmem_alloc(&tslot, 64);
     if (tid == 0) {
-        for (int s = 0; s < kXStages; s++) { mbar_init(&full_raw[s], 1); mbar_init(&full_a[s], 4); mbar_init(&empty[s], 1); }
-        mbar_init(&fields_full, 1);
+        for (int s = 0; s < kXStages; s++) { mbar_init(&full_a[s], 4); mbar_init(&empty[s], 1); }
         mbar_init(&done, 1);
         fail = 0;
+        cfail[0] = cfail[1] = 0;
         mbar_fence_init();
     }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = tslot;
-    if (warp == 5) tmem_relinquish();
+    if (warp == 4) tmem_relinquish();
     pdl_wait();
     const int nch = g.meta[0];
     const bool live = c < nch;
@@ -168,47 +180,7 @@ __global__ void __launch_bounds__(kXThreads, 1) k_moe_tc(const __grid_constant__
     const uint8_t * tiles = live ? g.tiles[e] + (size_t) tile0 * t.tb : nullptr;
     const uint8_t * bsrc = g.bop + (size_t) c * moe_xb_bytes(K);
 
-    if (!live) {
-        // nothing to do; fall through to the common exit
-    } else if (warp == 4) {
-        // ---------------- producer
-        if (lane == 0) mbar_expect_tx(&fields_full, (uint32_t) ntl * fb);
-        __syncwarp();
-        for (int i = lane; i < ntl; i += 32) {
-            const uint8_t * tl = tiles + (size_t) i * t.tb;
-            uint8_t * d = fields + (size_t) i * fb;
-            bulk_g2s(d, tl + tg.sq_off, f_sq, &fields_full);
-            bulk_g2s(d + f_sq, t.has_min ? tl + tg.mq_off : tl + tg.sq_off, f_sq, &fields_full);
-            bulk_g2s(d + 2 * f_sq, tl + tg.sd_off, f_sd, &fields_full);
-            bulk_g2s(d + 2 * f_sq + f_sd, t.has_min ? tl + tg.md_off : tl + tg.sd_off, f_sd, &fields_full);
-        }
-        const uint32_t run = 32u * TR;                        // bytes of two units of one section, one tile
-        for (int kc = 0; kc < nkc; kc++) {
-            const int s = kc % kXStages, lap = kc / kXStages;
-            bool ok = true;
-            if (lap > 0) ok = xt_wait(&empty[s], (lap - 1) & 1, g.err, 120, &fail);
-            ok = __all_sync(0xffffffffu, ok);
-            if (!ok) break;
-            uint8_t * st = xsm + (size_t) s * stage_b;
-            if (lane == 0) {
-                mbar_expect_tx(&full_raw[s], kXCodeBytes + (uint32_t) Np * 256);
-                bulk_g2s(st + kXABytes, bsrc + (size_t) kc * kXBBytes, (uint32_t) Np * 256, &full_raw[s]);
-            }
-            __syncwarp();
-            for (int i = lane; i < ntl; i += 32) {
-                const uint8_t * sec = tiles + (size_t) i * t.tb + tg.pl_off[0] + (size_t) (2 * kc) * TR * 16;
-                uint8_t * d = st + kXABytes + kXBBytes + (size_t) i * 2 * run;
-                bulk_g2s(d, sec, run, &full_raw[s]);
-                bulk_g2s(d + run, sec + tg.pl_sec[0], run, &full_raw[s]);
-            }
-        }
-        // nothing may land after this warp leaves
-        if (lane == 0) {
-            for (int kc = nkc - kXStages > 0 ? nkc - kXStages : 0; kc < nkc; kc++)
-                if (!fail) mbar_wait(&full_raw[kc % kXStages], (kc / kXStages) & 1, g.err, 121);
-            if (!fail) mbar_wait(&fields_full, 0, g.err, 122);
-        }
-    } else if (warp == 5) {
+    if (live && warp == 4) {
         // ---------------- MMA issuer
         if (lane == 0) {
             const uint32_t idesc = (1u << 4) | ((uint32_t) (Np >> 3) << 17) | ((uint32_t) (128 >> 4) << 24);
@@ -226,8 +198,8 @@ __global__ void __launch_bounds__(kXThreads, 1) k_moe_tc(const __grid_constant__
             }
             tc_commit(&done);
         }
-    } else {
-        // ---------------- decode (one A row per thread), then the epilogue
+    } else if (live) {
+        // ---------------- copies, decode (one A row per thread), epilogue
         const int r = tid;                                    // A row 0..127
         int i, j;
         if (MODE == MG_GU) {
@@ -238,15 +210,56 @@ __global__ void __launch_bounds__(kXThreads, 1) k_moe_tc(const __grid_constant__
             i = r / TR;
             j = r % TR;
         }
+        const uint32_t run = 32u * TR, ptile = 2 * run;       // one tile's code bytes per chunk: two runs
+        // chunk kc into stage kc % 3: the rows' code bytes and the chunk's B block
+        auto issue = [&](int kc) {
+            uint8_t * st = xsm + (size_t) (kc % kXStages) * stage_b;
+            const int pr = (int) (run / 16), pt = 2 * pr;
+            for (int p = tid; p < ntl * pt; p += 128) {
+                const int ti = p / pt, rem = p % pt, sec = rem / pr, off = rem % pr;
+                const uint8_t * src = tiles + (size_t) ti * t.tb + tg.pl_off[0] + (sec ? tg.pl_sec[0] : 0) +
+                                      (size_t) (2 * kc) * TR * 16 + (size_t) off * 16;
+                xa_cp16(st + kXABytes + kXBBytes + (size_t) ti * ptile + (size_t) sec * run + (size_t) off * 16, src);
+            }
+            for (int p = tid; p < Np * 16; p += 128)
+                xa_cp16(st + kXABytes + (size_t) p * 16, bsrc + (size_t) kc * kXBBytes + (size_t) p * 16);
+        };
+        // the rows' group fields over the whole width, then the first two chunks
+        {
+            const int pf = (int) (fb / 16);
+            for (int p = tid; p < ntl * pf; p += 128) {
+                const int ti = p / pf;
+                const uint32_t q = (uint32_t) (p % pf) * 16;
+                const uint8_t * tl = tiles + (size_t) ti * t.tb;
+                const uint8_t * src = q < f_sq ? tl + tg.sq_off + q
+                                    : q < 2 * f_sq ? (t.has_min ? tl + tg.mq_off : tl + tg.sq_off) + (q - f_sq)
+                                    : q < 2 * f_sq + f_sd ? tl + tg.sd_off + (q - 2 * f_sq)
+                                    : (t.has_min ? tl + tg.md_off : tl + tg.sd_off) + (q - 2 * f_sq - f_sd);
+                xa_cp16(fields + (size_t) ti * fb + q, src);
+            }
+        }
+        issue(0);
+        xa_commit();
+        if (nkc > 1) issue(1);
+        xa_commit();
         const uint8_t * fl = fields + (size_t) i * fb;
-        const uint32_t run = 32u * TR;
-        bool ok = xt_wait(&fields_full, 0, g.err, 124, &fail);
-        for (int kc = 0; ok && kc < nkc; kc++) {
+        bool ok = true;
+        for (int kc = 0; kc < nkc; kc++) {
             const int s = kc % kXStages;
-            ok = xt_wait(&full_raw[s], (kc / kXStages) & 1, g.err, 125, &fail);
-            if (!ok) break;
+            // chunk kc + 2 into its stage once the MMAs of chunk kc - 1, its last user, are done
+            bool bad = false;
+            if (kc + 2 < nkc) {
+                if (kc >= 1 && !xt_wait(&empty[(kc + 2) % kXStages], ((kc - 1) / kXStages) & 1, g.err, 120, &fail))
+                    bad = true;
+                if (!bad) issue(kc + 2);
+            }
+            xa_commit();
+            xa_wait<2>();                                     // this thread's copies of chunk kc have landed
+            if (bad) cfail[kc & 1] = 1;
+            bar_sync(1, 128);                                 // and every thread's
+            if (cfail[kc & 1]) { ok = false; break; }
             uint8_t * As = xsm + (size_t) s * stage_b;
-            const uint8_t * raw = As + kXABytes + kXBBytes + (size_t) i * 2 * run;
+            const uint8_t * raw = As + kXABytes + kXBBytes + (size_t) i * ptile;
             // fields of the quad kc: four groups' sq and mq, the superblock's d and md
             const uint32_t sq4 = *reinterpret_cast<const uint32_t *>(fl + (size_t) (kc * TR + j) * 4);
             const uint32_t mq4 = *reinterpret_cast<const uint32_t *>(fl + f_sq + (size_t) (kc * TR + j) * 4);
@@ -286,16 +299,19 @@ __global__ void __launch_bounds__(kXThreads, 1) k_moe_tc(const __grid_constant__
             put(13, dq8<true>(h0.z, h0.w, sg[3], mg[3]));
             put(14, dq8<true>(h1.x, h1.y, sg[3], mg[3]));
             put(15, dq8<true>(h1.z, h1.w, sg[3], mg[3]));
+            // the B block was written by copies (generic proxy) and A here:
+            // both must be visible to the tensor core's reads
             fence_proxy_async_smem();
             __syncwarp();
             if (lane == 0) mbar_arrive(&full_a[s]);
         }
+        xa_wait<0>();                                         // no copy lands after the CTA leaves
         ok = ok && xt_wait(&done, 0, g.err, 126, &fail);
-        // every converter warp knows whether the CTA failed before it reads TMEM
+        // every copy/decode warp knows whether the CTA failed before it reads TMEM
         bar_sync(1, 128);
         ok = ok && !fail;
         const int q = warp;                                   // TMEM lanes 32 q .. 32 q + 31
-        float d[kXN];
+        float dv[kXN];
         if (ok) {
             tc_fence_after();
 #pragma unroll
@@ -304,7 +320,7 @@ __global__ void __launch_bounds__(kXThreads, 1) k_moe_tc(const __grid_constant__
                     uint32_t r8[8];
                     tmem_ld8(tmem + ((uint32_t) (32 * q) << 16) + (uint32_t) cc, r8);
 #pragma unroll
-                    for (int k = 0; k < 8; k++) d[cc + k] = __uint_as_float(r8[k]);
+                    for (int k = 0; k < 8; k++) dv[cc + k] = __uint_as_float(r8[k]);
                 }
             }
             tmem_wait_ld();
@@ -313,24 +329,23 @@ __global__ void __launch_bounds__(kXThreads, 1) k_moe_tc(const __grid_constant__
             if (ok) {
                 const int row = 128 * mb + r;
                 for (int tt = 0; tt < ntok; tt++)
-                    g.out[(size_t) g.slots[s0 + tt] * g.out_stride + row] = d[tt];
+                    g.out[(size_t) g.slots[s0 + tt] * g.out_stride + row] = dv[tt];
             }
         } else {
             // up rows (TMEM lanes 64..127) to the gate rows' threads through
             // shared memory (stage 0's A block: every MMA is done)
             float * xch = reinterpret_cast<float *>(xsm);
             if (ok && r >= 64)
-                for (int tt = 0; tt < ntok; tt++) xch[(r - 64) * (kXN + 1) + tt] = d[tt];
+                for (int tt = 0; tt < ntok; tt++) xch[(r - 64) * (kXN + 1) + tt] = dv[tt];
             bar_sync(1, 128);
             if (ok && r < 64) {
                 const int f = 64 * mb + r;
                 const int k = g.scatter[e][f];
-                const int nkd = g.ffn_f / 128;
                 uint8_t * blk = g.hb + (size_t) c * moe_xb_bytes(g.ffn_f) + (size_t) (k >> 7) * kXBBytes;
-                if (SB_CHECK(g.err, k >= 0 && k < g.ffn_f && (k >> 7) < nkd, 127)) {
+                if (SB_CHECK(g.err, k >= 0 && k < g.ffn_f, 127)) {
                     for (int tt = 0; tt < Np; tt++) {
-                        const float h = tt < ntok ? silu_mul(d[tt], xch[r * (kXN + 1) + tt]) : 0.0f;
-                        *reinterpret_cast<__half *>(blk + tc_off(Np, tt, 2 * (k & 127))) = __float2half_rn(h);
+                        const float hv = tt < ntok ? silu_mul(dv[tt], xch[r * (kXN + 1) + tt]) : 0.0f;
+                        *reinterpret_cast<__half *>(blk + tc_off(Np, tt, 2 * (k & 127))) = __float2half_rn(hv);
                     }
                 }
             }
@@ -338,7 +353,7 @@ __global__ void __launch_bounds__(kXThreads, 1) k_moe_tc(const __grid_constant__
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == 4) {
         tc_fence_after();
         tmem_dealloc(tmem, 64);
     }
@@ -399,8 +414,17 @@ cudaError_t moe_tc_enqueue(const MoeLayer & m, const MoeScratch & s, const float
         const size_t smem = moe_tc_smem(m.E, m.gu.TR, m.gu.has_min);
         static bool attr = false;
         if (!attr) {
-            cudaFuncSetAttribute(k_moe_tc<MG_GU>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-            cudaFuncSetAttribute(k_moe_tc<MG_DN>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+            // the dynamic limit: the device's opt-in maximum less the kernel's static shared memory
+            int dev = 0, optin = 0;
+            cudaGetDevice(&dev);
+            cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+            cudaFuncAttributes fa;
+            if (cudaFuncGetAttributes(&fa, k_moe_tc<MG_GU>) == cudaSuccess)
+                cudaFuncSetAttribute(k_moe_tc<MG_GU>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     optin - (int) fa.sharedSizeBytes);
+            if (cudaFuncGetAttributes(&fa, k_moe_tc<MG_DN>) == cudaSuccess)
+                cudaFuncSetAttribute(k_moe_tc<MG_DN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     optin - (int) fa.sharedSizeBytes);
             attr = true;
         }
         cfg.gridDim = dim3(m.F / 64, nch_max);

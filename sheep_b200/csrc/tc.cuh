@@ -71,6 +71,16 @@ SB_DEV void tc_mma_s8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t 
                  : "memory");
 }
 
+// D (TMEM, fp32) = A * B^T (+ D), fp16 operands (kind::f16), one thread issues.
+SB_DEV void tc_mma_f16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, bool accumulate) {
+    const uint32_t z = 0;
+    asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+                 "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n\t}"
+                 :: "r"(tmem_d), "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t) accumulate),
+                    "r"(z), "r"(z), "r"(z), "r"(z)
+                 : "memory");
+}
+
 // Arrive once on *bar when every MMA this thread issued before has completed.
 SB_DEV void tc_commit(uint64_t * bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"

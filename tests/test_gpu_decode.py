@@ -55,6 +55,17 @@ def test_decode_bit_exact_against_oracle(cfg):
     assert _first_diff(got, want) is None, _first_diff(got, want)
 
 
+def test_decode_long_context_bit_exact():
+    """Positions past the attention's 192 staged rows (keys read in place,
+    values through double-buffered blocks of 96 rows): 300 teacher-forced
+    positions, two blocks and a partial one past the staged rows, every logit
+    bit-equal to the oracle's."""
+    path = helpers.model_path(sheep_b200.spec_for("tiny-q4"))
+    toks = np.random.default_rng(31).integers(0, 1024, 300)
+    got, want = _teacher_forced(path, toks, n_ctx=320)
+    assert _first_diff(got, want) is None, _first_diff(got, want)
+
+
 @pytest.mark.parametrize("nb,six", WIDTHS)
 def test_decode_every_width_bit_exact(nb, six):
     """Every code width Q2..Q8 with 8- and 6-bit group fields: the ladder,

@@ -87,7 +87,9 @@ def test_route_rejects_bad_arguments():
 
 
 def _check_layer(path, T, seed, layer=0):
+    """The integer kernels (tensor cores off) against the oracle."""
     m = sheep_b200.MoeLayer(path, layer=layer, max_tokens=max(T, 1))
+    m.tensor_cores(False)
     orc = helpers.Oracle(path, n_ctx=64)
     try:
         x = _rows(seed, T, m.n_embd)
@@ -142,8 +144,108 @@ def test_rows_do_not_depend_on_the_batch():
                                seed=42)
     path = helpers.model_path(spec)
     m = sheep_b200.MoeLayer(path, max_tokens=64)
+    m.tensor_cores(False)
     try:
         x = _rows(5, 64, m.n_embd)
+        a = m.forward(x[:16])[0]
+        b = m.forward(x)[0][:16]
+        c = m.forward(x[::-1].copy())[0][::-1][:16]
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))
+        assert np.array_equal(a.view(np.uint32), c.view(np.uint32))
+    finally:
+        m.close()
+
+
+# The tensor-core path (calls of 16+ rows): fp16 weights decoded from the
+# four-bit codes, fp16 rows, fp32 sums. Checked against the layer computed
+# exactly (float64 over the dequantized weights): per row within 3e-3 relative
+# RMS (fp16 rounding of both operands and of the hidden vector). The decode
+# arithmetic (int8 rows per 32 before each product, the reference's) is itself
+# ~1e-2 from exact at these shapes, so the two paths differ by about that much.
+TC_EXACT = 3e-3
+TC_VS_DECODE = 3e-2
+
+
+def _exact_layer(orc, path, x, sel, w, layer=0):
+    """The MoE FFN in float64 over the oracle's dequantized weights: each
+    chosen expert's SiLU(gate x) * (up x), its down product, weighted sum."""
+    T, E = x.shape
+    recs = helpers.read_records(path)
+    y = np.zeros((T, E), np.float64)
+    for e in np.unique(sel):
+        g, u, d = (f"blk.{layer}.ffn_{n}.{e}.weight" for n in ("gate", "up", "down"))
+        F = recs[g]["rows"]
+        Wg = np.array([orc.dequant_row(g, r, E) for r in range(F)], np.float64)
+        Wu = np.array([orc.dequant_row(u, r, E) for r in range(F)], np.float64)
+        Wd = np.array([orc.dequant_row(d, r, F) for r in range(E)], np.float64)
+        pg, pd = helpers.read_perm(path, g), helpers.read_perm(path, d)
+        for t, j in zip(*np.nonzero(sel == e)):
+            xg = x[t].astype(np.float64)[pg]          # column k of gate/up takes x[perm[k]]
+            a, b = Wg @ xg, Wu @ xg
+            h = a / (1.0 + np.exp(-a)) * b
+            y[t] += float(w[t, j]) * (Wd @ h[pd])
+    return y
+
+
+def _check_tc(path, T, seed, exact=True):
+    m = sheep_b200.MoeLayer(path, max_tokens=T)
+    orc = helpers.Oracle(path, n_ctx=64)
+    try:
+        assert m.tensor_cores(True)
+        x = _rows(seed, T, m.n_embd)
+        y, sel, w, n_active = m.forward(x)
+        m.tensor_cores(False)
+        yi = m.forward(x)[0]
+        yo, so, wo = orc.moe_ffn(0, x)
+        assert np.array_equal(sel, so)
+        assert np.allclose(w, wo, rtol=W_RTOL, atol=0)
+        # the layer's input rows as the experts see them (no norm in sb_moe: x itself)
+        errs_d = np.array([helpers.rel_rms(yo[t], y[t]) for t in range(T)])
+        errs_i = np.array([helpers.rel_rms(yi[t], y[t]) for t in range(T)])
+        print(f"T={T}: tensor cores vs decode arithmetic rel-RMS median {np.median(errs_d):.2e} max {errs_d.max():.2e}; "
+              f"vs integer kernels max {errs_i.max():.2e}")
+        assert errs_d.max() <= TC_VS_DECODE and errs_i.max() <= TC_VS_DECODE
+        if exact:
+            ye = _exact_layer(orc, path, x, sel, w)
+            errs_e = np.array([helpers.rel_rms(ye[t], y[t]) for t in range(T)])
+            errs_de = np.array([helpers.rel_rms(ye[t], yo[t]) for t in range(T)])
+            print(f"T={T}: vs exact: tensor cores max {errs_e.max():.2e} median {np.median(errs_e):.2e}; "
+                  f"decode arithmetic max {errs_de.max():.2e} median {np.median(errs_de):.2e}")
+            assert errs_e.max() <= TC_EXACT, errs_e.max()
+    finally:
+        m.close()
+        orc.close()
+
+
+def test_layer_tensor_cores_cfg2_shape():
+    """The Qwen3-30B-A3B-shaped layer at 16, 64 and 256 tokens a step on the
+    tensor cores: the same routing, outputs within the stated tolerance of the
+    oracle and of the integer kernels."""
+    path = helpers.model_path(sheep_b200.spec_for("qwen3-30b-a3b-moe-layer"))
+    for T in (16, 64, 256):
+        _check_tc(path, T, seed=100 + T, exact=T == 16)
+
+
+def test_layer_tensor_cores_split_chunks():
+    """16 experts, top 4, 256 tokens: most experts get more than 64 rows, so
+    their rows split over several chunks; also a call of exactly 16 rows."""
+    spec = sheep_b200.spec_for("tiny-q4", n_layer=1, n_expert=16, n_expert_used=4, moe_flags=1, expert_ff=256,
+                               seed=43)
+    path = helpers.model_path(spec)
+    _check_tc(path, 256, seed=6)
+    _check_tc(path, 16, seed=7)
+
+
+def test_layer_tensor_cores_rows_independent():
+    """On the tensor cores too a row's output does not depend on the rows
+    sharing its step (its column of the product is its own), bit for bit."""
+    spec = sheep_b200.spec_for("tiny-q4", n_layer=1, n_expert=16, n_expert_used=4, moe_flags=1, expert_ff=256,
+                               seed=44)
+    path = helpers.model_path(spec)
+    m = sheep_b200.MoeLayer(path, max_tokens=96)
+    try:
+        assert m.tensor_cores(True)
+        x = _rows(8, 96, m.n_embd)
         a = m.forward(x[:16])[0]
         b = m.forward(x)[0][:16]
         c = m.forward(x[::-1].copy())[0][::-1][:16]
