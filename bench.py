@@ -556,8 +556,10 @@ def decode_cfg4_batch(peak, n_seq=64, prompt=1024, ngen=32, nwarm=2):
     """Configuration 4 as batched serving on one GPU: n_seq sequences of a
     `prompt`-id random prompt stepped through the batched engine, then ngen
     greedy tokens each decoded together: per MoE layer the router and the
-    chosen experts of all n_seq rows on the tensor cores (f16, codes decoded
-    in shared memory), the attention products on the int8 tensor-core path.
+    chosen experts of all n_seq rows (the automatic choice: at 64 rows x 8
+    choices over 128 experts, 4 rows per expert, the integer kernels, which
+    beat the f16 tensor-core path below 8 rows per expert), the attention
+    products on the int8 tensor-core path.
     Experts drawn on the device (the direct=2 file). Bytes per step: the
     attention and head weights once (as stored), every expert (at 64 rows x 8
     choices almost all of the 128 are chosen in every layer) and the KV caches
@@ -589,7 +591,8 @@ def decode_cfg4_batch(peak, n_seq=64, prompt=1024, ngen=32, nwarm=2):
                 "ms_per_step": round(ms / steps, 3), "bytes_per_step_alg": int(alg),
                 "gbs_alg": round(alg * steps / (ms / 1000.0) / 1e9, 1),
                 "frac_alg": round(alg * steps / (ms / 1000.0) / 1e9 / peak, 4),
-                "experts": "drawn on the device (direct=2 file); expert products on the tensor cores",
+                "experts": "drawn on the device (direct=2 file); expert products on the integer kernels "
+                           "(automatic choice at 4 rows per expert)",
                 "launches_per_step": b.launches, "open_s": round(t_open, 1), "run_s": round(t_run, 1)}
     finally:
         b.close()
@@ -658,7 +661,8 @@ def moe_microbench(peak, reps=20):
     out = []
     try:
         for T in (1, 16, 64, 256):
-            # 16+ rows: the tensor-core path (the default), then the integer kernels
+            # 16+ rows: both paths (the default picks the tensor cores from 8
+            # chosen rows per expert on average: here 128 rows)
             for tc in ((True, False) if T >= 16 else (False,)):
                 m.tensor_cores(tc)
                 ms, na = m.time(fp16_rows(100 + T, T, m.n_embd), reps)
@@ -667,7 +671,7 @@ def moe_microbench(peak, reps=20):
                 out.append({"tokens": T, "path": "tensor cores (f16)" if tc else "integer (dp4a)",
                             "us": round(ms * 1000.0, 2), "tok_s": round(T / (ms / 1000.0), 1),
                             "experts_read": na, "bytes": nbytes, "gbs": round(gbs, 1), "frac": round(gbs / peak, 4)})
-            m.tensor_cores(True)
+            m.tensor_cores("auto")
     finally:
         m.close()
     return out

@@ -202,13 +202,15 @@ int sb_moe_forward_host(sb_moe * m, const float * x, int n_tok, float * y, int *
 // Mean device time (CUDA events) of one forward over rows already on the
 // device, with a buffer larger than L2 rewritten before each timed run.
 int sb_moe_time(sb_moe * m, const float * x_host, int n_tok, int reps, float * ms_avg, int * n_active);
-// Calls of 16 or more rows run the expert products on the tensor cores
-// (tcgen05 kind::f16: the experts' four-bit codes decoded to fp16 in shared
-// memory, rows in fp16, fp32 sums; within about 1e-3 of the decode
-// arithmetic) unless switched off here; fewer rows, and experts that are not
-// four-bit codes with 8-bit group fields, always take the integer kernels.
-// Returns 1 if the handle can use the tensor-core path (max_tokens >= 16 and
-// suitable experts), else 0. On by default.
+// Which calls run the expert products on the tensor cores (tcgen05
+// kind::f16: the experts' four-bit codes decoded to fp16 in shared memory,
+// rows in fp16, fp32 sums; within about 1e-3 of the decode arithmetic):
+// on = 1 every call of 16 or more rows, 0 none, 2 (the default) those whose
+// chosen rows are at least 8 per expert on average (n_tok * k >= 8 * n_expert),
+// where they are faster than the integer kernels. Fewer than 16 rows, and
+// experts that are not four-bit codes with 8-bit group fields, always take the
+// integer kernels. Returns 1 if the handle can use the tensor-core path
+// (max_tokens >= 16 and suitable experts), else 0.
 int sb_moe_set_tensor_cores(sb_moe * m, int on);
 // Routing alone, device pointers: logits[n_tok][n_expert] -> sel, w
 // [n_tok][k] (sml_moe_route, sml/sml-run.c:2925, for moe_flags 0 and 1).

@@ -402,9 +402,11 @@ class MoeLayer:
         return y, sel, w, na.value
 
     def tensor_cores(self, on):
-        """Calls of 16+ rows on the tensor cores (on, the default) or on the
-        integer kernels; returns whether this handle can use the tensor cores."""
-        return bool(lib().sb_moe_set_tensor_cores(self.h, 1 if on else 0))
+        """Calls of 16+ rows on the tensor cores (True), on the integer kernels
+        (False), or "auto" (the default: the tensor cores from 8 chosen rows
+        per expert on average); returns whether this handle can use the tensor
+        cores."""
+        return bool(lib().sb_moe_set_tensor_cores(self.h, 2 if on == "auto" else 1 if on else 0))
 
     def forward_dev(self, x_ptr, n_tok, y_ptr, stream=0):
         if not lib().sb_moe_forward(self.h, x_ptr, n_tok, y_ptr, stream):

@@ -64,7 +64,7 @@ struct sb_moe {
     const ExpfEntry * xtab = nullptr;     // the host libm's expf corrections (expf_libm.h)
     float xnear = 0.0f;
     int nsm = 148, tmax = 0, layer = 0;
-    bool tc = true;                       // calls of 16+ rows on the tensor cores (moe_tc.cu)
+    int tc = MOE_TC_AUTO;                 // MoeTc: which calls run on the tensor cores (moe_tc.cu)
     cudaStream_t st = nullptr;
     void * flush = nullptr;               // timing: a buffer larger than L2, rewritten between runs
     size_t flush_n = 0;
@@ -222,7 +222,7 @@ static bool enqueue(sb_moe * h, const float * x, int T, float * y, cudaStream_t 
 
 extern "C" int sb_moe_set_tensor_cores(sb_moe * h, int on) {
     if (!h) return 0;
-    h->tc = on != 0;
+    h->tc = on == 0 ? MOE_TC_OFF : on == 2 ? MOE_TC_AUTO : MOE_TC_ON;
     return h->s.tc_chunks > 0 ? 1 : 0;
 }
 

@@ -47,7 +47,13 @@ int moe_tc_chunks(const MoeLayer & m, int T);
 size_t moe_tc_scratch(const MoeLayer & m, int T);
 cudaError_t moe_tc_enqueue(const MoeLayer & m, const MoeScratch & s, const float * in, int T, int nch_max,
                            cudaStream_t st, bool pdl, int * err);
-constexpr int kMoeTcRows = 16;        // rows per call from which the tensor-core path runs
+constexpr int kMoeTcRows = 16;        // rows per call from which the tensor-core path can run
+// In the automatic choice the tensor cores take a call whose chosen rows are at
+// least this many per expert on average (T k >= kMoeTcAuto E): below it the
+// integer kernels are faster (configuration 2 measured: integer 190 / 369 us at
+// 16 / 64 rows, the tensor cores 328 / 540; at 256 rows 963 against 793).
+constexpr int kMoeTcAuto = 8;
+enum MoeTc { MOE_TC_OFF = 0, MOE_TC_ON = 1, MOE_TC_AUTO = 2 };
 constexpr int kMoeTcChunk = 64;       // most rows of one expert per chunk on it
 
 inline uint64_t moe_rec_bytes(const ssf_rec * r) {
@@ -232,15 +238,17 @@ struct MoeExchange {
 // routing (x RMS-normalized by norm_w first when given), gate/up, down, combine
 // into y ([T][E]; added to it when resid). post(err, name) sees every launch.
 // With ex (expert parallelism) the per-choice outputs are zeroed first and
-// summed across GPUs before the combine. With tc, calls of kMoeTcRows rows or
-// more run the expert products on the tensor cores (moe_tc.cu) when the
-// scratch was carved for it.
+// summed across GPUs before the combine. tc (MoeTc): ON runs the expert
+// products of calls of kMoeTcRows rows or more on the tensor cores (moe_tc.cu)
+// when the scratch was carved for it; AUTO only those with at least
+// kMoeTcAuto chosen rows per expert on average.
 template <class Post>
 inline void moe_enqueue(const MoeLayer & m, const MoeScratch & s, const float * x, int T, const float * norm_w,
                         float eps, float * y, int resid, int nsm, cudaStream_t st, bool pdl, int * err,
                         unsigned long long * trace, int launch_id, Post post, const MoeExchange * ex = nullptr,
-                        const ExpfEntry * xtab = nullptr, float xnear = 0.0f, bool tc = false) {
-    const bool use_tc = tc && s.tc_chunks > 0 && T >= kMoeTcRows;
+                        const ExpfEntry * xtab = nullptr, float xnear = 0.0f, int tc = MOE_TC_OFF) {
+    const bool use_tc = tc != MOE_TC_OFF && s.tc_chunks > 0 && T >= kMoeTcRows &&
+                        (tc == MOE_TC_ON || (long) T * m.k >= (long) kMoeTcAuto * m.ne);
     // one token per chunk at T = 1: a token never picks an expert twice
     const int nt = use_tc ? kMoeTcChunk : T == 1 ? 1 : 8;
     if (ex) post(cudaMemsetAsync(s.yk, 0, (size_t) T * m.k * m.E * 4, st), "moe.zero");

@@ -16,12 +16,12 @@
 //                RMS-normalized, or SiLU(gate) * up), the B operand, a block of
 //                N x 256 bytes per (N tokens, superblock), and the scale.
 //   k_tcgemm<N>  one CTA per (128 rows, N tokens, slice of the superblocks),
-//                six warps: a producer (bulk copies of both blocks of a
+//                ten warps: a producer (bulk copies of both blocks of a
 //                superblock into a 4-stage ring), an MMA issuer (8 MMAs of
 //                K = 32 per superblock into one of four TMEM accumulators, then
-//                commits), and four epilogue warps (TMEM lanes 0..127 = rows)
-//                that apply the superblock's scales while the next superblock
-//                multiplies. The slices of a tile run as one thread-block
+//                commits), and eight epilogue warps, two per quarter of the TMEM
+//                lanes (rows), each taking half the tokens, that apply the
+//                superblock's scales while the next superblock multiplies. The slices of a tile run as one thread-block
 //                cluster and meet in the leader CTA's shared memory, where
 //                they are added in slice order (split-K). The epilogue may add
 //                a bias or accumulate into y (a residual).
@@ -36,6 +36,8 @@ namespace sb {
 
 constexpr int kTcStages = 4;
 constexpr int kTcAcc = 4;        // TMEM accumulators: the MMAs run up to 3 superblocks ahead of the epilogue
+constexpr int kTcEpiWarps = 8;   // two per quarter of the TMEM lanes, each half of the tokens
+constexpr int kTcThreads = (2 + kTcEpiWarps) * 32;
 
 
 #ifdef SB_TRACE
@@ -156,7 +158,7 @@ SB_DEV bool tc_wait(uint64_t * bar, uint32_t parity, int * err, int code, volati
 }
 
 template <int N>
-__global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArgs g) {
+__global__ void __launch_bounds__(kTcThreads, 1) k_tcgemm(const __grid_constant__ TcArgs g) {
     extern __shared__ __align__(1024) uint8_t tsm[];
     __shared__ __align__(8) uint64_t full[kTcStages], empty[kTcStages], accf[kTcAcc], acce[kTcAcc];
     __shared__ uint32_t tslot;
@@ -174,9 +176,9 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
     const int s0 = z * per, ns = min(g.nsb, s0 + per) - s0;
     if (warp == 1) tmem_alloc(&tslot, ncols);
     if (tid == 0) {
-        // a stage is free once its MMAs are done (commit) and the 4 epilogue warps read its scales
-        for (int s = 0; s < kTcStages; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 5); }
-        for (int b = 0; b < kTcAcc; b++) { mbar_init(&accf[b], 1); mbar_init(&acce[b], 4); }
+        // a stage is free once its MMAs are done (commit) and the epilogue warps read its scales
+        for (int s = 0; s < kTcStages; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], kTcEpiWarps + 1); }
+        for (int b = 0; b < kTcAcc; b++) { mbar_init(&accf[b], 1); mbar_init(&acce[b], kTcEpiWarps); }
         fail = 0;
         mbar_fence_init();
     }
@@ -186,8 +188,11 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
     const uint32_t tmem = tslot;
     if (warp == 1) tmem_relinquish();
     if (tid == 0) TC_MARK(0);
-    const int q = warp & 3, row = 32 * q + lane, r = mb * 128 + row;   // epilogue warps: TMEM lane = row
-    float acc[N];
+    // epilogue warps: TMEM lane = row (a warp may read lanes 32 (warp % 4) ..),
+    // tokens c0 .. c0 + H - 1
+    constexpr int H = N / 2;
+    const int q = warp & 3, row = 32 * q + lane, r = mb * 128 + row, c0 = warp >= 6 ? H : 0;
+    float acc[H];
     bool ok = true;
 
     if (warp == 0) {
@@ -223,8 +228,8 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
             }
         }
     } else {
-        // ---------------- epilogue: TMEM lanes (rows) 32 q .. 32 q + 31
-        for (int t = 0; t < N; t++) acc[t] = 0.0f;
+        // ---------------- epilogue: TMEM lanes (rows) 32 q .. 32 q + 31, tokens c0 ..
+        for (int t = 0; t < H; t++) acc[t] = 0.0f;
         for (int i = 0; i < ns; i++) {
             const int buf = i % kTcAcc, s = i % kTcStages;
             // the stage's scales: landed with its operands, and the stage is held
@@ -232,10 +237,10 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
             ok = ok && tc_wait(&full[s], (i / kTcStages) & 1, g.err, 44, &fail);
             const float * ssc = reinterpret_cast<const float *>(tsm + (size_t) s * SB + kTcABytes + BB);
             const float s8v = ssc[row];
-            float xsv[N];
+            float xsv[H];
 #pragma unroll
-            for (int t = 0; t < N; t += 4) {
-                const float4 v4 = *reinterpret_cast<const float4 *>(ssc + 128 + t);
+            for (int t = 0; t < H; t += 4) {
+                const float4 v4 = *reinterpret_cast<const float4 *>(ssc + 128 + c0 + t);
                 xsv[t] = v4.x; xsv[t + 1] = v4.y; xsv[t + 2] = v4.z; xsv[t + 3] = v4.w;
             }
             __syncwarp();
@@ -243,11 +248,11 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
             ok = ok && tc_wait(&accf[buf], (i / kTcAcc) & 1, g.err, 43, &fail);
             if (i == 0 && tid == 64) TC_MARK(1);
             tc_fence_after();
-            uint32_t d[N];
+            uint32_t d[H];
 #pragma unroll
-            for (int c = 0; c < N; c += 8) {
+            for (int c = 0; c < H; c += 8) {
                 uint32_t r8[8];
-                tmem_ld8(tmem + ((uint32_t) (32 * q) << 16) + (uint32_t) (buf * N + c), r8);
+                tmem_ld8(tmem + ((uint32_t) (32 * q) << 16) + (uint32_t) (buf * N + c0 + c), r8);
 #pragma unroll
                 for (int k = 0; k < 8; k++) d[c + k] = r8[k];
             }
@@ -256,7 +261,7 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
             __syncwarp();
             if (lane == 0) mbar_arrive(&acce[buf]);
 #pragma unroll
-            for (int t = 0; t < N; t++) acc[t] = __fmaf_rn(__fmul_rn(s8v, xsv[t]), (float) (int) d[t], acc[t]);
+            for (int t = 0; t < H; t++) acc[t] = __fmaf_rn(__fmul_rn(s8v, xsv[t]), (float) (int) d[t], acc[t]);
         }
         if (tid == 64) TC_MARK(2);
     }
@@ -272,8 +277,8 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
         if (warp >= 2 && z > 0) {
             const uint32_t base = cluster_map(pbuf + (size_t) (z - 1) * N * 128 + row * 4, 0);
 #pragma unroll
-            for (int t = 0; t < N; t += 4)
-                st_cluster4(base + (uint32_t) (t * 128 * 4), acc[t], acc[t + 1], acc[t + 2], acc[t + 3]);
+            for (int t = 0; t < H; t += 4)
+                st_cluster4(base + (uint32_t) ((c0 + t) * 128 * 4), acc[t], acc[t + 1], acc[t + 2], acc[t + 3]);
         }
         cluster_sync();
         if (warp >= 2) {
@@ -281,8 +286,8 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
                 for (int k = 1; k < g.split; k++) {
                     const float * pk = pbuf + (size_t) (k - 1) * N * 128 + row * 4;
 #pragma unroll
-                    for (int t = 0; t < N; t += 4) {
-                        const float4 v = *reinterpret_cast<const float4 *>(pk + t * 128);
+                    for (int t = 0; t < H; t += 4) {
+                        const float4 v = *reinterpret_cast<const float4 *>(pk + (c0 + t) * 128);
                         acc[t] = __fadd_rn(acc[t], v.x);
                         acc[t + 1] = __fadd_rn(acc[t + 1], v.y);
                         acc[t + 2] = __fadd_rn(acc[t + 2], v.z);
@@ -297,20 +302,20 @@ __global__ void __launch_bounds__(192, 1) k_tcgemm(const __grid_constant__ TcArg
     if (warp >= 2) {
         if (tid == 64) TC_MARK(3);
         if (ok && r < g.rows) {
-            const int nt = min(N, g.T - tb * N);
-            float * yr = g.y + (size_t) tb * N * g.ldy + r;
+            const int nt = min(N, g.T - tb * N) - c0;
+            float * yr = g.y + ((size_t) tb * N + c0) * g.ldy + r;
             if (g.accumulate) {
                 // every token's old value read before any is written (they never alias)
-                float old[N];
+                float old[H];
 #pragma unroll
-                for (int t = 0; t < N; t++) old[t] = t < nt ? yr[(size_t) t * g.ldy] : 0.0f;
+                for (int t = 0; t < H; t++) old[t] = t < nt ? yr[(size_t) t * g.ldy] : 0.0f;
 #pragma unroll
-                for (int t = 0; t < N; t++)
+                for (int t = 0; t < H; t++)
                     if (t < nt) yr[(size_t) t * g.ldy] = __fadd_rn(old[t], acc[t]);
             } else {
                 const float b = g.bias ? g.bias[r] : 0.0f;
 #pragma unroll
-                for (int t = 0; t < N; t++)
+                for (int t = 0; t < H; t++)
                     if (t < nt) yr[(size_t) t * g.ldy] = g.bias ? __fadd_rn(acc[t], b) : acc[t];
             }
         }
@@ -362,7 +367,7 @@ static cudaError_t launch_gemm(const TcArgs & a, cudaStream_t st) {
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.rows_pad / 128, a.T_pad / N, a.split);
-    cfg.blockDim = dim3(192);
+    cfg.blockDim = dim3(kTcThreads);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute at[1];
