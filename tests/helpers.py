@@ -50,6 +50,54 @@ def model_path(spec):
     return path
 
 
+# The letters a-z are the vocabulary's only byte tokens (ids 0..25): a prompt
+# of lowercase letters encodes one id per letter. Every other id but the last is
+# a filler spelled "[id]", the last is the end-of-text special.
+VOCAB_LETTERS = "abcdefghijklmnopqrstuvwxyz"
+
+
+def with_vocab(path):
+    """A copy of the SSF at `path` with a binary vocabulary appended (the
+    layout sml_vocab_init reads, sml/sml-vocab.c:64-79: n_tokens, n_merges,
+    bos, eos, offsets[n_tokens + 1], the token bytes, no merges) and the
+    header's tok_off / tok_n pointing at it. Token strings are in the GPT-2
+    byte-to-symbol spelling the reference's encoder looks up; letters and the
+    characters of "[0123456789]" spell themselves in it."""
+    import struct
+    out = path[:-4] + ".vocab.ssf"
+    if os.path.exists(out):
+        return out
+    with open(path, "rb") as f:
+        data = bytearray(f.read())
+    nv = struct.unpack_from("<I", data, 28)[0]
+    toks = [c.encode() for c in VOCAB_LETTERS]
+    toks += [f"[{i}]".encode() for i in range(len(toks), nv - 1)]
+    toks.append(b"<|endoftext|>")
+    offs, pos = [], 0
+    for t in toks:
+        offs.append(pos)
+        pos += len(t)
+    offs.append(pos)
+    blob = struct.pack("<4I", nv, 0, nv - 1, nv - 1) + struct.pack(f"<{nv + 1}I", *offs) + b"".join(toks)
+    tok_off = (len(data) + 15) // 16 * 16
+    data += b"\0" * (tok_off - len(data)) + blob
+    struct.pack_into("<2Q", data, 100, tok_off, len(blob))   # ssf header: tok_off, tok_n
+    tmp = out + f".tmp{os.getpid()}"
+    with open(tmp, "wb") as f:
+        f.write(data)
+    os.replace(tmp, out)
+    return out
+
+
+def vocab_ids(text):
+    """Token ids of a reply written with with_vocab's vocabulary."""
+    import re
+    ids = []
+    for m in re.finditer(r"\[(\d+)\]|([a-z])", text):
+        ids.append(int(m.group(1)) if m.group(1) else VOCAB_LETTERS.index(m.group(2)))
+    return ids
+
+
 def file_sha(path):
     h = hashlib.sha256()
     with open(path, "rb") as f:
