@@ -267,6 +267,35 @@ const float * sb_batch_device_logits(const sb_batch * b);
 int sb_batch_kv(const sb_batch * b, int layer, int slot, int pos, uint16_t * k, uint16_t * v);
 const char * sb_batch_last_error(void);
 
+// Continuous batching over a paged KV cache. The reference's
+// sml_forward_multi (sml/sml-run.c:2559-2604) takes one context per sequence
+// (cs[b], each owning its cache and positions) for whichever conversations a
+// step runs; sml-server's slots (sml/sml-server.c:1300-1330) pick the context a
+// request continues. Here a sequence is the context: its cache lives in pages
+// of 64 positions taken from one pool (n_pages per layer) as its positions
+// reach them, and a step runs up to n_slots live sequences in any slots, so a
+// sequence can join or leave between any two steps without moving its cache.
+// The arithmetic per slot is sb_forward_multi's: a sequence's logits do not
+// depend on its slot, its pages or the other sequences of the step.
+sb_batch * sb_batch_open_paged(const char * path, int n_slots, int n_ctx, int n_pages, char * why, int nwhy);
+// A new, empty sequence (its id), or -1. Ids of freed sequences are reused.
+int sb_seq_new(sb_batch * b);
+// Give every page of the sequence back to the pool; the id becomes free.
+int sb_seq_free(sb_batch * b, int seq);
+// Keep positions 0 .. n - 1 of the sequence; pages past them go back to the pool.
+int sb_seq_truncate(sb_batch * b, int seq, int n);
+// One step: slot s (s < ns <= n_slots) runs sequence seqs[s] with tokens[s] at
+// absolute position pos[s] (continuing what the sequence holds); slots past ns
+// idle. Pages the positions reach are taken from the pool first; a step whose
+// sequences need more pages than are free fails without changing anything.
+// Returns a host pointer to [ns][n_vocab] logits owned by the library, NULL on
+// failure (a sequence not live or in two slots, ids or positions out of range).
+const float * sb_forward_seqs(sb_batch * b, const int * seqs, const int * tokens, const int * pos, int ns);
+// out (int[4]): pages in the pool, free pages, live sequences, n_ctx.
+void sb_batch_pages(const sb_batch * b, int * out);
+// The cached key and value rows of a sequence at `pos` in `layer` (as sb_batch_kv).
+int sb_seq_kv(const sb_batch * b, int layer, int seq, int pos, uint16_t * k, uint16_t * v);
+
 // ------------------------------------------------------------------ models
 // Seeded synthetic SSF writer (the inputs every test and bench runs on; the
 // reference builds SSF files offline, tooling/sml_quantize.py:596-651).

@@ -116,6 +116,13 @@ def lib():
         "sb_batch_device_logits": (vp, [vp]),
         "sb_batch_last_error": (cp, []),
         "sb_batch_kv": (ip, [vp, ip, ip, ip, vp, vp]),
+        "sb_batch_open_paged": (vp, [cp, ip, ip, ip, cp, ip]),
+        "sb_seq_new": (ip, [vp]),
+        "sb_seq_free": (ip, [vp, ip]),
+        "sb_seq_truncate": (ip, [vp, ip, ip]),
+        "sb_forward_seqs": (fp, [vp, vp, vp, vp, ip]),
+        "sb_batch_pages": (None, [vp, vp]),
+        "sb_seq_kv": (ip, [vp, ip, ip, ip, vp, vp]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -478,6 +485,70 @@ class Batch:
         v = np.zeros(n_kv_dim, np.uint16)
         if not lib().sb_batch_kv(self.h, layer, slot, pos, _p(k), _p(v)):
             raise RuntimeError(f"sb_batch_kv: {lib().sb_batch_last_error().decode()}")
+        return k, v
+
+    def close(self):
+        if self.h:
+            lib().sb_batch_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *a):
+        self.close()
+
+
+class PagedBatch:
+    """Continuous batching over a paged KV cache (sb_batch_open_paged): up to
+    n_slots live sequences per step, in any slots, each holding pages of 64
+    positions from a pool of n_pages."""
+
+    def __init__(self, path, n_slots, n_ctx, n_pages):
+        why = ctypes.create_string_buffer(512)
+        self.h = lib().sb_batch_open_paged(path.encode(), n_slots, n_ctx, n_pages, why, 512)
+        if not self.h:
+            raise RuntimeError(f"sb_batch_open_paged: {why.value.decode()}")
+        info = (ctypes.c_int * 16)()
+        lib().sb_batch_info(self.h, info)
+        self.n_slots, self.n_ctx, self.n_vocab = info[0], info[1], info[2]
+
+    def new_seq(self):
+        s = lib().sb_seq_new(self.h)
+        if s < 0:
+            raise RuntimeError(f"sb_seq_new: {lib().sb_batch_last_error().decode()}")
+        return s
+
+    def free_seq(self, seq):
+        if not lib().sb_seq_free(self.h, seq):
+            raise RuntimeError(f"sb_seq_free: {lib().sb_batch_last_error().decode()}")
+
+    def truncate(self, seq, n):
+        if not lib().sb_seq_truncate(self.h, seq, n):
+            raise RuntimeError(f"sb_seq_truncate: {lib().sb_batch_last_error().decode()}")
+
+    def forward(self, seqs, tokens, pos):
+        """logits [len(seqs), n_vocab]: slot s runs sequence seqs[s] with tokens[s] at pos[s]."""
+        q = np.ascontiguousarray(seqs, np.int32)
+        t = np.ascontiguousarray(tokens, np.int32)
+        p = np.ascontiguousarray(pos, np.int32)
+        assert len(q) == len(t) == len(p)
+        r = lib().sb_forward_seqs(self.h, _p(q), _p(t), _p(p), len(q))
+        if not r:
+            raise RuntimeError(f"sb_forward_seqs: {lib().sb_batch_last_error().decode()}")
+        return np.ctypeslib.as_array(r, shape=(len(q) * self.n_vocab,)).reshape(len(q), self.n_vocab).copy()
+
+    def pages(self):
+        """(pages in the pool, free pages, live sequences)."""
+        out = (ctypes.c_int * 4)()
+        lib().sb_batch_pages(self.h, out)
+        return out[0], out[1], out[2]
+
+    def kv(self, layer, seq, pos, n_kv_dim):
+        k = np.zeros(n_kv_dim, np.uint16)
+        v = np.zeros(n_kv_dim, np.uint16)
+        if not lib().sb_seq_kv(self.h, layer, seq, pos, _p(k), _p(v)):
+            raise RuntimeError("sb_seq_kv failed")
         return k, v
 
     def close(self):

@@ -20,8 +20,14 @@
 //
 // HBM layout: the int8 weights as 32 KB (128 rows x 256 columns) blocks in the
 // tensor cores' operand layout, q|k|v and gate|up each one tensor (segments
-// padded to 128 rows); the KV cache [layer][seq][kv head][n_ctx][hd] fp16, so a
-// chunk of one head's positions is one contiguous bulk copy.
+// padded to 128 rows); the KV cache in pages of 64 positions,
+// [layer][page][kv head][64][hd] fp16, so a chunk of one head's positions is
+// one contiguous copy. Each slot reads its positions through a page table
+// ([slot][n_ctx / 64] page ids): fixed pages per slot for sb_batch_open
+// (slot s owns pages s * maxp ..), or pages from a shared pool that
+// sequences take as they grow and give back when freed (sb_batch_open_paged,
+// sb_forward_seqs): continuous batching, where a sequence joins or leaves the
+// step between any two steps and may run in any slot.
 #include "batch.cuh"
 #include "moe_host.h"
 #include "tc_batch.h"
@@ -99,6 +105,13 @@ struct sb_batch {
     float * x = nullptr, * qkv = nullptr, * att = nullptr, * hid = nullptr, * logits = nullptr;
     uint16_t * kc = nullptr, * vc = nullptr;
     float * rcos = nullptr, * rsin = nullptr;
+    int maxp = 0, n_pages = 0;        // pages of 64 positions a sequence can hold; pages in the cache
+    int * pages = nullptr;            // device [B][maxp]: each slot's page table for the step
+    int * h_pages = nullptr;          // pinned staging of the tables (paged handles)
+    bool paged = false;               // sequences on pooled pages (sb_forward_seqs), not fixed slots
+    std::vector<std::vector<int>> seq_pages;   // paged: each sequence's pages in position order
+    std::vector<char> seq_live;
+    std::vector<int> free_pages, free_seqs;
     int * tok = nullptr, * pos = nullptr, * tlog = nullptr;
     uint8_t * xblk = nullptr;
     float * xs = nullptr, * apart = nullptr;
@@ -271,9 +284,10 @@ static bool b_build(sb_batch * b, char * why, int nwhy) {
     b->att = (float *) b->ar.carve((size_t) B * b->qd * 4);
     b->hid = (float *) b->ar.carve((size_t) B * 2 * b->Fp * 4);
     b->logits = (float *) b->ar.carve((size_t) B * b->head.rows * 4);
-    const size_t kv = (size_t) b->n_layer * B * b->nkv * b->n_ctx * b->hd * 2;
+    const size_t kv = (size_t) b->n_layer * b->n_pages * b->nkv * 64 * b->hd * 2;
     b->kc = (uint16_t *) b->ar.carve(kv);
     b->vc = (uint16_t *) b->ar.carve(kv);
+    b->pages = (int *) b->ar.carve((size_t) B * b->maxp * 4);
     b->rcos = (float *) b->ar.carve((size_t) b->n_ctx * (b->hd / 2) * 4);
     b->rsin = (float *) b->ar.carve((size_t) b->n_ctx * (b->hd / 2) * 4);
     b->tok = (int *) b->ar.carve((size_t) B * 4);
@@ -352,9 +366,10 @@ static void b_attn(sb_batch * b, const BLayer & y, int l) {
     a.qkv = b->qkv; a.ldq = b->qkv_rows; a.koff = b->koff; a.voff = b->voff;
     a.n_head = b->nh; a.n_kv = b->nkv; a.qn = y.qn; a.kn = y.kn; a.eps = b->eps;
     a.rcos = b->rcos; a.rsin = b->rsin;
-    const size_t per_layer = (size_t) b->B * b->nkv * b->n_ctx * b->hd;
+    const size_t per_layer = (size_t) b->n_pages * b->nkv * 64 * b->hd;
     a.kc = b->kc + (size_t) l * per_layer;
     a.vc = b->vc + (size_t) l * per_layer;
+    a.pages = b->pages; a.maxp = b->maxp; a.n_pages = b->n_pages;
     a.n_ctx = b->n_ctx; a.pos = b->pos; a.nsplit = b->attn_split; a.hgroups = b->attn_groups; a.scale = b->scale;
     a.part = b->apart; a.cnt = b->acnt; a.out = b->att; a.ldo = b->qd; a.err = b->err;
     const dim3 grid(b->attn_split, b->nkv * b->attn_groups, b->B);
@@ -411,6 +426,7 @@ static void b_close_all(sb_batch * b) {
     b->ar.release();
     if (b->h_logits) cudaFreeHost(b->h_logits);
     if (b->h_io) cudaFreeHost(b->h_io);
+    if (b->h_pages) cudaFreeHost(b->h_pages);
     ssf_close(&b->f);
 }
 
@@ -421,11 +437,14 @@ static sb_batch * b_fail(sb_batch * b, char * why, int nwhy, const char * msg) {
     return nullptr;
 }
 
-extern "C" sb_batch * sb_batch_open(const char * path, int n_seq, int n_ctx, char * why, int nwhy) {
+// n_pages 0: fixed slots (slot s owns pages s * maxp ..); else a pool of that
+// many pages for sequences (sb_seq_new / sb_forward_seqs).
+static sb_batch * open_batch(const char * path, int n_seq, int n_ctx, int n_pages, char * why, int nwhy) {
     g_berr[0] = 0;
     if (why && nwhy) why[0] = 0;
     sb_batch * b = new sb_batch();
     if (n_seq < 1 || n_seq > kMaxBatchSeqs) return b_fail(b, why, nwhy, "n_seq out of range");
+    if (n_pages < 0) return b_fail(b, why, nwhy, "n_pages out of range");
     if (!ssf_open(&b->f, path, why, nwhy)) { delete b; return nullptr; }
     const ssf_hdr * h = b->f.hdr;
     if (const char * u = ssf_unsupported(b->f)) {
@@ -442,6 +461,10 @@ extern "C" sb_batch * sb_batch_open(const char * path, int n_seq, int n_ctx, cha
     b->scale = h->attn_scale != 0.0f ? h->attn_scale : 1.0f / sqrtf((float) b->hd);
     b->n_ctx = n_ctx > 0 ? n_ctx : 256;
     b->B = n_seq;
+    b->maxp = (b->n_ctx + 63) / 64;
+    b->paged = n_pages > 0;
+    b->n_pages = b->paged ? n_pages : n_seq * b->maxp;
+    for (int p = b->n_pages - 1; b->paged && p >= 0; p--) b->free_pages.push_back(p);
     b->N = tc_tile_n(n_seq);
     b->T_pad = tc_tokens_pad(n_seq);
     b->qkv_rows = round128(b->qd) + 2 * round128(b->kvd);
@@ -482,6 +505,16 @@ extern "C" sb_batch * sb_batch_open(const char * path, int n_seq, int n_ctx, cha
         return b_fail(b, why, nwhy, g_berr);
     std::vector<int> idle(b->B, -1);
     cudaMemcpy(b->pos, idle.data(), (size_t) b->B * 4, cudaMemcpyHostToDevice);
+    {
+        // fixed slots: slot s's positions 64c .. on page s * maxp + c; a paged
+        // handle starts with empty tables (every step uploads its own)
+        std::vector<int> tab((size_t) b->B * b->maxp, -1);
+        for (int sl = 0; !b->paged && sl < b->B; sl++)
+            for (int c = 0; c < b->maxp; c++) tab[(size_t) sl * b->maxp + c] = sl * b->maxp + c;
+        if (!bck(cudaMemcpy(b->pages, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice), "page tables") ||
+            (b->paged && !bck(cudaMallocHost(&b->h_pages, tab.size() * 4), "pinned page tables")))
+            return b_fail(b, why, nwhy, g_berr);
+    }
     const char * sm = getenv("SB_SYNC");
     b->sync_mode = sm && atoi(sm) != 0;
     b->launches = 0;
@@ -499,6 +532,19 @@ extern "C" sb_batch * sb_batch_open(const char * path, int n_seq, int n_ctx, cha
     ok = ok && bck(cudaDeviceSynchronize(), "open") && !b->failed;
     if (!ok) return b_fail(b, why, nwhy, g_berr);
     return b;
+}
+
+extern "C" sb_batch * sb_batch_open(const char * path, int n_seq, int n_ctx, char * why, int nwhy) {
+    return open_batch(path, n_seq, n_ctx, 0, why, nwhy);
+}
+
+extern "C" sb_batch * sb_batch_open_paged(const char * path, int n_slots, int n_ctx, int n_pages, char * why,
+                                          int nwhy) {
+    if (n_pages < 1) {
+        if (why && nwhy) snprintf(why, nwhy, "n_pages must be at least 1");
+        return nullptr;
+    }
+    return open_batch(path, n_slots, n_ctx, n_pages, why, nwhy);
 }
 
 extern "C" void sb_batch_close(sb_batch * b) {
@@ -544,6 +590,7 @@ static bool b_check_err(sb_batch * b, const char * what) {
 extern "C" const float * sb_forward_multi(sb_batch * b, const int * tokens, const int * pos) {
     g_berr[0] = 0;
     if (!b || !tokens || !pos) return nullptr;
+    if (b->paged) { snprintf(g_berr, sizeof g_berr, "a paged handle runs sequences: sb_forward_seqs"); return nullptr; }
     for (int s = 0; s < b->B; s++) {
         if (pos[s] >= b->n_ctx || (pos[s] >= 0 && (tokens[s] < 0 || tokens[s] >= b->V))) {
             snprintf(g_berr, sizeof g_berr, "slot %d: token %d at position %d out of range", s, tokens[s], pos[s]);
@@ -569,8 +616,8 @@ extern "C" int sb_batch_generate(sb_batch * b, const int * prompts, int np, int 
                                  float * ms) {
     g_berr[0] = 0;
     const int total = nwarm + ngen;
-    if (!b || !prompts || !ids || np < 1 || nwarm < 0 || ngen < 1 || np + total - 1 > b->n_ctx) {
-        snprintf(g_berr, sizeof g_berr, "generate: bad arguments");
+    if (!b || !prompts || !ids || np < 1 || nwarm < 0 || ngen < 1 || np + total - 1 > b->n_ctx || b->paged) {
+        snprintf(g_berr, sizeof g_berr, "generate: bad arguments%s", b && b->paged ? " (a paged handle)" : "");
         return 0;
     }
     for (size_t i = 0; i < (size_t) b->B * np; i++)
@@ -620,15 +667,136 @@ extern "C" const float * sb_batch_device_logits(const sb_batch * b) { return b ?
 
 // The cached key and value rows of one slot at one position of one layer
 // (host buffers of n_kv * hd fp16 each, head-major), for checks and export.
-extern "C" int sb_batch_kv(const sb_batch * b, int layer, int slot, int pos, uint16_t * k, uint16_t * v) {
-    if (!b || layer < 0 || layer >= b->n_layer || slot < 0 || slot >= b->B || pos < 0 || pos >= b->n_ctx || !k || !v)
-        return 0;
-    const size_t per_layer = (size_t) b->B * b->nkv * b->n_ctx * b->hd;
+static bool kv_rows_at(const sb_batch * b, int layer, int page, int pos, uint16_t * k, uint16_t * v) {
+    const size_t per_layer = (size_t) b->n_pages * b->nkv * 64 * b->hd;
     for (int h = 0; h < b->nkv; h++) {
-        const size_t at = (size_t) layer * per_layer + (((size_t) slot * b->nkv + h) * b->n_ctx + pos) * b->hd;
+        const size_t at = (size_t) layer * per_layer + (((size_t) page * b->nkv + h) * 64 + pos % 64) * b->hd;
         if (!bck(cudaMemcpy(k + (size_t) h * b->hd, b->kc + at, (size_t) b->hd * 2, cudaMemcpyDeviceToHost), "kv") ||
             !bck(cudaMemcpy(v + (size_t) h * b->hd, b->vc + at, (size_t) b->hd * 2, cudaMemcpyDeviceToHost), "kv"))
-            return 0;
+            return false;
+    }
+    return true;
+}
+
+extern "C" int sb_batch_kv(const sb_batch * b, int layer, int slot, int pos, uint16_t * k, uint16_t * v) {
+    if (!b || b->paged || layer < 0 || layer >= b->n_layer || slot < 0 || slot >= b->B || pos < 0 || pos >= b->n_ctx ||
+        !k || !v)
+        return 0;
+    return kv_rows_at(b, layer, slot * b->maxp + pos / 64, pos, k, v) ? 1 : 0;
+}
+
+// ------------------------------------------------------------------ sequences
+// A paged handle serves sequences rather than slots: each sequence holds the
+// pages its positions reached (taken from the pool when first needed), a
+// step runs any set of live sequences in its slots (in any order), and a
+// freed sequence's pages go back to the pool at once.
+
+extern "C" int sb_seq_new(sb_batch * b) {
+    g_berr[0] = 0;
+    if (!b || !b->paged) { snprintf(g_berr, sizeof g_berr, "sb_seq_new: not a paged handle"); return -1; }
+    int id;
+    if (!b->free_seqs.empty()) {
+        id = b->free_seqs.back();
+        b->free_seqs.pop_back();
+    } else {
+        id = (int) b->seq_pages.size();
+        b->seq_pages.emplace_back();
+        b->seq_live.push_back(0);
+    }
+    b->seq_pages[id].clear();
+    b->seq_live[id] = 1;
+    return id;
+}
+
+static bool seq_ok(const sb_batch * b, int id) {
+    return b && b->paged && id >= 0 && id < (int) b->seq_live.size() && b->seq_live[id];
+}
+
+// Keep the first n positions of a sequence: pages past them go back to the pool.
+extern "C" int sb_seq_truncate(sb_batch * b, int id, int n) {
+    g_berr[0] = 0;
+    if (!seq_ok(b, id) || n < 0) { snprintf(g_berr, sizeof g_berr, "sb_seq_truncate: no such sequence"); return 0; }
+    std::vector<int> & pg = b->seq_pages[id];
+    const size_t keep = (size_t) (n + 63) / 64;
+    while (pg.size() > keep) {
+        b->free_pages.push_back(pg.back());
+        pg.pop_back();
     }
     return 1;
+}
+
+extern "C" int sb_seq_free(sb_batch * b, int id) {
+    if (!sb_seq_truncate(b, id, 0)) return 0;
+    b->seq_live[id] = 0;
+    b->free_seqs.push_back(id);
+    return 1;
+}
+
+// out[0] pages in the pool, out[1] free pages, out[2] live sequences, out[3]
+// positions a sequence may reach (n_ctx).
+extern "C" void sb_batch_pages(const sb_batch * b, int * out) {
+    int live = 0;
+    for (char c : b->seq_live) live += c;
+    out[0] = b->n_pages;
+    out[1] = b->paged ? (int) b->free_pages.size() : 0;
+    out[2] = live;
+    out[3] = b->n_ctx;
+}
+
+extern "C" const float * sb_forward_seqs(sb_batch * b, const int * seqs, const int * tokens, const int * pos, int ns) {
+    g_berr[0] = 0;
+    if (!b || !b->paged || !seqs || !tokens || !pos || ns < 0 || ns > b->B) {
+        snprintf(g_berr, sizeof g_berr, "sb_forward_seqs: bad arguments (a paged handle, 0..%d sequences)", b ? b->B : 0);
+        return nullptr;
+    }
+    // every check and the pages the step needs before any state changes
+    size_t need = 0;
+    for (int s = 0; s < ns; s++) {
+        if (!seq_ok(b, seqs[s])) { snprintf(g_berr, sizeof g_berr, "slot %d: sequence %d is not live", s, seqs[s]); return nullptr; }
+        for (int r = 0; r < s; r++)
+            if (seqs[r] == seqs[s]) { snprintf(g_berr, sizeof g_berr, "sequence %d in two slots", seqs[s]); return nullptr; }
+        if (pos[s] < 0 || pos[s] >= b->n_ctx || tokens[s] < 0 || tokens[s] >= b->V) {
+            snprintf(g_berr, sizeof g_berr, "slot %d: token %d at position %d out of range", s, tokens[s], pos[s]);
+            return nullptr;
+        }
+        const size_t have = b->seq_pages[seqs[s]].size(), want = (size_t) pos[s] / 64 + 1;
+        if (want > have) need += want - have;
+    }
+    if (need > b->free_pages.size()) {
+        snprintf(g_berr, sizeof g_berr, "the step needs %zu more pages, %zu are free", need, b->free_pages.size());
+        return nullptr;
+    }
+    for (int s = 0; s < ns; s++) {
+        std::vector<int> & pg = b->seq_pages[seqs[s]];
+        while (pg.size() < (size_t) pos[s] / 64 + 1) {
+            pg.push_back(b->free_pages.back());
+            b->free_pages.pop_back();
+        }
+    }
+    for (int s = 0; s < b->B; s++) {
+        int * row = b->h_pages + (size_t) s * b->maxp;
+        for (int c = 0; c < b->maxp; c++) row[c] = -1;
+        if (s < ns) {
+            const std::vector<int> & pg = b->seq_pages[seqs[s]];
+            for (size_t c = 0; c < pg.size(); c++) row[c] = pg[c];
+        }
+        b->h_io[s] = s < ns ? tokens[s] : 0;
+        b->h_io[b->B + s] = s < ns ? pos[s] : -1;
+    }
+    if (!bck(cudaMemcpyAsync(b->pages, b->h_pages, (size_t) b->B * b->maxp * 4, cudaMemcpyHostToDevice, b->st), "page tables") ||
+        !bck(cudaMemcpyAsync(b->tok, b->h_io, (size_t) b->B * 4, cudaMemcpyHostToDevice, b->st), "tokens") ||
+        !bck(cudaMemcpyAsync(b->pos, b->h_io + b->B, (size_t) b->B * 4, cudaMemcpyHostToDevice, b->st), "positions") ||
+        !b_run(b) ||
+        !bck(cudaMemcpyAsync(b->h_logits, b->logits, (size_t) ns * b->V * 4, cudaMemcpyDeviceToHost, b->st), "logits") ||
+        !bck(cudaStreamSynchronize(b->st), "step") || !b_check_err(b, "step"))
+        return nullptr;
+    return b->h_logits;
+}
+
+// The cached key and value rows of a sequence at one position of one layer.
+extern "C" int sb_seq_kv(const sb_batch * b, int layer, int id, int pos, uint16_t * k, uint16_t * v) {
+    if (!seq_ok(b, id) || layer < 0 || layer >= b->n_layer || pos < 0 || pos >= b->n_ctx || !k || !v ||
+        (size_t) pos / 64 >= b->seq_pages[id].size())
+        return 0;
+    return kv_rows_at(b, layer, b->seq_pages[id][pos / 64], pos, k, v) ? 1 : 0;
 }

@@ -47,8 +47,10 @@ struct BAttnArgs {
     const float * qn, * kn;  // Q/K norm gains (hd long) or NULL
     float eps;
     const float * rcos, * rsin;   // [n_ctx][hd / 2]
-    uint16_t * kc, * vc;     // this layer's cache: [B][n_kv][n_ctx][hd] fp16
+    uint16_t * kc, * vc;     // this layer's cache pages: [n_pages][n_kv][kBChunk][hd] fp16
     int n_ctx;
+    const int * pages;       // [B][maxp]: the page of each slot's positions 64c .. 64c + 63
+    int maxp, n_pages;
     const int * pos;         // [B]; < 0: an idle slot
     int nsplit;              // CTAs sharing one (sequence, head group)'s positions
     int hgroups;             // head groups per KV head (ceil(rep / HG))
@@ -59,6 +61,21 @@ struct BAttnArgs {
     int ldo;
     int * err;
 };
+
+// Row of position t (of slot b, KV head kvh) in the paged cache, in units of
+// hd halves: a page holds 64 consecutive positions of every KV head, so a
+// chunk of 64 positions is one contiguous run of one head's rows. A slot whose
+// table holds no page there (the host never launches one) records an error
+// and reads page 0 instead, so every access stays inside the cache and the
+// CTAs of the step still meet.
+SB_DEV size_t kv_row(const BAttnArgs & g, int b, int kvh, int t) {
+    int page = g.pages[(size_t) b * g.maxp + t / 64];
+    if (page < 0 || page >= g.n_pages) {
+        atomicExch(g.err, 215);
+        page = 0;
+    }
+    return ((size_t) page * g.n_kv + kvh) * 64 + (t % 64);
+}
 
 // Ring stages of 64 positions' keys and values, and query heads per CTA.
 __host__ __device__ constexpr int battn_stages(int hd) { return hd <= 128 ? 3 : 2; }
@@ -132,7 +149,6 @@ __global__ void __launch_bounds__(kBThreads, 2) k_battn(const __grid_constant__ 
     float * kn = qs + HG * HD, * vn = kn + HD, * cs = vn + HD, * sn = cs + HD / 2;
     float * sc = sn + HD / 2;                                                // [kBChunk][HG]
     float * ro = reinterpret_cast<float *>(bsm);                             // [NW][HG][HD] at the end
-    const size_t row0 = ((size_t) b * g.n_kv + kvh) * g.n_ctx;
 
     if (tid == 0) {
         for (int s = 0; s < S; s++) mbar_init(&full[s], 1);
@@ -144,8 +160,9 @@ __global__ void __launch_bounds__(kBThreads, 2) k_battn(const __grid_constant__ 
         uint16_t * Ks = ring + (size_t) (j % S) * 2 * kBChunk * HD;
         const uint32_t bytes = (uint32_t) nt * HD * 2;
         mbar_expect_tx(&full[j % S], 2 * bytes);
-        bulk_g2s(Ks, g.kc + (row0 + t0) * HD, bytes, &full[j % S]);
-        bulk_g2s(Ks + kBChunk * HD, g.vc + (row0 + t0) * HD, bytes, &full[j % S]);
+        const size_t r0 = kv_row(g, b, kvh, t0);
+        bulk_g2s(Ks, g.kc + r0 * HD, bytes, &full[j % S]);
+        bulk_g2s(Ks + kBChunk * HD, g.vc + r0 * HD, bytes, &full[j % S]);
     };
     if (tid == 0)
         for (int j = 0; j < S && j < nmine; j++) issue(j);
@@ -178,13 +195,14 @@ __global__ void __launch_bounds__(kBThreads, 2) k_battn(const __grid_constant__ 
         ok = mbar_wait(&full[j % S], (uint32_t) (j / S) & 1u, g.err, 212) && ok;
         if (c == nchunk - 1 && ok) {
             const int r = pos - t0;
+            const size_t rp = h0 == 0 ? kv_row(g, b, kvh, pos) : 0;
             for (int i = tid; i < HD; i += kBThreads) {
                 const uint16_t kh = f2h(kn[i]), vh = f2h(vn[i]);
                 Ks[r * HD + i] = kh;
                 Vs[r * HD + i] = vh;
                 if (h0 == 0) {
-                    g.kc[(row0 + pos) * HD + i] = kh;
-                    g.vc[(row0 + pos) * HD + i] = vh;
+                    g.kc[rp * HD + i] = kh;
+                    g.vc[rp * HD + i] = vh;
                 }
             }
         }
@@ -373,6 +391,7 @@ SB_DEV void split_h2(float a, float b, uint32_t & hi, uint32_t & lo) {
 }
 
 constexpr int kMChunk = 64;      // positions per ring stage
+static_assert(kBChunk == 64 && kMChunk == 64, "a cache page holds one attention chunk of each KV head");
 constexpr int kMStages = 3;
 constexpr int kMThreads = 128;   // 4 warps, 16 positions of each chunk apiece
 constexpr int kMHeads = 16;      // query heads per CTA (the MMA's M)
@@ -438,15 +457,15 @@ __global__ void __launch_bounds__(kMThreads, 2) k_battn_mma(const __grid_constan
     float * qs = reinterpret_cast<float *>(bsm + (RING > COMB ? RING : COMB));   // [nq][HD]
     float * kn = qs + nq * HD, * vn = kn + HD, * cs = vn + HD, * sn = cs + HD / 2;
     float * comb = reinterpret_cast<float *>(bsm);                                 // [NW][16][HD] at the end
-    const size_t row0 = ((size_t) b * g.n_kv + kvh) * g.n_ctx;
 
     auto issue = [&](int j) {   // chunk c0 + j into stage j % kMStages
         const int t0 = (c0 + j) * kMChunk, nt = min(pos + 1, t0 + kMChunk) - t0;
         uint16_t * Ks = ring + (size_t) (j % kMStages) * STAGE;
+        const size_t r0 = kv_row(g, b, kvh, t0);
         for (int i = tid; i < 2 * kMChunk * PIECES; i += kMThreads) {
             const int kv = i / (kMChunk * PIECES), rem = i % (kMChunk * PIECES);
             const int r = rem / PIECES, pc = rem % PIECES;
-            const uint16_t * src = (kv ? g.vc : g.kc) + (row0 + t0 + min(r, nt - 1)) * HD + pc * 8;
+            const uint16_t * src = (kv ? g.vc : g.kc) + (r0 + min(r, nt - 1)) * HD + pc * 8;
             cp_async16(smem_u32(Ks + (size_t) kv * kMChunk * RS + r * RS + pc * 8), src, r < nt ? 16u : 0u);
         }
     };
@@ -495,13 +514,14 @@ __global__ void __launch_bounds__(kMThreads, 2) k_battn_mma(const __grid_constan
         if (c == nchunk - 1) {
             // the new key and value, fp16 round to nearest even, over the stale row
             const int r = pos - t0;
+            const size_t rp = h0 == 0 ? kv_row(g, b, kvh, pos) : 0;
             for (int i = tid; i < HD; i += kMThreads) {
                 const uint16_t kh = f2h(kn[i]), vh = f2h(vn[i]);
                 Ks[r * RS + i] = kh;
                 Vs[r * RS + i] = vh;
                 if (h0 == 0) {
-                    g.kc[(row0 + pos) * HD + i] = kh;
-                    g.vc[(row0 + pos) * HD + i] = vh;
+                    g.kc[rp * HD + i] = kh;
+                    g.vc[rp * HD + i] = vh;
                 }
             }
             __syncthreads();
