@@ -623,10 +623,12 @@ def gemm_tc_microbench(peak, reps=20):
 
 def moe_ep_microbench(peak, dist, world, rank, max_over_ranks, reps=20):
     """Configuration 2's MoE layer over `world` GPUs (expert parallelism): every
-    rank holds 128/world experts and passes all T tokens; timed per rank by
-    CUDA events with L2 flushed, the max over ranks reported. Bytes: the chosen
-    experts summed over the ranks (each rank reads only those it holds) plus
-    every rank's router."""
+    rank holds 128/world experts. Two exchanges: "all-reduce" (every rank
+    passes all T tokens, the per-choice outputs summed over the GPUs) and
+    "all-to-all" (each rank passes T/world tokens of its own, rows sent to the
+    GPUs holding their experts and back). Timed per rank by CUDA events with L2
+    flushed, the max over ranks reported. Bytes: the chosen experts summed over
+    the ranks (each rank reads only those it holds) plus every rank's router."""
     import sheep_b200
     from sheep_b200 import configs
     from sheep_b200 import dist as sdist
@@ -635,19 +637,27 @@ def moe_ep_microbench(peak, dist, world, rank, max_over_ranks, reps=20):
                             ep=(world, rank, nid))
     out = []
     try:
-        for T in (1, 16, 64, 256):
-            ms, na = m.time(fp16_rows(100 + T, T, m.n_embd), reps)
-            ms = max_over_ranks(ms)
-            import torch
-            t = torch.tensor([float(na)], dtype=torch.float64, device="cuda")
-            if dist is not None:
-                dist.all_reduce(t)
-            na_all = int(t.item())
-            nbytes = na_all * m.expert_bytes + world * m.router_bytes
-            gbs = nbytes / (ms / 1000.0) / 1e9
-            out.append({"tokens": T, "gpus": world, "us": round(ms * 1000.0, 2), "tok_s": round(T / (ms / 1000.0), 1),
-                        "experts_read": na_all, "bytes": nbytes, "gbs": round(gbs, 1),
-                        "frac_of_n_gpus": round(gbs / (peak * world), 4)})
+        import torch
+        for mode in ("all-reduce", "all-to-all"):
+            m.exchange(mode)
+            for T in (1, 16, 64, 256):
+                if mode == "all-to-all" and T < world:
+                    continue
+                # all-to-all: this rank's share of the T tokens (rows of the same seeded set)
+                x = fp16_rows(100 + T, T, m.n_embd)
+                if mode == "all-to-all":
+                    x = x[T * rank // world:T * (rank + 1) // world]
+                ms, na = m.time(x, reps)
+                ms = max_over_ranks(ms)
+                t = torch.tensor([float(na)], dtype=torch.float64, device="cuda")
+                if dist is not None:
+                    dist.all_reduce(t)
+                na_all = int(t.item())
+                nbytes = na_all * m.expert_bytes + world * m.router_bytes
+                gbs = nbytes / (ms / 1000.0) / 1e9
+                out.append({"exchange": mode, "tokens": T, "gpus": world, "us": round(ms * 1000.0, 2),
+                            "tok_s": round(T / (ms / 1000.0), 1), "experts_read": na_all, "bytes": nbytes,
+                            "gbs": round(gbs, 1), "frac_of_n_gpus": round(gbs / (peak * world), 4)})
     finally:
         m.close()
     return out

@@ -187,6 +187,26 @@ sb_moe * sb_moe_open(const char * path, int layer, int max_tokens, char * why, i
 sb_moe * sb_moe_open_ep(const char * path, int layer, int max_tokens, int world, int rank, const void * nccl_id,
                         char * why, int nwhy);
 int sb_nccl_unique_id(void * id128);
+// How an expert-parallel handle exchanges rows: 0 (the default) the all-reduce
+// above; 1 all-to-all (the dispatch / combine of a token-sharded deployment):
+// every process passes ITS OWN tokens (up to max_tokens, the same max_tokens on
+// every process), routes them, and the processes exchange their choices (an
+// all-gather), send each (token, choice) row to the GPU holding its expert
+// (grouped ncclSend / ncclRecv), run their experts over the rows they received,
+// send the results back and combine them in choice order: each process's y
+// equals the single-GPU layer's rows for its tokens bit for bit. The host plans
+// between the exchanges, so a call returns with the device synchronized.
+// Returns 0 for a single-GPU handle.
+int sb_moe_set_exchange(sb_moe * m, int mode);
+// The all-to-all exchange's plan for one rank (host only; no GPU needed): from
+// every rank's chosen experts (n_tok[world]; sel: the ranks' [n_tok[r]][k]
+// choices concatenated) the rows this rank sends to and receives from each
+// rank (send_cnt, recv_cnt [world]), the slot (token * k + choice) of each row
+// it sends, grouped by destination in slot order (send_slot), and the expert of
+// each row it receives, grouped by source (recv_expert). Any output may be
+// NULL. Returns the chunks of at most 8 rows its experts run, -1 on bad input.
+int sb_moe_a2a_plan(int world, int rank, int n_expert, int k, const int * n_tok, const int * sel, int * send_cnt,
+                    int * recv_cnt, int * send_slot, int * recv_expert);
 void sb_moe_close(sb_moe * m);
 // out[14]: n_embd, expert hidden size, experts, experts per token, flags,
 // max_tokens, expert width in bits, bytes of one expert as stored (low, high),

@@ -103,6 +103,8 @@ def lib():
         "sb_moe_route": (ip, [vp, ip, ip, ip, ctypes.c_uint, vp, vp, vp]),
         "sb_moe_last_error": (cp, []),
         "sb_moe_set_tensor_cores": (ip, [vp, ip]),
+        "sb_moe_set_exchange": (ip, [vp, ip]),
+        "sb_moe_a2a_plan": (ip, [ip, ip, ip, ip, vp, vp, vp, vp, vp, vp]),
         "sb_moe_open_ep": (vp, [cp, ip, ip, ip, ip, vp, cp, ip]),
         "sb_nccl_unique_id": (ip, [vp]),
         "sb_tc_imma": (ip, [vp, vp, vp, ip, ip, ip, vp, vp]),
@@ -408,6 +410,12 @@ class MoeLayer:
             raise RuntimeError(f"sb_moe_forward_host: {lib().sb_moe_last_error().decode()}")
         return y, sel, w, na.value
 
+    def exchange(self, mode):
+        """An expert-parallel handle's exchange: "all-reduce" (every rank passes
+        all tokens) or "all-to-all" (every rank passes its own tokens)."""
+        if not lib().sb_moe_set_exchange(self.h, {"all-reduce": 0, "all-to-all": 1}[mode]):
+            raise RuntimeError(f"sb_moe_set_exchange: {lib().sb_moe_last_error().decode()}")
+
     def tensor_cores(self, on):
         """Calls of 16+ rows on the tensor cores (True), on the integer kernels
         (False), or "auto" (the default: the tensor cores from 8 chosen rows
@@ -561,6 +569,23 @@ class PagedBatch:
 
     def __exit__(self, *a):
         self.close()
+
+
+def moe_a2a_plan(world, rank, n_expert, sels):
+    """The all-to-all exchange's plan of `rank` (sb_moe_a2a_plan, host only):
+    sels[r] is rank r's [n_tok, k] chosen experts. Returns (send_cnt,
+    recv_cnt, send_slot, recv_expert, chunks)."""
+    k = sels[0].shape[1]
+    n_tok = np.array([len(s_) for s_ in sels], np.int32)
+    sel = np.ascontiguousarray(np.concatenate([np.asarray(s_, np.int32).reshape(-1) for s_ in sels]), np.int32)
+    send_cnt, recv_cnt = np.zeros(world, np.int32), np.zeros(world, np.int32)
+    send_slot = np.zeros(max(1, n_tok[rank] * k), np.int32)
+    recv_exp = np.zeros(max(1, len(sel)), np.int32)
+    nch = lib().sb_moe_a2a_plan(world, rank, n_expert, k, _p(n_tok), _p(sel), _p(send_cnt), _p(recv_cnt),
+                                _p(send_slot), _p(recv_exp))
+    if nch < 0:
+        raise RuntimeError("sb_moe_a2a_plan: bad input")
+    return send_cnt, recv_cnt, send_slot[:int(send_cnt.sum())], recv_exp[:int(recv_cnt.sum())], nch
 
 
 def moe_route_dev(logits_ptr, n_tok, n_expert, k, flags, sel_ptr, w_ptr, stream=0):

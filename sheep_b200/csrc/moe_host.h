@@ -225,6 +225,54 @@ inline cudaError_t moe_gemv(int mode, int nt, const MoeGArgs & g, int grid, cuda
     return r;
 }
 
+// The router over T rows (RMS-normalized by norm_w first when given): logits,
+// each row's chosen experts and weights, and the dispatch of the slots whose
+// expert lies in [e_lo, e_hi) in chunks of at most nt rows (none when the range
+// is empty).
+inline cudaError_t moe_router_launch(const MoeLayer & m, const MoeScratch & s, const float * x, int T,
+                                     const float * norm_w, float eps, int nt, int e_lo, int e_hi, cudaStream_t st,
+                                     bool pdl, int * err, unsigned long long * trace, int launch_id,
+                                     const ExpfEntry * xtab, float xnear) {
+    MoeRouterArgs r;
+    memset(&r, 0, sizeof r);
+    r.x = x; r.norm_w = norm_w; r.eps = eps; r.xn = norm_w ? s.xn : nullptr; r.wr = m.router;
+    r.T = T; r.E = m.E; r.ne = m.ne; r.k = m.k; r.nt = nt; r.flags = m.flags; r.r = s.r;
+    r.e_lo = e_lo; r.e_hi = e_hi;
+    r.xtab = xtab; r.xnear = xnear;
+    r.err = err; r.trace = trace; r.launch_id = launch_id;
+    static bool attr = false;
+    if (!attr) {
+        cudaFuncSetAttribute(k_moe_router, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 8192 * 4);
+        attr = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(m.ne);
+    cfg.blockDim = dim3(kRouterThreads);
+    cfg.dynamicSmemBytes = (size_t) m.E * 4 * (norm_w ? 2 : 1);
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_moe_router, r);
+}
+
+// y[t] (+)= the choice-order combine of the per-choice outputs s.yk ([T*k][E]).
+inline cudaError_t moe_comb_launch(const MoeLayer & m, const MoeScratch & s, int T, float * y, int resid,
+                                   cudaStream_t st, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((m.E + 255) / 256, T);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, k_moe_comb, (const float *) s.yk, (const float *) s.r.w, T, m.k, m.E, y, resid);
+}
+
 // Expert parallelism: the per-choice down outputs ([T*k][E]) are summed over
 // the GPUs between the down GEMV and the combine. Each row is written by the one
 // GPU holding its expert and is zero on the others, so the sum is exact and the
@@ -252,31 +300,8 @@ inline void moe_enqueue(const MoeLayer & m, const MoeScratch & s, const float * 
     // one token per chunk at T = 1: a token never picks an expert twice
     const int nt = use_tc ? kMoeTcChunk : T == 1 ? 1 : 8;
     if (ex) post(cudaMemsetAsync(s.yk, 0, (size_t) T * m.k * m.E * 4, st), "moe.zero");
-    {
-        MoeRouterArgs r;
-        memset(&r, 0, sizeof r);
-        r.x = x; r.norm_w = norm_w; r.eps = eps; r.xn = norm_w ? s.xn : nullptr; r.wr = m.router;
-        r.T = T; r.E = m.E; r.ne = m.ne; r.k = m.k; r.nt = nt; r.flags = m.flags; r.r = s.r;
-        r.e_lo = m.e_lo; r.e_hi = m.e_hi;
-        r.xtab = xtab; r.xnear = xnear;
-        r.err = err; r.trace = trace; r.launch_id = launch_id;
-        static bool attr = false;
-        if (!attr) {
-            cudaFuncSetAttribute(k_moe_router, cudaFuncAttributeMaxDynamicSharedMemorySize, 2 * 8192 * 4);
-            attr = true;
-        }
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3(m.ne);
-        cfg.blockDim = dim3(kRouterThreads);
-        cfg.dynamicSmemBytes = (size_t) m.E * 4 * (norm_w ? 2 : 1);
-        cfg.stream = st;
-        cudaLaunchAttribute at[1];
-        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        at[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = at;
-        cfg.numAttrs = pdl ? 1 : 0;
-        post(cudaLaunchKernelEx(&cfg, k_moe_router, r), "moe.router");
-    }
+    post(moe_router_launch(m, s, x, T, norm_w, eps, nt, m.e_lo, m.e_hi, st, pdl, err, trace, launch_id, xtab, xnear),
+         "moe.router");
     MoeGArgs g;
     memset(&g, 0, sizeof g);
     g.slots = s.r.slots; g.ch_e = s.r.ch_e; g.ch_s0 = s.r.ch_s0; g.ch_n = s.r.ch_n; g.meta = s.r.meta;
@@ -304,19 +329,7 @@ inline void moe_enqueue(const MoeLayer & m, const MoeScratch & s, const float * 
         }
     }
     if (ex) post(ex->sum(ex->ctx, s.yk, (size_t) T * m.k * m.E, st), "moe.exchange");
-    {
-        cudaLaunchConfig_t cfg = {};
-        cfg.gridDim = dim3((m.E + 255) / 256, T);
-        cfg.blockDim = dim3(256);
-        cfg.stream = st;
-        cudaLaunchAttribute at[1];
-        at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-        at[0].val.programmaticStreamSerializationAllowed = 1;
-        cfg.attrs = at;
-        cfg.numAttrs = pdl ? 1 : 0;
-        post(cudaLaunchKernelEx(&cfg, k_moe_comb, (const float *) s.yk, (const float *) s.r.w, T, m.k, m.E, y, resid),
-             "moe.combine");
-    }
+    post(moe_comb_launch(m, s, T, y, resid, st, pdl), "moe.combine");
 }
 
 }  // namespace sb
