@@ -242,6 +242,8 @@ def main():
         return
 
     import torch
+    # NCCL's start-up banner would land on stdout beside the one JSON line
+    os.environ.setdefault("NCCL_DEBUG", "WARN")
     dist = sdist.init("nccl", timeout_s=300)
     if dist is None:
         torch.cuda.set_device(0)
