@@ -25,8 +25,10 @@ with a 512 MB buffer rewritten before it, so the weights come from HBM; and
 configuration 3's batch-1 decode (Llama-3-8B shape, 4.2 GB per token) and its
 batched serving at 64 slots (2048-id prompts, 256 generated ids each).
 extras with N > 1 GPUs: configuration 3 split the same way over the N GPUs,
-and configuration 2's MoE layer spread over them (expert parallelism,
-sb_moe_open_ep), the max over ranks at 1/16/64/256 tokens.
+configuration 2's MoE layer spread over them (expert parallelism,
+sb_moe_open_ep, with the all-reduce and the all-to-all exchanges), the max
+over ranks at 1/16/64/256 tokens, and configuration 4's batch-1 decode with
+each layer's experts spread over the GPUs.
 """
 import argparse
 import ctypes
@@ -330,8 +332,9 @@ def main():
         peak0, _ = peaks()
         d3 = decode_cfg3(peak0, tp=(world, rank, dist), max_over_ranks=max_over_ranks)
         ep = moe_ep_microbench(peak0, dist, world, rank, max_over_ranks)
+        d4 = decode_cfg4(peak0, tp=(world, rank, dist), max_over_ranks=max_over_ranks)
         if rank == 0:
-            extras = {"decode_cfg3_tp": d3, "moe_cfg2_ep": ep}
+            extras = {"decode_cfg3_tp": d3, "moe_cfg2_ep": ep, "decode_cfg4_tp": d4}
     if rank == 0 and world == 1:
         peak0, _ = peaks()
         from sheep_b200 import configs as cf
@@ -481,34 +484,47 @@ def decode_cfg3(peak, ngen=64, tp=None, max_over_ranks=None):
         eng.close()
 
 
-def decode_cfg4(peak, prompt=1024, ngen=64, nwarm=8):
+def decode_cfg4(peak, prompt=1024, ngen=64, nwarm=8, tp=None, max_over_ranks=None):
     """Configuration 4 (Qwen3-235B-A22B shape, 94 MoE layers, ~136 GB of Q4)
-    at batch 1 on one GPU: a `prompt`-id random prompt stepped, then the
-    device-resident greedy loop. The file holds everything but the experts
-    (writer mode direct=2); the engine draws the experts' tiles on the device
+    at batch 1: a `prompt`-id random prompt stepped, then the device-resident
+    greedy loop. The file holds everything but the experts (writer mode
+    direct=2); the engine draws the experts' tiles on the device
     (sb_draw_experts), so a token reads the bytes a full file would give: the
     attention projections, the router, the 8 chosen experts of every layer and
-    the head."""
+    the head. With tp=(world, rank, dist) (every rank calls this) one stream
+    over the GPUs: attention replicated, each layer's experts spread over them
+    (their per-choice outputs summed by NCCL), the head split by rows."""
     import sheep_b200
     from sheep_b200 import configs
-    path = model_path(configs.CONFIGS["qwen3-235b-a22b-q4"], 0, None)
+    rank, dist = (tp[1], tp[2]) if tp else (0, None)
+    path = model_path(configs.CONFIGS["qwen3-235b-a22b-q4"], rank, dist)
     sheep_b200.draw_experts(235)
     t0 = time.time()
     try:
-        eng = sheep_b200.Engine(path, n_ctx=prompt + nwarm + ngen + 8)
+        eng = sheep_b200.Engine(path, n_ctx=prompt + nwarm + ngen + 8, tp=tp)
     finally:
         sheep_b200.draw_experts(0)
     open_s = time.time() - t0
     try:
         p = np.random.default_rng(1234).integers(0, eng.n_vocab, prompt).astype(np.int32)
         ids, ms = eng.generate(p, ngen + 1, timed=True, warmup=nwarm)
+        if max_over_ranks:
+            ms = max_over_ranks(ms)
         tps = ngen / (ms / 1000.0)
         nb = float(eng.bytes_per_token)
+        world = tp[0] if tp else 1
+        if dist is not None:
+            import torch
+            t = torch.tensor([nb], dtype=torch.float64, device="cuda")
+            dist.all_reduce(t)
+            nb = float(t.item())
         gbs = nb * tps / 1e9
-        return {"tok_s": round(tps, 1), "ms_per_token": round(ms / ngen, 4), "prompt": prompt, "tokens": ngen,
-                "bytes_per_token": int(nb), "gbs": round(gbs, 1), "frac": round(gbs / peak, 4),
-                "experts": "drawn on the device (direct=2 file)", "open_s": round(open_s, 1),
-                "launches_per_token": eng.launches_per_token, "greedy_ids_head": [int(i) for i in ids[:8]]}
+        return {"tok_s": round(tps, 1), "ms_per_token": round(ms / ngen, 4), "gpus": world, "prompt": prompt,
+                "tokens": ngen, "bytes_per_token_all_gpus": int(nb), "gbs": round(gbs, 1),
+                "frac_of_n_gpus": round(gbs / (peak * world), 4),
+                "experts": "drawn on the device (direct=2 file)" + (f"; spread over {world} GPUs" if world > 1 else ""),
+                "open_s": round(open_s, 1), "launches_per_token": eng.launches_per_token,
+                "greedy_ids_head": [int(i) for i in ids[:8]]}
     finally:
         eng.close()
 

@@ -8,6 +8,7 @@
 // graph replays with no host round trip.
 #include "decode.cuh"
 #include "moe_host.h"
+#include "nccl_rt.h"
 #include "tc_batch.h"
 #include "tgemv.cuh"
 #include "sheep_b200.h"
@@ -109,6 +110,8 @@ struct sb_engine {
     const ExpfEntry * xtab = nullptr;  // the host libm's expf corrections (expf_libm.h)
     float xnear = 0.0f;                // ... looked up within this midpoint distance
     MoeScratch ms;                    // routing scratch shared by every MoE layer (one token)
+    ncclComm_t comm = nullptr;        // tensor parallelism over MoE layers: experts spread over the
+    MoeExchange moe_ex{};             // ranks, per-choice outputs summed by an NCCL all-reduce
     int * err = nullptr;              // bounded waits that gave up
     unsigned long long * trace = nullptr;   // trace build: [launch][cta][8] timestamps
     int n_launch_trace = 0;
@@ -243,8 +246,12 @@ static void tp_counts(sb_engine * e) {
     unsigned c = 0;
     auto grid = [&](const TT & tt) { return (unsigned) (tt.ntiles < e->nsm ? tt.ntiles : e->nsm); };
     for (const LayerD & y : e->L) {
-        c += grid(y.gateup); t.cum.push_back(c);
-        c += grid(y.down); t.cum.push_back(c);
+        // an MoE layer's output is the same on every rank (routing everywhere,
+        // the per-choice rows summed by NCCL): its events raise nothing
+        if (!y.moe) c += grid(y.gateup);
+        t.cum.push_back(c);
+        if (!y.moe) c += grid(y.down);
+        t.cum.push_back(c);
     }
     c += grid(e->head); t.cum.push_back(c);
 }
@@ -305,8 +312,8 @@ static void enqueue_token(sb_engine * e) {
             // router on rmsnorm(x), experts, combine added to x (sml/sml-run.c:3503-3507)
             snprintf(e->cur, sizeof e->cur, "L%d.moe", l);
             moe_enqueue(y.ml, e->ms, e->x, 1, y.fn, e->eps, e->x, 1, e->nsm, e->st, true, e->err, e->trace,
-                        e->launches, [&](cudaError_t r, const char *) { after_launch(e, r); }, nullptr, e->xtab,
-                        e->xnear);
+                        e->launches, [&](cudaError_t r, const char *) { after_launch(e, r); },
+                        e->tp.n > 1 ? &e->moe_ex : nullptr, e->xtab, e->xnear);
             continue;
         }
         snprintf(e->cur, sizeof e->cur, "L%d.ffn", l);
@@ -361,6 +368,7 @@ static void close_all(sb_engine * e) {
     if (e->tp.reg) cudaFree(e->tp.reg);
     e->pf.ar.release();
     if (e->pf.h_tok) cudaFreeHost(e->pf.h_tok);
+    if (e->comm) nccl_api()->destroy(e->comm);
     e->ar.release();
     if (e->h_logits) cudaFreeHost(e->h_logits);
     if (e->h_io) cudaFreeHost(e->h_io);
@@ -429,9 +437,18 @@ static bool build(sb_engine * e, char * why, int nwhy) {
                      : r < e->qd + 2 * e->kvd ? RowSrc{v, r - e->qd - e->kvd} : RowSrc{nullptr, 0}; },
                        y.qkv, why, nwhy))
             return false;
-        if (y.moe && tp > 1) { snprintf(why, nwhy, "layer %d: tensor parallelism over MoE layers is not built", l); return false; }
         if (y.moe) {
-            if (!moe_upload(e->ar, f, l, y.ml, why, nwhy)) return false;
+            // over tp GPUs (expert parallelism inside the tensor-parallel engine):
+            // this rank's experts [ne r / tp, ne (r + 1) / tp)
+            int e_lo = 0, e_hi = 0;
+            if (tp > 1) {
+                const ssf_rec * rt = R("blk.%d.ffn_gate_inp.weight");
+                const int ne = (int) ((uint64_t) rt->rows * rt->cols / e->E);
+                if (ne < tp) { snprintf(why, nwhy, "layer %d: %d experts cannot spread over %d GPUs", l, ne, tp); return false; }
+                e_lo = (int) ((long) ne * rk / tp);
+                e_hi = (int) ((long) ne * (rk + 1) / tp);
+            }
+            if (!moe_upload(e->ar, f, l, y.ml, why, nwhy, e_lo, e_hi)) return false;
             if (moe0 && (y.ml.E != moe0->E || y.ml.F != moe0->F || y.ml.ne != moe0->ne || y.ml.k != moe0->k)) {
                 snprintf(why, nwhy, "layer %d: MoE layers differ in shape", l);
                 return false;
@@ -475,7 +492,7 @@ static bool build(sb_engine * e, char * why, int nwhy) {
         }
         // per token: the router and the k chosen experts (as tiles)
         e->bytes_tok += tt_bytes(y.qkv) + tt_bytes(y.o) +
-                        (y.moe ? y.ml.router_bytes + (uint64_t) y.ml.k * (tt_bytes(y.ml.gu) + tt_bytes(y.ml.dn))
+                        (y.moe ? y.ml.router_bytes + (uint64_t) y.ml.k * (tt_bytes(y.ml.gu) + tt_bytes(y.ml.dn)) / tp
                                : tt_bytes(y.gateup) + tt_bytes(y.down));
         y.an = up_f32(e, R("blk.%d.attn_norm.weight"));
         y.fn = up_f32(e, R("blk.%d.ffn_norm.weight"));
@@ -740,8 +757,42 @@ int sb_tp_handle(const sb_engine * e, void * out) {
     return 1;
 }
 
+static cudaError_t engine_moe_sum(void * ctx, float * buf, size_t n, cudaStream_t st) {
+    sb_engine * e = (sb_engine *) ctx;
+    const ncclResult_t r = nccl_api()->all_reduce(buf, buf, n, ncclFloat, ncclSum, e->comm, st);
+    if (r != ncclSuccess) {
+        snprintf(g_err, sizeof g_err, "ncclAllReduce: %s", nccl_api()->error(r));
+        return cudaErrorUnknown;
+    }
+    return cudaSuccess;
+}
+
+int sb_tp_nccl(sb_engine * e, const void * nccl_id, char * why, int nwhy) {
+    if (!e || e->tp.n <= 1 || !nccl_id || e->g_tok || e->comm) {
+        snprintf(why, nwhy, "not a tensor-parallel engine awaiting its peers");
+        return 0;
+    }
+    if (!nccl_api()) { snprintf(why, nwhy, "NCCL (libnccl.so.2) could not be loaded"); return 0; }
+    ncclUniqueId uid;
+    memcpy(&uid, nccl_id, sizeof uid);
+    const ncclResult_t r = nccl_api()->init_rank(&e->comm, e->tp.n, uid, e->tp.rank);
+    if (r != ncclSuccess) {
+        snprintf(why, nwhy, "ncclCommInitRank: %s", nccl_api()->error(r));
+        e->comm = nullptr;
+        return 0;
+    }
+    e->moe_ex.sum = engine_moe_sum;
+    e->moe_ex.ctx = e;
+    return 1;
+}
+
 int sb_tp_connect(sb_engine * e, const void * handles, char * why, int nwhy) {
     if (!e || e->tp.n <= 1 || !handles || e->g_tok) { snprintf(why, nwhy, "not a tensor-parallel engine awaiting its peers"); return 0; }
+    for (const LayerD & y : e->L)
+        if (y.moe && !e->comm) {
+            snprintf(why, nwhy, "MoE layers over several GPUs: every rank calls sb_tp_nccl before sb_tp_connect");
+            return 0;
+        }
     TpState & t = e->tp;
     for (int p = 0; p < t.n; p++) {
         if (p == t.rank) continue;

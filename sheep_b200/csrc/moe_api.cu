@@ -8,6 +8,7 @@
 // batches tokens by layer and for measurement at 1..256 tokens a step.
 #include "moe_a2a.h"
 #include "moe_host.h"
+#include "nccl_rt.h"
 #include "sheep_b200.h"
 #include "ssf.h"
 
@@ -23,23 +24,7 @@ static thread_local char g_err[512];
 
 extern "C" const char * sb_moe_last_error(void) { return g_err; }
 
-// NCCL, loaded when an expert-parallel layer is opened (single-GPU users need
-// no NCCL; in a process that already loaded one, dlopen returns that one).
-struct NcclApi {
-    ncclResult_t (*get_id)(ncclUniqueId *);
-    ncclResult_t (*init_rank)(ncclComm_t *, int, ncclUniqueId, int);
-    ncclResult_t (*all_reduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
-    ncclResult_t (*destroy)(ncclComm_t);
-    const char * (*error)(ncclResult_t);
-    // the all-to-all exchange
-    ncclResult_t (*all_gather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
-    ncclResult_t (*send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
-    ncclResult_t (*recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
-    ncclResult_t (*group_start)();
-    ncclResult_t (*group_end)();
-};
-
-static const NcclApi * nccl_api() {
+const NcclApi * sb::nccl_api() {
     static NcclApi api;
     static int state = 0;   // 0 untried, 1 loaded, -1 unavailable
     if (state) return state > 0 ? &api : nullptr;
@@ -65,6 +50,7 @@ static const NcclApi * nccl_api() {
     state = 1;
     return &api;
 }
+
 
 struct sb_moe {
     ssf_file f{};

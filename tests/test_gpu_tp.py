@@ -1,6 +1,7 @@
 """Tensor-parallel decode (sb_open_tp) on two GPUs, one process per GPU: q|k|v,
 attention and o replicated, gate/up, down and the head split by rows, the
-rows exchanged over NVLink by the GEMVs themselves. Every rank's logits must
+rows exchanged over NVLink by the GEMVs themselves; MoE layers' experts spread
+over the GPUs, their per-choice outputs summed by an NCCL all-reduce. Every rank's logits must
 equal the single-GPU engine's bit for bit at every teacher-forced position,
 and the device-resident greedy loop must pick the same ids. Skipped with
 fewer than two GPUs."""
@@ -62,10 +63,16 @@ def _worker(rank, world, port, path, toks, prompt, out):
 
 
 @pytest.mark.skipif(_gpus() < 2, reason="needs two GPUs")
-@pytest.mark.parametrize("cfg", ["tiny-q4", "small-q4-tied"])
-def test_tensor_parallel_two_gpus_bitexact(cfg):
+@pytest.mark.parametrize("cfg,over", [
+    ("tiny-q4", {}),
+    ("small-q4-tied", {}),
+    # a Qwen3-MoE-shaped decoder (configuration 4's features): Q/K norm, 16
+    # experts top-4 spread over the GPUs, their outputs summed by NCCL
+    ("tiny-q4", dict(n_expert=16, n_expert_used=4, moe_flags=1, expert_ff=256, qk_norm=1, qkv_bias=0, seed=77)),
+])
+def test_tensor_parallel_two_gpus_bitexact(cfg, over):
     import multiprocessing as mp
-    path = helpers.model_path(sheep_b200.spec_for(cfg))
+    path = helpers.model_path(sheep_b200.spec_for(cfg, **over))
     rng = np.random.default_rng(31)
     toks = rng.integers(0, 1024, 20)
     prompt = rng.integers(0, 1024, 6).astype(np.int32)
