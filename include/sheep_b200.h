@@ -25,7 +25,11 @@ void        sb_close(sb_engine * e);
 // this is the row-split GEMV with an exchange north of it): attention, q|k|v
 // and o replicated on every rank; gate/up, down and the head split by rows;
 // each GEMV stores its rows into every rank's copy of the vector over NVLink
-// and raises a flag the consuming kernel waits on. Results equal one GPU's bit
+// and raises a flag the consuming kernel waits on. A mixture-of-experts layer's
+// experts are spread over the ranks ([ne r / tp, ne (r + 1) / tp) on rank r):
+// the router runs on every rank, each runs the chosen experts it holds and its
+// expert down GEMV stores every row into all ranks' per-choice buffer the same
+// way; the combine, in choice order, waits for them. Results equal one GPU's bit
 // for bit. Open on every rank (the current device is the rank's GPU), pass
 // each rank's handle to every rank (rank order), then connect; every rank must
 // then make the same calls in the same order (steps, prefill, generation).
@@ -33,14 +37,6 @@ void        sb_close(sb_engine * e);
 sb_engine * sb_open_tp(const char * path, int n_ctx, int tp, int rank, char * why, int nwhy);
 int         sb_tp_handle(const sb_engine * e, void * out);   // SB_TP_HANDLE_BYTES of this rank's exchange region
 int         sb_tp_connect(sb_engine * e, const void * handles, char * why, int nwhy);
-// A model with mixture-of-experts layers spreads each layer's experts over the
-// ranks (rank r holds [ne r / tp, ne (r + 1) / tp)); the router runs on every
-// rank, each runs the chosen experts it holds and the per-choice outputs are
-// summed by an NCCL all-reduce inside the token's graph (exact: each row is one
-// rank's, zeros elsewhere), then combined in choice order everywhere. Such an
-// engine needs the ranks' communicator before sb_tp_connect: every rank passes
-// the same 128-byte id (sb_nccl_unique_id on one rank, shared by the host).
-int         sb_tp_nccl(sb_engine * e, const void * nccl_id, char * why, int nwhy);
 // out[0..12]: n_layer, n_embd, n_head, n_head_kv, head_dim, n_ff, n_vocab,
 // n_ctx, n_expert, n_expert_used, weight bytes per token (low, high 32 bits),
 // 0 (reserved)

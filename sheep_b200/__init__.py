@@ -58,7 +58,6 @@ def lib():
         "sb_kv_rows": (ip, [vp, ip, ip, vp, vp]),
         "sb_prompt_splits": (ip, [vp, vp]),
         "sb_tp_connect": (ip, [vp, vp, cp, ip]),
-        "sb_tp_nccl": (ip, [vp, vp, cp, ip]),
         "sb_close": (None, [vp]),
         "sb_info": (None, [vp, vp]),
         "sb_bytes_per_token": (ctypes.c_uint64, [vp]),
@@ -181,15 +180,6 @@ class Engine:
             raise RuntimeError(f"sb_open: {why.value.decode()}")
         if tp is not None and tp[0] > 1:
             world, rank, dist = tp
-            info = (ctypes.c_int * 16)()
-            lib().sb_info(self.h, info)
-            if info[8] > 0:
-                # MoE layers: the experts spread over the ranks, summed by the library's NCCL
-                ids = [None] * world
-                dist.all_gather_object(ids, nccl_unique_id() if rank == 0 else None)
-                idbuf = ctypes.create_string_buffer(bytes(ids[0]), 128)
-                if not lib().sb_tp_nccl(self.h, idbuf, why, 512):
-                    raise RuntimeError(f"sb_tp_nccl: {why.value.decode()}")
             hb = ctypes.create_string_buffer(64)
             if not lib().sb_tp_handle(self.h, hb):
                 raise RuntimeError(f"sb_tp_handle: {lib().sb_last_error().decode()}")

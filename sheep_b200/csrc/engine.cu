@@ -8,7 +8,6 @@
 // graph replays with no host round trip.
 #include "decode.cuh"
 #include "moe_host.h"
-#include "nccl_rt.h"
 #include "tc_batch.h"
 #include "tgemv.cuh"
 #include "sheep_b200.h"
@@ -63,6 +62,7 @@ struct TpState {
     size_t reg_bytes = 0;
     void * peer[kMaxTp] = {};         // every rank's region as mapped here (this rank's = reg)
     size_t off_x = 0, off_hp = 0, off_lg = 0;   // vectors in the region (flags at 0)
+    size_t off_yk = 0;                          // MoE layers: the per-choice rows [2][k][E] (by layer parity)
     unsigned * tok_seq = nullptr;
     std::vector<unsigned> cum;        // arrivals per token up to each event (tp_counts)
 };
@@ -110,8 +110,6 @@ struct sb_engine {
     const ExpfEntry * xtab = nullptr;  // the host libm's expf corrections (expf_libm.h)
     float xnear = 0.0f;                // ... looked up within this midpoint distance
     MoeScratch ms;                    // routing scratch shared by every MoE layer (one token)
-    ncclComm_t comm = nullptr;        // tensor parallelism over MoE layers: experts spread over the
-    MoeExchange moe_ex{};             // ranks, per-choice outputs summed by an NCCL all-reduce
     int * err = nullptr;              // bounded waits that gave up
     unsigned long long * trace = nullptr;   // trace build: [launch][cta][8] timestamps
     int n_launch_trace = 0;
@@ -218,10 +216,11 @@ static void set_next(TGArgs & g, const TT * nt, int nsm) {
 // this rank's region (its rows go to the same offset in every peer's); raise:
 // its CTAs arrive at the peers; wait_ev: the event (index into tp.cum) whose
 // arrivals it waits for, -1 none.
-static void set_tp(sb_engine * e, TGArgs & g, bool raise, int wait_ev, float * out) {
+static TpX make_tpx(sb_engine * e, bool raise, int wait_ev, float * out) {
     TpState & t = e->tp;
-    if (t.n <= 1) return;
-    TpX & x = g.tp;
+    TpX x;
+    memset(&x, 0, sizeof x);
+    if (t.n <= 1) return x;
     x.n = t.n; x.rank = t.rank;
     for (int p = 0; p < t.n; p++) {
         x.peer_out[p] = nullptr;
@@ -236,6 +235,10 @@ static void set_tp(sb_engine * e, TGArgs & g, bool raise, int wait_ev, float * o
     x.wait_count = wait_ev >= 0 ? t.cum[wait_ev] : 0u;
     x.raise = raise ? 1 : 0;
     x.err = e->err;
+    return x;
+}
+static void set_tp(sb_engine * e, TGArgs & g, bool raise, int wait_ev, float * out) {
+    if (e->tp.n > 1) g.tp = make_tpx(e, raise, wait_ev, out);
 }
 
 // Arrivals per token up to each event (hidden(l) = 2l, x(l) = 2l+1, logits =
@@ -246,11 +249,10 @@ static void tp_counts(sb_engine * e) {
     unsigned c = 0;
     auto grid = [&](const TT & tt) { return (unsigned) (tt.ntiles < e->nsm ? tt.ntiles : e->nsm); };
     for (const LayerD & y : e->L) {
-        // an MoE layer's output is the same on every rank (routing everywhere,
-        // the per-choice rows summed by NCCL): its events raise nothing
+        // an MoE layer: its expert down GEMV (grid nsm) raises x(l); its hidden event is empty
         if (!y.moe) c += grid(y.gateup);
         t.cum.push_back(c);
-        if (!y.moe) c += grid(y.down);
+        c += y.moe ? (unsigned) e->nsm : grid(y.down);
         t.cum.push_back(c);
     }
     c += grid(e->head); t.cum.push_back(c);
@@ -311,9 +313,18 @@ static void enqueue_token(sb_engine * e) {
         if (y.moe) {
             // router on rmsnorm(x), experts, combine added to x (sml/sml-run.c:3503-3507)
             snprintf(e->cur, sizeof e->cur, "L%d.moe", l);
-            moe_enqueue(y.ml, e->ms, e->x, 1, y.fn, e->eps, e->x, 1, e->nsm, e->st, true, e->err, e->trace,
-                        e->launches, [&](cudaError_t r, const char *) { after_launch(e, r); },
-                        e->tp.n > 1 ? &e->moe_ex : nullptr, e->xtab, e->xnear);
+            // over GPUs: each row of a chosen expert is stored by the GPU holding it
+            // into every GPU's per-choice buffer; the combine waits for them (event x(l))
+            MoePeerX px;
+            MoeScratch ms = e->ms;
+            if (e->tp.n > 1) {
+                ms.yk = e->ms.yk + (size_t) (l & 1) * y.ml.k * y.ml.E;
+                px.dn = make_tpx(e, true, -1, ms.yk);
+                px.comb = make_tpx(e, false, 2 * l + 1, nullptr);
+            }
+            moe_enqueue(y.ml, ms, e->x, 1, y.fn, e->eps, e->x, 1, e->nsm, e->st, true, e->err, e->trace,
+                        e->launches, [&](cudaError_t r, const char *) { after_launch(e, r); }, nullptr, e->xtab,
+                        e->xnear, MOE_TC_OFF, e->tp.n > 1 ? &px : nullptr);
             continue;
         }
         snprintf(e->cur, sizeof e->cur, "L%d.ffn", l);
@@ -368,7 +379,6 @@ static void close_all(sb_engine * e) {
     if (e->tp.reg) cudaFree(e->tp.reg);
     e->pf.ar.release();
     if (e->pf.h_tok) cudaFreeHost(e->pf.h_tok);
-    if (e->comm) nccl_api()->destroy(e->comm);
     e->ar.release();
     if (e->h_logits) cudaFreeHost(e->h_logits);
     if (e->h_io) cudaFreeHost(e->h_io);
@@ -531,7 +541,8 @@ static bool build(sb_engine * e, char * why, int nwhy) {
         t.off_x = 256;
         t.off_hp = t.off_x + r256((size_t) e->E * 4);
         t.off_lg = t.off_hp + r256((size_t) (e->F > 0 ? e->F : 1) * 4);
-        t.reg_bytes = t.off_lg + r256((size_t) e->V * 4);
+        t.off_yk = t.off_lg + r256((size_t) e->V * 4);
+        t.reg_bytes = t.off_yk + (moe0 ? r256((size_t) 2 * moe0->k * moe0->E * 4) : 0);
         if (t.reg) {
             e->x = (float *) (t.reg + t.off_x);
             e->hp = (float *) (t.reg + t.off_hp);
@@ -557,6 +568,10 @@ static bool build(sb_engine * e, char * why, int nwhy) {
     }
     e->err = (int *) carve(e, 4);
     if (moe0) moe_carve(e->ar, *moe0, 1, e->ms);
+    // MoE layers over GPUs: the per-choice rows in the region the peers map, one
+    // buffer per layer parity -- a peer writes the same buffer again only two
+    // layers on, after waiting for an event this GPU raises after its combine
+    if (moe0 && tp > 1 && e->tp.reg) e->ms.yk = (float *) (e->tp.reg + e->tp.off_yk);
 #ifdef SB_TRACE
     e->n_launch_trace = 8 * e->n_layer + 8;
     e->trace = (unsigned long long *) carve(e, (size_t) e->n_launch_trace * kTraceCtas * 8 * 8);
@@ -757,42 +772,8 @@ int sb_tp_handle(const sb_engine * e, void * out) {
     return 1;
 }
 
-static cudaError_t engine_moe_sum(void * ctx, float * buf, size_t n, cudaStream_t st) {
-    sb_engine * e = (sb_engine *) ctx;
-    const ncclResult_t r = nccl_api()->all_reduce(buf, buf, n, ncclFloat, ncclSum, e->comm, st);
-    if (r != ncclSuccess) {
-        snprintf(g_err, sizeof g_err, "ncclAllReduce: %s", nccl_api()->error(r));
-        return cudaErrorUnknown;
-    }
-    return cudaSuccess;
-}
-
-int sb_tp_nccl(sb_engine * e, const void * nccl_id, char * why, int nwhy) {
-    if (!e || e->tp.n <= 1 || !nccl_id || e->g_tok || e->comm) {
-        snprintf(why, nwhy, "not a tensor-parallel engine awaiting its peers");
-        return 0;
-    }
-    if (!nccl_api()) { snprintf(why, nwhy, "NCCL (libnccl.so.2) could not be loaded"); return 0; }
-    ncclUniqueId uid;
-    memcpy(&uid, nccl_id, sizeof uid);
-    const ncclResult_t r = nccl_api()->init_rank(&e->comm, e->tp.n, uid, e->tp.rank);
-    if (r != ncclSuccess) {
-        snprintf(why, nwhy, "ncclCommInitRank: %s", nccl_api()->error(r));
-        e->comm = nullptr;
-        return 0;
-    }
-    e->moe_ex.sum = engine_moe_sum;
-    e->moe_ex.ctx = e;
-    return 1;
-}
-
 int sb_tp_connect(sb_engine * e, const void * handles, char * why, int nwhy) {
     if (!e || e->tp.n <= 1 || !handles || e->g_tok) { snprintf(why, nwhy, "not a tensor-parallel engine awaiting its peers"); return 0; }
-    for (const LayerD & y : e->L)
-        if (y.moe && !e->comm) {
-            snprintf(why, nwhy, "MoE layers over several GPUs: every rank calls sb_tp_nccl before sb_tp_connect");
-            return 0;
-        }
     TpState & t = e->tp;
     for (int p = 0; p < t.n; p++) {
         if (p == t.rank) continue;

@@ -79,6 +79,9 @@ struct MoeGArgs {
     int * err;
     unsigned long long * trace;
     int launch_id;
+    // DN on a tensor-parallel engine: every output row also stored into each
+    // peer's copy of `out`, then each CTA arrives at the peers (tgemv.cuh TpX)
+    TpX tp;
 };
 
 // ---------------------------------------------------------------- routing
@@ -285,9 +288,16 @@ static __global__ void k_moe_route(const float * lg, int T, int ne, int k, unsig
 // y[t][i] = sum_j w[t][j] * yk[t*k + j][i] in choice order from 0, each step
 // one fused multiply-add as gcc contracts acc += w*t (sml/sml-run.c:3120),
 // added to y[t][i] when resid (the layer's residual add, x + xb).
-static __global__ void k_moe_comb(const float * yk, const float * w, int T, int k, int E, float * y, int resid) {
+// On a tensor-parallel engine (tp.wait_count) the rows of the choices other
+// GPUs hold arrive from them first: one thread of each block waits (bounded).
+static __global__ void k_moe_comb(const float * yk, const float * w, int T, int k, int E, float * y, int resid,
+                                  const __grid_constant__ TpX tp) {
     pdl_launch_dependents();
     pdl_wait();
+    if (tp.n > 1 && tp.wait_count) {
+        if (threadIdx.x == 0) tp_wait(tp);
+        __syncthreads();
+    }
     const int i = blockIdx.x * blockDim.x + threadIdx.x, t = blockIdx.y;
     if (i >= E || t >= T) return;
     float acc = 0.0f;
@@ -535,12 +545,23 @@ __global__ void __launch_bounds__(kTgThreads, 1) k_moe_gemv(const __grid_constan
                         g.out[(size_t) slot[tt] * g.out_stride + scat[idx]] = silu_mul(a, up);
                 } else {
                     const int r = i * TR + lane;
-                    if (lane < TR && r < t.rows) g.out[(size_t) slot[tt] * g.out_stride + r] = a;
+                    if (lane < TR && r < t.rows) {
+                        const size_t at = (size_t) slot[tt] * g.out_stride + r;
+                        g.out[at] = a;
+                        for (int p = 0; p < g.tp.n; p++)
+                            if (g.tp.peer_out[p]) g.tp.peer_out[p][at] = a;
+                    }
                 }
             }
         }
         bar_sync(1, kConsThreads);   // the chunk's activations are free again
         q = qe;
+    }
+    if (g.tp.n > 1 && g.tp.raise) {
+        // every consumer's stores to the peers are ordered before this CTA's
+        // arrival by the barrier of the last chunk (or there were none)
+        bar_sync(1, kConsThreads);
+        if (threadIdx.x == 0) tp_arrive(g.tp);
     }
     SB_MARK(g.trace, g.launch_id, 4);
 }

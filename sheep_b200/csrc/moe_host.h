@@ -258,9 +258,12 @@ inline cudaError_t moe_router_launch(const MoeLayer & m, const MoeScratch & s, c
     return cudaLaunchKernelEx(&cfg, k_moe_router, r);
 }
 
-// y[t] (+)= the choice-order combine of the per-choice outputs s.yk ([T*k][E]).
+// y[t] (+)= the choice-order combine of the per-choice outputs s.yk ([T*k][E]),
+// after waiting for the peers' rows when tp is given.
 inline cudaError_t moe_comb_launch(const MoeLayer & m, const MoeScratch & s, int T, float * y, int resid,
-                                   cudaStream_t st, bool pdl) {
+                                   cudaStream_t st, bool pdl, const TpX * tp = nullptr) {
+    TpX none;
+    memset(&none, 0, sizeof none);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3((m.E + 255) / 256, T);
     cfg.blockDim = dim3(256);
@@ -270,8 +273,17 @@ inline cudaError_t moe_comb_launch(const MoeLayer & m, const MoeScratch & s, int
     at[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = at;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, k_moe_comb, (const float *) s.yk, (const float *) s.r.w, T, m.k, m.E, y, resid);
+    return cudaLaunchKernelEx(&cfg, k_moe_comb, (const float *) s.yk, (const float *) s.r.w, T, m.k, m.E, y, resid,
+                              tp ? *tp : none);
 }
+
+// A tensor-parallel engine's exchange of an MoE layer's rows: the down GEMV
+// stores each row into every rank's per-choice buffer (s.yk lies in the
+// region the peers map) and its CTAs arrive at the peers; the combine waits
+// for them. Each row is computed by the one GPU holding its expert.
+struct MoePeerX {
+    TpX dn, comb;
+};
 
 // Expert parallelism: the per-choice down outputs ([T*k][E]) are summed over
 // the GPUs between the down GEMV and the combine. Each row is written by the one
@@ -294,7 +306,8 @@ template <class Post>
 inline void moe_enqueue(const MoeLayer & m, const MoeScratch & s, const float * x, int T, const float * norm_w,
                         float eps, float * y, int resid, int nsm, cudaStream_t st, bool pdl, int * err,
                         unsigned long long * trace, int launch_id, Post post, const MoeExchange * ex = nullptr,
-                        const ExpfEntry * xtab = nullptr, float xnear = 0.0f, int tc = MOE_TC_OFF) {
+                        const ExpfEntry * xtab = nullptr, float xnear = 0.0f, int tc = MOE_TC_OFF,
+                        const MoePeerX * px = nullptr) {
     const bool use_tc = tc != MOE_TC_OFF && s.tc_chunks > 0 && T >= kMoeTcRows &&
                         (tc == MOE_TC_ON || (long) T * m.k >= (long) kMoeTcAuto * m.ne);
     // one token per chunk at T = 1: a token never picks an expert twice
@@ -325,11 +338,12 @@ inline void moe_enqueue(const MoeLayer & m, const MoeScratch & s, const float * 
             a.out = s.yk; a.out_stride = m.E;
             a.nstage = moe_stages(m.dn, nt);
             a.launch_id = launch_id + 2;
+            if (px) a.tp = px->dn;
             post(moe_gemv(MG_DN, nt, a, nsm, st, pdl), "moe.down");
         }
     }
     if (ex) post(ex->sum(ex->ctx, s.yk, (size_t) T * m.k * m.E, st), "moe.exchange");
-    post(moe_comb_launch(m, s, T, y, resid, st, pdl), "moe.combine");
+    post(moe_comb_launch(m, s, T, y, resid, st, pdl, px ? &px->comb : nullptr), "moe.combine");
 }
 
 }  // namespace sb
