@@ -117,7 +117,7 @@ struct sb_batch {
     float * xs = nullptr, * apart = nullptr;
     unsigned * acnt = nullptr;
     int attn_split = 1, attn_hg = 4, attn_groups = 1;
-    bool attn_mma = true;
+    int attn_t = 0;                   // k_battn_t with 1 or 2 n-tiles of 8 heads (hd 64, 128); 0: k_battn
     int * err = nullptr;
     cudaStream_t st = nullptr;
     cudaGraphExec_t g = nullptr;
@@ -299,8 +299,9 @@ static bool b_build(sb_batch * b, char * why, int nwhy) {
     // (sequence, group) split over attn_split CTAs so that the grid fills the
     // SMs' resident slots in whole waves (two CTAs per SM up to hd 128)
     const int rep = b->nh / b->nkv;
-    b->attn_mma = b->hd <= 128;   // tensor-core attention for hd 64 and 128
-    b->attn_hg = b->attn_mma ? kMHeads : battn_hg(rep);
+    // tensor-core attention for hd 64 and 128 (groups of 8 or 16 heads), CUDA cores for 256
+    b->attn_t = b->hd <= 128 ? (rep <= 8 ? 1 : 2) : 0;
+    b->attn_hg = b->attn_t ? 8 * b->attn_t : battn_hg(rep);
     b->attn_groups = (rep + b->attn_hg - 1) / b->attn_hg;
     {
         const int pairs = B * b->nkv * b->attn_groups, slots = (b->hd <= 128 ? 2 : 1) * b->nsm;
@@ -373,10 +374,15 @@ static void b_attn(sb_batch * b, const BLayer & y, int l) {
     a.n_ctx = b->n_ctx; a.pos = b->pos; a.nsplit = b->attn_split; a.hgroups = b->attn_groups; a.scale = b->scale;
     a.part = b->apart; a.cnt = b->acnt; a.out = b->att; a.ldo = b->qd; a.err = b->err;
     const dim3 grid(b->attn_split, b->nkv * b->attn_groups, b->B);
-    if (b->attn_mma) {
-        const size_t smem = battn_mma_smem(b->hd, b->nh / b->nkv);
-        if (b->hd == 64) k_battn_mma<64><<<grid, kMThreads, smem, b->st>>>(a);
-        else k_battn_mma<128><<<grid, kMThreads, smem, b->st>>>(a);
+    if (b->attn_t) {
+        const size_t smem = battn_t_smem(b->hd, b->attn_t);
+        if (b->hd == 64) {
+            if (b->attn_t == 1) k_battn_t<64, 1><<<grid, kMThreads, smem, b->st>>>(a);
+            else k_battn_t<64, 2><<<grid, kMThreads, smem, b->st>>>(a);
+        } else {
+            if (b->attn_t == 1) k_battn_t<128, 1><<<grid, kMThreads, smem, b->st>>>(a);
+            else k_battn_t<128, 2><<<grid, kMThreads, smem, b->st>>>(a);
+        }
         b_after(b, cudaGetLastError());
         return;
     }
@@ -495,11 +501,14 @@ static sb_batch * open_batch(const char * path, int n_seq, int n_ctx, int n_page
     upload_rope(b->rcos, b->rsin, b->n_ctx, b->hd, b->theta);
     BAttnArgs none;
     memset(&none, 0, sizeof none);
-    const int msm = (int) battn_mma_smem(b->hd, b->nh / b->nkv);
-    const cudaError_t ar =
-        !b->attn_mma ? b_attn_launch(b->hd, b->attn_hg, dim3(1), battn_smem(b->hd, b->attn_hg), b->st, none, true)
-        : b->hd == 64 ? cudaFuncSetAttribute(k_battn_mma<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, msm)
-                      : cudaFuncSetAttribute(k_battn_mma<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, msm);
+    cudaError_t ar;
+    if (b->attn_t) {
+        void (*kt)(BAttnArgs) = b->hd == 64 ? (b->attn_t == 1 ? k_battn_t<64, 1> : k_battn_t<64, 2>)
+                                            : (b->attn_t == 1 ? k_battn_t<128, 1> : k_battn_t<128, 2>);
+        ar = cudaFuncSetAttribute(kt, cudaFuncAttributeMaxDynamicSharedMemorySize, (int) battn_t_smem(b->hd, b->attn_t));
+    } else {
+        ar = b_attn_launch(b->hd, b->attn_hg, dim3(1), battn_smem(b->hd, b->attn_hg), b->st, none, true);
+    }
     if (!bck(ar, "attention shared memory") || !bck(cudaMallocHost(&b->h_logits, (size_t) b->B * b->V * 4), "pinned logits") ||
         !bck(cudaMallocHost(&b->h_io, (size_t) 2 * b->B * 4), "pinned io"))
         return b_fail(b, why, nwhy, g_berr);

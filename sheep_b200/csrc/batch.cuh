@@ -353,9 +353,7 @@ __global__ void __launch_bounds__(kBThreads, 2) k_battn(const __grid_constant__ 
 // ---------------------------------------------------------------- attention on the tensor cores
 
 // Warp-level f16 MMA (m16n8k16, fp32 accumulate), ldmatrix and 16-byte async
-// copies. Decode attention has 1-16 query heads per KV head, so the product is
-// M = heads (padded to 16) by N = positions: the warp-level form keeps scores
-// in registers and hands them to the value product as its A fragments.
+// copies (k_battn_t).
 SB_DEV void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
     asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
                  "{%0,%1,%2,%3};"
@@ -394,48 +392,48 @@ constexpr int kMChunk = 64;      // positions per ring stage
 static_assert(kBChunk == 64 && kMChunk == 64, "a cache page holds one attention chunk of each KV head");
 constexpr int kMStages = 3;
 constexpr int kMThreads = 128;   // 4 warps, 16 positions of each chunk apiece
-constexpr int kMHeads = 16;      // query heads per CTA (the MMA's M)
 
-__host__ __device__ inline int battn_mma_q(int rep) { return (rep < kMHeads ? rep : kMHeads + 3) / 4 * 4; }
-__host__ __device__ inline size_t battn_mma_smem(int hd, int rep) {
-    const size_t ring = (size_t) kMStages * 2 * kMChunk * (hd + 8) * 2;
-    const size_t comb = (size_t) (kMThreads / 32) * kMHeads * hd * 4;
-    const int nq = rep < kMHeads ? (rep + 3) / 4 * 4 : kMHeads;
-    return (ring > comb ? ring : comb) + (size_t) (nq * hd + 3 * hd) * 4 + 16;
-}
 
-// One CTA per (split of the positions, KV head x group of up to 16 query heads,
-// sequence), 4 warps. Chunks of 64 positions stream into a 3-stage ring by
-// 16-byte async copies into rows padded by 16 bytes (ldmatrix without bank
-// conflicts; rows past the position are zero-filled). Per chunk each warp
-// takes 16 positions:
-//   scores  S[head][pos] = Q K^T over hd/16 K steps, Q as fp16 hi + lo
-//           fragments in registers, K fragments by ldmatrix (2 x 8 positions);
-//   softmax the warp's own running max and sum per head (rows g and g+8 of
-//           the fragment), expf, its accumulators rescaled;
-//   values  O[head][d] += P V with P (hi + lo) taken straight from the score
-//           accumulators, V fragments by ldmatrix.trans.
-// The 4 warps' (max, sum, O) merge at the end, then the splits as in k_battn.
-template <int HD>
-__global__ void __launch_bounds__(kMThreads, 2) k_battn_mma(const __grid_constant__ BAttnArgs g) {
+// Decode attention of a batch on the tensor cores (hd 64, 128). One CTA per
+// (split of the positions, KV head x group of up to 16 query heads, sequence),
+// 4 warps. Chunks of 64 positions stream into a 3-stage ring by 16-byte async
+// copies into rows padded by 16 bytes (ldmatrix without bank conflicts; rows
+// past the position are zero-filled). Decode has few query heads per KV head
+// (configuration 3 has 4, configuration 0 6, configuration 4 16), so the
+// products are turned over: M = the 16 positions of a warp, N = the CTA's
+// heads in n-tiles of 8 (NH8 tiles) -- a KV head's 4 query heads fill half an
+// n-tile, where as the 16-row M of a heads-by-positions product they filled a
+// quarter, and the two products need half the MMAs:
+//   scores  S^T[pos][head] = K Q^T: K rows by ldmatrix as the A fragment, Q^T
+//           (hi + lo fp16 halves) as B fragments in registers;
+//   softmax per head column: the 16 positions' max and sum by shuffles across
+//           the fragment rows, the running state per head in every lane;
+//   values  O^T[dim][head] += V^T P^T: V^T fragments by ldmatrix.trans, P^T
+//           (hi + lo) as B fragments, turned from the score layout through a
+//           small tile in shared memory.
+// Rows past the position are masked. The 4 warps' (max, sum, O) merge at the
+// end, then the splits as in k_battn.
+template <int HD, int NH8>
+__global__ void __launch_bounds__(kMThreads, 2) k_battn_t(const __grid_constant__ BAttnArgs g) {
+    constexpr int HG = 8 * NH8;          // query heads of the CTA
     constexpr int RS = HD + 8;           // padded row, halves
     constexpr int KS = HD / 16;          // K steps of the scores
-    constexpr int NT = HD / 8;           // n-tiles of the output
+    constexpr int MT = HD / 16;          // m-tiles of the output (dims)
     constexpr int NW = kMThreads / 32;
     constexpr int PIECES = HD / 8;       // 16-byte pieces per row
     constexpr size_t STAGE = (size_t) 2 * kMChunk * RS;   // halves
     constexpr size_t RING = (size_t) kMStages * STAGE * 2;
-    constexpr size_t COMB = (size_t) NW * kMHeads * HD * 4;
+    constexpr size_t COMB = (size_t) NW * HG * HD * 4;
     extern __shared__ __align__(16) uint8_t bsm[];
     __shared__ double red[NW];
-    __shared__ float wm[NW][kMHeads], wl[NW][kMHeads];
+    __shared__ float wm[NW][HG], wl[NW][HG];
+    __shared__ float pt[NW][16][HG + 1];   // a warp's probabilities, [position][head]
     __shared__ unsigned last_flag;
     const int split = blockIdx.x, gy = blockIdx.y, b = blockIdx.z;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int gq = lane >> 2, tq = lane & 3;   // fragment row / column pair
     const int rep = g.n_head / g.n_kv;
-    const int kvh = gy / g.hgroups, h0 = (gy % g.hgroups) * kMHeads, nh = min(kMHeads, rep - h0);
-    const int nq = (nh + 3) / 4 * 4;           // query rows kept in shared memory
+    const int kvh = gy / g.hgroups, h0 = (gy % g.hgroups) * HG, nh = min(HG, rep - h0);
     const int pos = g.pos[b];
     float * outb = g.out + (size_t) b * g.ldo + ((size_t) kvh * rep + h0) * HD;
     if (pos < 0) {
@@ -444,7 +442,7 @@ __global__ void __launch_bounds__(kMThreads, 2) k_battn_mma(const __grid_constan
         return;
     }
     if (pos >= g.n_ctx || rep > kBMaxRep) {
-        if (tid == 0) atomicExch(g.err, 213);
+        if (tid == 0) atomicExch(g.err, 214);
         return;
     }
     const int nchunk = pos / kMChunk + 1;
@@ -454,9 +452,9 @@ __global__ void __launch_bounds__(kMThreads, 2) k_battn_mma(const __grid_constan
     if (c0 >= nchunk) return;
     const int nmine = c1 - c0;
     uint16_t * ring = reinterpret_cast<uint16_t *>(bsm);
-    float * qs = reinterpret_cast<float *>(bsm + (RING > COMB ? RING : COMB));   // [nq][HD]
-    float * kn = qs + nq * HD, * vn = kn + HD, * cs = vn + HD, * sn = cs + HD / 2;
-    float * comb = reinterpret_cast<float *>(bsm);                                 // [NW][16][HD] at the end
+    float * qs = reinterpret_cast<float *>(bsm + (RING > COMB ? RING : COMB));   // [HG][HD]
+    float * kn = qs + HG * HD, * vn = kn + HD, * cs = vn + HD, * sn = cs + HD / 2;
+    float * comb = reinterpret_cast<float *>(bsm);                              // [NW][HG][HD] at the end
 
     auto issue = [&](int j) {   // chunk c0 + j into stage j % kMStages
         const int t0 = (c0 + j) * kMChunk, nt = min(pos + 1, t0 + kMChunk) - t0;
@@ -479,7 +477,7 @@ __global__ void __launch_bounds__(kMThreads, 2) k_battn_mma(const __grid_constan
         cs[i] = g.rcos[(size_t) pos * (HD / 2) + i];
         sn[i] = g.rsin[(size_t) pos * (HD / 2) + i];
     }
-    for (int i = tid; i < nq * HD; i += kMThreads)
+    for (int i = tid; i < HG * HD; i += kMThreads)
         qs[i] = i < nh * HD ? qrow[((size_t) kvh * rep + h0) * HD + i] : 0.0f;
     for (int i = tid; i < HD; i += kMThreads) {
         kn[i] = qrow[g.koff + kvh * HD + i];
@@ -488,23 +486,29 @@ __global__ void __launch_bounds__(kMThreads, 2) k_battn_mma(const __grid_constan
     __syncthreads();
     for (int h = 0; h < nh; h++) norm_rope(qs + h * HD, g.qn, g.eps, HD, cs, sn, red);
     norm_rope(kn, g.kn, g.eps, HD, cs, sn, red);
-    // Q fragments (rows gq and gq + 8 are heads; columns the K step's dims)
-    uint32_t qa[KS][4], ql[KS][4];
+    // Q^T as B fragments: head gq of n-tile n, dims ks*16 + 2 tq (+1) and + 8 (+9)
+    uint32_t qb[NH8][KS][2], qbl[NH8][KS][2];
 #pragma unroll
-    for (int ks = 0; ks < KS; ks++) {
+    for (int n = 0; n < NH8; n++)
 #pragma unroll
-        for (int e = 0; e < 4; e++) {
-            const int row = gq + (e & 1) * 8, col = ks * 16 + 2 * tq + (e >> 1) * 8;
-            const float x0 = row < nq ? qs[row * HD + col] : 0.0f, x1 = row < nq ? qs[row * HD + col + 1] : 0.0f;
-            split_h2(x0, x1, qa[ks][e], ql[ks][e]);
-        }
+        for (int ks = 0; ks < KS; ks++)
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const float * q = qs + (n * 8 + gq) * HD + ks * 16 + 2 * tq + e * 8;
+                split_h2(q[0], q[1], qb[n][ks][e], qbl[n][ks][e]);
+            }
+    // running state of heads n*8 + 2 tq (+1), the same in every lane of a column
+    float mh[NH8][2], lh[NH8][2];
+    float o[MT][NH8][4];
+#pragma unroll
+    for (int n = 0; n < NH8; n++) {
+        mh[n][0] = mh[n][1] = -INFINITY;
+        lh[n][0] = lh[n][1] = 0.0f;
+#pragma unroll
+        for (int m = 0; m < MT; m++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) o[m][n][e] = 0.0f;
     }
-    float m2[2] = {-INFINITY, -INFINITY}, l2[2] = {0.0f, 0.0f};
-    float o[NT][4];
-#pragma unroll
-    for (int n = 0; n < NT; n++)
-#pragma unroll
-        for (int e = 0; e < 4; e++) o[n][e] = 0.0f;
     const int pw = warp * 16;   // the warp's positions in each chunk
     for (int j = 0; j < nmine; j++) {
         const int c = c0 + j, t0 = c * kMChunk, nt = min(pos + 1, t0 + kMChunk) - t0;
@@ -527,80 +531,72 @@ __global__ void __launch_bounds__(kMThreads, 2) k_battn_mma(const __grid_constan
             __syncthreads();
         }
         if (pw < nt) {
-            // ---- scores of positions pw .. pw + 15 (two n-tiles of 8)
-            // hi and lo parts in their own accumulators: four independent MMA chains
-            float sc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
-            float sl[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
-            const uint32_t kaddr = smem_u32(Ks + (pw + ((lane >> 4) << 3) + (lane & 7)) * RS + ((lane >> 3) & 1) * 8);
+            // ---- scores: rows gq, gq + 8 are positions pw + ..., columns heads
+            float sc[NH8][4], sl[NH8][4];
+#pragma unroll
+            for (int n = 0; n < NH8; n++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) sc[n][e] = sl[n][e] = 0.0f;
+            const uint32_t kaddr = smem_u32(Ks + (pw + (lane & 15)) * RS + (lane >> 4) * 8);
 #pragma unroll
             for (int ks = 0; ks < KS; ks++) {
-                uint32_t b0, b1, b2, b3;
-                ldsm4(kaddr + ks * 32, b0, b1, b2, b3);
-                mma16816(sc[0], qa[ks], b0, b1);
-                mma16816(sl[0], ql[ks], b0, b1);
-                mma16816(sc[1], qa[ks], b2, b3);
-                mma16816(sl[1], ql[ks], b2, b3);
-            }
+                uint32_t a[4];
+                ldsm4(kaddr + ks * 32, a[0], a[1], a[2], a[3]);
 #pragma unroll
-            for (int n = 0; n < 2; n++)
-#pragma unroll
-                for (int e = 0; e < 4; e++) sc[n][e] += sl[n][e];
-            // ---- online softmax per head row (gq: e = 0,1; gq + 8: e = 2,3)
-            float pr[2][4];
-#pragma unroll
-            for (int rr = 0; rr < 2; rr++) {
-                float mx = -INFINITY;
-#pragma unroll
-                for (int n = 0; n < 2; n++)
-#pragma unroll
-                    for (int e = 0; e < 2; e++) {
-                        const int col = pw + n * 8 + 2 * tq + e;
-                        const float v = col < nt ? sc[n][2 * rr + e] * g.scale : -INFINITY;
-                        sc[n][2 * rr + e] = v;
-                        mx = fmaxf(mx, v);
-                    }
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-                mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-                const float mn = fmaxf(m2[rr], mx);
-                const float alpha = m2[rr] == -INFINITY ? 0.0f : expf(m2[rr] - mn);
-                float sum = 0.0f;
-#pragma unroll
-                for (int n = 0; n < 2; n++)
-#pragma unroll
-                    for (int e = 0; e < 2; e++) {
-                        const float v = sc[n][2 * rr + e];
-                        const float pe = v == -INFINITY ? 0.0f : expf(v - mn);
-                        pr[n][2 * rr + e] = pe;
-                        sum += pe;
-                    }
-                sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-                sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-                l2[rr] = l2[rr] * alpha + sum;
-                m2[rr] = mn;
-#pragma unroll
-                for (int n = 0; n < NT; n++) {
-                    o[n][2 * rr] *= alpha;
-                    o[n][2 * rr + 1] *= alpha;
+                for (int n = 0; n < NH8; n++) {
+                    mma16816(sc[n], a, qb[n][ks][0], qb[n][ks][1]);
+                    mma16816(sl[n], a, qbl[n][ks][0], qbl[n][ks][1]);
                 }
             }
-            // ---- values: P (16 heads x 16 positions) from the score fragments
-            uint32_t pa[4], pl[4];
-            split_h2(pr[0][0], pr[0][1], pa[0], pl[0]);
-            split_h2(pr[0][2], pr[0][3], pa[1], pl[1]);
-            split_h2(pr[1][0], pr[1][1], pa[2], pl[2]);
-            split_h2(pr[1][2], pr[1][3], pa[3], pl[3]);
-            const uint32_t vaddr = smem_u32(Vs + (pw + ((lane >> 3) & 1) * 8 + (lane & 7)) * RS + (lane >> 4) * 8);
+            const bool in0 = pw + gq < nt, in1 = pw + gq + 8 < nt;
 #pragma unroll
-            // four output tiles at a time: their hi MMAs, then their lo MMAs, so
-            // the two MMAs into one accumulator are four apart
-            for (int n = 0; n < NT; n += 4) {
-                uint32_t b[8];
-                ldsm4t(vaddr + n * 16, b[0], b[1], b[2], b[3]);
-                ldsm4t(vaddr + (n + 2) * 16, b[4], b[5], b[6], b[7]);
+            for (int n = 0; n < NH8; n++) {
 #pragma unroll
-                for (int i = 0; i < 4; i++) mma16816(o[n + i], pa, b[2 * i], b[2 * i + 1]);
+                for (int hh = 0; hh < 2; hh++) {
+                    // head n*8 + 2 tq + hh: its values at positions gq (e = hh) and gq + 8 (e = 2 + hh)
+                    const float v0 = in0 ? (sc[n][hh] + sl[n][hh]) * g.scale : -INFINITY;
+                    const float v1 = in1 ? (sc[n][2 + hh] + sl[n][2 + hh]) * g.scale : -INFINITY;
+                    float mx = fmaxf(v0, v1);
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+                    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+                    const float mn = fmaxf(mh[n][hh], mx);
+                    const float alpha = mh[n][hh] == -INFINITY ? 0.0f : expf(mh[n][hh] - mn);
+                    const float p0 = v0 == -INFINITY ? 0.0f : expf(v0 - mn);
+                    const float p1 = v1 == -INFINITY ? 0.0f : expf(v1 - mn);
+                    float sum = p0 + p1;
+                    sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+                    sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+                    sum += __shfl_xor_sync(0xffffffffu, sum, 16);
+                    lh[n][hh] = lh[n][hh] * alpha + sum;
+                    mh[n][hh] = mn;
 #pragma unroll
-                for (int i = 0; i < 4; i++) mma16816(o[n + i], pl, b[2 * i], b[2 * i + 1]);
+                    for (int m = 0; m < MT; m++) {
+                        o[m][n][hh] *= alpha;
+                        o[m][n][2 + hh] *= alpha;
+                    }
+                    pt[warp][gq][n * 8 + 2 * tq + hh] = p0;
+                    pt[warp][gq + 8][n * 8 + 2 * tq + hh] = p1;
+                }
+            }
+            __syncwarp();
+            // ---- values: P^T (positions x heads) as B fragments: head gq, positions 2 tq (+1), + 8 (+9)
+            uint32_t pb[NH8][2], pbl[NH8][2];
+#pragma unroll
+            for (int n = 0; n < NH8; n++) {
+                split_h2(pt[warp][2 * tq][n * 8 + gq], pt[warp][2 * tq + 1][n * 8 + gq], pb[n][0], pbl[n][0]);
+                split_h2(pt[warp][2 * tq + 8][n * 8 + gq], pt[warp][2 * tq + 9][n * 8 + gq], pb[n][1], pbl[n][1]);
+            }
+            __syncwarp();
+            const uint32_t vaddr = smem_u32(Vs + (pw + ((lane >> 4) << 3) + (lane & 7)) * RS + ((lane >> 3) & 1) * 8);
+#pragma unroll
+            for (int m = 0; m < MT; m++) {
+                uint32_t a[4];
+                ldsm4t(vaddr + m * 32, a[0], a[1], a[2], a[3]);
+#pragma unroll
+                for (int n = 0; n < NH8; n++) mma16816(o[m][n], a, pb[n][0], pb[n][1]);
+#pragma unroll
+                for (int n = 0; n < NH8; n++) mma16816(o[m][n], a, pbl[n][0], pbl[n][1]);
             }
         }
         __syncthreads();   // the stage is free
@@ -610,20 +606,27 @@ __global__ void __launch_bounds__(kMThreads, 2) k_battn_mma(const __grid_constan
     cp_async_wait<0>();
     __syncthreads();
     // ---- the warps' partial softmax states merge (the ring is free)
-    if (tq == 0) {
-        wm[warp][gq] = m2[0]; wm[warp][gq + 8] = m2[1];
-        wl[warp][gq] = l2[0]; wl[warp][gq + 8] = l2[1];
+    if (gq == 0) {
+#pragma unroll
+        for (int n = 0; n < NH8; n++)
+#pragma unroll
+            for (int hh = 0; hh < 2; hh++) {
+                wm[warp][n * 8 + 2 * tq + hh] = mh[n][hh];
+                wl[warp][n * 8 + 2 * tq + hh] = lh[n][hh];
+            }
     }
 #pragma unroll
-    for (int n = 0; n < NT; n++) {
-        comb[(warp * kMHeads + gq) * HD + n * 8 + 2 * tq] = o[n][0];
-        comb[(warp * kMHeads + gq) * HD + n * 8 + 2 * tq + 1] = o[n][1];
-        comb[(warp * kMHeads + gq + 8) * HD + n * 8 + 2 * tq] = o[n][2];
-        comb[(warp * kMHeads + gq + 8) * HD + n * 8 + 2 * tq + 1] = o[n][3];
-    }
+    for (int m = 0; m < MT; m++)
+#pragma unroll
+        for (int n = 0; n < NH8; n++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int d = m * 16 + gq + (e >> 1) * 8, h = n * 8 + 2 * tq + (e & 1);
+                comb[(warp * HG + h) * HD + d] = o[m][n][e];
+            }
     __syncthreads();
     const size_t grp = (size_t) b * g.n_kv * g.hgroups + gy;
-    float * pb = g.part + (grp * g.nsplit + split) * kMHeads * (HD + 2);
+    float * pbuf = g.part + (grp * g.nsplit + split) * HG * (HD + 2);
     for (int i = tid; i < nh * HD; i += kMThreads) {
         const int h = i / HD, d = i % HD;
         float M = -INFINITY;
@@ -635,12 +638,12 @@ __global__ void __launch_bounds__(kMThreads, 2) k_battn_mma(const __grid_constan
             if (wm[w][h] == -INFINITY) continue;
             const float e = expf(wm[w][h] - M);
             L += wl[w][h] * e;
-            ov += comb[(w * kMHeads + h) * HD + d] * e;
+            ov += comb[(w * HG + h) * HD + d] * e;
         }
         if (nact == 1) outb[h * HD + d] = ov / L;
         else {
-            pb[h * (HD + 2) + 2 + d] = ov;
-            if (d == 0) { pb[h * (HD + 2)] = M; pb[h * (HD + 2) + 1] = L; }
+            pbuf[h * (HD + 2) + 2 + d] = ov;
+            if (d == 0) { pbuf[h * (HD + 2)] = M; pbuf[h * (HD + 2) + 1] = L; }
         }
     }
     if (nact == 1) return;
@@ -650,8 +653,8 @@ __global__ void __launch_bounds__(kMThreads, 2) k_battn_mma(const __grid_constan
     __syncthreads();
     if (!last_flag) return;
     __threadfence();
-    const float * P = g.part + grp * g.nsplit * kMHeads * (HD + 2);
-    const size_t sst = (size_t) kMHeads * (HD + 2);
+    const float * P = g.part + grp * g.nsplit * HG * (HD + 2);
+    const size_t sst = (size_t) HG * (HD + 2);
     for (int i = tid; i < nh * HD; i += kMThreads) {
         const int h = i / HD, d = i % HD;
         float M = -INFINITY;
@@ -665,6 +668,12 @@ __global__ void __launch_bounds__(kMThreads, 2) k_battn_mma(const __grid_constan
         outb[h * HD + d] = ov / L;
     }
     if (tid == 0) g.cnt[grp] = 0;
+}
+
+__host__ __device__ inline size_t battn_t_smem(int hd, int nh8) {
+    const size_t ring = (size_t) kMStages * 2 * kMChunk * (hd + 8) * 2;
+    const size_t comb = (size_t) (kMThreads / 32) * 8 * nh8 * hd * 4;
+    return (ring > comb ? ring : comb) + (size_t) (8 * nh8 * hd + 3 * hd) * 4 + 16;
 }
 
 // Greedy choice per sequence: the first index of the largest logit
