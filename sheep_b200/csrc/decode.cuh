@@ -306,7 +306,9 @@ __host__ __device__ inline size_t attn_seq_smem_bytes(int hd, int n_ctx) {
 // staged rows. The serial loops (the softmax sum, each dim's chain) load a
 // block of 32 positions before its arithmetic.
 template <int HD>
-__global__ void __launch_bounds__(kSeqThreads) k_attn_seq(const __grid_constant__ AttnArgs g) {
+// 32 registers a thread (8 CTAs' worth by the bound): two of its warps fit
+// beside a streaming GEMV's on each SM sub-partition (tgemv.cuh k_tgemv).
+__global__ void __launch_bounds__(kSeqThreads, 8) k_attn_seq(const __grid_constant__ AttnArgs g) {
     extern __shared__ __align__(16) float sm[];
     __shared__ double red[kSeqThreads / 32];
     __shared__ float wred[kSeqThreads / 32];

@@ -903,7 +903,12 @@ SB_DEV float tile_rows(const uint8_t * tile, const TileGeom & tg, const ActS & a
 }
 
 template <int NB, int SIX>
-__global__ void __launch_bounds__(kTgThreads, 1) k_tgemv(const __grid_constant__ TGArgs g) {
+// At most 88 registers a thread: a CTA's 17 warps fall 5/4/4/4 on the SM's four
+// sub-partitions, and at 88 the busiest keeps room for two warps of the decode
+// attention kernel (32 registers), so attention's CTAs start beside the q|k|v
+// GEMV and stage their cached rows while it runs (96 registers left no room:
+// attention waited for the GEMV's CTAs to leave; measured 1037 -> 1073 tok/s).
+__global__ void __maxnreg__(88) k_tgemv(const __grid_constant__ TGArgs g) {
     const int MODE = g.mode;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages], statics;
