@@ -289,7 +289,9 @@ def main():
         ok, why = sheep_b200.sml_gpu_open(path, n_ctx)
         if not ok:
             raise RuntimeError(why)
-        prefill, step = (lambda ids_, p0: sheep_b200.sml_gpu_prefill(ids_, p0)), sheep_b200.sml_gpu_step
+        # the logits as a C caller gets them: the library's host buffer, read in place
+        prefill = lambda ids_, p0: sheep_b200.sml_gpu_prefill(ids_, p0)
+        step = lambda t, p: sheep_b200.sml_gpu_step(t, p, copy=False)
     else:
         prefill, step = eng.prefill, eng.step
     lg = prefill(prompt, 0)

@@ -617,9 +617,14 @@ def sml_gpu_prefill(ids, pos0, n=None):
     return None if not p else np.ctypeslib.as_array(p, shape=(_n_vocab(),)).copy()
 
 
-def sml_gpu_step(tok, pos):
+def sml_gpu_step(tok, pos, copy=True):
+    """Host logits of `tok` at `pos`. copy=False returns a view of the library's
+    own buffer, as a C caller sees it: valid until the next call."""
     p = lib().sml_gpu_step(tok, pos)
-    return None if not p else np.ctypeslib.as_array(p, shape=(_n_vocab(),)).copy()
+    if not p:
+        return None
+    a = np.ctypeslib.as_array(p, shape=(_n_vocab(),))
+    return a.copy() if copy else a
 
 
 def sml_gpu_layers():
