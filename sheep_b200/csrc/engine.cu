@@ -554,8 +554,9 @@ static bool build(sb_engine * e, char * why, int nwhy) {
     e->vc = (uint16_t *) carve(e, kv);
     e->rcos = (float *) carve(e, (size_t) e->n_ctx * (e->hd / 2) * 4);
     e->rsin = (float *) carve(e, (size_t) e->n_ctx * (e->hd / 2) * 4);
-    e->tok = (int *) carve(e, 4);
-    e->pos = (int *) carve(e, 4);
+    // tok and pos side by side: one 8-byte copy sets both
+    e->tok = (int *) carve(e, 8);
+    e->pos = e->tok + 1;
     e->tlog = (int *) carve(e, (size_t) (e->n_ctx + 1) * 4);
     e->am_val = (float *) carve(e, (size_t) 4 * e->nsm * 4);
     e->am_idx = (int *) carve(e, (size_t) 4 * e->nsm * 4);
@@ -811,8 +812,7 @@ const float * sb_device_logits(const sb_engine * e) { return e->logits; }
 static bool set_tok_pos(sb_engine * e, int tok, int pos) {
     e->h_io[0] = tok;
     e->h_io[1] = pos;
-    return ck(cudaMemcpyAsync(e->tok, &e->h_io[0], 4, cudaMemcpyHostToDevice, e->st), "tok") &&
-           ck(cudaMemcpyAsync(e->pos, &e->h_io[1], 4, cudaMemcpyHostToDevice, e->st), "pos");
+    return ck(cudaMemcpyAsync(e->tok, &e->h_io[0], 8, cudaMemcpyHostToDevice, e->st), "tok and pos");
 }
 
 // One token through the captured graph, or eagerly with per-kernel checks.
@@ -824,6 +824,14 @@ static bool run_token(sb_engine * e) {
 
 // After a synchronize: the kernels' error flag (a bounded wait that gave up, a
 // failed check) makes the call fail with its code.
+static bool report_err(int err) {
+    if (err) {
+        snprintf(g_err, sizeof g_err, "a kernel reported error code %d (%s)", err,
+                 err == 7 ? "a tensor-parallel peer's event did not arrive" : "a bounded wait or check");
+        return false;
+    }
+    return true;
+}
 static bool check_err(sb_engine * e) {
     int err = 0;
     if (!ck(cudaMemcpy(&err, e->err, 4, cudaMemcpyDeviceToHost), "error flag")) return false;
@@ -839,8 +847,11 @@ const float * sb_step(sb_engine * e, int tok, int pos) {
     if (!e || pos < 0 || pos >= e->n_ctx || tok < 0 || tok >= e->V) return nullptr;
     if (!set_tok_pos(e, tok, pos)) return nullptr;
     if (!run_token(e)) return nullptr;
-    if (!ck(cudaMemcpyAsync(e->h_logits, e->logits, (size_t) e->V * 4, cudaMemcpyDeviceToHost, e->st), "logits")) return nullptr;
-    if (!ck(cudaStreamSynchronize(e->st), "step") || !check_err(e)) return nullptr;
+    // the logits and the kernels' error flag come back with one synchronization
+    if (!ck(cudaMemcpyAsync(e->h_logits, e->logits, (size_t) e->V * 4, cudaMemcpyDeviceToHost, e->st), "logits") ||
+        !ck(cudaMemcpyAsync(&e->h_io[63], e->err, 4, cudaMemcpyDeviceToHost, e->st), "error flag"))
+        return nullptr;
+    if (!ck(cudaStreamSynchronize(e->st), "step") || !report_err(e->h_io[63])) return nullptr;
     return e->h_logits;
 }
 
@@ -1041,8 +1052,7 @@ const float * sb_prefill(sb_engine * e, const int * ids, int pos0, int n) {
         const int slot = 2 + (i % 30) * 2;
         e->h_io[slot] = ids[i];
         e->h_io[slot + 1] = pos0 + i;
-        if (!ck(cudaMemcpyAsync(e->tok, &e->h_io[slot], 4, cudaMemcpyHostToDevice, e->st), "tok") ||
-            !ck(cudaMemcpyAsync(e->pos, &e->h_io[slot + 1], 4, cudaMemcpyHostToDevice, e->st), "pos") ||
+        if (!ck(cudaMemcpyAsync(e->tok, &e->h_io[slot], 8, cudaMemcpyHostToDevice, e->st), "tok and pos") ||
             !run_token(e))
             return nullptr;
         if (i % 30 == 29) { if (!ck(cudaStreamSynchronize(e->st), "prefill") || !check_err(e)) return nullptr; }
