@@ -576,10 +576,8 @@ def decode_cfg4_batch(peak, n_seq=64, prompt=1024, ngen=32, nwarm=2):
     """Configuration 4 as batched serving on one GPU: n_seq sequences of a
     `prompt`-id random prompt stepped through the batched engine, then ngen
     greedy tokens each decoded together: per MoE layer the router and the
-    chosen experts of all n_seq rows (the automatic choice: at 64 rows x 8
-    choices over 128 experts, 4 rows per expert, the integer kernels, which
-    beat the f16 tensor-core path below 8 rows per expert), the attention
-    products on the int8 tensor-core path.
+    chosen experts of all n_seq rows on the tensor cores (f16, codes decoded
+    in shared memory), the attention products on the int8 tensor-core path.
     Experts drawn on the device (the direct=2 file). Bytes per step: the
     attention and head weights once (as stored), every expert (at 64 rows x 8
     choices almost all of the 128 are chosen in every layer) and the KV caches
@@ -611,8 +609,7 @@ def decode_cfg4_batch(peak, n_seq=64, prompt=1024, ngen=32, nwarm=2):
                 "ms_per_step": round(ms / steps, 3), "bytes_per_step_alg": int(alg),
                 "gbs_alg": round(alg * steps / (ms / 1000.0) / 1e9, 1),
                 "frac_alg": round(alg * steps / (ms / 1000.0) / 1e9 / peak, 4),
-                "experts": "drawn on the device (direct=2 file); expert products on the integer kernels "
-                           "(automatic choice at 4 rows per expert)",
+                "experts": "drawn on the device (direct=2 file); expert products on the tensor cores",
                 "launches_per_step": b.launches, "open_s": round(t_open, 1), "run_s": round(t_run, 1)}
     finally:
         b.close()

@@ -408,7 +408,7 @@ static void b_enqueue(sb_batch * b) {
             snprintf(b->cur, sizeof b->cur, "L%d.moe", l);
             moe_enqueue(y.ml, b->ms, b->x, b->B, y.fn, b->eps, b->x, 1, b->nsm, b->st, false, b->err, nullptr,
                         b->launches, [&](cudaError_t r, const char *) { b_after(b, r); }, nullptr, nullptr, 0.0f,
-                        MOE_TC_AUTO);
+                        MOE_TC_ON);   // configuration 4 at 64 slots: 1160 tok/s here, 759 on the integer kernels
             continue;
         }
         snprintf(b->cur, sizeof b->cur, "L%d.ffn", l);
