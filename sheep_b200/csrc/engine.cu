@@ -110,6 +110,7 @@ struct sb_engine {
     const ExpfEntry * xtab = nullptr;  // the host libm's expf corrections (expf_libm.h)
     float xnear = 0.0f;                // ... looked up within this midpoint distance
     MoeScratch ms;                    // routing scratch shared by every MoE layer (one token)
+    uint8_t * hq = nullptr;           // down's input quantized by the gate/up GEMV (TGArgs.hq; one GPU)
     int * err = nullptr;              // bounded waits that gave up
     unsigned long long * trace = nullptr;   // trace build: [launch][cta][8] timestamps
     int n_launch_trace = 0;
@@ -258,6 +259,21 @@ static void tp_counts(sb_engine * e) {
     c += grid(e->head); t.cum.push_back(c);
 }
 
+// One GPU: the gate/up GEMV quantizes the hidden vector for the down GEMV (its
+// CTAs take whole groups; TGArgs.grp_tiles) when the groups a CTA takes fit its
+// buffer and the block copies in 16-byte units.
+static bool hq_plan(const sb_engine * e, const TT & gu, int F) {
+    if (!e->hq || e->tp.n > 1 || gu.TR < 2 || gu.TR > 16 || F % 32 || gu.cols < kHqMaxGroups * 32) return false;
+    const int ng = F / 32, grid = gu.ntiles < e->nsm ? gu.ntiles : e->nsm;
+    return gu.ntiles == ng * (64 / gu.TR) && (ng + grid - 1) / grid <= kHqMaxGroups && (F + ng * 8) % 16 == 0;
+}
+static void set_hq(sb_engine * e, TGArgs & ffn, TGArgs * down, const LayerD & y) {
+    if (!hq_plan(e, y.gateup, e->F)) return;
+    ffn.grp_tiles = 64 / y.gateup.TR;
+    ffn.hq = e->hq;
+    if (down) down->in_act = e->hq;
+}
+
 static void launch_tg(sb_engine * e, int mode, const TGArgs & g0) {
     const int grid = g0.t.ntiles < e->nsm ? g0.t.ntiles : e->nsm;
     TGArgs g = g0;
@@ -335,6 +351,7 @@ static void enqueue_token(sb_engine * e) {
             g.scatter = y.down_iperm;
             set_next(g, &y.down, e->nsm);
             set_tp(e, g, true, -1, e->hp);
+            set_hq(e, g, nullptr, y);
             launch_tg(e, GM_FFN, g);
         }
         snprintf(e->cur, sizeof e->cur, "L%d.down", l);
@@ -343,6 +360,7 @@ static void enqueue_token(sb_engine * e) {
             float * xo = e->x + (size_t) e->E * e->tp.rank / e->tp.n;
             TGArgs g = tg_args(e, y.down, e->hp, nullptr, xo);
             g.in_permuted = 1;
+            if (hq_plan(e, y.gateup, e->F)) g.in_act = e->hq;
             set_next(g, l + 1 < e->n_layer ? &e->L[l + 1].qkv : nullptr, e->nsm);
             set_tp(e, g, true, 2 * l, xo);
             launch_tg(e, GM_DOWN, g);
@@ -470,20 +488,13 @@ static bool build(sb_engine * e, char * why, int nwhy) {
                        y.o, why, nwhy))
             return false;
         if (!y.moe) {
-            if (tp == 1) {
-                const int gtr = tr_for(gt, 2 * F, 1);
-                if (!upload_tt(e->ar, f, gt, 2 * F, gtr, min_tiles, 1, [&](int r) {
-                        const int h = gtr / 2, ti = r / gtr, j = r % gtr, i = ti * h + j % h;
-                        return i >= F ? RowSrc{nullptr, 0} : RowSrc{j < h ? gt : up, i}; },
-                               y.gateup, why, nwhy) ||
-                    !upload_tt(e->ar, f, dn, e->E, tr_for(dn, e->E, 0, 1, 0), min_tiles, 0,
-                               [&](int r) { return RowSrc{r < e->E ? dn : nullptr, r}; }, y.down, why, nwhy))
-                    return false;
-                y.down_iperm = y.down.iperm;
-            } else {
-                // this rank: down's column positions [F r/tp, ..) -- whole groups -- i.e. hidden
-                // values perm[j]; their gate/up rows interleaved by tile as above, each value
-                // written at its position j of the whole (permuted) hidden vector
+            {
+                // gate/up rows in down's column order (a tile of TR rows holds TR/2 gate rows
+                // then the same TR/2 up rows): tile k yields hidden positions k TR/2 ..,
+                // written at their place j of the permuted hidden vector, so consecutive
+                // tiles give whole groups of down's input. Over tp GPUs this rank takes
+                // the positions [F r/tp, F (r+1)/tp) -- whole groups -- and down's rows
+                // [E r/tp, ..).
                 if (F % (32 * tp)) { snprintf(why, nwhy, "layer %d: FFN %d not in whole groups per rank", l, F); return false; }
                 const int fn = F / tp, j0 = fn * rk, en = e->E / tp, e0 = en * rk;
                 const int32_t * dperm = (const int32_t *) (f.base + dn->perm_off);
@@ -534,6 +545,7 @@ static bool build(sb_engine * e, char * why, int nwhy) {
         e->x = (float *) carve(e, (size_t) e->E * 4);
         e->hp = (float *) carve(e, (size_t) (e->F > 0 ? e->F : 1) * 4);
         e->logits = (float *) carve(e, (size_t) e->V * 4);
+        if (e->F > 0) e->hq = (uint8_t *) carve(e, (size_t) e->F + (size_t) (e->F / 32) * 8);
     } else {
         // the exchanged vectors live in the region the peers map: [flags | x | hidden | logits]
         TpState & t = e->tp;
@@ -621,8 +633,11 @@ extern "C" int sb_time_kernel(sb_engine * e, int which, int reps, float * ms_avg
         case 2: g = tg_args(e, y.o, e->att, nullptr, e->x); launch_tg(e, GM_O, g); break;
         case 3: g = tg_args(e, y.gateup, e->x, y.fn, e->hp); g.ffn_f = y.gateup.rows / 2; g.ffn_n = e->F;
                 g.scatter = y.down_iperm;
+                set_hq(e, g, nullptr, y);
                 launch_tg(e, GM_FFN, g); break;
-        case 4: g = tg_args(e, y.down, e->hp, nullptr, e->x); g.in_permuted = 1; launch_tg(e, GM_DOWN, g); break;
+        case 4: g = tg_args(e, y.down, e->hp, nullptr, e->x); g.in_permuted = 1;
+                if (hq_plan(e, y.gateup, e->F)) g.in_act = e->hq;
+                launch_tg(e, GM_DOWN, g); break;
         default: g = tg_args(e, e->head, e->x, e->out_norm, e->logits); g.prefetch = 0;
                  g.am_val = e->am_val; g.am_idx = e->am_idx; g.am_cnt = e->am_cnt;
                  g.tok = e->tok; g.pos = e->pos; g.tlog = nullptr; launch_tg(e, GM_HEAD, g); break;

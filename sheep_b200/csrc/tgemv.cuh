@@ -47,6 +47,10 @@ constexpr size_t kSmemBudget = 225 * 1024;
 // all (their CTA counts, summed on the host), so event e of the current token
 // is complete at (tokens before it) * c_tok + the count up to e.
 constexpr int kMaxTp = 8;
+// Most groups of 32 hidden values one gate/up CTA quantizes for the down GEMV
+// (their floats are kept in the column-order region of its shared memory, free
+// once the input is staged: the input has at least this many values).
+constexpr int kHqMaxGroups = 8;
 struct TpX {
     int n, rank;                       // ranks; this one
     float * peer_out[kMaxTp];          // the output pointer as each peer maps it (NULL for this rank)
@@ -111,6 +115,18 @@ struct TGArgs {
     int * err;               // set if a bounded wait gave up
     unsigned long long * trace;   // trace build: per-CTA timestamps
     int launch_id;
+    // The gate/up GEMV quantizing the hidden vector for the down GEMV: with
+    // grp_tiles > 0 each CTA takes whole groups of 32 hidden values (tiles in
+    // down's column order, grp_tiles tiles a group), keeps its values in shared
+    // memory (the gathered input's column-order region) and writes their int8
+    // codes, scales and scale * sums into hq in the
+    // activation's shared-memory layout (ActS: codes in the slot order, then
+    // xs[ng], then xsum[ng]). The down GEMV given in_act copies that block into
+    // its shared memory with one bulk copy instead of reading the floats and
+    // quantizing them after its wait. The codes are quant_lanes' own.
+    int grp_tiles;
+    uint8_t * hq;
+    const uint8_t * in_act;
     // the next GEMV's tiles: this CTA prefetches the range its own index will
     // take there into L2, so the next kernel's bulk copies hit L2
     const uint8_t * next_tiles;
@@ -911,7 +927,7 @@ template <int NB, int SIX>
 __global__ void __maxnreg__(88) k_tgemv(const __grid_constant__ TGArgs g) {
     const int MODE = g.mode;
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages], statics;
+    __shared__ __align__(8) uint64_t full[kMaxStages], empty[kMaxStages], statics, actbar;
     __shared__ double red[kConsWarps];
     __shared__ float am_v[kConsWarps];
     __shared__ int am_i[kConsWarps];
@@ -920,7 +936,10 @@ __global__ void __maxnreg__(88) k_tgemv(const __grid_constant__ TGArgs g) {
     const TT & t = g.t;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int T = t.ntiles;
-    const int t0 = (int) ((long) T * blockIdx.x / gridDim.x), t1 = (int) ((long) T * (blockIdx.x + 1) / gridDim.x);
+    // whole groups of hidden values per CTA when the gate/up GEMV quantizes for down
+    const int gt = g.grp_tiles > 0 ? g.grp_tiles : 1, ngq = T / gt;
+    const int t0 = (int) ((long) ngq * blockIdx.x / gridDim.x) * gt;
+    const int t1 = (int) ((long) ngq * (blockIdx.x + 1) / gridDim.x) * gt;
     const int ns = g.nstage;
     const StageLayout SL = stage_layout(t.cols, !g.in_permuted, g.norm_w != nullptr, g.x_smem, tg_dot_bytes(t));
     uint8_t * ring = smem + SL.ring_off;
@@ -936,6 +955,7 @@ __global__ void __maxnreg__(88) k_tgemv(const __grid_constant__ TGArgs g) {
     if (threadIdx.x == 0) {
         for (int s = 0; s < ns; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], 1); }
         mbar_init(&statics, 1);
+        mbar_init(&actbar, 1);
         mbar_fence_init();
     }
     __syncthreads();
@@ -1027,7 +1047,17 @@ __global__ void __maxnreg__(88) k_tgemv(const __grid_constant__ TGArgs g) {
         if (threadIdx.x == 0) tp_wait(g.tp);
         bar_sync(1, kConsThreads);
     }
-    tg_stage(g, a, red, smem, SL, &statics, failed);
+    if (g.in_act) {
+        // the input already quantized by the gate/up GEMV, in this layout: one copy
+        const uint32_t ab = (uint32_t) t.cols + (uint32_t) (t.cols / kGroup) * 8u;
+        if (threadIdx.x == 0) {
+            mbar_expect_tx(&actbar, ab);
+            bulk_g2s(smem, g.in_act, ab, &actbar);
+        }
+        if (!failed && !mbar_wait(&actbar, 0, g.err, 9)) failed = true;
+    } else {
+        tg_stage(g, a, red, smem, SL, &statics, failed);
+    }
     SB_MARK(g.trace, g.launch_id, 2);
     const TileGeom tg = tile_geom(t.cols, t.TR, NB, SIX, t.has_min);
     const int TR = t.TR;
@@ -1061,6 +1091,10 @@ __global__ void __maxnreg__(88) k_tgemv(const __grid_constant__ TGArgs g) {
                 if (SB_CHECK(g.err, sc >= 0 && sc < g.ffn_n, 108)) {
                     const float h = silu_mul(gv, uv);
                     g.out[sc] = h;
+                    // the CTA's groups hold hidden positions [t0 TR/2, t1 TR/2)
+                    // (kept where the column order lay: staging is over)
+                    if (g.grp_tiles && SB_CHECK(g.err, !g.in_permuted && sc >= t0 * (TR / 2) && sc < t1 * (TR / 2), 109))
+                        reinterpret_cast<float *>(smem + SL.perm_off)[sc - t0 * (TR / 2)] = h;
                     for (int p = 0; p < g.tp.n; p++)
                         if (g.tp.peer_out[p]) g.tp.peer_out[p][sc] = h;
                 }
@@ -1085,6 +1119,26 @@ __global__ void __maxnreg__(88) k_tgemv(const __grid_constant__ TGArgs g) {
         }
     }
 
+    if (MODE == GM_FFN && g.grp_tiles) {
+        // every hidden value of the CTA's groups is in shared memory: their codes
+        // for the down GEMV, one lane per group, quant_lanes as its staging would
+        bar_sync(1, kConsThreads);
+        const float * hq_vals = reinterpret_cast<const float *>(smem + SL.perm_off);
+        const int F = g.ffn_n, ng = F / kGroup;
+        ActS ga;
+        ga.q = reinterpret_cast<int8_t *>(g.hq);
+        ga.xs = reinterpret_cast<float *>(g.hq + F);
+        ga.xsum = ga.xs + ng;
+        ga.n = F;
+        const int gq0 = t0 / g.grp_tiles, gq1 = t1 / g.grp_tiles;
+        for (int grp = gq0 + (int) threadIdx.x; grp < gq1; grp += kConsThreads) {
+            const float4 * src = reinterpret_cast<const float4 *>(hq_vals + (grp - gq0) * kGroup);
+            float4 v[8];
+#pragma unroll
+            for (int k = 0; k < 8; k++) v[k] = src[k];
+            quant_lanes<1>(v, grp, 0, ga, g, false, true);
+        }
+    }
     if (g.tp.n > 1 && g.tp.raise) {
         // every consumer's stores to the peers, then this CTA's arrival
         bar_sync(1, kConsThreads);
