@@ -157,8 +157,11 @@ def test_gemv_cfg0_shapes_stage_reuse():
 
 @pytest.mark.parametrize("n_ff", [8960, 1408])
 def test_gemv_prepermuted_staging_bitexact(n_ff):
-    """The staging the decode chain's down projection runs: its input already
-    in the tensor's column order, quantized one lane per group (no gather). On
+    """The pre-permuted staging: the input already in the tensor's column
+    order, quantized one lane per group (no gather), as the tensor-parallel
+    down projection stages it and as the one-GPU gate/up GEMV quantizes the
+    hidden vector for down (the same quant_lanes code; that path is checked
+    end to end by the decode tests' bit-exact logits). On
     configuration 0's 8960-column input and on 1408 columns (44 groups: not a
     multiple of the 512 consumer threads' groups): the exported codes, scales
     and sums equal the per-32 quantization of the same values, bit for bit,
